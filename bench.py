@@ -1,0 +1,496 @@
+#!/usr/bin/env python
+"""Benchmark of the attention hot path on B200 (one JSON line on rank 0).
+
+Workload (BASELINE.json metric "attn+DeltaNet decode tok/s & % HBM roofline
+@32K ctx"; config 3 with the config-2 DeltaNet layers): one decode step of a
+32-sequence batch per GPU through one model layer group -- three Gated
+DeltaNet layers (linear_core, src/model/ops.rs:647-742) and one gated
+full-attention layer (full_core, ops.rs:812-940) over a bf16 KV cache holding
+32768 positions per sequence. Every step appends one position per sequence.
+Inputs are seeded synthetic data with the configs' distributions (no
+checkpoint is available); the KV cache (4.3 GB) is larger than L2, so no L2
+flush is needed between steps.
+
+  value  tokens/s over all ranks, device-timed (CUDA events), inputs resident
+         in HBM; max over ranks.
+  e2e    the same metric through the host-pointer C-ABI calls
+         (q38_linear_decode_host / q38_full_decode_host): pinned host inputs
+         copied in and outputs copied back every step, host wall clock.
+  roofline  the full-attention decode operation (prep + split-KV + merge
+         kernels, the dominant cost) against the measured HBM copy bandwidth.
+  cpu_baseline  the CPU oracle (a restatement of the reference's Rust cores,
+         threaded over heads like its rayon regions) on a bounded sample of the
+         same workload, rank 0 at N=1 only.
+
+--impl reference runs only the CPU oracle (the reference's algorithm; the
+Rust crate itself cannot be built here), rank 0 only.
+
+Multi-GPU: one process per GPU (torchrun); every rank owns its own 32
+sequences (weak scaling, no data-path collective).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO / "qwen3.8_27b_in_rust_b200"))
+
+METRIC = "attn+DeltaNet decode tok/s & % HBM roofline @32K ctx; prefill TFLOP/s; 1-8 GPU"
+FULL_LAYER = 3
+LINEAR_LAYERS = (0, 1, 2)
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=400)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--batch", type=int, default=32)
+    ap.add_argument("--context", type=int, default=32768)
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--cpu-seconds", type=float, default=10.0,
+                    help="CPU work budget of the cpu_baseline sample")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    return ap.parse_args()
+
+
+# ---------------------------------------------------------------------------
+# Byte accounting (algorithmic bytes, fp32 I/O, bf16 KV)
+# ---------------------------------------------------------------------------
+def attn_bytes_per_seq(positions: int) -> int:
+    """Full-attention decode of one sequence at `positions` cached rows
+    (including the new one): K and V rows read (bf16), q/gate/key/value in,
+    key and attention out, the appended K/V row."""
+    kv = positions * 4 * 256 * 2 * 2
+    io = (12288 + 1024 + 1024) * 4 + (1024 + 6144) * 4 + 2 * 1024 * 2
+    return kv + io
+
+
+def deltanet_bytes_per_seq() -> int:
+    """One DeltaNet decode step of one sequence: the 48x128x128 f32 state read
+    and written, the conv state read and written, conv weights, qkv/z/beta/alpha
+    in, qkv/beta/alpha/attention out."""
+    state = 2 * 48 * 128 * 128 * 4
+    conv = 2 * 10240 * 3 * 4 + 10240 * 4 * 4
+    io = (10240 + 6144 + 96) * 4 + (10240 + 96 + 6144) * 4
+    return state + conv + io
+
+
+def load_peaks() -> tuple[float, str]:
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+        except Exception:
+            pass
+    return 6650.0, "fallback"
+
+
+def load_traffic_profile() -> dict | None:
+    p = REPO / "profiles" / "attn_decode_traffic.json"
+    if p.exists():
+        try:
+            return json.loads(p.read_text())
+        except Exception:
+            return None
+    return None
+
+
+# ---------------------------------------------------------------------------
+# Clock sampling during the timed region (NVML, read-only)
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    def __init__(self, device_index: int, period_s: float = 0.02):
+        self.samples = []
+        self.reasons = set()
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._thread = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self._nvml = pynvml
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self._nvml = None
+        self.period = period_s
+
+    def _reason_names(self, bits: int) -> list[str]:
+        names = {
+            0x0000000000000004: "sw_power_cap",
+            0x0000000000000008: "hw_slowdown",
+            0x0000000000000020: "sw_thermal_slowdown",
+            0x0000000000000040: "hw_thermal_slowdown",
+            0x0000000000000080: "hw_power_brake_slowdown",
+        }
+        return [n for b, n in names.items() if bits & b]
+
+    def _run(self):
+        nv = self._nvml
+        while not self._stop.is_set():
+            try:
+                mhz = nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM)
+                bits = nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+                self.samples.append(mhz)
+                self.reasons.update(self._reason_names(bits))
+            except Exception:
+                pass
+            self._stop.wait(self.period)
+
+    def __enter__(self):
+        if self._nvml is not None:
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._thread is not None:
+            self._thread.join()
+
+    def summary(self) -> dict:
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples)}
+
+
+# ---------------------------------------------------------------------------
+# CPU legs (the oracle restates the reference's algorithm; checker only)
+# ---------------------------------------------------------------------------
+class CpuWorkload:
+    """One sequence of the bench workload on the CPU oracle: a 32768-position
+    f32 cache holding bf16-rounded values (what the GPU's bf16 cache holds),
+    three DeltaNet layers and one full-attention layer."""
+
+    def __init__(self, context: int, seed: int):
+        sys.path.insert(0, str(REPO / "oracle"))
+        import numpy as np
+
+        import oracle
+        from q38attn import synth
+        oracle.build()
+        oracle.set_threads(os.cpu_count() or 1)
+        self.np, self.oracle = np, oracle
+        g = synth.rng(seed + 1000)
+        self.context = context
+        self.cap = context + 4096
+        self.kc = np.zeros((self.cap, 1024), np.float32)
+        self.vc = np.zeros((self.cap, 1024), np.float32)
+        for i in range(0, context, 4096):
+            n = min(4096, context - i)
+            k, v = synth.kv_rows(g, n, bf16=True)
+            self.kc[i:i + n], self.vc[i:i + n] = k, v
+        self.wf = synth.full_weights(g)
+        self.wl = [synth.linear_weights(g) for _ in LINEAR_LAYERS]
+        self.sl = [synth.linear_state(g) for _ in LINEAR_LAYERS]
+        self.full_in = {k: v[0] for k, v in synth.full_step(g).items()}
+        self.lin_in = {k: v[0] for k, v in synth.linear_step(g).items()}
+        self.pos = context
+        self.q = np.zeros(6144, np.float32)
+        self.gate = np.zeros(6144, np.float32)
+        self.scores = np.zeros(24 * self.cap, np.float32)
+        self.att = np.zeros(6144, np.float32)
+
+    def token(self) -> None:
+        np, o = self.np, self.oracle
+        for i, _ in enumerate(LINEAR_LAYERS):
+            x = {k: v.copy() for k, v in self.lin_in.items()}
+            o.linear_core(self.wl[i], self.sl[i]["conv_state"], self.sl[i]["delta_state"],
+                          x["qkv"], x["z"], x["beta"], x["alpha"], self.att)
+        if self.pos >= self.cap:
+            self.pos = self.context
+        key = self.full_in["key"].copy()
+        rc = o.full_core(self.wf, self.full_in["q_and_gate"], key, self.full_in["value"],
+                         self.q, self.gate, self.scores, self.att, self.kc, self.vc, self.cap,
+                         self.pos, FULL_LAYER % 4, True)
+        assert rc == 0
+        self.pos += 1
+
+
+def cpu_baseline(args) -> dict:
+    w = CpuWorkload(args.context, args.seed)
+    w.token()  # warm
+    t0 = time.perf_counter()
+    n = 0
+    while True:
+        w.token()
+        n += 1
+        if time.perf_counter() - t0 >= args.cpu_seconds:
+            break
+    dt = time.perf_counter() - t0
+    return {"value": n / dt, "unit": "tok/s", "cores": w.oracle.get_threads(), "kind": "port",
+            "sample": f"{n} sequence-tokens of the workload (3 DeltaNet layers + 1 full-attention "
+                      f"layer at {args.context} cached positions each), {dt:.1f} s, C++ "
+                      f"restatement of the reference cores, OpenMP over heads"}
+
+
+def run_reference(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    w = CpuWorkload(args.context, args.seed)
+    for _ in range(args.warmup):
+        w.token()
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        w.token()
+        times.append(time.perf_counter() - t0)
+    total = sum(times)
+    value = args.steps / total
+    line = {
+        "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * total / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded; config distributions)", "impl": "reference",
+        "config": workload_config(args),
+        "cpu_baseline": {"value": value, "unit": "tok/s", "cores": w.oracle.get_threads(),
+                         "kind": "port",
+                         "sample": "1 sequence-token per step (3 DeltaNet layers + 1 "
+                                   f"full-attention layer at {args.context} cached positions)"},
+        "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def workload_config(args) -> dict:
+    return {
+        "workload": ("config3+config2: per GPU, 32-sequence decode step through 3 Gated "
+                     "DeltaNet layers + 1 gated full-attention layer, bf16 KV cache at "
+                     f"{args.context} cached positions per sequence"),
+        "global_batch": args.batch * args.gpus, "batch_per_gpu": args.batch,
+        "seq_len": args.context, "kv_dtype": "bf16", "state_dtype": "f32",
+        "geometry": "24Q/4KV x 256 (RoPE 64, theta 1e7); DeltaNet 16K/48V x 128, conv 4",
+        "parallelism": f"sequences sharded, {args.gpus} rank(s), no collective",
+        "l2": "inputs > L2 (4.3 GB KV per GPU); no flush",
+    }
+
+
+# ---------------------------------------------------------------------------
+# GPU arm
+# ---------------------------------------------------------------------------
+def run_ours(args) -> None:
+    import numpy as np
+    import torch
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+
+    import q38attn
+    from q38attn import synth
+
+    B, ctx_pos = args.batch, args.context
+    total_steps = args.warmup + args.steps
+    e2e_steps = 0 if args.no_e2e else min(args.steps, 50)
+    cap = ctx_pos + total_steps + e2e_steps + 8
+    ctx = q38attn.Context(local)
+    g = synth.rng(args.seed + 7919 * rank)
+    wf = synth.full_weights(g)
+    ctx.bind_full_layer(FULL_LAYER, wf["q_norm"], wf["k_norm"])
+    for l in LINEAR_LAYERS:
+        wl = synth.linear_weights(g)
+        ctx.bind_linear_layer(l, wl["conv1d"], wl["dt_bias"], wl["ssm_a"], wl["ssm_norm"])
+    st = ctx.state(B, cap, full_slots=1, linear_slots=len(LINEAR_LAYERS),
+                   kv_dtype=q38attn.Q38_KV_BF16)
+
+    # Device-side init of the resident state (seeded).
+    tg = torch.Generator(device="cuda")
+    tg.manual_seed(args.seed + 1000003 * rank)
+    kview, vview = st.kv_views(FULL_LAYER)
+    for b in range(B):
+        kview[b, :, :ctx_pos].normal_(generator=tg)
+        vview[b, :, :ctx_pos].normal_(generator=tg)
+    for l in LINEAR_LAYERS:
+        cview, dview = st.linear_views(l)
+        cview.normal_(generator=tg)
+        dview.normal_(0.0, 0.02, generator=tg)
+    del kview, vview
+
+    # Two pristine per-step input sets in one flat buffer each.
+    n_lin = len(LINEAR_LAYERS)
+    sizes = [("qg", (B, 12288)), ("key", (B, 1024)), ("value", (B, 1024))]
+    for i in range(n_lin):
+        sizes += [(f"qkv{i}", (B, 10240)), (f"z{i}", (B, 6144)), (f"beta{i}", (B, 48)),
+                  (f"alpha{i}", (B, 48))]
+    total = sum(int(np.prod(s)) for _, s in sizes)
+
+    def views(flat):
+        out, off = {}, 0
+        for name, shape in sizes:
+            n = int(np.prod(shape))
+            out[name] = flat[off:off + n].view(*shape)
+            off += n
+        return out
+
+    pristine = [torch.randn(total, device="cuda", generator=tg) for _ in range(2)]
+    work = torch.empty(total, device="cuda")
+    wv = views(work)
+    out_full = torch.empty(B, 6144, device="cuda")
+    out_lin = [torch.empty(B, 6144, device="cuda") for _ in range(n_lin)]
+    positions = (torch.arange(total_steps, device="cuda", dtype=torch.int32)[:, None] + ctx_pos
+                 ).expand(total_steps, B).contiguous()
+    stream = torch.cuda.current_stream()
+
+    ev_attn = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for _ in range(args.steps)]
+    ev_lin = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+              for _ in range(args.steps)]
+
+    def step(s: int, timed_index: int = -1):
+        work.copy_(pristine[s % 2])
+        if timed_index >= 0:
+            ev_lin[timed_index][0].record(stream)
+        for i, l in enumerate(LINEAR_LAYERS):
+            ctx.linear_decode(st, l, wv[f"qkv{i}"], wv[f"z{i}"], wv[f"beta{i}"], wv[f"alpha{i}"],
+                              out_lin[i], stream=stream)
+        if timed_index >= 0:
+            ev_lin[timed_index][1].record(stream)
+            ev_attn[timed_index][0].record(stream)
+        ctx.full_decode(st, FULL_LAYER, wv["qg"], wv["key"], wv["value"], positions[s],
+                        out_full, max_position=ctx_pos + s, stream=stream)
+        if timed_index >= 0:
+            ev_attn[timed_index][1].record(stream)
+
+    for s in range(args.warmup):
+        step(s)
+    torch.cuda.synchronize()
+    if st.errors():
+        raise RuntimeError("device error bits set during warm-up")
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_end = torch.cuda.Event(enable_timing=True)
+    barrier()
+    with ClockSampler(local) as clocks:
+        t_start.record(stream)
+        for k in range(args.steps):
+            step(args.warmup + k, k)
+        t_end.record(stream)
+        torch.cuda.synchronize()
+    barrier()
+    ms = t_start.elapsed_time(t_end)
+    attn_ms = statistics.mean(a.elapsed_time(b) for a, b in ev_attn)
+    lin_ms = statistics.mean(a.elapsed_time(b) for a, b in ev_lin)
+    if st.errors():
+        raise RuntimeError("device error bits set during the timed region")
+
+    # End-to-end through the host-pointer C-ABI calls.
+    e2e = None
+    if e2e_steps:
+        host = []
+        for p in pristine:
+            h = torch.empty(total, dtype=torch.float32, pin_memory=True)
+            h.copy_(p)
+            host.append({k: v.numpy() for k, v in views(h).items()})
+        outs_full = torch.empty(B, 6144, pin_memory=True).numpy()
+        outs_lin = torch.empty(B, 6144, pin_memory=True).numpy()
+        pos_host = torch.empty(B, dtype=torch.int32, pin_memory=True).numpy()
+        base = ctx_pos + total_steps
+        h2d = B * (12288 + 2048) * 4 + B * 4 + n_lin * B * (10240 + 6144 + 96) * 4
+        d2h = B * (6144 + 1024) * 4 + n_lin * B * (6144 + 10240 + 96) * 4
+        barrier()
+        t0 = time.perf_counter()
+        for s in range(e2e_steps):
+            hv = host[s % 2]
+            for i, l in enumerate(LINEAR_LAYERS):
+                ctx.linear_decode_host(st, l, hv[f"qkv{i}"], hv[f"z{i}"], hv[f"beta{i}"],
+                                       hv[f"alpha{i}"], outs_lin, stream=stream)
+            pos_host[:] = base + s
+            ctx.full_decode_host(st, FULL_LAYER, hv["qg"], hv["key"], hv["value"], pos_host,
+                                 outs_full, stream=stream)
+        e2e_s = time.perf_counter() - t0
+        barrier()
+        e2e = [e2e_s, h2d, d2h]
+
+    # Max over ranks.
+    vals = torch.tensor([ms, attn_ms, lin_ms, e2e[0] if e2e else 0.0], device="cuda",
+                        dtype=torch.float64)
+    if dist is not None:
+        dist.all_reduce(vals, op=dist.ReduceOp.MAX)
+    ms, attn_ms, lin_ms, e2e_s = vals.tolist()
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cpu = cpu_baseline(args)
+
+    if rank == 0:
+        step_ms = ms / args.steps
+        tokens = B * world
+        mean_pos = ctx_pos + args.warmup + (args.steps - 1) / 2.0 + 1
+        attn_bytes = B * attn_bytes_per_seq(int(round(mean_pos)))
+        lin_bytes = n_lin * B * deltanet_bytes_per_seq()
+        peak, peak_kind = load_peaks()
+        achieved = attn_bytes / (attn_ms * 1e-3) / 1e9
+        traffic = None
+        prof = load_traffic_profile()
+        if prof and prof.get("dram_bytes_per_kv_byte"):
+            traffic = prof["dram_bytes_per_kv_byte"] * B * int(round(mean_pos)) * 4 * 256 * 2 * 2
+        line = {
+            "metric": METRIC, "value": tokens / (step_ms * 1e-3), "unit": "tok/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": step_ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32 (bf16 KV cache)",
+            "data": "synthetic (seeded; config distributions)",
+            "config": workload_config(args),
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": traffic,
+                         "kernel": "full-attention decode op (prep + split-KV + merge)",
+                         "algorithmic_bytes": attn_bytes, "launch_ms": attn_ms,
+                         "peak_source": f"{peak_kind} hbm_gbs"},
+            "deltanet": {"layers": n_lin, "ms_per_step": lin_ms,
+                         "achieved_gbs": lin_bytes / (lin_ms * 1e-3) / 1e9,
+                         "frac": lin_bytes / (lin_ms * 1e-3) / 1e9 / peak},
+            "step_gbs": (attn_bytes + lin_bytes) / (step_ms * 1e-3) / 1e9,
+            "gpu_launches": 9 * args.steps,
+            "clocks": clocks.summary(),
+        }
+        if e2e:
+            line["e2e"] = {"value": tokens * e2e_steps / e2e_s, "unit": "tok/s",
+                           "h2d_bytes_per_step": e2e[1], "d2h_bytes_per_step": e2e[2],
+                           "steps": e2e_steps}
+        if cpu:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line), flush=True)
+
+    st.close()
+    ctx.close()
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main() -> None:
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

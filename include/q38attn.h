@@ -1,0 +1,220 @@
+/*
+ * q38attn.h -- C ABI of the B200 (sm_100a) attention hot path of
+ * StepfenShawn/qwen3.8_27b_in_rust: gated full attention and Gated DeltaNet,
+ * decode and prefill.
+ *
+ * This is the boundary the reference's Rust host binds with a thin
+ * `extern "C"` FFI crate (INTEGRATION.md shows the binding). It replaces the
+ * two crate-private cores and the per-token loops that call them:
+ *
+ *   linear_core   src/model/ops.rs:647-742   -> q38_linear_decode / q38_linear_core
+ *   full_core     src/model/ops.rs:812-940   -> q38_full_decode   / q38_full_core
+ *   batch_linear_attention loop  ops.rs:1088-1099 -> q38_linear_prefill
+ *   batch_full_attention loop    ops.rs:1156-1172 -> q38_full_prefill
+ *   Q38Model state fields  src/model/mod.rs:155-158, allocated at
+ *   src/model/ops.rs:1461-1490  -> q38_state_create
+ *
+ * Conventions
+ *  - Every function returns an int status: Q38_OK (0), Q38_ERR_ARG (-1, the
+ *    reference's Err(-1): bad shape, bad layer kind, cache row out of range),
+ *    Q38_ERR_CUDA (-2), Q38_ERR_TIMEOUT (-3, a bounded device wait gave up).
+ *    q38_last_error() returns a message for the calling thread's last failure.
+ *  - Functions named *_decode / *_prefill take DEVICE pointers and are
+ *    stream-ordered on `stream` (a cudaStream_t passed as void*; NULL is the
+ *    legacy default stream). They never allocate and never synchronise.
+ *    Device-side argument errors (a position outside the cache) are recorded
+ *    in the state and reported by q38_state_errors().
+ *  - Functions named *_core and *_host take HOST pointers, copy through the
+ *    state's staging buffers, and return after the stream has synchronised.
+ *  - `layer` is the reference's layer index (0..64). Full-attention layers are
+ *    those with (layer+1)%4==0 or layer==64 (ops.rs:39-41) and use KV slot
+ *    layer/4; the others are DeltaNet layers with state slot
+ *    layer-(layer+1)/4 (ops.rs:45-47). Calling a function of the wrong layer
+ *    kind returns Q38_ERR_ARG, as the reference's let-else does.
+ *  - Arrays are row-major f32 in the reference's layouts unless noted.
+ *  - Not re-entrant on one state: calls on one state must be ordered (same
+ *    stream, or externally synchronised), like the reference's &mut borrows.
+ */
+#ifndef Q38ATTN_H
+#define Q38ATTN_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define Q38_OK 0
+#define Q38_ERR_ARG (-1)
+#define Q38_ERR_CUDA (-2)
+#define Q38_ERR_TIMEOUT (-3)
+
+/* KV cache element type. F32 matches the reference's Vec<f32> cache
+ * (src/model/ops.rs:1465); BF16 halves the decode traffic. */
+#define Q38_KV_F32 0
+#define Q38_KV_BF16 1
+
+/* Device error bits returned by q38_state_errors. */
+#define Q38_DEVERR_POSITION 1
+#define Q38_DEVERR_TIMEOUT 2
+#define Q38_DEVERR_SHAPE 4
+
+typedef struct q38_ctx q38_ctx;
+typedef struct q38_state q38_state;
+
+/* Model geometry, src/model/mod.rs:13-26. q38_geom_default fills the
+ * reference's constants; the kernels are specialised for head_dim 256 with
+ * RoPE on 64 dims and a GQA group of 6, and DeltaNet head_dim 128 with a
+ * kernel-4 conv; other values are rejected with Q38_ERR_ARG. Head counts may
+ * vary (attn_heads = 6*attn_kv_heads, linear_v_heads a multiple of
+ * linear_qk_heads). */
+typedef struct q38_geom {
+    int32_t attn_heads;      /* Q38_ATTN_HEADS      24 */
+    int32_t attn_kv_heads;   /* Q38_ATTN_KV_HEADS    4 */
+    int32_t attn_head_dim;   /* Q38_ATTN_HEAD_DIM  256 */
+    int32_t rope_dims;       /* rope(): lanes [0,64)    ops.rs:595-610 */
+    float rope_theta;        /* 1e7                     ops.rs:596 */
+    int32_t linear_qk_heads; /* Q38_LINEAR_QK_HEADS 16 */
+    int32_t linear_v_heads;  /* Q38_LINEAR_V_HEADS  48 */
+    int32_t linear_head_dim; /* Q38_LINEAR_HEAD_DIM 128 */
+    int32_t conv_kernel;     /* ssm_conv1d width 4      ops.rs:665-676 */
+    float rms_eps;           /* Q38_RMS_EPS 1e-6 */
+} q38_geom;
+
+void q38_geom_default(q38_geom *geom);
+
+/* Last error message of the calling thread ("" if none). */
+const char *q38_last_error(void);
+
+/* Library version string. */
+const char *q38_version(void);
+
+/* ---------------------------------------------------------------- context */
+
+/* Creates a context on CUDA device `device`. geom==NULL: the reference's
+ * geometry. Replaces the weight/geometry half of Q38Model::bind
+ * (src/model/ops.rs:1450-1459). */
+int q38_ctx_create(const q38_geom *geom, int device, q38_ctx **out);
+int q38_ctx_destroy(q38_ctx *ctx);
+
+/* Copies a full-attention layer's F32 norm weights (HOST pointers, 256 each)
+ * to the device: attn_q_norm / attn_k_norm, read via scalar() at
+ * src/model/ops.rs:838-850. */
+int q38_bind_full_layer(q38_ctx *ctx, int layer, const float *q_norm, const float *k_norm);
+
+/* Copies a DeltaNet layer's F32 weights (HOST pointers) to the device:
+ * ssm_conv1d [qkv_dim][4], ssm_dt.bias [v_heads], ssm_a [v_heads],
+ * ssm_norm [head_dim] (src/model/ops.rs:658-663, 665-740). */
+int q38_bind_linear_layer(q38_ctx *ctx, int layer, const float *conv1d, const float *dt_bias,
+                          const float *ssm_a, const float *ssm_norm);
+
+/* ------------------------------------------------------------------ state */
+
+/* Allocates device-resident per-sequence state for `batch` sequences:
+ * full_slots KV caches of context_length positions each (the reference has
+ * 17: 16 layers + the MTP slot) and linear_slots conv/delta states (the
+ * reference has 48), plus the decode scratch. Zero-initialised.
+ * Replaces src/model/ops.rs:1461-1490. Device layouts:
+ *   key/value cache [full_slot][batch][kv_heads][context_length][256] (kv_dtype)
+ *   conv state      [linear_slot][batch][qkv_dim][3] f32 (reference layout)
+ *   delta state     [linear_slot][batch][v_heads][128][128] f32 (reference layout) */
+int q38_state_create(q38_ctx *ctx, int batch, int context_length, int full_slots,
+                     int linear_slots, int kv_dtype, q38_state **out);
+int q38_state_destroy(q38_state *st);
+
+/* Zeroes all caches and recurrent state (Q38ModelOps::reset). */
+int q38_state_reset(q38_state *st, void *stream);
+
+/* Reads and clears the device error bits (synchronises the device). */
+int q38_state_errors(q38_state *st, int *bits);
+
+/* Device pointers of one slot's buffers, for callers that manage their own
+ * copies. Any output pointer may be NULL. */
+int q38_state_full_slot(q38_state *st, int layer, void **key_cache, void **value_cache,
+                        size_t *bytes_each);
+int q38_state_linear_slot(q38_state *st, int layer, float **conv_state, float **delta_state);
+
+/* Host <-> device copies in the reference's host layouts (synchronous).
+ * KV rows: key_rows/value_rows [count][kv_heads*256] f32 for positions
+ * first..first+count-1 of sequence `seq` (bf16 caches round on upload).
+ * Linear: conv_state [qkv_dim][3], delta_state [v_heads][128][128]. */
+int q38_state_upload_kv(q38_state *st, int layer, int seq, int first, int count,
+                        const float *key_rows, const float *value_rows);
+int q38_state_download_kv(q38_state *st, int layer, int seq, int first, int count,
+                          float *key_rows, float *value_rows);
+int q38_state_upload_linear(q38_state *st, int layer, int seq, const float *conv_state,
+                            const float *delta_state);
+int q38_state_download_linear(q38_state *st, int layer, int seq, float *conv_state,
+                              float *delta_state);
+
+/* ------------------------------------------------------------ decode (device) */
+
+/* One full-attention decode step for `batch` sequences (full_core,
+ * src/model/ops.rs:812-940, batched). DEVICE pointers:
+ *   q_and_gate [batch][heads*512]   per head 256 query then 256 gate lanes
+ *   key        [batch][kv_heads*256] in: projection; out: RMSNorm+RoPE'd key
+ *   value      [batch][kv_heads*256]
+ *   positions  [batch] int32         current_position of each sequence
+ *   attention  [batch][heads*256]    output
+ * max_position: host upper bound on every positions[b] (sizes the split grid;
+ * <0 means context_length-1). A position outside [0, context_length) or above
+ * max_position is flagged Q38_DEVERR_POSITION and that sequence is skipped. */
+int q38_full_decode(q38_ctx *ctx, q38_state *st, int layer, int batch, const float *q_and_gate,
+                    float *key, const float *value, const int32_t *positions, int max_position,
+                    float *attention, void *stream);
+
+/* One Gated DeltaNet decode step for `batch` sequences (linear_core,
+ * src/model/ops.rs:647-742, batched). DEVICE pointers:
+ *   qkv   [batch][qkv_dim]  in: projections; out: conv+SiLU+L2 values (as the
+ *                           reference leaves them)
+ *   z     [batch][v_heads*128]
+ *   beta  [batch][v_heads]  in: logits; out: sigmoid(beta)
+ *   alpha [batch][v_heads]  in: logits; out: ssm_a*softplus(alpha+dt_bias)
+ *   attention [batch][v_heads*128] output */
+int q38_linear_decode(q38_ctx *ctx, q38_state *st, int layer, int batch, float *qkv,
+                      const float *z, float *beta, float *alpha, float *attention,
+                      void *stream);
+
+/* ---------------------------------------------------------- decode (host) */
+
+/* Host-pointer forms of the two decode calls: copy the step's inputs from
+ * host memory (pinned for best speed), run the step on the device-resident
+ * state, copy the outputs (and the in-place-modified inputs) back, and
+ * synchronise. positions is a HOST array here; an out-of-range position
+ * returns Q38_ERR_ARG before any work, as full_core does (ops.rs:860-864). */
+int q38_full_decode_host(q38_ctx *ctx, q38_state *st, int layer, int batch,
+                         const float *q_and_gate, float *key, const float *value,
+                         const int32_t *positions, float *attention, void *stream);
+int q38_linear_decode_host(q38_ctx *ctx, q38_state *st, int layer, int batch, float *qkv,
+                           const float *z, float *beta, float *alpha, float *attention,
+                           void *stream);
+
+/* ------------------------------------------------- reference-signature mirrors */
+
+/* Exactly the argument meaning of the reference's linear_core
+ * (src/model/ops.rs:647-657) with host slices: conv_state [qkv_dim][3] and
+ * delta_state [v_heads][128][128] are uploaded into sequence 0 of `layer`'s
+ * slot of `st`, the step runs on the GPU, and every &mut slice is written
+ * back. For parity checks; resident-state callers use q38_linear_decode. */
+int q38_linear_core(q38_ctx *ctx, q38_state *st, int layer, float *conv_state,
+                    float *delta_state, float *qkv, const float *z, float *beta, float *alpha,
+                    float *attention);
+
+/* Exactly the argument meaning of the reference's full_core
+ * (src/model/ops.rs:812-827) with host slices. key_cache/value_cache hold
+ * cache_rows rows of kv_heads*256 floats, row = (layer/4)*context_length+pos;
+ * positions 0..current_position-1 of this layer are uploaded into sequence 0
+ * of `st`, the step runs on the GPU, and row current_position, key, q, gate,
+ * scores (the softmax numerators exp(s-max) per head, as the reference leaves
+ * them) and attention are written back. q/gate/scores may be NULL. */
+int q38_full_core(q38_ctx *ctx, q38_state *st, int layer, const float *q_and_gate, float *key,
+                  const float *value, float *q, float *gate, float *scores, float *attention,
+                  float *key_cache, float *value_cache, size_t cache_rows,
+                  size_t context_length, uint32_t current_position);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* Q38ATTN_H */

@@ -1,0 +1,160 @@
+"""ctypes binding of the CPU oracle (libq38oracle.so).
+
+TEST INFRASTRUCTURE ONLY: the parity checker for tests/, __graft_entry__.smoke()
+and the CPU legs of bench.py. The product library never imports this module.
+
+The oracle restates the reference's linear_core (src/model/ops.rs:647-742),
+full_core (ops.rs:812-940) and their per-token prefill loops (ops.rs:1088-1099,
+1156-1172) in C++ (q38_oracle.cpp). Parity with the Rust is unpinned by the
+reference itself (no Rust toolchain here, no golden vectors upstream); see
+q38_oracle.h for how it is pinned instead.
+"""
+from __future__ import annotations
+
+import ctypes
+import subprocess
+from ctypes import c_float, c_int, c_int64, c_size_t, c_uint32, c_void_p
+from pathlib import Path
+
+import numpy as np
+
+ORACLE_DIR = Path(__file__).resolve().parent
+LIB_PATH = ORACLE_DIR / "libq38oracle.so"
+
+QKV = 10240
+V_DIM = 6144
+V_HEADS = 48
+QK_HEADS = 16
+HD = 128
+QG = 12288
+KV = 1024
+Q_DIM = 6144
+
+_lib = None
+
+
+def build(force: bool = False) -> Path:
+    src = [ORACLE_DIR / "q38_oracle.cpp", ORACLE_DIR / "q38_oracle.h", ORACLE_DIR / "Makefile"]
+    if force or not LIB_PATH.exists() or any(p.stat().st_mtime > LIB_PATH.stat().st_mtime
+                                               for p in src):
+        subprocess.run(["make", "-C", str(ORACLE_DIR), "-B" if force else "all"], check=True)
+    return LIB_PATH
+
+
+def load() -> ctypes.CDLL:
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            build()
+        lib = ctypes.CDLL(str(LIB_PATH))
+        P = c_void_p
+        lib.q38o_set_threads.argtypes = [c_int]
+        lib.q38o_get_threads.restype = c_int
+        lib.q38o_linear_core.argtypes = [P] * 11
+        lib.q38o_linear_core.restype = c_int
+        lib.q38o_full_core.argtypes = [P] * 11 + [c_size_t, c_size_t, c_uint32, c_size_t, c_int]
+        lib.q38o_full_core.restype = c_int
+        lib.q38o_linear_prefill.argtypes = [P] * 11 + [c_size_t]
+        lib.q38o_linear_prefill.restype = c_int
+        lib.q38o_full_prefill.argtypes = [P] * 8 + [c_size_t, c_size_t, c_uint32, c_size_t,
+                                                    c_size_t, c_int]
+        lib.q38o_full_prefill.restype = c_int
+        lib.q38o_full_prefill_rows.argtypes = [P] * 8 + [c_size_t, c_size_t, c_uint32, c_size_t,
+                                                         c_size_t, P, c_size_t, c_int]
+        lib.q38o_full_prefill_rows.restype = c_int
+        lib.q38o_rms_scale.argtypes = [P, c_size_t]
+        lib.q38o_rms_scale.restype = c_float
+        lib.q38o_l2norm.argtypes = [P, c_size_t]
+        lib.q38o_rope.argtypes = [P, c_size_t, c_uint32]
+        for name in ("q38o_sigmoid", "q38o_silu", "q38o_softplus", "q38o_round_bf16"):
+            getattr(lib, name).argtypes = [c_float]
+            getattr(lib, name).restype = c_float
+        _lib = lib
+    return _lib
+
+
+def _p(a, dtype=np.float32):
+    if a is None:
+        return None
+    assert isinstance(a, np.ndarray) and a.dtype == dtype and a.flags.c_contiguous, a.dtype
+    return c_void_p(a.ctypes.data)
+
+
+def set_threads(n: int) -> None:
+    load().q38o_set_threads(n)
+
+
+def get_threads() -> int:
+    return load().q38o_get_threads()
+
+
+def linear_core(w: dict, conv_state, delta_state, qkv, z, beta, alpha, attention) -> int:
+    """linear_core (ops.rs:647-742); every array is updated in place."""
+    return load().q38o_linear_core(_p(w["conv1d"]), _p(w["dt_bias"]), _p(w["ssm_a"]),
+                                   _p(w["ssm_norm"]), _p(conv_state), _p(delta_state), _p(qkv),
+                                   _p(z), _p(beta), _p(alpha), _p(attention))
+
+
+def linear_prefill(w: dict, conv_state, delta_state, qkv, z, beta, alpha, attention) -> int:
+    count = qkv.size // QKV
+    return load().q38o_linear_prefill(_p(w["conv1d"]), _p(w["dt_bias"]), _p(w["ssm_a"]),
+                                      _p(w["ssm_norm"]), _p(conv_state), _p(delta_state),
+                                      _p(qkv), _p(z), _p(beta), _p(alpha), _p(attention), count)
+
+
+def full_core(w: dict, q_and_gate, key, value, q, gate, scores, attention, key_cache,
+              value_cache, context_length: int, position: int, layer: int,
+              kv_round_bf16: bool = False) -> int:
+    """full_core (ops.rs:812-940); cache arrays are [rows][1024]."""
+    rows = min(key_cache.size, value_cache.size) // KV
+    return load().q38o_full_core(_p(w["q_norm"]), _p(w["k_norm"]), _p(q_and_gate), _p(key),
+                                 _p(value), _p(q), _p(gate), _p(scores), _p(attention),
+                                 _p(key_cache), _p(value_cache), rows, context_length, position,
+                                 layer, int(kv_round_bf16))
+
+
+def full_prefill(w: dict, q_and_gate, key, value, attention, key_cache, value_cache,
+                 context_length: int, base_position: int, layer: int,
+                 kv_round_bf16: bool = False, rows_wanted=None) -> int:
+    rows = min(key_cache.size, value_cache.size) // KV
+    count = q_and_gate.size // QG
+    lib = load()
+    if rows_wanted is None:
+        return lib.q38o_full_prefill(_p(w["q_norm"]), _p(w["k_norm"]), _p(q_and_gate), _p(key),
+                                     _p(value), _p(attention), _p(key_cache), _p(value_cache),
+                                     rows, context_length, base_position, layer, count,
+                                     int(kv_round_bf16))
+    r = np.ascontiguousarray(np.sort(np.asarray(rows_wanted, dtype=np.int64)))
+    return lib.q38o_full_prefill_rows(_p(w["q_norm"]), _p(w["k_norm"]), _p(q_and_gate),
+                                      _p(key), _p(value), _p(attention), _p(key_cache),
+                                      _p(value_cache), rows, context_length, base_position,
+                                      layer, count, _p(r, np.int64), r.size, int(kv_round_bf16))
+
+
+def rms_scale(x: np.ndarray) -> float:
+    x = np.ascontiguousarray(x, np.float32)
+    return float(load().q38o_rms_scale(_p(x), x.size))
+
+
+def l2norm(x: np.ndarray) -> None:
+    load().q38o_l2norm(_p(x), x.size)
+
+
+def rope(x: np.ndarray, heads: int, position: int) -> None:
+    load().q38o_rope(_p(x), heads, position)
+
+
+def sigmoid(x: float) -> float:
+    return float(load().q38o_sigmoid(x))
+
+
+def silu(x: float) -> float:
+    return float(load().q38o_silu(x))
+
+
+def softplus(x: float) -> float:
+    return float(load().q38o_softplus(x))
+
+
+def round_bf16(x: float) -> float:
+    return float(load().q38o_round_bf16(x))

@@ -1,0 +1,522 @@
+// attn_decode.cu -- gated full-attention decode (full_core, src/model/ops.rs:812-940)
+// as three stream-ordered kernels chained with programmatic dependent launch:
+//
+//   K1 attn_decode_prep   one CTA per (head, sequence): split q/gate, q/k RMSNorm
+//                         (f64 sum, ops.rs:476-498), partial RoPE with the
+//                         iterative f32 angle (ops.rs:595-610), KV append at
+//                         the sequence's position (ops.rs:858-866).
+//   K2 attn_decode_split  one CTA per (split, kv head, sequence): flash-decoding
+//                         over a contiguous range of cached positions. KV tiles
+//                         of 32 KB are staged global->shared by the bulk-copy
+//                         engine (cp.async.bulk + mbarrier, 3-deep ring). The 6
+//                         query heads of the GQA group share every tile. Pass 1
+//                         computes scores for the split (q in registers, FFMA2,
+//                         warp-shuffle transpose-reduce); per-head max and
+//                         exp-sum follow; pass 2 accumulates exp(s-m)*V.
+//                         Writes the partial (m, l, o) triple per head.
+//   K3 attn_decode_merge  one CTA per (head, sequence): LSE merge of the split
+//                         partials, normalisation and the sigmoid output gate
+//                         (ops.rs:915-919).
+//
+// HBM layout of one KV slot: [batch][kv_heads][context_length][256] in f32 or
+// bf16, so a split's range of one kv head is one contiguous byte range.
+#include "q38_common.cuh"
+
+#include <algorithm>
+#include <cstdlib>
+
+namespace q38 {
+namespace {
+
+constexpr int kThreads = 256;      // 8 warps
+constexpr int kWarps = kThreads / 32;
+constexpr int kTileBytes = 32768;  // one staged KV tile
+constexpr int kStages = 3;
+constexpr int kMaxChunk = 4096;    // positions per split (scores smem: chunk*32 B)
+constexpr int kMinSplitsCap = 64;
+
+template <typename KV>
+struct Tile {
+    static constexpr int kPositions = kTileBytes / (kAttnHeadDim * int(sizeof(KV)));  // 64 | 32
+    static constexpr int kPerWarp = kPositions / kWarps;                             // 8 | 4
+};
+
+__host__ __device__ inline int tile_positions(int kv_dtype) {
+    return kv_dtype == Q38_KV_BF16 ? 64 : 32;
+}
+
+// ----------------------------------------------------------------------------
+// K1: prep
+// ----------------------------------------------------------------------------
+struct PrepParams {
+    const float *q_and_gate;
+    float *key;
+    const float *value;
+    const int32_t *positions;
+    void *kcache, *vcache;
+    float *qprep;
+    int *err;
+    const float *q_norm, *k_norm;
+    int context_length, heads, kv_heads, max_position;
+    float theta_scale, eps;
+};
+
+template <typename KV>
+__global__ void __launch_bounds__(kAttnHeadDim) attn_decode_prep_kernel(PrepParams p) {
+    pdl_launch_dependents();
+    __shared__ double red[32];
+    __shared__ float cs[32], sn[32];
+    __shared__ float xs[kAttnHeadDim];
+    const int h = blockIdx.x, b = blockIdx.y, i = threadIdx.x;
+    const int pos = p.positions[b];
+    if (pos < 0 || pos >= p.context_length || pos > p.max_position) {
+        if (h == 0 && i == 0) set_error(p.err, kDevErrPosition);
+        return;
+    }
+    const bool is_q = h < p.heads;
+    const int kvh = h - p.heads;
+    float x = is_q ? p.q_and_gate[(size_t(b) * p.heads + h) * 2 * kAttnHeadDim + i]
+                   : p.key[(size_t(b) * p.kv_heads + kvh) * kAttnHeadDim + i];
+    // rmsnorm_inplace (ops.rs:493-498) with rms_scale's f64 accumulation.
+    const double sum = block_sum_f64(double(x) * double(x), red);
+    const float scale = rms_scale_from_sum(sum, kAttnHeadDim, p.eps);
+    x = x * scale * (is_q ? p.q_norm[i] : p.k_norm[i]);
+    // rope (ops.rs:595-610): theta_j = pos * scale^j by repeated f32 products.
+    if (i < kRopeDims / 2) {
+        float theta = float(pos);
+        for (int j = 0; j < i; ++j) theta *= p.theta_scale;
+        cs[i] = cosf(theta);
+        sn[i] = sinf(theta);
+    }
+    xs[i] = x;
+    __syncthreads();
+    if (i < kRopeDims / 2) {
+        x = xs[i] * cs[i] - xs[i + kRopeDims / 2] * sn[i];
+    } else if (i < kRopeDims) {
+        const int j = i - kRopeDims / 2;
+        x = xs[j] * sn[j] + xs[i] * cs[j];
+    }
+    if (is_q) {
+        p.qprep[(size_t(b) * p.heads + h) * kAttnHeadDim + i] = x;
+    } else {
+        const size_t kv_off = (size_t(b) * p.kv_heads + kvh) * kAttnHeadDim + i;
+        p.key[kv_off] = x;
+        const size_t row =
+            ((size_t(b) * p.kv_heads + kvh) * p.context_length + pos) * kAttnHeadDim + i;
+        static_cast<KV *>(p.kcache)[row] = KvTraits<KV>::store(x);
+        static_cast<KV *>(p.vcache)[row] = KvTraits<KV>::store(p.value[kv_off]);
+    }
+}
+
+// ----------------------------------------------------------------------------
+// K2: split-KV attention
+// ----------------------------------------------------------------------------
+struct SplitParams {
+    const void *kcache, *vcache;
+    const float *qprep;
+    const int32_t *positions;
+    float *part_o, *part_ml;
+    int *err;
+    int context_length, heads, kv_heads, chunk, max_splits, max_position;
+};
+
+// Dimension of the head that slot j (0..7) of lane `lane` owns. bf16 rows are
+// 512 B: lane l owns dims [8l, 8l+8), one 16-byte load. f32 rows are 1 KB:
+// lane l owns [4l, 4l+4) and [128+4l, 128+4l+4), two conflict-free 16-byte loads.
+template <typename KV>
+__device__ __forceinline__ int lane_dim(int lane, int j) {
+    if constexpr (sizeof(KV) == 2) {
+        return 8 * lane + j;
+    } else {
+        return j < 4 ? 4 * lane + j : 128 + 4 * lane + (j - 4);
+    }
+}
+
+// Loads the 8 elements of row `row` (a smem pointer to 256 elements) that
+// this lane owns, as 4 float pairs.
+template <typename KV>
+__device__ __forceinline__ void load_row8(const unsigned char *row, int lane, float2 (&v)[4]) {
+    if constexpr (sizeof(KV) == 2) {
+        const uint4 w = *reinterpret_cast<const uint4 *>(row + lane * 16);
+        v[0] = bf16x2_to_float2(w.x);
+        v[1] = bf16x2_to_float2(w.y);
+        v[2] = bf16x2_to_float2(w.z);
+        v[3] = bf16x2_to_float2(w.w);
+    } else {
+        const float4 a = *reinterpret_cast<const float4 *>(row + lane * 16);
+        const float4 c = *reinterpret_cast<const float4 *>(row + 512 + lane * 16);
+        v[0] = make_float2(a.x, a.y);
+        v[1] = make_float2(a.z, a.w);
+        v[2] = make_float2(c.x, c.y);
+        v[3] = make_float2(c.z, c.w);
+    }
+}
+
+// One halving step of the transpose-reduce: lanes whose `mask` bit is set keep
+// the upper half of the array, the others the lower half; each adds its
+// partner's copy of the half it keeps.
+template <int N>
+__device__ __forceinline__ void halve(const float (&in)[N], float (&out)[N / 2], int lane,
+                                      int mask) {
+    const bool up = (lane & mask) != 0;
+#pragma unroll
+    for (int i = 0; i < N / 2; ++i) {
+        const float keep = up ? in[N / 2 + i] : in[i];
+        const float send = up ? in[i] : in[N / 2 + i];
+        out[i] = keep + __shfl_xor_sync(0xffffffffu, send, mask);
+    }
+}
+
+// Reduces part[P][6] over the 32 lanes. On return the lane holds the totals
+// of position *pp and heads *h0..*h0+2, and *writer says whether it is the
+// lane that stores them.
+template <int P>
+__device__ __forceinline__ void transpose_reduce(const float (&part)[P * kGroup], int lane,
+                                                 float (&tot)[3], int *pp, int *h0,
+                                                 bool *writer) {
+    static_assert(P == 8 || P == 4, "positions per warp");
+    if constexpr (P == 8) {
+        float a[24], b[12], c[6];
+        halve<48>(part, a, lane, 16);
+        halve<24>(a, b, lane, 8);
+        halve<12>(b, c, lane, 4);
+        halve<6>(c, tot, lane, 2);
+#pragma unroll
+        for (int i = 0; i < 3; ++i) tot[i] += __shfl_xor_sync(0xffffffffu, tot[i], 1);
+        *pp = ((lane >> 4) & 1) * 4 + ((lane >> 3) & 1) * 2 + ((lane >> 2) & 1);
+        *h0 = ((lane >> 1) & 1) * 3;
+        *writer = (lane & 1) == 0;
+    } else {
+        float a[12], c[6];
+        halve<24>(part, a, lane, 16);
+        halve<12>(a, c, lane, 8);
+        halve<6>(c, tot, lane, 4);
+#pragma unroll
+        for (int i = 0; i < 3; ++i) {
+            tot[i] += __shfl_xor_sync(0xffffffffu, tot[i], 2);
+            tot[i] += __shfl_xor_sync(0xffffffffu, tot[i], 1);
+        }
+        *pp = ((lane >> 4) & 1) * 2 + ((lane >> 3) & 1);
+        *h0 = ((lane >> 2) & 1) * 3;
+        *writer = (lane & 3) == 0;
+    }
+}
+
+template <typename KV>
+__global__ void __launch_bounds__(kThreads) attn_decode_split_kernel(SplitParams p) {
+    using T = Tile<KV>;
+    constexpr int kRowBytes = kAttnHeadDim * int(sizeof(KV));
+    extern __shared__ __align__(128) unsigned char smem[];
+    unsigned char *stage = smem;                                      // kStages * 32 KB
+    float *scores = reinterpret_cast<float *>(smem + kStages * kTileBytes);  // [chunk][8]
+    __shared__ uint64_t bars[kStages];
+    __shared__ float ml_s[kGroup][2];
+    __shared__ volatile int abort_flag;
+
+    const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int pos = p.positions[b];
+    if (pos < 0 || pos >= p.context_length || pos > p.max_position) return;
+    const int n = pos + 1;
+    const int start = split * p.chunk;
+    if (start >= n) return;
+    const int cnt = min(n, start + p.chunk) - start;
+    const int ntiles = (cnt + T::kPositions - 1) / T::kPositions;
+    const int total_tiles = 2 * ntiles;
+
+    const size_t head_base = (size_t(b) * p.kv_heads + kvh) * p.context_length + start;
+    const unsigned char *kbase =
+        static_cast<const unsigned char *>(p.kcache) + head_base * kRowBytes;
+    const unsigned char *vbase =
+        static_cast<const unsigned char *>(p.vcache) + head_base * kRowBytes;
+
+    auto tile_rows = [&](int j) {
+        const int t = j < ntiles ? j : j - ntiles;
+        return min(T::kPositions, cnt - t * T::kPositions);
+    };
+    auto issue = [&](int j) {
+        const int t = j < ntiles ? j : j - ntiles;
+        const unsigned char *src = (j < ntiles ? kbase : vbase) + size_t(t) * kTileBytes;
+        const uint32_t bytes = uint32_t(tile_rows(j)) * kRowBytes;
+        mbar_arrive_expect_tx(&bars[j % kStages], bytes);
+        bulk_load(stage + (j % kStages) * kTileBytes, src, bytes, &bars[j % kStages]);
+    };
+
+    if (threadIdx.x == 0) {
+        abort_flag = 0;
+        for (int s = 0; s < kStages; ++s) mbar_init(&bars[s], 1);
+        fence_barrier_init();
+    }
+    __syncthreads();
+    // K1 wrote this sequence's new KV row and its prepared queries.
+    pdl_wait_primary();
+    if (threadIdx.x == 0) {
+        for (int j = 0; j < kStages && j < total_tiles; ++j) issue(j);
+    }
+
+    // Queries of the group, this lane's 8 dims, as float pairs.
+    float2 q2[kGroup][4];
+    {
+        const float *qg = p.qprep + (size_t(b) * p.heads + size_t(kvh) * kGroup) * kAttnHeadDim;
+#pragma unroll
+        for (int h = 0; h < kGroup; ++h)
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+                q2[h][j] = make_float2(qg[h * kAttnHeadDim + lane_dim<KV>(lane, 2 * j)],
+                                       qg[h * kAttnHeadDim + lane_dim<KV>(lane, 2 * j + 1)]);
+    }
+    const float score_scale = 1.0f / sqrtf(float(kAttnHeadDim));  // ops.rs:873
+
+    float2 acc[kGroup][4];
+#pragma unroll
+    for (int h = 0; h < kGroup; ++h)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[h][j] = make_float2(0.f, 0.f);
+
+    int waited = 0;  // tiles whose barrier this thread has passed
+    for (int j = 0; j < total_tiles; ++j) {
+        const int s = j % kStages;
+        if (!mbar_wait(&bars[s], uint32_t(j / kStages) & 1u)) {
+            abort_flag = 1;
+            set_error(p.err, kDevErrTimeout);
+        }
+        waited = j + 1;
+        const unsigned char *tile = stage + s * kTileBytes;
+        const int rows = tile_rows(j);
+        if (!abort_flag) {
+            if (j < ntiles) {
+                // Pass 1: scores of this warp's positions for the 6 heads.
+                float part[T::kPerWarp * kGroup];
+#pragma unroll
+                for (int pp = 0; pp < T::kPerWarp; ++pp) {
+                    const int pl = warp * T::kPerWarp + pp;
+                    float2 k2[4];
+                    if (pl < rows) {
+                        load_row8<KV>(tile + pl * kRowBytes, lane, k2);
+                    } else {
+#pragma unroll
+                        for (int jj = 0; jj < 4; ++jj) k2[jj] = make_float2(0.f, 0.f);
+                    }
+#pragma unroll
+                    for (int h = 0; h < kGroup; ++h) {
+                        float2 d = make_float2(0.f, 0.f);
+#pragma unroll
+                        for (int jj = 0; jj < 4; ++jj) d = ffma2(q2[h][jj], k2[jj], d);
+                        part[pp * kGroup + h] = d.x + d.y;
+                    }
+                }
+                float tot[3];
+                int pp, h0;
+                bool writer;
+                transpose_reduce<T::kPerWarp>(part, lane, tot, &pp, &h0, &writer);
+                const int pl = warp * T::kPerWarp + pp;
+                if (writer && pl < rows) {
+                    float *dst = scores + size_t(j * T::kPositions + pl) * 8 + h0;
+#pragma unroll
+                    for (int i = 0; i < 3; ++i) dst[i] = tot[i] * score_scale;
+                }
+            } else {
+                // Pass 2: acc[h] += exp(s-m)[h] * V.
+                const int t = j - ntiles;
+#pragma unroll
+                for (int pp = 0; pp < T::kPerWarp; ++pp) {
+                    const int pl = warp * T::kPerWarp + pp;
+                    if (pl < rows) {
+                        float2 v2[4];
+                        load_row8<KV>(tile + pl * kRowBytes, lane, v2);
+                        const float4 *e4 =
+                            reinterpret_cast<const float4 *>(scores + size_t(t * T::kPositions + pl) * 8);
+                        const float4 ea = e4[0], eb = e4[1];
+                        const float e[kGroup] = {ea.x, ea.y, ea.z, ea.w, eb.x, eb.y};
+#pragma unroll
+                        for (int h = 0; h < kGroup; ++h) {
+                            const float2 ee = make_float2(e[h], e[h]);
+#pragma unroll
+                            for (int jj = 0; jj < 4; ++jj) acc[h][jj] = ffma2(ee, v2[jj], acc[h][jj]);
+                        }
+                    }
+                }
+            }
+        }
+        __syncthreads();
+        if (abort_flag) break;
+        if (j == ntiles - 1) {
+            // Softmax statistics of the split: max and sum of exp(s - max).
+            if (warp < kGroup) {
+                float m = -INFINITY;
+                for (int q = lane; q < cnt; q += 32) m = fmaxf(m, scores[q * 8 + warp]);
+                m = warp_max(m);
+                float l = 0.f;
+                for (int q = lane; q < cnt; q += 32) {
+                    const float e = expf(scores[q * 8 + warp] - m);
+                    scores[q * 8 + warp] = e;
+                    l += e;
+                }
+                l = warp_sum(l);
+                if (lane == 0) {
+                    ml_s[warp][0] = m;
+                    ml_s[warp][1] = l;
+                }
+            }
+            __syncthreads();
+        }
+        if (threadIdx.x == 0 && j + kStages < total_tiles) issue(j + kStages);
+    }
+
+    if (abort_flag) {
+        // Let copies still in flight land before the CTA's shared memory is
+        // released (bounded as well).
+        if (threadIdx.x == 0) {
+            const int issued = min(total_tiles, waited + kStages - 1);
+            for (int j = max(0, waited - 1); j < issued; ++j)
+                (void)mbar_wait(&bars[j % kStages], uint32_t(j / kStages) & 1u);
+        }
+        return;
+    }
+
+    // Cross-warp reduction of acc through the (now idle) stage buffers.
+    float *red = reinterpret_cast<float *>(stage);  // [warps][6][256]
+#pragma unroll
+    for (int h = 0; h < kGroup; ++h)
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj) {
+            red[(warp * kGroup + h) * kAttnHeadDim + lane_dim<KV>(lane, 2 * jj)] = acc[h][jj].x;
+            red[(warp * kGroup + h) * kAttnHeadDim + lane_dim<KV>(lane, 2 * jj + 1)] = acc[h][jj].y;
+        }
+    __syncthreads();
+    const int d = threadIdx.x;
+#pragma unroll 1
+    for (int h = 0; h < kGroup; ++h) {
+        float o = 0.f;
+#pragma unroll
+        for (int w = 0; w < kWarps; ++w) o += red[(w * kGroup + h) * kAttnHeadDim + d];
+        const size_t slot = (size_t(b) * p.heads + size_t(kvh) * kGroup + h) * p.max_splits + split;
+        p.part_o[slot * kAttnHeadDim + d] = o;
+        if (d == 0) {
+            p.part_ml[slot * 2 + 0] = ml_s[h][0];
+            p.part_ml[slot * 2 + 1] = ml_s[h][1];
+        }
+    }
+}
+
+// ----------------------------------------------------------------------------
+// K3: merge + gate
+// ----------------------------------------------------------------------------
+struct MergeParams {
+    const float *part_o, *part_ml;
+    const float *q_and_gate;
+    const int32_t *positions;
+    float *attention;
+    int context_length, heads, chunk, max_splits, max_position;
+};
+
+__global__ void __launch_bounds__(kAttnHeadDim) attn_decode_merge_kernel(MergeParams p) {
+    const int h = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
+    const int pos = p.positions[b];
+    pdl_wait_primary();
+    if (pos < 0 || pos >= p.context_length || pos > p.max_position) return;
+    const int nsplit = (pos + p.chunk) / p.chunk;  // ceil((pos+1)/chunk)
+    const size_t base = (size_t(b) * p.heads + h) * p.max_splits;
+    const float2 *ml = reinterpret_cast<const float2 *>(p.part_ml) + base;
+    float m = -INFINITY;
+    for (int s = 0; s < nsplit; ++s) m = fmaxf(m, ml[s].x);
+    float l = 0.f, o = 0.f;
+    for (int s = 0; s < nsplit; ++s) {
+        const float2 v = ml[s];
+        const float w = expf(v.x - m);
+        l += w * v.y;
+        o += w * p.part_o[(base + s) * kAttnHeadDim + d];
+    }
+    const float gate = p.q_and_gate[(size_t(b) * p.heads + h) * 2 * kAttnHeadDim + kAttnHeadDim + d];
+    p.attention[(size_t(b) * p.heads + h) * kAttnHeadDim + d] = (o / l) * sigmoidf_ref(gate);
+}
+
+int env_chunk_override() {
+    static const int v = [] {
+        const char *s = std::getenv("Q38_DECODE_CHUNK");
+        return s ? std::atoi(s) : 0;
+    }();
+    return v;
+}
+
+template <typename KV>
+cudaError_t launch_typed(const AttnDecodeLaunch &a, int sm_count, cudaStream_t stream) {
+    const DecodeSplitPlan plan =
+        plan_attn_decode(a.batch, a.kv_heads, a.max_position, a.kv_dtype, sm_count);
+    if (plan.nsplit > a.max_splits) return cudaErrorInvalidValue;
+
+    PrepParams pp{a.q_and_gate, a.key,    a.value,    a.positions,  a.kcache,     a.vcache,
+                  a.qprep,      a.err,    a.q_norm,   a.k_norm,     a.context_length,
+                  a.heads,      a.kv_heads, a.max_position, a.theta_scale, a.eps};
+    attn_decode_prep_kernel<KV>
+        <<<dim3(a.heads + a.kv_heads, a.batch), kAttnHeadDim, 0, stream>>>(pp);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+
+    SplitParams sp{a.kcache, a.vcache, a.qprep,    a.positions,  a.part_o,   a.part_ml,
+                   a.err,    a.context_length, a.heads, a.kv_heads, plan.chunk,
+                   a.max_splits, a.max_position};
+    const size_t smem = size_t(kStages) * kTileBytes + size_t(plan.chunk) * 8 * sizeof(float);
+    e = cudaFuncSetAttribute(attn_decode_split_kernel<KV>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             int(size_t(kStages) * kTileBytes + size_t(kMaxChunk) * 32));
+    if (e != cudaSuccess) return e;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(plan.nsplit, a.kv_heads, a.batch);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, attn_decode_split_kernel<KV>, sp);
+    if (e != cudaSuccess) return e;
+
+    MergeParams mp{a.part_o, a.part_ml, a.q_and_gate, a.positions, a.attention,
+                   a.context_length, a.heads, plan.chunk, a.max_splits, a.max_position};
+    cfg.gridDim = dim3(a.heads, a.batch);
+    cfg.blockDim = dim3(kAttnHeadDim);
+    cfg.dynamicSmemBytes = 0;
+    return cudaLaunchKernelEx(&cfg, attn_decode_merge_kernel, mp);
+}
+
+}  // namespace
+
+int attn_decode_max_splits(int context_length, int kv_dtype) {
+    const int tile = tile_positions(kv_dtype);
+    const int by_tile = (context_length + tile - 1) / tile;
+    const int by_chunk = (context_length + kMaxChunk - 1) / kMaxChunk;
+    return std::min(by_tile, std::max(kMinSplitsCap, by_chunk));
+}
+
+DecodeSplitPlan plan_attn_decode(int batch, int kv_heads, int max_position, int kv_dtype,
+                                 int sm_count) {
+    const int tile = tile_positions(kv_dtype);
+    const int n = max_position + 1;
+    const int units = std::max(1, batch * kv_heads);
+    // Aim for at least two CTAs per SM over the whole grid.
+    const int want = std::max(1, (2 * sm_count + units - 1) / units);
+    int chunk = (n + want - 1) / want;
+    // Bound the number of splits (partial buffers are sized for it).
+    chunk = std::max(chunk, (n + kMinSplitsCap - 1) / kMinSplitsCap);
+    if (int o = env_chunk_override(); o > 0) chunk = o;
+    chunk = ((chunk + tile - 1) / tile) * tile;
+    chunk = std::min(std::max(chunk, tile), kMaxChunk);
+    // Never more splits than attn_decode_max_splits allows for this n.
+    const int cap = std::max(kMinSplitsCap, (n + kMaxChunk - 1) / kMaxChunk);
+    if ((n + chunk - 1) / chunk > cap) chunk = ((n + cap - 1) / cap + tile - 1) / tile * tile;
+    DecodeSplitPlan plan;
+    plan.chunk = chunk;
+    plan.nsplit = (n + chunk - 1) / chunk;
+    return plan;
+}
+
+cudaError_t launch_attn_decode(const AttnDecodeLaunch &a, int sm_count, cudaStream_t stream) {
+    if (a.kv_dtype == Q38_KV_BF16) return launch_typed<__nv_bfloat16>(a, sm_count, stream);
+    return launch_typed<float>(a, sm_count, stream);
+}
+
+}  // namespace q38

@@ -1,0 +1,111 @@
+// q38_internal.h -- host-side structures shared by the C-ABI layer and the
+// kernel launchers. Not part of the public ABI.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include <map>
+#include <string>
+
+#include "../../include/q38attn.h"
+
+namespace q38 {
+
+constexpr int kAttnHeadDim = 256;
+constexpr int kRopeDims = 64;
+constexpr int kGroup = 6;  // query heads per KV head (Q38_ATTN_HEADS / Q38_ATTN_KV_HEADS)
+constexpr int kLinHeadDim = 128;
+constexpr int kConvKernel = 4;
+
+struct FullWeights {
+    float *q_norm = nullptr;  // [256]
+    float *k_norm = nullptr;  // [256]
+};
+
+struct LinearWeights {
+    float *conv_w = nullptr;    // [qkv_dim][4]
+    float *dt_bias = nullptr;   // [v_heads]
+    float *ssm_a = nullptr;     // [v_heads]
+    float *ssm_norm = nullptr;  // [128]
+};
+
+// Split-KV decode launch configuration.
+struct DecodeSplitPlan {
+    int chunk = 0;   // positions per split CTA (multiple of the tile)
+    int nsplit = 0;  // split CTAs per (sequence, kv head)
+};
+
+}  // namespace q38
+
+struct q38_ctx {
+    int device = 0;
+    q38_geom geom{};
+    int sm_count = 0;
+    float theta_scale = 0.f;  // rope_theta^(-2/rope_dims), computed with powf
+    int qg_dim = 0, q_dim = 0, kv_dim = 0;
+    int qk_dim = 0, v_dim = 0, qkv_dim = 0;
+    std::map<int, q38::FullWeights> full;
+    std::map<int, q38::LinearWeights> linear;
+};
+
+struct q38_state {
+    q38_ctx *ctx = nullptr;
+    int batch = 0, context_length = 0, full_slots = 0, linear_slots = 0, kv_dtype = 0;
+    size_t kv_elem = 0;             // bytes per cache element
+    size_t kv_slot_elems = 0;       // batch*kv_heads*context_length*256
+    void *kcache = nullptr, *vcache = nullptr;
+    float *conv_state = nullptr;    // [linear_slots][batch][qkv_dim][3]
+    float *delta_state = nullptr;   // [linear_slots][batch][v_heads][128][128]
+    float *qprep = nullptr;         // [batch][heads][256]
+    float *part_o = nullptr;        // [batch][heads][max_splits][256]
+    float *part_ml = nullptr;       // [batch][heads][max_splits][2]
+    int max_splits = 0;
+    int *d_err = nullptr;           // device error bits
+    // staging for the host-pointer calls (device, sized for `batch`)
+    float *stage = nullptr;
+    size_t stage_floats = 0;
+    int32_t *stage_pos = nullptr;
+};
+
+namespace q38 {
+
+// Layer-kind helpers (src/model/ops.rs:39-47).
+inline bool is_full_attention(int layer) { return (layer + 1) % 4 == 0 || layer == 64; }
+inline int full_index(int layer) { return layer / 4; }
+inline int recurrent_index(int layer) { return layer - (layer + 1) / 4; }
+
+// Kernel launchers (attn_decode.cu, deltanet_decode.cu).
+struct AttnDecodeLaunch {
+    const float *q_and_gate;
+    float *key;
+    const float *value;
+    const int32_t *positions;
+    float *attention;
+    void *kcache;  // this slot: [batch][kv_heads][context_length][256]
+    void *vcache;
+    float *qprep, *part_o, *part_ml;
+    int *err;
+    const float *q_norm, *k_norm;
+    int batch, context_length, heads, kv_heads, kv_dtype, max_position, max_splits;
+    float theta_scale, eps;
+};
+cudaError_t launch_attn_decode(const AttnDecodeLaunch &a, int sm_count, cudaStream_t stream);
+DecodeSplitPlan plan_attn_decode(int batch, int kv_heads, int max_position, int kv_dtype,
+                                 int sm_count);
+int attn_decode_max_splits(int context_length, int kv_dtype);
+
+struct LinearDecodeLaunch {
+    float *qkv;
+    const float *z;
+    float *beta, *alpha, *attention;
+    float *conv_state;   // this slot: [batch][qkv_dim][3]
+    float *delta_state;  // this slot: [batch][v_heads][128][128]
+    const float *conv_w, *dt_bias, *ssm_a, *ssm_norm;
+    int batch, qk_heads, v_heads;
+    float eps;
+};
+cudaError_t launch_linear_decode(const LinearDecodeLaunch &a, cudaStream_t stream);
+
+}  // namespace q38

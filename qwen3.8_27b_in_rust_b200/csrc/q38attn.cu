@@ -1,0 +1,701 @@
+// q38attn.cu -- the C ABI (include/q38attn.h): context, weights, device state,
+// argument validation and the host-pointer mirrors of the reference's
+// linear_core / full_core. Kernels live in attn_decode.cu and
+// deltanet_decode.cu; nothing here computes on the CPU.
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "q38_internal.h"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char *fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    std::vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+    return code;
+}
+
+int cuda_fail(cudaError_t e, const char *what) {
+    cudaGetLastError();  // clear the sticky-free error so later calls start clean
+    return fail(Q38_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+#define Q38_CUDA(call)                                             \
+    do {                                                           \
+        cudaError_t e_ = (call);                                   \
+        if (e_ != cudaSuccess) return cuda_fail(e_, #call);        \
+    } while (0)
+
+// Makes `device` current for the duration of a call and restores the
+// caller's device afterwards.
+struct DeviceGuard {
+    int prev = -1, dev;
+    explicit DeviceGuard(int d) : dev(d) {
+        if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+        if (prev != dev) cudaSetDevice(dev);
+    }
+    ~DeviceGuard() {
+        if (prev >= 0 && prev != dev) cudaSetDevice(prev);
+    }
+};
+
+uint16_t f32_to_bf16_bits(float x) {
+    uint32_t u;
+    std::memcpy(&u, &x, 4);
+    if ((u & 0x7f800000u) == 0x7f800000u && (u & 0x007fffffu)) return uint16_t((u >> 16) | 0x40);
+    u += 0x7fffu + ((u >> 16) & 1u);
+    return uint16_t(u >> 16);
+}
+
+float bf16_bits_to_f32(uint16_t h) {
+    const uint32_t u = uint32_t(h) << 16;
+    float x;
+    std::memcpy(&x, &u, 4);
+    return x;
+}
+
+int check_geom(const q38_geom &g) {
+    if (g.attn_head_dim != q38::kAttnHeadDim || g.rope_dims != q38::kRopeDims)
+        return fail(Q38_ERR_ARG, "attention head_dim must be 256 with 64 RoPE dims");
+    if (g.attn_kv_heads <= 0 || g.attn_heads != q38::kGroup * g.attn_kv_heads)
+        return fail(Q38_ERR_ARG, "attn_heads must be 6 * attn_kv_heads (got %d, %d)",
+                    g.attn_heads, g.attn_kv_heads);
+    if (g.linear_head_dim != q38::kLinHeadDim || g.conv_kernel != q38::kConvKernel)
+        return fail(Q38_ERR_ARG, "DeltaNet head_dim must be 128 with a kernel-4 conv");
+    if (g.linear_qk_heads <= 0 || g.linear_v_heads <= 0 ||
+        g.linear_v_heads % g.linear_qk_heads != 0)
+        return fail(Q38_ERR_ARG, "linear_v_heads must be a positive multiple of linear_qk_heads");
+    if (!(g.rope_theta > 0.f) || !(g.rms_eps > 0.f))
+        return fail(Q38_ERR_ARG, "rope_theta and rms_eps must be positive");
+    return Q38_OK;
+}
+
+int check_ctx(const q38_ctx *ctx) {
+    if (!ctx) return fail(Q38_ERR_ARG, "null context");
+    return Q38_OK;
+}
+
+int check_state(const q38_ctx *ctx, const q38_state *st) {
+    if (int rc = check_ctx(ctx)) return rc;
+    if (!st) return fail(Q38_ERR_ARG, "null state");
+    if (st->ctx != ctx) return fail(Q38_ERR_ARG, "state belongs to another context");
+    return Q38_OK;
+}
+
+int full_slot_of(const q38_state *st, int layer, int *slot) {
+    if (layer < 0 || layer > 64 || !q38::is_full_attention(layer))
+        return fail(Q38_ERR_ARG, "layer %d is not a full-attention layer", layer);
+    const int s = q38::full_index(layer);
+    if (s >= st->full_slots)
+        return fail(Q38_ERR_ARG, "layer %d needs KV slot %d but the state has %d", layer, s,
+                    st->full_slots);
+    *slot = s;
+    return Q38_OK;
+}
+
+int linear_slot_of(const q38_state *st, int layer, int *slot) {
+    if (layer < 0 || layer >= 64 || q38::is_full_attention(layer))
+        return fail(Q38_ERR_ARG, "layer %d is not a Gated DeltaNet layer", layer);
+    const int s = q38::recurrent_index(layer);
+    if (s >= st->linear_slots)
+        return fail(Q38_ERR_ARG, "layer %d needs recurrent slot %d but the state has %d", layer,
+                    s, st->linear_slots);
+    *slot = s;
+    return Q38_OK;
+}
+
+size_t kv_seq_elems(const q38_state *st) {
+    return size_t(st->ctx->geom.attn_kv_heads) * st->context_length * q38::kAttnHeadDim;
+}
+
+unsigned char *kv_seq_base(const q38_state *st, void *cache, int slot, int seq) {
+    return static_cast<unsigned char *>(cache) +
+           (size_t(slot) * st->kv_slot_elems + size_t(seq) * kv_seq_elems(st)) * st->kv_elem;
+}
+
+size_t conv_seq_floats(const q38_ctx *ctx) { return size_t(ctx->qkv_dim) * 3; }
+size_t delta_seq_floats(const q38_ctx *ctx) {
+    return size_t(ctx->geom.linear_v_heads) * q38::kLinHeadDim * q38::kLinHeadDim;
+}
+
+template <typename T>
+int device_copy_of(const float *host, size_t n, T **dev) {
+    Q38_CUDA(cudaMalloc(dev, n * sizeof(float)));
+    Q38_CUDA(cudaMemcpy(*dev, host, n * sizeof(float), cudaMemcpyHostToDevice));
+    return Q38_OK;
+}
+
+void free_full(q38::FullWeights &w) {
+    cudaFree(w.q_norm);
+    cudaFree(w.k_norm);
+    w = {};
+}
+
+void free_linear(q38::LinearWeights &w) {
+    cudaFree(w.conv_w);
+    cudaFree(w.dt_bias);
+    cudaFree(w.ssm_a);
+    cudaFree(w.ssm_norm);
+    w = {};
+}
+
+void free_state(q38_state *st) {
+    cudaFree(st->kcache);
+    cudaFree(st->vcache);
+    cudaFree(st->conv_state);
+    cudaFree(st->delta_state);
+    cudaFree(st->qprep);
+    cudaFree(st->part_o);
+    cudaFree(st->part_ml);
+    cudaFree(st->d_err);
+    cudaFree(st->stage);
+    cudaFree(st->stage_pos);
+}
+
+// Validates a decode call and fills the launch arguments (device pointers).
+int prepare_full_decode(q38_ctx *ctx, q38_state *st, int layer, int batch,
+                        const float *q_and_gate, float *key, const float *value,
+                        const int32_t *positions, int max_position, float *attention,
+                        q38::AttnDecodeLaunch *a) {
+    if (int rc = check_state(ctx, st)) return rc;
+    int slot;
+    if (int rc = full_slot_of(st, layer, &slot)) return rc;
+    if (batch <= 0 || batch > st->batch)
+        return fail(Q38_ERR_ARG, "batch %d outside 1..%d", batch, st->batch);
+    if (!q_and_gate || !key || !value || !positions || !attention)
+        return fail(Q38_ERR_ARG, "null tensor argument");
+    auto it = ctx->full.find(layer);
+    if (it == ctx->full.end())
+        return fail(Q38_ERR_ARG, "full-attention layer %d has no bound weights", layer);
+    if (max_position < 0) max_position = st->context_length - 1;
+    if (max_position >= st->context_length)
+        return fail(Q38_ERR_ARG, "max_position %d >= context_length %d", max_position,
+                    st->context_length);
+    const q38_geom &g = ctx->geom;
+    *a = q38::AttnDecodeLaunch{};
+    a->q_and_gate = q_and_gate;
+    a->key = key;
+    a->value = value;
+    a->positions = positions;
+    a->attention = attention;
+    a->kcache = kv_seq_base(st, st->kcache, slot, 0);
+    a->vcache = kv_seq_base(st, st->vcache, slot, 0);
+    a->qprep = st->qprep;
+    a->part_o = st->part_o;
+    a->part_ml = st->part_ml;
+    a->err = st->d_err;
+    a->q_norm = it->second.q_norm;
+    a->k_norm = it->second.k_norm;
+    a->batch = batch;
+    a->context_length = st->context_length;
+    a->heads = g.attn_heads;
+    a->kv_heads = g.attn_kv_heads;
+    a->kv_dtype = st->kv_dtype;
+    a->max_position = max_position;
+    a->max_splits = st->max_splits;
+    a->theta_scale = ctx->theta_scale;
+    a->eps = g.rms_eps;
+    return Q38_OK;
+}
+
+int prepare_linear_decode(q38_ctx *ctx, q38_state *st, int layer, int batch, float *qkv,
+                          const float *z, float *beta, float *alpha, float *attention,
+                          q38::LinearDecodeLaunch *a) {
+    if (int rc = check_state(ctx, st)) return rc;
+    int slot;
+    if (int rc = linear_slot_of(st, layer, &slot)) return rc;
+    if (batch <= 0 || batch > st->batch)
+        return fail(Q38_ERR_ARG, "batch %d outside 1..%d", batch, st->batch);
+    if (!qkv || !z || !beta || !alpha || !attention)
+        return fail(Q38_ERR_ARG, "null tensor argument");
+    auto it = ctx->linear.find(layer);
+    if (it == ctx->linear.end())
+        return fail(Q38_ERR_ARG, "DeltaNet layer %d has no bound weights", layer);
+    const q38_geom &g = ctx->geom;
+    *a = q38::LinearDecodeLaunch{};
+    a->qkv = qkv;
+    a->z = z;
+    a->beta = beta;
+    a->alpha = alpha;
+    a->attention = attention;
+    a->conv_state = st->conv_state + size_t(slot) * st->batch * conv_seq_floats(ctx);
+    a->delta_state = st->delta_state + size_t(slot) * st->batch * delta_seq_floats(ctx);
+    a->conv_w = it->second.conv_w;
+    a->dt_bias = it->second.dt_bias;
+    a->ssm_a = it->second.ssm_a;
+    a->ssm_norm = it->second.ssm_norm;
+    a->batch = batch;
+    a->qk_heads = g.linear_qk_heads;
+    a->v_heads = g.linear_v_heads;
+    a->eps = g.rms_eps;
+    return Q38_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+void q38_geom_default(q38_geom *g) {
+    if (!g) return;
+    g->attn_heads = 24;
+    g->attn_kv_heads = 4;
+    g->attn_head_dim = 256;
+    g->rope_dims = 64;
+    g->rope_theta = 10000000.0f;
+    g->linear_qk_heads = 16;
+    g->linear_v_heads = 48;
+    g->linear_head_dim = 128;
+    g->conv_kernel = 4;
+    g->rms_eps = 1e-6f;
+}
+
+const char *q38_last_error(void) { return g_last_error.c_str(); }
+
+const char *q38_version(void) { return "q38attn 0.1.0 (sm_100a)"; }
+
+int q38_ctx_create(const q38_geom *geom, int device, q38_ctx **out) {
+    if (!out) return fail(Q38_ERR_ARG, "null output pointer");
+    *out = nullptr;
+    q38_geom g;
+    q38_geom_default(&g);
+    if (geom) g = *geom;
+    if (int rc = check_geom(g)) return rc;
+    int count = 0;
+    Q38_CUDA(cudaGetDeviceCount(&count));
+    if (device < 0 || device >= count)
+        return fail(Q38_ERR_ARG, "device %d outside 0..%d", device, count - 1);
+    DeviceGuard guard(device);
+    cudaDeviceProp prop;
+    Q38_CUDA(cudaGetDeviceProperties(&prop, device));
+    if (prop.major != 10)
+        return fail(Q38_ERR_ARG, "device %d is sm_%d%d; this library is built for sm_100a",
+                    device, prop.major, prop.minor);
+    q38_ctx *ctx = new q38_ctx();
+    ctx->device = device;
+    ctx->geom = g;
+    ctx->sm_count = prop.multiProcessorCount;
+    // rope(): theta_scale = theta^(-2/64) (ops.rs:596), evaluated with powf.
+    ctx->theta_scale = std::pow(g.rope_theta, -2.0f / float(g.rope_dims));
+    ctx->q_dim = g.attn_heads * g.attn_head_dim;
+    ctx->qg_dim = 2 * ctx->q_dim;
+    ctx->kv_dim = g.attn_kv_heads * g.attn_head_dim;
+    ctx->qk_dim = g.linear_qk_heads * g.linear_head_dim;
+    ctx->v_dim = g.linear_v_heads * g.linear_head_dim;
+    ctx->qkv_dim = 2 * ctx->qk_dim + ctx->v_dim;
+    *out = ctx;
+    return Q38_OK;
+}
+
+int q38_ctx_destroy(q38_ctx *ctx) {
+    if (!ctx) return Q38_OK;
+    {
+        DeviceGuard guard(ctx->device);
+        for (auto &kv : ctx->full) free_full(kv.second);
+        for (auto &kv : ctx->linear) free_linear(kv.second);
+    }
+    delete ctx;
+    return Q38_OK;
+}
+
+int q38_bind_full_layer(q38_ctx *ctx, int layer, const float *q_norm, const float *k_norm) {
+    if (int rc = check_ctx(ctx)) return rc;
+    if (layer < 0 || layer > 64 || !q38::is_full_attention(layer))
+        return fail(Q38_ERR_ARG, "layer %d is not a full-attention layer", layer);
+    if (!q_norm || !k_norm) return fail(Q38_ERR_ARG, "null weight");
+    DeviceGuard guard(ctx->device);
+    q38::FullWeights w;
+    int rc = device_copy_of(q_norm, q38::kAttnHeadDim, &w.q_norm);
+    if (!rc) rc = device_copy_of(k_norm, q38::kAttnHeadDim, &w.k_norm);
+    if (rc) {
+        free_full(w);
+        return rc;
+    }
+    auto it = ctx->full.find(layer);
+    if (it != ctx->full.end()) free_full(it->second);
+    ctx->full[layer] = w;
+    return Q38_OK;
+}
+
+int q38_bind_linear_layer(q38_ctx *ctx, int layer, const float *conv1d, const float *dt_bias,
+                          const float *ssm_a, const float *ssm_norm) {
+    if (int rc = check_ctx(ctx)) return rc;
+    if (layer < 0 || layer >= 64 || q38::is_full_attention(layer))
+        return fail(Q38_ERR_ARG, "layer %d is not a Gated DeltaNet layer", layer);
+    if (!conv1d || !dt_bias || !ssm_a || !ssm_norm) return fail(Q38_ERR_ARG, "null weight");
+    DeviceGuard guard(ctx->device);
+    q38::LinearWeights w;
+    const size_t vh = size_t(ctx->geom.linear_v_heads);
+    int rc = device_copy_of(conv1d, size_t(ctx->qkv_dim) * q38::kConvKernel, &w.conv_w);
+    if (!rc) rc = device_copy_of(dt_bias, vh, &w.dt_bias);
+    if (!rc) rc = device_copy_of(ssm_a, vh, &w.ssm_a);
+    if (!rc) rc = device_copy_of(ssm_norm, q38::kLinHeadDim, &w.ssm_norm);
+    if (rc) {
+        free_linear(w);
+        return rc;
+    }
+    auto it = ctx->linear.find(layer);
+    if (it != ctx->linear.end()) free_linear(it->second);
+    ctx->linear[layer] = w;
+    return Q38_OK;
+}
+
+int q38_state_create(q38_ctx *ctx, int batch, int context_length, int full_slots,
+                     int linear_slots, int kv_dtype, q38_state **out) {
+    if (!out) return fail(Q38_ERR_ARG, "null output pointer");
+    *out = nullptr;
+    if (int rc = check_ctx(ctx)) return rc;
+    if (batch <= 0 || context_length <= 0 || full_slots < 0 || linear_slots < 0 ||
+        full_slots > 17 || linear_slots > 48)
+        return fail(Q38_ERR_ARG,
+                    "bad state shape (batch %d, context %d, full slots %d, linear slots %d)",
+                    batch, context_length, full_slots, linear_slots);
+    if (kv_dtype != Q38_KV_F32 && kv_dtype != Q38_KV_BF16)
+        return fail(Q38_ERR_ARG, "unknown kv_dtype %d", kv_dtype);
+    DeviceGuard guard(ctx->device);
+    q38_state *st = new q38_state();
+    st->ctx = ctx;
+    st->batch = batch;
+    st->context_length = context_length;
+    st->full_slots = full_slots;
+    st->linear_slots = linear_slots;
+    st->kv_dtype = kv_dtype;
+    st->kv_elem = kv_dtype == Q38_KV_BF16 ? 2 : 4;
+    st->kv_slot_elems = size_t(batch) * kv_seq_elems(st);
+    st->max_splits = q38::attn_decode_max_splits(context_length, kv_dtype);
+    const q38_geom &g = ctx->geom;
+    const size_t kv_bytes = size_t(full_slots) * st->kv_slot_elems * st->kv_elem;
+    const size_t conv_floats = size_t(linear_slots) * batch * conv_seq_floats(ctx);
+    const size_t delta_floats = size_t(linear_slots) * batch * delta_seq_floats(ctx);
+    const size_t parts = size_t(batch) * g.attn_heads * st->max_splits;
+    const size_t full_stage = size_t(ctx->qg_dim) + 2 * ctx->kv_dim + ctx->q_dim;
+    const size_t lin_stage = size_t(ctx->qkv_dim) + ctx->v_dim + 2 * g.linear_v_heads + ctx->v_dim;
+    st->stage_floats = size_t(batch) * (full_stage > lin_stage ? full_stage : lin_stage);
+    auto alloc = [&](void **p, size_t bytes) -> cudaError_t {
+        if (bytes == 0) return cudaSuccess;
+        cudaError_t e = cudaMalloc(p, bytes);
+        if (e == cudaSuccess) e = cudaMemset(*p, 0, bytes);
+        return e;
+    };
+    cudaError_t e = cudaSuccess;
+    if (e == cudaSuccess) e = alloc(&st->kcache, kv_bytes);
+    if (e == cudaSuccess) e = alloc(&st->vcache, kv_bytes);
+    if (e == cudaSuccess) e = alloc((void **)&st->conv_state, conv_floats * 4);
+    if (e == cudaSuccess) e = alloc((void **)&st->delta_state, delta_floats * 4);
+    if (e == cudaSuccess) e = alloc((void **)&st->qprep, size_t(batch) * ctx->q_dim * 4);
+    if (e == cudaSuccess) e = alloc((void **)&st->part_o, parts * q38::kAttnHeadDim * 4);
+    if (e == cudaSuccess) e = alloc((void **)&st->part_ml, parts * 2 * 4);
+    if (e == cudaSuccess) e = alloc((void **)&st->d_err, sizeof(int));
+    if (e == cudaSuccess) e = alloc((void **)&st->stage, st->stage_floats * 4);
+    if (e == cudaSuccess) e = alloc((void **)&st->stage_pos, size_t(batch) * 4);
+    if (e != cudaSuccess) {
+        free_state(st);
+        delete st;
+        return cuda_fail(e, "q38_state_create allocation");
+    }
+    *out = st;
+    return Q38_OK;
+}
+
+int q38_state_destroy(q38_state *st) {
+    if (!st) return Q38_OK;
+    {
+        DeviceGuard guard(st->ctx->device);
+        free_state(st);
+    }
+    delete st;
+    return Q38_OK;
+}
+
+int q38_state_reset(q38_state *st, void *stream) {
+    if (!st) return fail(Q38_ERR_ARG, "null state");
+    DeviceGuard guard(st->ctx->device);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const size_t kv_bytes = size_t(st->full_slots) * st->kv_slot_elems * st->kv_elem;
+    if (kv_bytes) {
+        Q38_CUDA(cudaMemsetAsync(st->kcache, 0, kv_bytes, s));
+        Q38_CUDA(cudaMemsetAsync(st->vcache, 0, kv_bytes, s));
+    }
+    const size_t n = size_t(st->linear_slots) * st->batch;
+    if (n) {
+        Q38_CUDA(cudaMemsetAsync(st->conv_state, 0, n * conv_seq_floats(st->ctx) * 4, s));
+        Q38_CUDA(cudaMemsetAsync(st->delta_state, 0, n * delta_seq_floats(st->ctx) * 4, s));
+    }
+    return Q38_OK;
+}
+
+int q38_state_errors(q38_state *st, int *bits) {
+    if (!st || !bits) return fail(Q38_ERR_ARG, "null argument");
+    DeviceGuard guard(st->ctx->device);
+    Q38_CUDA(cudaDeviceSynchronize());
+    Q38_CUDA(cudaMemcpy(bits, st->d_err, sizeof(int), cudaMemcpyDeviceToHost));
+    Q38_CUDA(cudaMemset(st->d_err, 0, sizeof(int)));
+    return Q38_OK;
+}
+
+int q38_state_full_slot(q38_state *st, int layer, void **key_cache, void **value_cache,
+                        size_t *bytes_each) {
+    if (!st) return fail(Q38_ERR_ARG, "null state");
+    int slot;
+    if (int rc = full_slot_of(st, layer, &slot)) return rc;
+    if (key_cache) *key_cache = kv_seq_base(st, st->kcache, slot, 0);
+    if (value_cache) *value_cache = kv_seq_base(st, st->vcache, slot, 0);
+    if (bytes_each) *bytes_each = st->kv_slot_elems * st->kv_elem;
+    return Q38_OK;
+}
+
+int q38_state_linear_slot(q38_state *st, int layer, float **conv_state, float **delta_state) {
+    if (!st) return fail(Q38_ERR_ARG, "null state");
+    int slot;
+    if (int rc = linear_slot_of(st, layer, &slot)) return rc;
+    if (conv_state) *conv_state = st->conv_state + size_t(slot) * st->batch * conv_seq_floats(st->ctx);
+    if (delta_state)
+        *delta_state = st->delta_state + size_t(slot) * st->batch * delta_seq_floats(st->ctx);
+    return Q38_OK;
+}
+
+int q38_state_upload_kv(q38_state *st, int layer, int seq, int first, int count,
+                        const float *key_rows, const float *value_rows) {
+    if (!st) return fail(Q38_ERR_ARG, "null state");
+    int slot;
+    if (int rc = full_slot_of(st, layer, &slot)) return rc;
+    if (seq < 0 || seq >= st->batch || first < 0 || count < 0 ||
+        size_t(first) + size_t(count) > size_t(st->context_length))
+        return fail(Q38_ERR_ARG, "KV rows [%d, %d) of sequence %d out of range", first,
+                    first + count, seq);
+    if (count == 0) return Q38_OK;
+    if (!key_rows || !value_rows) return fail(Q38_ERR_ARG, "null rows");
+    DeviceGuard guard(st->ctx->device);
+    const int kvh = st->ctx->geom.attn_kv_heads, D = q38::kAttnHeadDim;
+    const size_t row = size_t(kvh) * D;
+    for (int which = 0; which < 2; ++which) {
+        const float *src = which ? value_rows : key_rows;
+        unsigned char *base = kv_seq_base(st, which ? st->vcache : st->kcache, slot, seq);
+        if (st->kv_dtype == Q38_KV_F32) {
+            for (int h = 0; h < kvh; ++h)
+                Q38_CUDA(cudaMemcpy2D(base + (size_t(h) * st->context_length + first) * D * 4,
+                                      D * 4, src + size_t(h) * D, row * 4, D * 4, count,
+                                      cudaMemcpyHostToDevice));
+        } else {
+            std::vector<uint16_t> tmp(size_t(count) * row);
+            for (size_t i = 0; i < tmp.size(); ++i) tmp[i] = f32_to_bf16_bits(src[i]);
+            for (int h = 0; h < kvh; ++h)
+                Q38_CUDA(cudaMemcpy2D(base + (size_t(h) * st->context_length + first) * D * 2,
+                                      D * 2, tmp.data() + size_t(h) * D, row * 2, D * 2, count,
+                                      cudaMemcpyHostToDevice));
+        }
+    }
+    return Q38_OK;
+}
+
+int q38_state_download_kv(q38_state *st, int layer, int seq, int first, int count,
+                          float *key_rows, float *value_rows) {
+    if (!st) return fail(Q38_ERR_ARG, "null state");
+    int slot;
+    if (int rc = full_slot_of(st, layer, &slot)) return rc;
+    if (seq < 0 || seq >= st->batch || first < 0 || count < 0 ||
+        size_t(first) + size_t(count) > size_t(st->context_length))
+        return fail(Q38_ERR_ARG, "KV rows [%d, %d) of sequence %d out of range", first,
+                    first + count, seq);
+    if (count == 0) return Q38_OK;
+    if (!key_rows || !value_rows) return fail(Q38_ERR_ARG, "null rows");
+    DeviceGuard guard(st->ctx->device);
+    const int kvh = st->ctx->geom.attn_kv_heads, D = q38::kAttnHeadDim;
+    const size_t row = size_t(kvh) * D;
+    for (int which = 0; which < 2; ++which) {
+        float *dst = which ? value_rows : key_rows;
+        const unsigned char *base = kv_seq_base(st, which ? st->vcache : st->kcache, slot, seq);
+        if (st->kv_dtype == Q38_KV_F32) {
+            for (int h = 0; h < kvh; ++h)
+                Q38_CUDA(cudaMemcpy2D(dst + size_t(h) * D, row * 4,
+                                      base + (size_t(h) * st->context_length + first) * D * 4,
+                                      D * 4, D * 4, count, cudaMemcpyDeviceToHost));
+        } else {
+            std::vector<uint16_t> tmp(size_t(count) * row);
+            for (int h = 0; h < kvh; ++h)
+                Q38_CUDA(cudaMemcpy2D(tmp.data() + size_t(h) * D, row * 2,
+                                      base + (size_t(h) * st->context_length + first) * D * 2,
+                                      D * 2, D * 2, count, cudaMemcpyDeviceToHost));
+            for (size_t i = 0; i < tmp.size(); ++i) dst[i] = bf16_bits_to_f32(tmp[i]);
+        }
+    }
+    return Q38_OK;
+}
+
+int q38_state_upload_linear(q38_state *st, int layer, int seq, const float *conv_state,
+                            const float *delta_state) {
+    if (!st) return fail(Q38_ERR_ARG, "null state");
+    float *conv, *delta;
+    if (int rc = q38_state_linear_slot(st, layer, &conv, &delta)) return rc;
+    if (seq < 0 || seq >= st->batch) return fail(Q38_ERR_ARG, "sequence %d out of range", seq);
+    DeviceGuard guard(st->ctx->device);
+    const size_t cn = conv_seq_floats(st->ctx), dn = delta_seq_floats(st->ctx);
+    if (conv_state)
+        Q38_CUDA(cudaMemcpy(conv + size_t(seq) * cn, conv_state, cn * 4, cudaMemcpyHostToDevice));
+    if (delta_state)
+        Q38_CUDA(cudaMemcpy(delta + size_t(seq) * dn, delta_state, dn * 4, cudaMemcpyHostToDevice));
+    return Q38_OK;
+}
+
+int q38_state_download_linear(q38_state *st, int layer, int seq, float *conv_state,
+                              float *delta_state) {
+    if (!st) return fail(Q38_ERR_ARG, "null state");
+    float *conv, *delta;
+    if (int rc = q38_state_linear_slot(st, layer, &conv, &delta)) return rc;
+    if (seq < 0 || seq >= st->batch) return fail(Q38_ERR_ARG, "sequence %d out of range", seq);
+    DeviceGuard guard(st->ctx->device);
+    const size_t cn = conv_seq_floats(st->ctx), dn = delta_seq_floats(st->ctx);
+    if (conv_state)
+        Q38_CUDA(cudaMemcpy(conv_state, conv + size_t(seq) * cn, cn * 4, cudaMemcpyDeviceToHost));
+    if (delta_state)
+        Q38_CUDA(cudaMemcpy(delta_state, delta + size_t(seq) * dn, dn * 4, cudaMemcpyDeviceToHost));
+    return Q38_OK;
+}
+
+int q38_full_decode(q38_ctx *ctx, q38_state *st, int layer, int batch, const float *q_and_gate,
+                    float *key, const float *value, const int32_t *positions, int max_position,
+                    float *attention, void *stream) {
+    q38::AttnDecodeLaunch a;
+    if (int rc = prepare_full_decode(ctx, st, layer, batch, q_and_gate, key, value, positions,
+                                     max_position, attention, &a))
+        return rc;
+    DeviceGuard guard(ctx->device);
+    cudaError_t e = q38::launch_attn_decode(a, ctx->sm_count, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "full-attention decode launch");
+    return Q38_OK;
+}
+
+int q38_linear_decode(q38_ctx *ctx, q38_state *st, int layer, int batch, float *qkv,
+                      const float *z, float *beta, float *alpha, float *attention,
+                      void *stream) {
+    q38::LinearDecodeLaunch a;
+    if (int rc = prepare_linear_decode(ctx, st, layer, batch, qkv, z, beta, alpha, attention, &a))
+        return rc;
+    DeviceGuard guard(ctx->device);
+    cudaError_t e = q38::launch_linear_decode(a, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "DeltaNet decode launch");
+    return Q38_OK;
+}
+
+int q38_full_decode_host(q38_ctx *ctx, q38_state *st, int layer, int batch,
+                         const float *q_and_gate, float *key, const float *value,
+                         const int32_t *positions, float *attention, void *stream) {
+    if (int rc = check_state(ctx, st)) return rc;
+    if (batch <= 0 || batch > st->batch)
+        return fail(Q38_ERR_ARG, "batch %d outside 1..%d", batch, st->batch);
+    if (!q_and_gate || !key || !value || !positions || !attention)
+        return fail(Q38_ERR_ARG, "null tensor argument");
+    int max_pos = 0;
+    for (int b = 0; b < batch; ++b) {
+        if (positions[b] < 0 || positions[b] >= st->context_length)
+            return fail(Q38_ERR_ARG, "position %d of sequence %d outside the %d-position cache",
+                        positions[b], b, st->context_length);
+        max_pos = positions[b] > max_pos ? positions[b] : max_pos;
+    }
+    DeviceGuard guard(ctx->device);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const size_t nqg = size_t(batch) * ctx->qg_dim, nkv = size_t(batch) * ctx->kv_dim,
+                 nq = size_t(batch) * ctx->q_dim;
+    float *d_qg = st->stage, *d_k = d_qg + nqg, *d_v = d_k + nkv, *d_out = d_v + nkv;
+    Q38_CUDA(cudaMemcpyAsync(d_qg, q_and_gate, nqg * 4, cudaMemcpyHostToDevice, s));
+    Q38_CUDA(cudaMemcpyAsync(d_k, key, nkv * 4, cudaMemcpyHostToDevice, s));
+    Q38_CUDA(cudaMemcpyAsync(d_v, value, nkv * 4, cudaMemcpyHostToDevice, s));
+    Q38_CUDA(cudaMemcpyAsync(st->stage_pos, positions, size_t(batch) * 4, cudaMemcpyHostToDevice, s));
+    if (int rc = q38_full_decode(ctx, st, layer, batch, d_qg, d_k, d_v, st->stage_pos, max_pos,
+                                 d_out, stream))
+        return rc;
+    Q38_CUDA(cudaMemcpyAsync(attention, d_out, nq * 4, cudaMemcpyDeviceToHost, s));
+    Q38_CUDA(cudaMemcpyAsync(key, d_k, nkv * 4, cudaMemcpyDeviceToHost, s));
+    Q38_CUDA(cudaStreamSynchronize(s));
+    return Q38_OK;
+}
+
+int q38_linear_decode_host(q38_ctx *ctx, q38_state *st, int layer, int batch, float *qkv,
+                           const float *z, float *beta, float *alpha, float *attention,
+                           void *stream) {
+    if (int rc = check_state(ctx, st)) return rc;
+    if (batch <= 0 || batch > st->batch)
+        return fail(Q38_ERR_ARG, "batch %d outside 1..%d", batch, st->batch);
+    if (!qkv || !z || !beta || !alpha || !attention)
+        return fail(Q38_ERR_ARG, "null tensor argument");
+    DeviceGuard guard(ctx->device);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const size_t nqkv = size_t(batch) * ctx->qkv_dim, nv = size_t(batch) * ctx->v_dim,
+                 nh = size_t(batch) * ctx->geom.linear_v_heads;
+    float *d_qkv = st->stage, *d_z = d_qkv + nqkv, *d_b = d_z + nv, *d_a = d_b + nh,
+          *d_out = d_a + nh;
+    Q38_CUDA(cudaMemcpyAsync(d_qkv, qkv, nqkv * 4, cudaMemcpyHostToDevice, s));
+    Q38_CUDA(cudaMemcpyAsync(d_z, z, nv * 4, cudaMemcpyHostToDevice, s));
+    Q38_CUDA(cudaMemcpyAsync(d_b, beta, nh * 4, cudaMemcpyHostToDevice, s));
+    Q38_CUDA(cudaMemcpyAsync(d_a, alpha, nh * 4, cudaMemcpyHostToDevice, s));
+    if (int rc = q38_linear_decode(ctx, st, layer, batch, d_qkv, d_z, d_b, d_a, d_out, stream))
+        return rc;
+    Q38_CUDA(cudaMemcpyAsync(attention, d_out, nv * 4, cudaMemcpyDeviceToHost, s));
+    Q38_CUDA(cudaMemcpyAsync(qkv, d_qkv, nqkv * 4, cudaMemcpyDeviceToHost, s));
+    Q38_CUDA(cudaMemcpyAsync(beta, d_b, nh * 4, cudaMemcpyDeviceToHost, s));
+    Q38_CUDA(cudaMemcpyAsync(alpha, d_a, nh * 4, cudaMemcpyDeviceToHost, s));
+    Q38_CUDA(cudaStreamSynchronize(s));
+    return Q38_OK;
+}
+
+int q38_linear_core(q38_ctx *ctx, q38_state *st, int layer, float *conv_state,
+                    float *delta_state, float *qkv, const float *z, float *beta, float *alpha,
+                    float *attention) {
+    if (int rc = check_state(ctx, st)) return rc;
+    if (!conv_state || !delta_state) return fail(Q38_ERR_ARG, "null state slice");
+    if (int rc = q38_state_upload_linear(st, layer, 0, conv_state, delta_state)) return rc;
+    if (int rc = q38_linear_decode_host(ctx, st, layer, 1, qkv, z, beta, alpha, attention, nullptr))
+        return rc;
+    return q38_state_download_linear(st, layer, 0, conv_state, delta_state);
+}
+
+int q38_full_core(q38_ctx *ctx, q38_state *st, int layer, const float *q_and_gate, float *key,
+                  const float *value, float *q, float *gate, float *scores, float *attention,
+                  float *key_cache, float *value_cache, size_t cache_rows,
+                  size_t context_length, uint32_t current_position) {
+    (void)scores;  // scratch in the reference; its callers never read it
+    if (int rc = check_state(ctx, st)) return rc;
+    int slot;
+    if (int rc = full_slot_of(st, layer, &slot)) return rc;
+    if (!key_cache || !value_cache) return fail(Q38_ERR_ARG, "null cache");
+    // ops.rs:858-864: the cache row must lie inside the caller's cache.
+    const size_t row = size_t(q38::full_index(layer)) * context_length + current_position;
+    if (row + 1 > cache_rows)
+        return fail(Q38_ERR_ARG, "cache row %zu outside a %zu-row cache", row, cache_rows);
+    if (current_position >= uint32_t(st->context_length))
+        return fail(Q38_ERR_ARG, "position %u outside the state's %d-position cache",
+                    current_position, st->context_length);
+    const size_t kv = size_t(ctx->kv_dim);
+    const float *layer_k = key_cache + size_t(q38::full_index(layer)) * context_length * kv;
+    const float *layer_v = value_cache + size_t(q38::full_index(layer)) * context_length * kv;
+    if (int rc = q38_state_upload_kv(st, layer, 0, 0, int(current_position), layer_k, layer_v))
+        return rc;
+    const int32_t pos = int32_t(current_position);
+    if (int rc = q38_full_decode_host(ctx, st, layer, 1, q_and_gate, key, value, &pos, attention,
+                                      nullptr))
+        return rc;
+    if (int rc = q38_state_download_kv(st, layer, 0, pos, 1, key_cache + row * kv,
+                                       value_cache + row * kv))
+        return rc;
+    DeviceGuard guard(ctx->device);
+    if (q) Q38_CUDA(cudaMemcpy(q, st->qprep, size_t(ctx->q_dim) * 4, cudaMemcpyDeviceToHost));
+    if (gate) {
+        const int D = q38::kAttnHeadDim;
+        for (int h = 0; h < ctx->geom.attn_heads; ++h)
+            std::memcpy(gate + size_t(h) * D, q_and_gate + size_t(h) * 2 * D + D, D * 4);
+    }
+    return Q38_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,355 @@
+"""q38attn -- host-side mirror of the reference's attention hot path over the
+B200 C ABI (include/q38attn.h, libq38attn.so).
+
+The reference (StepfenShawn/qwen3.8_27b_in_rust) calls two crate-private
+functions per layer:
+
+* ``linear_core`` (src/model/ops.rs:647-742), the Gated DeltaNet step, and
+* ``full_core`` (src/model/ops.rs:812-940), the gated full-attention step,
+
+once per token, including inside the prefill loops (ops.rs:1088-1099,
+1156-1172). :class:`Context` exposes the same operations with the same names
+and argument meaning, backed only by the sm_100a kernels:
+
+* :meth:`Context.linear_core` / :meth:`Context.full_core` take host (numpy)
+  slices exactly like the Rust signatures and write every ``&mut`` argument
+  back; they are the parity surface.
+* :meth:`Context.linear_decode` / :meth:`Context.full_decode` take device
+  tensors for a batch of sequences whose state stays resident in a
+  :class:`State`; they are the serving surface.
+
+Errors follow the reference's convention: an argument error (the Rust
+``Err(-1)``) raises :class:`Q38Error` with ``code == -1``. There is no CPU
+fallback: without the built library or a B200 nothing runs.
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import Optional
+
+import numpy as np
+
+from ._lib import (Q38_DEVERR_POSITION, Q38_DEVERR_SHAPE, Q38_DEVERR_TIMEOUT, Q38_ERR_ARG,
+                   Q38_ERR_CUDA, Q38_ERR_TIMEOUT, Q38_KV_BF16, Q38_KV_F32, Q38_OK, Q38Error,
+                   Q38Geom, check, last_error, load)
+
+__all__ = [
+    "Context", "State", "Q38Error", "Q38Geom", "geometry", "load", "last_error",
+    "Q38_OK", "Q38_ERR_ARG", "Q38_ERR_CUDA", "Q38_ERR_TIMEOUT", "Q38_KV_F32", "Q38_KV_BF16",
+    "Q38_DEVERR_POSITION", "Q38_DEVERR_TIMEOUT", "Q38_DEVERR_SHAPE",
+    "is_full_attention", "full_index", "recurrent_index",
+]
+
+# Geometry of src/model/mod.rs:13-26.
+ATTN_HEADS = 24
+ATTN_KV_HEADS = 4
+ATTN_HEAD_DIM = 256
+ATTN_Q_DIM = 6144
+ATTN_QG_DIM = 12288
+ATTN_KV_DIM = 1024
+LINEAR_QK_HEADS = 16
+LINEAR_V_HEADS = 48
+LINEAR_HEAD_DIM = 128
+LINEAR_QK_DIM = 2048
+LINEAR_V_DIM = 6144
+LINEAR_QKV_DIM = 10240
+RMS_EPS = 1e-6
+FULL_SLOTS = 17     # Q38_TOTAL_FULL_LAYERS
+LINEAR_SLOTS = 48   # Q38_RECURRENT_LAYERS
+
+
+def is_full_attention(layer: int) -> bool:
+    """src/model/ops.rs:39-41."""
+    return (layer + 1) % 4 == 0 or layer == 64
+
+
+def full_index(layer: int) -> int:
+    return layer // 4
+
+
+def recurrent_index(layer: int) -> int:
+    """src/model/ops.rs:45-47."""
+    return layer - (layer + 1) // 4
+
+
+def geometry() -> Q38Geom:
+    g = Q38Geom()
+    load().q38_geom_default(ctypes.byref(g))
+    return g
+
+
+def _host_ptr(a, name: str, writable: bool = False, dtype=np.float32):
+    if a is None:
+        return None
+    if not isinstance(a, np.ndarray):
+        raise TypeError(f"{name} must be a numpy array")
+    if a.dtype != dtype or not a.flags.c_contiguous:
+        raise TypeError(f"{name} must be a C-contiguous {np.dtype(dtype).name} array")
+    if writable and not a.flags.writeable:
+        raise TypeError(f"{name} must be writable")
+    return ctypes.c_void_p(a.ctypes.data)
+
+
+def _host_len(a, n: int, name: str):
+    if a is not None and a.size < n:
+        raise Q38Error(Q38_ERR_ARG, f"{name} holds {a.size} values, needs {n}")
+
+
+def _dev_ptr(t, name: str, dtype_name: str = "float32"):
+    import torch
+    if not isinstance(t, torch.Tensor) or not t.is_cuda:
+        raise TypeError(f"{name} must be a CUDA tensor")
+    if str(t.dtype) != f"torch.{dtype_name}" or not t.is_contiguous():
+        raise TypeError(f"{name} must be a contiguous {dtype_name} CUDA tensor")
+    return ctypes.c_void_p(t.data_ptr())
+
+
+class _CudaArray:
+    """Minimal __cuda_array_interface__ holder for wrapping library memory."""
+
+    def __init__(self, ptr: int, shape: tuple, typestr: str):
+        self.__cuda_array_interface__ = {
+            "data": (int(ptr), False), "shape": tuple(shape), "typestr": typestr,
+            "strides": None, "version": 2,
+        }
+
+
+def _cai_tensor(ptr: int, shape: tuple, typestr: str):
+    import torch
+    return torch.as_tensor(_CudaArray(ptr, shape, typestr), device="cuda")
+
+
+def _stream_ptr(stream):
+    if stream is None:
+        import torch
+        return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    if isinstance(stream, int):
+        return ctypes.c_void_p(stream)
+    return ctypes.c_void_p(stream.cuda_stream)
+
+
+class State:
+    """Device-resident per-sequence state: KV caches, conv and delta states
+    (the Q38Model fields of src/model/mod.rs:155-158)."""
+
+    def __init__(self, ctx: "Context", batch: int, context_length: int,
+                 full_slots: int = FULL_SLOTS, linear_slots: int = LINEAR_SLOTS,
+                 kv_dtype: int = Q38_KV_F32):
+        self._lib = load()
+        self.ctx = ctx
+        self.batch = batch
+        self.context_length = context_length
+        self.full_slots = full_slots
+        self.linear_slots = linear_slots
+        self.kv_dtype = kv_dtype
+        h = ctypes.c_void_p()
+        check(self._lib.q38_state_create(ctx.handle, batch, context_length, full_slots,
+                                         linear_slots, kv_dtype, ctypes.byref(h)))
+        self.handle = h
+
+    def close(self) -> None:
+        if self.handle:
+            check(self._lib.q38_state_destroy(self.handle))
+            self.handle = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def reset(self, stream=None) -> None:
+        check(self._lib.q38_state_reset(self.handle, _stream_ptr(stream)))
+
+    def errors(self) -> int:
+        bits = ctypes.c_int(0)
+        check(self._lib.q38_state_errors(self.handle, ctypes.byref(bits)))
+        return bits.value
+
+    def full_slot_ptrs(self, layer: int):
+        k, v, n = ctypes.c_void_p(), ctypes.c_void_p(), ctypes.c_size_t()
+        check(self._lib.q38_state_full_slot(self.handle, layer, ctypes.byref(k),
+                                            ctypes.byref(v), ctypes.byref(n)))
+        return k.value, v.value, n.value
+
+    def linear_slot_ptrs(self, layer: int):
+        c, d = ctypes.c_void_p(), ctypes.c_void_p()
+        check(self._lib.q38_state_linear_slot(self.handle, layer, ctypes.byref(c),
+                                              ctypes.byref(d)))
+        return c.value, d.value
+
+    def kv_views(self, layer: int):
+        """Zero-copy torch views of one KV slot, [batch][kv_heads][context][256]
+        (bf16 or f32), for bulk device-side initialisation."""
+        import torch
+        k, v, _ = self.full_slot_ptrs(layer)
+        shape = (self.batch, ATTN_KV_HEADS, self.context_length, ATTN_HEAD_DIM)
+        if self.kv_dtype == Q38_KV_BF16:
+            return (_cai_tensor(k, shape, "<i2").view(torch.bfloat16),
+                    _cai_tensor(v, shape, "<i2").view(torch.bfloat16))
+        return _cai_tensor(k, shape, "<f4"), _cai_tensor(v, shape, "<f4")
+
+    def linear_views(self, layer: int):
+        """Zero-copy torch views of one recurrent slot: conv state
+        [batch][qkv_dim][3] and delta state [batch][v_heads][128][128], f32."""
+        c, d = self.linear_slot_ptrs(layer)
+        return (_cai_tensor(c, (self.batch, LINEAR_QKV_DIM, 3), "<f4"),
+                _cai_tensor(d, (self.batch, LINEAR_V_HEADS, LINEAR_HEAD_DIM, LINEAR_HEAD_DIM),
+                            "<f4"))
+
+    def upload_kv(self, layer: int, seq: int, first: int, key_rows: np.ndarray,
+                  value_rows: np.ndarray) -> None:
+        count = key_rows.shape[0] if key_rows.ndim > 1 else key_rows.size // ATTN_KV_DIM
+        check(self._lib.q38_state_upload_kv(self.handle, layer, seq, first, count,
+                                            _host_ptr(key_rows, "key_rows"),
+                                            _host_ptr(value_rows, "value_rows")))
+
+    def download_kv(self, layer: int, seq: int, first: int, count: int):
+        k = np.empty((count, ATTN_KV_DIM), np.float32)
+        v = np.empty((count, ATTN_KV_DIM), np.float32)
+        check(self._lib.q38_state_download_kv(self.handle, layer, seq, first, count,
+                                              _host_ptr(k, "k", True), _host_ptr(v, "v", True)))
+        return k, v
+
+    def upload_linear(self, layer: int, seq: int, conv_state: Optional[np.ndarray],
+                      delta_state: Optional[np.ndarray]) -> None:
+        check(self._lib.q38_state_upload_linear(self.handle, layer, seq,
+                                                _host_ptr(conv_state, "conv_state"),
+                                                _host_ptr(delta_state, "delta_state")))
+
+    def download_linear(self, layer: int, seq: int):
+        c = np.empty((LINEAR_QKV_DIM, 3), np.float32)
+        d = np.empty((LINEAR_V_HEADS, LINEAR_HEAD_DIM, LINEAR_HEAD_DIM), np.float32)
+        check(self._lib.q38_state_download_linear(self.handle, layer, seq,
+                                                  _host_ptr(c, "c", True),
+                                                  _host_ptr(d, "d", True)))
+        return c, d
+
+
+class Context:
+    """A device, the model geometry and the bound per-layer weights
+    (the weight half of Q38Model::bind, src/model/ops.rs:1450-1459)."""
+
+    def __init__(self, device: int = 0, geom: Optional[Q38Geom] = None):
+        self._lib = load()
+        h = ctypes.c_void_p()
+        check(self._lib.q38_ctx_create(ctypes.byref(geom) if geom is not None else None,
+                                       device, ctypes.byref(h)))
+        self.handle = h
+        self.device = device
+        self._states = []
+
+    def close(self) -> None:
+        if self.handle:
+            check(self._lib.q38_ctx_destroy(self.handle))
+            self.handle = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    # weights -------------------------------------------------------------
+    def bind_full_layer(self, layer: int, q_norm: np.ndarray, k_norm: np.ndarray) -> None:
+        _host_len(q_norm, ATTN_HEAD_DIM, "q_norm")
+        _host_len(k_norm, ATTN_HEAD_DIM, "k_norm")
+        check(self._lib.q38_bind_full_layer(self.handle, layer, _host_ptr(q_norm, "q_norm"),
+                                            _host_ptr(k_norm, "k_norm")))
+
+    def bind_linear_layer(self, layer: int, conv1d: np.ndarray, dt_bias: np.ndarray,
+                          ssm_a: np.ndarray, ssm_norm: np.ndarray) -> None:
+        _host_len(conv1d, LINEAR_QKV_DIM * 4, "conv1d")
+        _host_len(dt_bias, LINEAR_V_HEADS, "dt_bias")
+        _host_len(ssm_a, LINEAR_V_HEADS, "ssm_a")
+        _host_len(ssm_norm, LINEAR_HEAD_DIM, "ssm_norm")
+        check(self._lib.q38_bind_linear_layer(self.handle, layer, _host_ptr(conv1d, "conv1d"),
+                                              _host_ptr(dt_bias, "dt_bias"),
+                                              _host_ptr(ssm_a, "ssm_a"),
+                                              _host_ptr(ssm_norm, "ssm_norm")))
+
+    def state(self, batch: int, context_length: int, full_slots: int = FULL_SLOTS,
+              linear_slots: int = LINEAR_SLOTS, kv_dtype: int = Q38_KV_F32) -> State:
+        return State(self, batch, context_length, full_slots, linear_slots, kv_dtype)
+
+    # device, batched, stream-ordered --------------------------------------
+    def full_decode(self, state: State, layer: int, q_and_gate, key, value, positions,
+                    attention, max_position: int = -1, stream=None) -> None:
+        b = q_and_gate.shape[0]
+        check(self._lib.q38_full_decode(self.handle, state.handle, layer, b,
+                                        _dev_ptr(q_and_gate, "q_and_gate"),
+                                        _dev_ptr(key, "key"), _dev_ptr(value, "value"),
+                                        _dev_ptr(positions, "positions", "int32"),
+                                        max_position, _dev_ptr(attention, "attention"),
+                                        _stream_ptr(stream)))
+
+    def linear_decode(self, state: State, layer: int, qkv, z, beta, alpha, attention,
+                      stream=None) -> None:
+        b = qkv.shape[0]
+        check(self._lib.q38_linear_decode(self.handle, state.handle, layer, b,
+                                          _dev_ptr(qkv, "qkv"), _dev_ptr(z, "z"),
+                                          _dev_ptr(beta, "beta"), _dev_ptr(alpha, "alpha"),
+                                          _dev_ptr(attention, "attention"),
+                                          _stream_ptr(stream)))
+
+    # host pointers, batched, synchronous -----------------------------------
+    def full_decode_host(self, state: State, layer: int, q_and_gate: np.ndarray,
+                         key: np.ndarray, value: np.ndarray, positions: np.ndarray,
+                         attention: np.ndarray, stream=0) -> None:
+        b = q_and_gate.shape[0]
+        check(self._lib.q38_full_decode_host(
+            self.handle, state.handle, layer, b, _host_ptr(q_and_gate, "q_and_gate"),
+            _host_ptr(key, "key", True), _host_ptr(value, "value"),
+            _host_ptr(positions, "positions", dtype=np.int32),
+            _host_ptr(attention, "attention", True), _stream_ptr(stream)))
+
+    def linear_decode_host(self, state: State, layer: int, qkv: np.ndarray, z: np.ndarray,
+                           beta: np.ndarray, alpha: np.ndarray, attention: np.ndarray,
+                           stream=0) -> None:
+        b = qkv.shape[0]
+        check(self._lib.q38_linear_decode_host(
+            self.handle, state.handle, layer, b, _host_ptr(qkv, "qkv", True),
+            _host_ptr(z, "z"), _host_ptr(beta, "beta", True), _host_ptr(alpha, "alpha", True),
+            _host_ptr(attention, "attention", True), _stream_ptr(stream)))
+
+    # reference-signature mirrors (host slices) ------------------------------
+    def linear_core(self, state: State, layer: int, conv_state: np.ndarray,
+                    delta_state: np.ndarray, qkv: np.ndarray, z: np.ndarray, beta: np.ndarray,
+                    alpha: np.ndarray, attention: np.ndarray) -> None:
+        """linear_core(weights, conv_state, delta_state, qkv, z, beta, alpha,
+        attention), src/model/ops.rs:647-657: every &mut slice is updated."""
+        _host_len(conv_state, LINEAR_QKV_DIM * 3, "conv_state")
+        _host_len(delta_state, LINEAR_V_HEADS * LINEAR_HEAD_DIM ** 2, "delta_state")
+        _host_len(qkv, LINEAR_QKV_DIM, "qkv")
+        _host_len(z, LINEAR_V_DIM, "z")
+        _host_len(beta, LINEAR_V_HEADS, "beta")
+        _host_len(alpha, LINEAR_V_HEADS, "alpha")
+        _host_len(attention, LINEAR_V_DIM, "attention")
+        check(self._lib.q38_linear_core(
+            self.handle, state.handle, layer, _host_ptr(conv_state, "conv_state", True),
+            _host_ptr(delta_state, "delta_state", True), _host_ptr(qkv, "qkv", True),
+            _host_ptr(z, "z"), _host_ptr(beta, "beta", True), _host_ptr(alpha, "alpha", True),
+            _host_ptr(attention, "attention", True)))
+
+    def full_core(self, state: State, layer: int, q_and_gate: np.ndarray, key: np.ndarray,
+                  value: np.ndarray, q: Optional[np.ndarray], gate: Optional[np.ndarray],
+                  scores: Optional[np.ndarray], attention: np.ndarray, key_cache: np.ndarray,
+                  value_cache: np.ndarray, context_length: int, current_position: int) -> None:
+        """full_core(weights, q_and_gate, key, value, q, gate, scores, attention,
+        key_cache, value_cache, context_length, current_position, layer),
+        src/model/ops.rs:812-827. Raises Q38Error(-1) where the reference
+        returns Err(-1). ``scores`` is scratch and is left untouched."""
+        _host_len(q_and_gate, ATTN_QG_DIM, "q_and_gate")
+        _host_len(key, ATTN_KV_DIM, "key")
+        _host_len(value, ATTN_KV_DIM, "value")
+        _host_len(attention, ATTN_Q_DIM, "attention")
+        _host_len(q, ATTN_Q_DIM, "q")
+        _host_len(gate, ATTN_Q_DIM, "gate")
+        rows = min(key_cache.size, value_cache.size) // ATTN_KV_DIM
+        check(self._lib.q38_full_core(
+            self.handle, state.handle, layer, _host_ptr(q_and_gate, "q_and_gate"),
+            _host_ptr(key, "key", True), _host_ptr(value, "value"), _host_ptr(q, "q", True),
+            _host_ptr(gate, "gate", True), _host_ptr(scores, "scores", True),
+            _host_ptr(attention, "attention", True), _host_ptr(key_cache, "key_cache", True),
+            _host_ptr(value_cache, "value_cache", True), rows, context_length,
+            current_position))

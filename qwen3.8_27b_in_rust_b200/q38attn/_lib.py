@@ -1,0 +1,110 @@
+"""ctypes binding of libq38attn.so (include/q38attn.h).
+
+The library is loaded from the package directory; there is no fallback: if it
+is missing, loading raises and nothing computes.
+"""
+from __future__ import annotations
+
+import ctypes
+import threading
+from ctypes import POINTER, c_char_p, c_float, c_int, c_int32, c_size_t, c_uint32, c_void_p
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent.parent / "libq38attn.so"
+HEADER_PATH = Path(__file__).resolve().parents[2] / "include" / "q38attn.h"
+
+Q38_OK = 0
+Q38_ERR_ARG = -1
+Q38_ERR_CUDA = -2
+Q38_ERR_TIMEOUT = -3
+Q38_KV_F32 = 0
+Q38_KV_BF16 = 1
+Q38_DEVERR_POSITION = 1
+Q38_DEVERR_TIMEOUT = 2
+Q38_DEVERR_SHAPE = 4
+
+
+class Q38Geom(ctypes.Structure):
+    _fields_ = [
+        ("attn_heads", c_int32),
+        ("attn_kv_heads", c_int32),
+        ("attn_head_dim", c_int32),
+        ("rope_dims", c_int32),
+        ("rope_theta", c_float),
+        ("linear_qk_heads", c_int32),
+        ("linear_v_heads", c_int32),
+        ("linear_head_dim", c_int32),
+        ("conv_kernel", c_int32),
+        ("rms_eps", c_float),
+    ]
+
+
+class Q38Error(RuntimeError):
+    """A non-zero status from the C ABI (code -1 argument, -2 CUDA, -3 timeout)."""
+
+    def __init__(self, code: int, message: str):
+        super().__init__(f"q38attn error {code}: {message}")
+        self.code = code
+
+
+_FP = POINTER(c_float)
+_IP = POINTER(c_int32)
+_VP = c_void_p
+
+# name -> (restype, argtypes); every function in include/q38attn.h.
+SIGNATURES = {
+    "q38_geom_default": (None, [POINTER(Q38Geom)]),
+    "q38_last_error": (c_char_p, []),
+    "q38_version": (c_char_p, []),
+    "q38_ctx_create": (c_int, [POINTER(Q38Geom), c_int, POINTER(c_void_p)]),
+    "q38_ctx_destroy": (c_int, [_VP]),
+    "q38_bind_full_layer": (c_int, [_VP, c_int, _VP, _VP]),
+    "q38_bind_linear_layer": (c_int, [_VP, c_int, _VP, _VP, _VP, _VP]),
+    "q38_state_create": (c_int, [_VP, c_int, c_int, c_int, c_int, c_int, POINTER(c_void_p)]),
+    "q38_state_destroy": (c_int, [_VP]),
+    "q38_state_reset": (c_int, [_VP, _VP]),
+    "q38_state_errors": (c_int, [_VP, POINTER(c_int)]),
+    "q38_state_full_slot": (c_int, [_VP, c_int, POINTER(c_void_p), POINTER(c_void_p),
+                                    POINTER(c_size_t)]),
+    "q38_state_linear_slot": (c_int, [_VP, c_int, POINTER(c_void_p), POINTER(c_void_p)]),
+    "q38_state_upload_kv": (c_int, [_VP, c_int, c_int, c_int, c_int, _VP, _VP]),
+    "q38_state_download_kv": (c_int, [_VP, c_int, c_int, c_int, c_int, _VP, _VP]),
+    "q38_state_upload_linear": (c_int, [_VP, c_int, c_int, _VP, _VP]),
+    "q38_state_download_linear": (c_int, [_VP, c_int, c_int, _VP, _VP]),
+    "q38_full_decode": (c_int, [_VP, _VP, c_int, c_int, _VP, _VP, _VP, _VP, c_int, _VP, _VP]),
+    "q38_linear_decode": (c_int, [_VP, _VP, c_int, c_int, _VP, _VP, _VP, _VP, _VP, _VP]),
+    "q38_full_decode_host": (c_int, [_VP, _VP, c_int, c_int, _VP, _VP, _VP, _VP, _VP, _VP]),
+    "q38_linear_decode_host": (c_int, [_VP, _VP, c_int, c_int, _VP, _VP, _VP, _VP, _VP, _VP]),
+    "q38_linear_core": (c_int, [_VP, _VP, c_int, _VP, _VP, _VP, _VP, _VP, _VP, _VP]),
+    "q38_full_core": (c_int, [_VP, _VP, c_int, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP,
+                              c_size_t, c_size_t, c_uint32]),
+}
+
+_lock = threading.Lock()
+_lib = None
+
+
+def load() -> ctypes.CDLL:
+    """Loads libq38attn.so once and declares every exported signature."""
+    global _lib
+    with _lock:
+        if _lib is None:
+            if not LIB_PATH.exists():
+                raise FileNotFoundError(
+                    f"{LIB_PATH} is missing; build it with `python qwen3.8_27b_in_rust_b200/build.py`")
+            lib = ctypes.CDLL(str(LIB_PATH))
+            for name, (res, args) in SIGNATURES.items():
+                fn = getattr(lib, name)
+                fn.restype = res
+                fn.argtypes = args
+            _lib = lib
+        return _lib
+
+
+def last_error() -> str:
+    return load().q38_last_error().decode()
+
+
+def check(rc: int) -> None:
+    if rc != Q38_OK:
+        raise Q38Error(rc, last_error())
