@@ -176,6 +176,37 @@ int q38_linear_decode(q38_ctx *ctx, q38_state *st, int layer, int batch, float *
                       const float *z, float *beta, float *alpha, float *attention,
                       void *stream);
 
+/* One full-attention decode step that allocates no device memory at all.
+ * No counterpart in the reference: the reference runs on the CPU and owns
+ * its buffers; this entry point exists for GPU callers that cannot call
+ * cudaMalloc -- hosts that reserve all of HBM for their own memory pool or
+ * KV-block arena (a library cudaMalloc would fail there, or synchronise the
+ * device and stall their other streams, or create memory they cannot account
+ * for).
+ *
+ * Same computation as q38_full_decode for the reference geometry (24 query
+ * heads, 4 KV heads, head_dim 256), but without a q38_ctx or q38_state: the
+ * caller passes every input and output as DEVICE pointers, including the
+ * norm weights (q_norm/k_norm, 256 f32 each) and its own KV cache
+ * (key_cache/value_cache laid out [batch][4][context_length][256] in kv_dtype).
+ * error_bits is an optional device int that receives Q38_DEVERR_* bits (it is
+ * OR-ed into, never cleared; NULL to skip).
+ *
+ * The kernels' scratch (prepared queries and split-KV partials) lives in a
+ * fixed 16 MiB device array inside the library, held on every GPU that loads
+ * the library until the process exits. A call whose batch and max_position
+ * would need more than 16 MiB is rejected with Q38_ERR_ARG before any work.
+ * The first call on each device looks the array's address up
+ * (cudaGetSymbolAddress) and caches it; make that first call before any
+ * stream capture. All calls on a device share the array, which keeps the
+ * last call's contents (no call relies on it starting at zero): calls whose
+ * executions overlap on the GPU race on it, so order them on one stream. */
+int q38_full_decode_noalloc(const float *q_norm, const float *k_norm, void *key_cache,
+                            void *value_cache, int batch, int context_length, int kv_dtype,
+                            const float *q_and_gate, float *key, const float *value,
+                            const int32_t *positions, int max_position, float *attention,
+                            int *error_bits, void *stream);
+
 /* ---------------------------------------------------------- decode (host) */
 
 /* Host-pointer forms of the two decode calls: copy the step's inputs from

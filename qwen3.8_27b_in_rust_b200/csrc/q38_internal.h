@@ -76,6 +76,9 @@ inline bool is_full_attention(int layer) { return (layer + 1) % 4 == 0 || layer 
 inline int full_index(int layer) { return layer / 4; }
 inline int recurrent_index(int layer) { return layer - (layer + 1) / 4; }
 
+// Sets the calling thread's q38_last_error() message (q38attn.cu).
+void record_error(const char *msg);
+
 // Kernel launchers (attn_decode.cu, deltanet_decode.cu).
 struct AttnDecodeLaunch {
     const float *q_and_gate;

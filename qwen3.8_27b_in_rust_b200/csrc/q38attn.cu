@@ -245,6 +245,8 @@ int prepare_linear_decode(q38_ctx *ctx, q38_state *st, int layer, int batch, flo
 
 }  // namespace
 
+void q38::record_error(const char *msg) { g_last_error = msg ? msg : ""; }
+
 extern "C" {
 
 void q38_geom_default(q38_geom *g) {
