@@ -33,7 +33,8 @@ constexpr int kWarps = kThreads / 32;
 constexpr int kTileBytes = 32768;  // one staged KV tile
 constexpr int kStages = 3;
 constexpr int kMaxChunk = 4096;    // positions per split (scores smem: chunk*32 B)
-constexpr int kMinSplitsCap = 64;
+constexpr int kFastChunk = 512;    // largest chunk that keeps 2 CTAs per SM (112 KB smem)
+constexpr int kMinSplitsCap = 128;
 
 template <typename KV>
 struct Tile {
@@ -202,12 +203,74 @@ __device__ __forceinline__ void transpose_reduce(const float (&part)[P * kGroup]
     }
 }
 
+// Scores of this warp's kPerWarp positions (rows [pl0, pl0+kPerWarp) of the
+// tile) for the 6 heads, reduced over the warp; written to scores[][8].
+template <typename KV, bool kFull>
+__device__ __forceinline__ void score_rows(const unsigned char *tile, int rows, int pl0, int lane,
+                                           const float2 (&q2)[kGroup][4], float *score_rows_out,
+                                           float score_scale) {
+    using T = Tile<KV>;
+    constexpr int kRowBytes = kAttnHeadDim * int(sizeof(KV));
+    float part[T::kPerWarp * kGroup];
+#pragma unroll
+    for (int pp = 0; pp < T::kPerWarp; ++pp) {
+        float2 k2[4];
+        if (kFull || pl0 + pp < rows) {
+            load_row8<KV>(tile + (pl0 + pp) * kRowBytes, lane, k2);
+        } else {
+#pragma unroll
+            for (int jj = 0; jj < 4; ++jj) k2[jj] = make_float2(0.f, 0.f);
+        }
+#pragma unroll
+        for (int h = 0; h < kGroup; ++h) {
+            float2 d = make_float2(0.f, 0.f);
+#pragma unroll
+            for (int jj = 0; jj < 4; ++jj) d = ffma2(q2[h][jj], k2[jj], d);
+            part[pp * kGroup + h] = d.x + d.y;
+        }
+    }
+    float tot[3];
+    int pp, h0;
+    bool writer;
+    transpose_reduce<T::kPerWarp>(part, lane, tot, &pp, &h0, &writer);
+    if (writer && (kFull || pl0 + pp < rows)) {
+        float *dst = score_rows_out + (pl0 + pp) * 8 + h0;
+#pragma unroll
+        for (int i = 0; i < 3; ++i) dst[i] = tot[i] * score_scale;
+    }
+}
+
+// acc[h] += e[pos][h] * V[pos] over this warp's kPerWarp rows of the tile.
+template <typename KV, bool kFull>
+__device__ __forceinline__ void accumulate_rows(const unsigned char *tile, int rows, int pl0,
+                                                int lane, const float *e_rows,
+                                                float2 (&acc)[kGroup][4]) {
+    using T = Tile<KV>;
+    constexpr int kRowBytes = kAttnHeadDim * int(sizeof(KV));
+#pragma unroll
+    for (int pp = 0; pp < T::kPerWarp; ++pp) {
+        if (kFull || pl0 + pp < rows) {
+            float2 v2[4];
+            load_row8<KV>(tile + (pl0 + pp) * kRowBytes, lane, v2);
+            const float4 *e4 = reinterpret_cast<const float4 *>(e_rows + (pl0 + pp) * 8);
+            const float4 ea = e4[0], eb = e4[1];
+            const float e[kGroup] = {ea.x, ea.y, ea.z, ea.w, eb.x, eb.y};
+#pragma unroll
+            for (int h = 0; h < kGroup; ++h) {
+                const float2 ee = make_float2(e[h], e[h]);
+#pragma unroll
+                for (int jj = 0; jj < 4; ++jj) acc[h][jj] = ffma2(ee, v2[jj], acc[h][jj]);
+            }
+        }
+    }
+}
+
 template <typename KV>
-__global__ void __launch_bounds__(kThreads) attn_decode_split_kernel(SplitParams p) {
+__global__ void __launch_bounds__(kThreads, 2) attn_decode_split_kernel(SplitParams p) {
     using T = Tile<KV>;
     constexpr int kRowBytes = kAttnHeadDim * int(sizeof(KV));
     extern __shared__ __align__(128) unsigned char smem[];
-    unsigned char *stage = smem;                                      // kStages * 32 KB
+    unsigned char *stage = smem;                                             // kStages * 32 KB
     float *scores = reinterpret_cast<float *>(smem + kStages * kTileBytes);  // [chunk][8]
     __shared__ uint64_t bars[kStages];
     __shared__ float ml_s[kGroup][2];
@@ -230,6 +293,7 @@ __global__ void __launch_bounds__(kThreads) attn_decode_split_kernel(SplitParams
     const unsigned char *vbase =
         static_cast<const unsigned char *>(p.vcache) + head_base * kRowBytes;
 
+    // Tile j < ntiles is K tile j, tile j >= ntiles is V tile j - ntiles.
     auto tile_rows = [&](int j) {
         const int t = j < ntiles ? j : j - ntiles;
         return min(T::kPositions, cnt - t * T::kPositions);
@@ -240,6 +304,18 @@ __global__ void __launch_bounds__(kThreads) attn_decode_split_kernel(SplitParams
         const uint32_t bytes = uint32_t(tile_rows(j)) * kRowBytes;
         mbar_arrive_expect_tx(&bars[j % kStages], bytes);
         bulk_load(stage + (j % kStages) * kTileBytes, src, bytes, &bars[j % kStages]);
+    };
+    // Waits for tile j; false (and the CTA-wide abort flag set) on timeout.
+    auto wait_tile = [&](int j) {
+        if (!mbar_wait(&bars[j % kStages], uint32_t(j / kStages) & 1u)) {
+            abort_flag = 1;
+            set_error(p.err, kDevErrTimeout);
+        }
+    };
+    // After every thread is done with tile j's stage: refill it with tile j+kStages.
+    auto release = [&](int j) {
+        __syncthreads();
+        if (threadIdx.x == 0 && !abort_flag && j + kStages < total_tiles) issue(j + kStages);
     };
 
     if (threadIdx.x == 0) {
@@ -253,10 +329,13 @@ __global__ void __launch_bounds__(kThreads) attn_decode_split_kernel(SplitParams
     if (threadIdx.x == 0) {
         for (int j = 0; j < kStages && j < total_tiles; ++j) issue(j);
     }
+    const float score_scale = 1.0f / sqrtf(float(kAttnHeadDim));  // ops.rs:873
+    const int pl0 = warp * T::kPerWarp;
+    int next = 0;  // first tile not yet waited for
 
-    // Queries of the group, this lane's 8 dims, as float pairs.
-    float2 q2[kGroup][4];
+    // Pass 1: scores of the split's positions for the 6 heads of the group.
     {
+        float2 q2[kGroup][4];
         const float *qg = p.qprep + (size_t(b) * p.heads + size_t(kvh) * kGroup) * kAttnHeadDim;
 #pragma unroll
         for (int h = 0; h < kGroup; ++h)
@@ -264,111 +343,74 @@ __global__ void __launch_bounds__(kThreads) attn_decode_split_kernel(SplitParams
             for (int j = 0; j < 4; ++j)
                 q2[h][j] = make_float2(qg[h * kAttnHeadDim + lane_dim<KV>(lane, 2 * j)],
                                        qg[h * kAttnHeadDim + lane_dim<KV>(lane, 2 * j + 1)]);
+        for (int j = 0; j < ntiles; ++j) {
+            wait_tile(j);
+            next = j + 1;
+            if (!abort_flag) {
+                const unsigned char *tile = stage + (j % kStages) * kTileBytes;
+                float *out = scores + size_t(j) * T::kPositions * 8;
+                const int rows = tile_rows(j);
+                if (rows == T::kPositions)
+                    score_rows<KV, true>(tile, rows, pl0, lane, q2, out, score_scale);
+                else
+                    score_rows<KV, false>(tile, rows, pl0, lane, q2, out, score_scale);
+            }
+            release(j);
+            if (abort_flag) break;
+        }
     }
-    const float score_scale = 1.0f / sqrtf(float(kAttnHeadDim));  // ops.rs:873
 
+    // Softmax statistics of the split: max and sum of exp(s - max); scores
+    // are replaced by exp(s - max).
+    if (!abort_flag && warp < kGroup) {
+        float m = -INFINITY;
+        for (int q = lane; q < cnt; q += 32) m = fmaxf(m, scores[q * 8 + warp]);
+        m = warp_max(m);
+        float l = 0.f;
+        for (int q = lane; q < cnt; q += 32) {
+            const float e = expf(scores[q * 8 + warp] - m);
+            scores[q * 8 + warp] = e;
+            l += e;
+        }
+        l = warp_sum(l);
+        if (lane == 0) {
+            ml_s[warp][0] = m;
+            ml_s[warp][1] = l;
+        }
+    }
+    __syncthreads();
+
+    // Pass 2: acc[h] += exp(s-m)[h] * V.
     float2 acc[kGroup][4];
 #pragma unroll
     for (int h = 0; h < kGroup; ++h)
 #pragma unroll
         for (int j = 0; j < 4; ++j) acc[h][j] = make_float2(0.f, 0.f);
-
-    int waited = 0;  // tiles whose barrier this thread has passed
-    for (int j = 0; j < total_tiles; ++j) {
-        const int s = j % kStages;
-        if (!mbar_wait(&bars[s], uint32_t(j / kStages) & 1u)) {
-            abort_flag = 1;
-            set_error(p.err, kDevErrTimeout);
-        }
-        waited = j + 1;
-        const unsigned char *tile = stage + s * kTileBytes;
-        const int rows = tile_rows(j);
-        if (!abort_flag) {
-            if (j < ntiles) {
-                // Pass 1: scores of this warp's positions for the 6 heads.
-                float part[T::kPerWarp * kGroup];
-#pragma unroll
-                for (int pp = 0; pp < T::kPerWarp; ++pp) {
-                    const int pl = warp * T::kPerWarp + pp;
-                    float2 k2[4];
-                    if (pl < rows) {
-                        load_row8<KV>(tile + pl * kRowBytes, lane, k2);
-                    } else {
-#pragma unroll
-                        for (int jj = 0; jj < 4; ++jj) k2[jj] = make_float2(0.f, 0.f);
-                    }
-#pragma unroll
-                    for (int h = 0; h < kGroup; ++h) {
-                        float2 d = make_float2(0.f, 0.f);
-#pragma unroll
-                        for (int jj = 0; jj < 4; ++jj) d = ffma2(q2[h][jj], k2[jj], d);
-                        part[pp * kGroup + h] = d.x + d.y;
-                    }
-                }
-                float tot[3];
-                int pp, h0;
-                bool writer;
-                transpose_reduce<T::kPerWarp>(part, lane, tot, &pp, &h0, &writer);
-                const int pl = warp * T::kPerWarp + pp;
-                if (writer && pl < rows) {
-                    float *dst = scores + size_t(j * T::kPositions + pl) * 8 + h0;
-#pragma unroll
-                    for (int i = 0; i < 3; ++i) dst[i] = tot[i] * score_scale;
-                }
-            } else {
-                // Pass 2: acc[h] += exp(s-m)[h] * V.
+    if (!abort_flag) {
+        for (int j = ntiles; j < total_tiles; ++j) {
+            wait_tile(j);
+            next = j + 1;
+            if (!abort_flag) {
                 const int t = j - ntiles;
-#pragma unroll
-                for (int pp = 0; pp < T::kPerWarp; ++pp) {
-                    const int pl = warp * T::kPerWarp + pp;
-                    if (pl < rows) {
-                        float2 v2[4];
-                        load_row8<KV>(tile + pl * kRowBytes, lane, v2);
-                        const float4 *e4 =
-                            reinterpret_cast<const float4 *>(scores + size_t(t * T::kPositions + pl) * 8);
-                        const float4 ea = e4[0], eb = e4[1];
-                        const float e[kGroup] = {ea.x, ea.y, ea.z, ea.w, eb.x, eb.y};
-#pragma unroll
-                        for (int h = 0; h < kGroup; ++h) {
-                            const float2 ee = make_float2(e[h], e[h]);
-#pragma unroll
-                            for (int jj = 0; jj < 4; ++jj) acc[h][jj] = ffma2(ee, v2[jj], acc[h][jj]);
-                        }
-                    }
-                }
+                const unsigned char *tile = stage + (j % kStages) * kTileBytes;
+                const float *e_rows = scores + size_t(t) * T::kPositions * 8;
+                const int rows = tile_rows(j);
+                if (rows == T::kPositions)
+                    accumulate_rows<KV, true>(tile, rows, pl0, lane, e_rows, acc);
+                else
+                    accumulate_rows<KV, false>(tile, rows, pl0, lane, e_rows, acc);
             }
+            release(j);
+            if (abort_flag) break;
         }
-        __syncthreads();
-        if (abort_flag) break;
-        if (j == ntiles - 1) {
-            // Softmax statistics of the split: max and sum of exp(s - max).
-            if (warp < kGroup) {
-                float m = -INFINITY;
-                for (int q = lane; q < cnt; q += 32) m = fmaxf(m, scores[q * 8 + warp]);
-                m = warp_max(m);
-                float l = 0.f;
-                for (int q = lane; q < cnt; q += 32) {
-                    const float e = expf(scores[q * 8 + warp] - m);
-                    scores[q * 8 + warp] = e;
-                    l += e;
-                }
-                l = warp_sum(l);
-                if (lane == 0) {
-                    ml_s[warp][0] = m;
-                    ml_s[warp][1] = l;
-                }
-            }
-            __syncthreads();
-        }
-        if (threadIdx.x == 0 && j + kStages < total_tiles) issue(j + kStages);
     }
 
     if (abort_flag) {
         // Let copies still in flight land before the CTA's shared memory is
         // released (bounded as well).
         if (threadIdx.x == 0) {
-            const int issued = min(total_tiles, waited + kStages - 1);
-            for (int j = max(0, waited - 1); j < issued; ++j)
+            const int issued = min(total_tiles, next + kStages - 1);
+            for (int j = max(0, next - 1); j < issued; ++j)
                 (void)mbar_wait(&bars[j % kStages], uint32_t(j / kStages) & 1u);
         }
         return;
@@ -504,7 +546,7 @@ DecodeSplitPlan plan_attn_decode(int batch, int kv_heads, int max_position, int 
     chunk = std::max(chunk, (n + kMinSplitsCap - 1) / kMinSplitsCap);
     if (int o = env_chunk_override(); o > 0) chunk = o;
     chunk = ((chunk + tile - 1) / tile) * tile;
-    chunk = std::min(std::max(chunk, tile), kMaxChunk);
+    chunk = std::min(std::max(chunk, tile), env_chunk_override() > 0 ? kMaxChunk : kFastChunk);
     // Never more splits than attn_decode_max_splits allows for this n.
     const int cap = std::max(kMinSplitsCap, (n + kMaxChunk - 1) / kMaxChunk);
     if ((n + chunk - 1) / chunk > cap) chunk = ((n + cap - 1) / cap + tile - 1) / tile * tile;
