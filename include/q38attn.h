@@ -207,6 +207,30 @@ int q38_full_decode_noalloc(const float *q_norm, const float *k_norm, void *key_
                             const int32_t *positions, int max_position, float *attention,
                             int *error_bits, void *stream);
 
+/* ------------------------------------------------------------ prefill */
+
+/* Reserves the state's prefill scratch for up to max_tokens prompt tokens
+ * per call (summed over the sequences of the call): the bf16 prepared
+ * queries, 12 KB per token. Allocates; call it once at set-up. */
+int q38_state_reserve_prefill(q38_state *st, int max_tokens);
+
+/* Causal prefill of `count` prompt tokens for each of the nseq sequences
+ * seq0..seq0+nseq-1, all starting at cache position base_position: token t
+ * attends to positions 0..base_position+t, exactly as the reference's
+ * per-token loop over full_core (batch_full_attention, ops.rs:1156-1172).
+ * Runs on the tcgen05 tensor cores with bf16 Q/K/V/P and f32 accumulation;
+ * needs a Q38_KV_BF16 state and q38_state_reserve_prefill(nseq*count).
+ * DEVICE pointers, token-major per sequence:
+ *   q_and_gate [nseq][count][heads*512]
+ *   key        [nseq][count][kv_heads*256] in: projections; out: RMSNorm+RoPE'd
+ *   value      [nseq][count][kv_heads*256]
+ *   attention  [nseq][count][heads*256]  output
+ * The K/V rows of positions base_position..base_position+count-1 are
+ * appended to the cache. */
+int q38_full_prefill(q38_ctx *ctx, q38_state *st, int layer, int seq0, int nseq, int count,
+                     int base_position, const float *q_and_gate, float *key, const float *value,
+                     float *attention, void *stream);
+
 /* ---------------------------------------------------------- decode (host) */
 
 /* Host-pointer forms of the two decode calls: copy the step's inputs from

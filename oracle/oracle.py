@@ -115,7 +115,9 @@ def full_core(w: dict, q_and_gate, key, value, q, gate, scores, attention, key_c
 
 def full_prefill(w: dict, q_and_gate, key, value, attention, key_cache, value_cache,
                  context_length: int, base_position: int, layer: int,
-                 kv_round_bf16: bool = False, rows_wanted=None) -> int:
+                 kv_round_bf16: int = 0, rows_wanted=None) -> int:
+    """Per-token loop of batch_full_attention (ops.rs:1156-1172). kv_round_bf16:
+    bit 0 rounds the stored K/V rows to bf16, bit 1 also rounds the query."""
     rows = min(key_cache.size, value_cache.size) // KV
     count = q_and_gate.size // QG
     lib = load()

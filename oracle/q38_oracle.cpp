@@ -166,6 +166,8 @@ int full_core_prepare(const float *q_norm, const float *k_norm, const float *q_a
         rmsnorm_inplace(key + h * Q38O_ATTN_HEAD_DIM, k_norm, Q38O_ATTN_HEAD_DIM);
     rope(q, Q38O_ATTN_HEADS, position);
     rope(key, Q38O_ATTN_KV_HEADS, position);
+    if (kv_round_bf16 & 2)
+        for (int i = 0; i < Q38O_ATTN_Q_DIM; ++i) q[i] = round_bf16(q[i]);
 
     const size_t full_index = layer / 4;
     const size_t row = full_index * context_length + size_t(position);
@@ -173,8 +175,8 @@ int full_core_prepare(const float *q_norm, const float *k_norm, const float *q_a
     float *kc = key_cache + row * Q38O_ATTN_KV_DIM;
     float *vc = value_cache + row * Q38O_ATTN_KV_DIM;
     for (int i = 0; i < Q38O_ATTN_KV_DIM; ++i) {
-        kc[i] = kv_round_bf16 ? round_bf16(key[i]) : key[i];
-        vc[i] = kv_round_bf16 ? round_bf16(value[i]) : value[i];
+        kc[i] = (kv_round_bf16 & 1) ? round_bf16(key[i]) : key[i];
+        vc[i] = (kv_round_bf16 & 1) ? round_bf16(value[i]) : value[i];
     }
     return 0;
 }

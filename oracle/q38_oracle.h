@@ -84,10 +84,13 @@ int q38o_linear_core(const float *conv_w, const float *dt_bias, const float *ssm
  *   attention       [6144]     output
  *   key_cache, value_cache     [cache_rows][1024], row = full_index*context+pos
  *   cache_rows                 rows in each cache array
- *   kv_round_bf16              0: f32 cache exactly as the reference stores it.
- *                              1: the new row is rounded to bf16 (RNE) before it
- *                              is stored, modelling a bf16 KV cache; earlier rows
- *                              are whatever the caller stored.
+ *   kv_round_bf16              bit 0 clear: f32 cache exactly as the reference
+ *                              stores it. bit 0 set: the new row is rounded to
+ *                              bf16 (RNE) before it is stored, modelling a bf16
+ *                              KV cache; earlier rows are whatever the caller
+ *                              stored. bit 1 set: the prepared query (after
+ *                              RMSNorm and RoPE) is rounded to bf16 too, the
+ *                              input precision of the tensor-core prefill.
  * Returns 0, or -1 when the cache row is out of range (ops.rs:860-864).
  */
 int q38o_full_core(const float *q_norm, const float *k_norm, const float *q_and_gate,

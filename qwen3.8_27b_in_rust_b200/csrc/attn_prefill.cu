@@ -1,0 +1,459 @@
+// attn_prefill.cu -- causal gated full-attention prefill on tcgen05 tensor
+// cores. Replaces the per-token full_core loop of batch_full_attention
+// (src/model/ops.rs:1156-1172): token t of the prompt attends to cache
+// positions 0..base+t, exactly as full_core at current_position = base+t.
+//
+//   P1 attn_prefill_prep  one CTA per (head, token, sequence): q/k RMSNorm
+//                         (f64 sum), partial RoPE (iterative f32 angle), K/V
+//                         append to the bf16 cache, key written back, and the
+//                         prepared query rounded to bf16 into the Q scratch
+//                         [seq][head][token][256].
+//   P2 attn_prefill       one CTA per (128-query tile, head, sequence),
+//                         heaviest (latest) tiles first. Warp roles:
+//                           warp 0   TMA producer: Q tile once, then K and V
+//                                    tiles of 64 keys into 2-deep rings
+//                                    (128-byte swizzle, no multicast);
+//                           warp 1   TMEM owner + single-thread MMA issuer:
+//                                    S = Q K^T (M=128, N=64, K=256) into one
+//                                    of two TMEM S buffers, O += P V
+//                                    (M=128, N=256, K=64, V MN-major);
+//                           warps 2-5 softmax, one query row per thread:
+//                                    S from TMEM, causal mask, online max
+//                                    with lazy O rescale (only when the max
+//                                    grows by more than 2^8), P = exp2 to
+//                                    f16 in swizzled shared memory; then
+//                                    the epilogue O / l * sigmoid(gate);
+//                           warps 6-9 convert each staged V tile from bf16
+//                                    to f16 in place (same swizzled layout).
+//                         TMEM: S0 | S1 (64 columns each) | O (256 columns).
+//
+// Precision: S = Q K^T from bf16 Q and K (the bf16 cache); O = P V in f16
+// (P rounded to f16 has 4x less error than bf16, which matters for the first
+// rows of a prompt that see only a few keys; bf16 V values are exact in f16
+// for 2^-14 <= |v| <= 65504); f32 accumulation throughout. Tolerance 2e-3.
+#include "q38_sm100.cuh"
+
+#include <cudaTypedefs.h>
+
+namespace q38 {
+namespace {
+
+using namespace sm100;
+
+constexpr int kBlockQ = 128;  // query rows per CTA (MMA M)
+constexpr int kBlockK = 64;   // keys per tile (QK N, PV K)
+constexpr int kThreadsPF = 320;
+constexpr uint32_t kQBytes = kBlockQ * kAttnHeadDim * 2;      // 64 KB
+constexpr uint32_t kKVBytes = kBlockK * kAttnHeadDim * 2;     // 32 KB
+constexpr uint32_t kPBytes = kBlockQ * kBlockK * 2;           // 16 KB
+constexpr uint32_t kSmemPF = kQBytes + 4 * kKVBytes + 2 * kPBytes + 1024;  // + alignment slack
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kColS = 0;     // S buffers at columns 0 and 64
+constexpr uint32_t kColO = 128;   // O at columns 128..383
+constexpr float kRescaleThreshold = 8.0f;  // log2 units
+
+// --------------------------------------------------------------------------
+// P1: prep
+// --------------------------------------------------------------------------
+struct PrefillPrepParams {
+    const float *q_and_gate;  // [nseq][count][heads*512]
+    float *key;               // [nseq][count][kv_heads*256]
+    const float *value;
+    __nv_bfloat16 *qp;        // [nseq][heads][count][256]
+    __nv_bfloat16 *kcache, *vcache;  // slot base: [batch][kv_heads][ctx][256]
+    const float *q_norm, *k_norm;
+    int seq0, count, base, context_length, heads, kv_heads;
+    float theta_scale, eps;
+};
+
+__global__ void __launch_bounds__(kAttnHeadDim) attn_prefill_prep_kernel(PrefillPrepParams p) {
+    pdl_launch_dependents();
+    __shared__ double red[32];
+    __shared__ float cs[32], sn[32];
+    __shared__ float xs[kAttnHeadDim];
+    const int h = blockIdx.x, t = blockIdx.y, s = blockIdx.z, i = threadIdx.x;
+    const int pos = p.base + t;
+    const bool is_q = h < p.heads;
+    const int kvh = h - p.heads;
+    const size_t tok = size_t(s) * p.count + t;
+    float x = is_q ? p.q_and_gate[(tok * p.heads + h) * 2 * kAttnHeadDim + i]
+                   : p.key[(tok * p.kv_heads + kvh) * kAttnHeadDim + i];
+    const double sum = block_sum_f64(double(x) * double(x), red);
+    const float scale = rms_scale_from_sum(sum, kAttnHeadDim, p.eps);
+    x = x * scale * (is_q ? p.q_norm[i] : p.k_norm[i]);
+    if (i < kRopeDims / 2) {
+        float theta = float(pos);
+        for (int j = 0; j < i; ++j) theta *= p.theta_scale;
+        cs[i] = cosf(theta);
+        sn[i] = sinf(theta);
+    }
+    xs[i] = x;
+    __syncthreads();
+    if (i < kRopeDims / 2) {
+        x = xs[i] * cs[i] - xs[i + kRopeDims / 2] * sn[i];
+    } else if (i < kRopeDims) {
+        const int j = i - kRopeDims / 2;
+        x = xs[j] * sn[j] + xs[i] * cs[j];
+    }
+    if (is_q) {
+        p.qp[((size_t(s) * p.heads + h) * p.count + t) * kAttnHeadDim + i] = __float2bfloat16_rn(x);
+    } else {
+        const size_t off = (tok * p.kv_heads + kvh) * kAttnHeadDim + i;
+        p.key[off] = x;
+        const size_t row =
+            ((size_t(p.seq0 + s) * p.kv_heads + kvh) * p.context_length + pos) * kAttnHeadDim + i;
+        p.kcache[row] = __float2bfloat16_rn(x);
+        p.vcache[row] = __float2bfloat16_rn(p.value[off]);
+    }
+}
+
+// --------------------------------------------------------------------------
+// P2: attention
+// --------------------------------------------------------------------------
+struct PrefillParams {
+    const float *q_and_gate;
+    float *attention;  // [nseq][count][heads*256]
+    int *err;
+    int seq0, count, base, heads, kv_heads, n_qtiles;
+};
+
+struct __align__(8) PrefillBarriers {
+    uint64_t q_full;
+    uint64_t k_full[2], k_empty[2], v_full[2], v_empty[2];
+    uint64_t s_full[2], p_full[2], v_conv[2], o_done;
+};
+
+__device__ __forceinline__ float ex2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+__global__ void __launch_bounds__(kThreadsPF, 1)
+    attn_prefill_kernel(const __grid_constant__ CUtensorMap map_q,
+                        const __grid_constant__ CUtensorMap map_k,
+                        const __grid_constant__ CUtensorMap map_v, PrefillParams p) {
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    unsigned char *smem =
+        reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    unsigned char *sQ = smem;
+    unsigned char *sK = sQ + kQBytes;       // 2 stages
+    unsigned char *sV = sK + 2 * kKVBytes;  // 2 stages
+    unsigned char *sP = sV + 2 * kKVBytes;  // 2 buffers
+    __shared__ PrefillBarriers bar;
+    __shared__ uint32_t tmem_base_s;
+    __shared__ volatile int abort_flag;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int qt = p.n_qtiles - 1 - int(blockIdx.x);  // latest (heaviest) tiles first
+    const int h = blockIdx.y, s = blockIdx.z;
+    const int kvh = h / kGroup;
+    const int q0 = qt * kBlockQ;
+    const int q_rows = min(kBlockQ, p.count - q0);
+    const int kend = p.base + q0 + q_rows;  // keys [0, kend) are visible to some row
+    const int nkt = (kend + kBlockK - 1) / kBlockK;
+
+    if (threadIdx.x == 0) {
+        abort_flag = 0;
+        mbar_init(&bar.q_full, 1);
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&bar.k_full[b], 1);
+            mbar_init(&bar.k_empty[b], 1);
+            mbar_init(&bar.v_full[b], 1);
+            mbar_init(&bar.v_empty[b], 1);
+            mbar_init(&bar.s_full[b], 1);
+            mbar_init(&bar.p_full[b], 128);
+            mbar_init(&bar.v_conv[b], 128);
+        }
+        mbar_init(&bar.o_done, 1);
+        fence_barrier_init();
+    }
+    if (warp == 1) {
+        tmem_alloc(&tmem_base_s, kTmemCols);
+        tmem_relinquish();
+    }
+    fence_before_sync();
+    __syncthreads();
+    fence_after_sync();
+    const uint32_t tmem = tmem_base_s;
+
+    auto fail = [&]() {
+        abort_flag = 1;
+        set_error(p.err, kDevErrTimeout);
+    };
+
+    if (warp == 0) {
+        // ------------------------------------------------------------ producer
+        if (lane == 0) {
+            tma_prefetch_desc(&map_q);
+            tma_prefetch_desc(&map_k);
+            tma_prefetch_desc(&map_v);
+            pdl_wait_primary();  // P1 wrote the Q scratch and the new K/V rows
+            const int qrow = s * p.heads + h;       // Q scratch plane
+            const int kvplane = (p.seq0 + s) * p.kv_heads + kvh;
+            mbar_arrive_expect_tx(&bar.q_full, kQBytes);
+            for (int cb = 0; cb < 4; ++cb)
+                tma_load_3d(sQ + cb * (kQBytes / 4), &map_q, cb * 64, q0, qrow, &bar.q_full);
+            for (int j = 0; j < nkt && !abort_flag; ++j) {
+                const int b = j & 1;
+                if (j >= 2 && !mbar_wait(&bar.k_empty[b], ((j - 2) >> 1) & 1)) { fail(); break; }
+                mbar_arrive_expect_tx(&bar.k_full[b], kKVBytes);
+                for (int cb = 0; cb < 4; ++cb)
+                    tma_load_3d(sK + b * kKVBytes + cb * (kKVBytes / 4), &map_k, cb * 64,
+                                j * kBlockK, kvplane, &bar.k_full[b]);
+                if (j >= 2 && !mbar_wait(&bar.v_empty[b], ((j - 2) >> 1) & 1)) { fail(); break; }
+                mbar_arrive_expect_tx(&bar.v_full[b], kKVBytes);
+                for (int cb = 0; cb < 4; ++cb)
+                    tma_load_3d(sV + b * kKVBytes + cb * (kKVBytes / 4), &map_v, cb * 64,
+                                j * kBlockK, kvplane, &bar.v_full[b]);
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            const uint32_t id_qk = idesc_bf16_f32(kBlockQ, kBlockK, 0, 0);
+            const uint32_t id_pv = idesc_f16_f32(kBlockQ, kAttnHeadDim, 0, 1, false);
+            const uint32_t sq = smem_addr(sQ), sk = smem_addr(sK), sv = smem_addr(sV),
+                           sp = smem_addr(sP);
+            auto pv = [&](int jj) -> bool {
+                const int bb = jj & 1;
+                if (!mbar_wait(&bar.p_full[bb], (jj >> 1) & 1)) return false;
+                if (!mbar_wait(&bar.v_conv[bb], (jj >> 1) & 1)) return false;
+                fence_after_sync();
+                for (int kk = 0; kk < kBlockK / 16; ++kk) {
+                    const uint64_t ad = smem_desc_sw128(sp + bb * kPBytes + kk * 32, 16, 1024);
+                    const uint64_t bd =
+                        smem_desc_sw128(sv + bb * kKVBytes + kk * 2048, kKVBytes / 4, 1024);
+                    mma_bf16(tmem + kColO, ad, bd, id_pv, (jj > 0 || kk > 0) ? 1u : 0u);
+                }
+                mma_commit(&bar.v_empty[bb]);
+                mma_commit(&bar.o_done);
+                return true;
+            };
+            bool ok = mbar_wait(&bar.q_full, 0);
+            for (int j = 0; ok && j < nkt; ++j) {
+                const int b = j & 1;
+                if (!mbar_wait(&bar.k_full[b], (j >> 1) & 1)) { ok = false; break; }
+                fence_after_sync();
+                for (int kk = 0; kk < kAttnHeadDim / 16; ++kk) {
+                    const uint64_t ad =
+                        smem_desc_sw128(sq + (kk >> 2) * (kQBytes / 4) + (kk & 3) * 32, 16, 1024);
+                    const uint64_t bd = smem_desc_sw128(
+                        sk + b * kKVBytes + (kk >> 2) * (kKVBytes / 4) + (kk & 3) * 32, 16, 1024);
+                    mma_bf16(tmem + kColS + b * kBlockK, ad, bd, id_qk, kk > 0 ? 1u : 0u);
+                }
+                mma_commit(&bar.s_full[b]);
+                mma_commit(&bar.k_empty[b]);
+                if (j >= 1 && !pv(j - 1)) { ok = false; break; }
+                if (abort_flag) { ok = false; break; }
+            }
+            if (ok && !pv(nkt - 1)) ok = false;
+            if (!ok) fail();
+        }
+    } else if (warp >= 6) {
+        // ------------------------------------------------------------ V bf16 -> f16
+        const int ct = threadIdx.x - 6 * 32;  // 0..127
+        for (int j = 0; j < nkt; ++j) {
+            const int b = j & 1;
+            if (!mbar_wait(&bar.v_full[b], (j >> 1) & 1)) { fail(); break; }
+            uint4 *tile = reinterpret_cast<uint4 *>(sV + b * kKVBytes);
+#pragma unroll 4
+            for (int c = ct; c < int(kKVBytes / 16); c += 128) {
+                uint4 w = tile[c];
+                float2 f;
+                f = bf16x2_to_float2(w.x); w.x = pack_f16x2(f.x, f.y);
+                f = bf16x2_to_float2(w.y); w.y = pack_f16x2(f.x, f.y);
+                f = bf16x2_to_float2(w.z); w.z = pack_f16x2(f.x, f.y);
+                f = bf16x2_to_float2(w.w); w.w = pack_f16x2(f.x, f.y);
+                tile[c] = w;
+            }
+            fence_proxy_async_smem();
+            mbar_arrive(&bar.v_conv[b]);
+            if (abort_flag) break;
+        }
+    } else {
+        // ------------------------------------------------------------ softmax
+        // tcgen05.ld/st are warp-collective: every decision that guards one
+        // (rescale, timeout exits) is made uniform across the warp.
+        const int sub = warp & 3;                 // TMEM lane quarter of this warp
+        const int r = sub * 32 + lane;            // query row within the tile
+        const uint32_t lane_addr = uint32_t(sub * 32) << 16;
+        const int t = q0 + r;                     // token index
+        const int qpos = p.base + min(t, p.count - 1);  // rows past the end mirror the last
+        const float sl2 = 1.4426950408889634f / 16.0f;  // log2(e) * score_scale
+        float m = -INFINITY, l = 0.f;
+        bool ok = true;
+        auto wait_all = [&](uint64_t *b, uint32_t parity) {
+            return __all_sync(0xffffffffu, mbar_wait(b, parity));
+        };
+        for (int j = 0; j < nkt; ++j) {
+            const int b = j & 1;
+            if (!wait_all(&bar.s_full[b], (j >> 1) & 1)) { ok = false; break; }
+            fence_after_sync();
+            uint32_t sr[2][32];
+            tmem_ld32(tmem + lane_addr + kColS + b * kBlockK, sr[0]);
+            tmem_ld32(tmem + lane_addr + kColS + b * kBlockK + 32, sr[1]);
+            tmem_wait_ld();
+            float sv[kBlockK];
+            const int key0 = j * kBlockK;
+            float mx = -INFINITY;
+#pragma unroll
+            for (int c = 0; c < kBlockK; ++c) {
+                float v = __uint_as_float(sr[c >> 5][c & 31]) * sl2;
+                v = (key0 + c <= qpos) ? v : -INFINITY;
+                sv[c] = v;
+                mx = fmaxf(mx, v);
+            }
+            const float m_new = fmaxf(m, mx);
+            if (__any_sync(0xffffffffu, m_new > m + kRescaleThreshold)) {
+                // Every row of the warp moves to its exact max (corr = 1 where
+                // the max did not change); O and l are scaled by the same factor.
+                const float corr = ex2(m - m_new);  // 0 on the first tile
+                if (j > 0) {
+                    // O holds PV(0..j-1): wait for PV(j-1), then rescale the rows.
+                    if (!wait_all(&bar.o_done, (j - 1) & 1)) { ok = false; break; }
+                    fence_after_sync();
+#pragma unroll 1
+                    for (int c = 0; c < kAttnHeadDim; c += 32) {
+                        uint32_t o[32];
+                        tmem_ld32(tmem + lane_addr + kColO + c, o);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int i = 0; i < 32; ++i)
+                            o[i] = __float_as_uint(__uint_as_float(o[i]) * corr);
+                        tmem_st32(tmem + lane_addr + kColO + c, o);
+                    }
+                    tmem_wait_st();
+                }
+                l *= corr;
+                m = m_new;
+            }
+            // P row into the swizzled K-major tile of buffer b.
+            unsigned char *prow = sP + b * kPBytes;
+            float psum = 0.f;
+#pragma unroll
+            for (int ch = 0; ch < kBlockK / 8; ++ch) {
+                uint32_t w[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const float p0 = ex2(sv[ch * 8 + 2 * e] - m);
+                    const float p1 = ex2(sv[ch * 8 + 2 * e + 1] - m);
+                    psum += p0 + p1;
+                    w[e] = pack_f16x2(p0, p1);
+                }
+                const uint32_t off = uint32_t(r) * 128u + ((uint32_t(ch) ^ (uint32_t(r) & 7u)) * 16u);
+                *reinterpret_cast<uint4 *>(prow + off) = make_uint4(w[0], w[1], w[2], w[3]);
+            }
+            l += psum;
+            fence_proxy_async_smem();
+            fence_before_sync();
+            mbar_arrive(&bar.p_full[b]);
+            if (__any_sync(0xffffffffu, abort_flag != 0)) { ok = false; break; }
+        }
+        // Wait for the last two PVs in order (a parity wait must never be
+        // more than one phase ahead of the barrier), then the epilogue.
+        if (ok && nkt >= 2 && !wait_all(&bar.o_done, (nkt - 2) & 1)) ok = false;
+        if (ok && !wait_all(&bar.o_done, (nkt - 1) & 1)) ok = false;
+        if (ok) {
+            fence_after_sync();
+            const float inv_l = 1.0f / l;
+            const bool store = r < q_rows;
+            const size_t tok = size_t(s) * p.count + min(t, p.count - 1);
+            const float *gate = p.q_and_gate + (tok * p.heads + h) * 2 * kAttnHeadDim + kAttnHeadDim;
+            float *out = p.attention + (tok * p.heads + h) * kAttnHeadDim;
+#pragma unroll 1
+            for (int c = 0; c < kAttnHeadDim; c += 32) {
+                uint32_t o[32];
+                tmem_ld32(tmem + lane_addr + kColO + c, o);
+                tmem_wait_ld();
+                if (store) {
+#pragma unroll
+                    for (int i = 0; i < 32; i += 4) {
+                        const float4 g = *reinterpret_cast<const float4 *>(gate + c + i);
+                        float4 y;
+                        y.x = __uint_as_float(o[i + 0]) * inv_l * sigmoidf_ref(g.x);
+                        y.y = __uint_as_float(o[i + 1]) * inv_l * sigmoidf_ref(g.y);
+                        y.z = __uint_as_float(o[i + 2]) * inv_l * sigmoidf_ref(g.z);
+                        y.w = __uint_as_float(o[i + 3]) * inv_l * sigmoidf_ref(g.w);
+                        *reinterpret_cast<float4 *>(out + c + i) = y;
+                    }
+                }
+            }
+        } else if (lane == 0) {
+            fail();
+        }
+    }
+
+    fence_before_sync();
+    __syncthreads();
+    fence_after_sync();
+    if (warp == 1) tmem_dealloc(tmem, kTmemCols);
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_tiled() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+        void *f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) !=
+                cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            f = nullptr;
+        return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+    }();
+    return fn;
+}
+
+// 3-D bf16 map over [planes][rows][256] with a box of 64 x box_rows x 1 and
+// 128-byte swizzle.
+bool make_map_bf16(CUtensorMap *m, const void *base, uint64_t rows, uint64_t planes,
+                   uint32_t box_rows) {
+    auto enc = encode_tiled();
+    if (!enc) return false;
+    cuuint64_t dims[3] = {uint64_t(kAttnHeadDim), rows, planes};
+    cuuint64_t strides[2] = {uint64_t(kAttnHeadDim) * 2, uint64_t(kAttnHeadDim) * 2 * rows};
+    cuuint32_t box[3] = {64, box_rows, 1};
+    cuuint32_t es[3] = {1, 1, 1};
+    return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void *>(base), dims, strides, box,
+               es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace
+
+cudaError_t launch_attn_prefill(const AttnPrefillLaunch &a, cudaStream_t stream) {
+    PrefillPrepParams pp{a.q_and_gate, a.key, a.value, a.qp, a.kcache, a.vcache, a.q_norm,
+                         a.k_norm, a.seq0, a.count, a.base, a.context_length, a.heads, a.kv_heads,
+                         a.theta_scale, a.eps};
+    attn_prefill_prep_kernel<<<dim3(a.heads + a.kv_heads, a.count, a.nseq), kAttnHeadDim, 0,
+                               stream>>>(pp);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+
+    CUtensorMap mq, mk, mv;
+    if (!make_map_bf16(&mq, a.qp, uint64_t(a.count), uint64_t(a.nseq) * a.heads, kBlockQ) ||
+        !make_map_bf16(&mk, a.kcache, uint64_t(a.context_length),
+                       uint64_t(a.batch) * a.kv_heads, kBlockK) ||
+        !make_map_bf16(&mv, a.vcache, uint64_t(a.context_length),
+                       uint64_t(a.batch) * a.kv_heads, kBlockK))
+        return cudaErrorInvalidValue;
+
+    const int n_qtiles = (a.count + kBlockQ - 1) / kBlockQ;
+    PrefillParams p{a.q_and_gate, a.attention, a.err, a.seq0, a.count, a.base, a.heads,
+                    a.kv_heads, n_qtiles};
+    e = cudaFuncSetAttribute(attn_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             int(kSmemPF));
+    if (e != cudaSuccess) return e;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(n_qtiles, a.heads, a.nseq);
+    cfg.blockDim = dim3(kThreadsPF);
+    cfg.dynamicSmemBytes = kSmemPF;
+    cfg.stream = stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, attn_prefill_kernel, mq, mk, mv, p);
+}
+
+}  // namespace q38

@@ -2,6 +2,7 @@
 // kernel launchers. Not part of the public ABI.
 #pragma once
 
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stddef.h>
 #include <stdint.h>
@@ -63,6 +64,8 @@ struct q38_state {
     float *part_ml = nullptr;       // [batch][heads][max_splits][2]
     int max_splits = 0;
     int *d_err = nullptr;           // device error bits
+    __nv_bfloat16 *prefill_q = nullptr;  // [tokens][heads][256] prepared queries
+    size_t prefill_tokens = 0;
     // staging for the host-pointer calls (device, sized for `batch`)
     float *stage = nullptr;
     size_t stage_floats = 0;
@@ -98,6 +101,20 @@ cudaError_t launch_attn_decode(const AttnDecodeLaunch &a, int sm_count, cudaStre
 DecodeSplitPlan plan_attn_decode(int batch, int kv_heads, int max_position, int kv_dtype,
                                  int sm_count);
 int attn_decode_max_splits(int context_length, int kv_dtype);
+
+struct AttnPrefillLaunch {
+    const float *q_and_gate;  // [nseq][count][heads*512]
+    float *key;               // [nseq][count][kv_heads*256]
+    const float *value;
+    float *attention;         // [nseq][count][heads*256]
+    __nv_bfloat16 *qp;        // scratch [nseq][heads][count][256]
+    __nv_bfloat16 *kcache, *vcache;  // slot base [batch][kv_heads][ctx][256]
+    const float *q_norm, *k_norm;
+    int *err;
+    int batch, seq0, nseq, count, base, context_length, heads, kv_heads;
+    float theta_scale, eps;
+};
+cudaError_t launch_attn_prefill(const AttnPrefillLaunch &a, cudaStream_t stream);
 
 struct LinearDecodeLaunch {
     float *qkv;

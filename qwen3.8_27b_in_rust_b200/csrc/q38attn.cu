@@ -162,6 +162,7 @@ void free_state(q38_state *st) {
     cudaFree(st->d_err);
     cudaFree(st->stage);
     cudaFree(st->stage_pos);
+    cudaFree(st->prefill_q);
 }
 
 // Validates a decode call and fills the launch arguments (device pointers).
@@ -587,6 +588,70 @@ int q38_linear_decode(q38_ctx *ctx, q38_state *st, int layer, int batch, float *
     DeviceGuard guard(ctx->device);
     cudaError_t e = q38::launch_linear_decode(a, static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return cuda_fail(e, "DeltaNet decode launch");
+    return Q38_OK;
+}
+
+int q38_state_reserve_prefill(q38_state *st, int max_tokens) {
+    if (!st) return fail(Q38_ERR_ARG, "null state");
+    if (max_tokens <= 0) return fail(Q38_ERR_ARG, "max_tokens must be positive");
+    if (size_t(max_tokens) <= st->prefill_tokens) return Q38_OK;
+    DeviceGuard guard(st->ctx->device);
+    cudaFree(st->prefill_q);
+    st->prefill_q = nullptr;
+    st->prefill_tokens = 0;
+    const size_t bytes = size_t(max_tokens) * st->ctx->q_dim * sizeof(__nv_bfloat16);
+    Q38_CUDA(cudaMalloc(&st->prefill_q, bytes));
+    st->prefill_tokens = size_t(max_tokens);
+    return Q38_OK;
+}
+
+int q38_full_prefill(q38_ctx *ctx, q38_state *st, int layer, int seq0, int nseq, int count,
+                     int base_position, const float *q_and_gate, float *key, const float *value,
+                     float *attention, void *stream) {
+    if (int rc = check_state(ctx, st)) return rc;
+    int slot;
+    if (int rc = full_slot_of(st, layer, &slot)) return rc;
+    if (st->kv_dtype != Q38_KV_BF16)
+        return fail(Q38_ERR_ARG, "tensor-core prefill needs a bf16 KV cache");
+    if (nseq <= 0 || seq0 < 0 || seq0 + nseq > st->batch)
+        return fail(Q38_ERR_ARG, "sequences [%d, %d) outside the state's %d", seq0, seq0 + nseq,
+                    st->batch);
+    if (count <= 0 || base_position < 0 ||
+        int64_t(base_position) + count > int64_t(st->context_length))
+        return fail(Q38_ERR_ARG, "positions [%d, %d) outside the %d-position cache",
+                    base_position, base_position + count, st->context_length);
+    if (size_t(nseq) * size_t(count) > st->prefill_tokens)
+        return fail(Q38_ERR_ARG, "%d tokens exceed the reserved prefill scratch (%zu)",
+                    nseq * count, st->prefill_tokens);
+    if (!q_and_gate || !key || !value || !attention)
+        return fail(Q38_ERR_ARG, "null tensor argument");
+    auto it = ctx->full.find(layer);
+    if (it == ctx->full.end())
+        return fail(Q38_ERR_ARG, "full-attention layer %d has no bound weights", layer);
+    q38::AttnPrefillLaunch a{};
+    a.q_and_gate = q_and_gate;
+    a.key = key;
+    a.value = value;
+    a.attention = attention;
+    a.qp = st->prefill_q;
+    a.kcache = reinterpret_cast<__nv_bfloat16 *>(kv_seq_base(st, st->kcache, slot, 0));
+    a.vcache = reinterpret_cast<__nv_bfloat16 *>(kv_seq_base(st, st->vcache, slot, 0));
+    a.q_norm = it->second.q_norm;
+    a.k_norm = it->second.k_norm;
+    a.err = st->d_err;
+    a.batch = st->batch;
+    a.seq0 = seq0;
+    a.nseq = nseq;
+    a.count = count;
+    a.base = base_position;
+    a.context_length = st->context_length;
+    a.heads = ctx->geom.attn_heads;
+    a.kv_heads = ctx->geom.attn_kv_heads;
+    a.theta_scale = ctx->theta_scale;
+    a.eps = ctx->geom.rms_eps;
+    DeviceGuard guard(ctx->device);
+    cudaError_t e = q38::launch_attn_prefill(a, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "full-attention prefill launch");
     return Q38_OK;
 }
 

@@ -178,6 +178,9 @@ class State:
                                               ctypes.byref(d)))
         return c.value, d.value
 
+    def reserve_prefill(self, max_tokens: int) -> None:
+        check(self._lib.q38_state_reserve_prefill(self.handle, max_tokens))
+
     def kv_views(self, layer: int):
         """Zero-copy torch views of one KV slot, [batch][kv_heads][context][256]
         (bf16 or f32), for bulk device-side initialisation."""
@@ -291,6 +294,17 @@ class Context:
                                           _dev_ptr(beta, "beta"), _dev_ptr(alpha, "alpha"),
                                           _dev_ptr(attention, "attention"),
                                           _stream_ptr(stream)))
+
+    def full_prefill(self, state: State, layer: int, seq0: int, q_and_gate, key, value,
+                     attention, base_position: int, stream=None) -> None:
+        """Causal prefill of q_and_gate.shape[1] tokens for q_and_gate.shape[0]
+        sequences starting at seq0 (the per-token full_core loop of
+        batch_full_attention, src/model/ops.rs:1156-1172), on tensor cores."""
+        nseq, count = q_and_gate.shape[0], q_and_gate.shape[1]
+        check(self._lib.q38_full_prefill(self.handle, state.handle, layer, seq0, nseq, count,
+                                         base_position, _dev_ptr(q_and_gate, "q_and_gate"),
+                                         _dev_ptr(key, "key"), _dev_ptr(value, "value"),
+                                         _dev_ptr(attention, "attention"), _stream_ptr(stream)))
 
     # host pointers, batched, synchronous -----------------------------------
     def full_decode_host(self, state: State, layer: int, q_and_gate: np.ndarray,

@@ -75,6 +75,9 @@ SIGNATURES = {
     "q38_linear_decode": (c_int, [_VP, _VP, c_int, c_int, _VP, _VP, _VP, _VP, _VP, _VP]),
     "q38_full_decode_noalloc": (c_int, [_VP, _VP, _VP, _VP, c_int, c_int, c_int, _VP, _VP, _VP,
                                         _VP, c_int, _VP, _VP, _VP]),
+    "q38_state_reserve_prefill": (c_int, [_VP, c_int]),
+    "q38_full_prefill": (c_int, [_VP, _VP, c_int, c_int, c_int, c_int, c_int, _VP, _VP, _VP, _VP,
+                                 _VP]),
     "q38_full_decode_host": (c_int, [_VP, _VP, c_int, c_int, _VP, _VP, _VP, _VP, _VP, _VP]),
     "q38_linear_decode_host": (c_int, [_VP, _VP, c_int, c_int, _VP, _VP, _VP, _VP, _VP, _VP]),
     "q38_linear_core": (c_int, [_VP, _VP, c_int, _VP, _VP, _VP, _VP, _VP, _VP, _VP]),
