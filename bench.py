@@ -59,6 +59,10 @@ def parse_args():
     ap.add_argument("--cpu-seconds", type=float, default=10.0,
                     help="CPU work budget of the cpu_baseline sample")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-prefill", action="store_true")
+    ap.add_argument("--prefill-batch", type=int, default=4)
+    ap.add_argument("--prefill-len", type=int, default=8192)
+    ap.add_argument("--prefill-iters", type=int, default=5)
     ap.add_argument("--no-cpu", action="store_true")
     return ap.parse_args()
 
@@ -93,6 +97,56 @@ def load_peaks() -> tuple[float, str]:
         except Exception:
             pass
     return 6650.0, "fallback"
+
+
+def load_tensor_peak() -> tuple[float, str]:
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["bf16_tflops"]), "measured"
+        except Exception:
+            pass
+    return 1590.0, "fallback"
+
+
+def prefill_flops(batch: int, seq: int) -> float:
+    """Causal attention FLOPs (config 4): batch * 24 heads * (2*256 for QK^T +
+    2*256 for PV) per visible (query, key) pair, seq*(seq+1)/2 pairs."""
+    return float(batch) * 24 * 4 * 256 * seq * (seq + 1) / 2
+
+
+def run_prefill(args, ctx, q38attn, synth, torch, rank: int) -> dict:
+    """Config 4: causal prefill of `prefill_batch` prompts of `prefill_len`
+    tokens through one full-attention layer, on the tensor cores."""
+    B, S = args.prefill_batch, args.prefill_len
+    layer = FULL_LAYER
+    st = ctx.state(B, S, full_slots=1, linear_slots=0, kv_dtype=q38attn.Q38_KV_BF16)
+    st.reserve_prefill(B * S)
+    tg = torch.Generator(device="cuda")
+    tg.manual_seed(args.seed + 77 + rank)
+    qg = torch.randn(B, S, 12288, device="cuda", generator=tg)
+    key0 = torch.randn(B, S, 1024, device="cuda", generator=tg)
+    val = torch.randn(B, S, 1024, device="cuda", generator=tg)
+    key = torch.empty_like(key0)
+    att = torch.empty(B, S, 6144, device="cuda")
+    stream = torch.cuda.current_stream()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(args.prefill_iters)]
+    for it in range(2 + args.prefill_iters):
+        key.copy_(key0)  # key is rewritten in place (RMSNorm + RoPE)
+        if it >= 2:
+            evs[it - 2][0].record(stream)
+        ctx.full_prefill(st, layer, 0, qg, key, val, att, 0, stream=stream)
+        if it >= 2:
+            evs[it - 2][1].record(stream)
+    torch.cuda.synchronize()
+    if st.errors():
+        raise RuntimeError("device error bits set during prefill")
+    ms = statistics.median(a.elapsed_time(b) for a, b in evs)
+    st.close()
+    del qg, key0, val, key, att
+    torch.cuda.empty_cache()
+    return {"ms": ms}
 
 
 def load_traffic_profile() -> dict | None:
@@ -399,6 +453,10 @@ def run_ours(args) -> None:
     if st.errors():
         raise RuntimeError("device error bits set during the timed region")
 
+    prefill = None
+    if not args.no_prefill:
+        prefill = run_prefill(args, ctx, q38attn, synth, torch, rank)
+
     # End-to-end through the host-pointer C-ABI calls.
     e2e = None
     if e2e_steps:
@@ -428,11 +486,11 @@ def run_ours(args) -> None:
         e2e = [e2e_s, h2d, d2h]
 
     # Max over ranks.
-    vals = torch.tensor([ms, attn_ms, lin_ms, e2e[0] if e2e else 0.0], device="cuda",
-                        dtype=torch.float64)
+    vals = torch.tensor([ms, attn_ms, lin_ms, e2e[0] if e2e else 0.0,
+                         prefill["ms"] if prefill else 0.0], device="cuda", dtype=torch.float64)
     if dist is not None:
         dist.all_reduce(vals, op=dist.ReduceOp.MAX)
-    ms, attn_ms, lin_ms, e2e_s = vals.tolist()
+    ms, attn_ms, lin_ms, e2e_s, prefill_ms = vals.tolist()
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -466,9 +524,23 @@ def run_ours(args) -> None:
                          "achieved_gbs": lin_bytes / (lin_ms * 1e-3) / 1e9,
                          "frac": lin_bytes / (lin_ms * 1e-3) / 1e9 / peak},
             "step_gbs": (attn_bytes + lin_bytes) / (step_ms * 1e-3) / 1e9,
-            "gpu_launches": 9 * args.steps,
+            "gpu_launches": 9 * args.steps,  # decode timed region (prefill timed separately)
             "clocks": clocks.summary(),
         }
+        if prefill:
+            tpeak, tpeak_kind = load_tensor_peak()
+            flops = prefill_flops(args.prefill_batch, args.prefill_len) * world
+            tflops = flops / (prefill_ms * 1e-3) / 1e12
+            line["prefill"] = {
+                "workload": (f"config4: {args.prefill_batch} x {args.prefill_len}-token causal "
+                             "prefill per GPU, 24Q/4KV x 256, RoPE 64, sigmoid gate; "
+                             "QK^T bf16, PV f16, f32 accumulate (tcgen05)"),
+                "ms": prefill_ms, "flops": flops, "tflops": tflops,
+                "roofline": {"bound": "tensor", "achieved": tflops, "peak": tpeak,
+                             "unit": "TFLOP/s", "frac": tflops / tpeak,
+                             "peak_source": f"{tpeak_kind} bf16_tflops (burst)",
+                             "kernel": "prep + attn_prefill (one op)"},
+            }
         if e2e:
             line["e2e"] = {"value": tokens * e2e_steps / e2e_s, "unit": "tok/s",
                            "h2d_bytes_per_step": e2e[1], "d2h_bytes_per_step": e2e[2],
