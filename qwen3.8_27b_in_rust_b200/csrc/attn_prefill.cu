@@ -10,13 +10,15 @@
 //                         [seq][head][token][256].
 //   P2 attn_prefill       one CTA per (128-query tile, head, sequence),
 //                         heaviest (latest) tiles first. Warp roles:
-//                           warp 0   TMA producer: Q tile once, then K and V
-//                                    tiles of 64 keys into 2-deep rings
-//                                    (128-byte swizzle, no multicast);
+//                           warp 0   TMA producer: the Q tile once (staged
+//                                    in the K ring), then K and V tiles of 64
+//                                    keys into 3-deep rings (128-byte
+//                                    swizzle, no multicast);
 //                           warp 1   TMEM owner + single-thread MMA issuer:
-//                                    S = Q K^T (M=128, N=64, K=256) into one
-//                                    of two TMEM S buffers, O += P V
-//                                    (M=128, N=256, K=64, V MN-major);
+//                                    S = Q K^T (M=128, N=64, K=256, Q read
+//                                    from TMEM) into one of two TMEM S
+//                                    buffers, O += P V (M=128, N=256, K=64,
+//                                    V MN-major);
 //                           warps 2-5 softmax, one query row per thread:
 //                                    S from TMEM, causal mask, online max
 //                                    with lazy O rescale (only when the max
@@ -25,7 +27,12 @@
 //                                    the epilogue O / l * sigmoid(gate);
 //                           warps 6-9 convert each staged V tile from bf16
 //                                    to f16 in place (same swizzled layout).
-//                         TMEM: S0 | S1 (64 columns each) | O (256 columns).
+//                           (warps 2-5 first copy their rows of the staged
+//                                    Q tile into TMEM.)
+//                         TMEM: S0 | S1 (64 columns each) | O (256) | Q (128,
+//                         bf16 pairs). Holding Q in TMEM frees 64 KB of shared
+//                         memory for deeper K/V rings and removes the per-step
+//                         re-read of Q from shared memory.
 //
 // Precision: S = Q K^T from bf16 Q and K (the bf16 cache); O = P V in f16
 // (P rounded to f16 has 4x less error than bf16, which matters for the first
@@ -46,10 +53,13 @@ constexpr int kThreadsPF = 320;
 constexpr uint32_t kQBytes = kBlockQ * kAttnHeadDim * 2;      // 64 KB
 constexpr uint32_t kKVBytes = kBlockK * kAttnHeadDim * 2;     // 32 KB
 constexpr uint32_t kPBytes = kBlockQ * kBlockK * 2;           // 16 KB
-constexpr uint32_t kSmemPF = kQBytes + 4 * kKVBytes + 2 * kPBytes + 1024;  // + alignment slack
+constexpr int kStagesKV = 3;
+constexpr uint32_t kSmemPF = 2 * kStagesKV * kKVBytes + 2 * kPBytes + 1024;  // + alignment slack
+static_assert(kQBytes <= kStagesKV * kKVBytes, "Q is staged in the K ring");
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColS = 0;     // S buffers at columns 0 and 64
 constexpr uint32_t kColO = 128;   // O at columns 128..383
+constexpr uint32_t kColQ = 384;   // Q at columns 384..511 (bf16 pairs)
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 
 // --------------------------------------------------------------------------
@@ -118,15 +128,25 @@ struct PrefillParams {
 };
 
 struct __align__(8) PrefillBarriers {
-    uint64_t q_full;
-    uint64_t k_full[2], k_empty[2], v_full[2], v_empty[2];
-    uint64_t s_full[2], p_full[2], v_conv[2], o_done;
+    uint64_t q_full, q_copied;
+    uint64_t k_full[kStagesKV], k_empty[kStagesKV], v_full[kStagesKV], v_empty[kStagesKV];
+    uint64_t v_conv[kStagesKV];
+    uint64_t s_full[2], p_full[2], o_done;
 };
 
 __device__ __forceinline__ float ex2(float x) {
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
     return y;
+}
+
+// 1/(1+exp(-x)) from the approximate exp2 and reciprocal (relative error
+// ~1e-7, far inside the prefill path's 2e-3 tolerance).
+__device__ __forceinline__ float sigmoid_fast(float x) {
+    float r;
+    const float d = 1.0f + ex2(-1.4426950408889634f * x);
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(d));
+    return r;
 }
 
 __global__ void __launch_bounds__(kThreadsPF, 1)
@@ -136,10 +156,9 @@ __global__ void __launch_bounds__(kThreadsPF, 1)
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char *smem =
         reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    unsigned char *sQ = smem;
-    unsigned char *sK = sQ + kQBytes;       // 2 stages
-    unsigned char *sV = sK + 2 * kKVBytes;  // 2 stages
-    unsigned char *sP = sV + 2 * kKVBytes;  // 2 buffers
+    unsigned char *sK = smem;                       // kStagesKV stages (Q staged here first)
+    unsigned char *sV = sK + kStagesKV * kKVBytes;  // kStagesKV stages
+    unsigned char *sP = sV + kStagesKV * kKVBytes;  // 2 buffers
     __shared__ PrefillBarriers bar;
     __shared__ uint32_t tmem_base_s;
     __shared__ volatile int abort_flag;
@@ -156,14 +175,17 @@ __global__ void __launch_bounds__(kThreadsPF, 1)
     if (threadIdx.x == 0) {
         abort_flag = 0;
         mbar_init(&bar.q_full, 1);
-        for (int b = 0; b < 2; ++b) {
+        mbar_init(&bar.q_copied, 128);
+        for (int b = 0; b < kStagesKV; ++b) {
             mbar_init(&bar.k_full[b], 1);
             mbar_init(&bar.k_empty[b], 1);
             mbar_init(&bar.v_full[b], 1);
             mbar_init(&bar.v_empty[b], 1);
+            mbar_init(&bar.v_conv[b], 128);
+        }
+        for (int b = 0; b < 2; ++b) {
             mbar_init(&bar.s_full[b], 1);
             mbar_init(&bar.p_full[b], 128);
-            mbar_init(&bar.v_conv[b], 128);
         }
         mbar_init(&bar.o_done, 1);
         fence_barrier_init();
@@ -193,15 +215,18 @@ __global__ void __launch_bounds__(kThreadsPF, 1)
             const int kvplane = (p.seq0 + s) * p.kv_heads + kvh;
             mbar_arrive_expect_tx(&bar.q_full, kQBytes);
             for (int cb = 0; cb < 4; ++cb)
-                tma_load_3d(sQ + cb * (kQBytes / 4), &map_q, cb * 64, q0, qrow, &bar.q_full);
+                tma_load_3d(sK + cb * (kQBytes / 4), &map_q, cb * 64, q0, qrow, &bar.q_full);
+            // The K ring holds the staged Q until the softmax warps copied it to TMEM.
+            if (!mbar_wait(&bar.q_copied, 0)) fail();
             for (int j = 0; j < nkt && !abort_flag; ++j) {
-                const int b = j & 1;
-                if (j >= 2 && !mbar_wait(&bar.k_empty[b], ((j - 2) >> 1) & 1)) { fail(); break; }
+                const int b = j % kStagesKV;
+                const uint32_t ph = uint32_t((j - kStagesKV) / kStagesKV) & 1u;
+                if (j >= kStagesKV && !mbar_wait(&bar.k_empty[b], ph)) { fail(); break; }
                 mbar_arrive_expect_tx(&bar.k_full[b], kKVBytes);
                 for (int cb = 0; cb < 4; ++cb)
                     tma_load_3d(sK + b * kKVBytes + cb * (kKVBytes / 4), &map_k, cb * 64,
                                 j * kBlockK, kvplane, &bar.k_full[b]);
-                if (j >= 2 && !mbar_wait(&bar.v_empty[b], ((j - 2) >> 1) & 1)) { fail(); break; }
+                if (j >= kStagesKV && !mbar_wait(&bar.v_empty[b], ph)) { fail(); break; }
                 mbar_arrive_expect_tx(&bar.v_full[b], kKVBytes);
                 for (int cb = 0; cb < 4; ++cb)
                     tma_load_3d(sV + b * kKVBytes + cb * (kKVBytes / 4), &map_v, cb * 64,
@@ -213,37 +238,35 @@ __global__ void __launch_bounds__(kThreadsPF, 1)
         if (lane == 0) {
             const uint32_t id_qk = idesc_bf16_f32(kBlockQ, kBlockK, 0, 0);
             const uint32_t id_pv = idesc_f16_f32(kBlockQ, kAttnHeadDim, 0, 1, false);
-            const uint32_t sq = smem_addr(sQ), sk = smem_addr(sK), sv = smem_addr(sV),
-                           sp = smem_addr(sP);
+            const uint32_t sk = smem_addr(sK), sv = smem_addr(sV), sp = smem_addr(sP);
             auto pv = [&](int jj) -> bool {
-                const int bb = jj & 1;
+                const int bb = jj & 1, vb = jj % kStagesKV;
                 if (!mbar_wait(&bar.p_full[bb], (jj >> 1) & 1)) return false;
-                if (!mbar_wait(&bar.v_conv[bb], (jj >> 1) & 1)) return false;
+                if (!mbar_wait(&bar.v_conv[vb], uint32_t(jj / kStagesKV) & 1u)) return false;
                 fence_after_sync();
                 for (int kk = 0; kk < kBlockK / 16; ++kk) {
                     const uint64_t ad = smem_desc_sw128(sp + bb * kPBytes + kk * 32, 16, 1024);
                     const uint64_t bd =
-                        smem_desc_sw128(sv + bb * kKVBytes + kk * 2048, kKVBytes / 4, 1024);
+                        smem_desc_sw128(sv + vb * kKVBytes + kk * 2048, kKVBytes / 4, 1024);
                     mma_bf16(tmem + kColO, ad, bd, id_pv, (jj > 0 || kk > 0) ? 1u : 0u);
                 }
-                mma_commit(&bar.v_empty[bb]);
+                mma_commit(&bar.v_empty[vb]);
                 mma_commit(&bar.o_done);
                 return true;
             };
-            bool ok = mbar_wait(&bar.q_full, 0);
+            bool ok = mbar_wait(&bar.q_copied, 0);
             for (int j = 0; ok && j < nkt; ++j) {
-                const int b = j & 1;
-                if (!mbar_wait(&bar.k_full[b], (j >> 1) & 1)) { ok = false; break; }
+                const int b = j & 1, kb = j % kStagesKV;
+                if (!mbar_wait(&bar.k_full[kb], uint32_t(j / kStagesKV) & 1u)) { ok = false; break; }
                 fence_after_sync();
                 for (int kk = 0; kk < kAttnHeadDim / 16; ++kk) {
-                    const uint64_t ad =
-                        smem_desc_sw128(sq + (kk >> 2) * (kQBytes / 4) + (kk & 3) * 32, 16, 1024);
                     const uint64_t bd = smem_desc_sw128(
-                        sk + b * kKVBytes + (kk >> 2) * (kKVBytes / 4) + (kk & 3) * 32, 16, 1024);
-                    mma_bf16(tmem + kColS + b * kBlockK, ad, bd, id_qk, kk > 0 ? 1u : 0u);
+                        sk + kb * kKVBytes + (kk >> 2) * (kKVBytes / 4) + (kk & 3) * 32, 16, 1024);
+                    mma_f16_ta(tmem + kColS + b * kBlockK, tmem + kColQ + kk * 8, bd, id_qk,
+                               kk > 0 ? 1u : 0u);
                 }
                 mma_commit(&bar.s_full[b]);
-                mma_commit(&bar.k_empty[b]);
+                mma_commit(&bar.k_empty[kb]);
                 if (j >= 1 && !pv(j - 1)) { ok = false; break; }
                 if (abort_flag) { ok = false; break; }
             }
@@ -254,8 +277,8 @@ __global__ void __launch_bounds__(kThreadsPF, 1)
         // ------------------------------------------------------------ V bf16 -> f16
         const int ct = threadIdx.x - 6 * 32;  // 0..127
         for (int j = 0; j < nkt; ++j) {
-            const int b = j & 1;
-            if (!mbar_wait(&bar.v_full[b], (j >> 1) & 1)) { fail(); break; }
+            const int b = j % kStagesKV;
+            if (!mbar_wait(&bar.v_full[b], uint32_t(j / kStagesKV) & 1u)) { fail(); break; }
             uint4 *tile = reinterpret_cast<uint4 *>(sV + b * kKVBytes);
 #pragma unroll 4
             for (int c = ct; c < int(kKVBytes / 16); c += 128) {
@@ -280,13 +303,37 @@ __global__ void __launch_bounds__(kThreadsPF, 1)
         const uint32_t lane_addr = uint32_t(sub * 32) << 16;
         const int t = q0 + r;                     // token index
         const int qpos = p.base + min(t, p.count - 1);  // rows past the end mirror the last
+        const int qpos_first = p.base + q0;              // smallest position in the tile
         const float sl2 = 1.4426950408889634f / 16.0f;  // log2(e) * score_scale
         float m = -INFINITY, l = 0.f;
         bool ok = true;
         auto wait_all = [&](uint64_t *b, uint32_t parity) {
             return __all_sync(0xffffffffu, mbar_wait(b, parity));
         };
-        for (int j = 0; j < nkt; ++j) {
+        // Copy this thread's row of the staged Q tile (four 64-column SW128
+        // blocks in the K ring) into TMEM columns kColQ.., two bf16 per column.
+        if (!wait_all(&bar.q_full, 0)) {
+            ok = false;
+        } else {
+#pragma unroll 1
+            for (int cb = 0; cb < 4; ++cb) {
+                uint32_t w[32];
+#pragma unroll
+                for (int ch = 0; ch < 8; ++ch) {
+                    const uint4 v = *reinterpret_cast<const uint4 *>(
+                        sK + cb * (kQBytes / 4) + r * 128 + ((ch ^ (r & 7)) * 16));
+                    w[ch * 4 + 0] = v.x;
+                    w[ch * 4 + 1] = v.y;
+                    w[ch * 4 + 2] = v.z;
+                    w[ch * 4 + 3] = v.w;
+                }
+                tmem_st32(tmem + lane_addr + kColQ + cb * 32, w);
+            }
+            tmem_wait_st();
+        }
+        fence_before_sync();
+        mbar_arrive(&bar.q_copied);
+        for (int j = 0; ok && j < nkt; ++j) {
             const int b = j & 1;
             if (!wait_all(&bar.s_full[b], (j >> 1) & 1)) { ok = false; break; }
             fence_after_sync();
@@ -296,14 +343,28 @@ __global__ void __launch_bounds__(kThreadsPF, 1)
             tmem_wait_ld();
             float sv[kBlockK];
             const int key0 = j * kBlockK;
-            float mx = -INFINITY;
+            // Independent partial maxima (8 chains) instead of one serial chain.
+            float mx8[8];
 #pragma unroll
-            for (int c = 0; c < kBlockK; ++c) {
-                float v = __uint_as_float(sr[c >> 5][c & 31]) * sl2;
-                v = (key0 + c <= qpos) ? v : -INFINITY;
-                sv[c] = v;
-                mx = fmaxf(mx, v);
+            for (int i = 0; i < 8; ++i) mx8[i] = -INFINITY;
+            if (key0 + kBlockK - 1 <= qpos_first) {
+                // Tile fully visible to every row of this CTA: no mask.
+#pragma unroll
+                for (int c = 0; c < kBlockK; ++c) {
+                    sv[c] = __uint_as_float(sr[c >> 5][c & 31]) * sl2;
+                    mx8[c & 7] = fmaxf(mx8[c & 7], sv[c]);
+                }
+            } else {
+#pragma unroll
+                for (int c = 0; c < kBlockK; ++c) {
+                    float v = __uint_as_float(sr[c >> 5][c & 31]) * sl2;
+                    v = (key0 + c <= qpos) ? v : -INFINITY;
+                    sv[c] = v;
+                    mx8[c & 7] = fmaxf(mx8[c & 7], v);
+                }
             }
+            const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                                   fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
             const float m_new = fmaxf(m, mx);
             if (__any_sync(0xffffffffu, m_new > m + kRescaleThreshold)) {
                 // Every row of the warp moves to its exact max (corr = 1 where
@@ -330,7 +391,9 @@ __global__ void __launch_bounds__(kThreadsPF, 1)
             }
             // P row into the swizzled K-major tile of buffer b.
             unsigned char *prow = sP + b * kPBytes;
-            float psum = 0.f;
+            float ps8[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) ps8[i] = 0.f;
 #pragma unroll
             for (int ch = 0; ch < kBlockK / 8; ++ch) {
                 uint32_t w[4];
@@ -338,12 +401,15 @@ __global__ void __launch_bounds__(kThreadsPF, 1)
                 for (int e = 0; e < 4; ++e) {
                     const float p0 = ex2(sv[ch * 8 + 2 * e] - m);
                     const float p1 = ex2(sv[ch * 8 + 2 * e + 1] - m);
-                    psum += p0 + p1;
+                    ps8[2 * e] += p0;
+                    ps8[2 * e + 1] += p1;
                     w[e] = pack_f16x2(p0, p1);
                 }
                 const uint32_t off = uint32_t(r) * 128u + ((uint32_t(ch) ^ (uint32_t(r) & 7u)) * 16u);
                 *reinterpret_cast<uint4 *>(prow + off) = make_uint4(w[0], w[1], w[2], w[3]);
             }
+            const float psum = ((ps8[0] + ps8[1]) + (ps8[2] + ps8[3])) +
+                               ((ps8[4] + ps8[5]) + (ps8[6] + ps8[7]));
             l += psum;
             fence_proxy_async_smem();
             fence_before_sync();
@@ -371,10 +437,10 @@ __global__ void __launch_bounds__(kThreadsPF, 1)
                     for (int i = 0; i < 32; i += 4) {
                         const float4 g = *reinterpret_cast<const float4 *>(gate + c + i);
                         float4 y;
-                        y.x = __uint_as_float(o[i + 0]) * inv_l * sigmoidf_ref(g.x);
-                        y.y = __uint_as_float(o[i + 1]) * inv_l * sigmoidf_ref(g.y);
-                        y.z = __uint_as_float(o[i + 2]) * inv_l * sigmoidf_ref(g.z);
-                        y.w = __uint_as_float(o[i + 3]) * inv_l * sigmoidf_ref(g.w);
+                        y.x = __uint_as_float(o[i + 0]) * inv_l * sigmoid_fast(g.x);
+                        y.y = __uint_as_float(o[i + 1]) * inv_l * sigmoid_fast(g.y);
+                        y.z = __uint_as_float(o[i + 2]) * inv_l * sigmoid_fast(g.z);
+                        y.w = __uint_as_float(o[i + 3]) * inv_l * sigmoid_fast(g.w);
                         *reinterpret_cast<float4 *>(out + c + i) = y;
                     }
                 }
