@@ -211,7 +211,10 @@ int q38_full_decode_noalloc(const float *q_norm, const float *k_norm, void *key_
 
 /* Reserves the state's prefill scratch for up to max_tokens prompt tokens
  * per call (summed over the sequences of the call): the bf16 prepared
- * queries, 12 KB per token. Allocates; call it once at set-up. */
+ * queries of the attention prefill (12 KB per token, when the state has full
+ * slots) and the chunk-local WY quantities of the DeltaNet prefill (about
+ * 62 KB per token, when it has linear slots). Allocates; call it once at
+ * set-up. */
 int q38_state_reserve_prefill(q38_state *st, int max_tokens);
 
 /* Causal prefill of `count` prompt tokens for each of the nseq sequences
@@ -230,6 +233,21 @@ int q38_state_reserve_prefill(q38_state *st, int max_tokens);
 int q38_full_prefill(q38_ctx *ctx, q38_state *st, int layer, int seq0, int nseq, int count,
                      int base_position, const float *q_and_gate, float *key, const float *value,
                      float *attention, void *stream);
+
+/* Chunked Gated DeltaNet prefill of `count` prompt tokens for each of the
+ * nseq sequences seq0..seq0+nseq-1, continuing each sequence's conv and
+ * delta state: the same result as the reference's per-token loop over
+ * linear_core (batch_linear_attention, ops.rs:1088-1099), computed in chunks
+ * of 64 tokens (WY form; f32). Needs q38_state_reserve_prefill(nseq*count).
+ * DEVICE pointers, token-major per sequence:
+ *   qkv   [nseq][count][qkv_dim]  in: projections; out: conv+SiLU+L2 values
+ *   z     [nseq][count][v_heads*128]
+ *   beta  [nseq][count][v_heads]  in: logits; out: sigmoid(beta)
+ *   alpha [nseq][count][v_heads]  in: logits; out: ssm_a*softplus(alpha+dt_bias)
+ *   attention [nseq][count][v_heads*128] output */
+int q38_linear_prefill(q38_ctx *ctx, q38_state *st, int layer, int seq0, int nseq, int count,
+                       float *qkv, const float *z, float *beta, float *alpha, float *attention,
+                       void *stream);
 
 /* ---------------------------------------------------------- decode (host) */
 

@@ -66,6 +66,8 @@ struct q38_state {
     int *d_err = nullptr;           // device error bits
     __nv_bfloat16 *prefill_q = nullptr;  // [tokens][heads][256] prepared queries
     size_t prefill_tokens = 0;
+    float *prefill_lin = nullptr;        // chunked DeltaNet scratch
+    size_t prefill_chunks = 0;           // chunk capacity of prefill_lin
     // staging for the host-pointer calls (device, sized for `batch`)
     float *stage = nullptr;
     size_t stage_floats = 0;
@@ -115,6 +117,21 @@ struct AttnPrefillLaunch {
     float theta_scale, eps;
 };
 cudaError_t launch_attn_prefill(const AttnPrefillLaunch &a, cudaStream_t stream);
+
+struct LinearPrefillLaunch {
+    float *qkv;                 // [nseq][count][qkv_dim] in/out
+    const float *z;             // [nseq][count][v_heads*128]
+    float *beta, *alpha;        // [nseq][count][v_heads] in/out
+    float *attention;           // [nseq][count][v_heads*128]
+    float *conv_state;          // slot base [batch][qkv_dim][3]
+    float *delta_state;         // slot base [batch][v_heads][128][128]
+    const float *conv_w, *dt_bias, *ssm_a, *ssm_norm;
+    float *scratch;             // linear_prefill_scratch_floats(nseq*nchunk, v_heads)
+    int seq0, nseq, count, qk_heads, v_heads;
+    float eps;
+};
+cudaError_t launch_linear_prefill(const LinearPrefillLaunch &a, cudaStream_t stream);
+size_t linear_prefill_scratch_floats(int nchunk_total, int v_heads);
 
 struct LinearDecodeLaunch {
     float *qkv;

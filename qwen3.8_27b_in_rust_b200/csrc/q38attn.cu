@@ -163,6 +163,7 @@ void free_state(q38_state *st) {
     cudaFree(st->stage);
     cudaFree(st->stage_pos);
     cudaFree(st->prefill_q);
+    cudaFree(st->prefill_lin);
 }
 
 // Validates a decode call and fills the launch arguments (device pointers).
@@ -597,10 +598,23 @@ int q38_state_reserve_prefill(q38_state *st, int max_tokens) {
     if (size_t(max_tokens) <= st->prefill_tokens) return Q38_OK;
     DeviceGuard guard(st->ctx->device);
     cudaFree(st->prefill_q);
+    cudaFree(st->prefill_lin);
     st->prefill_q = nullptr;
+    st->prefill_lin = nullptr;
     st->prefill_tokens = 0;
-    const size_t bytes = size_t(max_tokens) * st->ctx->q_dim * sizeof(__nv_bfloat16);
-    Q38_CUDA(cudaMalloc(&st->prefill_q, bytes));
+    st->prefill_chunks = 0;
+    if (st->full_slots > 0) {
+        const size_t bytes = size_t(max_tokens) * st->ctx->q_dim * sizeof(__nv_bfloat16);
+        Q38_CUDA(cudaMalloc(&st->prefill_q, bytes));
+    }
+    if (st->linear_slots > 0) {
+        // One partial chunk per sequence on top of the full chunks.
+        const size_t chunks = (size_t(max_tokens) + 63) / 64 + size_t(st->batch);
+        const size_t floats =
+            q38::linear_prefill_scratch_floats(int(chunks), st->ctx->geom.linear_v_heads);
+        Q38_CUDA(cudaMalloc(&st->prefill_lin, floats * sizeof(float)));
+        st->prefill_chunks = chunks;
+    }
     st->prefill_tokens = size_t(max_tokens);
     return Q38_OK;
 }
@@ -652,6 +666,50 @@ int q38_full_prefill(q38_ctx *ctx, q38_state *st, int layer, int seq0, int nseq,
     DeviceGuard guard(ctx->device);
     cudaError_t e = q38::launch_attn_prefill(a, static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return cuda_fail(e, "full-attention prefill launch");
+    return Q38_OK;
+}
+
+int q38_linear_prefill(q38_ctx *ctx, q38_state *st, int layer, int seq0, int nseq, int count,
+                       float *qkv, const float *z, float *beta, float *alpha, float *attention,
+                       void *stream) {
+    if (int rc = check_state(ctx, st)) return rc;
+    int slot;
+    if (int rc = linear_slot_of(st, layer, &slot)) return rc;
+    if (nseq <= 0 || seq0 < 0 || seq0 + nseq > st->batch)
+        return fail(Q38_ERR_ARG, "sequences [%d, %d) outside the state's %d", seq0, seq0 + nseq,
+                    st->batch);
+    if (count <= 0) return fail(Q38_ERR_ARG, "count must be positive");
+    const size_t chunks = size_t(nseq) * ((size_t(count) + 63) / 64);
+    if (size_t(nseq) * size_t(count) > st->prefill_tokens || chunks > st->prefill_chunks)
+        return fail(Q38_ERR_ARG, "%d tokens exceed the reserved prefill scratch (%zu)",
+                    nseq * count, st->prefill_tokens);
+    if (!qkv || !z || !beta || !alpha || !attention)
+        return fail(Q38_ERR_ARG, "null tensor argument");
+    auto it = ctx->linear.find(layer);
+    if (it == ctx->linear.end())
+        return fail(Q38_ERR_ARG, "DeltaNet layer %d has no bound weights", layer);
+    q38::LinearPrefillLaunch a{};
+    a.qkv = qkv;
+    a.z = z;
+    a.beta = beta;
+    a.alpha = alpha;
+    a.attention = attention;
+    a.conv_state = st->conv_state + size_t(slot) * st->batch * conv_seq_floats(ctx);
+    a.delta_state = st->delta_state + size_t(slot) * st->batch * delta_seq_floats(ctx);
+    a.conv_w = it->second.conv_w;
+    a.dt_bias = it->second.dt_bias;
+    a.ssm_a = it->second.ssm_a;
+    a.ssm_norm = it->second.ssm_norm;
+    a.scratch = st->prefill_lin;
+    a.seq0 = seq0;
+    a.nseq = nseq;
+    a.count = count;
+    a.qk_heads = ctx->geom.linear_qk_heads;
+    a.v_heads = ctx->geom.linear_v_heads;
+    a.eps = ctx->geom.rms_eps;
+    DeviceGuard guard(ctx->device);
+    cudaError_t e = q38::launch_linear_prefill(a, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "DeltaNet prefill launch");
     return Q38_OK;
 }
 

@@ -306,6 +306,18 @@ class Context:
                                          _dev_ptr(key, "key"), _dev_ptr(value, "value"),
                                          _dev_ptr(attention, "attention"), _stream_ptr(stream)))
 
+    def linear_prefill(self, state: State, layer: int, seq0: int, qkv, z, beta, alpha,
+                       attention, stream=None) -> None:
+        """Chunked DeltaNet prefill of qkv.shape[1] tokens for qkv.shape[0]
+        sequences starting at seq0 (the per-token linear_core loop of
+        batch_linear_attention, src/model/ops.rs:1088-1099)."""
+        nseq, count = qkv.shape[0], qkv.shape[1]
+        check(self._lib.q38_linear_prefill(self.handle, state.handle, layer, seq0, nseq, count,
+                                           _dev_ptr(qkv, "qkv"), _dev_ptr(z, "z"),
+                                           _dev_ptr(beta, "beta"), _dev_ptr(alpha, "alpha"),
+                                           _dev_ptr(attention, "attention"),
+                                           _stream_ptr(stream)))
+
     # host pointers, batched, synchronous -----------------------------------
     def full_decode_host(self, state: State, layer: int, q_and_gate: np.ndarray,
                          key: np.ndarray, value: np.ndarray, positions: np.ndarray,

@@ -78,6 +78,8 @@ SIGNATURES = {
     "q38_state_reserve_prefill": (c_int, [_VP, c_int]),
     "q38_full_prefill": (c_int, [_VP, _VP, c_int, c_int, c_int, c_int, c_int, _VP, _VP, _VP, _VP,
                                  _VP]),
+    "q38_linear_prefill": (c_int, [_VP, _VP, c_int, c_int, c_int, c_int, _VP, _VP, _VP, _VP,
+                                   _VP, _VP]),
     "q38_full_decode_host": (c_int, [_VP, _VP, c_int, c_int, _VP, _VP, _VP, _VP, _VP, _VP]),
     "q38_linear_decode_host": (c_int, [_VP, _VP, c_int, c_int, _VP, _VP, _VP, _VP, _VP, _VP]),
     "q38_linear_core": (c_int, [_VP, _VP, c_int, _VP, _VP, _VP, _VP, _VP, _VP, _VP]),
