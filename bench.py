@@ -149,6 +149,53 @@ def run_prefill(args, ctx, q38attn, synth, torch, rank: int) -> dict:
     return {"ms": ms}
 
 
+def linear_prefill_flops(batch: int, seq: int) -> float:
+    """Chunked DeltaNet prefill FLOPs (config 5, C=64, dk=dv=128, 48 value heads):
+    per chunk and head 2*(C*C*dk [KK^T] + C*C*dk [W] + C*C*dv [Ut] + C*dk*dv [WS]
+    + C*C*dk [QK^T] + C*dk*dv [QS] + C*C*dv [PU] + C*dk*dv [state])."""
+    C, dk = 64, 128
+    per_chunk = 2 * (5 * C * C * dk + 3 * C * dk * dk)
+    return float(batch) * 48 * (seq // C) * per_chunk
+
+
+def run_linear_prefill(args, ctx, q38attn, torch, rank: int) -> dict:
+    """Config 5: chunked DeltaNet prefill of `prefill_batch` prompts of
+    `prefill_len` tokens through one DeltaNet layer from a zero state."""
+    B, S = args.prefill_batch, args.prefill_len
+    layer = LINEAR_LAYERS[0]
+    st = ctx.state(B, 16, full_slots=0, linear_slots=1)
+    st.reserve_prefill(B * S)
+    tg = torch.Generator(device="cuda")
+    tg.manual_seed(args.seed + 99 + rank)
+    qkv0 = torch.randn(B, S, 10240, device="cuda", generator=tg)
+    z = torch.randn(B, S, 6144, device="cuda", generator=tg)
+    b0 = torch.randn(B, S, 48, device="cuda", generator=tg)
+    a0 = torch.randn(B, S, 48, device="cuda", generator=tg)
+    qkv, beta, alpha = torch.empty_like(qkv0), torch.empty_like(b0), torch.empty_like(a0)
+    att = torch.empty(B, S, 6144, device="cuda")
+    stream = torch.cuda.current_stream()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(args.prefill_iters)]
+    for it in range(2 + args.prefill_iters):
+        st.reset(stream)  # a fresh prompt each time (zero conv and delta state)
+        qkv.copy_(qkv0)   # qkv/beta/alpha are rewritten in place
+        beta.copy_(b0)
+        alpha.copy_(a0)
+        if it >= 2:
+            evs[it - 2][0].record(stream)
+        ctx.linear_prefill(st, layer, 0, qkv, z, beta, alpha, att, stream=stream)
+        if it >= 2:
+            evs[it - 2][1].record(stream)
+    torch.cuda.synchronize()
+    if st.errors():
+        raise RuntimeError("device error bits set during DeltaNet prefill")
+    ms = statistics.median(a.elapsed_time(b) for a, b in evs)
+    st.close()
+    del qkv0, z, b0, a0, qkv, beta, alpha, att
+    torch.cuda.empty_cache()
+    return {"ms": ms}
+
+
 def load_traffic_profile() -> dict | None:
     p = REPO / "profiles" / "attn_decode_traffic.json"
     if p.exists():
@@ -453,9 +500,10 @@ def run_ours(args) -> None:
     if st.errors():
         raise RuntimeError("device error bits set during the timed region")
 
-    prefill = None
+    prefill = lin_prefill = None
     if not args.no_prefill:
         prefill = run_prefill(args, ctx, q38attn, synth, torch, rank)
+        lin_prefill = run_linear_prefill(args, ctx, q38attn, torch, rank)
 
     # End-to-end through the host-pointer C-ABI calls.
     e2e = None
@@ -487,10 +535,12 @@ def run_ours(args) -> None:
 
     # Max over ranks.
     vals = torch.tensor([ms, attn_ms, lin_ms, e2e[0] if e2e else 0.0,
-                         prefill["ms"] if prefill else 0.0], device="cuda", dtype=torch.float64)
+                         prefill["ms"] if prefill else 0.0,
+                         lin_prefill["ms"] if lin_prefill else 0.0],
+                        device="cuda", dtype=torch.float64)
     if dist is not None:
         dist.all_reduce(vals, op=dist.ReduceOp.MAX)
-    ms, attn_ms, lin_ms, e2e_s, prefill_ms = vals.tolist()
+    ms, attn_ms, lin_ms, e2e_s, prefill_ms, lin_prefill_ms = vals.tolist()
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -540,6 +590,16 @@ def run_ours(args) -> None:
                              "unit": "TFLOP/s", "frac": tflops / tpeak,
                              "peak_source": f"{tpeak_kind} bf16_tflops (burst)",
                              "kernel": "prep + attn_prefill (one op)"},
+            }
+        if lin_prefill:
+            flops = linear_prefill_flops(args.prefill_batch, args.prefill_len) * world
+            toks = args.prefill_batch * args.prefill_len * world
+            line["deltanet_prefill"] = {
+                "workload": (f"config5: {args.prefill_batch} x {args.prefill_len}-token chunked "
+                             "Gated DeltaNet prefill per GPU (C=64, 16K/48V x 128) from a zero "
+                             "state, outputs + final f32 state; f32 CUDA cores"),
+                "ms": lin_prefill_ms, "tok_s": toks / (lin_prefill_ms * 1e-3),
+                "flops": flops, "tflops": flops / (lin_prefill_ms * 1e-3) / 1e12,
             }
         if e2e:
             line["e2e"] = {"value": tokens * e2e_steps / e2e_s, "unit": "tok/s",
