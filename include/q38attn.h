@@ -164,6 +164,28 @@ int q38_full_decode(q38_ctx *ctx, q38_state *st, int layer, int batch, const flo
                     float *key, const float *value, const int32_t *positions, int max_position,
                     float *attention, void *stream);
 
+/* Split-sequence decode, shard side: this state holds global positions
+ * pos_offset .. pos_offset+context_length-1 of each sequence (one contiguous
+ * range per GPU). Runs the same prep and split-KV attention over the rows this
+ * shard holds that are <= positions[b] (RoPE at the global position; the new
+ * K/V row is appended only by the shard whose range contains it) and writes,
+ * instead of the output, the shard's softmax partial per (sequence, head):
+ *   partials [batch][heads][258] f32 = o[256] (sum of exp(s-m) v), m, l
+ * (m = -inf, l = 0 for a shard with no visible row). Replaces the position
+ * loop of full_core (ops.rs:884-913) for one range of positions. */
+int q38_full_decode_shard(q38_ctx *ctx, q38_state *st, int layer, int batch,
+                          const float *q_and_gate, float *key, const float *value,
+                          const int32_t *positions, int max_position, int pos_offset,
+                          float *partials, void *stream);
+
+/* Split-sequence decode, merge side: combines nparts shard partials
+ * [nparts][batch][heads][258] (gathered from every shard, e.g. by an NCCL
+ * all-gather) by log-sum-exp, normalises and applies the sigmoid output gate
+ * of q_and_gate [batch][heads*512] (ops.rs:898-919) into attention
+ * [batch][heads*256]. DEVICE pointers, stream-ordered. */
+int q38_attn_merge_shards(q38_ctx *ctx, int nparts, int batch, const float *partials,
+                          const float *q_and_gate, float *attention, void *stream);
+
 /* One Gated DeltaNet decode step for `batch` sequences (linear_core,
  * src/model/ops.rs:647-742, batched). DEVICE pointers:
  *   qkv   [batch][qkv_dim]  in: projections; out: conv+SiLU+L2 values (as the

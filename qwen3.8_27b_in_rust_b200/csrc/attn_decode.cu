@@ -58,9 +58,21 @@ struct PrepParams {
     float *qprep;
     int *err;
     const float *q_norm, *k_norm;
-    int context_length, heads, kv_heads, max_position;
+    int context_length, heads, kv_heads, max_position, pos_offset, sharded;
     float theta_scale, eps;
 };
+
+// A sequence at global position pos appends its K/V row at local cache row
+// pos - pos_offset (pos_offset is 0 unless the sequence's positions are
+// sharded across GPUs); RoPE always uses the global position. Unsharded, a
+// position outside the cache is an error; sharded, a position past this
+// shard's range only means the shard contributes all its rows and appends
+// nothing.
+__device__ __forceinline__ bool position_ok(int pos, int pos_offset, int context_length,
+                                            int max_position, int sharded) {
+    if (pos < 0 || pos > max_position) return false;
+    return sharded || pos - pos_offset < context_length;
+}
 
 template <typename KV>
 __global__ void __launch_bounds__(kAttnHeadDim) attn_decode_prep_kernel(PrepParams p) {
@@ -70,10 +82,12 @@ __global__ void __launch_bounds__(kAttnHeadDim) attn_decode_prep_kernel(PrepPara
     __shared__ float xs[kAttnHeadDim];
     const int h = blockIdx.x, b = blockIdx.y, i = threadIdx.x;
     const int pos = p.positions[b];
-    if (pos < 0 || pos >= p.context_length || pos > p.max_position) {
+    if (!position_ok(pos, p.pos_offset, p.context_length, p.max_position, p.sharded)) {
         if (h == 0 && i == 0) set_error(p.err, kDevErrPosition);
         return;
     }
+    // Local row of the new K/V; outside [0, context_length) another shard owns it.
+    const int row_local = pos - p.pos_offset;
     const bool is_q = h < p.heads;
     const int kvh = h - p.heads;
     float x = is_q ? p.q_and_gate[(size_t(b) * p.heads + h) * 2 * kAttnHeadDim + i]
@@ -102,10 +116,12 @@ __global__ void __launch_bounds__(kAttnHeadDim) attn_decode_prep_kernel(PrepPara
     } else {
         const size_t kv_off = (size_t(b) * p.kv_heads + kvh) * kAttnHeadDim + i;
         p.key[kv_off] = x;
-        const size_t row =
-            ((size_t(b) * p.kv_heads + kvh) * p.context_length + pos) * kAttnHeadDim + i;
-        static_cast<KV *>(p.kcache)[row] = KvTraits<KV>::store(x);
-        static_cast<KV *>(p.vcache)[row] = KvTraits<KV>::store(p.value[kv_off]);
+        if (row_local >= 0 && row_local < p.context_length) {
+            const size_t row =
+                ((size_t(b) * p.kv_heads + kvh) * p.context_length + row_local) * kAttnHeadDim + i;
+            static_cast<KV *>(p.kcache)[row] = KvTraits<KV>::store(x);
+            static_cast<KV *>(p.vcache)[row] = KvTraits<KV>::store(p.value[kv_off]);
+        }
     }
 }
 
@@ -118,8 +134,13 @@ struct SplitParams {
     const int32_t *positions;
     float *part_o, *part_ml;
     int *err;
-    int context_length, heads, kv_heads, chunk, max_splits, max_position;
+    int context_length, heads, kv_heads, chunk, max_splits, max_position, pos_offset, sharded;
 };
+
+// Rows of the local cache a sequence at global position pos attends to.
+__device__ __forceinline__ int local_rows(int pos, int pos_offset, int context_length) {
+    return min(pos - pos_offset + 1, context_length);
+}
 
 // Dimension of the head that slot j (0..7) of lane `lane` owns. bf16 rows are
 // 512 B: lane l owns dims [8l, 8l+8), one 16-byte load. f32 rows are 1 KB:
@@ -279,8 +300,8 @@ __global__ void __launch_bounds__(kThreads, 2) attn_decode_split_kernel(SplitPar
     const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int pos = p.positions[b];
-    if (pos < 0 || pos >= p.context_length || pos > p.max_position) return;
-    const int n = pos + 1;
+    if (!position_ok(pos, p.pos_offset, p.context_length, p.max_position, p.sharded)) return;
+    const int n = local_rows(pos, p.pos_offset, p.context_length);
     const int start = split * p.chunk;
     if (start >= n) return;
     const int cnt = min(n, start + p.chunk) - start;
@@ -449,15 +470,17 @@ struct MergeParams {
     const float *q_and_gate;
     const int32_t *positions;
     float *attention;
-    int context_length, heads, chunk, max_splits, max_position;
+    float *partial_out;  // non-null: write (o, m, l) [batch][heads][258] instead
+    int context_length, heads, chunk, max_splits, max_position, pos_offset, sharded;
 };
 
 __global__ void __launch_bounds__(kAttnHeadDim) attn_decode_merge_kernel(MergeParams p) {
     const int h = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
     const int pos = p.positions[b];
     pdl_wait_primary();
-    if (pos < 0 || pos >= p.context_length || pos > p.max_position) return;
-    const int nsplit = (pos + p.chunk) / p.chunk;  // ceil((pos+1)/chunk)
+    if (!position_ok(pos, p.pos_offset, p.context_length, p.max_position, p.sharded)) return;
+    const int n = local_rows(pos, p.pos_offset, p.context_length);
+    const int nsplit = n > 0 ? (n + p.chunk - 1) / p.chunk : 0;
     const size_t base = (size_t(b) * p.heads + h) * p.max_splits;
     const float2 *ml = reinterpret_cast<const float2 *>(p.part_ml) + base;
     float m = -INFINITY;
@@ -468,6 +491,45 @@ __global__ void __launch_bounds__(kAttnHeadDim) attn_decode_merge_kernel(MergePa
         const float w = expf(v.x - m);
         l += w * v.y;
         o += w * p.part_o[(base + s) * kAttnHeadDim + d];
+    }
+    if (p.partial_out) {
+        // This shard's (o, m, l) relative to its own max m (m = -inf, l = 0,
+        // o = 0 when the shard holds no visible row).
+        float *dst = p.partial_out + (size_t(b) * p.heads + h) * (kAttnHeadDim + 2);
+        dst[d] = nsplit > 0 ? o : 0.f;
+        if (d == 0) {
+            dst[kAttnHeadDim] = m;
+            dst[kAttnHeadDim + 1] = l;
+        }
+        return;
+    }
+    const float gate = p.q_and_gate[(size_t(b) * p.heads + h) * 2 * kAttnHeadDim + kAttnHeadDim + d];
+    p.attention[(size_t(b) * p.heads + h) * kAttnHeadDim + d] = (o / l) * sigmoidf_ref(gate);
+}
+
+// Cross-shard merge: nparts packed (o, m, l) partials per (sequence, head),
+// [nparts][batch][heads][258], combined by log-sum-exp, normalised and gated.
+struct ShardMergeParams {
+    const float *partials;
+    const float *q_and_gate;
+    float *attention;
+    int nparts, batch, heads;
+};
+
+__global__ void __launch_bounds__(kAttnHeadDim) attn_merge_shards_kernel(ShardMergeParams p) {
+    const int h = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
+    const size_t stride = size_t(p.batch) * p.heads * (kAttnHeadDim + 2);
+    const float *base = p.partials + (size_t(b) * p.heads + h) * (kAttnHeadDim + 2);
+    float m = -INFINITY;
+    for (int r = 0; r < p.nparts; ++r) m = fmaxf(m, base[r * stride + kAttnHeadDim]);
+    float l = 0.f, o = 0.f;
+    for (int r = 0; r < p.nparts; ++r) {
+        const float *part = base + r * stride;
+        const float mr = part[kAttnHeadDim];
+        if (mr == -INFINITY) continue;  // an empty shard
+        const float w = expf(mr - m);
+        l += w * part[kAttnHeadDim + 1];
+        o += w * part[d];
     }
     const float gate = p.q_and_gate[(size_t(b) * p.heads + h) * 2 * kAttnHeadDim + kAttnHeadDim + d];
     p.attention[(size_t(b) * p.heads + h) * kAttnHeadDim + d] = (o / l) * sigmoidf_ref(gate);
@@ -483,13 +545,16 @@ int env_chunk_override() {
 
 template <typename KV>
 cudaError_t launch_typed(const AttnDecodeLaunch &a, int sm_count, cudaStream_t stream) {
+    // Rows any sequence of this call attends to in the local cache.
+    const int max_rows = std::min(a.max_position - a.pos_offset + 1, a.context_length);
     const DecodeSplitPlan plan =
-        plan_attn_decode(a.batch, a.kv_heads, a.max_position, a.kv_dtype, sm_count);
+        plan_attn_decode(a.batch, a.kv_heads, std::max(max_rows, 1) - 1, a.kv_dtype, sm_count);
     if (plan.nsplit > a.max_splits) return cudaErrorInvalidValue;
 
-    PrepParams pp{a.q_and_gate, a.key,    a.value,    a.positions,  a.kcache,     a.vcache,
-                  a.qprep,      a.err,    a.q_norm,   a.k_norm,     a.context_length,
-                  a.heads,      a.kv_heads, a.max_position, a.theta_scale, a.eps};
+    PrepParams pp{a.q_and_gate, a.key,      a.value,        a.positions,  a.kcache,
+                  a.vcache,     a.qprep,    a.err,          a.q_norm,     a.k_norm,
+                  a.context_length, a.heads, a.kv_heads,    a.max_position, a.pos_offset,
+                  a.partial_out != nullptr, a.theta_scale, a.eps};
     attn_decode_prep_kernel<KV>
         <<<dim3(a.heads + a.kv_heads, a.batch), kAttnHeadDim, 0, stream>>>(pp);
     cudaError_t e = cudaGetLastError();
@@ -499,9 +564,10 @@ cudaError_t launch_typed(const AttnDecodeLaunch &a, int sm_count, cudaStream_t s
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
 
-    SplitParams sp{a.kcache, a.vcache, a.qprep,    a.positions,  a.part_o,   a.part_ml,
-                   a.err,    a.context_length, a.heads, a.kv_heads, plan.chunk,
-                   a.max_splits, a.max_position};
+    SplitParams sp{a.kcache,   a.vcache,  a.qprep,  a.positions,       a.part_o,
+                   a.part_ml,  a.err,     a.context_length, a.heads, a.kv_heads,
+                   plan.chunk, a.max_splits, a.max_position, a.pos_offset,
+                   a.partial_out != nullptr};
     const size_t smem = size_t(kStages) * kTileBytes + size_t(plan.chunk) * 8 * sizeof(float);
     e = cudaFuncSetAttribute(attn_decode_split_kernel<KV>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -517,8 +583,9 @@ cudaError_t launch_typed(const AttnDecodeLaunch &a, int sm_count, cudaStream_t s
     e = cudaLaunchKernelEx(&cfg, attn_decode_split_kernel<KV>, sp);
     if (e != cudaSuccess) return e;
 
-    MergeParams mp{a.part_o, a.part_ml, a.q_and_gate, a.positions, a.attention,
-                   a.context_length, a.heads, plan.chunk, a.max_splits, a.max_position};
+    MergeParams mp{a.part_o,   a.part_ml,  a.q_and_gate, a.positions,  a.attention,
+                   a.partial_out, a.context_length, a.heads, plan.chunk, a.max_splits,
+                   a.max_position, a.pos_offset, a.partial_out != nullptr};
     cfg.gridDim = dim3(a.heads, a.batch);
     cfg.blockDim = dim3(kAttnHeadDim);
     cfg.dynamicSmemBytes = 0;
@@ -554,6 +621,14 @@ DecodeSplitPlan plan_attn_decode(int batch, int kv_heads, int max_position, int 
     plan.chunk = chunk;
     plan.nsplit = (n + chunk - 1) / chunk;
     return plan;
+}
+
+cudaError_t launch_attn_merge_shards(const float *partials, int nparts, int batch, int heads,
+                                     const float *q_and_gate, float *attention,
+                                     cudaStream_t stream) {
+    ShardMergeParams p{partials, q_and_gate, attention, nparts, batch, heads};
+    attn_merge_shards_kernel<<<dim3(heads, batch), kAttnHeadDim, 0, stream>>>(p);
+    return cudaGetLastError();
 }
 
 cudaError_t launch_attn_decode(const AttnDecodeLaunch &a, int sm_count, cudaStream_t stream) {

@@ -98,8 +98,13 @@ struct AttnDecodeLaunch {
     const float *q_norm, *k_norm;
     int batch, context_length, heads, kv_heads, kv_dtype, max_position, max_splits;
     float theta_scale, eps;
+    int pos_offset = 0;            // first global position held by this cache (sharding)
+    float *partial_out = nullptr;  // non-null: packed (o, m, l) partials instead of output
 };
 cudaError_t launch_attn_decode(const AttnDecodeLaunch &a, int sm_count, cudaStream_t stream);
+cudaError_t launch_attn_merge_shards(const float *partials, int nparts, int batch, int heads,
+                                     const float *q_and_gate, float *attention,
+                                     cudaStream_t stream);
 DecodeSplitPlan plan_attn_decode(int batch, int kv_heads, int max_position, int kv_dtype,
                                  int sm_count);
 int attn_decode_max_splits(int context_length, int kv_dtype);

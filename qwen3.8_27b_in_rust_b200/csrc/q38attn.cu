@@ -167,22 +167,24 @@ void free_state(q38_state *st) {
 }
 
 // Validates a decode call and fills the launch arguments (device pointers).
+// Sharded calls (split-sequence decode) write partials instead of `attention`
+// and may see positions past this shard's capacity.
 int prepare_full_decode(q38_ctx *ctx, q38_state *st, int layer, int batch,
                         const float *q_and_gate, float *key, const float *value,
                         const int32_t *positions, int max_position, float *attention,
-                        q38::AttnDecodeLaunch *a) {
+                        q38::AttnDecodeLaunch *a, bool sharded = false) {
     if (int rc = check_state(ctx, st)) return rc;
     int slot;
     if (int rc = full_slot_of(st, layer, &slot)) return rc;
     if (batch <= 0 || batch > st->batch)
         return fail(Q38_ERR_ARG, "batch %d outside 1..%d", batch, st->batch);
-    if (!q_and_gate || !key || !value || !positions || !attention)
+    if (!q_and_gate || !key || !value || !positions || (!attention && !sharded))
         return fail(Q38_ERR_ARG, "null tensor argument");
     auto it = ctx->full.find(layer);
     if (it == ctx->full.end())
         return fail(Q38_ERR_ARG, "full-attention layer %d has no bound weights", layer);
     if (max_position < 0) max_position = st->context_length - 1;
-    if (max_position >= st->context_length)
+    if (!sharded && max_position >= st->context_length)
         return fail(Q38_ERR_ARG, "max_position %d >= context_length %d", max_position,
                     st->context_length);
     const q38_geom &g = ctx->geom;
@@ -577,6 +579,39 @@ int q38_full_decode(q38_ctx *ctx, q38_state *st, int layer, int batch, const flo
     DeviceGuard guard(ctx->device);
     cudaError_t e = q38::launch_attn_decode(a, ctx->sm_count, static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return cuda_fail(e, "full-attention decode launch");
+    return Q38_OK;
+}
+
+int q38_full_decode_shard(q38_ctx *ctx, q38_state *st, int layer, int batch,
+                          const float *q_and_gate, float *key, const float *value,
+                          const int32_t *positions, int max_position, int pos_offset,
+                          float *partials, void *stream) {
+    if (int rc = check_state(ctx, st)) return rc;
+    if (pos_offset < 0) return fail(Q38_ERR_ARG, "pos_offset must be >= 0");
+    if (!partials) return fail(Q38_ERR_ARG, "null partials");
+    if (max_position < 0) return fail(Q38_ERR_ARG, "max_position is required when sharding");
+    q38::AttnDecodeLaunch a;
+    if (int rc = prepare_full_decode(ctx, st, layer, batch, q_and_gate, key, value, positions,
+                                     max_position, nullptr, &a, true))
+        return rc;
+    a.pos_offset = pos_offset;
+    a.partial_out = partials;
+    DeviceGuard guard(ctx->device);
+    cudaError_t e = q38::launch_attn_decode(a, ctx->sm_count, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "sharded full-attention decode launch");
+    return Q38_OK;
+}
+
+int q38_attn_merge_shards(q38_ctx *ctx, int nparts, int batch, const float *partials,
+                          const float *q_and_gate, float *attention, void *stream) {
+    if (int rc = check_ctx(ctx)) return rc;
+    if (nparts <= 0 || batch <= 0) return fail(Q38_ERR_ARG, "nparts and batch must be positive");
+    if (!partials || !q_and_gate || !attention) return fail(Q38_ERR_ARG, "null tensor argument");
+    DeviceGuard guard(ctx->device);
+    cudaError_t e = q38::launch_attn_merge_shards(partials, nparts, batch, ctx->geom.attn_heads,
+                                                  q_and_gate, attention,
+                                                  static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "shard merge launch");
     return Q38_OK;
 }
 

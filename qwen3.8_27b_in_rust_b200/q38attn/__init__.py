@@ -286,6 +286,27 @@ class Context:
                                         max_position, _dev_ptr(attention, "attention"),
                                         _stream_ptr(stream)))
 
+    def full_decode_shard(self, state: State, layer: int, q_and_gate, key, value, positions,
+                          partials, max_position: int, pos_offset: int, stream=None) -> None:
+        """Split-sequence decode, shard side: writes this shard's (o, m, l)
+        partials [batch][24][258] over its positions pos_offset.. (see
+        q38_full_decode_shard)."""
+        b = q_and_gate.shape[0]
+        check(self._lib.q38_full_decode_shard(
+            self.handle, state.handle, layer, b, _dev_ptr(q_and_gate, "q_and_gate"),
+            _dev_ptr(key, "key"), _dev_ptr(value, "value"),
+            _dev_ptr(positions, "positions", "int32"), max_position, pos_offset,
+            _dev_ptr(partials, "partials"), _stream_ptr(stream)))
+
+    def merge_shards(self, partials, q_and_gate, attention, stream=None) -> None:
+        """Split-sequence decode, merge side: partials [nparts][batch][24][258]."""
+        nparts, b = partials.shape[0], partials.shape[1]
+        check(self._lib.q38_attn_merge_shards(self.handle, nparts, b,
+                                              _dev_ptr(partials, "partials"),
+                                              _dev_ptr(q_and_gate, "q_and_gate"),
+                                              _dev_ptr(attention, "attention"),
+                                              _stream_ptr(stream)))
+
     def linear_decode(self, state: State, layer: int, qkv, z, beta, alpha, attention,
                       stream=None) -> None:
         b = qkv.shape[0]

@@ -72,6 +72,9 @@ SIGNATURES = {
     "q38_state_upload_linear": (c_int, [_VP, c_int, c_int, _VP, _VP]),
     "q38_state_download_linear": (c_int, [_VP, c_int, c_int, _VP, _VP]),
     "q38_full_decode": (c_int, [_VP, _VP, c_int, c_int, _VP, _VP, _VP, _VP, c_int, _VP, _VP]),
+    "q38_full_decode_shard": (c_int, [_VP, _VP, c_int, c_int, _VP, _VP, _VP, _VP, c_int, c_int,
+                                      _VP, _VP]),
+    "q38_attn_merge_shards": (c_int, [_VP, c_int, c_int, _VP, _VP, _VP, _VP]),
     "q38_linear_decode": (c_int, [_VP, _VP, c_int, c_int, _VP, _VP, _VP, _VP, _VP, _VP]),
     "q38_full_decode_noalloc": (c_int, [_VP, _VP, _VP, _VP, c_int, c_int, c_int, _VP, _VP, _VP,
                                         _VP, c_int, _VP, _VP, _VP]),
