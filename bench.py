@@ -64,6 +64,9 @@ def parse_args():
     ap.add_argument("--prefill-len", type=int, default=8192)
     ap.add_argument("--prefill-iters", type=int, default=5)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-split", action="store_true")
+    ap.add_argument("--split-context", type=int, default=131072)
+    ap.add_argument("--split-steps", type=int, default=50)
     return ap.parse_args()
 
 
@@ -193,6 +196,60 @@ def run_linear_prefill(args, ctx, q38attn, torch, rank: int) -> dict:
     st.close()
     del qkv0, z, b0, a0, qkv, beta, alpha, att
     torch.cuda.empty_cache()
+    return {"ms": ms}
+
+
+def run_split_sequence(args, ctx, q38attn, torch, dist, rank: int, world: int) -> dict:
+    """Config 3, split-sequence variant: one sequence with `split_context`
+    cached bf16 positions, sharded into contiguous ranges across the ranks;
+    each decode step computes per-shard softmax partials, all-gathers them over
+    NCCL and merges (q38attn.parallel.SplitSequenceDecoder). At one GPU the
+    plain decode runs over the whole range."""
+    from q38attn.parallel import SplitSequenceDecoder, position_ranges
+    P = args.split_context
+    cap = P + args.split_steps + 8
+    p0, p1 = position_ranges(cap, world)[rank]
+    st = ctx.state(1, p1 - p0, full_slots=1, linear_slots=0, kv_dtype=q38attn.Q38_KV_BF16)
+    kview, vview = st.kv_views(FULL_LAYER)
+    tg = torch.Generator(device="cuda")
+    tg.manual_seed(args.seed + 555 + rank)
+    n = max(0, min(p1, P) - p0)
+    if n:
+        kview[0, :, :n].normal_(generator=tg)
+        vview[0, :, :n].normal_(generator=tg)
+    del kview, vview
+    qg = torch.randn(1, 12288, device="cuda", generator=tg)
+    key0 = torch.randn(1, 1024, device="cuda", generator=tg)
+    val = torch.randn(1, 1024, device="cuda", generator=tg)
+    key = torch.empty_like(key0)
+    out = torch.empty(1, 6144, device="cuda")
+    pos = torch.arange(P, P + args.split_steps + 3, device="cuda", dtype=torch.int32)
+    dec = SplitSequenceDecoder(ctx, st, FULL_LAYER, p0) if world > 1 else None
+    stream = torch.cuda.current_stream()
+
+    def one(i):
+        key.copy_(key0)
+        if dec is not None:
+            dec.step(qg, key, val, pos[i:i + 1], out, cap - 1, stream=stream)
+        else:
+            ctx.full_decode(st, FULL_LAYER, qg, key, val, pos[i:i + 1], out,
+                            max_position=P + i, stream=stream)
+
+    for i in range(3):
+        one(i)
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(args.split_steps):
+        one(3 + i)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.split_steps
+    if st.errors():
+        raise RuntimeError("device error bits set during split-sequence decode")
+    st.close()
     return {"ms": ms}
 
 
@@ -500,6 +557,10 @@ def run_ours(args) -> None:
     if st.errors():
         raise RuntimeError("device error bits set during the timed region")
 
+    split = None
+    if not args.no_split:
+        split = run_split_sequence(args, ctx, q38attn, torch, dist, rank, world)
+
     prefill = lin_prefill = None
     if not args.no_prefill:
         prefill = run_prefill(args, ctx, q38attn, synth, torch, rank)
@@ -536,11 +597,12 @@ def run_ours(args) -> None:
     # Max over ranks.
     vals = torch.tensor([ms, attn_ms, lin_ms, e2e[0] if e2e else 0.0,
                          prefill["ms"] if prefill else 0.0,
-                         lin_prefill["ms"] if lin_prefill else 0.0],
+                         lin_prefill["ms"] if lin_prefill else 0.0,
+                         split["ms"] if split else 0.0],
                         device="cuda", dtype=torch.float64)
     if dist is not None:
         dist.all_reduce(vals, op=dist.ReduceOp.MAX)
-    ms, attn_ms, lin_ms, e2e_s, prefill_ms, lin_prefill_ms = vals.tolist()
+    ms, attn_ms, lin_ms, e2e_s, prefill_ms, lin_prefill_ms, split_ms = vals.tolist()
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -590,6 +652,15 @@ def run_ours(args) -> None:
                              "unit": "TFLOP/s", "frac": tflops / tpeak,
                              "peak_source": f"{tpeak_kind} bf16_tflops (burst)",
                              "kernel": "prep + attn_prefill (one op)"},
+            }
+        if split:
+            kv_bytes = args.split_context * 4 * 256 * 2 * 2
+            line["split_sequence"] = {
+                "workload": (f"config3 split-sequence: 1 sequence, {args.split_context} cached "
+                             f"bf16 positions sharded over {world} GPU(s); per-shard partials, "
+                             "NCCL all-gather, LSE merge (strong scaling)"),
+                "ms_per_token": split_ms, "tok_s": 1e3 / split_ms,
+                "kv_gbs": kv_bytes / (split_ms * 1e-3) / 1e9,
             }
         if lin_prefill:
             flops = linear_prefill_flops(args.prefill_batch, args.prefill_len) * world
