@@ -131,7 +131,7 @@ struct __align__(8) PrefillBarriers {
     uint64_t q_full, q_copied;
     uint64_t k_full[kStagesKV], k_empty[kStagesKV], v_full[kStagesKV], v_empty[kStagesKV];
     uint64_t v_conv[kStagesKV];
-    uint64_t s_full[2], p_full[2], o_done;
+    uint64_t s_full[2], p_full[2], o_done, o_final;
 };
 
 __device__ __forceinline__ float ex2(float x) {
@@ -188,6 +188,7 @@ __global__ void __launch_bounds__(kThreadsPF, 1)
             mbar_init(&bar.p_full[b], 128);
         }
         mbar_init(&bar.o_done, 1);
+        mbar_init(&bar.o_final, 1);
         fence_barrier_init();
     }
     if (warp == 1) {
@@ -271,6 +272,10 @@ __global__ void __launch_bounds__(kThreadsPF, 1)
                 if (abort_flag) { ok = false; break; }
             }
             if (ok && !pv(nkt - 1)) ok = false;
+            // One completion for the epilogue: by the time the softmax warps
+            // wait, both of the last two PVs may have completed, which a parity
+            // wait on o_done cannot tell from "neither has".
+            if (ok) mma_commit(&bar.o_final);
             if (!ok) fail();
         }
     } else if (warp >= 6) {
@@ -416,10 +421,8 @@ __global__ void __launch_bounds__(kThreadsPF, 1)
             mbar_arrive(&bar.p_full[b]);
             if (__any_sync(0xffffffffu, abort_flag != 0)) { ok = false; break; }
         }
-        // Wait for the last two PVs in order (a parity wait must never be
-        // more than one phase ahead of the barrier), then the epilogue.
-        if (ok && nkt >= 2 && !wait_all(&bar.o_done, (nkt - 2) & 1)) ok = false;
-        if (ok && !wait_all(&bar.o_done, (nkt - 1) & 1)) ok = false;
+        // The epilogue waits on o_final, committed once after the last PV.
+        if (ok && !wait_all(&bar.o_final, 0)) ok = false;
         if (ok) {
             fence_after_sync();
             const float inv_l = 1.0f / l;
