@@ -3,7 +3,7 @@
 // (src/model/ops.rs:1156-1172): token t of the prompt attends to cache
 // positions 0..base+t, exactly as full_core at current_position = base+t.
 //
-//   P1 attn_prefill_prep  one CTA per (head, token, sequence): q/k RMSNorm
+//   P1 attn_prefill_prep  one CTA per (token, sequence), a warp per head: q/k RMSNorm
 //                         (f64 sum), partial RoPE (iterative f32 angle), K/V
 //                         append to the bf16 cache, key written back, and the
 //                         prepared query rounded to bf16 into the Q scratch
@@ -76,44 +76,83 @@ struct PrefillPrepParams {
     float theta_scale, eps;
 };
 
-__global__ void __launch_bounds__(kAttnHeadDim) attn_prefill_prep_kernel(PrefillPrepParams p) {
+// One CTA per (token, sequence); warp w handles heads w, w+8, ... of the
+// heads + kv_heads heads. Lane l holds dims [8l, 8l+8) of a head, so the RoPE
+// partner of dim i < 32 (dim i + 32) sits in lane l ^ 4 at the same slot.
+constexpr int kPrepWarps = 8;
+
+__global__ void __launch_bounds__(kPrepWarps * 32) attn_prefill_prep_kernel(PrefillPrepParams p) {
     pdl_launch_dependents();
-    __shared__ double red[32];
     __shared__ float cs[32], sn[32];
-    __shared__ float xs[kAttnHeadDim];
-    const int h = blockIdx.x, t = blockIdx.y, s = blockIdx.z, i = threadIdx.x;
+    const int t = blockIdx.x, s = blockIdx.y;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int pos = p.base + t;
-    const bool is_q = h < p.heads;
-    const int kvh = h - p.heads;
-    const size_t tok = size_t(s) * p.count + t;
-    float x = is_q ? p.q_and_gate[(tok * p.heads + h) * 2 * kAttnHeadDim + i]
-                   : p.key[(tok * p.kv_heads + kvh) * kAttnHeadDim + i];
-    const double sum = block_sum_f64(double(x) * double(x), red);
-    const float scale = rms_scale_from_sum(sum, kAttnHeadDim, p.eps);
-    x = x * scale * (is_q ? p.q_norm[i] : p.k_norm[i]);
-    if (i < kRopeDims / 2) {
+    // rope (ops.rs:595-610): theta_j = pos * scale^j by repeated f32 products.
+    if (threadIdx.x < kRopeDims / 2) {
         float theta = float(pos);
-        for (int j = 0; j < i; ++j) theta *= p.theta_scale;
-        cs[i] = cosf(theta);
-        sn[i] = sinf(theta);
+        for (int j = 0; j < int(threadIdx.x); ++j) theta *= p.theta_scale;
+        cs[threadIdx.x] = cosf(theta);
+        sn[threadIdx.x] = sinf(theta);
     }
-    xs[i] = x;
     __syncthreads();
-    if (i < kRopeDims / 2) {
-        x = xs[i] * cs[i] - xs[i + kRopeDims / 2] * sn[i];
-    } else if (i < kRopeDims) {
-        const int j = i - kRopeDims / 2;
-        x = xs[j] * sn[j] + xs[i] * cs[j];
-    }
-    if (is_q) {
-        p.qp[((size_t(s) * p.heads + h) * p.count + t) * kAttnHeadDim + i] = __float2bfloat16_rn(x);
-    } else {
-        const size_t off = (tok * p.kv_heads + kvh) * kAttnHeadDim + i;
-        p.key[off] = x;
-        const size_t row =
-            ((size_t(p.seq0 + s) * p.kv_heads + kvh) * p.context_length + pos) * kAttnHeadDim + i;
-        p.kcache[row] = __float2bfloat16_rn(x);
-        p.vcache[row] = __float2bfloat16_rn(p.value[off]);
+    const size_t tok = size_t(s) * p.count + t;
+    const int d0 = 8 * lane;
+    for (int h = warp; h < p.heads + p.kv_heads; h += kPrepWarps) {
+        const bool is_q = h < p.heads;
+        const int kvh = h - p.heads;
+        const float *src = is_q ? p.q_and_gate + (tok * p.heads + h) * 2 * kAttnHeadDim
+                                : p.key + (tok * p.kv_heads + kvh) * kAttnHeadDim;
+        const float4 a = reinterpret_cast<const float4 *>(src + d0)[0];
+        const float4 b = reinterpret_cast<const float4 *>(src + d0)[1];
+        float x[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+        // rmsnorm_inplace (ops.rs:493-498) with rms_scale's f64 accumulation.
+        double sum = 0.0;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) sum += double(x[j]) * double(x[j]);
+        sum = warp_sum_f64(sum);
+        const float scale = rms_scale_from_sum(sum, kAttnHeadDim, p.eps);
+        const float *w = is_q ? p.q_norm : p.k_norm;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) x[j] = x[j] * scale * w[d0 + j];
+        // RoPE on dims [0, 64): lanes 0-3 hold dims i < 32, lanes 4-7 dims i+32.
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const float other = __shfl_xor_sync(0xffffffffu, x[j], 4);
+            if (lane < 4) {
+                const int i = d0 + j;
+                x[j] = x[j] * cs[i] - other * sn[i];
+            } else if (lane < 8) {
+                const int i = d0 + j - 32;
+                x[j] = other * sn[i] + x[j] * cs[i];
+            }
+        }
+        if (is_q) {
+            uint4 o;
+            o.x = pack_bf16x2_rn(x[0], x[1]);
+            o.y = pack_bf16x2_rn(x[2], x[3]);
+            o.z = pack_bf16x2_rn(x[4], x[5]);
+            o.w = pack_bf16x2_rn(x[6], x[7]);
+            *reinterpret_cast<uint4 *>(p.qp + ((size_t(s) * p.heads + h) * p.count + t) * kAttnHeadDim + d0) = o;
+        } else {
+            const size_t off = (tok * p.kv_heads + kvh) * kAttnHeadDim + d0;
+            reinterpret_cast<float4 *>(p.key + off)[0] = make_float4(x[0], x[1], x[2], x[3]);
+            reinterpret_cast<float4 *>(p.key + off)[1] = make_float4(x[4], x[5], x[6], x[7]);
+            const size_t row =
+                ((size_t(p.seq0 + s) * p.kv_heads + kvh) * p.context_length + pos) * kAttnHeadDim + d0;
+            uint4 kk, vv;
+            kk.x = pack_bf16x2_rn(x[0], x[1]);
+            kk.y = pack_bf16x2_rn(x[2], x[3]);
+            kk.z = pack_bf16x2_rn(x[4], x[5]);
+            kk.w = pack_bf16x2_rn(x[6], x[7]);
+            const float4 va = reinterpret_cast<const float4 *>(p.value + off)[0];
+            const float4 vb = reinterpret_cast<const float4 *>(p.value + off)[1];
+            vv.x = pack_bf16x2_rn(va.x, va.y);
+            vv.y = pack_bf16x2_rn(va.z, va.w);
+            vv.z = pack_bf16x2_rn(vb.x, vb.y);
+            vv.w = pack_bf16x2_rn(vb.z, vb.w);
+            *reinterpret_cast<uint4 *>(p.kcache + row) = kk;
+            *reinterpret_cast<uint4 *>(p.vcache + row) = vv;
+        }
     }
 }
 
@@ -493,8 +532,7 @@ cudaError_t launch_attn_prefill(const AttnPrefillLaunch &a, cudaStream_t stream)
     PrefillPrepParams pp{a.q_and_gate, a.key, a.value, a.qp, a.kcache, a.vcache, a.q_norm,
                          a.k_norm, a.seq0, a.count, a.base, a.context_length, a.heads, a.kv_heads,
                          a.theta_scale, a.eps};
-    attn_prefill_prep_kernel<<<dim3(a.heads + a.kv_heads, a.count, a.nseq), kAttnHeadDim, 0,
-                               stream>>>(pp);
+    attn_prefill_prep_kernel<<<dim3(a.count, a.nseq), kPrepWarps * 32, 0, stream>>>(pp);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
 

@@ -15,11 +15,13 @@
 // Rows of S evolve independently (row j only sees v[j] and u[j]), so the
 // state pass splits each head's 128 rows into 4 slices of 32.
 //
-//   L1 linear_prefill_conv   one thread per (channel, sequence): the kernel-4
-//                            causal conv down the prompt with the carried state
-//                            (multiply then add, ops.rs:665-676) and SiLU, in
-//                            place; the last three inputs become the new
-//                            conv state.
+//   L1 linear_prefill_conv   one thread per (channel, 64-token segment,
+//                            sequence): the kernel-4 causal conv with the
+//                            carried state (multiply then add, ops.rs:665-676)
+//                            and SiLU, in place; a pre-pass saves the three
+//                            original inputs before each segment so segments
+//                            run in parallel; the last three inputs become the
+//                            new conv state.
 //   L2 linear_prefill_norm   one CTA per (token, sequence): L2-norm of the q and
 //                            k heads (f64 sums) and the beta/alpha gates, in place.
 //   L3 linear_prefill_local  one CTA per (chunk, value head, sequence): the
@@ -51,19 +53,42 @@ struct ConvParams {
     float *qkv;          // [nseq][count][qkv_dim]
     float *conv_state;   // slot base [batch][qkv_dim][3]
     const float *conv_w; // [qkv_dim][4]
-    int seq0, count, qkv_dim;
+    float *bounds;       // [nseq][nseg][3][qkv_dim]: inputs preceding each segment
+    int seq0, count, qkv_dim, nseg;
 };
 
+constexpr int kSeg = 64;  // tokens per conv segment
+
+// The three inputs that precede segment g: the carried conv state for g = 0,
+// otherwise the (not yet convolved) inputs g*kSeg-3 .. g*kSeg-1.
+__global__ void __launch_bounds__(128) linear_prefill_conv_bounds_kernel(ConvParams p) {
+    const int c = blockIdx.x * 128 + threadIdx.x;
+    const int g = blockIdx.y, s = blockIdx.z;
+    if (c >= p.qkv_dim) return;
+    float *dst = p.bounds + (size_t(s) * p.nseg + g) * 3 * p.qkv_dim + c;
+    if (g == 0) {
+        const float *st = p.conv_state + (size_t(p.seq0 + s) * p.qkv_dim + c) * 3;
+        for (int k = 0; k < 3; ++k) dst[size_t(k) * p.qkv_dim] = st[k];
+    } else {
+        const float *x = p.qkv + (size_t(s) * p.count + g * kSeg - 3) * p.qkv_dim + c;
+        for (int k = 0; k < 3; ++k) dst[size_t(k) * p.qkv_dim] = x[size_t(k) * p.qkv_dim];
+    }
+}
+
+// One thread per (channel, segment, sequence): the kernel-4 causal conv over
+// the segment (multiply then add, ops.rs:665-676) and SiLU, in place. The
+// last segment leaves the last three inputs as the new conv state.
 __global__ void __launch_bounds__(128) linear_prefill_conv_kernel(ConvParams p) {
     const int c = blockIdx.x * 128 + threadIdx.x;
-    const int s = blockIdx.y;
+    const int g = blockIdx.y, s = blockIdx.z;
     if (c >= p.qkv_dim) return;
-    float *st = p.conv_state + (size_t(p.seq0 + s) * p.qkv_dim + c) * 3;
+    const float *bnd = p.bounds + (size_t(s) * p.nseg + g) * 3 * p.qkv_dim + c;
+    float s0 = bnd[0], s1 = bnd[p.qkv_dim], s2 = bnd[2 * size_t(p.qkv_dim)];
     const float4 w = reinterpret_cast<const float4 *>(p.conv_w)[c];
-    float s0 = st[0], s1 = st[1], s2 = st[2];
+    const int t0 = g * kSeg, t1 = min(p.count, t0 + kSeg);
     float *x = p.qkv + size_t(s) * p.count * p.qkv_dim + c;
-#pragma unroll 4
-    for (int t = 0; t < p.count; ++t) {
+#pragma unroll 8
+    for (int t = t0; t < t1; ++t) {
         const float xt = x[size_t(t) * p.qkv_dim];
         float v = s0 * w.x;
         v += s1 * w.y;
@@ -74,9 +99,12 @@ __global__ void __launch_bounds__(128) linear_prefill_conv_kernel(ConvParams p) 
         s2 = xt;
         x[size_t(t) * p.qkv_dim] = siluf_ref(v);
     }
-    st[0] = s0;
-    st[1] = s1;
-    st[2] = s2;
+    if (g == p.nseg - 1) {
+        float *st = p.conv_state + (size_t(p.seq0 + s) * p.qkv_dim + c) * 3;
+        st[0] = s0;
+        st[1] = s1;
+        st[2] = s2;
+    }
 }
 
 // ----------------------------------------------------------------------------
@@ -467,10 +495,16 @@ size_t linear_prefill_scratch_floats(int nchunk_total, int v_heads) {
 cudaError_t launch_linear_prefill(const LinearPrefillLaunch &a, cudaStream_t stream) {
     const int qkv_dim = (2 * a.qk_heads + a.v_heads) * kD;
     const int nchunk = (a.count + kC - 1) / kC;
-    ConvParams cp{a.qkv, a.conv_state, a.conv_w, a.seq0, a.count, qkv_dim};
-    linear_prefill_conv_kernel<<<dim3((qkv_dim + 127) / 128, a.nseq), 128, 0, stream>>>(cp);
+    // The segment boundaries live at the start of the W scratch, which L3
+    // only writes after the conv has finished.
+    const int nseg = (a.count + kSeg - 1) / kSeg;
+    ConvParams cp{a.qkv, a.conv_state, a.conv_w, a.scratch, a.seq0, a.count, qkv_dim, nseg};
+    const dim3 conv_grid((qkv_dim + 127) / 128, nseg, a.nseq);
+    linear_prefill_conv_bounds_kernel<<<conv_grid, 128, 0, stream>>>(cp);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
+    linear_prefill_conv_kernel<<<conv_grid, 128, 0, stream>>>(cp);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
 
     NormParams np{a.qkv, a.beta, a.alpha, a.dt_bias, a.ssm_a, a.count, a.qk_heads, a.v_heads,
                   qkv_dim, a.eps};

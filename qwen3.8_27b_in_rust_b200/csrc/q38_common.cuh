@@ -178,6 +178,12 @@ __device__ __forceinline__ float rms_scale_from_sum(double sum, int n, float eps
     return 1.0f / sqrtf(mean + eps);
 }
 
+// Two floats -> bf16x2 (round to nearest even), lo in the low half.
+__device__ __forceinline__ uint32_t pack_bf16x2_rn(float lo, float hi) {
+    const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t *>(&v);
+}
+
 template <typename T>
 struct KvTraits;
 template <>
