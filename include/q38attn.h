@@ -243,7 +243,8 @@ int q38_state_reserve_prefill(q38_state *st, int max_tokens);
  * seq0..seq0+nseq-1, all starting at cache position base_position: token t
  * attends to positions 0..base_position+t, exactly as the reference's
  * per-token loop over full_core (batch_full_attention, ops.rs:1156-1172).
- * Runs on the tcgen05 tensor cores with bf16 Q/K/V/P and f32 accumulation;
+ * Runs on the tcgen05 tensor cores: S = Q K^T from bf16 Q and K, O = P V in
+ * f16, f32 accumulation;
  * needs a Q38_KV_BF16 state and q38_state_reserve_prefill(nseq*count).
  * DEVICE pointers, token-major per sequence:
  *   q_and_gate [nseq][count][heads*512]
@@ -270,6 +271,22 @@ int q38_full_prefill(q38_ctx *ctx, q38_state *st, int layer, int seq0, int nseq,
 int q38_linear_prefill(q38_ctx *ctx, q38_state *st, int layer, int seq0, int nseq, int count,
                        float *qkv, const float *z, float *beta, float *alpha, float *attention,
                        void *stream);
+
+/* Host-pointer forms of the two prefill calls, for the reference's host
+ * slices (batch_full_attention / batch_linear_attention, ops.rs:1156-1172,
+ * :1088-1099, which hold [count][dim] rows per sequence): the same
+ * [nseq][count][dim] layouts as above in HOST memory (pinned for best speed).
+ * The prompt is streamed through a device staging buffer that
+ * q38_state_reserve_prefill sizes, piece by piece; each piece continues from
+ * the cache rows / recurrent state the previous piece left, so the result is
+ * that of one call. The in-place inputs (key; qkv, beta, alpha) are written
+ * back, and the call synchronises `stream` before returning. */
+int q38_full_prefill_host(q38_ctx *ctx, q38_state *st, int layer, int seq0, int nseq, int count,
+                          int base_position, const float *q_and_gate, float *key,
+                          const float *value, float *attention, void *stream);
+int q38_linear_prefill_host(q38_ctx *ctx, q38_state *st, int layer, int seq0, int nseq,
+                            int count, float *qkv, const float *z, float *beta, float *alpha,
+                            float *attention, void *stream);
 
 /* ---------------------------------------------------------- decode (host) */
 

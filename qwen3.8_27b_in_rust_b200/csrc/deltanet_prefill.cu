@@ -47,7 +47,7 @@ constexpr int kD = kLinHeadDim;  // 128
 constexpr int kSlice = 32;   // state rows per CTA in the state pass
 
 // ----------------------------------------------------------------------------
-// L1: conv + SiLU down the prompt
+// L1: conv + SiLU, 64-token segments in parallel
 // ----------------------------------------------------------------------------
 struct ConvParams {
     float *qkv;          // [nseq][count][qkv_dim]

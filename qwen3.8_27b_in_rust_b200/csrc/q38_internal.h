@@ -68,6 +68,8 @@ struct q38_state {
     size_t prefill_tokens = 0;
     float *prefill_lin = nullptr;        // chunked DeltaNet scratch
     size_t prefill_chunks = 0;           // chunk capacity of prefill_lin
+    float *prefill_stage = nullptr;      // device staging of the *_prefill_host forms
+    size_t prefill_stage_tokens = 0;     // tokens (all sequences) one staged piece holds
     // staging for the host-pointer calls (device, sized for `batch`)
     float *stage = nullptr;
     size_t stage_floats = 0;

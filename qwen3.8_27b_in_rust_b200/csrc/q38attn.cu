@@ -4,6 +4,7 @@
 // deltanet_decode.cu; nothing here computes on the CPU.
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
@@ -164,6 +165,7 @@ void free_state(q38_state *st) {
     cudaFree(st->stage_pos);
     cudaFree(st->prefill_q);
     cudaFree(st->prefill_lin);
+    cudaFree(st->prefill_stage);
 }
 
 // Validates a decode call and fills the launch arguments (device pointers).
@@ -627,6 +629,39 @@ int q38_linear_decode(q38_ctx *ctx, q38_state *st, int layer, int batch, float *
     return Q38_OK;
 }
 
+namespace {
+
+constexpr size_t kHostPieceTokens = 4096;
+
+// Floats one token needs in the host-prefill staging buffer: the larger of
+// the full-attention inputs+output and the DeltaNet inputs+output.
+size_t host_prefill_token_floats(const q38_ctx *ctx) {
+    const size_t full = size_t(ctx->qg_dim) + 2 * ctx->kv_dim + ctx->q_dim;
+    const size_t lin = size_t(ctx->qkv_dim) + 2 * ctx->v_dim + 2 * ctx->geom.linear_v_heads;
+    return std::max(full, lin);
+}
+
+// Tokens per sequence in one staged piece of a host prefill.
+int host_piece(const q38_state *st, int nseq, int count, int align) {
+    int piece = int(st->prefill_stage_tokens / size_t(nseq));
+    if (piece >= align) piece -= piece % align;
+    return std::max(1, std::min(piece, count));
+}
+
+// Copies rows [t0, t0+n) of each of nseq sequences of a [nseq][count][dim]
+// tensor to or from a [nseq][n][dim] staging block.
+cudaError_t copy_piece(float *dst, const float *src, int nseq, int count, int t0, int n, int dim,
+                       cudaMemcpyKind kind, cudaStream_t s) {
+    const size_t row = size_t(n) * dim * sizeof(float);
+    if (kind == cudaMemcpyHostToDevice)
+        return cudaMemcpy2DAsync(dst, row, src + size_t(t0) * dim, size_t(count) * dim * 4, row,
+                                 nseq, kind, s);
+    return cudaMemcpy2DAsync(dst + size_t(t0) * dim, size_t(count) * dim * 4, src, row, row, nseq,
+                             kind, s);
+}
+
+}  // namespace
+
 int q38_state_reserve_prefill(q38_state *st, int max_tokens) {
     if (!st) return fail(Q38_ERR_ARG, "null state");
     if (max_tokens <= 0) return fail(Q38_ERR_ARG, "max_tokens must be positive");
@@ -634,10 +669,13 @@ int q38_state_reserve_prefill(q38_state *st, int max_tokens) {
     DeviceGuard guard(st->ctx->device);
     cudaFree(st->prefill_q);
     cudaFree(st->prefill_lin);
+    cudaFree(st->prefill_stage);
     st->prefill_q = nullptr;
     st->prefill_lin = nullptr;
+    st->prefill_stage = nullptr;
     st->prefill_tokens = 0;
     st->prefill_chunks = 0;
+    st->prefill_stage_tokens = 0;
     if (st->full_slots > 0) {
         const size_t bytes = size_t(max_tokens) * st->ctx->q_dim * sizeof(__nv_bfloat16);
         Q38_CUDA(cudaMalloc(&st->prefill_q, bytes));
@@ -650,6 +688,13 @@ int q38_state_reserve_prefill(q38_state *st, int max_tokens) {
         Q38_CUDA(cudaMalloc(&st->prefill_lin, floats * sizeof(float)));
         st->prefill_chunks = chunks;
     }
+    // Host-pointer prefill streams the prompt through a staging buffer of at
+    // most kHostPieceTokens tokens (but never fewer than one per sequence).
+    const size_t stage_tokens =
+        std::min(size_t(max_tokens), std::max(kHostPieceTokens, size_t(st->batch)));
+    Q38_CUDA(cudaMalloc(&st->prefill_stage,
+                        stage_tokens * host_prefill_token_floats(st->ctx) * sizeof(float)));
+    st->prefill_stage_tokens = stage_tokens;
     st->prefill_tokens = size_t(max_tokens);
     return Q38_OK;
 }
@@ -745,6 +790,93 @@ int q38_linear_prefill(q38_ctx *ctx, q38_state *st, int layer, int seq0, int nse
     DeviceGuard guard(ctx->device);
     cudaError_t e = q38::launch_linear_prefill(a, static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return cuda_fail(e, "DeltaNet prefill launch");
+    return Q38_OK;
+}
+
+int q38_full_prefill_host(q38_ctx *ctx, q38_state *st, int layer, int seq0, int nseq, int count,
+                          int base_position, const float *q_and_gate, float *key,
+                          const float *value, float *attention, void *stream) {
+    if (int rc = check_state(ctx, st)) return rc;
+    if (!q_and_gate || !key || !value || !attention)
+        return fail(Q38_ERR_ARG, "null tensor argument");
+    if (nseq <= 0 || count <= 0 || seq0 < 0 || seq0 + nseq > st->batch)
+        return fail(Q38_ERR_ARG, "sequences [%d, %d) x %d tokens outside the state's %d",
+                    seq0, seq0 + nseq, count, st->batch);
+    if (!st->prefill_stage || size_t(nseq) * size_t(count) > st->prefill_tokens)
+        return fail(Q38_ERR_ARG, "%d tokens exceed the reserved prefill scratch (%zu)",
+                    nseq * count, st->prefill_tokens);
+    if (base_position < 0 || int64_t(base_position) + count > int64_t(st->context_length))
+        return fail(Q38_ERR_ARG, "positions [%d, %d) outside the %d-position cache",
+                    base_position, base_position + count, st->context_length);
+    DeviceGuard guard(ctx->device);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const int piece = host_piece(st, nseq, count, 128);
+    const size_t n_max = size_t(nseq) * piece;
+    float *d_qg = st->prefill_stage, *d_k = d_qg + n_max * ctx->qg_dim,
+          *d_v = d_k + n_max * ctx->kv_dim, *d_out = d_v + n_max * ctx->kv_dim;
+    // Token t of a piece starting at t0 is prompt token t0+t at position
+    // base_position+t0+t; earlier pieces are already in the cache, so the
+    // pieces give the per-token loop's result.
+    for (int t0 = 0; t0 < count; t0 += piece) {
+        const int n = std::min(piece, count - t0);
+        Q38_CUDA(copy_piece(d_qg, q_and_gate, nseq, count, t0, n, ctx->qg_dim,
+                            cudaMemcpyHostToDevice, s));
+        Q38_CUDA(copy_piece(d_k, key, nseq, count, t0, n, ctx->kv_dim, cudaMemcpyHostToDevice, s));
+        Q38_CUDA(copy_piece(d_v, value, nseq, count, t0, n, ctx->kv_dim, cudaMemcpyHostToDevice, s));
+        if (int rc = q38_full_prefill(ctx, st, layer, seq0, nseq, n, base_position + t0, d_qg, d_k,
+                                      d_v, d_out, stream)) {
+            cudaStreamSynchronize(s);  // the caller's buffers may go once we return
+            return rc;
+        }
+        Q38_CUDA(copy_piece(attention, d_out, nseq, count, t0, n, ctx->q_dim,
+                            cudaMemcpyDeviceToHost, s));
+        Q38_CUDA(copy_piece(key, d_k, nseq, count, t0, n, ctx->kv_dim, cudaMemcpyDeviceToHost, s));
+    }
+    Q38_CUDA(cudaStreamSynchronize(s));
+    return Q38_OK;
+}
+
+int q38_linear_prefill_host(q38_ctx *ctx, q38_state *st, int layer, int seq0, int nseq,
+                            int count, float *qkv, const float *z, float *beta, float *alpha,
+                            float *attention, void *stream) {
+    if (int rc = check_state(ctx, st)) return rc;
+    if (!qkv || !z || !beta || !alpha || !attention)
+        return fail(Q38_ERR_ARG, "null tensor argument");
+    if (nseq <= 0 || count <= 0 || seq0 < 0 || seq0 + nseq > st->batch)
+        return fail(Q38_ERR_ARG, "sequences [%d, %d) x %d tokens outside the state's %d",
+                    seq0, seq0 + nseq, count, st->batch);
+    if (!st->prefill_stage || size_t(nseq) * size_t(count) > st->prefill_tokens)
+        return fail(Q38_ERR_ARG, "%d tokens exceed the reserved prefill scratch (%zu)",
+                    nseq * count, st->prefill_tokens);
+    DeviceGuard guard(ctx->device);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const int piece = host_piece(st, nseq, count, 64);
+    const size_t n_max = size_t(nseq) * piece;
+    const int vh = ctx->geom.linear_v_heads;
+    float *d_qkv = st->prefill_stage, *d_z = d_qkv + n_max * ctx->qkv_dim,
+          *d_b = d_z + n_max * ctx->v_dim, *d_a = d_b + n_max * vh, *d_out = d_a + n_max * vh;
+    // The conv and delta states carry from one piece to the next exactly as
+    // from one token to the next.
+    for (int t0 = 0; t0 < count; t0 += piece) {
+        const int n = std::min(piece, count - t0);
+        Q38_CUDA(copy_piece(d_qkv, qkv, nseq, count, t0, n, ctx->qkv_dim, cudaMemcpyHostToDevice,
+                            s));
+        Q38_CUDA(copy_piece(d_z, z, nseq, count, t0, n, ctx->v_dim, cudaMemcpyHostToDevice, s));
+        Q38_CUDA(copy_piece(d_b, beta, nseq, count, t0, n, vh, cudaMemcpyHostToDevice, s));
+        Q38_CUDA(copy_piece(d_a, alpha, nseq, count, t0, n, vh, cudaMemcpyHostToDevice, s));
+        if (int rc = q38_linear_prefill(ctx, st, layer, seq0, nseq, n, d_qkv, d_z, d_b, d_a, d_out,
+                                        stream)) {
+            cudaStreamSynchronize(s);
+            return rc;
+        }
+        Q38_CUDA(copy_piece(attention, d_out, nseq, count, t0, n, ctx->v_dim,
+                            cudaMemcpyDeviceToHost, s));
+        Q38_CUDA(copy_piece(qkv, d_qkv, nseq, count, t0, n, ctx->qkv_dim, cudaMemcpyDeviceToHost,
+                            s));
+        Q38_CUDA(copy_piece(beta, d_b, nseq, count, t0, n, vh, cudaMemcpyDeviceToHost, s));
+        Q38_CUDA(copy_piece(alpha, d_a, nseq, count, t0, n, vh, cudaMemcpyDeviceToHost, s));
+    }
+    Q38_CUDA(cudaStreamSynchronize(s));
     return Q38_OK;
 }
 

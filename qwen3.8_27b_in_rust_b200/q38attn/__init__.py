@@ -359,6 +359,30 @@ class Context:
             _host_ptr(z, "z"), _host_ptr(beta, "beta", True), _host_ptr(alpha, "alpha", True),
             _host_ptr(attention, "attention", True), _stream_ptr(stream)))
 
+    def full_prefill_host(self, state: State, layer: int, seq0: int, q_and_gate: np.ndarray,
+                          key: np.ndarray, value: np.ndarray, attention: np.ndarray,
+                          base_position: int, stream=0) -> None:
+        """Host-pointer form of full_prefill ([nseq][count][...] numpy arrays):
+        the prompt is streamed through the state's staging buffer in pieces
+        and the call returns when attention and key are written back."""
+        nseq, count = q_and_gate.shape[0], q_and_gate.shape[1]
+        check(self._lib.q38_full_prefill_host(
+            self.handle, state.handle, layer, seq0, nseq, count, base_position,
+            _host_ptr(q_and_gate, "q_and_gate"), _host_ptr(key, "key", True),
+            _host_ptr(value, "value"), _host_ptr(attention, "attention", True),
+            _stream_ptr(stream)))
+
+    def linear_prefill_host(self, state: State, layer: int, seq0: int, qkv: np.ndarray,
+                            z: np.ndarray, beta: np.ndarray, alpha: np.ndarray,
+                            attention: np.ndarray, stream=0) -> None:
+        """Host-pointer form of linear_prefill; qkv, beta and alpha are
+        rewritten in place as the reference's loop leaves them."""
+        nseq, count = qkv.shape[0], qkv.shape[1]
+        check(self._lib.q38_linear_prefill_host(
+            self.handle, state.handle, layer, seq0, nseq, count, _host_ptr(qkv, "qkv", True),
+            _host_ptr(z, "z"), _host_ptr(beta, "beta", True), _host_ptr(alpha, "alpha", True),
+            _host_ptr(attention, "attention", True), _stream_ptr(stream)))
+
     # reference-signature mirrors (host slices) ------------------------------
     def linear_core(self, state: State, layer: int, conv_state: np.ndarray,
                     delta_state: np.ndarray, qkv: np.ndarray, z: np.ndarray, beta: np.ndarray,

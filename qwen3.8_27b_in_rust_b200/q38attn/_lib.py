@@ -83,6 +83,10 @@ SIGNATURES = {
                                  _VP]),
     "q38_linear_prefill": (c_int, [_VP, _VP, c_int, c_int, c_int, c_int, _VP, _VP, _VP, _VP,
                                    _VP, _VP]),
+    "q38_full_prefill_host": (c_int, [_VP, _VP, c_int, c_int, c_int, c_int, c_int, _VP, _VP,
+                                      _VP, _VP, _VP]),
+    "q38_linear_prefill_host": (c_int, [_VP, _VP, c_int, c_int, c_int, c_int, _VP, _VP, _VP,
+                                        _VP, _VP, _VP]),
     "q38_full_decode_host": (c_int, [_VP, _VP, c_int, c_int, _VP, _VP, _VP, _VP, _VP, _VP]),
     "q38_linear_decode_host": (c_int, [_VP, _VP, c_int, c_int, _VP, _VP, _VP, _VP, _VP, _VP]),
     "q38_linear_core": (c_int, [_VP, _VP, c_int, _VP, _VP, _VP, _VP, _VP, _VP, _VP]),
