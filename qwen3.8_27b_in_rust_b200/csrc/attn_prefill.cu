@@ -49,15 +49,15 @@ using namespace sm100;
 
 constexpr int kBlockQ = 128;  // query rows per CTA (MMA M)
 constexpr int kBlockK = 64;   // keys per tile (QK N, PV K)
-constexpr int kThreadsPF = 320;
+constexpr int kThreadsPF = 256;
 constexpr uint32_t kQBytes = kBlockQ * kAttnHeadDim * 2;      // 64 KB
 constexpr uint32_t kKVBytes = kBlockK * kAttnHeadDim * 2;     // 32 KB
-constexpr uint32_t kPBytes = kBlockQ * kBlockK * 2;           // 16 KB
-constexpr int kStagesKV = 3;
-constexpr uint32_t kSmemPF = 2 * kStagesKV * kKVBytes + 2 * kPBytes + 1024;  // + alignment slack
-static_assert(kQBytes <= kStagesKV * kKVBytes, "Q is staged in the K ring");
+constexpr int kStagesK = 4;
+constexpr int kStagesV = 3;
+constexpr uint32_t kSmemPF = (kStagesK + kStagesV) * kKVBytes + 1024;  // + alignment slack
+static_assert(kQBytes <= kStagesK * kKVBytes, "Q is staged in the K ring");
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kColS = 0;     // S buffers at columns 0 and 64
+constexpr uint32_t kColS = 0;     // S buffers at columns 0 and 64 (P aliases their first 32)
 constexpr uint32_t kColO = 128;   // O at columns 128..383
 constexpr uint32_t kColQ = 384;   // Q at columns 384..511 (bf16 pairs)
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
@@ -71,6 +71,7 @@ struct PrefillPrepParams {
     const float *value;
     __nv_bfloat16 *qp;        // [nseq][heads][count][256]
     __nv_bfloat16 *kcache, *vcache;  // slot base: [batch][kv_heads][ctx][256]
+    __half *v16;                     // [nseq][kv_heads][ctx][256]: V as f16 for P V
     const float *q_norm, *k_norm;
     int seq0, count, base, context_length, heads, kv_heads;
     float theta_scale, eps;
@@ -152,8 +153,45 @@ __global__ void __launch_bounds__(kPrepWarps * 32) attn_prefill_prep_kernel(Pref
             vv.w = pack_bf16x2_rn(vb.z, vb.w);
             *reinterpret_cast<uint4 *>(p.kcache + row) = kk;
             *reinterpret_cast<uint4 *>(p.vcache + row) = vv;
+            // The same bf16 values as f16 (exact for 2^-14 <= |v| <= 65504).
+            uint4 vh;
+            float2 f;
+            f = bf16x2_to_float2(vv.x); vh.x = pack_f16x2(f.x, f.y);
+            f = bf16x2_to_float2(vv.y); vh.y = pack_f16x2(f.x, f.y);
+            f = bf16x2_to_float2(vv.z); vh.z = pack_f16x2(f.x, f.y);
+            f = bf16x2_to_float2(vv.w); vh.w = pack_f16x2(f.x, f.y);
+            *reinterpret_cast<uint4 *>(
+                p.v16 + ((size_t(s) * p.kv_heads + kvh) * p.context_length + pos) * kAttnHeadDim +
+                d0) = vh;
         }
     }
+}
+
+// --------------------------------------------------------------------------
+// P1b: f16 copy of the cached prefix's V rows
+// --------------------------------------------------------------------------
+struct PrefixParams {
+    const __nv_bfloat16 *vcache;  // slot base [batch][kv_heads][ctx][256]
+    __half *v16;                  // [nseq][kv_heads][ctx][256]
+    int seq0, base, context_length, kv_heads;
+};
+
+// One thread per 8 values of the rows [0, base) of each (sequence, kv head).
+__global__ void __launch_bounds__(256) attn_prefill_prefix_kernel(PrefixParams p) {
+    const int i = blockIdx.x * 256 + threadIdx.x;
+    if (i >= p.base * (kAttnHeadDim / 8)) return;
+    const int kvh = blockIdx.y, s = blockIdx.z;
+    const size_t row = size_t(i) / (kAttnHeadDim / 8), c8 = size_t(i) % (kAttnHeadDim / 8);
+    const size_t src =
+        ((size_t(p.seq0 + s) * p.kv_heads + kvh) * p.context_length + row) * kAttnHeadDim + c8 * 8;
+    const size_t dst = ((size_t(s) * p.kv_heads + kvh) * p.context_length + row) * kAttnHeadDim + c8 * 8;
+    uint4 w = *reinterpret_cast<const uint4 *>(p.vcache + src);
+    float2 f;
+    f = bf16x2_to_float2(w.x); w.x = pack_f16x2(f.x, f.y);
+    f = bf16x2_to_float2(w.y); w.y = pack_f16x2(f.x, f.y);
+    f = bf16x2_to_float2(w.z); w.z = pack_f16x2(f.x, f.y);
+    f = bf16x2_to_float2(w.w); w.w = pack_f16x2(f.x, f.y);
+    *reinterpret_cast<uint4 *>(p.v16 + dst) = w;
 }
 
 // --------------------------------------------------------------------------
@@ -168,9 +206,8 @@ struct PrefillParams {
 
 struct __align__(8) PrefillBarriers {
     uint64_t q_full, q_copied;
-    uint64_t k_full[kStagesKV], k_empty[kStagesKV], v_full[kStagesKV], v_empty[kStagesKV];
-    uint64_t v_conv[kStagesKV];
-    uint64_t s_full[2], p_full[2], o_done, o_final;
+    uint64_t k_full[kStagesK], k_empty[kStagesK], v_full[kStagesV], v_empty[kStagesV];
+    uint64_t s_full[2], s_free[2], p_full[2], o_done, o_final;
 };
 
 __device__ __forceinline__ float ex2(float x) {
@@ -195,9 +232,8 @@ __global__ void __launch_bounds__(kThreadsPF, 1)
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char *smem =
         reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    unsigned char *sK = smem;                       // kStagesKV stages (Q staged here first)
-    unsigned char *sV = sK + kStagesKV * kKVBytes;  // kStagesKV stages
-    unsigned char *sP = sV + kStagesKV * kKVBytes;  // 2 buffers
+    unsigned char *sK = smem;                      // kStagesK stages (Q staged here first)
+    unsigned char *sV = sK + kStagesK * kKVBytes;  // kStagesV stages (f16)
     __shared__ PrefillBarriers bar;
     __shared__ uint32_t tmem_base_s;
     __shared__ volatile int abort_flag;
@@ -215,15 +251,17 @@ __global__ void __launch_bounds__(kThreadsPF, 1)
         abort_flag = 0;
         mbar_init(&bar.q_full, 1);
         mbar_init(&bar.q_copied, 128);
-        for (int b = 0; b < kStagesKV; ++b) {
+        for (int b = 0; b < kStagesK; ++b) {
             mbar_init(&bar.k_full[b], 1);
             mbar_init(&bar.k_empty[b], 1);
+        }
+        for (int b = 0; b < kStagesV; ++b) {
             mbar_init(&bar.v_full[b], 1);
             mbar_init(&bar.v_empty[b], 1);
-            mbar_init(&bar.v_conv[b], 128);
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&bar.s_full[b], 1);
+            mbar_init(&bar.s_free[b], 1);
             mbar_init(&bar.p_full[b], 128);
         }
         mbar_init(&bar.o_done, 1);
@@ -245,60 +283,68 @@ __global__ void __launch_bounds__(kThreadsPF, 1)
     };
 
     if (warp == 0) {
-        // ------------------------------------------------------------ producer
+        // ------------------------------------------------------------ Q, K producer
         if (lane == 0) {
             tma_prefetch_desc(&map_q);
             tma_prefetch_desc(&map_k);
-            tma_prefetch_desc(&map_v);
             pdl_wait_primary();  // P1 wrote the Q scratch and the new K/V rows
-            const int qrow = s * p.heads + h;       // Q scratch plane
-            const int kvplane = (p.seq0 + s) * p.kv_heads + kvh;
+            const int qrow = s * p.heads + h;  // Q scratch plane
+            const int kplane = (p.seq0 + s) * p.kv_heads + kvh;
             mbar_arrive_expect_tx(&bar.q_full, kQBytes);
             for (int cb = 0; cb < 4; ++cb)
                 tma_load_3d(sK + cb * (kQBytes / 4), &map_q, cb * 64, q0, qrow, &bar.q_full);
             // The K ring holds the staged Q until the softmax warps copied it to TMEM.
             if (!mbar_wait(&bar.q_copied, 0)) fail();
             for (int j = 0; j < nkt && !abort_flag; ++j) {
-                const int b = j % kStagesKV;
-                const uint32_t ph = uint32_t((j - kStagesKV) / kStagesKV) & 1u;
-                if (j >= kStagesKV && !mbar_wait(&bar.k_empty[b], ph)) { fail(); break; }
+                const int b = j % kStagesK;
+                if (j >= kStagesK &&
+                    !mbar_wait(&bar.k_empty[b], uint32_t(j / kStagesK - 1) & 1u)) {
+                    fail();
+                    break;
+                }
                 mbar_arrive_expect_tx(&bar.k_full[b], kKVBytes);
                 for (int cb = 0; cb < 4; ++cb)
                     tma_load_3d(sK + b * kKVBytes + cb * (kKVBytes / 4), &map_k, cb * 64,
-                                j * kBlockK, kvplane, &bar.k_full[b]);
-                if (j >= kStagesKV && !mbar_wait(&bar.v_empty[b], ph)) { fail(); break; }
+                                j * kBlockK, kplane, &bar.k_full[b]);
+            }
+        }
+    } else if (warp == 7) {
+        // ------------------------------------------------------------ V producer (f16)
+        if (lane == 0) {
+            tma_prefetch_desc(&map_v);
+            pdl_wait_primary();
+            const int vplane = s * p.kv_heads + kvh;
+            for (int j = 0; j < nkt && !abort_flag; ++j) {
+                const int b = j % kStagesV;
+                if (j >= kStagesV &&
+                    !mbar_wait(&bar.v_empty[b], uint32_t(j / kStagesV - 1) & 1u)) {
+                    fail();
+                    break;
+                }
                 mbar_arrive_expect_tx(&bar.v_full[b], kKVBytes);
                 for (int cb = 0; cb < 4; ++cb)
                     tma_load_3d(sV + b * kKVBytes + cb * (kKVBytes / 4), &map_v, cb * 64,
-                                j * kBlockK, kvplane, &bar.v_full[b]);
+                                j * kBlockK, vplane, &bar.v_full[b]);
             }
         }
     } else if (warp == 1) {
-        // ------------------------------------------------------------ MMA issuer
+        // ------------------------------------------------------------ S = Q K^T issuer
+        // A single thread waits ~100 cycles per tcgen05.mma issue, so QK and PV
+        // are issued from two warps to keep both streams in the tensor pipe.
         if (lane == 0) {
             const uint32_t id_qk = idesc_bf16_f32(kBlockQ, kBlockK, 0, 0);
-            const uint32_t id_pv = idesc_f16_f32(kBlockQ, kAttnHeadDim, 0, 1, false);
-            const uint32_t sk = smem_addr(sK), sv = smem_addr(sV), sp = smem_addr(sP);
-            auto pv = [&](int jj) -> bool {
-                const int bb = jj & 1, vb = jj % kStagesKV;
-                if (!mbar_wait(&bar.p_full[bb], (jj >> 1) & 1)) return false;
-                if (!mbar_wait(&bar.v_conv[vb], uint32_t(jj / kStagesKV) & 1u)) return false;
-                fence_after_sync();
-                for (int kk = 0; kk < kBlockK / 16; ++kk) {
-                    const uint64_t ad = smem_desc_sw128(sp + bb * kPBytes + kk * 32, 16, 1024);
-                    const uint64_t bd =
-                        smem_desc_sw128(sv + vb * kKVBytes + kk * 2048, kKVBytes / 4, 1024);
-                    mma_bf16(tmem + kColO, ad, bd, id_pv, (jj > 0 || kk > 0) ? 1u : 0u);
-                }
-                mma_commit(&bar.v_empty[vb]);
-                mma_commit(&bar.o_done);
-                return true;
-            };
+            const uint32_t sk = smem_addr(sK);
             bool ok = mbar_wait(&bar.q_copied, 0);
             for (int j = 0; ok && j < nkt; ++j) {
-                const int b = j & 1, kb = j % kStagesKV;
-                if (!mbar_wait(&bar.k_full[kb], uint32_t(j / kStagesKV) & 1u)) { ok = false; break; }
+                const int b = j & 1, kb = j % kStagesK;
+                if (!mbar_wait(&bar.k_full[kb], uint32_t(j / kStagesK) & 1u)) { ok = false; break; }
+                // S buffer b holds P(j-2) until PV(j-2) has read it.
+                if (j >= 2 && !mbar_wait(&bar.s_free[b], uint32_t((j - 2) >> 1) & 1u)) {
+                    ok = false;
+                    break;
+                }
                 fence_after_sync();
+#pragma unroll
                 for (int kk = 0; kk < kAttnHeadDim / 16; ++kk) {
                     const uint64_t bd = smem_desc_sw128(
                         sk + kb * kKVBytes + (kk >> 2) * (kKVBytes / 4) + (kk & 3) * 32, 16, 1024);
@@ -307,36 +353,39 @@ __global__ void __launch_bounds__(kThreadsPF, 1)
                 }
                 mma_commit(&bar.s_full[b]);
                 mma_commit(&bar.k_empty[kb]);
-                if (j >= 1 && !pv(j - 1)) { ok = false; break; }
                 if (abort_flag) { ok = false; break; }
             }
-            if (ok && !pv(nkt - 1)) ok = false;
+            if (!ok) fail();
+        }
+    } else if (warp == 6) {
+        // ------------------------------------------------------------ O += P V issuer
+        if (lane == 0) {
+            const uint32_t id_pv = idesc_f16_f32(kBlockQ, kAttnHeadDim, 0, 1, false);
+            const uint32_t sv = smem_addr(sV);
+            bool ok = true;
+            for (int j = 0; j < nkt; ++j) {
+                const int b = j & 1, vb = j % kStagesV;
+                if (!mbar_wait(&bar.p_full[b], uint32_t(j >> 1) & 1u)) { ok = false; break; }
+                if (!mbar_wait(&bar.v_full[vb], uint32_t(j / kStagesV) & 1u)) { ok = false; break; }
+                fence_after_sync();
+#pragma unroll
+                for (int kk = 0; kk < kBlockK / 16; ++kk) {
+                    const uint64_t bd =
+                        smem_desc_sw128(sv + vb * kKVBytes + kk * 2048, kKVBytes / 4, 1024);
+                    // P(j) sits in the first 32 columns of S buffer b (f16 pairs).
+                    mma_f16_ta(tmem + kColO, tmem + kColS + b * kBlockK + kk * 8, bd, id_pv,
+                               (j > 0 || kk > 0) ? 1u : 0u);
+                }
+                mma_commit(&bar.v_empty[vb]);
+                mma_commit(&bar.s_free[b]);
+                mma_commit(&bar.o_done);
+                if (abort_flag) { ok = false; break; }
+            }
             // One completion for the epilogue: by the time the softmax warps
             // wait, both of the last two PVs may have completed, which a parity
             // wait on o_done cannot tell from "neither has".
             if (ok) mma_commit(&bar.o_final);
             if (!ok) fail();
-        }
-    } else if (warp >= 6) {
-        // ------------------------------------------------------------ V bf16 -> f16
-        const int ct = threadIdx.x - 6 * 32;  // 0..127
-        for (int j = 0; j < nkt; ++j) {
-            const int b = j % kStagesKV;
-            if (!mbar_wait(&bar.v_full[b], uint32_t(j / kStagesKV) & 1u)) { fail(); break; }
-            uint4 *tile = reinterpret_cast<uint4 *>(sV + b * kKVBytes);
-#pragma unroll 4
-            for (int c = ct; c < int(kKVBytes / 16); c += 128) {
-                uint4 w = tile[c];
-                float2 f;
-                f = bf16x2_to_float2(w.x); w.x = pack_f16x2(f.x, f.y);
-                f = bf16x2_to_float2(w.y); w.y = pack_f16x2(f.x, f.y);
-                f = bf16x2_to_float2(w.z); w.z = pack_f16x2(f.x, f.y);
-                f = bf16x2_to_float2(w.w); w.w = pack_f16x2(f.x, f.y);
-                tile[c] = w;
-            }
-            fence_proxy_async_smem();
-            mbar_arrive(&bar.v_conv[b]);
-            if (abort_flag) break;
         }
     } else {
         // ------------------------------------------------------------ softmax
@@ -416,6 +465,9 @@ __global__ void __launch_bounds__(kThreadsPF, 1)
                 const float corr = ex2(m - m_new);  // 0 on the first tile
                 if (j > 0) {
                     // O holds PV(0..j-1): wait for PV(j-1), then rescale the rows.
+                    // PV(j-2) completed before QK(j) could start, and PV(j)
+                    // needs this tile's P, so o_done has completed j-1 or j
+                    // phases here: the parity wait is exact.
                     if (!wait_all(&bar.o_done, (j - 1) & 1)) { ok = false; break; }
                     fence_after_sync();
 #pragma unroll 1
@@ -428,34 +480,29 @@ __global__ void __launch_bounds__(kThreadsPF, 1)
                             o[i] = __float_as_uint(__uint_as_float(o[i]) * corr);
                         tmem_st32(tmem + lane_addr + kColO + c, o);
                     }
-                    tmem_wait_st();
                 }
                 l *= corr;
                 m = m_new;
             }
-            // P row into the swizzled K-major tile of buffer b.
-            unsigned char *prow = sP + b * kPBytes;
+            // P row as f16 pairs over the first 32 columns of S buffer b (the
+            // S values are in registers now); PV(j) reads it from TMEM.
+            uint32_t pw[32];
             float ps8[8];
 #pragma unroll
             for (int i = 0; i < 8; ++i) ps8[i] = 0.f;
 #pragma unroll
-            for (int ch = 0; ch < kBlockK / 8; ++ch) {
-                uint32_t w[4];
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const float p0 = ex2(sv[ch * 8 + 2 * e] - m);
-                    const float p1 = ex2(sv[ch * 8 + 2 * e + 1] - m);
-                    ps8[2 * e] += p0;
-                    ps8[2 * e + 1] += p1;
-                    w[e] = pack_f16x2(p0, p1);
-                }
-                const uint32_t off = uint32_t(r) * 128u + ((uint32_t(ch) ^ (uint32_t(r) & 7u)) * 16u);
-                *reinterpret_cast<uint4 *>(prow + off) = make_uint4(w[0], w[1], w[2], w[3]);
+            for (int c = 0; c < kBlockK / 2; ++c) {
+                const float p0 = ex2(sv[2 * c] - m);
+                const float p1 = ex2(sv[2 * c + 1] - m);
+                ps8[(2 * c) & 7] += p0;
+                ps8[(2 * c + 1) & 7] += p1;
+                pw[c] = pack_f16x2(p0, p1);
             }
+            tmem_st32(tmem + lane_addr + kColS + b * kBlockK, pw);
             const float psum = ((ps8[0] + ps8[1]) + (ps8[2] + ps8[3])) +
                                ((ps8[4] + ps8[5]) + (ps8[6] + ps8[7]));
             l += psum;
-            fence_proxy_async_smem();
+            tmem_wait_st();
             fence_before_sync();
             mbar_arrive(&bar.p_full[b]);
             if (__any_sync(0xffffffffu, abort_flag != 0)) { ok = false; break; }
@@ -511,37 +558,44 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_tiled() {
     return fn;
 }
 
-// 3-D bf16 map over [planes][rows][256] with a box of 64 x box_rows x 1 and
-// 128-byte swizzle.
-bool make_map_bf16(CUtensorMap *m, const void *base, uint64_t rows, uint64_t planes,
-                   uint32_t box_rows) {
+// 3-D map of 16-bit elements over [planes][rows][256] with a box of
+// 64 x box_rows x 1 and 128-byte swizzle.
+bool make_map_16(CUtensorMap *m, const void *base, CUtensorMapDataType type, uint64_t rows,
+                 uint64_t planes, uint32_t box_rows) {
     auto enc = encode_tiled();
     if (!enc) return false;
     cuuint64_t dims[3] = {uint64_t(kAttnHeadDim), rows, planes};
     cuuint64_t strides[2] = {uint64_t(kAttnHeadDim) * 2, uint64_t(kAttnHeadDim) * 2 * rows};
     cuuint32_t box[3] = {64, box_rows, 1};
     cuuint32_t es[3] = {1, 1, 1};
-    return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void *>(base), dims, strides, box,
-               es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+    return enc(m, type, 3, const_cast<void *>(base), dims, strides, box, es,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 }  // namespace
 
 cudaError_t launch_attn_prefill(const AttnPrefillLaunch &a, cudaStream_t stream) {
-    PrefillPrepParams pp{a.q_and_gate, a.key, a.value, a.qp, a.kcache, a.vcache, a.q_norm,
+    cudaError_t e;
+    if (a.base > 0) {
+        PrefixParams xp{a.vcache, a.v16, a.seq0, a.base, a.context_length, a.kv_heads};
+        const int n8 = a.base * (kAttnHeadDim / 8);
+        attn_prefill_prefix_kernel<<<dim3((n8 + 255) / 256, a.kv_heads, a.nseq), 256, 0, stream>>>(xp);
+        if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    }
+    PrefillPrepParams pp{a.q_and_gate, a.key, a.value, a.qp, a.kcache, a.vcache, a.v16, a.q_norm,
                          a.k_norm, a.seq0, a.count, a.base, a.context_length, a.heads, a.kv_heads,
                          a.theta_scale, a.eps};
     attn_prefill_prep_kernel<<<dim3(a.count, a.nseq), kPrepWarps * 32, 0, stream>>>(pp);
-    cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess) return e;
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
 
     CUtensorMap mq, mk, mv;
-    if (!make_map_bf16(&mq, a.qp, uint64_t(a.count), uint64_t(a.nseq) * a.heads, kBlockQ) ||
-        !make_map_bf16(&mk, a.kcache, uint64_t(a.context_length),
-                       uint64_t(a.batch) * a.kv_heads, kBlockK) ||
-        !make_map_bf16(&mv, a.vcache, uint64_t(a.context_length),
-                       uint64_t(a.batch) * a.kv_heads, kBlockK))
+    if (!make_map_16(&mq, a.qp, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, uint64_t(a.count),
+                     uint64_t(a.nseq) * a.heads, kBlockQ) ||
+        !make_map_16(&mk, a.kcache, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, uint64_t(a.context_length),
+                     uint64_t(a.batch) * a.kv_heads, kBlockK) ||
+        !make_map_16(&mv, a.v16, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, uint64_t(a.context_length),
+                     uint64_t(a.nseq) * a.kv_heads, kBlockK))
         return cudaErrorInvalidValue;
 
     const int n_qtiles = (a.count + kBlockQ - 1) / kBlockQ;

@@ -3,6 +3,7 @@
 #pragma once
 
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stddef.h>
 #include <stdint.h>
@@ -65,6 +66,8 @@ struct q38_state {
     int max_splits = 0;
     int *d_err = nullptr;           // device error bits
     __nv_bfloat16 *prefill_q = nullptr;  // [tokens][heads][256] prepared queries
+    __half *prefill_v16 = nullptr;       // [v16_seqs][kv_heads][context][256] V as f16
+    int prefill_v16_seqs = 0;
     size_t prefill_tokens = 0;
     float *prefill_lin = nullptr;        // chunked DeltaNet scratch
     size_t prefill_chunks = 0;           // chunk capacity of prefill_lin
@@ -118,6 +121,7 @@ struct AttnPrefillLaunch {
     float *attention;         // [nseq][count][heads*256]
     __nv_bfloat16 *qp;        // scratch [nseq][heads][count][256]
     __nv_bfloat16 *kcache, *vcache;  // slot base [batch][kv_heads][ctx][256]
+    __half *v16;                     // scratch [nseq][kv_heads][ctx][256]
     const float *q_norm, *k_norm;
     int *err;
     int batch, seq0, nseq, count, base, context_length, heads, kv_heads;

@@ -164,6 +164,7 @@ void free_state(q38_state *st) {
     cudaFree(st->stage);
     cudaFree(st->stage_pos);
     cudaFree(st->prefill_q);
+    cudaFree(st->prefill_v16);
     cudaFree(st->prefill_lin);
     cudaFree(st->prefill_stage);
 }
@@ -668,9 +669,12 @@ int q38_state_reserve_prefill(q38_state *st, int max_tokens) {
     if (size_t(max_tokens) <= st->prefill_tokens) return Q38_OK;
     DeviceGuard guard(st->ctx->device);
     cudaFree(st->prefill_q);
+    cudaFree(st->prefill_v16);
     cudaFree(st->prefill_lin);
     cudaFree(st->prefill_stage);
     st->prefill_q = nullptr;
+    st->prefill_v16 = nullptr;
+    st->prefill_v16_seqs = 0;
     st->prefill_lin = nullptr;
     st->prefill_stage = nullptr;
     st->prefill_tokens = 0;
@@ -679,6 +683,15 @@ int q38_state_reserve_prefill(q38_state *st, int max_tokens) {
     if (st->full_slots > 0) {
         const size_t bytes = size_t(max_tokens) * st->ctx->q_dim * sizeof(__nv_bfloat16);
         Q38_CUDA(cudaMalloc(&st->prefill_q, bytes));
+        // f16 copy of the V rows a prefill reads (prefix and prompt), one
+        // cache-sized plane per sequence that one call can cover.
+        const int seqs = std::min(st->batch, max_tokens);
+        const size_t v16_bytes = size_t(seqs) * st->ctx->kv_dim * st->context_length * 2;
+        Q38_CUDA(cudaMalloc(&st->prefill_v16, v16_bytes));
+        // Rows past a prompt's last position sit in its last key tile with
+        // P = 0; they must hold finite values (0 * NaN would be NaN).
+        Q38_CUDA(cudaMemset(st->prefill_v16, 0, v16_bytes));
+        st->prefill_v16_seqs = seqs;
     }
     if (st->linear_slots > 0) {
         // One partial chunk per sequence on top of the full chunks.
@@ -714,7 +727,7 @@ int q38_full_prefill(q38_ctx *ctx, q38_state *st, int layer, int seq0, int nseq,
         int64_t(base_position) + count > int64_t(st->context_length))
         return fail(Q38_ERR_ARG, "positions [%d, %d) outside the %d-position cache",
                     base_position, base_position + count, st->context_length);
-    if (size_t(nseq) * size_t(count) > st->prefill_tokens)
+    if (size_t(nseq) * size_t(count) > st->prefill_tokens || nseq > st->prefill_v16_seqs)
         return fail(Q38_ERR_ARG, "%d tokens exceed the reserved prefill scratch (%zu)",
                     nseq * count, st->prefill_tokens);
     if (!q_and_gate || !key || !value || !attention)
@@ -728,6 +741,7 @@ int q38_full_prefill(q38_ctx *ctx, q38_state *st, int layer, int seq0, int nseq,
     a.value = value;
     a.attention = attention;
     a.qp = st->prefill_q;
+    a.v16 = st->prefill_v16;
     a.kcache = reinterpret_cast<__nv_bfloat16 *>(kv_seq_base(st, st->kcache, slot, 0));
     a.vcache = reinterpret_cast<__nv_bfloat16 *>(kv_seq_base(st, st->vcache, slot, 0));
     a.q_norm = it->second.q_norm;
