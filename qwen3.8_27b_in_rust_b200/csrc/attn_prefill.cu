@@ -49,7 +49,7 @@ using namespace sm100;
 
 constexpr int kBlockQ = 128;  // query rows per CTA (MMA M)
 constexpr int kBlockK = 64;   // keys per tile (QK N, PV K)
-constexpr int kThreadsPF = 256;
+constexpr int kThreadsPF = 288;
 constexpr uint32_t kQBytes = kBlockQ * kAttnHeadDim * 2;      // 64 KB
 constexpr uint32_t kKVBytes = kBlockK * kAttnHeadDim * 2;     // 32 KB
 constexpr int kStagesK = 4;
@@ -210,6 +210,14 @@ struct __align__(8) PrefillBarriers {
     uint64_t s_full[2], s_free[2], p_full[2], o_done, o_final;
 };
 
+__device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
+    uint64_t r;
+    asm("add.rn.f32x2 %0, %1, %2;"
+        : "=l"(r)
+        : "l"(*reinterpret_cast<uint64_t *>(&a)), "l"(*reinterpret_cast<uint64_t *>(&b)));
+    return *reinterpret_cast<float2 *>(&r);
+}
+
 __device__ __forceinline__ float ex2(float x) {
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
@@ -327,15 +335,16 @@ __global__ void __launch_bounds__(kThreadsPF, 1)
                                 j * kBlockK, vplane, &bar.v_full[b]);
             }
         }
-    } else if (warp == 1) {
-        // ------------------------------------------------------------ S = Q K^T issuer
-        // A single thread waits ~100 cycles per tcgen05.mma issue, so QK and PV
-        // are issued from two warps to keep both streams in the tensor pipe.
+    } else if (warp == 1 || warp == 8) {
+        // ------------------------------------------------------------ S = Q K^T issuers
+        // A thread issuing tcgen05.mma waits ~100 cycles per instruction, so
+        // QK of even tiles (warp 1), QK of odd tiles (warp 8) and PV (warp 6)
+        // are three issuers whose streams overlap in the tensor pipe.
         if (lane == 0) {
             const uint32_t id_qk = idesc_bf16_f32(kBlockQ, kBlockK, 0, 0);
             const uint32_t sk = smem_addr(sK);
             bool ok = mbar_wait(&bar.q_copied, 0);
-            for (int j = 0; ok && j < nkt; ++j) {
+            for (int j = warp == 1 ? 0 : 1; ok && j < nkt; j += 2) {
                 const int b = j & 1, kb = j % kStagesK;
                 if (!mbar_wait(&bar.k_full[kb], uint32_t(j / kStagesK) & 1u)) { ok = false; break; }
                 // S buffer b holds P(j-2) until PV(j-2) has read it.
@@ -436,7 +445,8 @@ __global__ void __launch_bounds__(kThreadsPF, 1)
             tmem_wait_ld();
             float sv[kBlockK];
             const int key0 = j * kBlockK;
-            // Independent partial maxima (8 chains) instead of one serial chain.
+            // Row max of the raw scores (scaling by sl2 > 0 keeps the order),
+            // in 8 independent chains.
             float mx8[8];
 #pragma unroll
             for (int i = 0; i < 8; ++i) mx8[i] = -INFINITY;
@@ -444,21 +454,20 @@ __global__ void __launch_bounds__(kThreadsPF, 1)
                 // Tile fully visible to every row of this CTA: no mask.
 #pragma unroll
                 for (int c = 0; c < kBlockK; ++c) {
-                    sv[c] = __uint_as_float(sr[c >> 5][c & 31]) * sl2;
+                    sv[c] = __uint_as_float(sr[c >> 5][c & 31]);
                     mx8[c & 7] = fmaxf(mx8[c & 7], sv[c]);
                 }
             } else {
 #pragma unroll
                 for (int c = 0; c < kBlockK; ++c) {
-                    float v = __uint_as_float(sr[c >> 5][c & 31]) * sl2;
-                    v = (key0 + c <= qpos) ? v : -INFINITY;
-                    sv[c] = v;
-                    mx8[c & 7] = fmaxf(mx8[c & 7], v);
+                    const float v = __uint_as_float(sr[c >> 5][c & 31]);
+                    sv[c] = (key0 + c <= qpos) ? v : -INFINITY;
+                    mx8[c & 7] = fmaxf(mx8[c & 7], sv[c]);
                 }
             }
             const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
                                    fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
-            const float m_new = fmaxf(m, mx);
+            const float m_new = fmaxf(m, mx * sl2);
             if (__any_sync(0xffffffffu, m_new > m + kRescaleThreshold)) {
                 // Every row of the warp moves to its exact max (corr = 1 where
                 // the max did not change); O and l are scaled by the same factor.
@@ -484,24 +493,24 @@ __global__ void __launch_bounds__(kThreadsPF, 1)
                 l *= corr;
                 m = m_new;
             }
-            // P row as f16 pairs over the first 32 columns of S buffer b (the
-            // S values are in registers now); PV(j) reads it from TMEM.
+            // P = 2^(s*sl2 - m) as f16 pairs over the first 32 columns of S
+            // buffer b (the S values are in registers now); PV(j) reads it
+            // from TMEM. Masked scores are -inf and give exactly 0.
             uint32_t pw[32];
-            float ps8[8];
+            float2 ps2[4];
 #pragma unroll
-            for (int i = 0; i < 8; ++i) ps8[i] = 0.f;
+            for (int i = 0; i < 4; ++i) ps2[i] = make_float2(0.f, 0.f);
+            const float2 scale2 = make_float2(sl2, sl2), negm2 = make_float2(-m, -m);
 #pragma unroll
             for (int c = 0; c < kBlockK / 2; ++c) {
-                const float p0 = ex2(sv[2 * c] - m);
-                const float p1 = ex2(sv[2 * c + 1] - m);
-                ps8[(2 * c) & 7] += p0;
-                ps8[(2 * c + 1) & 7] += p1;
-                pw[c] = pack_f16x2(p0, p1);
+                const float2 x = ffma2(make_float2(sv[2 * c], sv[2 * c + 1]), scale2, negm2);
+                const float2 pr = make_float2(ex2(x.x), ex2(x.y));
+                ps2[c & 3] = fadd2(ps2[c & 3], pr);
+                pw[c] = pack_f16x2(pr.x, pr.y);
             }
             tmem_st32(tmem + lane_addr + kColS + b * kBlockK, pw);
-            const float psum = ((ps8[0] + ps8[1]) + (ps8[2] + ps8[3])) +
-                               ((ps8[4] + ps8[5]) + (ps8[6] + ps8[7]));
-            l += psum;
+            l += ((ps2[0].x + ps2[0].y) + (ps2[1].x + ps2[1].y)) +
+                 ((ps2[2].x + ps2[2].y) + (ps2[3].x + ps2[3].y));
             tmem_wait_st();
             fence_before_sync();
             mbar_arrive(&bar.p_full[b]);
