@@ -52,12 +52,13 @@ constexpr int kBlockK = 64;   // keys per tile (QK N, PV K)
 constexpr int kThreadsPF = 288;
 constexpr uint32_t kQBytes = kBlockQ * kAttnHeadDim * 2;      // 64 KB
 constexpr uint32_t kKVBytes = kBlockK * kAttnHeadDim * 2;     // 32 KB
-constexpr int kStagesK = 4;
+constexpr uint32_t kPBytes = kBlockQ * kBlockK * 2;           // 16 KB
+constexpr int kStagesK = 3;
 constexpr int kStagesV = 3;
-constexpr uint32_t kSmemPF = (kStagesK + kStagesV) * kKVBytes + 1024;  // + alignment slack
+constexpr uint32_t kSmemPF = (kStagesK + kStagesV) * kKVBytes + 2 * kPBytes + 1024;  // + alignment slack
 static_assert(kQBytes <= kStagesK * kKVBytes, "Q is staged in the K ring");
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kColS = 0;     // S buffers at columns 0 and 64 (P aliases their first 32)
+constexpr uint32_t kColS = 0;     // S buffers at columns 0 and 64
 constexpr uint32_t kColO = 128;   // O at columns 128..383
 constexpr uint32_t kColQ = 384;   // Q at columns 384..511 (bf16 pairs)
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
@@ -207,7 +208,7 @@ struct PrefillParams {
 struct __align__(8) PrefillBarriers {
     uint64_t q_full, q_copied;
     uint64_t k_full[kStagesK], k_empty[kStagesK], v_full[kStagesV], v_empty[kStagesV];
-    uint64_t s_full[2], s_free[2], p_full[2], o_done, o_final;
+    uint64_t s_full[2], s_free[2], p_full[2], p_free[2], o_done, o_final;
 };
 
 __device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
@@ -242,6 +243,7 @@ __global__ void __launch_bounds__(kThreadsPF, 1)
         reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     unsigned char *sK = smem;                      // kStagesK stages (Q staged here first)
     unsigned char *sV = sK + kStagesK * kKVBytes;  // kStagesV stages (f16)
+    unsigned char *sP = sV + kStagesV * kKVBytes;  // 2 buffers (f16, K-major SW128)
     __shared__ PrefillBarriers bar;
     __shared__ uint32_t tmem_base_s;
     __shared__ volatile int abort_flag;
@@ -269,8 +271,9 @@ __global__ void __launch_bounds__(kThreadsPF, 1)
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&bar.s_full[b], 1);
-            mbar_init(&bar.s_free[b], 1);
+            mbar_init(&bar.s_free[b], 128);
             mbar_init(&bar.p_full[b], 128);
+            mbar_init(&bar.p_free[b], 1);
         }
         mbar_init(&bar.o_done, 1);
         mbar_init(&bar.o_final, 1);
@@ -347,7 +350,7 @@ __global__ void __launch_bounds__(kThreadsPF, 1)
             for (int j = warp == 1 ? 0 : 1; ok && j < nkt; j += 2) {
                 const int b = j & 1, kb = j % kStagesK;
                 if (!mbar_wait(&bar.k_full[kb], uint32_t(j / kStagesK) & 1u)) { ok = false; break; }
-                // S buffer b holds P(j-2) until PV(j-2) has read it.
+                // S buffer b is free once the softmax warps have read S(j-2).
                 if (j >= 2 && !mbar_wait(&bar.s_free[b], uint32_t((j - 2) >> 1) & 1u)) {
                     ok = false;
                     break;
@@ -370,7 +373,7 @@ __global__ void __launch_bounds__(kThreadsPF, 1)
         // ------------------------------------------------------------ O += P V issuer
         if (lane == 0) {
             const uint32_t id_pv = idesc_f16_f32(kBlockQ, kAttnHeadDim, 0, 1, false);
-            const uint32_t sv = smem_addr(sV);
+            const uint32_t sv = smem_addr(sV), sp = smem_addr(sP);
             bool ok = true;
             for (int j = 0; j < nkt; ++j) {
                 const int b = j & 1, vb = j % kStagesV;
@@ -379,14 +382,13 @@ __global__ void __launch_bounds__(kThreadsPF, 1)
                 fence_after_sync();
 #pragma unroll
                 for (int kk = 0; kk < kBlockK / 16; ++kk) {
+                    const uint64_t ad = smem_desc_sw128(sp + b * kPBytes + kk * 32, 16, 1024);
                     const uint64_t bd =
                         smem_desc_sw128(sv + vb * kKVBytes + kk * 2048, kKVBytes / 4, 1024);
-                    // P(j) sits in the first 32 columns of S buffer b (f16 pairs).
-                    mma_f16_ta(tmem + kColO, tmem + kColS + b * kBlockK + kk * 8, bd, id_pv,
-                               (j > 0 || kk > 0) ? 1u : 0u);
+                    mma_bf16(tmem + kColO, ad, bd, id_pv, (j > 0 || kk > 0) ? 1u : 0u);
                 }
                 mma_commit(&bar.v_empty[vb]);
-                mma_commit(&bar.s_free[b]);
+                mma_commit(&bar.p_free[b]);
                 mma_commit(&bar.o_done);
                 if (abort_flag) { ok = false; break; }
             }
@@ -443,6 +445,9 @@ __global__ void __launch_bounds__(kThreadsPF, 1)
             tmem_ld32(tmem + lane_addr + kColS + b * kBlockK, sr[0]);
             tmem_ld32(tmem + lane_addr + kColS + b * kBlockK + 32, sr[1]);
             tmem_wait_ld();
+            // S(j) is in registers: QK(j+2) may overwrite buffer b.
+            fence_before_sync();
+            mbar_arrive(&bar.s_free[b]);
             float sv[kBlockK];
             const int key0 = j * kBlockK;
             // Row max of the raw scores (scaling by sl2 > 0 keeps the order),
@@ -468,15 +473,19 @@ __global__ void __launch_bounds__(kThreadsPF, 1)
             const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
                                    fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
             const float m_new = fmaxf(m, mx * sl2);
+            // P buffer b held P(j-2): wait until PV(j-2) has read it. After
+            // this, o_done has completed j-1 or j phases (PV(j) needs this
+            // tile's P), so the rescale's parity wait below is exact.
+            if (j >= 2 && !wait_all(&bar.p_free[b], uint32_t((j - 2) >> 1) & 1u)) {
+                ok = false;
+                break;
+            }
             if (__any_sync(0xffffffffu, m_new > m + kRescaleThreshold)) {
                 // Every row of the warp moves to its exact max (corr = 1 where
                 // the max did not change); O and l are scaled by the same factor.
                 const float corr = ex2(m - m_new);  // 0 on the first tile
                 if (j > 0) {
                     // O holds PV(0..j-1): wait for PV(j-1), then rescale the rows.
-                    // PV(j-2) completed before QK(j) could start, and PV(j)
-                    // needs this tile's P, so o_done has completed j-1 or j
-                    // phases here: the parity wait is exact.
                     if (!wait_all(&bar.o_done, (j - 1) & 1)) { ok = false; break; }
                     fence_after_sync();
 #pragma unroll 1
@@ -493,24 +502,30 @@ __global__ void __launch_bounds__(kThreadsPF, 1)
                 l *= corr;
                 m = m_new;
             }
-            // P = 2^(s*sl2 - m) as f16 pairs over the first 32 columns of S
-            // buffer b (the S values are in registers now); PV(j) reads it
-            // from TMEM. Masked scores are -inf and give exactly 0.
-            uint32_t pw[32];
+            // P = 2^(s*sl2 - m) as f16 into the swizzled K-major tile of P
+            // buffer b. Masked scores are -inf and give exactly 0.
+            unsigned char *prow = sP + b * kPBytes;
             float2 ps2[4];
 #pragma unroll
             for (int i = 0; i < 4; ++i) ps2[i] = make_float2(0.f, 0.f);
             const float2 scale2 = make_float2(sl2, sl2), negm2 = make_float2(-m, -m);
 #pragma unroll
-            for (int c = 0; c < kBlockK / 2; ++c) {
-                const float2 x = ffma2(make_float2(sv[2 * c], sv[2 * c + 1]), scale2, negm2);
-                const float2 pr = make_float2(ex2(x.x), ex2(x.y));
-                ps2[c & 3] = fadd2(ps2[c & 3], pr);
-                pw[c] = pack_f16x2(pr.x, pr.y);
+            for (int ch = 0; ch < kBlockK / 8; ++ch) {
+                uint32_t w[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const int c = ch * 8 + 2 * e;
+                    const float2 x = ffma2(make_float2(sv[c], sv[c + 1]), scale2, negm2);
+                    const float2 pr = make_float2(ex2(x.x), ex2(x.y));
+                    ps2[e] = fadd2(ps2[e], pr);
+                    w[e] = pack_f16x2(pr.x, pr.y);
+                }
+                const uint32_t off = uint32_t(r) * 128u + ((uint32_t(ch) ^ (uint32_t(r) & 7u)) * 16u);
+                *reinterpret_cast<uint4 *>(prow + off) = make_uint4(w[0], w[1], w[2], w[3]);
             }
-            tmem_st32(tmem + lane_addr + kColS + b * kBlockK, pw);
             l += ((ps2[0].x + ps2[0].y) + (ps2[1].x + ps2[1].y)) +
                  ((ps2[2].x + ps2[2].y) + (ps2[3].x + ps2[3].y));
+            fence_proxy_async_smem();
             tmem_wait_st();
             fence_before_sync();
             mbar_arrive(&bar.p_full[b]);
