@@ -668,7 +668,7 @@ def run_ours(args) -> None:
             line["deltanet_prefill"] = {
                 "workload": (f"config5: {args.prefill_batch} x {args.prefill_len}-token chunked "
                              "Gated DeltaNet prefill per GPU (C=64, 16K/48V x 128) from a zero "
-                             "state, outputs + final f32 state; f32 CUDA cores"),
+                             "state, outputs + final f32 state; chunk-local WY terms on f32 CUDA cores, state pass on tcgen05 split-tf32 (3 products, ~f32 accuracy)"),
                 "ms": lin_prefill_ms, "tok_s": toks / (lin_prefill_ms * 1e-3),
                 "flops": flops, "tflops": flops / (lin_prefill_ms * 1e-3) / 1e12,
             }

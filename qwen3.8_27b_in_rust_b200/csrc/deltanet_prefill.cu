@@ -37,14 +37,23 @@
 // Everything is f32 on the CUDA cores (register-tiled products from shared
 // memory), so the chunked result stays within f32 rounding of the per-token
 // recurrence.
-#include "q38_common.cuh"
+#include "q38_sm100.cuh"
+
+#include <cudaTypedefs.h>
 
 namespace q38 {
 namespace {
 
 constexpr int kC = 64;       // chunk length
 constexpr int kD = kLinHeadDim;  // 128
-constexpr int kSlice = 32;   // state rows per CTA in the state pass
+
+// Round to the nearest tf32 (ties away): the tensor cores then see exactly
+// this value instead of a truncated one.
+__device__ __forceinline__ float tf32_rna(float x) {
+    uint32_t r;
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+    return __uint_as_float(r);
+}
 
 // ----------------------------------------------------------------------------
 // L1: conv + SiLU, 64-token segments in parallel
@@ -152,7 +161,8 @@ struct LocalParams {
     const float *beta, *alpha;   // sigmoid(beta), g
     float *w_out, *ut_out;       // [nseq][nchunk][v_heads][64][128]
     float *p_out;                // [nseq][nchunk][v_heads][64][64]
-    float *gam_out;              // [nseq][nchunk][v_heads][64]  gamma_r (log space)
+    float *eg_out;               // [nseq][nchunk][v_heads][64]  e^{gamma_r}
+    float *kt_out;               // [nseq][nchunk][v_heads][128][64]  e^{gamma_C-gamma_r} K^T
     int count, nchunk, qk_heads, v_heads, qkv_dim;
 };
 
@@ -267,7 +277,7 @@ __global__ void __launch_bounds__(256, 2) linear_prefill_local_kernel(LocalParam
     const size_t wbase = ((size_t(s) * p.nchunk + chunk) * p.v_heads + h) * kC * kD;
     const int rb = tid / 32, cg = tid % 32;
     auto tri_times = [&](const float *X, const float *scale_a, const float *scale_b,
-                         float *out) {
+                         float *out, bool round_tf32) {
         float acc[8][4] = {};
 #pragma unroll 4
         for (int m = 0; m < kC; ++m) {
@@ -283,11 +293,25 @@ __global__ void __launch_bounds__(256, 2) linear_prefill_local_kernel(LocalParam
             }
         }
 #pragma unroll
-        for (int a = 0; a < 8; ++a)
+        for (int a = 0; a < 8; ++a) {
+            if (round_tf32) {
+#pragma unroll
+                for (int b = 0; b < 4; ++b) acc[a][b] = tf32_rna(acc[a][b]);
+            }
             reinterpret_cast<float4 *>(out + (rb * 8 + a) * kD)[cg] =
                 make_float4(acc[a][0], acc[a][1], acc[a][2], acc[a][3]);
+        }
     };
-    tri_times(Ks, bet, egs, p.w_out + wbase);
+    tri_times(Ks, bet, egs, p.w_out + wbase, false);
+    // K~^T[i][r] = e^{gamma_C - gamma_r} K[r][i] (the state update's B operand).
+    {
+        float *kt = p.kt_out + ((size_t(s) * p.nchunk + chunk) * p.v_heads + h) * kD * kC;
+        const float gC = gam[kC - 1];
+        for (int idx = tid; idx < kD * kC; idx += 256) {
+            const int i = idx / kC, r = idx % kC;
+            kt[idx] = expf(gC - gam[r]) * Ks[r * kPad + i];
+        }
+    }
     __syncthreads();  // Xs (Q) is no longer needed: load V
     for (int idx = tid; idx < kC * (kD / 4); idx += 256) {
         const int r = idx / (kD / 4), c4 = idx % (kD / 4);
@@ -300,158 +324,429 @@ __global__ void __launch_bounds__(256, 2) linear_prefill_local_kernel(LocalParam
         vd[0] = v.x; vd[1] = v.y; vd[2] = v.z; vd[3] = v.w;
     }
     __syncthreads();
-    tri_times(Xs, bet, nullptr, p.ut_out + wbase);
+    tri_times(Xs, bet, nullptr, p.ut_out + wbase, false);
     if (tid < kC)
-        p.gam_out[((size_t(s) * p.nchunk + chunk) * p.v_heads + h) * kC + tid] = gam[tid];
+        p.eg_out[((size_t(s) * p.nchunk + chunk) * p.v_heads + h) * kC + tid] = egs[tid];
 }
 
 // ----------------------------------------------------------------------------
-// L4: sequential state pass over the chunks
+// L4: sequential state pass over the chunks, on tcgen05 (kind::tf32, split)
 // ----------------------------------------------------------------------------
-struct StateParams {
-    const float *qkv;
-    const float *w, *ut, *pm, *gam;  // from L3
-    float *delta_state;             // slot base [batch][v_heads][128][128]
-    float *o_out;                   // [nseq][count][v_heads*128]
-    int seq0, count, nchunk, qk_heads, v_heads, qkv_dim;
+// One CTA per (value head, sequence). The head's state S [128 j][128 i] lives
+// in TMEM (lane j) for the whole prompt; per chunk, with U^T [j][r] = U[r][j]:
+//   D_U | D_O = S [W ; Q~]^T      (M=128, N=128, K=128; A = S from TMEM)
+//   U^T       = Ut^T - D_U         (epilogue warps)
+//   D_PU      = U^T P^T            (M=128, N=64,  K=64;  A = U^T from TMEM)
+//   S         = e^{gamma_C} S      (epilogue warps)
+//   S        += U^T K~             (M=128, N=128, K=64)
+//   O[r][j]   = (D_O[j][r] + D_PU[j][r]) / sqrt(128),   Q~ = diag(e^gamma) Q
+// tf32 keeps 10 mantissa bits, which alone leaves errors of a few 1e-3 after
+// the output RMSNorm; so every operand X is split as X = hi + lo with
+// hi = tf32(X) and lo = X - hi (exact in f32), and each product is
+// A.B = hi(A).hi(B) + lo(A).hi(B) + hi(A).lo(B) (the dropped lo.lo term is
+// 2^-22 relative): three MMAs per K step, f32 accumulation, ~f32 accuracy.
+// S and U^T are kept as (hi, lo) column pairs in TMEM; the B operands are
+// split in shared memory right after their TMA load, by four splitter warps.
+constexpr int kThreadsLS = 352;  // w0 W/Q/P loads, w1 MMA, w2-5 epilogue, w6 K~ loads, w7-10 split
+constexpr uint32_t kB1Bytes = 128 * 128 * 4;  // [W ; Q~]: 4 column blocks of 128 rows x 128 B
+constexpr uint32_t kPmBytes = 64 * 64 * 4;    // P: 2 column blocks of 64 rows x 128 B
+constexpr uint32_t kKtBytes = 128 * 64 * 4;   // K~^T: 2 column blocks of 128 rows x 128 B
+constexpr uint32_t kSmemLS = 2 * (kB1Bytes + kPmBytes + kKtBytes) + 1024;
+// TMEM columns: S (hi, or the f32 value around the update) | S lo | D_U, then
+// U^T hi | D_O | U^T lo | D_PU.
+constexpr uint32_t kColSh = 0, kColSl = 128, kColU = 256, kColOq = 320, kColUl = 384,
+                   kColPU = 448, kTmemColsLS = 512;
+
+struct StateTcParams {
+    const float *ut;      // [planes][64][128]
+    const float *eg;      // [planes][64]  e^{gamma_r}
+    float *delta_state;   // slot base [batch][v_heads][128][128]
+    float *o_out;         // [nseq][count][v_heads*128]
+    int *err;
+    int seq0, count, nchunk, qk_heads, v_heads;
 };
 
-__global__ void __launch_bounds__(256) linear_prefill_state_kernel(StateParams p) {
-    extern __shared__ float sm[];
-    float *Ss = sm;                    // [32][129]   state slice (rows j, dims i)
-    float *Bs = Ss + kSlice * kPad;    // [64][129]   W, then K
-    float *Qs = Bs + kC * kPad;        // [64][129]   Q
-    float *Ps = Qs + kC * kPad;        // [64][65]    P
-    float *Us = Ps + kC * (kC + 1);    // [64][33]    U slice
-    __shared__ float gs[kC];
+struct __align__(8) StateTcBarriers {
+    uint64_t b1_raw, b1_split, b1_free, p_raw, p_split, p_free, k_raw, k_split, k_free;
+    uint64_t s_ready, uo_full, u_ready, s_scaled, pu_full, s_done, s_split;
+};
 
-    const int slice = blockIdx.x, h = blockIdx.y, s = blockIdx.z;
-    const int tid = threadIdx.x;
-    const int kh = h % p.qk_heads;
-    const int j0 = slice * kSlice;
-    const int qk_dim = p.qk_heads * kD;
-    float *S = p.delta_state + ((size_t(p.seq0 + s) * p.v_heads + h) * kD + j0) * kD;
-    const float query_scale = 1.0f / sqrtf(float(kD));
+__device__ __forceinline__ void mma_tf32_ts(uint32_t d, uint32_t a_tmem, uint64_t b,
+                                            uint32_t id, uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d),
+        "r"(a_tmem), "l"(b), "r"(id), "r"(acc)
+        : "memory");
+}
+__host__ __device__ constexpr uint32_t idesc_tf32(int M, int N) {
+    return (1u << 4) | (2u << 7) | (2u << 10) | (uint32_t(N >> 3) << 17) | (uint32_t(M >> 4) << 24);
+}
 
-    for (int idx = tid; idx < kSlice * kD; idx += 256)
-        Ss[(idx / kD) * kPad + idx % kD] = S[idx];
-
-    // Thread tiles: for U and O (64 rows x 32 cols): 2 rows... use rows ru..ru+7, col cu.
-    const int ru = (tid / 32) * 8, cu = tid % 32;
-    // For the state update (32 rows x 128 dims): row js, dims 4*id..4*id+3 (8 rows per thread).
-    const int jsb = (tid / 32) * 4, idb = tid % 32;
-
-    for (int chunk = 0; chunk < p.nchunk; ++chunk) {
-        const int t0 = chunk * kC;
-        const size_t lb = ((size_t(s) * p.nchunk + chunk) * p.v_heads + h);
-        __syncthreads();
-        // Stage W, Q, P and e^gamma for this chunk.
-        for (int idx = tid; idx < kC * (kD / 4); idx += 256) {
-            const int r = idx / (kD / 4), c4 = idx % (kD / 4);
-            const float4 w4 = reinterpret_cast<const float4 *>(p.w + lb * kC * kD)[idx];
-            float4 q4 = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (t0 + r < p.count)
-                q4 = reinterpret_cast<const float4 *>(
-                    p.qkv + (size_t(s) * p.count + t0 + r) * p.qkv_dim + kh * kD)[c4];
-            float *wd = Bs + r * kPad + c4 * 4;
-            float *qd = Qs + r * kPad + c4 * 4;
-            wd[0] = w4.x; wd[1] = w4.y; wd[2] = w4.z; wd[3] = w4.w;
-            qd[0] = q4.x; qd[1] = q4.y; qd[2] = q4.z; qd[3] = q4.w;
+// hi/lo split of n_vec4 float4s of `hi` in place, lo into `lo`; rows of 128 B
+// at or past `scaled_row0` within each 128-row block are first multiplied by
+// scale[row - scaled_row0] (Q~ = e^gamma Q).
+__device__ __forceinline__ void split_tile(unsigned char *hi, unsigned char *lo, int n_vec4,
+                                           int t, int nthreads, int scaled_row0,
+                                           const float *scale) {
+    for (int v = t; v < n_vec4; v += nthreads) {
+        float4 x = reinterpret_cast<float4 *>(hi)[v];
+        const int row = (v * 16 % 16384) / 128;
+        if (scale && row >= scaled_row0) {
+            const float f = scale[row - scaled_row0];
+            x.x *= f;
+            x.y *= f;
+            x.z *= f;
+            x.w *= f;
         }
-        for (int idx = tid; idx < kC * kC; idx += 256)
-            Ps[(idx / kC) * (kC + 1) + idx % kC] = p.pm[lb * kC * kC + idx];
-        if (tid < kC) gs[tid] = p.gam[lb * kC + tid];
-        __syncthreads();
-
-        // U = Ut - W S^T  (rows r: ru..ru+7, column j = cu) and Q S^T for O.
-        float u[8], qs[8];
-        {
-            const float *ut = p.ut + lb * kC * kD;
-#pragma unroll
-            for (int a = 0; a < 8; ++a) {
-                u[a] = ut[(ru + a) * kD + j0 + cu];
-                qs[a] = 0.f;
-            }
-            float wsum[8] = {}, qsum[8] = {};
-#pragma unroll 4
-            for (int i = 0; i < kD; ++i) {
-                const float sv = Ss[cu * kPad + i];
-#pragma unroll
-                for (int a = 0; a < 8; ++a) {
-                    wsum[a] = fmaf(Bs[(ru + a) * kPad + i], sv, wsum[a]);
-                    qsum[a] = fmaf(Qs[(ru + a) * kPad + i], sv, qsum[a]);
-                }
-            }
-#pragma unroll
-            for (int a = 0; a < 8; ++a) {
-                u[a] -= wsum[a];
-                qs[a] = qsum[a];
-                Us[(ru + a) * (kSlice + 1) + cu] = u[a];
-            }
-        }
-        __syncthreads();
-        // O = diag(e^gamma) Q S^T + P U, scaled by 1/sqrt(128).
-        {
-            float o[8];
-#pragma unroll
-            for (int a = 0; a < 8; ++a) o[a] = expf(gs[ru + a]) * qs[a];
-#pragma unroll 4
-            for (int m = 0; m < kC; ++m) {
-                const float um = Us[m * (kSlice + 1) + cu];
-#pragma unroll
-                for (int a = 0; a < 8; ++a) o[a] = fmaf(Ps[(ru + a) * (kC + 1) + m], um, o[a]);
-            }
-#pragma unroll
-            for (int a = 0; a < 8; ++a) {
-                const int t = t0 + ru + a;
-                if (t < p.count)
-                    p.o_out[(size_t(s) * p.count + t) * (size_t(p.v_heads) * kD) + h * kD + j0 + cu] =
-                        o[a] * query_scale;
-            }
-        }
-        // Stage K (over W) for the state update.
-        __syncthreads();
-        for (int idx = tid; idx < kC * (kD / 4); idx += 256) {
-            const int r = idx / (kD / 4), c4 = idx % (kD / 4);
-            float4 k4 = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (t0 + r < p.count)
-                k4 = reinterpret_cast<const float4 *>(
-                    p.qkv + (size_t(s) * p.count + t0 + r) * p.qkv_dim + qk_dim + kh * kD)[c4];
-            float *kd = Bs + r * kPad + c4 * 4;
-            kd[0] = k4.x; kd[1] = k4.y; kd[2] = k4.z; kd[3] = k4.w;
-        }
-        __syncthreads();
-        // S' = e^{gamma_C} S + U^T diag(e^{gamma_C - gamma}) K.
-        {
-            const float gC = gs[kC - 1];
-            float acc[4][4];
-            const float egC = expf(gC);
-#pragma unroll
-            for (int a = 0; a < 4; ++a)
-#pragma unroll
-                for (int b = 0; b < 4; ++b) acc[a][b] = egC * Ss[(jsb + a) * kPad + idb * 4 + b];
-#pragma unroll 2
-            for (int m = 0; m < kC; ++m) {
-                const float dec = expf(gC - gs[m]);
-                float kv[4];
-#pragma unroll
-                for (int b = 0; b < 4; ++b) kv[b] = Bs[m * kPad + idb * 4 + b] * dec;
-#pragma unroll
-                for (int a = 0; a < 4; ++a) {
-                    const float um = Us[m * (kSlice + 1) + jsb + a];
-#pragma unroll
-                    for (int b = 0; b < 4; ++b) acc[a][b] = fmaf(um, kv[b], acc[a][b]);
-                }
-            }
-            __syncthreads();
-#pragma unroll
-            for (int a = 0; a < 4; ++a)
-#pragma unroll
-                for (int b = 0; b < 4; ++b) Ss[(jsb + a) * kPad + idb * 4 + b] = acc[a][b];
-        }
+        float4 h4, l4;
+        h4.x = tf32_rna(x.x);
+        h4.y = tf32_rna(x.y);
+        h4.z = tf32_rna(x.z);
+        h4.w = tf32_rna(x.w);
+        l4.x = x.x - h4.x;
+        l4.y = x.y - h4.y;
+        l4.z = x.z - h4.z;
+        l4.w = x.w - h4.w;
+        reinterpret_cast<float4 *>(hi)[v] = h4;
+        reinterpret_cast<float4 *>(lo)[v] = l4;
     }
+}
+
+__global__ void __launch_bounds__(kThreadsLS, 1)
+    linear_prefill_state_kernel(const __grid_constant__ CUtensorMap map_w,
+                                const __grid_constant__ CUtensorMap map_q,
+                                const __grid_constant__ CUtensorMap map_p,
+                                const __grid_constant__ CUtensorMap map_kt, StateTcParams p) {
+    using namespace sm100;
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    unsigned char *smem =
+        reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    unsigned char *sB1h = smem, *sB1l = sB1h + kB1Bytes;
+    unsigned char *sPh = sB1l + kB1Bytes, *sPl = sPh + kPmBytes;
+    unsigned char *sKh = sPl + kPmBytes, *sKl = sKh + kKtBytes;
+    __shared__ StateTcBarriers bar;
+    __shared__ uint32_t tmem_base_s;
+    __shared__ volatile int abort_flag;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int h = blockIdx.x, s = blockIdx.y;
+    const int kh = h % p.qk_heads;  // ops.rs:699
+    auto plane = [&](int c) { return (s * p.nchunk + c) * p.v_heads + h; };
+
+    if (threadIdx.x == 0) {
+        abort_flag = 0;
+        mbar_init(&bar.b1_raw, 1);
+        mbar_init(&bar.b1_split, 128);
+        mbar_init(&bar.b1_free, 1);
+        mbar_init(&bar.p_raw, 1);
+        mbar_init(&bar.p_split, 128);
+        mbar_init(&bar.p_free, 1);
+        mbar_init(&bar.k_raw, 1);
+        mbar_init(&bar.k_split, 128);
+        mbar_init(&bar.k_free, 1);
+        mbar_init(&bar.s_ready, 128);
+        mbar_init(&bar.uo_full, 1);
+        mbar_init(&bar.u_ready, 128);
+        mbar_init(&bar.s_scaled, 128);
+        mbar_init(&bar.pu_full, 1);
+        mbar_init(&bar.s_done, 1);
+        mbar_init(&bar.s_split, 128);
+        fence_barrier_init();
+    }
+    if (warp == 1) {
+        tmem_alloc(&tmem_base_s, kTmemColsLS);
+        tmem_relinquish();
+    }
+    fence_before_sync();
     __syncthreads();
-    for (int idx = tid; idx < kSlice * kD; idx += 256) S[idx] = Ss[(idx / kD) * kPad + idx % kD];
+    fence_after_sync();
+    const uint32_t tmem = tmem_base_s;
+    auto fail = [&]() {
+        abort_flag = 1;
+        set_error(p.err, kDevErrTimeout);
+    };
+
+    if (warp == 0) {
+        // ---------------------------------------------------------- [W ; Q] and P loads
+        if (lane == 0) {
+            tma_prefetch_desc(&map_w);
+            tma_prefetch_desc(&map_q);
+            tma_prefetch_desc(&map_p);
+            for (int c = 0; c < p.nchunk && !abort_flag; ++c) {
+                const uint32_t prev = uint32_t(c - 1) & 1u;
+                if (c >= 1 && !mbar_wait(&bar.b1_free, prev)) { fail(); break; }
+                mbar_arrive_expect_tx(&bar.b1_raw, kB1Bytes);
+                for (int blk = 0; blk < 4; ++blk) {
+                    tma_load_3d(sB1h + blk * 16384, &map_w, blk * 32, 0, plane(c), &bar.b1_raw);
+                    tma_load_3d(sB1h + blk * 16384 + 8192, &map_q, kh * kD + blk * 32,
+                                s * p.count + c * kC, 0, &bar.b1_raw);
+                }
+                if (c >= 1 && !mbar_wait(&bar.p_free, prev)) { fail(); break; }
+                mbar_arrive_expect_tx(&bar.p_raw, kPmBytes);
+                for (int blk = 0; blk < 2; ++blk)
+                    tma_load_3d(sPh + blk * 8192, &map_p, blk * 32, 0, plane(c), &bar.p_raw);
+            }
+        }
+    } else if (warp == 6) {
+        // ---------------------------------------------------------- K~^T loads
+        if (lane == 0) {
+            tma_prefetch_desc(&map_kt);
+            for (int c = 0; c < p.nchunk && !abort_flag; ++c) {
+                if (c >= 1 && !mbar_wait(&bar.k_free, uint32_t(c - 1) & 1u)) { fail(); break; }
+                mbar_arrive_expect_tx(&bar.k_raw, kKtBytes);
+                for (int blk = 0; blk < 2; ++blk)
+                    tma_load_3d(sKh + blk * 16384, &map_kt, blk * 32, 0, plane(c), &bar.k_raw);
+            }
+        }
+    } else if (warp >= 7) {
+        // ---------------------------------------------------------- hi/lo splitters
+        const int t = threadIdx.x - 7 * 32;  // 0..127
+        bool ok = true;
+        for (int c = 0; ok && c < p.nchunk; ++c) {
+            const uint32_t ph = uint32_t(c) & 1u;
+            const float *egp = p.eg + size_t(plane(c)) * kC;
+            if (!mbar_wait(&bar.b1_raw, ph)) { ok = false; break; }
+            split_tile(sB1h, sB1l, int(kB1Bytes / 16), t, 128, kC, egp);
+            fence_proxy_async_smem();
+            mbar_arrive(&bar.b1_split);
+            if (!mbar_wait(&bar.p_raw, ph)) { ok = false; break; }
+            split_tile(sPh, sPl, int(kPmBytes / 16), t, 128, kC, nullptr);
+            fence_proxy_async_smem();
+            mbar_arrive(&bar.p_split);
+            if (!mbar_wait(&bar.k_raw, ph)) { ok = false; break; }
+            split_tile(sKh, sKl, int(kKtBytes / 16), t, 128, kD, nullptr);
+            fence_proxy_async_smem();
+            mbar_arrive(&bar.k_split);
+            if (abort_flag) ok = false;
+        }
+        if (!ok && t == 0) fail();
+    } else if (warp == 1) {
+        // ---------------------------------------------------------- MMA issuer
+        if (lane == 0) {
+            const uint32_t id_n128 = idesc_tf32(128, 128), id_n64 = idesc_tf32(128, 64);
+            const uint32_t b1h = smem_addr(sB1h), b1l = smem_addr(sB1l), ph_ = smem_addr(sPh),
+                           pl_ = smem_addr(sPl), khh = smem_addr(sKh), kll = smem_addr(sKl);
+            bool ok = mbar_wait(&bar.s_ready, 0);
+            for (int c = 0; ok && c < p.nchunk; ++c) {
+                const uint32_t ph = uint32_t(c) & 1u;
+                // S of this chunk is split (which follows the last update and
+                // the epilogue's reads of D_O / U^T of the previous chunk).
+                if (c >= 1 && !mbar_wait(&bar.s_split, ph ^ 1u)) { ok = false; break; }
+                if (!mbar_wait(&bar.b1_split, ph)) { ok = false; break; }
+                fence_after_sync();
+#pragma unroll 1
+                for (int kk = 0; kk < kD / 8; ++kk) {
+                    const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
+                    const uint64_t bh = smem_desc_sw128(b1h + off, 16, 1024);
+                    const uint64_t bl = smem_desc_sw128(b1l + off, 16, 1024);
+                    mma_tf32_ts(tmem + kColU, tmem + kColSh + kk * 8, bh, id_n128, kk > 0 ? 1u : 0u);
+                    mma_tf32_ts(tmem + kColU, tmem + kColSl + kk * 8, bh, id_n128, 1u);
+                    mma_tf32_ts(tmem + kColU, tmem + kColSh + kk * 8, bl, id_n128, 1u);
+                }
+                mma_commit(&bar.uo_full);
+                mma_commit(&bar.b1_free);
+                if (!mbar_wait(&bar.u_ready, ph) || !mbar_wait(&bar.p_split, ph)) {
+                    ok = false;
+                    break;
+                }
+                fence_after_sync();
+#pragma unroll 1
+                for (int kk = 0; kk < kC / 8; ++kk) {
+                    const uint32_t off = (kk >> 2) * 8192 + (kk & 3) * 32;
+                    const uint64_t bh = smem_desc_sw128(ph_ + off, 16, 1024);
+                    const uint64_t bl = smem_desc_sw128(pl_ + off, 16, 1024);
+                    mma_tf32_ts(tmem + kColPU, tmem + kColU + kk * 8, bh, id_n64, kk > 0 ? 1u : 0u);
+                    mma_tf32_ts(tmem + kColPU, tmem + kColUl + kk * 8, bh, id_n64, 1u);
+                    mma_tf32_ts(tmem + kColPU, tmem + kColU + kk * 8, bl, id_n64, 1u);
+                }
+                mma_commit(&bar.pu_full);
+                mma_commit(&bar.p_free);
+                if (!mbar_wait(&bar.s_scaled, ph) || !mbar_wait(&bar.k_split, ph)) {
+                    ok = false;
+                    break;
+                }
+                fence_after_sync();
+#pragma unroll 1
+                for (int kk = 0; kk < kC / 8; ++kk) {
+                    const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
+                    const uint64_t bh = smem_desc_sw128(khh + off, 16, 1024);
+                    const uint64_t bl = smem_desc_sw128(kll + off, 16, 1024);
+                    mma_tf32_ts(tmem + kColSh, tmem + kColU + kk * 8, bh, id_n128, 1u);
+                    mma_tf32_ts(tmem + kColSh, tmem + kColUl + kk * 8, bh, id_n128, 1u);
+                    mma_tf32_ts(tmem + kColSh, tmem + kColU + kk * 8, bl, id_n128, 1u);
+                }
+                mma_commit(&bar.s_done);
+                mma_commit(&bar.k_free);
+                if (abort_flag) { ok = false; break; }
+            }
+            if (!ok) fail();
+        }
+    } else {
+        // ---------------------------------------------------------- epilogue (row j per thread)
+        const int sub = warp & 3;
+        const int j = sub * 32 + lane;
+        const uint32_t lane_addr = uint32_t(sub * 32) << 16;
+        const float query_scale = 1.0f / sqrtf(float(kD));
+        float *S = p.delta_state + ((size_t(p.seq0 + s) * p.v_heads + h) * kD + j) * kD;
+        auto wait_all = [&](uint64_t *b, uint32_t parity) {
+            return __all_sync(0xffffffffu, mbar_wait(b, parity));
+        };
+        // Writes hi/lo of the 32 values in w to TMEM columns col_hi / col_lo.
+        auto st_split = [&](uint32_t col_hi, uint32_t col_lo, uint32_t (&w)[32]) {
+            uint32_t lo[32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+                const float x = __uint_as_float(w[i]);
+                const float hi = tf32_rna(x);
+                lo[i] = __float_as_uint(x - hi);
+                w[i] = __float_as_uint(hi);
+            }
+            tmem_st32(tmem + lane_addr + col_hi, w);
+            tmem_st32(tmem + lane_addr + col_lo, lo);
+        };
+        bool ok = true;
+#pragma unroll 1
+        for (int cb = 0; cb < 4; ++cb) {
+            uint32_t w[32];
+#pragma unroll
+            for (int i = 0; i < 32; i += 4) {
+                const float4 v = *reinterpret_cast<const float4 *>(S + cb * 32 + i);
+                w[i] = __float_as_uint(v.x);
+                w[i + 1] = __float_as_uint(v.y);
+                w[i + 2] = __float_as_uint(v.z);
+                w[i + 3] = __float_as_uint(v.w);
+            }
+            st_split(kColSh + cb * 32, kColSl + cb * 32, w);
+        }
+        tmem_wait_st();
+        fence_before_sync();
+        mbar_arrive(&bar.s_ready);
+        for (int c = 0; ok && c < p.nchunk; ++c) {
+            const uint32_t ph = uint32_t(c) & 1u;
+            const size_t lb = size_t(plane(c));
+            const float *utp = p.ut + lb * kC * kD + j;
+            float ut[kC];
+#pragma unroll
+            for (int r = 0; r < kC; ++r) ut[r] = utp[r * kD];
+            const float egC = p.eg[lb * kC + kC - 1];
+            if (!wait_all(&bar.uo_full, ph)) { ok = false; break; }
+            fence_after_sync();
+            // U^T row j = Ut^T - D_U as (hi, lo).
+#pragma unroll
+            for (int half = 0; half < 2; ++half) {
+                uint32_t d[32];
+                tmem_ld32(tmem + lane_addr + kColU + half * 32, d);
+                tmem_wait_ld();
+#pragma unroll
+                for (int i = 0; i < 32; ++i)
+                    d[i] = __float_as_uint(ut[half * 32 + i] - __uint_as_float(d[i]));
+                st_split(kColU + half * 32, kColUl + half * 32, d);
+            }
+            // e^{gamma_r} (S0 q_r), kept until D_PU is ready.
+            float os[kC];
+#pragma unroll
+            for (int half = 0; half < 2; ++half) {
+                uint32_t d[32];
+                tmem_ld32(tmem + lane_addr + kColOq + half * 32, d);
+                tmem_wait_ld();
+#pragma unroll
+                for (int i = 0; i < 32; ++i) os[half * 32 + i] = __uint_as_float(d[i]);
+            }
+            tmem_wait_st();
+            fence_before_sync();
+            mbar_arrive(&bar.u_ready);
+            // S <- e^{gamma_C} (hi + lo), as one f32 value for the update.
+#pragma unroll 1
+            for (int cb = 0; cb < 4; ++cb) {
+                uint32_t a[32], b[32];
+                tmem_ld32(tmem + lane_addr + kColSh + cb * 32, a);
+                tmem_ld32(tmem + lane_addr + kColSl + cb * 32, b);
+                tmem_wait_ld();
+#pragma unroll
+                for (int i = 0; i < 32; ++i)
+                    a[i] = __float_as_uint((__uint_as_float(a[i]) + __uint_as_float(b[i])) * egC);
+                tmem_st32(tmem + lane_addr + kColSh + cb * 32, a);
+            }
+            tmem_wait_st();
+            fence_before_sync();
+            mbar_arrive(&bar.s_scaled);
+            if (!wait_all(&bar.pu_full, ph)) { ok = false; break; }
+            fence_after_sync();
+            const int t0 = c * kC;
+            float *orow = p.o_out + (size_t(s) * p.count + t0) * (size_t(p.v_heads) * kD) + h * kD + j;
+#pragma unroll
+            for (int half = 0; half < 2; ++half) {
+                uint32_t d[32];
+                tmem_ld32(tmem + lane_addr + kColPU + half * 32, d);
+                tmem_wait_ld();
+#pragma unroll
+                for (int i = 0; i < 32; ++i) {
+                    const int r = half * 32 + i;
+                    if (t0 + r < p.count)
+                        orow[size_t(r) * p.v_heads * kD] =
+                            (os[r] + __uint_as_float(d[i])) * query_scale;
+                }
+            }
+            // The updated S as (hi, lo) for the next chunk; the last one is
+            // the final state.
+            if (!wait_all(&bar.s_done, ph)) { ok = false; break; }
+            fence_after_sync();
+            const bool last = c == p.nchunk - 1;
+#pragma unroll 1
+            for (int cb = 0; cb < 4; ++cb) {
+                uint32_t w[32];
+                tmem_ld32(tmem + lane_addr + kColSh + cb * 32, w);
+                tmem_wait_ld();
+                if (last) {
+#pragma unroll
+                    for (int i = 0; i < 32; i += 4)
+                        *reinterpret_cast<float4 *>(S + cb * 32 + i) =
+                            make_float4(__uint_as_float(w[i]), __uint_as_float(w[i + 1]),
+                                        __uint_as_float(w[i + 2]), __uint_as_float(w[i + 3]));
+                } else {
+                    st_split(kColSh + cb * 32, kColSl + cb * 32, w);
+                }
+            }
+            tmem_wait_st();
+            fence_before_sync();
+            mbar_arrive(&bar.s_split);
+            if (__any_sync(0xffffffffu, abort_flag != 0)) { ok = false; break; }
+        }
+        if (!ok && lane == 0) fail();
+    }
+    fence_before_sync();
+    __syncthreads();
+    fence_after_sync();
+    if (warp == 1) tmem_dealloc(tmem, kTmemColsLS);
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_tiled_ls() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+        void *f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) !=
+                cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            f = nullptr;
+        return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+    }();
+    return fn;
+}
+
+// 3-D f32 map over [planes][rows][cols] with a box of 32 x box_rows x 1 and
+// 128-byte swizzle (K-major tf32 operand tiles).
+bool make_map_f32(CUtensorMap *m, const void *base, uint64_t cols, uint64_t rows, uint64_t planes,
+                  uint32_t box_rows) {
+    auto enc = encode_tiled_ls();
+    if (!enc) return false;
+    cuuint64_t dims[3] = {cols, rows, planes};
+    cuuint64_t strides[2] = {cols * 4, cols * 4 * rows};
+    cuuint32_t box[3] = {32, box_rows, 1};
+    cuuint32_t es[3] = {1, 1, 1};
+    return enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<void *>(base), dims, strides, box,
+               es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 // ----------------------------------------------------------------------------
@@ -488,8 +783,9 @@ __global__ void __launch_bounds__(256) linear_prefill_out_kernel(OutParams p) {
 }  // namespace
 
 size_t linear_prefill_scratch_floats(int nchunk_total, int v_heads) {
-    // W and Ut: [chunks][v_heads][64][128] each; P: [chunks][v_heads][64][64]; gamma.
-    return size_t(nchunk_total) * v_heads * kC * (2 * kD + kC + 1);
+    // W, Ut: [chunks][v_heads][64][128] each; P: [..][64][64]; e^gamma: [..][64];
+    // K~^T: [..][128][64].
+    return size_t(nchunk_total) * v_heads * kC * (3 * kD + kC + 1);
 }
 
 cudaError_t launch_linear_prefill(const LinearPrefillLaunch &a, cudaStream_t stream) {
@@ -515,8 +811,9 @@ cudaError_t launch_linear_prefill(const LinearPrefillLaunch &a, cudaStream_t str
     float *w = a.scratch;
     float *ut = w + per * kC * kD;
     float *pm = ut + per * kC * kD;
-    float *gm = pm + per * kC * kC;
-    LocalParams lp{a.qkv, a.beta, a.alpha, w, ut, pm, gm, a.count, nchunk, a.qk_heads,
+    float *eg = pm + per * kC * kC;
+    float *kt = eg + per * kC;
+    LocalParams lp{a.qkv, a.beta, a.alpha, w, ut, pm, eg, kt, a.count, nchunk, a.qk_heads,
                    a.v_heads, qkv_dim};
     const size_t smem_l = size_t(2 * kC * kPad + 2 * kC * (kC + 1)) * sizeof(float);
     if ((e = cudaFuncSetAttribute(linear_prefill_local_kernel,
@@ -526,15 +823,19 @@ cudaError_t launch_linear_prefill(const LinearPrefillLaunch &a, cudaStream_t str
     linear_prefill_local_kernel<<<dim3(nchunk, a.v_heads, a.nseq), 256, smem_l, stream>>>(lp);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
 
-    StateParams sp{a.qkv, w, ut, pm, gm, a.delta_state, a.attention, a.seq0, a.count, nchunk,
-                   a.qk_heads, a.v_heads, qkv_dim};
-    const size_t smem_s = size_t(kSlice * kPad + 2 * kC * kPad + kC * (kC + 1) +
-                                 kC * (kSlice + 1)) * sizeof(float);
+    CUtensorMap mw, mq, mp, mk;
+    if (!make_map_f32(&mw, w, kD, kC, per, kC) ||
+        !make_map_f32(&mq, a.qkv, qkv_dim, uint64_t(a.nseq) * a.count, 1, kC) ||
+        !make_map_f32(&mp, pm, kC, kC, per, kC) || !make_map_f32(&mk, kt, kC, kD, per, kD))
+        return cudaErrorInvalidValue;
+    StateTcParams sp{ut, eg, a.delta_state, a.attention, a.err, a.seq0, a.count, nchunk,
+                     a.qk_heads, a.v_heads};
     if ((e = cudaFuncSetAttribute(linear_prefill_state_kernel,
-                                  cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem_s))) !=
+                                  cudaFuncAttributeMaxDynamicSharedMemorySize, int(kSmemLS))) !=
         cudaSuccess)
         return e;
-    linear_prefill_state_kernel<<<dim3(kD / kSlice, a.v_heads, a.nseq), 256, smem_s, stream>>>(sp);
+    linear_prefill_state_kernel<<<dim3(a.v_heads, a.nseq), kThreadsLS, kSmemLS, stream>>>(
+        mw, mq, mp, mk, sp);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
 
     OutParams op{a.z, a.ssm_norm, a.attention, a.count, a.v_heads, a.eps};

@@ -138,6 +138,7 @@ struct LinearPrefillLaunch {
     float *delta_state;         // slot base [batch][v_heads][128][128]
     const float *conv_w, *dt_bias, *ssm_a, *ssm_norm;
     float *scratch;             // linear_prefill_scratch_floats(nseq*nchunk, v_heads)
+    int *err;                   // device error bits
     int seq0, nseq, count, qk_heads, v_heads;
     float eps;
 };

@@ -795,6 +795,7 @@ int q38_linear_prefill(q38_ctx *ctx, q38_state *st, int layer, int seq0, int nse
     a.ssm_a = it->second.ssm_a;
     a.ssm_norm = it->second.ssm_norm;
     a.scratch = st->prefill_lin;
+    a.err = st->d_err;
     a.seq0 = seq0;
     a.nseq = nseq;
     a.count = count;
