@@ -255,20 +255,52 @@ __global__ void __launch_bounds__(256, 2) linear_prefill_local_kernel(LocalParam
     }
     __syncthreads();
 
-    // T = (I + A)^-1 by forward substitution, one row per step:
-    // T[r][c] = delta_rc - sum_{c <= m < r} A[r][m] T[m][c]; four threads per column.
+    // T = (I + A)^-1 in 16x16 blocks (A strictly lower). The diagonal blocks
+    // T_ii = (I + A_ii)^-1 by forward substitution, one warp each; then the
+    // block sub-diagonals d = 1, 2, 3 in turn:
+    //   T_ij = -T_ii sum_{k=j}^{i-1} A_ik T_kj   (j = i - d).
+    // Q (in Xs) is no longer needed: Xs holds the block products.
     {
-        const int c = tid >> 2, part = tid & 3;
-        if (part == 0) Ts[0 * (kC + 1) + c] = (c == 0) ? 1.f : 0.f;
+        const int warp = tid >> 5, lane = tid & 31;
+        for (int idx = tid; idx < kC * (kC + 1); idx += 256) Ts[idx] = 0.f;
         __syncthreads();
-        for (int r = 1; r < kC; ++r) {
-            float acc = 0.f;
-            if (c < r) {
-                for (int m = c + part; m < r; m += 4) acc = fmaf(As[r * (kC + 1) + m], Ts[m * (kC + 1) + c], acc);
+        if (warp < 4 && lane < 16) {
+            const int b0 = warp * 16, c = lane;
+            float tcol[16];
+#pragma unroll
+            for (int r = 0; r < 16; ++r) {
+                float acc = (r == c) ? 1.f : 0.f;
+#pragma unroll
+                for (int m = 0; m < r; ++m) acc = fmaf(-As[(b0 + r) * (kC + 1) + b0 + m], tcol[m], acc);
+                tcol[r] = (r < c) ? 0.f : acc;
             }
-            acc += __shfl_xor_sync(0xffffffffu, acc, 1);
-            acc += __shfl_xor_sync(0xffffffffu, acc, 2);
-            if (part == 0) Ts[r * (kC + 1) + c] = (c < r) ? -acc : (c == r ? 1.f : 0.f);
+#pragma unroll
+            for (int r = 0; r < 16; ++r) Ts[(b0 + r) * (kC + 1) + b0 + c] = tcol[r];
+        }
+        __syncthreads();
+        for (int d = 1; d < 4; ++d) {
+            const int nblk = 4 - d;
+            for (int idx = tid; idx < nblk * 256; idx += 256) {
+                const int blk = idx >> 8, e = idx & 255, r = e >> 4, c = e & 15;
+                const int i = blk + d, j = blk;
+                float acc = 0.f;
+                for (int k = j; k < i; ++k)
+#pragma unroll
+                    for (int m = 0; m < 16; ++m)
+                        acc = fmaf(As[(16 * i + r) * (kC + 1) + 16 * k + m],
+                                   Ts[(16 * k + m) * (kC + 1) + 16 * j + c], acc);
+                Xs[idx] = acc;
+            }
+            __syncthreads();
+            for (int idx = tid; idx < nblk * 256; idx += 256) {
+                const int blk = idx >> 8, e = idx & 255, r = e >> 4, c = e & 15;
+                const int i = blk + d, j = blk;
+                float acc = 0.f;
+#pragma unroll
+                for (int m = 0; m < 16; ++m)
+                    acc = fmaf(Ts[(16 * i + r) * (kC + 1) + 16 * i + m], Xs[(blk << 8) + m * 16 + c], acc);
+                Ts[(16 * i + r) * (kC + 1) + 16 * j + c] = -acc;
+            }
             __syncthreads();
         }
     }
@@ -306,10 +338,13 @@ __global__ void __launch_bounds__(256, 2) linear_prefill_local_kernel(LocalParam
     // K~^T[i][r] = e^{gamma_C - gamma_r} K[r][i] (the state update's B operand).
     {
         float *kt = p.kt_out + ((size_t(s) * p.nchunk + chunk) * p.v_heads + h) * kD * kC;
-        const float gC = gam[kC - 1];
+        // e^{gamma_C - gamma_r}, kept in As row 0 (A is no longer needed).
+        float *dec = As;
+        if (tid < kC) dec[tid] = expf(gam[kC - 1] - gam[tid]);
+        __syncthreads();
         for (int idx = tid; idx < kD * kC; idx += 256) {
             const int i = idx / kC, r = idx % kC;
-            kt[idx] = expf(gC - gam[r]) * Ks[r * kPad + i];
+            kt[idx] = dec[r] * Ks[r * kPad + i];
         }
     }
     __syncthreads();  // Xs (Q) is no longer needed: load V
