@@ -8,31 +8,28 @@
 //                         append to the bf16 cache, key written back, and the
 //                         prepared query rounded to bf16 into the Q scratch
 //                         [seq][head][token][256].
-//   P2 attn_prefill       one CTA per (128-query tile, head, sequence),
-//                         heaviest (latest) tiles first. Warp roles:
-//                           warp 0   TMA producer: the Q tile once (staged
-//                                    in the K ring), then K and V tiles of 64
-//                                    keys into 3-deep rings (128-byte
-//                                    swizzle, no multicast);
-//                           warp 1   TMEM owner + single-thread MMA issuer:
-//                                    S = Q K^T (M=128, N=64, K=256, Q read
-//                                    from TMEM) into one of two TMEM S
-//                                    buffers, O += P V (M=128, N=256, K=64,
-//                                    V MN-major);
-//                           warps 2-5 softmax, one query row per thread:
-//                                    S from TMEM, causal mask, online max
-//                                    with lazy O rescale (only when the max
-//                                    grows by more than 2^8), P = exp2 to
-//                                    f16 in swizzled shared memory; then
-//                                    the epilogue O / l * sigmoid(gate);
-//                           warps 6-9 convert each staged V tile from bf16
-//                                    to f16 in place (same swizzled layout).
-//                           (warps 2-5 first copy their rows of the staged
-//                                    Q tile into TMEM.)
-//                         TMEM: S0 | S1 (64 columns each) | O (256) | Q (128,
-//                         bf16 pairs). Holding Q in TMEM frees 64 KB of shared
-//                         memory for deeper K/V rings and removes the per-step
-//                         re-read of Q from shared memory.
+//   P1b attn_prefill_prefix  only when base > 0: the cached prefix's V rows
+//                         (bf16) copied as f16 into the V scratch.
+//   P2 attn_prefill_pair  a cluster of two CTAs per (256-query pair of tiles,
+//                         head, sequence), heaviest pairs first; every MMA is a
+//                         cta_group::2 MMA that the leader CTA issues for both
+//                         SMs (see the kernel's comment). Warp roles per CTA:
+//                           warp 0   TMA: this CTA's Q rows once, then its half
+//                                    (32 keys) of every K tile, 4-deep ring;
+//                           warp 7   TMA: its half (128 dims) of every f16 V
+//                                    tile, 4-deep ring;
+//                           warps 1, 8  (leader) S = Q K^T of even / odd key
+//                                    tiles, M=256 N=64 K=256, Q from shared
+//                                    memory, into four TMEM S buffers;
+//                           warp 6   (leader) O += P V, M=256 N=256 K=64, P
+//                                    from TMEM (f16 over the S buffer), V
+//                                    MN-major;
+//                           warps 2-5 softmax, one query row per thread: S
+//                                    from TMEM, causal mask, online max with
+//                                    lazy O rescale (only when the max grows by
+//                                    more than 2^8), P = exp2 in f16 into TMEM;
+//                                    then the epilogue O / l * sigmoid(gate).
+//                         TMEM per CTA: S0..S3 (64 columns each) | O (256).
 //
 // Precision: S = Q K^T from bf16 Q and K (the bf16 cache); O = P V in f16
 // (P rounded to f16 has 4x less error than bf16, which matters for the first
@@ -51,16 +48,7 @@ constexpr int kBlockQ = 128;  // query rows per CTA (MMA M)
 constexpr int kBlockK = 64;   // keys per tile (QK N, PV K)
 constexpr int kThreadsPF = 288;
 constexpr uint32_t kQBytes = kBlockQ * kAttnHeadDim * 2;      // 64 KB
-constexpr uint32_t kKVBytes = kBlockK * kAttnHeadDim * 2;     // 32 KB
-constexpr uint32_t kPBytes = kBlockQ * kBlockK * 2;           // 16 KB
-constexpr int kStagesK = 3;
-constexpr int kStagesV = 3;
-constexpr uint32_t kSmemPF = (kStagesK + kStagesV) * kKVBytes + 2 * kPBytes + 1024;  // + alignment slack
-static_assert(kQBytes <= kStagesK * kKVBytes, "Q is staged in the K ring");
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kColS = 0;     // S buffers at columns 0 and 64
-constexpr uint32_t kColO = 128;   // O at columns 128..383
-constexpr uint32_t kColQ = 384;   // Q at columns 384..511 (bf16 pairs)
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 
 // --------------------------------------------------------------------------
@@ -205,12 +193,6 @@ struct PrefillParams {
     int seq0, count, base, heads, kv_heads, n_qtiles;
 };
 
-struct __align__(8) PrefillBarriers {
-    uint64_t q_full, q_copied;
-    uint64_t k_full[kStagesK], k_empty[kStagesK], v_full[kStagesV], v_empty[kStagesV];
-    uint64_t s_full[2], s_free[2], p_full[2], p_free[2], o_done, o_final;
-};
-
 __device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
     uint64_t r;
     asm("add.rn.f32x2 %0, %1, %2;"
@@ -234,57 +216,91 @@ __device__ __forceinline__ float sigmoid_fast(float x) {
     return r;
 }
 
-__global__ void __launch_bounds__(kThreadsPF, 1)
-    attn_prefill_kernel(const __grid_constant__ CUtensorMap map_q,
-                        const __grid_constant__ CUtensorMap map_k,
-                        const __grid_constant__ CUtensorMap map_v, PrefillParams p) {
+// --------------------------------------------------------------------------
+// P2 (pair form): two CTAs of a cluster share every MMA (cta_group::2).
+// --------------------------------------------------------------------------
+// The pair covers 256 query rows of one (head, sequence): the leader (rank 0)
+// rows q0..q0+127, the peer rows q0+128..q0+255, each in its own TMEM lanes.
+// One S = Q K^T instruction (M=256, N=64, Q from shared memory) and one
+// O += P V instruction (M=256, N=256, P from TMEM) serve both SMs, so each
+// SM pays half the per-instruction issue cost and stages only half of every
+// K tile (32 keys) and half of every V tile (128 dims). With Q in shared
+// memory, TMEM holds four S buffers next to O, so four QK tiles can be in
+// flight; P(j) is written over the first 32 columns of S buffer j % 4, which
+// is free again once PV(j) has completed. The leader's warps 1, 8 (QK) and 6
+// (PV) issue all MMAs; both CTAs load, run the softmax and write their rows.
+constexpr int kPairRows = 2 * kBlockQ;
+constexpr int kPairSBuf = 4;
+constexpr uint32_t kKHalf = (kBlockK / 2) * kAttnHeadDim * 2;  // 16 KB: 32 keys x 256 dims
+constexpr uint32_t kVHalf = kBlockK * (kAttnHeadDim / 2) * 2;  // 16 KB: 64 keys x 128 dims
+constexpr int kPairStagesK = 4;
+constexpr int kPairStagesV = 4;
+constexpr uint32_t kSmemPair = kQBytes + kPairStagesK * kKHalf + kPairStagesV * kVHalf + 1024;
+constexpr uint32_t kPairColO = kPairSBuf * kBlockK;  // 256: O after the four S buffers
+
+struct __align__(8) PairBarriers {
+    uint64_t q_full;
+    uint64_t k_full[kPairStagesK], k_empty[kPairStagesK], v_full[kPairStagesV], v_empty[kPairStagesV];
+    uint64_t s_full[kPairSBuf], p_full[kPairSBuf], s_free[kPairSBuf], o_final;
+};
+
+// Arrival on a barrier of the leader CTA (cluster address), ordered like the
+// local tcgen05 handshakes (tcgen05.wait + fence::before_thread_sync first).
+__device__ __forceinline__ void mbar_arrive_leader(uint32_t cluster_bar) {
+    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
+}
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsPF, 1)
+    attn_prefill_pair_kernel(const __grid_constant__ CUtensorMap map_q,
+                             const __grid_constant__ CUtensorMap map_k,
+                             const __grid_constant__ CUtensorMap map_v, PrefillParams p) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char *smem =
         reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    unsigned char *sK = smem;                      // kStagesK stages (Q staged here first)
-    unsigned char *sV = sK + kStagesK * kKVBytes;  // kStagesV stages (f16)
-    unsigned char *sP = sV + kStagesV * kKVBytes;  // 2 buffers (f16, K-major SW128)
-    __shared__ PrefillBarriers bar;
+    unsigned char *sQ = smem;                          // this CTA's 128 query rows (bf16)
+    unsigned char *sK = sQ + kQBytes;                  // kPairStagesK half tiles
+    unsigned char *sV = sK + kPairStagesK * kKHalf;    // kPairStagesV half tiles (f16)
+    __shared__ PairBarriers bar;
     __shared__ uint32_t tmem_base_s;
     __shared__ volatile int abort_flag;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int qt = p.n_qtiles - 1 - int(blockIdx.x);  // latest (heaviest) tiles first
+    const uint32_t rank = cluster_ctarank();
+    const bool leader = rank == 0;
+    const int n_pairs = (p.n_qtiles + 1) / 2;
+    const int pair = n_pairs - 1 - int(blockIdx.x >> 1);  // latest (heaviest) pairs first
     const int h = blockIdx.y, s = blockIdx.z;
     const int kvh = h / kGroup;
-    const int q0 = qt * kBlockQ;
-    const int q_rows = min(kBlockQ, p.count - q0);
-    const int kend = p.base + q0 + q_rows;  // keys [0, kend) are visible to some row
+    const int q0 = pair * kPairRows + int(rank) * kBlockQ;
+    const int q_rows = min(kBlockQ, p.count - q0);        // may be <= 0 for the peer
+    const int kend = p.base + min(pair * kPairRows + kPairRows, p.count);
     const int nkt = (kend + kBlockK - 1) / kBlockK;
 
     if (threadIdx.x == 0) {
         abort_flag = 0;
         mbar_init(&bar.q_full, 1);
-        mbar_init(&bar.q_copied, 128);
-        for (int b = 0; b < kStagesK; ++b) {
+        for (int b = 0; b < kPairStagesK; ++b) {
             mbar_init(&bar.k_full[b], 1);
             mbar_init(&bar.k_empty[b], 1);
         }
-        for (int b = 0; b < kStagesV; ++b) {
+        for (int b = 0; b < kPairStagesV; ++b) {
             mbar_init(&bar.v_full[b], 1);
             mbar_init(&bar.v_empty[b], 1);
         }
-        for (int b = 0; b < 2; ++b) {
+        for (int b = 0; b < kPairSBuf; ++b) {
             mbar_init(&bar.s_full[b], 1);
-            mbar_init(&bar.s_free[b], 128);
-            mbar_init(&bar.p_full[b], 128);
-            mbar_init(&bar.p_free[b], 1);
+            mbar_init(&bar.p_full[b], 2 * 4);  // one arrival per softmax warp of each CTA
+            mbar_init(&bar.s_free[b], 1);
         }
-        mbar_init(&bar.o_done, 1);
         mbar_init(&bar.o_final, 1);
         fence_barrier_init();
     }
     if (warp == 1) {
-        tmem_alloc(&tmem_base_s, kTmemCols);
-        tmem_relinquish();
+        tmem_alloc_pair(&tmem_base_s, kTmemCols);
+        tmem_relinquish_pair();
     }
     fence_before_sync();
-    __syncthreads();
+    cluster_sync();  // barriers of both CTAs initialised before any remote use
     fence_after_sync();
     const uint32_t tmem = tmem_base_s;
 
@@ -294,169 +310,140 @@ __global__ void __launch_bounds__(kThreadsPF, 1)
     };
 
     if (warp == 0) {
-        // ------------------------------------------------------------ Q, K producer
+        // ------------------------------------------------------------ Q, K-half producer
         if (lane == 0) {
             tma_prefetch_desc(&map_q);
             tma_prefetch_desc(&map_k);
             pdl_wait_primary();  // P1 wrote the Q scratch and the new K/V rows
-            const int qrow = s * p.heads + h;  // Q scratch plane
+            const int qrow = s * p.heads + h;
             const int kplane = (p.seq0 + s) * p.kv_heads + kvh;
-            mbar_arrive_expect_tx(&bar.q_full, kQBytes);
+            if (leader) mbar_arrive_expect_tx(&bar.q_full, 2 * kQBytes);
+            const uint32_t qfull = cluster_addr(&bar.q_full, 0);
             for (int cb = 0; cb < 4; ++cb)
-                tma_load_3d(sK + cb * (kQBytes / 4), &map_q, cb * 64, q0, qrow, &bar.q_full);
-            // The K ring holds the staged Q until the softmax warps copied it to TMEM.
-            if (!mbar_wait(&bar.q_copied, 0)) fail();
+                tma_load_3d_pair(sQ + cb * (kQBytes / 4), &map_q, cb * 64, q0, qrow, qfull);
             for (int j = 0; j < nkt && !abort_flag; ++j) {
-                const int b = j % kStagesK;
-                if (j >= kStagesK &&
-                    !mbar_wait(&bar.k_empty[b], uint32_t(j / kStagesK - 1) & 1u)) {
+                const int b = j % kPairStagesK;
+                if (j >= kPairStagesK &&
+                    !mbar_wait(&bar.k_empty[b], uint32_t(j / kPairStagesK - 1) & 1u)) {
                     fail();
                     break;
                 }
-                mbar_arrive_expect_tx(&bar.k_full[b], kKVBytes);
+                if (leader) mbar_arrive_expect_tx(&bar.k_full[b], 2 * kKHalf);
+                const uint32_t full = cluster_addr(&bar.k_full[b], 0);
                 for (int cb = 0; cb < 4; ++cb)
-                    tma_load_3d(sK + b * kKVBytes + cb * (kKVBytes / 4), &map_k, cb * 64,
-                                j * kBlockK, kplane, &bar.k_full[b]);
+                    tma_load_3d_pair(sK + b * kKHalf + cb * (kKHalf / 4), &map_k, cb * 64,
+                                     j * kBlockK + int(rank) * (kBlockK / 2), kplane, full);
             }
         }
     } else if (warp == 7) {
-        // ------------------------------------------------------------ V producer (f16)
+        // ------------------------------------------------------------ V-half producer (f16)
         if (lane == 0) {
             tma_prefetch_desc(&map_v);
             pdl_wait_primary();
             const int vplane = s * p.kv_heads + kvh;
             for (int j = 0; j < nkt && !abort_flag; ++j) {
-                const int b = j % kStagesV;
-                if (j >= kStagesV &&
-                    !mbar_wait(&bar.v_empty[b], uint32_t(j / kStagesV - 1) & 1u)) {
+                const int b = j % kPairStagesV;
+                if (j >= kPairStagesV &&
+                    !mbar_wait(&bar.v_empty[b], uint32_t(j / kPairStagesV - 1) & 1u)) {
                     fail();
                     break;
                 }
-                mbar_arrive_expect_tx(&bar.v_full[b], kKVBytes);
-                for (int cb = 0; cb < 4; ++cb)
-                    tma_load_3d(sV + b * kKVBytes + cb * (kKVBytes / 4), &map_v, cb * 64,
-                                j * kBlockK, vplane, &bar.v_full[b]);
+                if (leader) mbar_arrive_expect_tx(&bar.v_full[b], 2 * kVHalf);
+                const uint32_t full = cluster_addr(&bar.v_full[b], 0);
+                for (int cb = 0; cb < 2; ++cb)
+                    tma_load_3d_pair(sV + b * kVHalf + cb * (kVHalf / 2), &map_v,
+                                     int(rank) * (kAttnHeadDim / 2) + cb * 64, j * kBlockK, vplane,
+                                     full);
             }
         }
     } else if (warp == 1 || warp == 8) {
-        // ------------------------------------------------------------ S = Q K^T issuers
+        // ------------------------------------------------------------ S = Q K^T issuers (leader)
         // A thread issuing tcgen05.mma waits ~100 cycles per instruction, so
-        // QK of even tiles (warp 1), QK of odd tiles (warp 8) and PV (warp 6)
-        // are three issuers whose streams overlap in the tensor pipe.
-        if (lane == 0) {
-            const uint32_t id_qk = idesc_bf16_f32(kBlockQ, kBlockK, 0, 0);
-            const uint32_t sk = smem_addr(sK);
-            bool ok = mbar_wait(&bar.q_copied, 0);
+        // even and odd tiles are issued from two warps.
+        if (leader && lane == 0) {
+            const uint32_t id_qk = idesc_bf16_f32(kPairRows, kBlockK, 0, 0);
+            const uint32_t sq = smem_addr(sQ), sk = smem_addr(sK);
+            bool ok = mbar_wait(&bar.q_full, 0);
             for (int j = warp == 1 ? 0 : 1; ok && j < nkt; j += 2) {
-                const int b = j & 1, kb = j % kStagesK;
-                if (!mbar_wait(&bar.k_full[kb], uint32_t(j / kStagesK) & 1u)) { ok = false; break; }
-                // S buffer b is free once the softmax warps have read S(j-2).
-                if (j >= 2 && !mbar_wait(&bar.s_free[b], uint32_t((j - 2) >> 1) & 1u)) {
+                const int b = j % kPairSBuf, kb = j % kPairStagesK;
+                if (!mbar_wait(&bar.k_full[kb], uint32_t(j / kPairStagesK) & 1u)) { ok = false; break; }
+                // S buffer b held S and P of tile j-4 until PV(j-4) completed.
+                if (j >= kPairSBuf && !mbar_wait(&bar.s_free[b], uint32_t(j / kPairSBuf - 1) & 1u)) {
                     ok = false;
                     break;
                 }
                 fence_after_sync();
 #pragma unroll
                 for (int kk = 0; kk < kAttnHeadDim / 16; ++kk) {
+                    const uint32_t off = (kk >> 2) * (kQBytes / 4) + (kk & 3) * 32;
+                    const uint64_t ad = smem_desc_sw128(sq + off, 16, 1024);
                     const uint64_t bd = smem_desc_sw128(
-                        sk + kb * kKVBytes + (kk >> 2) * (kKVBytes / 4) + (kk & 3) * 32, 16, 1024);
-                    mma_f16_ta(tmem + kColS + b * kBlockK, tmem + kColQ + kk * 8, bd, id_qk,
-                               kk > 0 ? 1u : 0u);
+                        sk + kb * kKHalf + (kk >> 2) * (kKHalf / 4) + (kk & 3) * 32, 16, 1024);
+                    mma_pair_ss(tmem + b * kBlockK, ad, bd, id_qk, kk > 0 ? 1u : 0u);
                 }
-                mma_commit(&bar.s_full[b]);
-                mma_commit(&bar.k_empty[kb]);
+                mma_commit_pair(&bar.s_full[b]);
+                mma_commit_pair(&bar.k_empty[kb]);
                 if (abort_flag) { ok = false; break; }
             }
             if (!ok) fail();
         }
     } else if (warp == 6) {
-        // ------------------------------------------------------------ O += P V issuer
-        if (lane == 0) {
-            const uint32_t id_pv = idesc_f16_f32(kBlockQ, kAttnHeadDim, 0, 1, false);
-            const uint32_t sv = smem_addr(sV), sp = smem_addr(sP);
+        // ------------------------------------------------------------ O += P V issuer (leader)
+        if (leader && lane == 0) {
+            const uint32_t id_pv = idesc_f16_f32(kPairRows, kAttnHeadDim, 0, 1, false);
+            const uint32_t sv = smem_addr(sV);
             bool ok = true;
             for (int j = 0; j < nkt; ++j) {
-                const int b = j & 1, vb = j % kStagesV;
-                if (!mbar_wait(&bar.p_full[b], uint32_t(j >> 1) & 1u)) { ok = false; break; }
-                if (!mbar_wait(&bar.v_full[vb], uint32_t(j / kStagesV) & 1u)) { ok = false; break; }
+                const int b = j % kPairSBuf, vb = j % kPairStagesV;
+                if (!mbar_wait(&bar.p_full[b], uint32_t(j / kPairSBuf) & 1u)) { ok = false; break; }
+                if (!mbar_wait(&bar.v_full[vb], uint32_t(j / kPairStagesV) & 1u)) { ok = false; break; }
                 fence_after_sync();
 #pragma unroll
                 for (int kk = 0; kk < kBlockK / 16; ++kk) {
-                    const uint64_t ad = smem_desc_sw128(sp + b * kPBytes + kk * 32, 16, 1024);
                     const uint64_t bd =
-                        smem_desc_sw128(sv + vb * kKVBytes + kk * 2048, kKVBytes / 4, 1024);
-                    mma_bf16(tmem + kColO, ad, bd, id_pv, (j > 0 || kk > 0) ? 1u : 0u);
+                        smem_desc_sw128(sv + vb * kVHalf + kk * 2048, kVHalf / 2, 1024);
+                    // P(j): f16 pairs in the first 32 columns of S buffer b.
+                    mma_pair_ta(tmem + kPairColO, tmem + b * kBlockK + kk * 8, bd, id_pv,
+                                (j > 0 || kk > 0) ? 1u : 0u);
                 }
-                mma_commit(&bar.v_empty[vb]);
-                mma_commit(&bar.p_free[b]);
-                mma_commit(&bar.o_done);
+                mma_commit_pair(&bar.v_empty[vb]);
+                mma_commit_pair(&bar.s_free[b]);
                 if (abort_flag) { ok = false; break; }
             }
-            // One completion for the epilogue: by the time the softmax warps
-            // wait, both of the last two PVs may have completed, which a parity
-            // wait on o_done cannot tell from "neither has".
-            if (ok) mma_commit(&bar.o_final);
+            // One completion for the epilogue, after the last PV.
+            if (ok) mma_commit_pair(&bar.o_final);
             if (!ok) fail();
         }
     } else {
-        // ------------------------------------------------------------ softmax
-        // tcgen05.ld/st are warp-collective: every decision that guards one
-        // (rescale, timeout exits) is made uniform across the warp.
-        const int sub = warp & 3;                 // TMEM lane quarter of this warp
-        const int r = sub * 32 + lane;            // query row within the tile
+        // ------------------------------------------------------------ softmax (both CTAs)
+        // tcgen05.ld/st are warp-collective: every decision that guards one is
+        // made uniform across the warp.
+        const int sub = warp & 3;
+        const int r = sub * 32 + lane;
         const uint32_t lane_addr = uint32_t(sub * 32) << 16;
-        const int t = q0 + r;                     // token index
+        const int t = q0 + r;
         const int qpos = p.base + min(t, p.count - 1);  // rows past the end mirror the last
-        const int qpos_first = p.base + q0;              // smallest position in the tile
+        const int qpos_first = p.base + min(q0, p.count - 1);
         const float sl2 = 1.4426950408889634f / 16.0f;  // log2(e) * score_scale
         float m = -INFINITY, l = 0.f;
         bool ok = true;
         auto wait_all = [&](uint64_t *b, uint32_t parity) {
             return __all_sync(0xffffffffu, mbar_wait(b, parity));
         };
-        // Copy this thread's row of the staged Q tile (four 64-column SW128
-        // blocks in the K ring) into TMEM columns kColQ.., two bf16 per column.
-        if (!wait_all(&bar.q_full, 0)) {
-            ok = false;
-        } else {
-#pragma unroll 1
-            for (int cb = 0; cb < 4; ++cb) {
-                uint32_t w[32];
-#pragma unroll
-                for (int ch = 0; ch < 8; ++ch) {
-                    const uint4 v = *reinterpret_cast<const uint4 *>(
-                        sK + cb * (kQBytes / 4) + r * 128 + ((ch ^ (r & 7)) * 16));
-                    w[ch * 4 + 0] = v.x;
-                    w[ch * 4 + 1] = v.y;
-                    w[ch * 4 + 2] = v.z;
-                    w[ch * 4 + 3] = v.w;
-                }
-                tmem_st32(tmem + lane_addr + kColQ + cb * 32, w);
-            }
-            tmem_wait_st();
-        }
-        fence_before_sync();
-        mbar_arrive(&bar.q_copied);
         for (int j = 0; ok && j < nkt; ++j) {
-            const int b = j & 1;
-            if (!wait_all(&bar.s_full[b], (j >> 1) & 1)) { ok = false; break; }
+            const int b = j % kPairSBuf;
+            if (!wait_all(&bar.s_full[b], uint32_t(j / kPairSBuf) & 1u)) { ok = false; break; }
             fence_after_sync();
             uint32_t sr[2][32];
-            tmem_ld32(tmem + lane_addr + kColS + b * kBlockK, sr[0]);
-            tmem_ld32(tmem + lane_addr + kColS + b * kBlockK + 32, sr[1]);
+            tmem_ld32(tmem + lane_addr + b * kBlockK, sr[0]);
+            tmem_ld32(tmem + lane_addr + b * kBlockK + 32, sr[1]);
             tmem_wait_ld();
-            // S(j) is in registers: QK(j+2) may overwrite buffer b.
-            fence_before_sync();
-            mbar_arrive(&bar.s_free[b]);
             float sv[kBlockK];
             const int key0 = j * kBlockK;
-            // Row max of the raw scores (scaling by sl2 > 0 keeps the order),
-            // in 8 independent chains.
             float mx8[8];
 #pragma unroll
             for (int i = 0; i < 8; ++i) mx8[i] = -INFINITY;
             if (key0 + kBlockK - 1 <= qpos_first) {
-                // Tile fully visible to every row of this CTA: no mask.
 #pragma unroll
                 for (int c = 0; c < kBlockK; ++c) {
                     sv[c] = __uint_as_float(sr[c >> 5][c & 31]);
@@ -473,65 +460,56 @@ __global__ void __launch_bounds__(kThreadsPF, 1)
             const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
                                    fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
             const float m_new = fmaxf(m, mx * sl2);
-            // P buffer b held P(j-2): wait until PV(j-2) has read it. After
-            // this, o_done has completed j-1 or j phases (PV(j) needs this
-            // tile's P), so the rescale's parity wait below is exact.
-            if (j >= 2 && !wait_all(&bar.p_free[b], uint32_t((j - 2) >> 1) & 1u)) {
-                ok = false;
-                break;
-            }
             if (__any_sync(0xffffffffu, m_new > m + kRescaleThreshold)) {
-                // Every row of the warp moves to its exact max (corr = 1 where
-                // the max did not change); O and l are scaled by the same factor.
                 const float corr = ex2(m - m_new);  // 0 on the first tile
                 if (j > 0) {
-                    // O holds PV(0..j-1): wait for PV(j-1), then rescale the rows.
-                    if (!wait_all(&bar.o_done, (j - 1) & 1)) { ok = false; break; }
+                    // O holds PV(0..j-1). PV(j-1) completing is phase (j-1)/4 of
+                    // s_free[(j-1)%4]; that barrier is at most one phase behind
+                    // (QK(j-1) needed PV(j-5)) and cannot be ahead (PV(j+3) needs
+                    // P(j+3)), so the parity wait is exact. PVs complete in order.
+                    const int jp = j - 1;
+                    if (!wait_all(&bar.s_free[jp % kPairSBuf], uint32_t(jp / kPairSBuf) & 1u)) {
+                        ok = false;
+                        break;
+                    }
                     fence_after_sync();
 #pragma unroll 1
                     for (int c = 0; c < kAttnHeadDim; c += 32) {
                         uint32_t o[32];
-                        tmem_ld32(tmem + lane_addr + kColO + c, o);
+                        tmem_ld32(tmem + lane_addr + kPairColO + c, o);
                         tmem_wait_ld();
 #pragma unroll
                         for (int i = 0; i < 32; ++i)
                             o[i] = __float_as_uint(__uint_as_float(o[i]) * corr);
-                        tmem_st32(tmem + lane_addr + kColO + c, o);
+                        tmem_st32(tmem + lane_addr + kPairColO + c, o);
                     }
                 }
                 l *= corr;
                 m = m_new;
             }
-            // P = 2^(s*sl2 - m) as f16 into the swizzled K-major tile of P
-            // buffer b. Masked scores are -inf and give exactly 0.
-            unsigned char *prow = sP + b * kPBytes;
+            // P = 2^(s*sl2 - m) as f16 pairs over the first 32 columns of S
+            // buffer b (S is in registers now). Masked scores give exactly 0.
+            uint32_t pw[32];
             float2 ps2[4];
 #pragma unroll
             for (int i = 0; i < 4; ++i) ps2[i] = make_float2(0.f, 0.f);
             const float2 scale2 = make_float2(sl2, sl2), negm2 = make_float2(-m, -m);
 #pragma unroll
-            for (int ch = 0; ch < kBlockK / 8; ++ch) {
-                uint32_t w[4];
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const int c = ch * 8 + 2 * e;
-                    const float2 x = ffma2(make_float2(sv[c], sv[c + 1]), scale2, negm2);
-                    const float2 pr = make_float2(ex2(x.x), ex2(x.y));
-                    ps2[e] = fadd2(ps2[e], pr);
-                    w[e] = pack_f16x2(pr.x, pr.y);
-                }
-                const uint32_t off = uint32_t(r) * 128u + ((uint32_t(ch) ^ (uint32_t(r) & 7u)) * 16u);
-                *reinterpret_cast<uint4 *>(prow + off) = make_uint4(w[0], w[1], w[2], w[3]);
+            for (int c = 0; c < kBlockK / 2; ++c) {
+                const float2 x = ffma2(make_float2(sv[2 * c], sv[2 * c + 1]), scale2, negm2);
+                const float2 pr = make_float2(ex2(x.x), ex2(x.y));
+                ps2[c & 3] = fadd2(ps2[c & 3], pr);
+                pw[c] = pack_f16x2(pr.x, pr.y);
             }
+            tmem_st32(tmem + lane_addr + b * kBlockK, pw);
             l += ((ps2[0].x + ps2[0].y) + (ps2[1].x + ps2[1].y)) +
                  ((ps2[2].x + ps2[2].y) + (ps2[3].x + ps2[3].y));
-            fence_proxy_async_smem();
             tmem_wait_st();
             fence_before_sync();
-            mbar_arrive(&bar.p_full[b]);
+            __syncwarp();
+            if (lane == 0) mbar_arrive_leader(cluster_addr(&bar.p_full[b], 0));
             if (__any_sync(0xffffffffu, abort_flag != 0)) { ok = false; break; }
         }
-        // The epilogue waits on o_final, committed once after the last PV.
         if (ok && !wait_all(&bar.o_final, 0)) ok = false;
         if (ok) {
             fence_after_sync();
@@ -543,7 +521,7 @@ __global__ void __launch_bounds__(kThreadsPF, 1)
 #pragma unroll 1
             for (int c = 0; c < kAttnHeadDim; c += 32) {
                 uint32_t o[32];
-                tmem_ld32(tmem + lane_addr + kColO + c, o);
+                tmem_ld32(tmem + lane_addr + kPairColO + c, o);
                 tmem_wait_ld();
                 if (store) {
 #pragma unroll
@@ -564,9 +542,9 @@ __global__ void __launch_bounds__(kThreadsPF, 1)
     }
 
     fence_before_sync();
-    __syncthreads();
+    cluster_sync();  // no CTA leaves while the pair's MMAs may use its memory
     fence_after_sync();
-    if (warp == 1) tmem_dealloc(tmem, kTmemCols);
+    if (warp == 1) tmem_dealloc_pair(tmem, kTmemCols);
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_tiled() {
@@ -617,28 +595,29 @@ cudaError_t launch_attn_prefill(const AttnPrefillLaunch &a, cudaStream_t stream)
     if (!make_map_16(&mq, a.qp, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, uint64_t(a.count),
                      uint64_t(a.nseq) * a.heads, kBlockQ) ||
         !make_map_16(&mk, a.kcache, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, uint64_t(a.context_length),
-                     uint64_t(a.batch) * a.kv_heads, kBlockK) ||
+                     uint64_t(a.batch) * a.kv_heads, kBlockK / 2) ||
         !make_map_16(&mv, a.v16, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, uint64_t(a.context_length),
                      uint64_t(a.nseq) * a.kv_heads, kBlockK))
         return cudaErrorInvalidValue;
 
     const int n_qtiles = (a.count + kBlockQ - 1) / kBlockQ;
+    const int n_pairs = (n_qtiles + 1) / 2;
     PrefillParams p{a.q_and_gate, a.attention, a.err, a.seq0, a.count, a.base, a.heads,
                     a.kv_heads, n_qtiles};
-    e = cudaFuncSetAttribute(attn_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             int(kSmemPF));
+    e = cudaFuncSetAttribute(attn_prefill_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             int(kSmemPair));
     if (e != cudaSuccess) return e;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cudaLaunchConfig_t cfg{};
-    cfg.gridDim = dim3(n_qtiles, a.heads, a.nseq);
+    cfg.gridDim = dim3(2 * n_pairs, a.heads, a.nseq);
     cfg.blockDim = dim3(kThreadsPF);
-    cfg.dynamicSmemBytes = kSmemPF;
+    cfg.dynamicSmemBytes = kSmemPair;
     cfg.stream = stream;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, attn_prefill_kernel, mq, mk, mv, p);
+    return cudaLaunchKernelEx(&cfg, attn_prefill_pair_kernel, mq, mk, mv, p);
 }
 
 }  // namespace q38
