@@ -24,19 +24,20 @@
 //                            new conv state.
 //   L2 linear_prefill_norm   one CTA per (token, sequence): L2-norm of the q and
 //                            k heads (f64 sums) and the beta/alpha gates, in place.
-//   L3 linear_prefill_local  one CTA per (chunk, value head, sequence): the
-//                            chunk-local W, Ut, P and gamma (all chunks in
-//                            parallel).
-//   L4 linear_prefill_state  one CTA per (32-row slice, value head, sequence):
-//                            walks the chunks in order, carrying its state
-//                            slice in shared memory; writes O (scaled by
+//   L3 linear_prefill_local  one CTA per (chunk, key head, sequence): K K^T and
+//                            Q K^T once, then per value head of that key head
+//                            the chunk-local W, Ut, P, K~ and e^gamma (all
+//                            chunks in parallel).
+//   L4 linear_prefill_state  one CTA per (value head, sequence): walks the
+//                            chunks in order with the head's state resident
+//                            in TMEM; all products on tcgen05 (kind::tf32 with
+//                            a hi/lo operand split); writes O (scaled by
 //                            1/sqrt(128)) and the final state.
 //   L5 linear_prefill_out    one CTA per (token, sequence): per-head RMSNorm
 //                            with ssm_norm and the SiLU(z) gate (ops.rs:735-740).
 //
-// Everything is f32 on the CUDA cores (register-tiled products from shared
-// memory), so the chunked result stays within f32 rounding of the per-token
-// recurrence.
+// L1-L3 and L5 are f32 CUDA-core kernels; L4's split-tf32 products keep the
+// chunked result within f32 rounding of the per-token recurrence.
 #include "q38_sm100.cuh"
 
 #include <cudaTypedefs.h>
@@ -168,17 +169,21 @@ struct LocalParams {
 
 constexpr int kPad = kD + 1;  // padded smem rows (bank-conflict-free column walks)
 
+// One CTA per (chunk, key head, sequence). The value heads h with
+// h % qk_heads == kh (ops.rs:699) share the chunk's K and Q, so K K^T and
+// Q K^T are computed once (held in registers, 4x4 per thread) and reused for
+// each of them; per value head only the decay/beta scaling, the triangular
+// solve and the two products with T differ.
 __global__ void __launch_bounds__(256, 2) linear_prefill_local_kernel(LocalParams p) {
     extern __shared__ float sm[];
     float *Ks = sm;                  // [64][129]
-    float *Xs = Ks + kC * kPad;      // [64][129]  Q, then V
+    float *Xs = Ks + kC * kPad;      // [64][129]  Q, then V of each head
     float *As = Xs + kC * kPad;      // [64][65]
     float *Ts = As + kC * (kC + 1);  // [64][65]
-    __shared__ float gam[kC], bet[kC], egs[kC];
+    __shared__ float gam[kC], bet[kC], egs[kC], dec[kC];
 
-    const int chunk = blockIdx.x, h = blockIdx.y, s = blockIdx.z;
-    const int tid = threadIdx.x;
-    const int kh = h % p.qk_heads;  // ops.rs:699
+    const int chunk = blockIdx.x, kh = blockIdx.y, s = blockIdx.z;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int t0 = chunk * kC;
     const int qk_dim = p.qk_heads * kD;
 
@@ -196,35 +201,13 @@ __global__ void __launch_bounds__(256, 2) linear_prefill_local_kernel(LocalParam
         kd[0] = k.x; kd[1] = k.y; kd[2] = k.z; kd[3] = k.w;
         qd[0] = q.x; qd[1] = q.y; qd[2] = q.z; qd[3] = q.w;
     }
-    if (tid < kC) {
-        const bool in = t0 + tid < p.count;
-        const size_t gi = (size_t(s) * p.count + t0 + tid) * p.v_heads + h;
-        bet[tid] = in ? p.beta[gi] : 0.f;
-        gam[tid] = in ? p.alpha[gi] : 0.f;
-    }
     __syncthreads();
-    if (tid < 32) {
-        // Inclusive prefix sum of g over the 64 tokens (two per lane).
-        float a = gam[2 * tid], b = gam[2 * tid + 1];
-        b += a;
-        float run = b;
-#pragma unroll
-        for (int off = 1; off < 32; off <<= 1) {
-            const float n = __shfl_up_sync(0xffffffffu, run, off);
-            if (tid >= off) run += n;
-        }
-        const float prev = run - b;
-        gam[2 * tid] = prev + a;
-        gam[2 * tid + 1] = run;
-    }
-    __syncthreads();
-    if (tid < kC) egs[tid] = expf(gam[tid]);
 
-    // K K^T -> A (scaled, strictly lower) and Q K^T -> P (decayed, lower).
-    // Thread (ty, tx) of a 16x16 grid owns rows 4ty.., columns 4tx...
-    {
-        const int ty = tid / 16, tx = tid % 16;
-        float akk[4][4] = {}, aqk[4][4] = {};
+    // K K^T and Q K^T: thread (ty, tx) of a 16x16 grid owns rows 4ty..,
+    // columns 4tx.. of both.
+    const int ty = tid / 16, tx = tid % 16;
+    float akk[4][4] = {}, aqk[4][4] = {};
+    if (tx <= ty) {  // only the lower triangle (c <= r) is used
 #pragma unroll 4
         for (int i = 0; i < kD; ++i) {
             float kr[4], qr[4], kc[4];
@@ -242,26 +225,58 @@ __global__ void __launch_bounds__(256, 2) linear_prefill_local_kernel(LocalParam
                     aqk[a][b] = fmaf(qr[a], kc[b], aqk[a][b]);
                 }
         }
-        float *pout = p.p_out + ((size_t(s) * p.nchunk + chunk) * p.v_heads + h) * kC * kC;
-#pragma unroll
-        for (int a = 0; a < 4; ++a)
-#pragma unroll
-            for (int b = 0; b < 4; ++b) {
-                const int r = 4 * ty + a, c = 4 * tx + b;
-                const float dec = expf(gam[r] - gam[c]);
-                As[r * (kC + 1) + c] = c < r ? bet[r] * dec * akk[a][b] : 0.f;
-                pout[r * kC + c] = c <= r ? dec * aqk[a][b] : 0.f;
-            }
     }
-    __syncthreads();
 
-    // T = (I + A)^-1 in 16x16 blocks (A strictly lower). The diagonal blocks
-    // T_ii = (I + A_ii)^-1 by forward substitution, one warp each; then the
-    // block sub-diagonals d = 1, 2, 3 in turn:
-    //   T_ij = -T_ii sum_{k=j}^{i-1} A_ik T_kj   (j = i - d).
-    // Q (in Xs) is no longer needed: Xs holds the block products.
-    {
-        const int warp = tid >> 5, lane = tid & 31;
+    for (int h = kh; h < p.v_heads; h += p.qk_heads) {
+        const size_t plane = (size_t(s) * p.nchunk + chunk) * p.v_heads + h;
+        __syncthreads();  // previous head done with gam/bet/As/Ts/Xs
+        if (tid < kC) {
+            const bool in = t0 + tid < p.count;
+            const size_t gi = (size_t(s) * p.count + t0 + tid) * p.v_heads + h;
+            bet[tid] = in ? p.beta[gi] : 0.f;
+            gam[tid] = in ? p.alpha[gi] : 0.f;
+        }
+        __syncthreads();
+        if (tid < 32) {
+            // Inclusive prefix sum of g over the 64 tokens (two per lane).
+            float a = gam[2 * tid], b = gam[2 * tid + 1];
+            b += a;
+            float run = b;
+#pragma unroll
+            for (int off = 1; off < 32; off <<= 1) {
+                const float n = __shfl_up_sync(0xffffffffu, run, off);
+                if (tid >= off) run += n;
+            }
+            const float prev = run - b;
+            gam[2 * tid] = prev + a;
+            gam[2 * tid + 1] = run;
+        }
+        __syncthreads();
+        if (tid < kC) {
+            egs[tid] = expf(gam[tid]);
+            dec[tid] = expf(gam[kC - 1] - gam[tid]);
+        }
+        // A = beta_r e^{gamma_r - gamma_s} K K^T (strictly lower) and
+        // P = e^{gamma_r - gamma_s} Q K^T (lower) for this head.
+        {
+            float *pout = p.p_out + plane * kC * kC;
+#pragma unroll
+            for (int a = 0; a < 4; ++a)
+#pragma unroll
+                for (int b = 0; b < 4; ++b) {
+                    const int r = 4 * ty + a, c = 4 * tx + b;
+                    const float d = (c <= r) ? expf(gam[r] - gam[c]) : 0.f;
+                    As[r * (kC + 1) + c] = c < r ? bet[r] * d * akk[a][b] : 0.f;
+                    pout[r * kC + c] = c <= r ? d * aqk[a][b] : 0.f;
+                }
+        }
+        __syncthreads();
+
+        // T = (I + A)^-1 in 16x16 blocks (A strictly lower). The diagonal
+        // blocks T_ii = (I + A_ii)^-1 by forward substitution, one warp each;
+        // then the block sub-diagonals d = 1, 2, 3 in turn:
+        //   T_ij = -T_ii sum_{k=j}^{i-1} A_ik T_kj   (j = i - d).
+        // The block products go to Xs (free until V is loaded).
         for (int idx = tid; idx < kC * (kC + 1); idx += 256) Ts[idx] = 0.f;
         __syncthreads();
         if (warp < 4 && lane < 16) {
@@ -303,65 +318,56 @@ __global__ void __launch_bounds__(256, 2) linear_prefill_local_kernel(LocalParam
             }
             __syncthreads();
         }
-    }
 
-    // W = T diag(beta e^gamma) K and Ut = T diag(beta) V. Thread: 8 rows x 4 columns.
-    const size_t wbase = ((size_t(s) * p.nchunk + chunk) * p.v_heads + h) * kC * kD;
-    const int rb = tid / 32, cg = tid % 32;
-    auto tri_times = [&](const float *X, const float *scale_a, const float *scale_b,
-                         float *out, bool round_tf32) {
-        float acc[8][4] = {};
+        // W = T diag(beta e^gamma) K and Ut = T diag(beta) V. Thread: 8 rows
+        // x 4 columns; T is lower triangular, so rows rb*8.. stop at m < rb*8+8.
+        const size_t wbase = plane * kC * kD;
+        const int rb = tid / 32, cg = tid % 32;
+        auto tri_times = [&](const float *X, const float *scale_b, float *out) {
+            float acc[8][4] = {};
+            const int mend = rb * 8 + 8;
 #pragma unroll 4
-        for (int m = 0; m < kC; ++m) {
-            const float f = scale_a[m] * (scale_b ? scale_b[m] : 1.f);
-            float x[4];
+            for (int m = 0; m < mend; ++m) {
+                const float f = bet[m] * (scale_b ? scale_b[m] : 1.f);
+                float x[4];
 #pragma unroll
-            for (int b = 0; b < 4; ++b) x[b] = X[m * kPad + cg * 4 + b] * f;
+                for (int b = 0; b < 4; ++b) x[b] = X[m * kPad + cg * 4 + b] * f;
 #pragma unroll
-            for (int a = 0; a < 8; ++a) {
-                const float tv = Ts[(rb * 8 + a) * (kC + 1) + m];
+                for (int a = 0; a < 8; ++a) {
+                    const float tv = Ts[(rb * 8 + a) * (kC + 1) + m];
 #pragma unroll
-                for (int b = 0; b < 4; ++b) acc[a][b] = fmaf(tv, x[b], acc[a][b]);
+                    for (int b = 0; b < 4; ++b) acc[a][b] = fmaf(tv, x[b], acc[a][b]);
+                }
+            }
+#pragma unroll
+            for (int a = 0; a < 8; ++a)
+                reinterpret_cast<float4 *>(out + (rb * 8 + a) * kD)[cg] =
+                    make_float4(acc[a][0], acc[a][1], acc[a][2], acc[a][3]);
+        };
+        tri_times(Ks, egs, p.w_out + wbase);
+        // K~^T[i][r] = e^{gamma_C - gamma_r} K[r][i] (the state update's B operand).
+        {
+            float *kt = p.kt_out + plane * kD * kC;
+            for (int idx = tid; idx < kD * kC; idx += 256) {
+                const int i = idx / kC, r = idx % kC;
+                kt[idx] = dec[r] * Ks[r * kPad + i];
             }
         }
-#pragma unroll
-        for (int a = 0; a < 8; ++a) {
-            if (round_tf32) {
-#pragma unroll
-                for (int b = 0; b < 4; ++b) acc[a][b] = tf32_rna(acc[a][b]);
+        if (tid < kC) p.eg_out[plane * kC + tid] = egs[tid];
+        __syncthreads();  // Xs (block products) is no longer needed: load V
+        for (int idx = tid; idx < kC * (kD / 4); idx += 256) {
+            const int r = idx / (kD / 4), c4 = idx % (kD / 4);
+            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (t0 + r < p.count) {
+                const float *row = p.qkv + (size_t(s) * p.count + t0 + r) * p.qkv_dim;
+                v = reinterpret_cast<const float4 *>(row + 2 * qk_dim + h * kD)[c4];
             }
-            reinterpret_cast<float4 *>(out + (rb * 8 + a) * kD)[cg] =
-                make_float4(acc[a][0], acc[a][1], acc[a][2], acc[a][3]);
+            float *vd = Xs + r * kPad + c4 * 4;
+            vd[0] = v.x; vd[1] = v.y; vd[2] = v.z; vd[3] = v.w;
         }
-    };
-    tri_times(Ks, bet, egs, p.w_out + wbase, false);
-    // K~^T[i][r] = e^{gamma_C - gamma_r} K[r][i] (the state update's B operand).
-    {
-        float *kt = p.kt_out + ((size_t(s) * p.nchunk + chunk) * p.v_heads + h) * kD * kC;
-        // e^{gamma_C - gamma_r}, kept in As row 0 (A is no longer needed).
-        float *dec = As;
-        if (tid < kC) dec[tid] = expf(gam[kC - 1] - gam[tid]);
         __syncthreads();
-        for (int idx = tid; idx < kD * kC; idx += 256) {
-            const int i = idx / kC, r = idx % kC;
-            kt[idx] = dec[r] * Ks[r * kPad + i];
-        }
+        tri_times(Xs, nullptr, p.ut_out + wbase);
     }
-    __syncthreads();  // Xs (Q) is no longer needed: load V
-    for (int idx = tid; idx < kC * (kD / 4); idx += 256) {
-        const int r = idx / (kD / 4), c4 = idx % (kD / 4);
-        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (t0 + r < p.count) {
-            const float *row = p.qkv + (size_t(s) * p.count + t0 + r) * p.qkv_dim;
-            v = reinterpret_cast<const float4 *>(row + 2 * qk_dim + h * kD)[c4];
-        }
-        float *vd = Xs + r * kPad + c4 * 4;
-        vd[0] = v.x; vd[1] = v.y; vd[2] = v.z; vd[3] = v.w;
-    }
-    __syncthreads();
-    tri_times(Xs, bet, nullptr, p.ut_out + wbase, false);
-    if (tid < kC)
-        p.eg_out[((size_t(s) * p.nchunk + chunk) * p.v_heads + h) * kC + tid] = egs[tid];
 }
 
 // ----------------------------------------------------------------------------
@@ -855,7 +861,7 @@ cudaError_t launch_linear_prefill(const LinearPrefillLaunch &a, cudaStream_t str
                                   cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem_l))) !=
         cudaSuccess)
         return e;
-    linear_prefill_local_kernel<<<dim3(nchunk, a.v_heads, a.nseq), 256, smem_l, stream>>>(lp);
+    linear_prefill_local_kernel<<<dim3(nchunk, a.qk_heads, a.nseq), 256, smem_l, stream>>>(lp);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
 
     CUtensorMap mw, mq, mp, mk;
