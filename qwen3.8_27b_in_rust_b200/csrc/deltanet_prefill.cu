@@ -30,14 +30,14 @@
 //                            chunks in parallel).
 //   L4 linear_prefill_state  one CTA per (value head, sequence): walks the
 //                            chunks in order with the head's state resident
-//                            in TMEM; all products on tcgen05 (kind::tf32 with
-//                            a hi/lo operand split); writes O (scaled by
+//                            in TMEM; all products on tcgen05 (kind::f16 with
+//                            bf16 hi/lo operand pairs); writes O (scaled by
 //                            1/sqrt(128)) and the final state.
 //   L5 linear_prefill_out    one CTA per (token, sequence): per-head RMSNorm
 //                            with ssm_norm and the SiLU(z) gate (ops.rs:735-740).
 //
-// L1-L3 and L5 are f32 CUDA-core kernels; L4's split-tf32 products keep the
-// chunked result within f32 rounding of the per-token recurrence.
+// L1-L3 and L5 are f32 CUDA-core kernels; L4's split-bf16 products keep the
+// chunked result within ~1e-5 of the per-token recurrence.
 #include "q38_sm100.cuh"
 
 #include <cudaTypedefs.h>
@@ -48,13 +48,6 @@ namespace {
 constexpr int kC = 64;       // chunk length
 constexpr int kD = kLinHeadDim;  // 128
 
-// Round to the nearest tf32 (ties away): the tensor cores then see exactly
-// this value instead of a truncated one.
-__device__ __forceinline__ float tf32_rna(float x) {
-    uint32_t r;
-    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
-    return __uint_as_float(r);
-}
 
 // ----------------------------------------------------------------------------
 // L1: conv + SiLU, 64-token segments in parallel
@@ -157,15 +150,27 @@ __global__ void __launch_bounds__(256) linear_prefill_norm_kernel(NormParams p) 
 // ----------------------------------------------------------------------------
 // L3: chunk-local quantities
 // ----------------------------------------------------------------------------
+// Operands of the state pass are stored as bf16 (hi, lo) pairs: plane
+// [2][rows][cols] with hi = bf16(x) and lo = bf16(x - hi), per (sequence,
+// chunk, value head) = "plane".
 struct LocalParams {
     const float *qkv;            // normalised [nseq][count][qkv_dim]
     const float *beta, *alpha;   // sigmoid(beta), g
-    float *w_out, *ut_out;       // [nseq][nchunk][v_heads][64][128]
-    float *p_out;                // [nseq][nchunk][v_heads][64][64]
-    float *eg_out;               // [nseq][nchunk][v_heads][64]  e^{gamma_r}
-    float *kt_out;               // [nseq][nchunk][v_heads][128][64]  e^{gamma_C-gamma_r} K^T
+    __nv_bfloat16 *w2;           // [planes][2][64 r][128 i]   W
+    __nv_bfloat16 *q2;           // [planes][2][64 r][128 i]   Q~ = diag(e^gamma) Q
+    __nv_bfloat16 *p2;           // [planes][2][64 r][64 s]    P
+    __nv_bfloat16 *k2;           // [planes][2][128 i][64 r]   K~^T = (diag(e^{gamma_C-gamma}) K)^T
+    float *ut_out;               // [planes][64][128]          Ut (f32)
+    float *eg_out;               // [planes][64]               e^{gamma_r}
     int count, nchunk, qk_heads, v_heads, qkv_dim;
 };
+
+// x -> (hi, lo) as bf16 with hi = bf16(x), lo = bf16(x - hi): hi + lo keeps
+// ~16 bits of x's mantissa.
+__device__ __forceinline__ void split_bf16(float x, __nv_bfloat16 &hi, __nv_bfloat16 &lo) {
+    hi = __float2bfloat16_rn(x);
+    lo = __float2bfloat16_rn(x - __bfloat162float(hi));
+}
 
 constexpr int kPad = kD + 1;  // padded smem rows (bank-conflict-free column walks)
 
@@ -259,7 +264,7 @@ __global__ void __launch_bounds__(256, 2) linear_prefill_local_kernel(LocalParam
         // A = beta_r e^{gamma_r - gamma_s} K K^T (strictly lower) and
         // P = e^{gamma_r - gamma_s} Q K^T (lower) for this head.
         {
-            float *pout = p.p_out + plane * kC * kC;
+            __nv_bfloat16 *ph = p.p2 + plane * 2 * kC * kC, *pl = ph + kC * kC;
 #pragma unroll
             for (int a = 0; a < 4; ++a)
 #pragma unroll
@@ -267,7 +272,7 @@ __global__ void __launch_bounds__(256, 2) linear_prefill_local_kernel(LocalParam
                     const int r = 4 * ty + a, c = 4 * tx + b;
                     const float d = (c <= r) ? expf(gam[r] - gam[c]) : 0.f;
                     As[r * (kC + 1) + c] = c < r ? bet[r] * d * akk[a][b] : 0.f;
-                    pout[r * kC + c] = c <= r ? d * aqk[a][b] : 0.f;
+                    split_bf16(c <= r ? d * aqk[a][b] : 0.f, ph[r * kC + c], pl[r * kC + c]);
                 }
         }
         __syncthreads();
@@ -323,7 +328,7 @@ __global__ void __launch_bounds__(256, 2) linear_prefill_local_kernel(LocalParam
         // x 4 columns; T is lower triangular, so rows rb*8.. stop at m < rb*8+8.
         const size_t wbase = plane * kC * kD;
         const int rb = tid / 32, cg = tid % 32;
-        auto tri_times = [&](const float *X, const float *scale_b, float *out) {
+        auto tri_times = [&](const float *X, const float *scale_b, auto &&store) {
             float acc[8][4] = {};
             const int mend = rb * 8 + 8;
 #pragma unroll 4
@@ -340,17 +345,42 @@ __global__ void __launch_bounds__(256, 2) linear_prefill_local_kernel(LocalParam
                 }
             }
 #pragma unroll
-            for (int a = 0; a < 8; ++a)
-                reinterpret_cast<float4 *>(out + (rb * 8 + a) * kD)[cg] =
-                    make_float4(acc[a][0], acc[a][1], acc[a][2], acc[a][3]);
+            for (int a = 0; a < 8; ++a) store(rb * 8 + a, cg, acc[a]);
         };
-        tri_times(Ks, egs, p.w_out + wbase);
+        // W as bf16 (hi, lo).
+        __nv_bfloat16 *wh = p.w2 + plane * 2 * kC * kD, *wl = wh + kC * kD;
+        tri_times(Ks, egs, [&](int r, int c4, const float (&v)[4]) {
+            __align__(8) __nv_bfloat16 h4[4], l4[4];
+#pragma unroll
+            for (int b = 0; b < 4; ++b) split_bf16(v[b], h4[b], l4[b]);
+            *reinterpret_cast<uint2 *>(wh + r * kD + c4 * 4) = *reinterpret_cast<const uint2 *>(h4);
+            *reinterpret_cast<uint2 *>(wl + r * kD + c4 * 4) = *reinterpret_cast<const uint2 *>(l4);
+        });
         // K~^T[i][r] = e^{gamma_C - gamma_r} K[r][i] (the state update's B operand).
         {
-            float *kt = p.kt_out + plane * kD * kC;
+            __nv_bfloat16 *kth = p.k2 + plane * 2 * kD * kC, *ktl = kth + kD * kC;
             for (int idx = tid; idx < kD * kC; idx += 256) {
                 const int i = idx / kC, r = idx % kC;
-                kt[idx] = dec[r] * Ks[r * kPad + i];
+                split_bf16(dec[r] * Ks[r * kPad + i], kth[idx], ktl[idx]);
+            }
+        }
+        // Q~ = diag(e^gamma) Q (Q re-read from the normalised qkv rows).
+        {
+            __nv_bfloat16 *qh = p.q2 + plane * 2 * kC * kD, *ql = qh + kC * kD;
+            for (int idx = tid; idx < kC * (kD / 4); idx += 256) {
+                const int r = idx / (kD / 4), c4 = idx % (kD / 4);
+                float4 q = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (t0 + r < p.count)
+                    q = reinterpret_cast<const float4 *>(
+                        p.qkv + (size_t(s) * p.count + t0 + r) * p.qkv_dim + kh * kD)[c4];
+                const float e = egs[r];
+                __align__(8) __nv_bfloat16 h4[4], l4[4];
+                split_bf16(q.x * e, h4[0], l4[0]);
+                split_bf16(q.y * e, h4[1], l4[1]);
+                split_bf16(q.z * e, h4[2], l4[2]);
+                split_bf16(q.w * e, h4[3], l4[3]);
+                *reinterpret_cast<uint2 *>(qh + r * kD + c4 * 4) = *reinterpret_cast<const uint2 *>(h4);
+                *reinterpret_cast<uint2 *>(ql + r * kD + c4 * 4) = *reinterpret_cast<const uint2 *>(l4);
             }
         }
         if (tid < kC) p.eg_out[plane * kC + tid] = egs[tid];
@@ -366,37 +396,38 @@ __global__ void __launch_bounds__(256, 2) linear_prefill_local_kernel(LocalParam
             vd[0] = v.x; vd[1] = v.y; vd[2] = v.z; vd[3] = v.w;
         }
         __syncthreads();
-        tri_times(Xs, nullptr, p.ut_out + wbase);
+        float *ut = p.ut_out + wbase;
+        tri_times(Xs, nullptr, [&](int r, int c4, const float (&v)[4]) {
+            reinterpret_cast<float4 *>(ut + r * kD)[c4] = make_float4(v[0], v[1], v[2], v[3]);
+        });
     }
 }
 
 // ----------------------------------------------------------------------------
-// L4: sequential state pass over the chunks, on tcgen05 (kind::tf32, split)
+// L4: sequential state pass over the chunks, on tcgen05 (bf16 hi/lo split)
 // ----------------------------------------------------------------------------
 // One CTA per (value head, sequence). The head's state S [128 j][128 i] lives
 // in TMEM (lane j) for the whole prompt; per chunk, with U^T [j][r] = U[r][j]:
 //   D_U | D_O = S [W ; Q~]^T      (M=128, N=128, K=128; A = S from TMEM)
 //   U^T       = Ut^T - D_U         (epilogue warps)
 //   D_PU      = U^T P^T            (M=128, N=64,  K=64;  A = U^T from TMEM)
-//   S         = e^{gamma_C} S      (epilogue warps)
-//   S        += U^T K~             (M=128, N=128, K=64)
+//   S         = e^{gamma_C} S + U^T K~   (M=128, N=128, K=64, into the f32 state)
 //   O[r][j]   = (D_O[j][r] + D_PU[j][r]) / sqrt(128),   Q~ = diag(e^gamma) Q
-// tf32 keeps 10 mantissa bits, which alone leaves errors of a few 1e-3 after
-// the output RMSNorm; so every operand X is split as X = hi + lo with
-// hi = tf32(X) and lo = X - hi (exact in f32), and each product is
-// A.B = hi(A).hi(B) + lo(A).hi(B) + hi(A).lo(B) (the dropped lo.lo term is
-// 2^-22 relative): three MMAs per K step, f32 accumulation, ~f32 accuracy.
-// S and U^T are kept as (hi, lo) column pairs in TMEM; the B operands are
-// split in shared memory right after their TMA load, by four splitter warps.
-constexpr int kThreadsLS = 352;  // w0 W/Q/P loads, w1 MMA, w2-5 epilogue, w6 K~ loads, w7-10 split
-constexpr uint32_t kB1Bytes = 128 * 128 * 4;  // [W ; Q~]: 4 column blocks of 128 rows x 128 B
-constexpr uint32_t kPmBytes = 64 * 64 * 4;    // P: 2 column blocks of 64 rows x 128 B
-constexpr uint32_t kKtBytes = 128 * 64 * 4;   // K~^T: 2 column blocks of 128 rows x 128 B
-constexpr uint32_t kSmemLS = 2 * (kB1Bytes + kPmBytes + kKtBytes) + 1024;
-// TMEM columns: S (hi, or the f32 value around the update) | S lo | D_U, then
-// U^T hi | D_O | U^T lo | D_PU.
-constexpr uint32_t kColSh = 0, kColSl = 128, kColU = 256, kColOq = 320, kColUl = 384,
-                   kColPU = 448, kTmemColsLS = 512;
+// Every operand X is a bf16 pair hi = bf16(X), lo = bf16(X - hi), and each
+// product is hi.hi + lo.hi + hi.lo (three kind::f16 MMAs, f32 accumulation):
+// ~16 bits of each operand, so the chunked result stays within ~1e-5 of the
+// per-token recurrence, at K = 16 per instruction. The f32 state is the MMA
+// accumulator; after each update the epilogue writes its (hi, lo) copy for
+// the next chunk's products and pre-multiplies it by the next chunk's decay.
+constexpr int kThreadsLS = 352;  // w0 TMA, w1 MMA (S products), w2-5 + w7-10 epilogue, w6 MMA (P U^T)
+constexpr uint32_t kB1Half = 128 * 128 * 2;   // [W ; Q~] hi or lo: 2 column blocks of 128 rows x 128 B
+constexpr uint32_t kPmHalf = 64 * 64 * 2;     // P hi or lo: 64 rows x 128 B
+constexpr uint32_t kKtHalf = 128 * 64 * 2;    // K~^T hi or lo: 128 rows x 128 B
+constexpr uint32_t kStageLS = 2 * (kB1Half + kPmHalf + kKtHalf);  // 112 KB
+constexpr uint32_t kSmemLS = 2 * kStageLS + 1024;
+// TMEM columns: f32 state | S hi | S lo (bf16 pairs) | D_U | D_O | U^T hi | U^T lo | D_PU.
+constexpr uint32_t kColS = 0, kColSh = 128, kColSl = 192, kColU = 256, kColOq = 320,
+                   kColUh = 384, kColUl = 416, kColPU = 448, kTmemColsLS = 512;
 
 struct StateTcParams {
     const float *ut;      // [planes][64][128]
@@ -408,50 +439,23 @@ struct StateTcParams {
 };
 
 struct __align__(8) StateTcBarriers {
-    uint64_t b1_raw, b1_split, b1_free, p_raw, p_split, p_free, k_raw, k_split, k_free;
-    uint64_t s_ready, uo_full, u_ready, s_scaled, pu_full, s_done, s_split;
+    uint64_t b1_full[2], b1_free[2], p_full[2], p_free[2], k_full[2], k_free[2];
+    uint64_t s_ready, uo_full, u_ready, pu_full, s_done;
 };
 
-__device__ __forceinline__ void mma_tf32_ts(uint32_t d, uint32_t a_tmem, uint64_t b,
-                                            uint32_t id, uint32_t acc) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d),
-        "r"(a_tmem), "l"(b), "r"(id), "r"(acc)
-        : "memory");
-}
-__host__ __device__ constexpr uint32_t idesc_tf32(int M, int N) {
-    return (1u << 4) | (2u << 7) | (2u << 10) | (uint32_t(N >> 3) << 17) | (uint32_t(M >> 4) << 24);
-}
-
-// hi/lo split of n_vec4 float4s of `hi` in place, lo into `lo`; rows of 128 B
-// at or past `scaled_row0` within each 128-row block are first multiplied by
-// scale[row - scaled_row0] (Q~ = e^gamma Q).
-__device__ __forceinline__ void split_tile(unsigned char *hi, unsigned char *lo, int n_vec4,
-                                           int t, int nthreads, int scaled_row0,
-                                           const float *scale) {
-    for (int v = t; v < n_vec4; v += nthreads) {
-        float4 x = reinterpret_cast<float4 *>(hi)[v];
-        const int row = (v * 16 % 16384) / 128;
-        if (scale && row >= scaled_row0) {
-            const float f = scale[row - scaled_row0];
-            x.x *= f;
-            x.y *= f;
-            x.z *= f;
-            x.w *= f;
-        }
-        float4 h4, l4;
-        h4.x = tf32_rna(x.x);
-        h4.y = tf32_rna(x.y);
-        h4.z = tf32_rna(x.z);
-        h4.w = tf32_rna(x.w);
-        l4.x = x.x - h4.x;
-        l4.y = x.y - h4.y;
-        l4.z = x.z - h4.z;
-        l4.w = x.w - h4.w;
-        reinterpret_cast<float4 *>(hi)[v] = h4;
-        reinterpret_cast<float4 *>(lo)[v] = l4;
+// (hi, lo) bf16 pairs of 32 f32 values, 2 per 32-bit word, into TMEM:
+// hi = bf16x2(a, b), lo = bf16x2(a - hi.a, b - hi.b) with packed conversions.
+__device__ __forceinline__ void st_split_bf16(uint32_t t_hi, uint32_t t_lo, const uint32_t (&w)[32]) {
+    uint32_t hi[16], lo[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+        const float a = __uint_as_float(w[2 * i]), b = __uint_as_float(w[2 * i + 1]);
+        hi[i] = pack_bf16x2_rn(a, b);
+        const float2 hf = bf16x2_to_float2(hi[i]);
+        lo[i] = pack_bf16x2_rn(a - hf.x, b - hf.y);
     }
+    sm100::tmem_st16(t_hi, hi);
+    sm100::tmem_st16(t_lo, lo);
 }
 
 __global__ void __launch_bounds__(kThreadsLS, 1)
@@ -463,36 +467,36 @@ __global__ void __launch_bounds__(kThreadsLS, 1)
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char *smem =
         reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    unsigned char *sB1h = smem, *sB1l = sB1h + kB1Bytes;
-    unsigned char *sPh = sB1l + kB1Bytes, *sPl = sPh + kPmBytes;
-    unsigned char *sKh = sPl + kPmBytes, *sKl = sKh + kKtBytes;
+    // Stage layout: B1 hi | B1 lo | P hi | P lo | K~ hi | K~ lo.
+    auto b1h = [&](int st) { return smem + st * kStageLS; };
+    auto b1l = [&](int st) { return smem + st * kStageLS + kB1Half; };
+    auto pmh = [&](int st) { return smem + st * kStageLS + 2 * kB1Half; };
+    auto pml = [&](int st) { return smem + st * kStageLS + 2 * kB1Half + kPmHalf; };
+    auto kth = [&](int st) { return smem + st * kStageLS + 2 * kB1Half + 2 * kPmHalf; };
+    auto ktl = [&](int st) { return smem + st * kStageLS + 2 * kB1Half + 2 * kPmHalf + kKtHalf; };
     __shared__ StateTcBarriers bar;
     __shared__ uint32_t tmem_base_s;
     __shared__ volatile int abort_flag;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int h = blockIdx.x, s = blockIdx.y;
-    const int kh = h % p.qk_heads;  // ops.rs:699
     auto plane = [&](int c) { return (s * p.nchunk + c) * p.v_heads + h; };
 
     if (threadIdx.x == 0) {
         abort_flag = 0;
-        mbar_init(&bar.b1_raw, 1);
-        mbar_init(&bar.b1_split, 128);
-        mbar_init(&bar.b1_free, 1);
-        mbar_init(&bar.p_raw, 1);
-        mbar_init(&bar.p_split, 128);
-        mbar_init(&bar.p_free, 1);
-        mbar_init(&bar.k_raw, 1);
-        mbar_init(&bar.k_split, 128);
-        mbar_init(&bar.k_free, 1);
-        mbar_init(&bar.s_ready, 128);
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&bar.b1_full[b], 1);
+            mbar_init(&bar.b1_free[b], 1);
+            mbar_init(&bar.p_full[b], 1);
+            mbar_init(&bar.p_free[b], 1);
+            mbar_init(&bar.k_full[b], 1);
+            mbar_init(&bar.k_free[b], 1);
+        }
+        mbar_init(&bar.s_ready, 256);
         mbar_init(&bar.uo_full, 1);
-        mbar_init(&bar.u_ready, 128);
-        mbar_init(&bar.s_scaled, 128);
+        mbar_init(&bar.u_ready, 256);
         mbar_init(&bar.pu_full, 1);
         mbar_init(&bar.s_done, 1);
-        mbar_init(&bar.s_split, 128);
         fence_barrier_init();
     }
     if (warp == 1) {
@@ -509,123 +513,119 @@ __global__ void __launch_bounds__(kThreadsLS, 1)
     };
 
     if (warp == 0) {
-        // ---------------------------------------------------------- [W ; Q] and P loads
+        // ---------------------------------------------------------- TMA: [W ; Q~], P, K~^T
         if (lane == 0) {
             tma_prefetch_desc(&map_w);
             tma_prefetch_desc(&map_q);
             tma_prefetch_desc(&map_p);
-            for (int c = 0; c < p.nchunk && !abort_flag; ++c) {
-                const uint32_t prev = uint32_t(c - 1) & 1u;
-                if (c >= 1 && !mbar_wait(&bar.b1_free, prev)) { fail(); break; }
-                mbar_arrive_expect_tx(&bar.b1_raw, kB1Bytes);
-                for (int blk = 0; blk < 4; ++blk) {
-                    tma_load_3d(sB1h + blk * 16384, &map_w, blk * 32, 0, plane(c), &bar.b1_raw);
-                    tma_load_3d(sB1h + blk * 16384 + 8192, &map_q, kh * kD + blk * 32,
-                                s * p.count + c * kC, 0, &bar.b1_raw);
-                }
-                if (c >= 1 && !mbar_wait(&bar.p_free, prev)) { fail(); break; }
-                mbar_arrive_expect_tx(&bar.p_raw, kPmBytes);
-                for (int blk = 0; blk < 2; ++blk)
-                    tma_load_3d(sPh + blk * 8192, &map_p, blk * 32, 0, plane(c), &bar.p_raw);
-            }
-        }
-    } else if (warp == 6) {
-        // ---------------------------------------------------------- K~^T loads
-        if (lane == 0) {
             tma_prefetch_desc(&map_kt);
             for (int c = 0; c < p.nchunk && !abort_flag; ++c) {
-                if (c >= 1 && !mbar_wait(&bar.k_free, uint32_t(c - 1) & 1u)) { fail(); break; }
-                mbar_arrive_expect_tx(&bar.k_raw, kKtBytes);
-                for (int blk = 0; blk < 2; ++blk)
-                    tma_load_3d(sKh + blk * 16384, &map_kt, blk * 32, 0, plane(c), &bar.k_raw);
+                const int st = c & 1;
+                const uint32_t ph = uint32_t((c - 2) >> 1) & 1u;
+                const int pl2 = 2 * plane(c);  // hi plane; lo = hi + 1
+                if (c >= 2 && !mbar_wait(&bar.b1_free[st], ph)) { fail(); break; }
+                mbar_arrive_expect_tx(&bar.b1_full[st], 2 * kB1Half);
+                for (int hl = 0; hl < 2; ++hl) {
+                    unsigned char *dst = hl ? b1l(st) : b1h(st);
+                    for (int blk = 0; blk < 2; ++blk) {
+                        tma_load_3d(dst + blk * 16384, &map_w, blk * 64, 0, pl2 + hl, &bar.b1_full[st]);
+                        tma_load_3d(dst + blk * 16384 + 8192, &map_q, blk * 64, 0, pl2 + hl,
+                                    &bar.b1_full[st]);
+                    }
+                }
+                if (c >= 2 && !mbar_wait(&bar.p_free[st], ph)) { fail(); break; }
+                mbar_arrive_expect_tx(&bar.p_full[st], 2 * kPmHalf);
+                tma_load_3d(pmh(st), &map_p, 0, 0, pl2, &bar.p_full[st]);
+                tma_load_3d(pml(st), &map_p, 0, 0, pl2 + 1, &bar.p_full[st]);
+                if (c >= 2 && !mbar_wait(&bar.k_free[st], ph)) { fail(); break; }
+                mbar_arrive_expect_tx(&bar.k_full[st], 2 * kKtHalf);
+                tma_load_3d(kth(st), &map_kt, 0, 0, pl2, &bar.k_full[st]);
+                tma_load_3d(ktl(st), &map_kt, 0, 0, pl2 + 1, &bar.k_full[st]);
             }
         }
-    } else if (warp >= 7) {
-        // ---------------------------------------------------------- hi/lo splitters
-        const int t = threadIdx.x - 7 * 32;  // 0..127
-        bool ok = true;
-        for (int c = 0; ok && c < p.nchunk; ++c) {
-            const uint32_t ph = uint32_t(c) & 1u;
-            const float *egp = p.eg + size_t(plane(c)) * kC;
-            if (!mbar_wait(&bar.b1_raw, ph)) { ok = false; break; }
-            split_tile(sB1h, sB1l, int(kB1Bytes / 16), t, 128, kC, egp);
-            fence_proxy_async_smem();
-            mbar_arrive(&bar.b1_split);
-            if (!mbar_wait(&bar.p_raw, ph)) { ok = false; break; }
-            split_tile(sPh, sPl, int(kPmBytes / 16), t, 128, kC, nullptr);
-            fence_proxy_async_smem();
-            mbar_arrive(&bar.p_split);
-            if (!mbar_wait(&bar.k_raw, ph)) { ok = false; break; }
-            split_tile(sKh, sKl, int(kKtBytes / 16), t, 128, kD, nullptr);
-            fence_proxy_async_smem();
-            mbar_arrive(&bar.k_split);
-            if (abort_flag) ok = false;
-        }
-        if (!ok && t == 0) fail();
     } else if (warp == 1) {
-        // ---------------------------------------------------------- MMA issuer
+        // ---------------------------------------------------------- MMA: S [W ; Q~]^T and the update
         if (lane == 0) {
-            const uint32_t id_n128 = idesc_tf32(128, 128), id_n64 = idesc_tf32(128, 64);
-            const uint32_t b1h = smem_addr(sB1h), b1l = smem_addr(sB1l), ph_ = smem_addr(sPh),
-                           pl_ = smem_addr(sPl), khh = smem_addr(sKh), kll = smem_addr(sKl);
-            bool ok = mbar_wait(&bar.s_ready, 0);
+            const uint32_t id_n128 = idesc_bf16_f32(128, 128, 0, 0);
+            bool ok = true;
             for (int c = 0; ok && c < p.nchunk; ++c) {
-                const uint32_t ph = uint32_t(c) & 1u;
-                // S of this chunk is split (which follows the last update and
-                // the epilogue's reads of D_O / U^T of the previous chunk).
-                if (c >= 1 && !mbar_wait(&bar.s_split, ph ^ 1u)) { ok = false; break; }
-                if (!mbar_wait(&bar.b1_split, ph)) { ok = false; break; }
+                const int st = c & 1;
+                const uint32_t ph1 = uint32_t(c) & 1u, ph2 = uint32_t(c >> 1) & 1u;
+                // s_ready(c): S of this chunk split into (hi, lo), the f32 state
+                // pre-multiplied by e^{gamma_C}, and the epilogue done with the
+                // previous chunk's D_U, D_O and D_PU.
+                if (!mbar_wait(&bar.s_ready, ph1) || !mbar_wait(&bar.b1_full[st], ph2)) {
+                    ok = false;
+                    break;
+                }
                 fence_after_sync();
+                const uint32_t bh = smem_addr(b1h(st)), bl = smem_addr(b1l(st));
 #pragma unroll 1
-                for (int kk = 0; kk < kD / 8; ++kk) {
+                for (int kk = 0; kk < kD / 16; ++kk) {
                     const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
-                    const uint64_t bh = smem_desc_sw128(b1h + off, 16, 1024);
-                    const uint64_t bl = smem_desc_sw128(b1l + off, 16, 1024);
-                    mma_tf32_ts(tmem + kColU, tmem + kColSh + kk * 8, bh, id_n128, kk > 0 ? 1u : 0u);
-                    mma_tf32_ts(tmem + kColU, tmem + kColSl + kk * 8, bh, id_n128, 1u);
-                    mma_tf32_ts(tmem + kColU, tmem + kColSh + kk * 8, bl, id_n128, 1u);
+                    const uint64_t dh = smem_desc_sw128(bh + off, 16, 1024);
+                    const uint64_t dl = smem_desc_sw128(bl + off, 16, 1024);
+                    mma_f16_ta(tmem + kColU, tmem + kColSh + kk * 8, dh, id_n128, kk > 0 ? 1u : 0u);
+                    mma_f16_ta(tmem + kColU, tmem + kColSl + kk * 8, dh, id_n128, 1u);
+                    mma_f16_ta(tmem + kColU, tmem + kColSh + kk * 8, dl, id_n128, 1u);
                 }
                 mma_commit(&bar.uo_full);
-                mma_commit(&bar.b1_free);
-                if (!mbar_wait(&bar.u_ready, ph) || !mbar_wait(&bar.p_split, ph)) {
+                mma_commit(&bar.b1_free[st]);
+                if (!mbar_wait(&bar.u_ready, ph1) || !mbar_wait(&bar.k_full[st], ph2)) {
                     ok = false;
                     break;
                 }
                 fence_after_sync();
+                const uint32_t kh_ = smem_addr(kth(st)), kl_ = smem_addr(ktl(st));
 #pragma unroll 1
-                for (int kk = 0; kk < kC / 8; ++kk) {
-                    const uint32_t off = (kk >> 2) * 8192 + (kk & 3) * 32;
-                    const uint64_t bh = smem_desc_sw128(ph_ + off, 16, 1024);
-                    const uint64_t bl = smem_desc_sw128(pl_ + off, 16, 1024);
-                    mma_tf32_ts(tmem + kColPU, tmem + kColU + kk * 8, bh, id_n64, kk > 0 ? 1u : 0u);
-                    mma_tf32_ts(tmem + kColPU, tmem + kColUl + kk * 8, bh, id_n64, 1u);
-                    mma_tf32_ts(tmem + kColPU, tmem + kColU + kk * 8, bl, id_n64, 1u);
-                }
-                mma_commit(&bar.pu_full);
-                mma_commit(&bar.p_free);
-                if (!mbar_wait(&bar.s_scaled, ph) || !mbar_wait(&bar.k_split, ph)) {
-                    ok = false;
-                    break;
-                }
-                fence_after_sync();
-#pragma unroll 1
-                for (int kk = 0; kk < kC / 8; ++kk) {
-                    const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
-                    const uint64_t bh = smem_desc_sw128(khh + off, 16, 1024);
-                    const uint64_t bl = smem_desc_sw128(kll + off, 16, 1024);
-                    mma_tf32_ts(tmem + kColSh, tmem + kColU + kk * 8, bh, id_n128, 1u);
-                    mma_tf32_ts(tmem + kColSh, tmem + kColUl + kk * 8, bh, id_n128, 1u);
-                    mma_tf32_ts(tmem + kColSh, tmem + kColU + kk * 8, bl, id_n128, 1u);
+                for (int kk = 0; kk < kC / 16; ++kk) {
+                    const uint64_t dh = smem_desc_sw128(kh_ + kk * 32, 16, 1024);
+                    const uint64_t dl = smem_desc_sw128(kl_ + kk * 32, 16, 1024);
+                    mma_f16_ta(tmem + kColS, tmem + kColUh + kk * 8, dh, id_n128, 1u);
+                    mma_f16_ta(tmem + kColS, tmem + kColUl + kk * 8, dh, id_n128, 1u);
+                    mma_f16_ta(tmem + kColS, tmem + kColUh + kk * 8, dl, id_n128, 1u);
                 }
                 mma_commit(&bar.s_done);
-                mma_commit(&bar.k_free);
+                mma_commit(&bar.k_free[st]);
                 if (abort_flag) { ok = false; break; }
             }
             if (!ok) fail();
         }
+    } else if (warp == 6) {
+        // ---------------------------------------------------------- MMA: D_PU = U^T P^T
+        if (lane == 0) {
+            const uint32_t id_n64 = idesc_bf16_f32(128, 64, 0, 0);
+            bool ok = true;
+            for (int c = 0; ok && c < p.nchunk; ++c) {
+                const int st = c & 1;
+                if (!mbar_wait(&bar.u_ready, uint32_t(c) & 1u) ||
+                    !mbar_wait(&bar.p_full[st], uint32_t(c >> 1) & 1u)) {
+                    ok = false;
+                    break;
+                }
+                fence_after_sync();
+                const uint32_t ph_ = smem_addr(pmh(st)), pl_ = smem_addr(pml(st));
+#pragma unroll 1
+                for (int kk = 0; kk < kC / 16; ++kk) {
+                    const uint64_t dh = smem_desc_sw128(ph_ + kk * 32, 16, 1024);
+                    const uint64_t dl = smem_desc_sw128(pl_ + kk * 32, 16, 1024);
+                    mma_f16_ta(tmem + kColPU, tmem + kColUh + kk * 8, dh, id_n64, kk > 0 ? 1u : 0u);
+                    mma_f16_ta(tmem + kColPU, tmem + kColUl + kk * 8, dh, id_n64, 1u);
+                    mma_f16_ta(tmem + kColPU, tmem + kColUh + kk * 8, dl, id_n64, 1u);
+                }
+                mma_commit(&bar.pu_full);
+                mma_commit(&bar.p_free[st]);
+                if (abort_flag) ok = false;
+            }
+            if (!ok) fail();
+        }
     } else {
-        // ---------------------------------------------------------- epilogue (row j per thread)
+        // ---------------------------------------------------------- epilogue
+        // Warps 2-5 and 7-10: two threads per state row j, each handling half
+        // of the row's columns (r in [32*half, 32*half+32) for U and O, state
+        // columns [64*half, 64*half+64)).
         const int sub = warp & 3;
+        const int half = warp >= 7 ? 1 : 0;
         const int j = sub * 32 + lane;
         const uint32_t lane_addr = uint32_t(sub * 32) << 16;
         const float query_scale = 1.0f / sqrtf(float(kD));
@@ -633,111 +633,86 @@ __global__ void __launch_bounds__(kThreadsLS, 1)
         auto wait_all = [&](uint64_t *b, uint32_t parity) {
             return __all_sync(0xffffffffu, mbar_wait(b, parity));
         };
-        // Writes hi/lo of the 32 values in w to TMEM columns col_hi / col_lo.
-        auto st_split = [&](uint32_t col_hi, uint32_t col_lo, uint32_t (&w)[32]) {
-            uint32_t lo[32];
-#pragma unroll
-            for (int i = 0; i < 32; ++i) {
-                const float x = __uint_as_float(w[i]);
-                const float hi = tf32_rna(x);
-                lo[i] = __float_as_uint(x - hi);
-                w[i] = __float_as_uint(hi);
-            }
-            tmem_st32(tmem + lane_addr + col_hi, w);
-            tmem_st32(tmem + lane_addr + col_lo, lo);
-        };
+        const int r0 = 32 * half;
+        // Initial state: (hi, lo) for chunk 0's products, e^{gamma_C(0)} S0 as the accumulator.
         bool ok = true;
+        {
+            const float eg0 = p.eg[size_t(plane(0)) * kC + kC - 1];
 #pragma unroll 1
-        for (int cb = 0; cb < 4; ++cb) {
-            uint32_t w[32];
+            for (int cb = 2 * half; cb < 2 * half + 2; ++cb) {
+                uint32_t w[32];
 #pragma unroll
-            for (int i = 0; i < 32; i += 4) {
-                const float4 v = *reinterpret_cast<const float4 *>(S + cb * 32 + i);
-                w[i] = __float_as_uint(v.x);
-                w[i + 1] = __float_as_uint(v.y);
-                w[i + 2] = __float_as_uint(v.z);
-                w[i + 3] = __float_as_uint(v.w);
+                for (int i = 0; i < 32; i += 4) {
+                    const float4 v = *reinterpret_cast<const float4 *>(S + cb * 32 + i);
+                    w[i] = __float_as_uint(v.x);
+                    w[i + 1] = __float_as_uint(v.y);
+                    w[i + 2] = __float_as_uint(v.z);
+                    w[i + 3] = __float_as_uint(v.w);
+                }
+                st_split_bf16(tmem + lane_addr + kColSh + cb * 16, tmem + lane_addr + kColSl + cb * 16, w);
+#pragma unroll
+                for (int i = 0; i < 32; ++i) w[i] = __float_as_uint(__uint_as_float(w[i]) * eg0);
+                tmem_st32(tmem + lane_addr + kColS + cb * 32, w);
             }
-            st_split(kColSh + cb * 32, kColSl + cb * 32, w);
+            tmem_wait_st();
+            fence_before_sync();
+            mbar_arrive(&bar.s_ready);
         }
-        tmem_wait_st();
-        fence_before_sync();
-        mbar_arrive(&bar.s_ready);
         for (int c = 0; ok && c < p.nchunk; ++c) {
             const uint32_t ph = uint32_t(c) & 1u;
             const size_t lb = size_t(plane(c));
-            const float *utp = p.ut + lb * kC * kD + j;
-            float ut[kC];
+            const float *utp = p.ut + (lb * kC + r0) * kD + j;
+            float ut[32];
 #pragma unroll
-            for (int r = 0; r < kC; ++r) ut[r] = utp[r * kD];
-            const float egC = p.eg[lb * kC + kC - 1];
+            for (int r = 0; r < 32; ++r) ut[r] = utp[r * kD];
             if (!wait_all(&bar.uo_full, ph)) { ok = false; break; }
             fence_after_sync();
-            // U^T row j = Ut^T - D_U as (hi, lo).
-#pragma unroll
-            for (int half = 0; half < 2; ++half) {
+            // U^T row j (this half's r) = Ut^T - D_U as bf16 (hi, lo).
+            {
                 uint32_t d[32];
-                tmem_ld32(tmem + lane_addr + kColU + half * 32, d);
+                tmem_ld32(tmem + lane_addr + kColU + r0, d);
                 tmem_wait_ld();
 #pragma unroll
-                for (int i = 0; i < 32; ++i)
-                    d[i] = __float_as_uint(ut[half * 32 + i] - __uint_as_float(d[i]));
-                st_split(kColU + half * 32, kColUl + half * 32, d);
+                for (int i = 0; i < 32; ++i) d[i] = __float_as_uint(ut[i] - __uint_as_float(d[i]));
+                st_split_bf16(tmem + lane_addr + kColUh + half * 16, tmem + lane_addr + kColUl + half * 16, d);
             }
-            // e^{gamma_r} (S0 q_r), kept until D_PU is ready.
-            float os[kC];
-#pragma unroll
-            for (int half = 0; half < 2; ++half) {
+            // e^{gamma_r} (S0 q_r) (Q~ carries the decay), kept until D_PU is ready.
+            float os[32];
+            {
                 uint32_t d[32];
-                tmem_ld32(tmem + lane_addr + kColOq + half * 32, d);
+                tmem_ld32(tmem + lane_addr + kColOq + r0, d);
                 tmem_wait_ld();
 #pragma unroll
-                for (int i = 0; i < 32; ++i) os[half * 32 + i] = __uint_as_float(d[i]);
+                for (int i = 0; i < 32; ++i) os[i] = __uint_as_float(d[i]);
             }
             tmem_wait_st();
             fence_before_sync();
             mbar_arrive(&bar.u_ready);
-            // S <- e^{gamma_C} (hi + lo), as one f32 value for the update.
-#pragma unroll 1
-            for (int cb = 0; cb < 4; ++cb) {
-                uint32_t a[32], b[32];
-                tmem_ld32(tmem + lane_addr + kColSh + cb * 32, a);
-                tmem_ld32(tmem + lane_addr + kColSl + cb * 32, b);
+            if (!wait_all(&bar.pu_full, ph)) { ok = false; break; }
+            fence_after_sync();
+            const int t0 = c * kC + r0;
+            float *orow = p.o_out + (size_t(s) * p.count + t0) * (size_t(p.v_heads) * kD) + h * kD + j;
+            {
+                uint32_t d[32];
+                tmem_ld32(tmem + lane_addr + kColPU + r0, d);
                 tmem_wait_ld();
 #pragma unroll
                 for (int i = 0; i < 32; ++i)
-                    a[i] = __float_as_uint((__uint_as_float(a[i]) + __uint_as_float(b[i])) * egC);
-                tmem_st32(tmem + lane_addr + kColSh + cb * 32, a);
+                    if (t0 + i < p.count)
+                        orow[size_t(i) * p.v_heads * kD] = (os[i] + __uint_as_float(d[i])) * query_scale;
             }
-            tmem_wait_st();
-            fence_before_sync();
-            mbar_arrive(&bar.s_scaled);
-            if (!wait_all(&bar.pu_full, ph)) { ok = false; break; }
-            fence_after_sync();
-            const int t0 = c * kC;
-            float *orow = p.o_out + (size_t(s) * p.count + t0) * (size_t(p.v_heads) * kD) + h * kD + j;
-#pragma unroll
-            for (int half = 0; half < 2; ++half) {
-                uint32_t d[32];
-                tmem_ld32(tmem + lane_addr + kColPU + half * 32, d);
-                tmem_wait_ld();
-#pragma unroll
-                for (int i = 0; i < 32; ++i) {
-                    const int r = half * 32 + i;
-                    if (t0 + r < p.count)
-                        orow[size_t(r) * p.v_heads * kD] =
-                            (os[r] + __uint_as_float(d[i])) * query_scale;
-                }
-            }
-            // The updated S as (hi, lo) for the next chunk; the last one is
-            // the final state.
+            // The updated state: (hi, lo) for the next chunk's products and the
+            // f32 accumulator pre-multiplied by the next chunk's e^{gamma_C};
+            // after the last chunk, the final state.
             if (!wait_all(&bar.s_done, ph)) { ok = false; break; }
             fence_after_sync();
             const bool last = c == p.nchunk - 1;
+            const float egn = last ? 1.f : p.eg[size_t(plane(c + 1)) * kC + kC - 1];
+            const float2 egn2 = make_float2(egn, egn);
 #pragma unroll 1
-            for (int cb = 0; cb < 4; ++cb) {
+            for (int cb = 2 * half; cb < 2 * half + 2; ++cb) {
                 uint32_t w[32];
-                tmem_ld32(tmem + lane_addr + kColSh + cb * 32, w);
+                tmem_ld32(tmem + lane_addr + kColS + cb * 32, w);
                 tmem_wait_ld();
                 if (last) {
 #pragma unroll
@@ -746,12 +721,22 @@ __global__ void __launch_bounds__(kThreadsLS, 1)
                             make_float4(__uint_as_float(w[i]), __uint_as_float(w[i + 1]),
                                         __uint_as_float(w[i + 2]), __uint_as_float(w[i + 3]));
                 } else {
-                    st_split(kColSh + cb * 32, kColSl + cb * 32, w);
+                    st_split_bf16(tmem + lane_addr + kColSh + cb * 16,
+                                  tmem + lane_addr + kColSl + cb * 16, w);
+#pragma unroll
+                    for (int i = 0; i < 32; i += 2) {
+                        const float2 v = fmul2(make_float2(__uint_as_float(w[i]), __uint_as_float(w[i + 1])), egn2);
+                        w[i] = __float_as_uint(v.x);
+                        w[i + 1] = __float_as_uint(v.y);
+                    }
+                    tmem_st32(tmem + lane_addr + kColS + cb * 32, w);
                 }
             }
-            tmem_wait_st();
-            fence_before_sync();
-            mbar_arrive(&bar.s_split);
+            if (!last) {
+                tmem_wait_st();
+                fence_before_sync();
+                mbar_arrive(&bar.s_ready);
+            }
             if (__any_sync(0xffffffffu, abort_flag != 0)) { ok = false; break; }
         }
         if (!ok && lane == 0) fail();
@@ -775,18 +760,18 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_tiled_ls() {
     return fn;
 }
 
-// 3-D f32 map over [planes][rows][cols] with a box of 32 x box_rows x 1 and
-// 128-byte swizzle (K-major tf32 operand tiles).
-bool make_map_f32(CUtensorMap *m, const void *base, uint64_t cols, uint64_t rows, uint64_t planes,
-                  uint32_t box_rows) {
+// 3-D bf16 map over [planes][rows][cols] with a box of 64 x box_rows x 1 and
+// 128-byte swizzle (K-major operand tiles of 64 bf16 per row).
+bool make_map_bf16_ls(CUtensorMap *m, const void *base, uint64_t cols, uint64_t rows,
+                      uint64_t planes, uint32_t box_rows) {
     auto enc = encode_tiled_ls();
     if (!enc) return false;
     cuuint64_t dims[3] = {cols, rows, planes};
-    cuuint64_t strides[2] = {cols * 4, cols * 4 * rows};
-    cuuint32_t box[3] = {32, box_rows, 1};
+    cuuint64_t strides[2] = {cols * 2, cols * 2 * rows};
+    cuuint32_t box[3] = {64, box_rows, 1};
     cuuint32_t es[3] = {1, 1, 1};
-    return enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<void *>(base), dims, strides, box,
-               es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+    return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void *>(base), dims, strides,
+               box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
@@ -824,9 +809,10 @@ __global__ void __launch_bounds__(256) linear_prefill_out_kernel(OutParams p) {
 }  // namespace
 
 size_t linear_prefill_scratch_floats(int nchunk_total, int v_heads) {
-    // W, Ut: [chunks][v_heads][64][128] each; P: [..][64][64]; e^gamma: [..][64];
-    // K~^T: [..][128][64].
-    return size_t(nchunk_total) * v_heads * kC * (3 * kD + kC + 1);
+    // Per (chunk, value head), in f32 units: W, Q~ as bf16 (hi, lo) [2][64][128]
+    // (one f32 each per element pair), P [2][64][64] bf16, K~^T [2][128][64]
+    // bf16, Ut [64][128] f32, e^gamma [64] f32.
+    return size_t(nchunk_total) * v_heads * kC * (4 * kD + kC + 1);
 }
 
 cudaError_t launch_linear_prefill(const LinearPrefillLaunch &a, cudaStream_t stream) {
@@ -849,12 +835,13 @@ cudaError_t launch_linear_prefill(const LinearPrefillLaunch &a, cudaStream_t str
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
 
     const size_t per = size_t(a.nseq) * nchunk * a.v_heads;
-    float *w = a.scratch;
-    float *ut = w + per * kC * kD;
-    float *pm = ut + per * kC * kD;
-    float *eg = pm + per * kC * kC;
-    float *kt = eg + per * kC;
-    LocalParams lp{a.qkv, a.beta, a.alpha, w, ut, pm, eg, kt, a.count, nchunk, a.qk_heads,
+    __nv_bfloat16 *w2 = reinterpret_cast<__nv_bfloat16 *>(a.scratch);
+    __nv_bfloat16 *q2 = w2 + per * 2 * kC * kD;
+    __nv_bfloat16 *p2 = q2 + per * 2 * kC * kD;
+    __nv_bfloat16 *k2 = p2 + per * 2 * kC * kC;
+    float *ut = reinterpret_cast<float *>(k2 + per * 2 * kD * kC);
+    float *eg = ut + per * kC * kD;
+    LocalParams lp{a.qkv, a.beta, a.alpha, w2, q2, p2, k2, ut, eg, a.count, nchunk, a.qk_heads,
                    a.v_heads, qkv_dim};
     const size_t smem_l = size_t(2 * kC * kPad + 2 * kC * (kC + 1)) * sizeof(float);
     if ((e = cudaFuncSetAttribute(linear_prefill_local_kernel,
@@ -865,9 +852,10 @@ cudaError_t launch_linear_prefill(const LinearPrefillLaunch &a, cudaStream_t str
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
 
     CUtensorMap mw, mq, mp, mk;
-    if (!make_map_f32(&mw, w, kD, kC, per, kC) ||
-        !make_map_f32(&mq, a.qkv, qkv_dim, uint64_t(a.nseq) * a.count, 1, kC) ||
-        !make_map_f32(&mp, pm, kC, kC, per, kC) || !make_map_f32(&mk, kt, kC, kD, per, kD))
+    if (!make_map_bf16_ls(&mw, w2, kD, kC, 2 * per, kC) ||
+        !make_map_bf16_ls(&mq, q2, kD, kC, 2 * per, kC) ||
+        !make_map_bf16_ls(&mp, p2, kC, kC, 2 * per, kC) ||
+        !make_map_bf16_ls(&mk, k2, kC, kD, 2 * per, kD))
         return cudaErrorInvalidValue;
     StateTcParams sp{ut, eg, a.delta_state, a.attention, a.err, a.seq0, a.count, nchunk,
                      a.qk_heads, a.v_heads};

@@ -124,6 +124,14 @@ __device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
     return *reinterpret_cast<float2 *>(&r);
 }
 
+__device__ __forceinline__ float2 fmul2(float2 a, float2 b) {
+    uint64_t r;
+    asm("mul.rn.f32x2 %0, %1, %2;"
+        : "=l"(r)
+        : "l"(*reinterpret_cast<uint64_t *>(&a)), "l"(*reinterpret_cast<uint64_t *>(&b)));
+    return *reinterpret_cast<float2 *>(&r);
+}
+
 // bf16x2 (one 32-bit word) -> two floats, exactly.
 __device__ __forceinline__ float2 bf16x2_to_float2(uint32_t w) {
     float2 r;
