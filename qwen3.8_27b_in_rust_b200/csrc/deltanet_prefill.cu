@@ -165,11 +165,12 @@ struct LocalParams {
     int count, nchunk, qk_heads, v_heads, qkv_dim;
 };
 
-// x -> (hi, lo) as bf16 with hi = bf16(x), lo = bf16(x - hi): hi + lo keeps
-// ~16 bits of x's mantissa.
-__device__ __forceinline__ void split_bf16(float x, __nv_bfloat16 &hi, __nv_bfloat16 &lo) {
-    hi = __float2bfloat16_rn(x);
-    lo = __float2bfloat16_rn(x - __bfloat162float(hi));
+// (a, b) -> bf16x2 pairs hi = bf16(a, b), lo = bf16(a - hi.a, b - hi.b): hi + lo
+// keeps ~16 bits of each value's mantissa.
+__device__ __forceinline__ void split_bf16x2(float a, float b, uint32_t &hi, uint32_t &lo) {
+    hi = pack_bf16x2_rn(a, b);
+    const float2 hf = bf16x2_to_float2(hi);
+    lo = pack_bf16x2_rn(a - hf.x, b - hf.y);
 }
 
 constexpr int kPad = kD + 1;  // padded smem rows (bank-conflict-free column walks)
@@ -211,26 +212,43 @@ __global__ void __launch_bounds__(256, 2) linear_prefill_local_kernel(LocalParam
     // K K^T and Q K^T: thread (ty, tx) of a 16x16 grid owns rows 4ty..,
     // columns 4tx.. of both.
     const int ty = tid / 16, tx = tid % 16;
-    float akk[4][4] = {}, aqk[4][4] = {};
+    // Accumulators as column pairs (packed f32x2 fma, the same rounding as fmaf).
+    float2 akk2[4][2], aqk2[4][2];
+#pragma unroll
+    for (int a = 0; a < 4; ++a)
+#pragma unroll
+        for (int b = 0; b < 2; ++b) akk2[a][b] = aqk2[a][b] = make_float2(0.f, 0.f);
     if (tx <= ty) {  // only the lower triangle (c <= r) is used
 #pragma unroll 4
         for (int i = 0; i < kD; ++i) {
-            float kr[4], qr[4], kc[4];
+            float kr[4], qr[4];
+            float2 kc2[2];
 #pragma unroll
             for (int a = 0; a < 4; ++a) {
                 kr[a] = Ks[(4 * ty + a) * kPad + i];
                 qr[a] = Xs[(4 * ty + a) * kPad + i];
-                kc[a] = Ks[(4 * tx + a) * kPad + i];
             }
+            kc2[0] = make_float2(Ks[(4 * tx + 0) * kPad + i], Ks[(4 * tx + 1) * kPad + i]);
+            kc2[1] = make_float2(Ks[(4 * tx + 2) * kPad + i], Ks[(4 * tx + 3) * kPad + i]);
 #pragma unroll
             for (int a = 0; a < 4; ++a)
 #pragma unroll
-                for (int b = 0; b < 4; ++b) {
-                    akk[a][b] = fmaf(kr[a], kc[b], akk[a][b]);
-                    aqk[a][b] = fmaf(qr[a], kc[b], aqk[a][b]);
+                for (int b = 0; b < 2; ++b) {
+                    akk2[a][b] = ffma2(make_float2(kr[a], kr[a]), kc2[b], akk2[a][b]);
+                    aqk2[a][b] = ffma2(make_float2(qr[a], qr[a]), kc2[b], aqk2[a][b]);
                 }
         }
     }
+    float akk[4][4], aqk[4][4];
+#pragma unroll
+    for (int a = 0; a < 4; ++a)
+#pragma unroll
+        for (int b = 0; b < 2; ++b) {
+            akk[a][2 * b] = akk2[a][b].x;
+            akk[a][2 * b + 1] = akk2[a][b].y;
+            aqk[a][2 * b] = aqk2[a][b].x;
+            aqk[a][2 * b + 1] = aqk2[a][b].y;
+        }
 
     for (int h = kh; h < p.v_heads; h += p.qk_heads) {
         const size_t plane = (size_t(s) * p.nchunk + chunk) * p.v_heads + h;
@@ -266,14 +284,22 @@ __global__ void __launch_bounds__(256, 2) linear_prefill_local_kernel(LocalParam
         {
             __nv_bfloat16 *ph = p.p2 + plane * 2 * kC * kC, *pl = ph + kC * kC;
 #pragma unroll
-            for (int a = 0; a < 4; ++a)
+            for (int a = 0; a < 4; ++a) {
+                const int r = 4 * ty + a;
+                float pv[4];
 #pragma unroll
                 for (int b = 0; b < 4; ++b) {
-                    const int r = 4 * ty + a, c = 4 * tx + b;
+                    const int c = 4 * tx + b;
                     const float d = (c <= r) ? expf(gam[r] - gam[c]) : 0.f;
                     As[r * (kC + 1) + c] = c < r ? bet[r] * d * akk[a][b] : 0.f;
-                    split_bf16(c <= r ? d * aqk[a][b] : 0.f, ph[r * kC + c], pl[r * kC + c]);
+                    pv[b] = c <= r ? d * aqk[a][b] : 0.f;
                 }
+                uint2 hv, lv;
+                split_bf16x2(pv[0], pv[1], hv.x, lv.x);
+                split_bf16x2(pv[2], pv[3], hv.y, lv.y);
+                *reinterpret_cast<uint2 *>(ph + r * kC + 4 * tx) = hv;
+                *reinterpret_cast<uint2 *>(pl + r * kC + 4 * tx) = lv;
+            }
         }
         __syncthreads();
 
@@ -329,39 +355,47 @@ __global__ void __launch_bounds__(256, 2) linear_prefill_local_kernel(LocalParam
         const size_t wbase = plane * kC * kD;
         const int rb = tid / 32, cg = tid % 32;
         auto tri_times = [&](const float *X, const float *scale_b, auto &&store) {
-            float acc[8][4] = {};
+            float2 acc[8][2];
+#pragma unroll
+            for (int a = 0; a < 8; ++a) acc[a][0] = acc[a][1] = make_float2(0.f, 0.f);
             const int mend = rb * 8 + 8;
 #pragma unroll 4
             for (int m = 0; m < mend; ++m) {
                 const float f = bet[m] * (scale_b ? scale_b[m] : 1.f);
-                float x[4];
-#pragma unroll
-                for (int b = 0; b < 4; ++b) x[b] = X[m * kPad + cg * 4 + b] * f;
+                const float *xr = X + m * kPad + cg * 4;
+                const float2 x0 = make_float2(xr[0] * f, xr[1] * f);
+                const float2 x1 = make_float2(xr[2] * f, xr[3] * f);
 #pragma unroll
                 for (int a = 0; a < 8; ++a) {
                     const float tv = Ts[(rb * 8 + a) * (kC + 1) + m];
-#pragma unroll
-                    for (int b = 0; b < 4; ++b) acc[a][b] = fmaf(tv, x[b], acc[a][b]);
+                    acc[a][0] = ffma2(make_float2(tv, tv), x0, acc[a][0]);
+                    acc[a][1] = ffma2(make_float2(tv, tv), x1, acc[a][1]);
                 }
             }
 #pragma unroll
-            for (int a = 0; a < 8; ++a) store(rb * 8 + a, cg, acc[a]);
+            for (int a = 0; a < 8; ++a) {
+                const float v[4] = {acc[a][0].x, acc[a][0].y, acc[a][1].x, acc[a][1].y};
+                store(rb * 8 + a, cg, v);
+            }
         };
         // W as bf16 (hi, lo).
         __nv_bfloat16 *wh = p.w2 + plane * 2 * kC * kD, *wl = wh + kC * kD;
         tri_times(Ks, egs, [&](int r, int c4, const float (&v)[4]) {
-            __align__(8) __nv_bfloat16 h4[4], l4[4];
-#pragma unroll
-            for (int b = 0; b < 4; ++b) split_bf16(v[b], h4[b], l4[b]);
-            *reinterpret_cast<uint2 *>(wh + r * kD + c4 * 4) = *reinterpret_cast<const uint2 *>(h4);
-            *reinterpret_cast<uint2 *>(wl + r * kD + c4 * 4) = *reinterpret_cast<const uint2 *>(l4);
+            uint2 hv, lv;
+            split_bf16x2(v[0], v[1], hv.x, lv.x);
+            split_bf16x2(v[2], v[3], hv.y, lv.y);
+            *reinterpret_cast<uint2 *>(wh + r * kD + c4 * 4) = hv;
+            *reinterpret_cast<uint2 *>(wl + r * kD + c4 * 4) = lv;
         });
         // K~^T[i][r] = e^{gamma_C - gamma_r} K[r][i] (the state update's B operand).
         {
             __nv_bfloat16 *kth = p.k2 + plane * 2 * kD * kC, *ktl = kth + kD * kC;
-            for (int idx = tid; idx < kD * kC; idx += 256) {
-                const int i = idx / kC, r = idx % kC;
-                split_bf16(dec[r] * Ks[r * kPad + i], kth[idx], ktl[idx]);
+            for (int idx = tid; idx < kD * kC / 2; idx += 256) {
+                const int i = idx / (kC / 2), r = 2 * (idx % (kC / 2));
+                uint32_t hv, lv;
+                split_bf16x2(dec[r] * Ks[r * kPad + i], dec[r + 1] * Ks[(r + 1) * kPad + i], hv, lv);
+                reinterpret_cast<uint32_t *>(kth)[idx] = hv;
+                reinterpret_cast<uint32_t *>(ktl)[idx] = lv;
             }
         }
         // Q~ = diag(e^gamma) Q (Q re-read from the normalised qkv rows).
@@ -374,13 +408,11 @@ __global__ void __launch_bounds__(256, 2) linear_prefill_local_kernel(LocalParam
                     q = reinterpret_cast<const float4 *>(
                         p.qkv + (size_t(s) * p.count + t0 + r) * p.qkv_dim + kh * kD)[c4];
                 const float e = egs[r];
-                __align__(8) __nv_bfloat16 h4[4], l4[4];
-                split_bf16(q.x * e, h4[0], l4[0]);
-                split_bf16(q.y * e, h4[1], l4[1]);
-                split_bf16(q.z * e, h4[2], l4[2]);
-                split_bf16(q.w * e, h4[3], l4[3]);
-                *reinterpret_cast<uint2 *>(qh + r * kD + c4 * 4) = *reinterpret_cast<const uint2 *>(h4);
-                *reinterpret_cast<uint2 *>(ql + r * kD + c4 * 4) = *reinterpret_cast<const uint2 *>(l4);
+                uint2 hv, lv;
+                split_bf16x2(q.x * e, q.y * e, hv.x, lv.x);
+                split_bf16x2(q.z * e, q.w * e, hv.y, lv.y);
+                *reinterpret_cast<uint2 *>(qh + r * kD + c4 * 4) = hv;
+                *reinterpret_cast<uint2 *>(ql + r * kD + c4 * 4) = lv;
             }
         }
         if (tid < kC) p.eg_out[plane * kC + tid] = egs[tid];
