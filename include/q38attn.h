@@ -126,6 +126,18 @@ int q38_state_destroy(q38_state *st);
 /* Zeroes all caches and recurrent state (Q38ModelOps::reset). */
 int q38_state_reset(q38_state *st, void *stream);
 
+/* Speculative-decoding rollback (checkpoint_state / restore_target_state,
+ * src/model/ops.rs:1627-1647): q38_state_checkpoint copies the recurrent state
+ * (conv and delta state of every DeltaNet slot) of sequences
+ * [seq0, seq0 + nseq) into the state's checkpoint area on the device, and
+ * q38_state_restore copies it back. The KV cache is not copied: as in the
+ * reference, cache rows past the restored position are overwritten when the
+ * committed tokens are re-run. The first checkpoint allocates the checkpoint
+ * area (the size of the recurrent state); restoring sequences that were never
+ * checkpointed is Q38_ERR_ARG. Device-to-device copies ordered on `stream`. */
+int q38_state_checkpoint(q38_state *st, int seq0, int nseq, void *stream);
+int q38_state_restore(q38_state *st, int seq0, int nseq, void *stream);
+
 /* Reads and clears the device error bits (synchronises the device). */
 int q38_state_errors(q38_state *st, int *bits);
 

@@ -10,6 +10,7 @@
 
 #include <map>
 #include <string>
+#include <vector>
 
 #include "../../include/q38attn.h"
 
@@ -71,6 +72,9 @@ struct q38_state {
     size_t prefill_tokens = 0;
     float *prefill_lin = nullptr;        // chunked DeltaNet scratch
     size_t prefill_chunks = 0;           // chunk capacity of prefill_lin
+    float *ckpt_conv = nullptr;          // checkpoint copies of conv_state / delta_state
+    float *ckpt_delta = nullptr;
+    std::vector<char> ckpt_valid;        // per sequence: has a checkpoint
     float *prefill_stage = nullptr;      // device staging of the *_prefill_host forms
     size_t prefill_stage_tokens = 0;     // tokens (all sequences) one staged piece holds
     // staging for the host-pointer calls (device, sized for `batch`)

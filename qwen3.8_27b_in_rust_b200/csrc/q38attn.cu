@@ -167,6 +167,8 @@ void free_state(q38_state *st) {
     cudaFree(st->prefill_v16);
     cudaFree(st->prefill_lin);
     cudaFree(st->prefill_stage);
+    cudaFree(st->ckpt_conv);
+    cudaFree(st->ckpt_delta);
 }
 
 // Validates a decode call and fills the launch arguments (device pointers).
@@ -442,6 +444,64 @@ int q38_state_reset(q38_state *st, void *stream) {
         Q38_CUDA(cudaMemsetAsync(st->delta_state, 0, n * delta_seq_floats(st->ctx) * 4, s));
     }
     return Q38_OK;
+}
+
+namespace {
+
+// Copies sequences [seq0, seq0+nseq) of every DeltaNet slot between the state
+// arrays and the checkpoint arrays: one strided copy per array (rows = slots).
+int copy_recurrent(q38_state *st, int seq0, int nseq, bool to_checkpoint, cudaStream_t s) {
+    const q38_ctx *ctx = st->ctx;
+    const size_t rows = size_t(st->linear_slots);
+    const size_t cs = conv_seq_floats(ctx) * 4, ds = delta_seq_floats(ctx) * 4;
+    float *c_src = to_checkpoint ? st->conv_state : st->ckpt_conv;
+    float *c_dst = to_checkpoint ? st->ckpt_conv : st->conv_state;
+    float *d_src = to_checkpoint ? st->delta_state : st->ckpt_delta;
+    float *d_dst = to_checkpoint ? st->ckpt_delta : st->delta_state;
+    const size_t c_off = size_t(seq0) * cs, d_off = size_t(seq0) * ds;
+    Q38_CUDA(cudaMemcpy2DAsync(reinterpret_cast<char *>(c_dst) + c_off, st->batch * cs,
+                               reinterpret_cast<const char *>(c_src) + c_off, st->batch * cs,
+                               size_t(nseq) * cs, rows, cudaMemcpyDeviceToDevice, s));
+    Q38_CUDA(cudaMemcpy2DAsync(reinterpret_cast<char *>(d_dst) + d_off, st->batch * ds,
+                               reinterpret_cast<const char *>(d_src) + d_off, st->batch * ds,
+                               size_t(nseq) * ds, rows, cudaMemcpyDeviceToDevice, s));
+    return Q38_OK;
+}
+
+int check_seq_range(const q38_state *st, int seq0, int nseq) {
+    if (nseq <= 0 || seq0 < 0 || seq0 + nseq > st->batch)
+        return fail(Q38_ERR_ARG, "sequences [%d, %d) outside the state's %d", seq0, seq0 + nseq,
+                    st->batch);
+    return Q38_OK;
+}
+
+}  // namespace
+
+int q38_state_checkpoint(q38_state *st, int seq0, int nseq, void *stream) {
+    if (!st) return fail(Q38_ERR_ARG, "null state");
+    if (int rc = check_seq_range(st, seq0, nseq)) return rc;
+    if (st->linear_slots == 0) return Q38_OK;  // no recurrent state to keep
+    DeviceGuard guard(st->ctx->device);
+    if (!st->ckpt_conv) {
+        const size_t n = size_t(st->linear_slots) * st->batch;
+        Q38_CUDA(cudaMalloc(&st->ckpt_conv, n * conv_seq_floats(st->ctx) * 4));
+        Q38_CUDA(cudaMalloc(&st->ckpt_delta, n * delta_seq_floats(st->ctx) * 4));
+        st->ckpt_valid.assign(size_t(st->batch), 0);
+    }
+    if (int rc = copy_recurrent(st, seq0, nseq, true, static_cast<cudaStream_t>(stream))) return rc;
+    for (int b = seq0; b < seq0 + nseq; ++b) st->ckpt_valid[size_t(b)] = 1;
+    return Q38_OK;
+}
+
+int q38_state_restore(q38_state *st, int seq0, int nseq, void *stream) {
+    if (!st) return fail(Q38_ERR_ARG, "null state");
+    if (int rc = check_seq_range(st, seq0, nseq)) return rc;
+    if (st->linear_slots == 0) return Q38_OK;
+    for (int b = seq0; b < seq0 + nseq; ++b)
+        if (st->ckpt_conv == nullptr || !st->ckpt_valid[size_t(b)])
+            return fail(Q38_ERR_ARG, "sequence %d has no checkpoint to restore", b);
+    DeviceGuard guard(st->ctx->device);
+    return copy_recurrent(st, seq0, nseq, false, static_cast<cudaStream_t>(stream));
 }
 
 int q38_state_errors(q38_state *st, int *bits) {

@@ -181,6 +181,18 @@ class State:
     def reserve_prefill(self, max_tokens: int) -> None:
         check(self._lib.q38_state_reserve_prefill(self.handle, max_tokens))
 
+    def checkpoint(self, seq0: int = 0, nseq: Optional[int] = None, stream=None) -> None:
+        """Keep the recurrent (conv + delta) state of sequences [seq0, seq0+nseq)
+        for a later restore (checkpoint_state, src/model/ops.rs:1627-1640)."""
+        nseq = self.batch - seq0 if nseq is None else nseq
+        check(self._lib.q38_state_checkpoint(self.handle, seq0, nseq, _stream_ptr(stream)))
+
+    def restore(self, seq0: int = 0, nseq: Optional[int] = None, stream=None) -> None:
+        """Roll the recurrent state of sequences [seq0, seq0+nseq) back to their
+        checkpoint (restore_target_state, src/model/ops.rs:1642-1647)."""
+        nseq = self.batch - seq0 if nseq is None else nseq
+        check(self._lib.q38_state_restore(self.handle, seq0, nseq, _stream_ptr(stream)))
+
     def kv_views(self, layer: int):
         """Zero-copy torch views of one KV slot, [batch][kv_heads][context][256]
         (bf16 or f32), for bulk device-side initialisation."""

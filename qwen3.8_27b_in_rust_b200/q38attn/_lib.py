@@ -79,6 +79,8 @@ SIGNATURES = {
     "q38_full_decode_noalloc": (c_int, [_VP, _VP, _VP, _VP, c_int, c_int, c_int, _VP, _VP, _VP,
                                         _VP, c_int, _VP, _VP, _VP]),
     "q38_state_reserve_prefill": (c_int, [_VP, c_int]),
+    "q38_state_checkpoint": (c_int, [_VP, c_int, c_int, _VP]),
+    "q38_state_restore": (c_int, [_VP, c_int, c_int, _VP]),
     "q38_full_prefill": (c_int, [_VP, _VP, c_int, c_int, c_int, c_int, c_int, _VP, _VP, _VP, _VP,
                                  _VP]),
     "q38_linear_prefill": (c_int, [_VP, _VP, c_int, c_int, c_int, c_int, _VP, _VP, _VP, _VP,
