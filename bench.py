@@ -639,8 +639,8 @@ def run_ours(args) -> None:
             "gpu_launches": 9 * args.steps,  # decode timed region (prefill timed separately)
             "clocks": clocks.summary(),
         }
+        tpeak, tpeak_kind = load_tensor_peak()
         if prefill:
-            tpeak, tpeak_kind = load_tensor_peak()
             flops = prefill_flops(args.prefill_batch, args.prefill_len) * world
             tflops = flops / (prefill_ms * 1e-3) / 1e12
             line["prefill"] = {
@@ -651,7 +651,7 @@ def run_ours(args) -> None:
                 "roofline": {"bound": "tensor", "achieved": tflops, "peak": tpeak,
                              "unit": "TFLOP/s", "frac": tflops / tpeak,
                              "peak_source": f"{tpeak_kind} bf16_tflops (burst)",
-                             "kernel": "prep + attn_prefill (one op)"},
+                             "kernel": "prep + attn_prefill_pair (one op)"},
             }
         if split:
             kv_bytes = args.split_context * 4 * 256 * 2 * 2
@@ -665,12 +665,24 @@ def run_ours(args) -> None:
         if lin_prefill:
             flops = linear_prefill_flops(args.prefill_batch, args.prefill_len) * world
             toks = args.prefill_batch * args.prefill_len * world
+            # Config 5's stated per-token traffic (~45 KB: q/k/v/z/gates in, output
+            # out, f32) and the WY-form FLOPs; the path is mixed-bound, so both
+            # fractions are reported.
+            lp_bytes = toks * 45 * 1024
             line["deltanet_prefill"] = {
                 "workload": (f"config5: {args.prefill_batch} x {args.prefill_len}-token chunked "
                              "Gated DeltaNet prefill per GPU (C=64, 16K/48V x 128) from a zero "
-                             "state, outputs + final f32 state; chunk-local WY terms on f32 CUDA cores, state pass on tcgen05 split-tf32 (3 products, ~f32 accuracy)"),
+                             "state, outputs + final f32 state; chunk-local WY terms on f32 CUDA "
+                             "cores, state pass on tcgen05 with bf16 hi/lo operand pairs "
+                             "(3 products, ~1e-5 of the per-token recurrence)"),
                 "ms": lin_prefill_ms, "tok_s": toks / (lin_prefill_ms * 1e-3),
                 "flops": flops, "tflops": flops / (lin_prefill_ms * 1e-3) / 1e12,
+                "roofline": {
+                    "bound": "mixed",
+                    "tensor_frac": flops / (lin_prefill_ms * 1e-3) / 1e12 / tpeak,
+                    "hbm_frac": lp_bytes / (lin_prefill_ms * 1e-3) / 1e9 / peak,
+                    "peak_tflops": tpeak, "peak_gbs": peak,
+                },
             }
         if e2e:
             line["e2e"] = {"value": tokens * e2e_steps / e2e_s, "unit": "tok/s",
