@@ -648,10 +648,12 @@ def run_ours(args) -> None:
                              "prefill per GPU, 24Q/4KV x 256, RoPE 64, sigmoid gate; "
                              "QK^T bf16, PV f16, f32 accumulate (tcgen05)"),
                 "ms": prefill_ms, "flops": flops, "tflops": tflops,
-                "roofline": {"bound": "tensor", "achieved": tflops, "peak": tpeak,
-                             "unit": "TFLOP/s", "frac": tflops / tpeak,
+                # Per GPU: every rank runs the same prefill, so one GPU's rate is
+                # the whole-job rate over the ranks.
+                "roofline": {"bound": "tensor", "achieved": tflops / world, "peak": tpeak,
+                             "unit": "TFLOP/s", "frac": tflops / world / tpeak,
                              "peak_source": f"{tpeak_kind} bf16_tflops (burst)",
-                             "kernel": "prep + attn_prefill_pair (one op)"},
+                             "kernel": "prep + attn_prefill_pair (one op), per GPU"},
             }
         if split:
             kv_bytes = args.split_context * 4 * 256 * 2 * 2
@@ -679,8 +681,8 @@ def run_ours(args) -> None:
                 "flops": flops, "tflops": flops / (lin_prefill_ms * 1e-3) / 1e12,
                 "roofline": {
                     "bound": "mixed",
-                    "tensor_frac": flops / (lin_prefill_ms * 1e-3) / 1e12 / tpeak,
-                    "hbm_frac": lp_bytes / (lin_prefill_ms * 1e-3) / 1e9 / peak,
+                    "tensor_frac": flops / world / (lin_prefill_ms * 1e-3) / 1e12 / tpeak,
+                    "hbm_frac": lp_bytes / world / (lin_prefill_ms * 1e-3) / 1e9 / peak,
                     "peak_tflops": tpeak, "peak_gbs": peak,
                 },
             }
