@@ -135,21 +135,24 @@ def run_prefill(args, ctx, q38attn, synth, torch, rank: int) -> dict:
     stream = torch.cuda.current_stream()
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
            for _ in range(args.prefill_iters)]
-    for it in range(2 + args.prefill_iters):
+    for it in range(2):
         key.copy_(key0)  # key is rewritten in place (RMSNorm + RoPE)
-        if it >= 2:
-            evs[it - 2][0].record(stream)
         ctx.full_prefill(st, layer, 0, qg, key, val, att, 0, stream=stream)
-        if it >= 2:
-            evs[it - 2][1].record(stream)
     torch.cuda.synchronize()
+    with ClockSampler(torch.cuda.current_device(), period_s=0.002) as clocks:
+        for it in range(args.prefill_iters):
+            key.copy_(key0)
+            evs[it][0].record(stream)
+            ctx.full_prefill(st, layer, 0, qg, key, val, att, 0, stream=stream)
+            evs[it][1].record(stream)
+        torch.cuda.synchronize()
     if st.errors():
         raise RuntimeError("device error bits set during prefill")
     ms = statistics.median(a.elapsed_time(b) for a, b in evs)
     st.close()
     del qg, key0, val, key, att
     torch.cuda.empty_cache()
-    return {"ms": ms}
+    return {"ms": ms, "clocks": clocks.summary()}
 
 
 def linear_prefill_flops(batch: int, seq: int) -> float:
@@ -179,24 +182,31 @@ def run_linear_prefill(args, ctx, q38attn, torch, rank: int) -> dict:
     stream = torch.cuda.current_stream()
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
            for _ in range(args.prefill_iters)]
-    for it in range(2 + args.prefill_iters):
+    def one(it):
         st.reset(stream)  # a fresh prompt each time (zero conv and delta state)
         qkv.copy_(qkv0)   # qkv/beta/alpha are rewritten in place
         beta.copy_(b0)
         alpha.copy_(a0)
-        if it >= 2:
-            evs[it - 2][0].record(stream)
+        if it >= 0:
+            evs[it][0].record(stream)
         ctx.linear_prefill(st, layer, 0, qkv, z, beta, alpha, att, stream=stream)
-        if it >= 2:
-            evs[it - 2][1].record(stream)
+        if it >= 0:
+            evs[it][1].record(stream)
+
+    one(-1)
+    one(-1)
     torch.cuda.synchronize()
+    with ClockSampler(torch.cuda.current_device(), period_s=0.002) as clocks:
+        for it in range(args.prefill_iters):
+            one(it)
+        torch.cuda.synchronize()
     if st.errors():
         raise RuntimeError("device error bits set during DeltaNet prefill")
     ms = statistics.median(a.elapsed_time(b) for a, b in evs)
     st.close()
     del qkv0, z, b0, a0, qkv, beta, alpha, att
     torch.cuda.empty_cache()
-    return {"ms": ms}
+    return {"ms": ms, "clocks": clocks.summary()}
 
 
 def run_split_sequence(args, ctx, q38attn, torch, dist, rank: int, world: int) -> dict:
@@ -654,6 +664,7 @@ def run_ours(args) -> None:
                              "unit": "TFLOP/s", "frac": tflops / world / tpeak,
                              "peak_source": f"{tpeak_kind} bf16_tflops (burst)",
                              "kernel": "prep + attn_prefill_pair (one op), per GPU"},
+                "clocks": prefill["clocks"],
             }
         if split:
             kv_bytes = args.split_context * 4 * 256 * 2 * 2
@@ -685,6 +696,7 @@ def run_ours(args) -> None:
                     "hbm_frac": lp_bytes / world / (lin_prefill_ms * 1e-3) / 1e9 / peak,
                     "peak_tflops": tpeak, "peak_gbs": peak,
                 },
+                "clocks": lin_prefill["clocks"],
             }
         if e2e:
             line["e2e"] = {"value": tokens * e2e_steps / e2e_s, "unit": "tok/s",

@@ -187,8 +187,6 @@ __global__ void __launch_bounds__(256) attn_prefill_prefix_kernel(PrefixParams p
 // P2: attention
 // --------------------------------------------------------------------------
 struct PrefillParams {
-    const float *q_and_gate;
-    float *attention;  // [nseq][count][heads*256]
     int *err;
     int seq0, count, base, heads, kv_heads, n_qtiles;
 };
@@ -242,7 +240,19 @@ struct __align__(8) PairBarriers {
     uint64_t q_full;
     uint64_t k_full[kPairStagesK], k_empty[kPairStagesK], v_full[kPairStagesV], v_empty[kPairStagesV];
     uint64_t s_full[kPairSBuf], p_full[kPairSBuf], s_free[kPairSBuf], o_final;
+    uint64_t gate_full, epi_l, epi_done;
 };
+
+// Epilogue staging: the gate block of the CTA's 128 rows (f32) lands by TMA
+// over the Q and K-ring region, free once the last S = Q K^T has completed,
+// as eight 32-column boxes of 128 rows x 128 B (128-byte swizzle); the output
+// O / l * sigmoid(gate) is written over it in place and stored by TMA.
+constexpr int kEpiBoxCols = 32;
+constexpr uint32_t kEpiBoxBytes = kBlockQ * kEpiBoxCols * 4;  // 16 KB
+constexpr int kEpiBoxes = kAttnHeadDim / kEpiBoxCols;          // 8
+static_assert(kEpiBoxes * kEpiBoxBytes == kQBytes + kPairStagesK * kKHalf,
+              "the gate block fills the Q and K-ring region exactly");
+constexpr int kGatePrefetchTiles = 8;  // L2 prefetch of the gate this many key tiles early
 
 // Arrival on a barrier of the leader CTA (cluster address), ordered like the
 // local tcgen05 handshakes (tcgen05.wait + fence::before_thread_sync first).
@@ -253,7 +263,9 @@ __device__ __forceinline__ void mbar_arrive_leader(uint32_t cluster_bar) {
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsPF, 1)
     attn_prefill_pair_kernel(const __grid_constant__ CUtensorMap map_q,
                              const __grid_constant__ CUtensorMap map_k,
-                             const __grid_constant__ CUtensorMap map_v, PrefillParams p) {
+                             const __grid_constant__ CUtensorMap map_v,
+                             const __grid_constant__ CUtensorMap map_g,
+                             const __grid_constant__ CUtensorMap map_o, PrefillParams p) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char *smem =
         reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -263,6 +275,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsPF, 1)
     __shared__ PairBarriers bar;
     __shared__ uint32_t tmem_base_s;
     __shared__ volatile int abort_flag;
+    __shared__ float inv_l_s[kBlockQ];
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t rank = cluster_ctarank();
@@ -275,6 +288,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsPF, 1)
     const int q_rows = min(kBlockQ, p.count - q0);        // may be <= 0 for the peer
     const int kend = p.base + min(pair * kPairRows + kPairRows, p.count);
     const int nkt = (kend + kBlockK - 1) / kBlockK;
+    const bool has_rows = q_rows > 0;
 
     if (threadIdx.x == 0) {
         abort_flag = 0;
@@ -293,6 +307,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsPF, 1)
             mbar_init(&bar.s_free[b], 1);
         }
         mbar_init(&bar.o_final, 1);
+        mbar_init(&bar.gate_full, 1);
+        mbar_init(&bar.epi_l, 4);     // the four softmax warps
+        mbar_init(&bar.epi_done, 8);  // the eight epilogue warps
         fence_barrier_init();
     }
     if (warp == 1) {
@@ -321,11 +338,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsPF, 1)
             const uint32_t qfull = cluster_addr(&bar.q_full, 0);
             for (int cb = 0; cb < 4; ++cb)
                 tma_load_3d_pair(sQ + cb * (kQBytes / 4), &map_q, cb * 64, q0, qrow, qfull);
-            for (int j = 0; j < nkt && !abort_flag; ++j) {
+            const int gate_x = kAttnHeadDim;  // the gate half of each head's 512 values
+            bool ok = true;
+            for (int j = 0; j < nkt; ++j) {
                 const int b = j % kPairStagesK;
                 if (j >= kPairStagesK &&
                     !mbar_wait(&bar.k_empty[b], uint32_t(j / kPairStagesK - 1) & 1u)) {
-                    fail();
+                    ok = false;
                     break;
                 }
                 if (leader) mbar_arrive_expect_tx(&bar.k_full[b], 2 * kKHalf);
@@ -333,6 +352,25 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsPF, 1)
                 for (int cb = 0; cb < 4; ++cb)
                     tma_load_3d_pair(sK + b * kKHalf + cb * (kKHalf / 4), &map_k, cb * 64,
                                      j * kBlockK + int(rank) * (kBlockK / 2), kplane, full);
+                if (has_rows && j == max(nkt - kGatePrefetchTiles, 0))
+                    for (int cb = 0; cb < kEpiBoxes; ++cb)
+                        tma_prefetch_4d(&map_g, gate_x + cb * kEpiBoxCols, h, q0, s);
+                if (abort_flag) { ok = false; break; }
+            }
+            // The gate block replaces Q and the K ring once the last two S = Q K^T
+            // (one per issuing warp) have completed. Tile j's completion is phase
+            // j / 4 of k_empty[j % 4], whose earlier phases this thread waited for
+            // before loading tile j, so the parity waits are exact.
+            for (int j = max(nkt - 2, 0); ok && j < nkt; ++j)
+                if (!mbar_wait(&bar.k_empty[j % kPairStagesK], uint32_t(j / kPairStagesK) & 1u))
+                    ok = false;
+            if (!ok) {
+                fail();
+            } else if (has_rows) {
+                mbar_arrive_expect_tx(&bar.gate_full, kEpiBoxes * kEpiBoxBytes);
+                for (int cb = 0; cb < kEpiBoxes; ++cb)
+                    tma_load_4d(smem + cb * kEpiBoxBytes, &map_g, gate_x + cb * kEpiBoxCols, h, q0, s,
+                                &bar.gate_full);
             }
         }
     } else if (warp == 7) {
@@ -510,34 +548,67 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsPF, 1)
             if (lane == 0) mbar_arrive_leader(cluster_addr(&bar.p_full[b], 0));
             if (__any_sync(0xffffffffu, abort_flag != 0)) { ok = false; break; }
         }
-        if (ok && !wait_all(&bar.o_final, 0)) ok = false;
+        // Publish 1/l for the epilogue warps that do not hold it.
         if (ok) {
-            fence_after_sync();
-            const float inv_l = 1.0f / l;
-            const bool store = r < q_rows;
-            const size_t tok = size_t(s) * p.count + min(t, p.count - 1);
-            const float *gate = p.q_and_gate + (tok * p.heads + h) * 2 * kAttnHeadDim + kAttnHeadDim;
-            float *out = p.attention + (tok * p.heads + h) * kAttnHeadDim;
-#pragma unroll 1
-            for (int c = 0; c < kAttnHeadDim; c += 32) {
-                uint32_t o[32];
-                tmem_ld32(tmem + lane_addr + kPairColO + c, o);
-                tmem_wait_ld();
-                if (store) {
-#pragma unroll
-                    for (int i = 0; i < 32; i += 4) {
-                        const float4 g = *reinterpret_cast<const float4 *>(gate + c + i);
-                        float4 y;
-                        y.x = __uint_as_float(o[i + 0]) * inv_l * sigmoid_fast(g.x);
-                        y.y = __uint_as_float(o[i + 1]) * inv_l * sigmoid_fast(g.y);
-                        y.z = __uint_as_float(o[i + 2]) * inv_l * sigmoid_fast(g.z);
-                        y.w = __uint_as_float(o[i + 3]) * inv_l * sigmoid_fast(g.w);
-                        *reinterpret_cast<float4 *>(out + c + i) = y;
-                    }
-                }
-            }
+            inv_l_s[r] = 1.0f / l;
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bar.epi_l);
         } else if (lane == 0) {
             fail();
+        }
+    }
+    __syncwarp();
+
+    // ---------------------------------------------------------------- epilogue
+    // Warps 0-7 (TMEM lane quarter warp % 4; warps 2-5 columns 0-127, the
+    // others 128-255): out = O / l * sigmoid(gate) in place over the staged
+    // gate block, then one thread stores the block by TMA.
+    if (warp < 8 && has_rows) {
+        const int quarter = warp & 3;
+        const int r = quarter * 32 + lane;
+        const int cb0 = (warp >= 2 && warp <= 5) ? 0 : kEpiBoxes / 2;
+        auto wait_all = [&](uint64_t *b, uint32_t parity) {
+            return __all_sync(0xffffffffu, mbar_wait(b, parity));
+        };
+        const bool ready =
+            wait_all(&bar.o_final, 0) && wait_all(&bar.epi_l, 0) && wait_all(&bar.gate_full, 0);
+        if (ready) {
+            fence_after_sync();
+            const float inv_l = inv_l_s[r];
+            const uint32_t lane_addr = uint32_t(quarter * 32) << 16;
+#pragma unroll 1
+            for (int cb = cb0; cb < cb0 + kEpiBoxes / 2; ++cb) {
+                uint32_t o[32];
+                tmem_ld32(tmem + lane_addr + kPairColO + cb * kEpiBoxCols, o);
+                tmem_wait_ld();
+                unsigned char *row = smem + cb * kEpiBoxBytes + r * 128;
+#pragma unroll
+                for (int c = 0; c < kEpiBoxCols / 4; ++c) {
+                    float4 *pg = reinterpret_cast<float4 *>(row + ((c ^ (r & 7)) << 4));
+                    const float4 g = *pg;
+                    float4 y;
+                    y.x = __uint_as_float(o[4 * c + 0]) * inv_l * sigmoid_fast(g.x);
+                    y.y = __uint_as_float(o[4 * c + 1]) * inv_l * sigmoid_fast(g.y);
+                    y.z = __uint_as_float(o[4 * c + 2]) * inv_l * sigmoid_fast(g.z);
+                    y.w = __uint_as_float(o[4 * c + 3]) * inv_l * sigmoid_fast(g.w);
+                    *pg = y;
+                }
+            }
+            fence_proxy_async_smem();  // the TMA store reads these writes
+        } else if (lane == 0) {
+            fail();
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bar.epi_done);
+        if (warp == 0 && lane == 0) {
+            if (!mbar_wait(&bar.epi_done, 0)) {
+                fail();
+            } else if (!abort_flag) {
+                for (int cb = 0; cb < kEpiBoxes; ++cb)
+                    tma_store_4d(&map_o, cb * kEpiBoxCols, h, q0, s, smem + cb * kEpiBoxBytes);
+                bulk_commit_group();
+                bulk_wait_group_read0();
+            }
         }
     }
 
@@ -575,6 +646,23 @@ bool make_map_16(CUtensorMap *m, const void *base, CUtensorMapDataType type, uin
                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// 4-D map of f32 over [nseq][count][heads][width] (row stride `width`) with a
+// box of 32 x 1 x 128 x 1 and 128-byte swizzle: the gate half of q_and_gate
+// (width 512) for loads, the attention output (width 256) for stores. Rows
+// past `count` fall outside the map, so loads read zeros and stores skip them.
+bool make_map_rows_f32(CUtensorMap *m, const void *base, uint64_t width, uint64_t heads,
+                       uint64_t count, uint64_t nseq) {
+    auto enc = encode_tiled();
+    if (!enc) return false;
+    cuuint64_t dims[4] = {width, heads, count, nseq};
+    cuuint64_t strides[3] = {width * 4, width * 4 * heads, width * 4 * heads * count};
+    cuuint32_t box[4] = {uint32_t(kEpiBoxCols), 1, uint32_t(kBlockQ), 1};
+    cuuint32_t es[4] = {1, 1, 1, 1};
+    return enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, const_cast<void *>(base), dims, strides, box,
+               es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 }  // namespace
 
 cudaError_t launch_attn_prefill(const AttnPrefillLaunch &a, cudaStream_t stream) {
@@ -591,8 +679,12 @@ cudaError_t launch_attn_prefill(const AttnPrefillLaunch &a, cudaStream_t stream)
     attn_prefill_prep_kernel<<<dim3(a.count, a.nseq), kPrepWarps * 32, 0, stream>>>(pp);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
 
-    CUtensorMap mq, mk, mv;
-    if (!make_map_16(&mq, a.qp, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, uint64_t(a.count),
+    CUtensorMap mq, mk, mv, mg, mo;
+    if (!make_map_rows_f32(&mg, a.q_and_gate, 2 * kAttnHeadDim, uint64_t(a.heads), uint64_t(a.count),
+                           uint64_t(a.nseq)) ||
+        !make_map_rows_f32(&mo, a.attention, kAttnHeadDim, uint64_t(a.heads), uint64_t(a.count),
+                           uint64_t(a.nseq)) ||
+        !make_map_16(&mq, a.qp, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, uint64_t(a.count),
                      uint64_t(a.nseq) * a.heads, kBlockQ) ||
         !make_map_16(&mk, a.kcache, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, uint64_t(a.context_length),
                      uint64_t(a.batch) * a.kv_heads, kBlockK / 2) ||
@@ -602,8 +694,7 @@ cudaError_t launch_attn_prefill(const AttnPrefillLaunch &a, cudaStream_t stream)
 
     const int n_qtiles = (a.count + kBlockQ - 1) / kBlockQ;
     const int n_pairs = (n_qtiles + 1) / 2;
-    PrefillParams p{a.q_and_gate, a.attention, a.err, a.seq0, a.count, a.base, a.heads,
-                    a.kv_heads, n_qtiles};
+    PrefillParams p{a.err, a.seq0, a.count, a.base, a.heads, a.kv_heads, n_qtiles};
     e = cudaFuncSetAttribute(attn_prefill_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              int(kSmemPair));
     if (e != cudaSuccess) return e;
@@ -617,7 +708,7 @@ cudaError_t launch_attn_prefill(const AttnPrefillLaunch &a, cudaStream_t stream)
     cfg.stream = stream;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, attn_prefill_pair_kernel, mq, mk, mv, p);
+    return cudaLaunchKernelEx(&cfg, attn_prefill_pair_kernel, mq, mk, mv, mg, mo, p);
 }
 
 }  // namespace q38

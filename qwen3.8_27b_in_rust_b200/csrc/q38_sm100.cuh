@@ -170,6 +170,44 @@ __device__ __forceinline__ void tma_load_3d(void *dst_smem, const CUtensorMap *m
         : "memory");
 }
 
+// 4-D tiled TMA load into this CTA's shared memory (no multicast).
+__device__ __forceinline__ void tma_load_4d(void *dst_smem, const CUtensorMap *map, int c0, int c1,
+                                           int c2, int c3, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
+        "[%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(smem_addr(dst_smem)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3),
+        "r"(smem_addr(bar))
+        : "memory");
+}
+
+// Prefetch of a 4-D tile into L2 (no shared-memory destination).
+__device__ __forceinline__ void tma_prefetch_4d(const CUtensorMap *map, int c0, int c1, int c2,
+                                               int c3) {
+    asm volatile("cp.async.bulk.prefetch.tensor.4d.L2.global.tile [%0, {%1, %2, %3, %4}];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+                 : "memory");
+}
+
+// 4-D tiled TMA store from this CTA's shared memory, tracked by bulk group.
+// Rows outside the tensor map's extents are not written.
+__device__ __forceinline__ void tma_store_4d(const CUtensorMap *map, int c0, int c1, int c2, int c3,
+                                            const void *src_smem) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.global.shared::cta.tile.bulk_group [%0, {%1, %2, %3, %4}], [%5];" ::"l"(
+            reinterpret_cast<uint64_t>(map)),
+        "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_addr(src_smem))
+        : "memory");
+}
+__device__ __forceinline__ void bulk_commit_group() {
+    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+// Waits until every committed bulk store has finished reading shared memory.
+__device__ __forceinline__ void bulk_wait_group_read0() {
+    asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+
 // Offset of element (row, col) of a K-major SW128 tile whose rows hold 64
 // bf16 (128 B): the 16-byte chunk index is XOR-ed with row % 8.
 __device__ __forceinline__ uint32_t sw128_offset(uint32_t row, uint32_t col) {

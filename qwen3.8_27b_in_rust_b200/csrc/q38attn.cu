@@ -792,6 +792,10 @@ int q38_full_prefill(q38_ctx *ctx, q38_state *st, int layer, int seq0, int nseq,
                     nseq * count, st->prefill_tokens);
     if (!q_and_gate || !key || !value || !attention)
         return fail(Q38_ERR_ARG, "null tensor argument");
+    // The kernels move rows as 16-byte vectors and by TMA.
+    if ((reinterpret_cast<uintptr_t>(q_and_gate) | reinterpret_cast<uintptr_t>(key) |
+         reinterpret_cast<uintptr_t>(value) | reinterpret_cast<uintptr_t>(attention)) & 15u)
+        return fail(Q38_ERR_ARG, "prefill tensors must be 16-byte aligned");
     auto it = ctx->full.find(layer);
     if (it == ctx->full.end())
         return fail(Q38_ERR_ARG, "full-attention layer %d has no bound weights", layer);
@@ -839,6 +843,10 @@ int q38_linear_prefill(q38_ctx *ctx, q38_state *st, int layer, int seq0, int nse
                     nseq * count, st->prefill_tokens);
     if (!qkv || !z || !beta || !alpha || !attention)
         return fail(Q38_ERR_ARG, "null tensor argument");
+    // The kernels read and write the per-token rows as 16-byte vectors.
+    if ((reinterpret_cast<uintptr_t>(qkv) | reinterpret_cast<uintptr_t>(z) |
+         reinterpret_cast<uintptr_t>(attention)) & 15u)
+        return fail(Q38_ERR_ARG, "prefill tensors must be 16-byte aligned");
     auto it = ctx->linear.find(layer);
     if (it == ctx->linear.end())
         return fail(Q38_ERR_ARG, "DeltaNet layer %d has no bound weights", layer);
