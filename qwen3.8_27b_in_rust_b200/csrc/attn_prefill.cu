@@ -45,6 +45,12 @@ namespace {
 using namespace sm100;
 
 constexpr int kBlockQ = 128;  // query rows per CTA (MMA M)
+constexpr int kRopeHalf = kRopeDims / 2;  // RoPE angles per position
+// RoPE table of a prefill call: per block of 128 positions, [64][128] f32
+// (cos of angles 0-31, then their sin, each over the block's positions), so
+// that one bulk copy brings a CTA's block and thread r reads column r.
+constexpr int kRopeBlockFloats = kRopeDims * kBlockQ;
+constexpr uint32_t kRopeBlockBytes = kRopeBlockFloats * 4;  // 32 KB
 constexpr int kBlockK = 64;   // keys per tile (QK N, PV K)
 constexpr int kThreadsPF = 288;
 constexpr uint32_t kQBytes = kBlockQ * kAttnHeadDim * 2;      // 64 KB
@@ -55,105 +61,101 @@ constexpr float kRescaleThreshold = 8.0f;  // log2 units
 // P1: prep
 // --------------------------------------------------------------------------
 struct PrefillPrepParams {
-    const float *q_and_gate;  // [nseq][count][heads*512]
     float *key;               // [nseq][count][kv_heads*256]
     const float *value;
-    __nv_bfloat16 *qp;        // [nseq][heads][count][256]
     __nv_bfloat16 *kcache, *vcache;  // slot base: [batch][kv_heads][ctx][256]
     __half *v16;                     // [nseq][kv_heads][ctx][256]: V as f16 for P V
-    const float *q_norm, *k_norm;
-    int seq0, count, base, context_length, heads, kv_heads;
+    float *rope;                     // RoPE table, blocks of [64][128] (see kRopeBlockFloats)
+    const float *k_norm;
+    int seq0, count, base, context_length, kv_heads;
     float theta_scale, eps;
 };
 
-// One CTA per (token, sequence); warp w handles heads w, w+8, ... of the
-// heads + kv_heads heads. Lane l holds dims [8l, 8l+8) of a head, so the RoPE
-// partner of dim i < 32 (dim i + 32) sits in lane l ^ 4 at the same slot.
+// One warp per (token, kv head), 8 / kv_heads tokens per CTA. Lane l holds
+// dims [8l, 8l+8) of a head, so the RoPE partner of dim i < 32 (dim i + 32)
+// sits in lane l ^ 4 at the same slot. The CTAs of the first sequence also
+// write the RoPE table that the attention kernel applies to the queries.
 constexpr int kPrepWarps = 8;
 
 __global__ void __launch_bounds__(kPrepWarps * 32) attn_prefill_prep_kernel(PrefillPrepParams p) {
     pdl_launch_dependents();
-    __shared__ float cs[32], sn[32];
-    const int t = blockIdx.x, s = blockIdx.y;
+    __shared__ float cs[kPrepWarps][32], sn[kPrepWarps][32];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int pos = p.base + t;
-    // rope (ops.rs:595-610): theta_j = pos * scale^j by repeated f32 products.
-    if (threadIdx.x < kRopeDims / 2) {
-        float theta = float(pos);
-        for (int j = 0; j < int(threadIdx.x); ++j) theta *= p.theta_scale;
-        cs[threadIdx.x] = cosf(theta);
-        sn[threadIdx.x] = sinf(theta);
-    }
-    __syncthreads();
-    const size_t tok = size_t(s) * p.count + t;
-    const int d0 = 8 * lane;
-    for (int h = warp; h < p.heads + p.kv_heads; h += kPrepWarps) {
-        const bool is_q = h < p.heads;
-        const int kvh = h - p.heads;
-        const float *src = is_q ? p.q_and_gate + (tok * p.heads + h) * 2 * kAttnHeadDim
-                                : p.key + (tok * p.kv_heads + kvh) * kAttnHeadDim;
-        const float4 a = reinterpret_cast<const float4 *>(src + d0)[0];
-        const float4 b = reinterpret_cast<const float4 *>(src + d0)[1];
-        float x[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-        // rmsnorm_inplace (ops.rs:493-498) with rms_scale's f64 accumulation.
-        double sum = 0.0;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) sum += double(x[j]) * double(x[j]);
-        sum = warp_sum_f64(sum);
-        const float scale = rms_scale_from_sum(sum, kAttnHeadDim, p.eps);
-        const float *w = is_q ? p.q_norm : p.k_norm;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) x[j] = x[j] * scale * w[d0 + j];
-        // RoPE on dims [0, 64): lanes 0-3 hold dims i < 32, lanes 4-7 dims i+32.
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            const float other = __shfl_xor_sync(0xffffffffu, x[j], 4);
-            if (lane < 4) {
-                const int i = d0 + j;
-                x[j] = x[j] * cs[i] - other * sn[i];
-            } else if (lane < 8) {
-                const int i = d0 + j - 32;
-                x[j] = other * sn[i] + x[j] * cs[i];
+    const int tokens = kPrepWarps / p.kv_heads;  // per CTA
+    const int s = blockIdx.y;
+    // rope (ops.rs:595-610): theta_i = pos * scale^i by repeated f32 products.
+    if (warp < tokens) {
+        const int t = blockIdx.x * tokens + warp;
+        if (t < p.count) {
+            float theta = float(p.base + t);
+            for (int j = 0; j < lane; ++j) theta *= p.theta_scale;
+            const float c = cosf(theta), sv = sinf(theta);
+            cs[warp][lane] = c;
+            sn[warp][lane] = sv;
+            if (s == 0) {
+                float *blk = p.rope + size_t(t / kBlockQ) * kRopeBlockFloats + t % kBlockQ;
+                blk[lane * kBlockQ] = c;
+                blk[(kRopeHalf + lane) * kBlockQ] = sv;
             }
         }
-        if (is_q) {
-            uint4 o;
-            o.x = pack_bf16x2_rn(x[0], x[1]);
-            o.y = pack_bf16x2_rn(x[2], x[3]);
-            o.z = pack_bf16x2_rn(x[4], x[5]);
-            o.w = pack_bf16x2_rn(x[6], x[7]);
-            *reinterpret_cast<uint4 *>(p.qp + ((size_t(s) * p.heads + h) * p.count + t) * kAttnHeadDim + d0) = o;
-        } else {
-            const size_t off = (tok * p.kv_heads + kvh) * kAttnHeadDim + d0;
-            reinterpret_cast<float4 *>(p.key + off)[0] = make_float4(x[0], x[1], x[2], x[3]);
-            reinterpret_cast<float4 *>(p.key + off)[1] = make_float4(x[4], x[5], x[6], x[7]);
-            const size_t row =
-                ((size_t(p.seq0 + s) * p.kv_heads + kvh) * p.context_length + pos) * kAttnHeadDim + d0;
-            uint4 kk, vv;
-            kk.x = pack_bf16x2_rn(x[0], x[1]);
-            kk.y = pack_bf16x2_rn(x[2], x[3]);
-            kk.z = pack_bf16x2_rn(x[4], x[5]);
-            kk.w = pack_bf16x2_rn(x[6], x[7]);
-            const float4 va = reinterpret_cast<const float4 *>(p.value + off)[0];
-            const float4 vb = reinterpret_cast<const float4 *>(p.value + off)[1];
-            vv.x = pack_bf16x2_rn(va.x, va.y);
-            vv.y = pack_bf16x2_rn(va.z, va.w);
-            vv.z = pack_bf16x2_rn(vb.x, vb.y);
-            vv.w = pack_bf16x2_rn(vb.z, vb.w);
-            *reinterpret_cast<uint4 *>(p.kcache + row) = kk;
-            *reinterpret_cast<uint4 *>(p.vcache + row) = vv;
-            // The same bf16 values as f16 (exact for 2^-14 <= |v| <= 65504).
-            uint4 vh;
-            float2 f;
-            f = bf16x2_to_float2(vv.x); vh.x = pack_f16x2(f.x, f.y);
-            f = bf16x2_to_float2(vv.y); vh.y = pack_f16x2(f.x, f.y);
-            f = bf16x2_to_float2(vv.z); vh.z = pack_f16x2(f.x, f.y);
-            f = bf16x2_to_float2(vv.w); vh.w = pack_f16x2(f.x, f.y);
-            *reinterpret_cast<uint4 *>(
-                p.v16 + ((size_t(s) * p.kv_heads + kvh) * p.context_length + pos) * kAttnHeadDim +
-                d0) = vh;
+    }
+    __syncthreads();
+    const int slot = warp / p.kv_heads, kvh = warp % p.kv_heads;
+    const int t = blockIdx.x * tokens + slot;
+    if (t >= p.count) return;
+    const int pos = p.base + t;
+    const size_t tok = size_t(s) * p.count + t;
+    const int d0 = 8 * lane;
+    const size_t off = (tok * p.kv_heads + kvh) * kAttnHeadDim + d0;
+    const float4 a = reinterpret_cast<const float4 *>(p.key + off)[0];
+    const float4 b = reinterpret_cast<const float4 *>(p.key + off)[1];
+    const float4 va = reinterpret_cast<const float4 *>(p.value + off)[0];
+    const float4 vb = reinterpret_cast<const float4 *>(p.value + off)[1];
+    float x[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+    // rmsnorm_inplace (ops.rs:493-498) with rms_scale's f64 accumulation.
+    double sum = 0.0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) sum += double(x[j]) * double(x[j]);
+    sum = warp_sum_f64(sum);
+    const float scale = rms_scale_from_sum(sum, kAttnHeadDim, p.eps);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) x[j] = x[j] * scale * p.k_norm[d0 + j];
+    // RoPE on dims [0, 64): lanes 0-3 hold dims i < 32, lanes 4-7 dims i+32.
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const float other = __shfl_xor_sync(0xffffffffu, x[j], 4);
+        if (lane < 4) {
+            const int i = d0 + j;
+            x[j] = x[j] * cs[slot][i] - other * sn[slot][i];
+        } else if (lane < 8) {
+            const int i = d0 + j - 32;
+            x[j] = other * sn[slot][i] + x[j] * cs[slot][i];
         }
     }
+    reinterpret_cast<float4 *>(p.key + off)[0] = make_float4(x[0], x[1], x[2], x[3]);
+    reinterpret_cast<float4 *>(p.key + off)[1] = make_float4(x[4], x[5], x[6], x[7]);
+    const size_t row =
+        ((size_t(p.seq0 + s) * p.kv_heads + kvh) * p.context_length + pos) * kAttnHeadDim + d0;
+    uint4 kk, vv;
+    kk.x = pack_bf16x2_rn(x[0], x[1]);
+    kk.y = pack_bf16x2_rn(x[2], x[3]);
+    kk.z = pack_bf16x2_rn(x[4], x[5]);
+    kk.w = pack_bf16x2_rn(x[6], x[7]);
+    vv.x = pack_bf16x2_rn(va.x, va.y);
+    vv.y = pack_bf16x2_rn(va.z, va.w);
+    vv.z = pack_bf16x2_rn(vb.x, vb.y);
+    vv.w = pack_bf16x2_rn(vb.z, vb.w);
+    *reinterpret_cast<uint4 *>(p.kcache + row) = kk;
+    *reinterpret_cast<uint4 *>(p.vcache + row) = vv;
+    // The same bf16 values as f16 (exact for 2^-14 <= |v| <= 65504).
+    uint4 vh;
+    float2 f;
+    f = bf16x2_to_float2(vv.x); vh.x = pack_f16x2(f.x, f.y);
+    f = bf16x2_to_float2(vv.y); vh.y = pack_f16x2(f.x, f.y);
+    f = bf16x2_to_float2(vv.z); vh.z = pack_f16x2(f.x, f.y);
+    f = bf16x2_to_float2(vv.w); vh.w = pack_f16x2(f.x, f.y);
+    *reinterpret_cast<uint4 *>(
+        p.v16 + ((size_t(s) * p.kv_heads + kvh) * p.context_length + pos) * kAttnHeadDim + d0) = vh;
 }
 
 // --------------------------------------------------------------------------
@@ -187,8 +189,11 @@ __global__ void __launch_bounds__(256) attn_prefill_prefix_kernel(PrefixParams p
 // P2: attention
 // --------------------------------------------------------------------------
 struct PrefillParams {
+    const float *q_norm;  // [256]
+    const float *rope;    // RoPE table, blocks of [64][128] (see kRopeBlockFloats)
     int *err;
     int seq0, count, base, heads, kv_heads, n_qtiles;
+    float eps;
 };
 
 __device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
@@ -233,11 +238,12 @@ constexpr uint32_t kKHalf = (kBlockK / 2) * kAttnHeadDim * 2;  // 16 KB: 32 keys
 constexpr uint32_t kVHalf = kBlockK * (kAttnHeadDim / 2) * 2;  // 16 KB: 64 keys x 128 dims
 constexpr int kPairStagesK = 4;
 constexpr int kPairStagesV = 4;
-constexpr uint32_t kSmemPair = kQBytes + kPairStagesK * kKHalf + kPairStagesV * kVHalf + 1024;
+constexpr uint32_t kSmemPair =
+    kQBytes + kPairStagesK * kKHalf + kPairStagesV * kVHalf + kRopeBlockBytes + 1024;
 constexpr uint32_t kPairColO = kPairSBuf * kBlockK;  // 256: O after the four S buffers
 
 struct __align__(8) PairBarriers {
-    uint64_t q_full;
+    uint64_t q_full, q_conv, q_pair;
     uint64_t k_full[kPairStagesK], k_empty[kPairStagesK], v_full[kPairStagesV], v_empty[kPairStagesV];
     uint64_t s_full[kPairSBuf], p_full[kPairSBuf], s_free[kPairSBuf], o_final;
     uint64_t gate_full, epi_l, epi_done;
@@ -253,6 +259,7 @@ constexpr int kEpiBoxes = kAttnHeadDim / kEpiBoxCols;          // 8
 static_assert(kEpiBoxes * kEpiBoxBytes == kQBytes + kPairStagesK * kKHalf,
               "the gate block fills the Q and K-ring region exactly");
 constexpr int kGatePrefetchTiles = 8;  // L2 prefetch of the gate this many key tiles early
+constexpr int kQueryWarps = 4;         // warps that prepare the query rows (one row per thread)
 
 // Arrival on a barrier of the leader CTA (cluster address), ordered like the
 // local tcgen05 handshakes (tcgen05.wait + fence::before_thread_sync first).
@@ -261,8 +268,7 @@ __device__ __forceinline__ void mbar_arrive_leader(uint32_t cluster_bar) {
 }
 
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsPF, 1)
-    attn_prefill_pair_kernel(const __grid_constant__ CUtensorMap map_q,
-                             const __grid_constant__ CUtensorMap map_k,
+    attn_prefill_pair_kernel(const __grid_constant__ CUtensorMap map_k,
                              const __grid_constant__ CUtensorMap map_v,
                              const __grid_constant__ CUtensorMap map_g,
                              const __grid_constant__ CUtensorMap map_o, PrefillParams p) {
@@ -272,6 +278,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsPF, 1)
     unsigned char *sQ = smem;                          // this CTA's 128 query rows (bf16)
     unsigned char *sK = sQ + kQBytes;                  // kPairStagesK half tiles
     unsigned char *sV = sK + kPairStagesK * kKHalf;    // kPairStagesV half tiles (f16)
+    unsigned char *sT = sV + kPairStagesV * kVHalf;    // RoPE rows of the CTA's positions
     __shared__ PairBarriers bar;
     __shared__ uint32_t tmem_base_s;
     __shared__ volatile int abort_flag;
@@ -293,6 +300,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsPF, 1)
     if (threadIdx.x == 0) {
         abort_flag = 0;
         mbar_init(&bar.q_full, 1);
+        mbar_init(&bar.q_conv, kQueryWarps);
+        mbar_init(&bar.q_pair, 2 * kQueryWarps);  // used in the leader only
         for (int b = 0; b < kPairStagesK; ++b) {
             mbar_init(&bar.k_full[b], 1);
             mbar_init(&bar.k_empty[b], 1);
@@ -326,21 +335,113 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsPF, 1)
         set_error(p.err, kDevErrTimeout);
     };
 
-    if (warp == 0) {
-        // ------------------------------------------------------------ Q, K-half producer
+    // ---------------------------------------------------------------- queries
+    // The CTA's 128 query rows (f32, q half of q_and_gate) land by TMA in the
+    // K and V rings as eight 32-column boxes (128-byte swizzle), and the RoPE
+    // angles of its positions by bulk copy ([64][128]: cos of angles 0-31,
+    // then sin, each over the 128 rows). Warps 0-3 take one row per thread:
+    // q RMSNorm with an f32 sum of squares (the reference sums in f64; these
+    // rows are rounded to bf16 for the tensor cores, whose 4e-3 dwarfs the
+    // ~1e-7 difference), RoPE, and bf16 Q into sQ in the SW128 K-major layout
+    // the QK MMA reads. The rings are then handed to the K/V producers
+    // (q_conv) and the pair's Q to the leader's QK issuers (q_pair).
+    auto stage_box = [&](int cb) { return cb < 4 ? sV + cb * kEpiBoxBytes : sK + (cb - 4) * kEpiBoxBytes; };
+    if (warp == 0 && lane == 0) {
+        tma_prefetch_desc(&map_g);
+        mbar_arrive_expect_tx(&bar.q_full, kEpiBoxes * kEpiBoxBytes + (has_rows ? kRopeBlockBytes : 0u));
+        for (int cb = 0; cb < kEpiBoxes; ++cb)
+            tma_load_4d(stage_box(cb), &map_g, cb * kEpiBoxCols, h, q0, s, &bar.q_full);
+        pdl_wait_primary();  // P1 wrote the RoPE table and the K/V rows loaded below
+        if (has_rows)
+            bulk_load(sT, p.rope + size_t(q0 / kBlockQ) * kRopeBlockFloats, kRopeBlockBytes, &bar.q_full);
+    }
+    if (warp < kQueryWarps) {
+        const uint32_t r = uint32_t(warp * 32 + lane);
+        const bool ready = __all_sync(0xffffffffu, mbar_wait(&bar.q_full, 0));
+        if (ready) {
+            float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+            for (int cb = 0; cb < kEpiBoxes; ++cb) {
+                const unsigned char *row = stage_box(cb) + r * 128;
+#pragma unroll
+                for (int c = 0; c < 8; ++c) {
+                    const float4 v = *reinterpret_cast<const float4 *>(row + ((c ^ (r & 7)) << 4));
+                    acc[c] = fmaf(v.x, v.x, acc[c]);
+                    acc[c] = fmaf(v.y, v.y, acc[c]);
+                    acc[c] = fmaf(v.z, v.z, acc[c]);
+                    acc[c] = fmaf(v.w, v.w, acc[c]);
+                }
+            }
+            const float sq = ((acc[0] + acc[1]) + (acc[2] + acc[3])) + ((acc[4] + acc[5]) + (acc[6] + acc[7]));
+            // rmsnorm_inplace (ops.rs:493-498)
+            const float scale = 1.0f / sqrtf(sq * (1.0f / kAttnHeadDim) + p.eps);
+            // Rows past the prompt's end (zeros from the TMA) take the last
+            // position's angles; a CTA without rows takes angle 0.
+            const float *tab = reinterpret_cast<const float *>(sT) + (has_rows ? min(int(r), q_rows - 1) : 0);
+#pragma unroll 1
+            for (int qb = 0; qb < 4; ++qb) {  // 64 dims: one 16 KB box of sQ
+                float x[64];
+#pragma unroll
+                for (int half = 0; half < 2; ++half) {
+                    const unsigned char *row = stage_box(2 * qb + half) + r * 128;
+#pragma unroll
+                    for (int c = 0; c < 8; ++c) {
+                        const float4 v = *reinterpret_cast<const float4 *>(row + ((c ^ (r & 7)) << 4));
+                        x[half * 32 + 4 * c + 0] = v.x;
+                        x[half * 32 + 4 * c + 1] = v.y;
+                        x[half * 32 + 4 * c + 2] = v.z;
+                        x[half * 32 + 4 * c + 3] = v.w;
+                    }
+                }
+                const float4 *w4 = reinterpret_cast<const float4 *>(p.q_norm + qb * 64);
+#pragma unroll
+                for (int k = 0; k < 16; ++k) {
+                    const float4 w = __ldg(w4 + k);
+                    x[4 * k + 0] = x[4 * k + 0] * scale * w.x;
+                    x[4 * k + 1] = x[4 * k + 1] * scale * w.y;
+                    x[4 * k + 2] = x[4 * k + 2] * scale * w.z;
+                    x[4 * k + 3] = x[4 * k + 3] * scale * w.w;
+                }
+                if (qb == 0) {
+                    // rope (ops.rs:595-610): the pair (i, i + 32) for i < 32.
+#pragma unroll
+                    for (int i = 0; i < kRopeHalf; ++i) {
+                        const float c = has_rows ? tab[i * kBlockQ] : 1.f;
+                        const float sn = has_rows ? tab[(kRopeHalf + i) * kBlockQ] : 0.f;
+                        const float lo = x[i], hi = x[i + kRopeHalf];
+                        x[i] = lo * c - hi * sn;
+                        x[i + kRopeHalf] = lo * sn + hi * c;
+                    }
+                }
+                unsigned char *dst = sQ + qb * (kQBytes / 4) + r * 128;
+#pragma unroll
+                for (int ch = 0; ch < 8; ++ch) {
+                    uint4 o;
+                    o.x = pack_bf16x2_rn(x[8 * ch + 0], x[8 * ch + 1]);
+                    o.y = pack_bf16x2_rn(x[8 * ch + 2], x[8 * ch + 3]);
+                    o.z = pack_bf16x2_rn(x[8 * ch + 4], x[8 * ch + 5]);
+                    o.w = pack_bf16x2_rn(x[8 * ch + 6], x[8 * ch + 7]);
+                    *reinterpret_cast<uint4 *>(dst + ((ch ^ (r & 7)) << 4)) = o;
+                }
+            }
+            fence_proxy_async_smem();  // the QK MMA reads sQ through the async proxy
+        }
+        __syncwarp();
         if (lane == 0) {
-            tma_prefetch_desc(&map_q);
+            if (!ready) fail();
+            mbar_arrive(&bar.q_conv);
+            mbar_arrive_remote(cluster_addr(&bar.q_pair, 0));
+        }
+    }
+
+    if (warp == 0) {
+        // ------------------------------------------------------------ K-half producer
+        if (lane == 0) {
             tma_prefetch_desc(&map_k);
-            pdl_wait_primary();  // P1 wrote the Q scratch and the new K/V rows
-            const int qrow = s * p.heads + h;
             const int kplane = (p.seq0 + s) * p.kv_heads + kvh;
-            if (leader) mbar_arrive_expect_tx(&bar.q_full, 2 * kQBytes);
-            const uint32_t qfull = cluster_addr(&bar.q_full, 0);
-            for (int cb = 0; cb < 4; ++cb)
-                tma_load_3d_pair(sQ + cb * (kQBytes / 4), &map_q, cb * 64, q0, qrow, qfull);
+            bool ok = mbar_wait(&bar.q_conv, 0);  // the K ring held query rows
             const int gate_x = kAttnHeadDim;  // the gate half of each head's 512 values
-            bool ok = true;
-            for (int j = 0; j < nkt; ++j) {
+            for (int j = 0; ok && j < nkt; ++j) {
                 const int b = j % kPairStagesK;
                 if (j >= kPairStagesK &&
                     !mbar_wait(&bar.k_empty[b], uint32_t(j / kPairStagesK - 1) & 1u)) {
@@ -377,8 +478,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsPF, 1)
         // ------------------------------------------------------------ V-half producer (f16)
         if (lane == 0) {
             tma_prefetch_desc(&map_v);
-            pdl_wait_primary();
+            pdl_wait_primary();  // P1 wrote the V rows
             const int vplane = s * p.kv_heads + kvh;
+            if (!mbar_wait(&bar.q_conv, 0)) fail();  // the V ring held query rows
             for (int j = 0; j < nkt && !abort_flag; ++j) {
                 const int b = j % kPairStagesV;
                 if (j >= kPairStagesV &&
@@ -401,7 +503,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsPF, 1)
         if (leader && lane == 0) {
             const uint32_t id_qk = idesc_bf16_f32(kPairRows, kBlockK, 0, 0);
             const uint32_t sq = smem_addr(sQ), sk = smem_addr(sK);
-            bool ok = mbar_wait(&bar.q_full, 0);
+            bool ok = mbar_wait_cluster(&bar.q_pair, 0);  // Q of both CTAs in shared memory
             for (int j = warp == 1 ? 0 : 1; ok && j < nkt; j += 2) {
                 const int b = j % kPairSBuf, kb = j % kPairStagesK;
                 if (!mbar_wait(&bar.k_full[kb], uint32_t(j / kPairStagesK) & 1u)) { ok = false; break; }
@@ -665,6 +767,10 @@ bool make_map_rows_f32(CUtensorMap *m, const void *base, uint64_t width, uint64_
 
 }  // namespace
 
+size_t attn_prefill_rope_floats(int max_tokens) {
+    return size_t((max_tokens + kBlockQ - 1) / kBlockQ) * kRopeBlockFloats;
+}
+
 cudaError_t launch_attn_prefill(const AttnPrefillLaunch &a, cudaStream_t stream) {
     cudaError_t e;
     if (a.base > 0) {
@@ -673,19 +779,20 @@ cudaError_t launch_attn_prefill(const AttnPrefillLaunch &a, cudaStream_t stream)
         attn_prefill_prefix_kernel<<<dim3((n8 + 255) / 256, a.kv_heads, a.nseq), 256, 0, stream>>>(xp);
         if ((e = cudaGetLastError()) != cudaSuccess) return e;
     }
-    PrefillPrepParams pp{a.q_and_gate, a.key, a.value, a.qp, a.kcache, a.vcache, a.v16, a.q_norm,
-                         a.k_norm, a.seq0, a.count, a.base, a.context_length, a.heads, a.kv_heads,
-                         a.theta_scale, a.eps};
-    attn_prefill_prep_kernel<<<dim3(a.count, a.nseq), kPrepWarps * 32, 0, stream>>>(pp);
+    if (a.kv_heads <= 0 || kPrepWarps % a.kv_heads != 0) return cudaErrorInvalidValue;
+    PrefillPrepParams pp{a.key,    a.value, a.kcache,         a.vcache,   a.v16,
+                         a.rope,   a.k_norm, a.seq0,          a.count,    a.base,
+                         a.context_length,   a.kv_heads,      a.theta_scale, a.eps};
+    const int prep_tokens = kPrepWarps / a.kv_heads;
+    attn_prefill_prep_kernel<<<dim3((a.count + prep_tokens - 1) / prep_tokens, a.nseq),
+                               kPrepWarps * 32, 0, stream>>>(pp);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
 
-    CUtensorMap mq, mk, mv, mg, mo;
+    CUtensorMap mk, mv, mg, mo;
     if (!make_map_rows_f32(&mg, a.q_and_gate, 2 * kAttnHeadDim, uint64_t(a.heads), uint64_t(a.count),
                            uint64_t(a.nseq)) ||
         !make_map_rows_f32(&mo, a.attention, kAttnHeadDim, uint64_t(a.heads), uint64_t(a.count),
                            uint64_t(a.nseq)) ||
-        !make_map_16(&mq, a.qp, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, uint64_t(a.count),
-                     uint64_t(a.nseq) * a.heads, kBlockQ) ||
         !make_map_16(&mk, a.kcache, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, uint64_t(a.context_length),
                      uint64_t(a.batch) * a.kv_heads, kBlockK / 2) ||
         !make_map_16(&mv, a.v16, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, uint64_t(a.context_length),
@@ -694,7 +801,8 @@ cudaError_t launch_attn_prefill(const AttnPrefillLaunch &a, cudaStream_t stream)
 
     const int n_qtiles = (a.count + kBlockQ - 1) / kBlockQ;
     const int n_pairs = (n_qtiles + 1) / 2;
-    PrefillParams p{a.err, a.seq0, a.count, a.base, a.heads, a.kv_heads, n_qtiles};
+    PrefillParams p{a.q_norm, a.rope,     a.err,     a.seq0, a.count, a.base,
+                    a.heads,  a.kv_heads, n_qtiles, a.eps};
     e = cudaFuncSetAttribute(attn_prefill_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              int(kSmemPair));
     if (e != cudaSuccess) return e;
@@ -708,7 +816,7 @@ cudaError_t launch_attn_prefill(const AttnPrefillLaunch &a, cudaStream_t stream)
     cfg.stream = stream;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, attn_prefill_pair_kernel, mq, mk, mv, mg, mo, p);
+    return cudaLaunchKernelEx(&cfg, attn_prefill_pair_kernel, mk, mv, mg, mo, p);
 }
 
 }  // namespace q38

@@ -66,7 +66,7 @@ struct q38_state {
     float *part_ml = nullptr;       // [batch][heads][max_splits][2]
     int max_splits = 0;
     int *d_err = nullptr;           // device error bits
-    __nv_bfloat16 *prefill_q = nullptr;  // [tokens][heads][256] prepared queries
+    float *prefill_rope = nullptr;       // RoPE table of the prompt's positions
     __half *prefill_v16 = nullptr;       // [v16_seqs][kv_heads][context][256] V as f16
     int prefill_v16_seqs = 0;
     size_t prefill_tokens = 0;
@@ -123,7 +123,7 @@ struct AttnPrefillLaunch {
     float *key;               // [nseq][count][kv_heads*256]
     const float *value;
     float *attention;         // [nseq][count][heads*256]
-    __nv_bfloat16 *qp;        // scratch [nseq][heads][count][256]
+    float *rope;              // scratch: RoPE table (attn_prefill_rope_floats)
     __nv_bfloat16 *kcache, *vcache;  // slot base [batch][kv_heads][ctx][256]
     __half *v16;                     // scratch [nseq][kv_heads][ctx][256]
     const float *q_norm, *k_norm;
@@ -132,6 +132,8 @@ struct AttnPrefillLaunch {
     float theta_scale, eps;
 };
 cudaError_t launch_attn_prefill(const AttnPrefillLaunch &a, cudaStream_t stream);
+// Floats of the RoPE table a prefill of up to max_tokens positions uses.
+size_t attn_prefill_rope_floats(int max_tokens);
 
 struct LinearPrefillLaunch {
     float *qkv;                 // [nseq][count][qkv_dim] in/out

@@ -163,7 +163,7 @@ void free_state(q38_state *st) {
     cudaFree(st->d_err);
     cudaFree(st->stage);
     cudaFree(st->stage_pos);
-    cudaFree(st->prefill_q);
+    cudaFree(st->prefill_rope);
     cudaFree(st->prefill_v16);
     cudaFree(st->prefill_lin);
     cudaFree(st->prefill_stage);
@@ -728,11 +728,11 @@ int q38_state_reserve_prefill(q38_state *st, int max_tokens) {
     if (max_tokens <= 0) return fail(Q38_ERR_ARG, "max_tokens must be positive");
     if (size_t(max_tokens) <= st->prefill_tokens) return Q38_OK;
     DeviceGuard guard(st->ctx->device);
-    cudaFree(st->prefill_q);
+    cudaFree(st->prefill_rope);
     cudaFree(st->prefill_v16);
     cudaFree(st->prefill_lin);
     cudaFree(st->prefill_stage);
-    st->prefill_q = nullptr;
+    st->prefill_rope = nullptr;
     st->prefill_v16 = nullptr;
     st->prefill_v16_seqs = 0;
     st->prefill_lin = nullptr;
@@ -741,8 +741,9 @@ int q38_state_reserve_prefill(q38_state *st, int max_tokens) {
     st->prefill_chunks = 0;
     st->prefill_stage_tokens = 0;
     if (st->full_slots > 0) {
-        const size_t bytes = size_t(max_tokens) * st->ctx->q_dim * sizeof(__nv_bfloat16);
-        Q38_CUDA(cudaMalloc(&st->prefill_q, bytes));
+        // RoPE table of the prompt's positions (cos | sin of 32 angles each).
+        Q38_CUDA(cudaMalloc(&st->prefill_rope,
+                            q38::attn_prefill_rope_floats(max_tokens) * sizeof(float)));
         // f16 copy of the V rows a prefill reads (prefix and prompt), one
         // cache-sized plane per sequence that one call can cover.
         const int seqs = std::min(st->batch, max_tokens);
@@ -804,7 +805,7 @@ int q38_full_prefill(q38_ctx *ctx, q38_state *st, int layer, int seq0, int nseq,
     a.key = key;
     a.value = value;
     a.attention = attention;
-    a.qp = st->prefill_q;
+    a.rope = st->prefill_rope;
     a.v16 = st->prefill_v16;
     a.kcache = reinterpret_cast<__nv_bfloat16 *>(kv_seq_base(st, st->kcache, slot, 0));
     a.vcache = reinterpret_cast<__nv_bfloat16 *>(kv_seq_base(st, st->vcache, slot, 0));
