@@ -246,7 +246,7 @@ struct __align__(8) PairBarriers {
     uint64_t q_full, q_conv, q_pair;
     uint64_t k_full[kPairStagesK], k_empty[kPairStagesK], v_full[kPairStagesV], v_empty[kPairStagesV];
     uint64_t s_full[kPairSBuf], p_full[kPairSBuf], s_free[kPairSBuf], o_final;
-    uint64_t gate_full, epi_l, epi_done;
+    uint64_t gate_full, epi_l, epi_box[8];
 };
 
 // Epilogue staging: the gate block of the CTA's 128 rows (f32) lands by TMA
@@ -259,10 +259,15 @@ constexpr int kEpiBoxes = kAttnHeadDim / kEpiBoxCols;          // 8
 static_assert(kEpiBoxes * kEpiBoxBytes == kQBytes + kPairStagesK * kKHalf,
               "the gate block fills the Q and K-ring region exactly");
 constexpr int kGatePrefetchTiles = 8;  // L2 prefetch of the gate this many key tiles early
-constexpr int kQueryWarps = 4;         // warps that prepare the query rows (one row per thread)
+constexpr int kQueryWarps = 8;         // warps 1-8 prepare the query rows (two threads per row)
 
 // Arrival on a barrier of the leader CTA (cluster address), ordered like the
 // local tcgen05 handshakes (tcgen05.wait + fence::before_thread_sync first).
+// Named barrier over `threads` threads (barrier 0 is __syncthreads).
+__device__ __forceinline__ void named_barrier_sync(int id, int threads) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
 __device__ __forceinline__ void mbar_arrive_leader(uint32_t cluster_bar) {
     asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
 }
@@ -318,7 +323,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsPF, 1)
         mbar_init(&bar.o_final, 1);
         mbar_init(&bar.gate_full, 1);
         mbar_init(&bar.epi_l, 4);     // the four softmax warps
-        mbar_init(&bar.epi_done, 8);  // the eight epilogue warps
+        for (int b = 0; b < kEpiBoxes; ++b)
+            mbar_init(&bar.epi_box[b], 4);  // the four warps (lane quarters) that fill a box
         fence_barrier_init();
     }
     if (warp == 1) {
@@ -336,16 +342,23 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsPF, 1)
     };
 
     // ---------------------------------------------------------------- queries
-    // The CTA's 128 query rows (f32, q half of q_and_gate) land by TMA in the
-    // K and V rings as eight 32-column boxes (128-byte swizzle), and the RoPE
-    // angles of its positions by bulk copy ([64][128]: cos of angles 0-31,
-    // then sin, each over the 128 rows). Warps 0-3 take one row per thread:
-    // q RMSNorm with an f32 sum of squares (the reference sums in f64; these
-    // rows are rounded to bf16 for the tensor cores, whose 4e-3 dwarfs the
-    // ~1e-7 difference), RoPE, and bf16 Q into sQ in the SW128 K-major layout
-    // the QK MMA reads. The rings are then handed to the K/V producers
-    // (q_conv) and the pair's Q to the leader's QK issuers (q_pair).
-    auto stage_box = [&](int cb) { return cb < 4 ? sV + cb * kEpiBoxBytes : sK + (cb - 4) * kEpiBoxBytes; };
+    // The CTA's 128 query rows (f32, q half of q_and_gate) land by TMA as
+    // eight 32-column boxes (128-byte swizzle): boxes 0, 1, 4, 5 over sQ and
+    // 2, 3, 6, 7 in the V ring, and the RoPE angles of its positions by bulk
+    // copy ([64][128]: cos of angles 0-31, then sin, each over the 128 rows).
+    // Warps 1-8 prepare them, two threads per row (warps 1-4 dims 0-127,
+    // warps 5-8 dims 128-255): q RMSNorm with an f32 sum of squares (the
+    // reference sums in f64; these rows are rounded to bf16 for the tensor
+    // cores, whose 4e-3 dwarfs the ~1e-7 difference), RoPE, and bf16 Q into
+    // sQ in the SW128 K-major layout the QK MMA reads. A thread's bf16 output
+    // only overwrites f32 rows that it has already read itself, so the
+    // conversion needs no shared-memory hand-off beyond the two halves'
+    // partial sums. The K ring is free throughout, so warp 0 streams K tiles
+    // meanwhile; the V ring goes to its producer (q_conv) and the pair's Q to
+    // the leader's QK issuers (q_pair) once every warp has finished.
+    auto stage_box = [&](int cb) {
+        return (((cb >> 1) & 1) ? sV : sQ) + ((cb & 1) + 2 * (cb >> 2)) * kEpiBoxBytes;
+    };
     if (warp == 0 && lane == 0) {
         tma_prefetch_desc(&map_g);
         mbar_arrive_expect_tx(&bar.q_full, kEpiBoxes * kEpiBoxBytes + (has_rows ? kRopeBlockBytes : 0u));
@@ -355,14 +368,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsPF, 1)
         if (has_rows)
             bulk_load(sT, p.rope + size_t(q0 / kBlockQ) * kRopeBlockFloats, kRopeBlockBytes, &bar.q_full);
     }
-    if (warp < kQueryWarps) {
-        const uint32_t r = uint32_t(warp * 32 + lane);
+    if (warp >= 1) {
+        const int quarter = warp & 3, half = warp >= 5 ? 1 : 0;
+        const uint32_t r = uint32_t(quarter * 32 + lane);
         const bool ready = __all_sync(0xffffffffu, mbar_wait(&bar.q_full, 0));
+        float part = 0.f;
         if (ready) {
             float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-            for (int cb = 0; cb < kEpiBoxes; ++cb) {
-                const unsigned char *row = stage_box(cb) + r * 128;
+            for (int k = 0; k < 4; ++k) {
+                const unsigned char *row = stage_box(4 * half + k) + r * 128;
 #pragma unroll
                 for (int c = 0; c < 8; ++c) {
                     const float4 v = *reinterpret_cast<const float4 *>(row + ((c ^ (r & 7)) << 4));
@@ -372,25 +387,34 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsPF, 1)
                     acc[c] = fmaf(v.w, v.w, acc[c]);
                 }
             }
-            const float sq = ((acc[0] + acc[1]) + (acc[2] + acc[3])) + ((acc[4] + acc[5]) + (acc[6] + acc[7]));
+            part = ((acc[0] + acc[1]) + (acc[2] + acc[3])) + ((acc[4] + acc[5]) + (acc[6] + acc[7]));
+        }
+        // Row total: half 1 hands its part to half 0, which returns the sum.
+        // Both warps of a quarter reach both barriers unconditionally.
+        if (half) inv_l_s[r] = part;
+        named_barrier_sync(1 + quarter, 64);
+        if (!half) inv_l_s[r] = part + inv_l_s[r];
+        named_barrier_sync(1 + quarter, 64);
+        const float sq = inv_l_s[r];
+        if (ready) {
             // rmsnorm_inplace (ops.rs:493-498)
             const float scale = 1.0f / sqrtf(sq * (1.0f / kAttnHeadDim) + p.eps);
             // Rows past the prompt's end (zeros from the TMA) take the last
             // position's angles; a CTA without rows takes angle 0.
             const float *tab = reinterpret_cast<const float *>(sT) + (has_rows ? min(int(r), q_rows - 1) : 0);
 #pragma unroll 1
-            for (int qb = 0; qb < 4; ++qb) {  // 64 dims: one 16 KB box of sQ
+            for (int qb = 2 * half; qb < 2 * half + 2; ++qb) {  // 64 dims: one 16 KB box of sQ
                 float x[64];
 #pragma unroll
-                for (int half = 0; half < 2; ++half) {
-                    const unsigned char *row = stage_box(2 * qb + half) + r * 128;
+                for (int k = 0; k < 2; ++k) {
+                    const unsigned char *row = stage_box(2 * qb + k) + r * 128;
 #pragma unroll
                     for (int c = 0; c < 8; ++c) {
                         const float4 v = *reinterpret_cast<const float4 *>(row + ((c ^ (r & 7)) << 4));
-                        x[half * 32 + 4 * c + 0] = v.x;
-                        x[half * 32 + 4 * c + 1] = v.y;
-                        x[half * 32 + 4 * c + 2] = v.z;
-                        x[half * 32 + 4 * c + 3] = v.w;
+                        x[k * 32 + 4 * c + 0] = v.x;
+                        x[k * 32 + 4 * c + 1] = v.y;
+                        x[k * 32 + 4 * c + 2] = v.z;
+                        x[k * 32 + 4 * c + 3] = v.w;
                     }
                 }
                 const float4 *w4 = reinterpret_cast<const float4 *>(p.q_norm + qb * 64);
@@ -439,7 +463,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsPF, 1)
         if (lane == 0) {
             tma_prefetch_desc(&map_k);
             const int kplane = (p.seq0 + s) * p.kv_heads + kvh;
-            bool ok = mbar_wait(&bar.q_conv, 0);  // the K ring held query rows
+            bool ok = true;
             const int gate_x = kAttnHeadDim;  // the gate half of each head's 512 values
             for (int j = 0; ok && j < nkt; ++j) {
                 const int b = j % kPairStagesK;
@@ -480,7 +504,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsPF, 1)
             tma_prefetch_desc(&map_v);
             pdl_wait_primary();  // P1 wrote the V rows
             const int vplane = s * p.kv_heads + kvh;
-            if (!mbar_wait(&bar.q_conv, 0)) fail();  // the V ring held query rows
+            if (!mbar_wait(&bar.q_conv, 0)) fail();  // the V ring held query rows until now
             for (int j = 0; j < nkt && !abort_flag; ++j) {
                 const int b = j % kPairStagesV;
                 if (j >= kPairStagesV &&
@@ -664,7 +688,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsPF, 1)
     // ---------------------------------------------------------------- epilogue
     // Warps 0-7 (TMEM lane quarter warp % 4; warps 2-5 columns 0-127, the
     // others 128-255): out = O / l * sigmoid(gate) in place over the staged
-    // gate block, then one thread stores the block by TMA.
+    // gate block, one 32-column box at a time; warp 8 stores each box by TMA
+    // as soon as its four warps have filled it.
     if (warp < 8 && has_rows) {
         const int quarter = warp & 3;
         const int r = quarter * 32 + lane;
@@ -674,12 +699,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsPF, 1)
         };
         const bool ready =
             wait_all(&bar.o_final, 0) && wait_all(&bar.epi_l, 0) && wait_all(&bar.gate_full, 0);
-        if (ready) {
-            fence_after_sync();
-            const float inv_l = inv_l_s[r];
-            const uint32_t lane_addr = uint32_t(quarter * 32) << 16;
+        if (ready) fence_after_sync();
+        else if (lane == 0) fail();
+        const float inv_l = inv_l_s[r];
+        const uint32_t lane_addr = uint32_t(quarter * 32) << 16;
 #pragma unroll 1
-            for (int cb = cb0; cb < cb0 + kEpiBoxes / 2; ++cb) {
+        for (int cb = cb0; cb < cb0 + kEpiBoxes / 2; ++cb) {
+            if (ready) {
                 uint32_t o[32];
                 tmem_ld32(tmem + lane_addr + kPairColO + cb * kEpiBoxCols, o);
                 tmem_wait_ld();
@@ -695,23 +721,26 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsPF, 1)
                     y.w = __uint_as_float(o[4 * c + 3]) * inv_l * sigmoid_fast(g.w);
                     *pg = y;
                 }
+                fence_proxy_async_smem();  // the TMA store reads these writes
             }
-            fence_proxy_async_smem();  // the TMA store reads these writes
-        } else if (lane == 0) {
-            fail();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bar.epi_box[cb]);
         }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&bar.epi_done);
-        if (warp == 0 && lane == 0) {
-            if (!mbar_wait(&bar.epi_done, 0)) {
-                fail();
-            } else if (!abort_flag) {
-                for (int cb = 0; cb < kEpiBoxes; ++cb)
-                    tma_store_4d(&map_o, cb * kEpiBoxCols, h, q0, s, smem + cb * kEpiBoxBytes);
-                bulk_commit_group();
-                bulk_wait_group_read0();
+    } else if (warp == 8 && has_rows && lane == 0) {
+        // Boxes complete in the order 0, 4, 1, 5, ... (two warps per quarter).
+        bool ok = true;
+        for (int k = 0; k < kEpiBoxes; ++k) {
+            const int cb = (k & 1) * (kEpiBoxes / 2) + (k >> 1);
+            if (!mbar_wait(&bar.epi_box[cb], 0)) {
+                ok = false;
+                break;
             }
+            if (abort_flag) break;
+            tma_store_4d(&map_o, cb * kEpiBoxCols, h, q0, s, smem + cb * kEpiBoxBytes);
+            bulk_commit_group();
         }
+        if (!ok) fail();
+        bulk_wait_group_read0();  // shared memory stays valid until the stores have read it
     }
 
     fence_before_sync();
