@@ -244,11 +244,12 @@ int q38_full_decode_noalloc(const float *q_norm, const float *k_norm, void *key_
 /* ------------------------------------------------------------ prefill */
 
 /* Reserves the state's prefill scratch for up to max_tokens prompt tokens
- * per call (summed over the sequences of the call): the bf16 prepared
- * queries of the attention prefill (12 KB per token, when the state has full
- * slots) and the chunk-local WY quantities of the DeltaNet prefill (about
- * 62 KB per token, when it has linear slots). Allocates; call it once at
- * set-up. */
+ * per call (summed over the sequences of the call): the RoPE table of the
+ * attention prefill (256 B per token) and an f16 copy of the V cache for the
+ * sequences of one call (when the state has full slots), the chunk-local WY
+ * quantities of the DeltaNet prefill (about 62 KB per token, when it has
+ * linear slots), and the staging of the host-pointer forms. Allocates; call
+ * it once at set-up. */
 int q38_state_reserve_prefill(q38_state *st, int max_tokens);
 
 /* Causal prefill of `count` prompt tokens for each of the nseq sequences
@@ -258,7 +259,8 @@ int q38_state_reserve_prefill(q38_state *st, int max_tokens);
  * Runs on the tcgen05 tensor cores: S = Q K^T from bf16 Q and K, O = P V in
  * f16, f32 accumulation;
  * needs a Q38_KV_BF16 state and q38_state_reserve_prefill(nseq*count).
- * DEVICE pointers, token-major per sequence:
+ * DEVICE pointers (16-byte aligned, else Q38_ERR_ARG), token-major per
+ * sequence:
  *   q_and_gate [nseq][count][heads*512]
  *   key        [nseq][count][kv_heads*256] in: projections; out: RMSNorm+RoPE'd
  *   value      [nseq][count][kv_heads*256]
@@ -274,7 +276,8 @@ int q38_full_prefill(q38_ctx *ctx, q38_state *st, int layer, int seq0, int nseq,
  * delta state: the same result as the reference's per-token loop over
  * linear_core (batch_linear_attention, ops.rs:1088-1099), computed in chunks
  * of 64 tokens (WY form; f32). Needs q38_state_reserve_prefill(nseq*count).
- * DEVICE pointers, token-major per sequence:
+ * DEVICE pointers (qkv, z, attention 16-byte aligned, else Q38_ERR_ARG),
+ * token-major per sequence:
  *   qkv   [nseq][count][qkv_dim]  in: projections; out: conv+SiLU+L2 values
  *   z     [nseq][count][v_heads*128]
  *   beta  [nseq][count][v_heads]  in: logits; out: sigmoid(beta)
