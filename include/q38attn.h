@@ -109,6 +109,27 @@ int q38_bind_full_layer(q38_ctx *ctx, int layer, const float *q_norm, const floa
 int q38_bind_linear_layer(q38_ctx *ctx, int layer, const float *conv1d, const float *dt_bias,
                           const float *ssm_a, const float *ssm_norm);
 
+/* ------------------------------------------------------------ GGUF weights */
+
+/* Reads the F32 tensor `name` of a GGUF checkpoint into HOST memory; n must
+ * equal its element count. The container is checked as the reference's
+ * Gguf::open checks it (src/gguf/mod.rs:459-533: magic, version 2..3,
+ * metadata types, tensor shapes and types, power-of-two general.alignment,
+ * tensor bytes inside the file). Returns Q38_ERR_ARG with the reason in
+ * q38_last_error() when the file is malformed or the tensor is missing, not
+ * F32, or of another size. Host only: needs no GPU. */
+int q38_gguf_read_f32(const char *path, const char *name, float *dst, int64_t n);
+
+/* Binds the F32 attention-core weights of layers first_layer..last_layer
+ * (inclusive; layer 64 is the MTP block, KV slot 16) from a GGUF checkpoint,
+ * by the reference's tensor names (bind_layer, ops.rs:53-100):
+ *   full layers:     blk.L.attn_q_norm.weight, blk.L.attn_k_norm.weight
+ *   DeltaNet layers: blk.L.ssm_conv1d.weight, blk.L.ssm_dt.bias, blk.L.ssm_a,
+ *                    blk.L.ssm_norm.weight
+ * Every layer of the range must be present; the result equals calling
+ * q38_bind_full_layer / q38_bind_linear_layer with the same values. */
+int q38_bind_gguf(q38_ctx *ctx, const char *path, int first_layer, int last_layer);
+
 /* ------------------------------------------------------------------ state */
 
 /* Allocates device-resident per-sequence state for `batch` sequences:

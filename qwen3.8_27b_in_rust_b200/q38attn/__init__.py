@@ -37,7 +37,7 @@ __all__ = [
     "Context", "State", "Q38Error", "Q38Geom", "geometry", "load", "last_error",
     "Q38_OK", "Q38_ERR_ARG", "Q38_ERR_CUDA", "Q38_ERR_TIMEOUT", "Q38_KV_F32", "Q38_KV_BF16",
     "Q38_DEVERR_POSITION", "Q38_DEVERR_TIMEOUT", "Q38_DEVERR_SHAPE",
-    "is_full_attention", "full_index", "recurrent_index",
+    "is_full_attention", "full_index", "recurrent_index", "gguf_read_f32",
 ]
 
 # Geometry of src/model/mod.rs:13-26.
@@ -241,6 +241,17 @@ class State:
         return c, d
 
 
+def gguf_read_f32(path, name: str, count: int) -> np.ndarray:
+    """The F32 tensor `name` of a GGUF checkpoint (count elements), read by
+    the library's parser (the checks of Gguf::open, src/gguf/mod.rs:459-533).
+    Host only; raises Q38Error(-1) on a malformed file or a missing, non-F32
+    or differently sized tensor."""
+    out = np.empty(count, np.float32)
+    check(load().q38_gguf_read_f32(str(path).encode(), name.encode(),
+                                   out.ctypes.data_as(ctypes.c_void_p), count))
+    return out
+
+
 class Context:
     """A device, the model geometry and the bound per-layer weights
     (the weight half of Q38Model::bind, src/model/ops.rs:1450-1459)."""
@@ -282,6 +293,11 @@ class Context:
                                               _host_ptr(dt_bias, "dt_bias"),
                                               _host_ptr(ssm_a, "ssm_a"),
                                               _host_ptr(ssm_norm, "ssm_norm")))
+
+    def bind_gguf(self, path, first_layer: int, last_layer: int) -> None:
+        """Binds layers first_layer..last_layer (64 = MTP) from a GGUF
+        checkpoint by the reference's tensor names (ops.rs:53-100)."""
+        check(self._lib.q38_bind_gguf(self.handle, str(path).encode(), first_layer, last_layer))
 
     def state(self, batch: int, context_length: int, full_slots: int = FULL_SLOTS,
               linear_slots: int = LINEAR_SLOTS, kv_dtype: int = Q38_KV_F32) -> State:

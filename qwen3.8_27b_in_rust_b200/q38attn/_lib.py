@@ -60,6 +60,8 @@ SIGNATURES = {
     "q38_ctx_destroy": (c_int, [_VP]),
     "q38_bind_full_layer": (c_int, [_VP, c_int, _VP, _VP]),
     "q38_bind_linear_layer": (c_int, [_VP, c_int, _VP, _VP, _VP, _VP]),
+    "q38_gguf_read_f32": (c_int, [c_char_p, c_char_p, _VP, ctypes.c_int64]),
+    "q38_bind_gguf": (c_int, [_VP, c_char_p, c_int, c_int]),
     "q38_state_create": (c_int, [_VP, c_int, c_int, c_int, c_int, c_int, POINTER(c_void_p)]),
     "q38_state_destroy": (c_int, [_VP]),
     "q38_state_reset": (c_int, [_VP, _VP]),
