@@ -263,11 +263,6 @@ constexpr int kQueryWarps = 8;         // warps 1-8 prepare the query rows (two 
 
 // Arrival on a barrier of the leader CTA (cluster address), ordered like the
 // local tcgen05 handshakes (tcgen05.wait + fence::before_thread_sync first).
-// Named barrier over `threads` threads (barrier 0 is __syncthreads).
-__device__ __forceinline__ void named_barrier_sync(int id, int threads) {
-    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
-}
-
 __device__ __forceinline__ void mbar_arrive_leader(uint32_t cluster_bar) {
     asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
 }

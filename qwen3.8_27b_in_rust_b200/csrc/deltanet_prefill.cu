@@ -159,9 +159,10 @@ struct LocalParams {
     __nv_bfloat16 *w2;           // [planes][2][64 r][128 i]   W
     __nv_bfloat16 *q2;           // [planes][2][64 r][128 i]   Q~ = diag(e^gamma) Q
     __nv_bfloat16 *p2;           // [planes][2][64 r][64 s]    P
-    __nv_bfloat16 *k2;           // [planes][2][128 i][64 r]   K~^T = (diag(e^{gamma_C-gamma}) K)^T
+    __nv_bfloat16 *k2;           // [planes][2][64 r][128 i]   K~ = diag(e^{gamma_C-gamma}) K
     float *ut_out;               // [planes][64][128]          Ut (f32)
     float *eg_out;               // [planes][64]               e^{gamma_r}
+    int *err;
     int count, nchunk, qk_heads, v_heads, qkv_dim;
 };
 
@@ -173,88 +174,168 @@ __device__ __forceinline__ void split_bf16x2(float a, float b, uint32_t &hi, uin
     lo = pack_bf16x2_rn(a - hf.x, b - hf.y);
 }
 
-constexpr int kPad = kD + 1;  // padded smem rows (bank-conflict-free column walks)
+constexpr int kPadA = kC + 1;  // padded f32 rows of A and T (conflict-free column walks)
 
-// One CTA per (chunk, key head, sequence). The value heads h with
-// h % qk_heads == kh (ops.rs:699) share the chunk's K and Q, so K K^T and
-// Q K^T are computed once (held in registers, 4x4 per thread) and reused for
-// each of them; per value head only the decay/beta scaling, the triangular
-// solve and the two products with T differ.
+// Shared-memory plan of L3 (bytes). Region R is reused phase by phase:
+//   G phase:       [K; Q] hi | [K; Q] lo, each two SW128 boxes of 128 rows x 64 dims
+//   A/P phase:     A f32 [64][65] | decay factors [64][65] | ... | P staging (hi | lo) at 40 KB
+//   inverse phase: A f32 [64][65] | T f32 [64][65] | block products [3][16][16]
+//   MMA phase:     B_W hi | B_W lo | B_U hi | B_U lo, each two SW128 boxes of 64 rows x 64 cols
+//   epilogue:      W hi | W lo | Ut staging for coalesced stores
+// Staging tiles hold 16-byte chunk c of row r at chunk c ^ (r % chunks per
+// row), so that one-row-per-thread writes and one-chunk-per-lane reads are
+// both free of bank conflicts.
+// then Tu = T diag(beta) hi | lo (SW128, 64 rows x 64 columns; an M=128 MMA
+// also reads 64 further rows, so 8 KB of padding follow), then the barriers.
+constexpr uint32_t kLocR = 64 * 1024;
+constexpr uint32_t kLocKQBox = 128 * 128;          // 128 rows x 128 B
+constexpr uint32_t kLocBBox = 64 * 128;            // 64 rows x 128 B
+constexpr uint32_t kLocTs = kC * kPadA * 4;        // offset of T within R
+constexpr uint32_t kLocXs = 2 * kC * kPadA * 4;    // offset of the block products
+constexpr uint32_t kLocPst = 40 * 1024;            // P (hi | lo) staging during the A/P phase
+constexpr uint32_t kLocTu = kLocR;                 // Tu hi at +0, lo at +8 KB, padding +16 KB
+constexpr uint32_t kLocSmem = kLocR + 3 * 8192 + 1024;
+static_assert(kLocXs + 3 * 256 * 4 <= kLocPst && kLocPst + 2 * kC * kC * 2 <= kLocR,
+              "inverse workspace and P staging fit R");
+constexpr uint32_t kLocTmemCols = 256;  // G (64) while it is read out, then W (128) | Ut (128)
+
+// e^x for the in-chunk decay factors e^{gamma_r - gamma_s} (x <= 0): the
+// hardware exp2 of x log2(e). Relative error ~1e-6 for |x| < 20 (smaller
+// factors vanish against the others), below the ~1e-5 of the bf16-pair
+// products these factors feed.
+__device__ __forceinline__ float decay_exp(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x * 1.4426950408889634f));
+    return y;
+}
+
+// Byte offset of 16-byte chunk c of row r in a staging tile of `chunks`
+// chunks per row (a power of two).
+__device__ __forceinline__ uint32_t stage_at(uint32_t r, uint32_t c, uint32_t chunks) {
+    return (r * chunks + (c ^ (r & (chunks - 1)))) * 16u;
+}
+
+// Element (row, col) of a SW128 tile of 64-column (128-byte) rows.
+__device__ __forceinline__ uint32_t sw128_bf16_at(uint32_t row, uint32_t col) {
+    return row * 128u + ((((col & 63u) >> 3) ^ (row & 7u)) << 4) + (col & 7u) * 2u;
+}
+
+// One CTA per (chunk, key head, sequence); 8 warps, two CTAs per SM. The
+// value heads h with h % qk_heads == kh (ops.rs:699) share the chunk's K and
+// Q, so G = [K; Q] K^T (K K^T in TMEM lanes 0-63, Q K^T in lanes 64-127) is
+// one M=128, N=64, K=128 tcgen05 product, read out once into registers
+// (thread = row, 32 columns). Per value head: A and P from G on the CUDA
+// cores, the blocked inverse T = (I + A)^-1 in f32, then W = Tu (e^gamma K)
+// and Ut = Tu V with Tu = T diag(beta) as two M=128 (64 real rows), N=128,
+// K=64 products. Every product is hi.hi + lo.hi + hi.lo of bf16 pairs
+// (kind::f16, f32 accumulation), the same ~16-bit operands as the state pass.
 __global__ void __launch_bounds__(256, 2) linear_prefill_local_kernel(LocalParams p) {
-    extern __shared__ float sm[];
-    float *Ks = sm;                  // [64][129]
-    float *Xs = Ks + kC * kPad;      // [64][129]  Q, then V of each head
-    float *As = Xs + kC * kPad;      // [64][65]
-    float *Ts = As + kC * (kC + 1);  // [64][65]
+    using namespace sm100;
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    unsigned char *smem =
+        reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    unsigned char *R = smem;
+    unsigned char *tu_hi = smem + kLocTu, *tu_lo = tu_hi + 8192;
+    float *As = reinterpret_cast<float *>(R);
+    float *Ts = reinterpret_cast<float *>(R + kLocTs);
+    float *Xs = reinterpret_cast<float *>(R + kLocXs);
     __shared__ float gam[kC], bet[kC], egs[kC], dec[kC];
+    __shared__ __align__(8) uint64_t g_done, mma_done;
+    __shared__ uint32_t tmem_base_s;
 
     const int chunk = blockIdx.x, kh = blockIdx.y, s = blockIdx.z;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int t0 = chunk * kC;
     const int qk_dim = p.qk_heads * kD;
+    const float *rows = p.qkv + (size_t(s) * p.count + t0) * p.qkv_dim;  // the chunk's first row
+    auto row_ok = [&](int r) { return t0 + r < p.count; };
 
-    // Load K and Q rows of the chunk (zero rows past the prompt's end).
-    for (int idx = tid; idx < kC * (kD / 4); idx += 256) {
-        const int r = idx / (kD / 4), c4 = idx % (kD / 4);
-        float4 k = make_float4(0.f, 0.f, 0.f, 0.f), q = k;
-        if (t0 + r < p.count) {
-            const float *row = p.qkv + (size_t(s) * p.count + t0 + r) * p.qkv_dim;
-            k = reinterpret_cast<const float4 *>(row + qk_dim + kh * kD)[c4];
-            q = reinterpret_cast<const float4 *>(row + kh * kD)[c4];
-        }
-        float *kd = Ks + r * kPad + c4 * 4;
-        float *qd = Xs + r * kPad + c4 * 4;
-        kd[0] = k.x; kd[1] = k.y; kd[2] = k.z; kd[3] = k.w;
-        qd[0] = q.x; qd[1] = q.y; qd[2] = q.z; qd[3] = q.w;
+    if (tid == 0) {
+        mbar_init(&g_done, 1);
+        mbar_init(&mma_done, 1);
+        fence_barrier_init();
     }
+    if (warp == 0) {
+        tmem_alloc(&tmem_base_s, kLocTmemCols);
+        tmem_relinquish();
+    }
+    // [K; Q] as bf16 (hi, lo) in SW128 K-major boxes; rows past the prompt's
+    // end are zero. Thread: row = tid / 2, 64 dims.
+    {
+        const int row = tid >> 1, half = tid & 1;  // row < 128: 0-63 K, 64-127 Q
+        const int r = row & 63;
+        const float *src = rows + size_t(r) * p.qkv_dim + (row < kC ? qk_dim : 0) + kh * kD + half * 64;
+        unsigned char *hi = R + half * kLocKQBox, *lo = R + 2 * kLocKQBox + half * kLocKQBox;
+        float4 v[16];  // all loads in flight before any shared-memory store
+#pragma unroll
+        for (int i = 0; i < 16; ++i)
+            v[i] = row_ok(r) ? __ldg(reinterpret_cast<const float4 *>(src) + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int c8 = 0; c8 < 8; ++c8) {
+            const float4 a = v[2 * c8], b = v[2 * c8 + 1];
+            uint4 h, l;
+            split_bf16x2(a.x, a.y, h.x, l.x);
+            split_bf16x2(a.z, a.w, h.y, l.y);
+            split_bf16x2(b.x, b.y, h.z, l.z);
+            split_bf16x2(b.z, b.w, h.w, l.w);
+            const uint32_t off = sw128_bf16_at(uint32_t(row), uint32_t(8 * c8));
+            *reinterpret_cast<uint4 *>(hi + off) = h;
+            *reinterpret_cast<uint4 *>(lo + off) = l;
+        }
+        // Tu's padding rows (read by the M=128 MMAs, results unused): zeros.
+        for (int i = tid; i < 8192 / 16; i += 256)
+            reinterpret_cast<uint4 *>(tu_hi + 2 * 8192)[i] = make_uint4(0u, 0u, 0u, 0u);
+    }
+    fence_proxy_async_smem();
+    fence_before_sync();
     __syncthreads();
+    fence_after_sync();
+    const uint32_t tmem = tmem_base_s;
+    bool ok = true;
 
-    // K K^T and Q K^T: thread (ty, tx) of a 16x16 grid owns rows 4ty..,
-    // columns 4tx.. of both.
-    const int ty = tid / 16, tx = tid % 16;
-    // Accumulators as column pairs (packed f32x2 fma, the same rounding as fmaf).
-    float2 akk2[4][2], aqk2[4][2];
+    if (tid == 0) {
+        const uint32_t idesc = idesc_bf16_f32(128, kC, 0, 0);
+        const uint32_t kq_hi = smem_addr(R), kq_lo = kq_hi + 2 * kLocKQBox;
+#pragma unroll 1
+        for (int prod = 0; prod < 3; ++prod) {  // hi.hi, lo.hi, hi.lo
+            const uint32_t a_base = prod == 1 ? kq_lo : kq_hi;
+            const uint32_t b_base = prod == 2 ? kq_lo : kq_hi;
 #pragma unroll
-    for (int a = 0; a < 4; ++a)
-#pragma unroll
-        for (int b = 0; b < 2; ++b) akk2[a][b] = aqk2[a][b] = make_float2(0.f, 0.f);
-    if (tx <= ty) {  // only the lower triangle (c <= r) is used
-#pragma unroll 4
-        for (int i = 0; i < kD; ++i) {
-            float kr[4], qr[4];
-            float2 kc2[2];
-#pragma unroll
-            for (int a = 0; a < 4; ++a) {
-                kr[a] = Ks[(4 * ty + a) * kPad + i];
-                qr[a] = Xs[(4 * ty + a) * kPad + i];
+            for (int kk = 0; kk < kD / 16; ++kk) {
+                const uint32_t off = (kk >> 2) * kLocKQBox + (kk & 3) * 32;
+                mma_bf16(tmem, smem_desc_sw128(a_base + off, 16, 1024),
+                         smem_desc_sw128(b_base + off, 16, 1024), idesc, (prod | kk) ? 1u : 0u);
             }
-            kc2[0] = make_float2(Ks[(4 * tx + 0) * kPad + i], Ks[(4 * tx + 1) * kPad + i]);
-            kc2[1] = make_float2(Ks[(4 * tx + 2) * kPad + i], Ks[(4 * tx + 3) * kPad + i]);
-#pragma unroll
-            for (int a = 0; a < 4; ++a)
-#pragma unroll
-                for (int b = 0; b < 2; ++b) {
-                    akk2[a][b] = ffma2(make_float2(kr[a], kr[a]), kc2[b], akk2[a][b]);
-                    aqk2[a][b] = ffma2(make_float2(qr[a], qr[a]), kc2[b], aqk2[a][b]);
-                }
         }
+        mma_commit(&g_done);
     }
-    float akk[4][4], aqk[4][4];
+    // G -> registers: warps 0, 1, 4, 5 hold K K^T rows, warps 2, 3, 6, 7 Q K^T
+    // rows (TMEM lane quarter = warp % 4); warps 0-3 columns 0-31, 4-7 32-63.
+    const bool is_kk = (warp & 3) < 2;
+    const int gr = 32 * (warp & 1) + lane;  // row of K K^T or Q K^T
+    const int gc0 = warp < 4 ? 0 : 32;
+    float gv[32];
+    {
+        ok = __all_sync(0xffffffffu, mbar_wait(&g_done, 0));
+        fence_after_sync();
+        uint32_t raw[32];
+        tmem_ld32(tmem + (uint32_t(32 * (warp & 3)) << 16) + uint32_t(gc0), raw);
+        tmem_wait_ld();
 #pragma unroll
-    for (int a = 0; a < 4; ++a)
-#pragma unroll
-        for (int b = 0; b < 2; ++b) {
-            akk[a][2 * b] = akk2[a][b].x;
-            akk[a][2 * b + 1] = akk2[a][b].y;
-            aqk[a][2 * b] = aqk2[a][b].x;
-            aqk[a][2 * b + 1] = aqk2[a][b].y;
-        }
+        for (int i = 0; i < 32; ++i) gv[i] = __uint_as_float(raw[i]);
+    }
+    if (!ok && lane == 0) set_error(p.err, kDevErrTimeout);
 
-    for (int h = kh; h < p.v_heads; h += p.qk_heads) {
+    const uint32_t idesc_x = idesc_bf16_f32(128, kD, 0, 1);
+    const uint32_t d_w = tmem, d_u = tmem + kD;  // W columns 0-127, Ut columns 128-255
+    int head_i = 0;
+    for (int h = kh; h < p.v_heads; h += p.qk_heads, ++head_i) {
         const size_t plane = (size_t(s) * p.nchunk + chunk) * p.v_heads + h;
-        __syncthreads();  // previous head done with gam/bet/As/Ts/Xs
+        fence_before_sync();
+        __syncthreads();  // previous head done with R, gam/bet and TMEM
+        fence_after_sync();
         if (tid < kC) {
-            const bool in = t0 + tid < p.count;
+            const bool in = row_ok(tid);
             const size_t gi = (size_t(s) * p.count + t0 + tid) * p.v_heads + h;
             bet[tid] = in ? p.beta[gi] : 0.f;
             gam[tid] = in ? p.alpha[gi] : 0.f;
@@ -279,49 +360,78 @@ __global__ void __launch_bounds__(256, 2) linear_prefill_local_kernel(LocalParam
             egs[tid] = expf(gam[tid]);
             dec[tid] = expf(gam[kC - 1] - gam[tid]);
         }
-        // A = beta_r e^{gamma_r - gamma_s} K K^T (strictly lower) and
-        // P = e^{gamma_r - gamma_s} Q K^T (lower) for this head.
+        // A = beta_r e^{gamma_r - gamma_s} K K^T (strictly lower) into smem;
+        // P = e^{gamma_r - gamma_s} Q K^T (lower) as bf16 pairs to global. The
+        // K K^T warp of a (rows, columns) block computes the decay factors and
+        // hands them to the Q K^T warp of the same block through smem (Ts,
+        // not yet in use).
         {
-            __nv_bfloat16 *ph = p.p2 + plane * 2 * kC * kC, *pl = ph + kC * kC;
+            const int r = gr;
+            float *Dm = Ts;
+            if (is_kk) {
 #pragma unroll
-            for (int a = 0; a < 4; ++a) {
-                const int r = 4 * ty + a;
-                float pv[4];
-#pragma unroll
-                for (int b = 0; b < 4; ++b) {
-                    const int c = 4 * tx + b;
-                    const float d = (c <= r) ? expf(gam[r] - gam[c]) : 0.f;
-                    As[r * (kC + 1) + c] = c < r ? bet[r] * d * akk[a][b] : 0.f;
-                    pv[b] = c <= r ? d * aqk[a][b] : 0.f;
+                for (int i = 0; i < 32; ++i) {
+                    const int c = gc0 + i;
+                    const float d = (c <= r) ? decay_exp(gam[r] - gam[c]) : 0.f;
+                    Dm[r * kPadA + c] = d;
+                    As[r * kPadA + c] = c < r ? bet[r] * d * gv[i] : 0.f;
                 }
-                uint2 hv, lv;
-                split_bf16x2(pv[0], pv[1], hv.x, lv.x);
-                split_bf16x2(pv[2], pv[3], hv.y, lv.y);
-                *reinterpret_cast<uint2 *>(ph + r * kC + 4 * tx) = hv;
-                *reinterpret_cast<uint2 *>(pl + r * kC + 4 * tx) = lv;
+            }
+            __syncthreads();
+            if (!is_kk) {
+                unsigned char *pst = R + kLocPst;
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    float pv[8];
+#pragma unroll
+                    for (int b = 0; b < 8; ++b) {
+                        const int c = gc0 + 8 * q + b;
+                        pv[b] = c <= r ? Dm[r * kPadA + c] * gv[8 * q + b] : 0.f;
+                    }
+                    uint4 hq, lq;
+                    split_bf16x2(pv[0], pv[1], hq.x, lq.x);
+                    split_bf16x2(pv[2], pv[3], hq.y, lq.y);
+                    split_bf16x2(pv[4], pv[5], hq.z, lq.z);
+                    split_bf16x2(pv[6], pv[7], hq.w, lq.w);
+                    const uint32_t off = stage_at(uint32_t(r), uint32_t(gc0 / 8 + q), 8);
+                    *reinterpret_cast<uint4 *>(pst + off) = hq;
+                    *reinterpret_cast<uint4 *>(pst + kC * kC * 2 + off) = lq;
+                }
             }
         }
         __syncthreads();
+        {
+            // P (hi | lo) to global, one 16-byte chunk per lane.
+            const unsigned char *pst = R + kLocPst;
+            uint4 *dst = reinterpret_cast<uint4 *>(p.p2 + plane * 2 * kC * kC);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const int idx = tid + 256 * k, pl = idx >> 9, r = (idx >> 3) & 63, c = idx & 7;
+                dst[idx] = *reinterpret_cast<const uint4 *>(pst + pl * kC * kC * 2 + stage_at(r, c, 8));
+            }
+        }
 
         // T = (I + A)^-1 in 16x16 blocks (A strictly lower). The diagonal
         // blocks T_ii = (I + A_ii)^-1 by forward substitution, one warp each;
         // then the block sub-diagonals d = 1, 2, 3 in turn:
         //   T_ij = -T_ii sum_{k=j}^{i-1} A_ik T_kj   (j = i - d).
-        // The block products go to Xs (free until V is loaded).
-        for (int idx = tid; idx < kC * (kC + 1); idx += 256) Ts[idx] = 0.f;
+        for (int idx = tid; idx < kC * kPadA; idx += 256) Ts[idx] = 0.f;
         __syncthreads();
         if (warp < 4 && lane < 16) {
+            // Column c of (I + A_ii)^-1 by right-looking forward substitution:
+            // once t[m] is final it updates every later row, so the dependent
+            // chain is 16 steps long instead of 120.
             const int b0 = warp * 16, c = lane;
-            float tcol[16];
+            float t[16];
 #pragma unroll
-            for (int r = 0; r < 16; ++r) {
-                float acc = (r == c) ? 1.f : 0.f;
+            for (int r = 0; r < 16; ++r) t[r] = (r == c) ? 1.f : 0.f;
 #pragma unroll
-                for (int m = 0; m < r; ++m) acc = fmaf(-As[(b0 + r) * (kC + 1) + b0 + m], tcol[m], acc);
-                tcol[r] = (r < c) ? 0.f : acc;
+            for (int m = 0; m < 15; ++m) {
+#pragma unroll
+                for (int r = m + 1; r < 16; ++r) t[r] = fmaf(-As[(b0 + r) * kPadA + b0 + m], t[m], t[r]);
             }
 #pragma unroll
-            for (int r = 0; r < 16; ++r) Ts[(b0 + r) * (kC + 1) + b0 + c] = tcol[r];
+            for (int r = 0; r < 16; ++r) Ts[(b0 + r) * kPadA + b0 + c] = t[r];
         }
         __syncthreads();
         for (int d = 1; d < 4; ++d) {
@@ -333,8 +443,8 @@ __global__ void __launch_bounds__(256, 2) linear_prefill_local_kernel(LocalParam
                 for (int k = j; k < i; ++k)
 #pragma unroll
                     for (int m = 0; m < 16; ++m)
-                        acc = fmaf(As[(16 * i + r) * (kC + 1) + 16 * k + m],
-                                   Ts[(16 * k + m) * (kC + 1) + 16 * j + c], acc);
+                        acc = fmaf(As[(16 * i + r) * kPadA + 16 * k + m],
+                                   Ts[(16 * k + m) * kPadA + 16 * j + c], acc);
                 Xs[idx] = acc;
             }
             __syncthreads();
@@ -344,95 +454,201 @@ __global__ void __launch_bounds__(256, 2) linear_prefill_local_kernel(LocalParam
                 float acc = 0.f;
 #pragma unroll
                 for (int m = 0; m < 16; ++m)
-                    acc = fmaf(Ts[(16 * i + r) * (kC + 1) + 16 * i + m], Xs[(blk << 8) + m * 16 + c], acc);
-                Ts[(16 * i + r) * (kC + 1) + 16 * j + c] = -acc;
+                    acc = fmaf(Ts[(16 * i + r) * kPadA + 16 * i + m], Xs[(blk << 8) + m * 16 + c], acc);
+                Ts[(16 * i + r) * kPadA + 16 * j + c] = -acc;
             }
             __syncthreads();
         }
-
-        // W = T diag(beta e^gamma) K and Ut = T diag(beta) V. Thread: 8 rows
-        // x 4 columns; T is lower triangular, so rows rb*8.. stop at m < rb*8+8.
-        const size_t wbase = plane * kC * kD;
-        const int rb = tid / 32, cg = tid % 32;
-        auto tri_times = [&](const float *X, const float *scale_b, auto &&store) {
-            float2 acc[8][2];
+        // Tu = T diag(beta) as bf16 pairs (K-major A operand): thread = (row
+        // tid / 4, 16 columns).
+        {
+            const int r = tid >> 2, m0 = 16 * (tid & 3);
 #pragma unroll
-            for (int a = 0; a < 8; ++a) acc[a][0] = acc[a][1] = make_float2(0.f, 0.f);
-            const int mend = rb * 8 + 8;
-#pragma unroll 4
-            for (int m = 0; m < mend; ++m) {
-                const float f = bet[m] * (scale_b ? scale_b[m] : 1.f);
-                const float *xr = X + m * kPad + cg * 4;
-                const float2 x0 = make_float2(xr[0] * f, xr[1] * f);
-                const float2 x1 = make_float2(xr[2] * f, xr[3] * f);
+            for (int c8 = 0; c8 < 2; ++c8) {
+                float v[8];
 #pragma unroll
-                for (int a = 0; a < 8; ++a) {
-                    const float tv = Ts[(rb * 8 + a) * (kC + 1) + m];
-                    acc[a][0] = ffma2(make_float2(tv, tv), x0, acc[a][0]);
-                    acc[a][1] = ffma2(make_float2(tv, tv), x1, acc[a][1]);
+                for (int e = 0; e < 8; ++e) v[e] = Ts[r * kPadA + m0 + 8 * c8 + e] * bet[m0 + 8 * c8 + e];
+                uint4 hq, lq;
+                split_bf16x2(v[0], v[1], hq.x, lq.x);
+                split_bf16x2(v[2], v[3], hq.y, lq.y);
+                split_bf16x2(v[4], v[5], hq.z, lq.z);
+                split_bf16x2(v[6], v[7], hq.w, lq.w);
+                const uint32_t off = sw128_bf16_at(uint32_t(r), uint32_t(m0 + 8 * c8));
+                *reinterpret_cast<uint4 *>(tu_hi + off) = hq;
+                *reinterpret_cast<uint4 *>(tu_lo + off) = lq;
+            }
+        }
+        __syncthreads();  // T and A are consumed: R takes the B operands
+        // B_W = diag(e^gamma) K and B_U = V (MN-major: rows m, 128 columns in
+        // two SW128 boxes), and K~ = diag(e^{gamma_C - gamma}) K (bf16 pairs,
+        // row-major, the state update's MN-major B operand) from the same K
+        // registers. Thread: 8 columns (chunk tid % 16) of rows tid / 16 + 16 k.
+        {
+            const int c = tid & 15;
+            unsigned char *bw_hi = R, *bw_lo = R + 2 * kLocBBox, *bu_hi = R + 4 * kLocBBox,
+                          *bu_lo = R + 6 * kLocBBox;
+            const uint32_t box = (c >> 3) * kLocBBox;
+            __nv_bfloat16 *kth = p.k2 + plane * 2 * kC * kD + 8 * c, *ktl = kth + kC * kD;
+            float4 x[8];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const int m = (tid >> 4) + 16 * k;
+                const float *krow = rows + size_t(m) * p.qkv_dim + qk_dim + kh * kD + 8 * c;
+                x[2 * k] = row_ok(m) ? __ldg(reinterpret_cast<const float4 *>(krow)) : make_float4(0.f, 0.f, 0.f, 0.f);
+                x[2 * k + 1] = row_ok(m) ? __ldg(reinterpret_cast<const float4 *>(krow) + 1) : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const int m = (tid >> 4) + 16 * k;
+                const float e = egs[m], dk = dec[m];
+                const float4 ka = x[2 * k], kb = x[2 * k + 1];
+                const uint32_t off = box + sw128_bf16_at(uint32_t(m), uint32_t(8 * c));
+                uint4 hq, lq;
+                split_bf16x2(ka.x * e, ka.y * e, hq.x, lq.x);
+                split_bf16x2(ka.z * e, ka.w * e, hq.y, lq.y);
+                split_bf16x2(kb.x * e, kb.y * e, hq.z, lq.z);
+                split_bf16x2(kb.z * e, kb.w * e, hq.w, lq.w);
+                *reinterpret_cast<uint4 *>(bw_hi + off) = hq;
+                *reinterpret_cast<uint4 *>(bw_lo + off) = lq;
+                split_bf16x2(dk * ka.x, dk * ka.y, hq.x, lq.x);
+                split_bf16x2(dk * ka.z, dk * ka.w, hq.y, lq.y);
+                split_bf16x2(dk * kb.x, dk * kb.y, hq.z, lq.z);
+                split_bf16x2(dk * kb.z, dk * kb.w, hq.w, lq.w);
+                *reinterpret_cast<uint4 *>(kth + m * kD) = hq;
+                *reinterpret_cast<uint4 *>(ktl + m * kD) = lq;
+            }
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const int m = (tid >> 4) + 16 * k;
+                const float *vrow = rows + size_t(m) * p.qkv_dim + 2 * qk_dim + h * kD + 8 * c;
+                x[2 * k] = row_ok(m) ? __ldg(reinterpret_cast<const float4 *>(vrow)) : make_float4(0.f, 0.f, 0.f, 0.f);
+                x[2 * k + 1] = row_ok(m) ? __ldg(reinterpret_cast<const float4 *>(vrow) + 1) : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const int m = (tid >> 4) + 16 * k;
+                const float4 va = x[2 * k], vb = x[2 * k + 1];
+                const uint32_t off = box + sw128_bf16_at(uint32_t(m), uint32_t(8 * c));
+                uint4 hq, lq;
+                split_bf16x2(va.x, va.y, hq.x, lq.x);
+                split_bf16x2(va.z, va.w, hq.y, lq.y);
+                split_bf16x2(vb.x, vb.y, hq.z, lq.z);
+                split_bf16x2(vb.z, vb.w, hq.w, lq.w);
+                *reinterpret_cast<uint4 *>(bu_hi + off) = hq;
+                *reinterpret_cast<uint4 *>(bu_lo + off) = lq;
+            }
+        }
+        fence_proxy_async_smem();
+        fence_before_sync();
+        __syncthreads();
+        if (tid == 0) {
+            fence_after_sync();
+            const uint32_t a_hi = smem_addr(tu_hi), a_lo = smem_addr(tu_lo);
+            const uint32_t bw_hi = smem_addr(R), bw_lo = bw_hi + 2 * kLocBBox;
+            const uint32_t bu_hi = bw_hi + 4 * kLocBBox, bu_lo = bw_hi + 6 * kLocBBox;
+#pragma unroll 1
+            for (int prod = 0; prod < 3; ++prod) {
+                const uint32_t a = prod == 1 ? a_lo : a_hi;
+#pragma unroll
+                for (int kk = 0; kk < kC / 16; ++kk) {
+                    const uint64_t ad = smem_desc_sw128(a + kk * 32, 16, 1024);
+                    const uint32_t acc = (prod | kk) ? 1u : 0u;
+                    mma_bf16(d_w, ad, smem_desc_sw128((prod == 2 ? bw_lo : bw_hi) + kk * 2048, kLocBBox, 1024),
+                             idesc_x, acc);
+                    mma_bf16(d_u, ad, smem_desc_sw128((prod == 2 ? bu_lo : bu_hi) + kk * 2048, kLocBBox, 1024),
+                             idesc_x, acc);
                 }
             }
+            mma_commit(&mma_done);
+        }
+        if (!__all_sync(0xffffffffu, mbar_wait(&mma_done, uint32_t(head_i & 1)))) {
+            if (lane == 0) set_error(p.err, kDevErrTimeout);
+        }
+        fence_after_sync();
+        if (is_kk) {
+            // W (bf16 pairs) and Ut (f32) rows 0-63 from TMEM lanes 0-63
+            // (warps 0, 1 columns 0-63, warps 4, 5 columns 64-127), staged in R
+            // (free once the MMAs have completed) and stored one 16-byte chunk
+            // per lane by these four warps.
+            const int r = gr, cbase = warp < 4 ? 0 : 64;
+            const uint32_t lane_addr = uint32_t(32 * (warp & 3)) << 16;
+            unsigned char *wst = R, *ust = R + 2 * kC * kD * 2;  // W hi | W lo | Ut
+#pragma unroll 1
+            for (int c32 = 0; c32 < 2; ++c32) {
+                const int c = cbase + 32 * c32;
+                uint32_t w[32], u[32];
+                tmem_ld32(d_w + lane_addr + uint32_t(c), w);
+                tmem_ld32(d_u + lane_addr + uint32_t(c), u);
+                tmem_wait_ld();
 #pragma unroll
-            for (int a = 0; a < 8; ++a) {
-                const float v[4] = {acc[a][0].x, acc[a][0].y, acc[a][1].x, acc[a][1].y};
-                store(rb * 8 + a, cg, v);
+                for (int q = 0; q < 4; ++q) {
+                    uint4 hq, lq;
+                    split_bf16x2(__uint_as_float(w[8 * q + 0]), __uint_as_float(w[8 * q + 1]), hq.x, lq.x);
+                    split_bf16x2(__uint_as_float(w[8 * q + 2]), __uint_as_float(w[8 * q + 3]), hq.y, lq.y);
+                    split_bf16x2(__uint_as_float(w[8 * q + 4]), __uint_as_float(w[8 * q + 5]), hq.z, lq.z);
+                    split_bf16x2(__uint_as_float(w[8 * q + 6]), __uint_as_float(w[8 * q + 7]), hq.w, lq.w);
+                    const uint32_t off = stage_at(uint32_t(r), uint32_t(c / 8 + q), 16);
+                    *reinterpret_cast<uint4 *>(wst + off) = hq;
+                    *reinterpret_cast<uint4 *>(wst + kC * kD * 2 + off) = lq;
+                }
+#pragma unroll
+                for (int q = 0; q < 8; ++q)
+                    *reinterpret_cast<uint4 *>(ust + stage_at(uint32_t(r), uint32_t(c / 4 + q), 32)) =
+                        make_uint4(u[4 * q], u[4 * q + 1], u[4 * q + 2], u[4 * q + 3]);
             }
-        };
-        // W as bf16 (hi, lo).
-        __nv_bfloat16 *wh = p.w2 + plane * 2 * kC * kD, *wl = wh + kC * kD;
-        tri_times(Ks, egs, [&](int r, int c4, const float (&v)[4]) {
-            uint2 hv, lv;
-            split_bf16x2(v[0], v[1], hv.x, lv.x);
-            split_bf16x2(v[2], v[3], hv.y, lv.y);
-            *reinterpret_cast<uint2 *>(wh + r * kD + c4 * 4) = hv;
-            *reinterpret_cast<uint2 *>(wl + r * kD + c4 * 4) = lv;
-        });
-        // K~^T[i][r] = e^{gamma_C - gamma_r} K[r][i] (the state update's B operand).
-        {
-            __nv_bfloat16 *kth = p.k2 + plane * 2 * kD * kC, *ktl = kth + kD * kC;
-            for (int idx = tid; idx < kD * kC / 2; idx += 256) {
-                const int i = idx / (kC / 2), r = 2 * (idx % (kC / 2));
-                uint32_t hv, lv;
-                split_bf16x2(dec[r] * Ks[r * kPad + i], dec[r + 1] * Ks[(r + 1) * kPad + i], hv, lv);
-                reinterpret_cast<uint32_t *>(kth)[idx] = hv;
-                reinterpret_cast<uint32_t *>(ktl)[idx] = lv;
+            named_barrier_sync(1, 128);  // the four K K^T warps
+            const int t = 32 * ((warp & 1) + 2 * (warp >> 2)) + lane;  // 0..127
+            uint4 *wdst = reinterpret_cast<uint4 *>(p.w2 + plane * 2 * kC * kD);
+#pragma unroll 4
+            for (int k = 0; k < 16; ++k) {  // W hi | lo: 2 x 64 rows x 16 chunks
+                const int idx = t + 128 * k, pl = idx >> 10, rr = (idx >> 4) & 63, cc = idx & 15;
+                wdst[idx] = *reinterpret_cast<const uint4 *>(wst + pl * kC * kD * 2 + stage_at(rr, cc, 16));
             }
+            uint4 *udst = reinterpret_cast<uint4 *>(p.ut_out + plane * kC * kD);
+#pragma unroll 4
+            for (int k = 0; k < 16; ++k) {  // Ut: 64 rows x 32 chunks
+                const int idx = t + 128 * k, rr = idx >> 5, cc = idx & 31;
+                udst[idx] = *reinterpret_cast<const uint4 *>(ust + stage_at(rr, cc, 32));
+            }
+        } else {
+            // Warps 2, 3, 6, 7 (128 threads): Q~ = diag(e^gamma) Q from the
+            // normalised rows. Thread: 8 columns (chunk t % 16) of rows
+            // t / 16 + 8 k, one 16-byte chunk per lane in each store.
+            const int t = 32 * ((warp & 1) + 2 * (warp >> 2)) + lane;  // 0..127
+            const int c = t & 15;
+            __nv_bfloat16 *qh = p.q2 + plane * 2 * kC * kD + 8 * c, *ql = qh + kC * kD;
+#pragma unroll
+            for (int half = 0; half < 2; ++half) {
+                float4 x[8];
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    const int r = (t >> 4) + 8 * (4 * half + k);
+                    const float4 *q4 = reinterpret_cast<const float4 *>(rows + size_t(r) * p.qkv_dim + kh * kD + 8 * c);
+                    x[2 * k] = row_ok(r) ? __ldg(q4) : make_float4(0.f, 0.f, 0.f, 0.f);
+                    x[2 * k + 1] = row_ok(r) ? __ldg(q4 + 1) : make_float4(0.f, 0.f, 0.f, 0.f);
+                }
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    const int r = (t >> 4) + 8 * (4 * half + k);
+                    const float e = egs[r];
+                    const float4 a = x[2 * k], b = x[2 * k + 1];
+                    uint4 hq, lq;
+                    split_bf16x2(a.x * e, a.y * e, hq.x, lq.x);
+                    split_bf16x2(a.z * e, a.w * e, hq.y, lq.y);
+                    split_bf16x2(b.x * e, b.y * e, hq.z, lq.z);
+                    split_bf16x2(b.z * e, b.w * e, hq.w, lq.w);
+                    *reinterpret_cast<uint4 *>(qh + r * kD) = hq;
+                    *reinterpret_cast<uint4 *>(ql + r * kD) = lq;
+                }
+            }
+            if (t < kC) p.eg_out[plane * kC + t] = egs[t];
         }
-        // Q~ = diag(e^gamma) Q (Q re-read from the normalised qkv rows).
-        {
-            __nv_bfloat16 *qh = p.q2 + plane * 2 * kC * kD, *ql = qh + kC * kD;
-            for (int idx = tid; idx < kC * (kD / 4); idx += 256) {
-                const int r = idx / (kD / 4), c4 = idx % (kD / 4);
-                float4 q = make_float4(0.f, 0.f, 0.f, 0.f);
-                if (t0 + r < p.count)
-                    q = reinterpret_cast<const float4 *>(
-                        p.qkv + (size_t(s) * p.count + t0 + r) * p.qkv_dim + kh * kD)[c4];
-                const float e = egs[r];
-                uint2 hv, lv;
-                split_bf16x2(q.x * e, q.y * e, hv.x, lv.x);
-                split_bf16x2(q.z * e, q.w * e, hv.y, lv.y);
-                *reinterpret_cast<uint2 *>(qh + r * kD + c4 * 4) = hv;
-                *reinterpret_cast<uint2 *>(ql + r * kD + c4 * 4) = lv;
-            }
-        }
-        if (tid < kC) p.eg_out[plane * kC + tid] = egs[tid];
-        __syncthreads();  // Xs (block products) is no longer needed: load V
-        for (int idx = tid; idx < kC * (kD / 4); idx += 256) {
-            const int r = idx / (kD / 4), c4 = idx % (kD / 4);
-            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (t0 + r < p.count) {
-                const float *row = p.qkv + (size_t(s) * p.count + t0 + r) * p.qkv_dim;
-                v = reinterpret_cast<const float4 *>(row + 2 * qk_dim + h * kD)[c4];
-            }
-            float *vd = Xs + r * kPad + c4 * 4;
-            vd[0] = v.x; vd[1] = v.y; vd[2] = v.z; vd[3] = v.w;
-        }
-        __syncthreads();
-        float *ut = p.ut_out + wbase;
-        tri_times(Xs, nullptr, [&](int r, int c4, const float (&v)[4]) {
-            reinterpret_cast<float4 *>(ut + r * kD)[c4] = make_float4(v[0], v[1], v[2], v[3]);
-        });
+        tmem_wait_ld();
     }
+    fence_before_sync();
+    __syncthreads();
+    fence_after_sync();
+    if (warp == 0) tmem_dealloc(tmem, kLocTmemCols);
 }
 
 // ----------------------------------------------------------------------------
@@ -454,7 +670,7 @@ __global__ void __launch_bounds__(256, 2) linear_prefill_local_kernel(LocalParam
 constexpr int kThreadsLS = 352;  // w0 TMA, w1 MMA (S products), w2-5 + w7-10 epilogue, w6 MMA (P U^T)
 constexpr uint32_t kB1Half = 128 * 128 * 2;   // [W ; Q~] hi or lo: 2 column blocks of 128 rows x 128 B
 constexpr uint32_t kPmHalf = 64 * 64 * 2;     // P hi or lo: 64 rows x 128 B
-constexpr uint32_t kKtHalf = 128 * 64 * 2;    // K~^T hi or lo: 128 rows x 128 B
+constexpr uint32_t kKtHalf = 64 * 128 * 2;    // K~ hi or lo: 2 column blocks of 64 rows x 128 B
 constexpr uint32_t kStageLS = 2 * (kB1Half + kPmHalf + kKtHalf);  // 112 KB
 constexpr uint32_t kSmemLS = 2 * kStageLS + 1024;
 // TMEM columns: f32 state | S hi | S lo (bf16 pairs) | D_U | D_O | U^T hi | U^T lo | D_PU.
@@ -545,7 +761,7 @@ __global__ void __launch_bounds__(kThreadsLS, 1)
     };
 
     if (warp == 0) {
-        // ---------------------------------------------------------- TMA: [W ; Q~], P, K~^T
+        // ---------------------------------------------------------- TMA: [W ; Q~], P, K~
         if (lane == 0) {
             tma_prefetch_desc(&map_w);
             tma_prefetch_desc(&map_q);
@@ -571,8 +787,11 @@ __global__ void __launch_bounds__(kThreadsLS, 1)
                 tma_load_3d(pml(st), &map_p, 0, 0, pl2 + 1, &bar.p_full[st]);
                 if (c >= 2 && !mbar_wait(&bar.k_free[st], ph)) { fail(); break; }
                 mbar_arrive_expect_tx(&bar.k_full[st], 2 * kKtHalf);
-                tma_load_3d(kth(st), &map_kt, 0, 0, pl2, &bar.k_full[st]);
-                tma_load_3d(ktl(st), &map_kt, 0, 0, pl2 + 1, &bar.k_full[st]);
+                for (int blk = 0; blk < 2; ++blk) {
+                    tma_load_3d(kth(st) + blk * (kKtHalf / 2), &map_kt, blk * 64, 0, pl2, &bar.k_full[st]);
+                    tma_load_3d(ktl(st) + blk * (kKtHalf / 2), &map_kt, blk * 64, 0, pl2 + 1,
+                                &bar.k_full[st]);
+                }
             }
         }
     } else if (warp == 1) {
@@ -608,14 +827,18 @@ __global__ void __launch_bounds__(kThreadsLS, 1)
                     break;
                 }
                 fence_after_sync();
+                // K~ [64 r][128 i] is the MN-major B operand (K = r, N = i):
+                // K-step kk is 16 rows (2048 B) in, the two 64-column blocks
+                // are kKtHalf / 2 apart.
                 const uint32_t kh_ = smem_addr(kth(st)), kl_ = smem_addr(ktl(st));
+                const uint32_t id_n128_mn = idesc_bf16_f32(128, 128, 0, 1);
 #pragma unroll 1
                 for (int kk = 0; kk < kC / 16; ++kk) {
-                    const uint64_t dh = smem_desc_sw128(kh_ + kk * 32, 16, 1024);
-                    const uint64_t dl = smem_desc_sw128(kl_ + kk * 32, 16, 1024);
-                    mma_f16_ta(tmem + kColS, tmem + kColUh + kk * 8, dh, id_n128, 1u);
-                    mma_f16_ta(tmem + kColS, tmem + kColUl + kk * 8, dh, id_n128, 1u);
-                    mma_f16_ta(tmem + kColS, tmem + kColUh + kk * 8, dl, id_n128, 1u);
+                    const uint64_t dh = smem_desc_sw128(kh_ + kk * 2048, kKtHalf / 2, 1024);
+                    const uint64_t dl = smem_desc_sw128(kl_ + kk * 2048, kKtHalf / 2, 1024);
+                    mma_f16_ta(tmem + kColS, tmem + kColUh + kk * 8, dh, id_n128_mn, 1u);
+                    mma_f16_ta(tmem + kColS, tmem + kColUl + kk * 8, dh, id_n128_mn, 1u);
+                    mma_f16_ta(tmem + kColS, tmem + kColUh + kk * 8, dl, id_n128_mn, 1u);
                 }
                 mma_commit(&bar.s_done);
                 mma_commit(&bar.k_free[st]);
@@ -842,7 +1065,7 @@ __global__ void __launch_bounds__(256) linear_prefill_out_kernel(OutParams p) {
 
 size_t linear_prefill_scratch_floats(int nchunk_total, int v_heads) {
     // Per (chunk, value head), in f32 units: W, Q~ as bf16 (hi, lo) [2][64][128]
-    // (one f32 each per element pair), P [2][64][64] bf16, K~^T [2][128][64]
+    // (one f32 each per element pair), P [2][64][64] bf16, K~ [2][64][128]
     // bf16, Ut [64][128] f32, e^gamma [64] f32.
     return size_t(nchunk_total) * v_heads * kC * (4 * kD + kC + 1);
 }
@@ -873,21 +1096,20 @@ cudaError_t launch_linear_prefill(const LinearPrefillLaunch &a, cudaStream_t str
     __nv_bfloat16 *k2 = p2 + per * 2 * kC * kC;
     float *ut = reinterpret_cast<float *>(k2 + per * 2 * kD * kC);
     float *eg = ut + per * kC * kD;
-    LocalParams lp{a.qkv, a.beta, a.alpha, w2, q2, p2, k2, ut, eg, a.count, nchunk, a.qk_heads,
-                   a.v_heads, qkv_dim};
-    const size_t smem_l = size_t(2 * kC * kPad + 2 * kC * (kC + 1)) * sizeof(float);
+    LocalParams lp{a.qkv, a.beta, a.alpha, w2, q2, p2, k2, ut, eg, a.err, a.count, nchunk,
+                   a.qk_heads, a.v_heads, qkv_dim};
     if ((e = cudaFuncSetAttribute(linear_prefill_local_kernel,
-                                  cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem_l))) !=
+                                  cudaFuncAttributeMaxDynamicSharedMemorySize, int(kLocSmem))) !=
         cudaSuccess)
         return e;
-    linear_prefill_local_kernel<<<dim3(nchunk, a.qk_heads, a.nseq), 256, smem_l, stream>>>(lp);
+    linear_prefill_local_kernel<<<dim3(nchunk, a.qk_heads, a.nseq), 256, kLocSmem, stream>>>(lp);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
 
     CUtensorMap mw, mq, mp, mk;
     if (!make_map_bf16_ls(&mw, w2, kD, kC, 2 * per, kC) ||
         !make_map_bf16_ls(&mq, q2, kD, kC, 2 * per, kC) ||
         !make_map_bf16_ls(&mp, p2, kC, kC, 2 * per, kC) ||
-        !make_map_bf16_ls(&mk, k2, kC, kD, 2 * per, kD))
+        !make_map_bf16_ls(&mk, k2, kD, kC, 2 * per, kC))
         return cudaErrorInvalidValue;
     StateTcParams sp{ut, eg, a.delta_state, a.attention, a.err, a.seq0, a.count, nchunk,
                      a.qk_heads, a.v_heads};

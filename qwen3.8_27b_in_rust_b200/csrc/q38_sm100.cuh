@@ -48,6 +48,12 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
+// Named barrier over `threads` threads of the CTA (barrier 0 is
+// __syncthreads). Callers make sure every participating warp reaches it.
+__device__ __forceinline__ void named_barrier_sync(int id, int threads) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
 // ---------------------------------------------------------------- MMA
 // Shared-memory matrix descriptor (SM100 format): start address, leading and
 // stride byte offsets (all >> 4), version 1, layout type 2 = SWIZZLE_128B.
