@@ -18,12 +18,13 @@
 //   L1 linear_prefill_conv   one thread per (channel, 64-token segment,
 //                            sequence): the kernel-4 causal conv with the
 //                            carried state (multiply then add, ops.rs:665-676)
-//                            and SiLU, in place; a pre-pass saves the three
-//                            original inputs before each segment so segments
-//                            run in parallel; the last three inputs become the
-//                            new conv state.
-//   L2 linear_prefill_norm   one CTA per (token, sequence): L2-norm of the q and
-//                            k heads (f64 sums) and the beta/alpha gates, in place.
+//                            and SiLU, in place, then the L2-norm of the q and
+//                            k heads (f64 sums; a CTA's 128 channels are one
+//                            head); a pre-pass saves the three original inputs
+//                            before each segment so segments run in parallel;
+//                            the last three inputs become the new conv state.
+//   L2 linear_prefill_norm   one CTA per (token, sequence): the beta/alpha
+//                            gates, in place.
 //   L3 linear_prefill_local  one CTA per (chunk, key head, sequence): K K^T and
 //                            Q K^T once, then per value head of that key head
 //                            the chunk-local W, Ut, P, K~ and e^gamma (all
@@ -58,6 +59,9 @@ struct ConvParams {
     const float *conv_w; // [qkv_dim][4]
     float *bounds;       // [nseq][nseg][3][qkv_dim]: inputs preceding each segment
     int seq0, count, qkv_dim, nseg;
+    int qk_channels;     // 2 * qk_heads * 128: the q and k channels, L2-normalised per head
+    float eps;
+    int *err;
 };
 
 constexpr int kSeg = 64;  // tokens per conv segment
@@ -78,21 +82,52 @@ __global__ void __launch_bounds__(128) linear_prefill_conv_bounds_kernel(ConvPar
     }
 }
 
-// One thread per (channel, segment, sequence): the kernel-4 causal conv over
-// the segment (multiply then add, ops.rs:665-676) and SiLU, in place. The
-// last segment leaves the last three inputs as the new conv state.
-__global__ void __launch_bounds__(128) linear_prefill_conv_kernel(ConvParams p) {
-    const int c = blockIdx.x * 128 + threadIdx.x;
-    const int g = blockIdx.y, s = blockIdx.z;
-    if (c >= p.qkv_dim) return;
-    const float *bnd = p.bounds + (size_t(s) * p.nseg + g) * 3 * p.qkv_dim + c;
-    float s0 = bnd[0], s1 = bnd[p.qkv_dim], s2 = bnd[2 * size_t(p.qkv_dim)];
-    const float4 w = reinterpret_cast<const float4 *>(p.conv_w)[c];
-    const int t0 = g * kSeg, t1 = min(p.count, t0 + kSeg);
-    float *x = p.qkv + size_t(s) * p.count * p.qkv_dim + c;
+// One CTA per (128 channels, 64-token segment, sequence); the segment's
+// [64 tokens][128 channels] f32 tile comes in by one TMA load and goes back by
+// one TMA store (rows past the prompt's end read as zeros and are not
+// written). Thread = channel: the kernel-4 causal conv (multiply then add,
+// ops.rs:665-676) and SiLU, in place in shared memory; the last segment
+// leaves the last three inputs as the new conv state. The first qk_channels
+// channels are the q and k heads (a CTA's 128 channels are one head): those
+// rows are then L2-normalised per token (l2norm, ops.rs:562-571: f64 sum of
+// squares, 1 / max(sqrt, eps)), a warp per token, so L2 only handles the
+// gates.
+constexpr uint32_t kConvTileBytes = kSeg * 128 * 4;  // 32 KB
+
+__global__ void __launch_bounds__(128) linear_prefill_conv_kernel(const __grid_constant__ CUtensorMap map_x,
+                                                                   ConvParams p) {
+    using namespace sm100;
+    extern __shared__ __align__(128) float tile[];  // [kSeg][128]
+    __shared__ __align__(8) uint64_t bar;
+    const int cb = blockIdx.x, g = blockIdx.y, s = blockIdx.z;
+    const int c = cb * 128 + threadIdx.x;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const bool live = c < p.qkv_dim;
+    const int t0 = g * kSeg, n = min(p.count - t0, kSeg);
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        fence_barrier_init();
+        mbar_arrive_expect_tx(&bar, kConvTileBytes);
+        tma_load_3d(tile, &map_x, cb * 128, t0, s, &bar);
+    }
+    float s0 = 0.f, s1 = 0.f, s2 = 0.f;
+    float4 w = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (live) {
+        const float *bnd = p.bounds + (size_t(s) * p.nseg + g) * 3 * p.qkv_dim + c;
+        s0 = bnd[0];
+        s1 = bnd[p.qkv_dim];
+        s2 = bnd[2 * size_t(p.qkv_dim)];
+        w = reinterpret_cast<const float4 *>(p.conv_w)[c];
+    }
+    __syncthreads();  // barrier initialised before anyone waits on it
+    if (!__syncthreads_and(mbar_wait(&bar, 0))) {
+        if (threadIdx.x == 0) set_error(p.err, kDevErrTimeout);
+        return;  // (uniform) a TMA that never completed: nothing of this tile is written
+    }
+    float *col = tile + threadIdx.x;
 #pragma unroll 8
-    for (int t = t0; t < t1; ++t) {
-        const float xt = x[size_t(t) * p.qkv_dim];
+    for (int t = 0; t < n; ++t) {
+        const float xt = col[t * 128];
         float v = s0 * w.x;
         v += s1 * w.y;
         v += s2 * w.z;
@@ -100,18 +135,42 @@ __global__ void __launch_bounds__(128) linear_prefill_conv_kernel(ConvParams p) 
         s0 = s1;
         s1 = s2;
         s2 = xt;
-        x[size_t(t) * p.qkv_dim] = siluf_ref(v);
+        // SiLU with the hardware exp2 and a fast divide (a few ulp from
+        // x / (1 + exp(-x)); the prefill path's tolerance is 1e-3).
+        col[t * 128] = __fdividef(v, 1.0f + __expf(-v));
     }
-    if (g == p.nseg - 1) {
+    if (live && g == p.nseg - 1) {
         float *st = p.conv_state + (size_t(p.seq0 + s) * p.qkv_dim + c) * 3;
         st[0] = s0;
         st[1] = s1;
         st[2] = s2;
     }
+    if (cb * 128 < p.qk_channels) {
+        __syncthreads();
+        for (int t = warp; t < n; t += 4) {
+            float4 *v4 = reinterpret_cast<float4 *>(tile + t * 128) + lane;
+            float4 v = *v4;
+            double sum = double(v.x) * v.x + double(v.y) * v.y + double(v.z) * v.z + double(v.w) * v.w;
+            sum = warp_sum_f64(sum);
+            const float scale = 1.0f / fmaxf(sqrtf(float(sum)), p.eps);
+            v.x *= scale;
+            v.y *= scale;
+            v.z *= scale;
+            v.w *= scale;
+            *v4 = v;
+        }
+    }
+    fence_proxy_async_smem();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        tma_store_3d(&map_x, cb * 128, t0, s, tile);
+        bulk_commit_group();
+        bulk_wait_group_read0();
+    }
 }
 
 // ----------------------------------------------------------------------------
-// L2: q/k L2-norm and gates
+// L2: gates
 // ----------------------------------------------------------------------------
 struct NormParams {
     float *qkv;
@@ -123,22 +182,7 @@ struct NormParams {
 
 __global__ void __launch_bounds__(256) linear_prefill_norm_kernel(NormParams p) {
     const int t = blockIdx.x, s = blockIdx.y;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const size_t tok = size_t(s) * p.count + t;
-    float *row = p.qkv + tok * p.qkv_dim;
-    // 2*qk_heads heads of 128 channels (q heads then k heads), one warp each.
-    for (int hh = warp; hh < 2 * p.qk_heads; hh += 8) {
-        float4 *v4 = reinterpret_cast<float4 *>(row + hh * kD) + lane;
-        float4 v = *v4;
-        double sum = double(v.x) * v.x + double(v.y) * v.y + double(v.z) * v.z + double(v.w) * v.w;
-        sum = warp_sum_f64(sum);
-        const float scale = 1.0f / fmaxf(sqrtf(float(sum)), p.eps);
-        v.x *= scale;
-        v.y *= scale;
-        v.z *= scale;
-        v.w *= scale;
-        *v4 = v;
-    }
     for (int h = threadIdx.x; h < p.v_heads; h += blockDim.x) {
         float *bp = p.beta + tok * p.v_heads + h;
         float *ap = p.alpha + tok * p.v_heads + h;
@@ -1030,6 +1074,21 @@ bool make_map_bf16_ls(CUtensorMap *m, const void *base, uint64_t cols, uint64_t 
                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// 3-D map of f32 over [planes][rows][cols] with a box of 128 x kSeg x 1, no
+// swizzle: a conv segment's channel block.
+bool make_map_f32_rows(CUtensorMap *m, const void *base, uint64_t cols, uint64_t rows,
+                       uint64_t planes) {
+    auto enc = encode_tiled_ls();
+    if (!enc) return false;
+    cuuint64_t dims[3] = {cols, rows, planes};
+    cuuint64_t strides[2] = {cols * 4, cols * 4 * rows};
+    cuuint32_t box[3] = {128, uint32_t(kSeg), 1};
+    cuuint32_t es[3] = {1, 1, 1};
+    return enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<void *>(base), dims, strides, box,
+               es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 // ----------------------------------------------------------------------------
 // L5: per-head RMSNorm + SiLU(z)
 // ----------------------------------------------------------------------------
@@ -1076,12 +1135,20 @@ cudaError_t launch_linear_prefill(const LinearPrefillLaunch &a, cudaStream_t str
     // The segment boundaries live at the start of the W scratch, which L3
     // only writes after the conv has finished.
     const int nseg = (a.count + kSeg - 1) / kSeg;
-    ConvParams cp{a.qkv, a.conv_state, a.conv_w, a.scratch, a.seq0, a.count, qkv_dim, nseg};
+    ConvParams cp{a.qkv, a.conv_state, a.conv_w, a.scratch, a.seq0, a.count, qkv_dim, nseg,
+                  2 * a.qk_heads * kD, a.eps, a.err};
     const dim3 conv_grid((qkv_dim + 127) / 128, nseg, a.nseq);
     linear_prefill_conv_bounds_kernel<<<conv_grid, 128, 0, stream>>>(cp);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
-    linear_prefill_conv_kernel<<<conv_grid, 128, 0, stream>>>(cp);
+    CUtensorMap mx;
+    if (!make_map_f32_rows(&mx, a.qkv, uint64_t(qkv_dim), uint64_t(a.count), uint64_t(a.nseq)))
+        return cudaErrorInvalidValue;
+    if ((e = cudaFuncSetAttribute(linear_prefill_conv_kernel,
+                                  cudaFuncAttributeMaxDynamicSharedMemorySize, int(kConvTileBytes))) !=
+        cudaSuccess)
+        return e;
+    linear_prefill_conv_kernel<<<conv_grid, 128, kConvTileBytes, stream>>>(mx, cp);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
 
     NormParams np{a.qkv, a.beta, a.alpha, a.dt_bias, a.ssm_a, a.count, a.qk_heads, a.v_heads,

@@ -206,6 +206,15 @@ __device__ __forceinline__ void tma_store_4d(const CUtensorMap *map, int c0, int
         "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_addr(src_smem))
         : "memory");
 }
+// 3-D tiled TMA store from this CTA's shared memory, tracked by bulk group.
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap *map, int c0, int c1, int c2,
+                                            const void *src_smem) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.global.shared::cta.tile.bulk_group [%0, {%1, %2, %3}], [%4];" ::"l"(
+            reinterpret_cast<uint64_t>(map)),
+        "r"(c0), "r"(c1), "r"(c2), "r"(smem_addr(src_smem))
+        : "memory");
+}
 __device__ __forceinline__ void bulk_commit_group() {
     asm volatile("cp.async.bulk.commit_group;" ::: "memory");
 }
