@@ -685,9 +685,9 @@ def run_ours(args) -> None:
             line["deltanet_prefill"] = {
                 "workload": (f"config5: {args.prefill_batch} x {args.prefill_len}-token chunked "
                              "Gated DeltaNet prefill per GPU (C=64, 16K/48V x 128) from a zero "
-                             "state, outputs + final f32 state; chunk-local WY terms on f32 CUDA "
-                             "cores, state pass on tcgen05 with bf16 hi/lo operand pairs "
-                             "(3 products, ~1e-5 of the per-token recurrence)"),
+                             "state, outputs + final f32 state; chunk-local WY products and "
+                             "state pass on tcgen05 with bf16 hi/lo operand pairs (3 products, "
+                             "~1e-5 of the per-token recurrence), TMA-tiled conv"),
                 "ms": lin_prefill_ms, "tok_s": toks / (lin_prefill_ms * 1e-3),
                 "flops": flops, "tflops": flops / (lin_prefill_ms * 1e-3) / 1e12,
                 "roofline": {
