@@ -21,6 +21,9 @@
 // HBM layout of one KV slot: [batch][kv_heads][context_length][256] in f32 or
 // bf16, so a split's range of one kv head is one contiguous byte range.
 #include "q38_common.cuh"
+#include "q38_sm100.cuh"
+
+#include <cudaTypedefs.h>
 
 #include <algorithm>
 #include <cstdlib>
@@ -31,7 +34,6 @@ namespace {
 constexpr int kThreads = 256;      // 8 warps
 constexpr int kWarps = kThreads / 32;
 constexpr int kTileBytes = 32768;  // one staged KV tile
-constexpr int kStages = 3;
 constexpr int kMaxChunk = 4096;    // positions per split (scores smem: chunk*32 B)
 constexpr int kFastChunk = 512;    // largest chunk that keeps 2 CTAs per SM (112 KB smem)
 constexpr int kMinSplitsCap = 128;
@@ -40,7 +42,20 @@ template <typename KV>
 struct Tile {
     static constexpr int kPositions = kTileBytes / (kAttnHeadDim * int(sizeof(KV)));  // 64 | 32
     static constexpr int kPerWarp = kPositions / kWarps;                             // 8 | 4
+    // Ring depth: the bf16 kernel also holds its tensor-core query operand, so
+    // two stages keep it at two CTAs per SM.
+    static constexpr int kStages = sizeof(KV) == 2 ? 2 : 3;
 };
+
+// bf16 scores on tcgen05: per 64-key tile S^T = K Q^T as an M=64, N=16, K=256
+// MMA (6 query heads in B rows 0-5), with the f32 queries split into bf16
+// (hi, lo) pairs (two products into separate TMEM columns). Shared memory:
+// the query operand after the scores, 4 SW128 boxes of 8 rows (rows 6-7 zero;
+// the MMA also reads rows 8-15, the next kilobyte, whose columns are unused)
+// for hi and for lo, then 1 KB of padding.
+constexpr uint32_t kQOperandBytes = 4 * 1024;
+constexpr uint32_t kQRegionBytes = 2 * kQOperandBytes + 1024;
+constexpr uint32_t kDecodeTmemCols = 256;  // 32 columns (hi | lo) per tile, 8 tiles in turn
 
 __host__ __device__ inline int tile_positions(int kv_dtype) {
     return kv_dtype == Q38_KV_BF16 ? 64 : 32;
@@ -287,13 +302,21 @@ __device__ __forceinline__ void accumulate_rows(const unsigned char *tile, int r
 }
 
 template <typename KV>
-__global__ void __launch_bounds__(kThreads, 2) attn_decode_split_kernel(SplitParams p) {
+__global__ void __launch_bounds__(kThreads, 2)
+    attn_decode_split_kernel(const __grid_constant__ CUtensorMap map_k, SplitParams p) {
     using T = Tile<KV>;
+    constexpr int kStages = T::kStages;
+    constexpr bool kTc = sizeof(KV) == 2;  // scores on the tensor cores
     constexpr int kRowBytes = kAttnHeadDim * int(sizeof(KV));
-    extern __shared__ __align__(128) unsigned char smem[];
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    unsigned char *smem =
+        reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     unsigned char *stage = smem;                                             // kStages * 32 KB
     float *scores = reinterpret_cast<float *>(smem + kStages * kTileBytes);  // [chunk][8]
+    unsigned char *qsm = smem + kStages * kTileBytes + size_t(p.chunk) * 8 * sizeof(float);
     __shared__ uint64_t bars[kStages];
+    __shared__ uint64_t mma_done[kStages], read_done[kStages];
+    __shared__ uint32_t tmem_base_s;
     __shared__ float ml_s[kGroup][2];
     __shared__ volatile int abort_flag;
 
@@ -321,6 +344,16 @@ __global__ void __launch_bounds__(kThreads, 2) attn_decode_split_kernel(SplitPar
     };
     auto issue = [&](int j) {
         const int t = j < ntiles ? j : j - ntiles;
+        if (kTc && j < ntiles) {
+            // K tile as the MMA's SW128 K-major A operand: 4 boxes of 64 dims;
+            // rows past the cache's end read as zeros.
+            mbar_arrive_expect_tx(&bars[j % kStages], kTileBytes);
+            for (int bx = 0; bx < 4; ++bx)
+                sm100::tma_load_3d(stage + (j % kStages) * kTileBytes + bx * (kTileBytes / 4), &map_k,
+                                   bx * 64, start + t * T::kPositions, b * p.kv_heads + kvh,
+                                   &bars[j % kStages]);
+            return;
+        }
         const unsigned char *src = (j < ntiles ? kbase : vbase) + size_t(t) * kTileBytes;
         const uint32_t bytes = uint32_t(tile_rows(j)) * kRowBytes;
         mbar_arrive_expect_tx(&bars[j % kStages], bytes);
@@ -341,10 +374,20 @@ __global__ void __launch_bounds__(kThreads, 2) attn_decode_split_kernel(SplitPar
 
     if (threadIdx.x == 0) {
         abort_flag = 0;
-        for (int s = 0; s < kStages; ++s) mbar_init(&bars[s], 1);
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(&bars[s], 1);
+            mbar_init(&mma_done[s], 2);  // one commit per issuing warp
+            mbar_init(&read_done[s], 4);  // the four reader warps
+        }
         fence_barrier_init();
     }
+    if (kTc && warp == 0) {
+        sm100::tmem_alloc(&tmem_base_s, kDecodeTmemCols);
+        sm100::tmem_relinquish();
+    }
+    sm100::fence_before_sync();
     __syncthreads();
+    sm100::fence_after_sync();
     // K1 wrote this sequence's new KV row and its prepared queries.
     pdl_wait_primary();
     if (threadIdx.x == 0) {
@@ -355,7 +398,113 @@ __global__ void __launch_bounds__(kThreads, 2) attn_decode_split_kernel(SplitPar
     int next = 0;  // first tile not yet waited for
 
     // Pass 1: scores of the split's positions for the 6 heads of the group.
-    {
+    if constexpr (kTc) {
+        using namespace sm100;
+        const uint32_t tmem = tmem_base_s;
+        // Queries as bf16 (hi, lo) pairs, B operand rows 0-5; thread = (row
+        // tid / 32, 8 dims); rows 6-7 and the padding are zero.
+        {
+            const int h = threadIdx.x >> 5, c8 = threadIdx.x & 31;
+            uint4 hq = make_uint4(0u, 0u, 0u, 0u), lq = hq;
+            if (h < kGroup) {
+                const float4 *q4 = reinterpret_cast<const float4 *>(
+                    p.qprep + ((size_t(b) * p.heads + size_t(kvh) * kGroup + h) * kAttnHeadDim + 8 * c8));
+                const float4 a = q4[0], c = q4[1];
+                const float v[8] = {a.x, a.y, a.z, a.w, c.x, c.y, c.z, c.w};
+                uint32_t hw[4], lw[4];
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    hw[i] = pack_bf16x2_rn(v[2 * i], v[2 * i + 1]);
+                    const float2 hf = bf16x2_to_float2(hw[i]);
+                    lw[i] = pack_bf16x2_rn(v[2 * i] - hf.x, v[2 * i + 1] - hf.y);
+                }
+                hq = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+                lq = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+            }
+            const uint32_t off = (c8 >> 3) * 1024 + h * 128 + (((c8 & 7) ^ h) << 4);
+            *reinterpret_cast<uint4 *>(qsm + off) = hq;
+            *reinterpret_cast<uint4 *>(qsm + kQOperandBytes + off) = lq;
+            if (threadIdx.x < 64)
+                reinterpret_cast<uint4 *>(qsm + 2 * kQOperandBytes)[threadIdx.x] = make_uint4(0u, 0u, 0u, 0u);
+        }
+        fence_proxy_async_smem();
+        __syncthreads();
+        if (warp == 5 || warp == 6) {
+            // MMA issuers (a thread issuing tcgen05.mma waits ~100 cycles per
+            // instruction, so the hi and lo products come from two warps):
+            // S^T of tile j into TMEM columns 32 (j % 8) (hi, warp 5) and
+            // 32 (j % 8) + 16 (lo, warp 6). Tile j's load follows the readout
+            // of tile j - kStages by every reader, so columns are never
+            // overwritten unread.
+            if (lane == 0) {
+                const uint32_t idesc = idesc_bf16_f32(64, 16, 0, 0);
+                const int part = warp - 5;  // 0: hi, 1: lo
+                const uint32_t qx = smem_addr(qsm) + part * kQOperandBytes;
+                for (int j = 0; j < ntiles; ++j) {
+                    if (!mbar_wait(&bars[j % kStages], uint32_t(j / kStages) & 1u)) {
+                        abort_flag = 1;
+                        set_error(p.err, kDevErrTimeout);
+                        break;
+                    }
+                    fence_after_sync();
+                    const uint32_t ks = smem_addr(stage + (j % kStages) * kTileBytes);
+#pragma unroll
+                    for (int kk = 0; kk < kAttnHeadDim / 16; ++kk) {
+                        const uint64_t ad =
+                            smem_desc_sw128(ks + (kk >> 2) * (kTileBytes / 4) + (kk & 3) * 32, 16, 1024);
+                        const uint32_t boff = (kk >> 2) * 1024 + (kk & 3) * 32;
+                        mma_bf16(tmem + 32 * (j & 7) + 16 * part, ad, smem_desc_sw128(qx + boff, 16, 1024),
+                                 idesc, kk > 0 ? 1u : 0u);
+                    }
+                    mma_commit(&mma_done[j % kStages]);
+                    if (abort_flag) break;
+                }
+            }
+        } else if (warp < 4) {
+            // Readers: an M=64 result has row m in TMEM lane 32 (m / 16) + m % 16,
+            // so lanes 0-15 of warp w hold keys 16 w .. 16 w + 15 of the tile.
+            const uint32_t lane_addr = uint32_t(32 * warp) << 16;
+            for (int j = 0; j < ntiles; ++j) {
+                if (!__all_sync(0xffffffffu, mbar_wait(&mma_done[j % kStages], uint32_t(j / kStages) & 1u))) {
+                    if (lane == 0) {
+                        abort_flag = 1;
+                        set_error(p.err, kDevErrTimeout);
+                    }
+                    break;
+                }
+                fence_after_sync();
+                uint32_t hi[16], lo[16];
+                tmem_ld16(tmem + lane_addr + 32 * (j & 7), hi);
+                tmem_ld16(tmem + lane_addr + 32 * (j & 7) + 16, lo);
+                tmem_wait_ld();
+                const int key = 16 * warp + lane;
+                if (lane < 16 && key < tile_rows(j)) {
+                    float *dst = scores + (size_t(j) * T::kPositions + key) * 8;
+#pragma unroll
+                    for (int h = 0; h < kGroup; ++h)
+                        dst[h] = (__uint_as_float(hi[h]) + __uint_as_float(lo[h])) * score_scale;
+                }
+                // Once every reader is done with tile j (and its MMAs, which
+                // completed before, with the stage), refill the stage.
+                fence_before_sync();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&read_done[j % kStages]);
+                if (threadIdx.x == 0 && !abort_flag && j + kStages < total_tiles) {
+                    if (mbar_wait(&read_done[j % kStages], uint32_t(j / kStages) & 1u)) {
+                        issue(j + kStages);
+                    } else {
+                        abort_flag = 1;
+                        set_error(p.err, kDevErrTimeout);
+                    }
+                }
+                if (__any_sync(0xffffffffu, abort_flag != 0)) break;
+            }
+        }
+        fence_before_sync();
+        __syncthreads();
+        fence_after_sync();
+        next = ntiles;
+    } else {
         float2 q2[kGroup][4];
         const float *qg = p.qprep + (size_t(b) * p.heads + size_t(kvh) * kGroup) * kAttnHeadDim;
 #pragma unroll
@@ -434,6 +583,7 @@ __global__ void __launch_bounds__(kThreads, 2) attn_decode_split_kernel(SplitPar
             for (int j = max(0, next - 1); j < issued; ++j)
                 (void)mbar_wait(&bars[j % kStages], uint32_t(j / kStages) & 1u);
         }
+        if (kTc && warp == 0) sm100::tmem_dealloc(tmem_base_s, kDecodeTmemCols);
         return;
     }
 
@@ -460,6 +610,8 @@ __global__ void __launch_bounds__(kThreads, 2) attn_decode_split_kernel(SplitPar
             p.part_ml[slot * 2 + 1] = ml_s[h][1];
         }
     }
+    // Every TMEM read finished before pass 1's closing barrier.
+    if (kTc && warp == 0) sm100::tmem_dealloc(tmem_base_s, kDecodeTmemCols);
 }
 
 // ----------------------------------------------------------------------------
@@ -535,6 +687,28 @@ __global__ void __launch_bounds__(kAttnHeadDim) attn_merge_shards_kernel(ShardMe
     p.attention[(size_t(b) * p.heads + h) * kAttnHeadDim + d] = (o / l) * sigmoidf_ref(gate);
 }
 
+// 3-D map of the bf16 key cache [planes][rows][256] with a box of 64 dims x
+// 64 rows and 128-byte swizzle: one quarter of a K tile as the MMA operand.
+bool make_map_kcache(CUtensorMap *m, const void *base, uint64_t rows, uint64_t planes) {
+    static PFN_cuTensorMapEncodeTiled_v12000 enc = [] {
+        void *f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) !=
+                cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            f = nullptr;
+        return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+    }();
+    if (!enc) return false;
+    cuuint64_t dims[3] = {uint64_t(kAttnHeadDim), rows, planes};
+    cuuint64_t strides[2] = {uint64_t(kAttnHeadDim) * 2, uint64_t(kAttnHeadDim) * 2 * rows};
+    cuuint32_t box[3] = {64, 64, 1};
+    cuuint32_t es[3] = {1, 1, 1};
+    return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void *>(base), dims, strides, box,
+               es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 int env_chunk_override() {
     static const int v = [] {
         const char *s = std::getenv("Q38_DECODE_CHUNK");
@@ -568,10 +742,17 @@ cudaError_t launch_typed(const AttnDecodeLaunch &a, int sm_count, cudaStream_t s
                    a.part_ml,  a.err,     a.context_length, a.heads, a.kv_heads,
                    plan.chunk, a.max_splits, a.max_position, a.pos_offset,
                    a.partial_out != nullptr};
-    const size_t smem = size_t(kStages) * kTileBytes + size_t(plan.chunk) * 8 * sizeof(float);
+    constexpr bool kTc = sizeof(KV) == 2;
+    CUtensorMap map_k{};
+    if (kTc && !make_map_kcache(&map_k, a.kcache, uint64_t(a.context_length),
+                                uint64_t(a.batch) * a.kv_heads))
+        return cudaErrorInvalidValue;
+    const size_t extra = (kTc ? kQRegionBytes : 0) + 1024;  // query operand, alignment
+    const size_t smem =
+        size_t(Tile<KV>::kStages) * kTileBytes + size_t(plan.chunk) * 8 * sizeof(float) + extra;
     e = cudaFuncSetAttribute(attn_decode_split_kernel<KV>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             int(size_t(kStages) * kTileBytes + size_t(kMaxChunk) * 32));
+                             int(size_t(Tile<KV>::kStages) * kTileBytes + size_t(kMaxChunk) * 32 + extra));
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(plan.nsplit, a.kv_heads, a.batch);
@@ -580,7 +761,7 @@ cudaError_t launch_typed(const AttnDecodeLaunch &a, int sm_count, cudaStream_t s
     cfg.stream = stream;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    e = cudaLaunchKernelEx(&cfg, attn_decode_split_kernel<KV>, sp);
+    e = cudaLaunchKernelEx(&cfg, attn_decode_split_kernel<KV>, map_k, sp);
     if (e != cudaSuccess) return e;
 
     MergeParams mp{a.part_o,   a.part_ml,  a.q_and_gate, a.positions,  a.attention,
