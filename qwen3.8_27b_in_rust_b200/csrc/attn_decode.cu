@@ -35,6 +35,7 @@ constexpr int kThreads = 256;      // 8 warps
 constexpr int kWarps = kThreads / 32;
 constexpr int kTileBytes = 32768;  // one staged KV tile
 constexpr int kMaxChunk = 4096;    // positions per split (scores smem: chunk*32 B)
+constexpr int kMaxChunkTc = 2048;  // bf16 (tensor-core) splits also stage P: chunk*64 B
 constexpr int kFastChunk = 512;    // largest chunk that keeps 2 CTAs per SM (112 KB smem)
 constexpr int kMinSplitsCap = 128;
 
@@ -303,7 +304,8 @@ __device__ __forceinline__ void accumulate_rows(const unsigned char *tile, int r
 
 template <typename KV>
 __global__ void __launch_bounds__(kThreads, 2)
-    attn_decode_split_kernel(const __grid_constant__ CUtensorMap map_k, SplitParams p) {
+    attn_decode_split_kernel(const __grid_constant__ CUtensorMap map_k,
+                             const __grid_constant__ CUtensorMap map_v, SplitParams p) {
     using T = Tile<KV>;
     constexpr int kStages = T::kStages;
     constexpr bool kTc = sizeof(KV) == 2;  // scores on the tensor cores
@@ -314,8 +316,10 @@ __global__ void __launch_bounds__(kThreads, 2)
     unsigned char *stage = smem;                                             // kStages * 32 KB
     float *scores = reinterpret_cast<float *>(smem + kStages * kTileBytes);  // [chunk][8]
     unsigned char *qsm = smem + kStages * kTileBytes + size_t(p.chunk) * 8 * sizeof(float);
+    unsigned char *psm = qsm + kQRegionBytes;  // bf16: P (hi, lo) operand of the PV MMAs
     __shared__ uint64_t bars[kStages];
-    __shared__ uint64_t mma_done[kStages], read_done[kStages];
+    __shared__ uint64_t mma_done[kStages], read_done[kStages], pv_final;
+    __shared__ int issued_s;  // tiles issued so far (thread 0 issues them all)
     __shared__ uint32_t tmem_base_s;
     __shared__ float ml_s[kGroup][2];
     __shared__ volatile int abort_flag;
@@ -344,14 +348,15 @@ __global__ void __launch_bounds__(kThreads, 2)
     };
     auto issue = [&](int j) {
         const int t = j < ntiles ? j : j - ntiles;
-        if (kTc && j < ntiles) {
-            // K tile as the MMA's SW128 K-major A operand: 4 boxes of 64 dims;
-            // rows past the cache's end read as zeros.
+        issued_s = j + 1;
+        if (kTc) {
+            // K or V tile as an SW128 MMA operand (K-major A of the scores, MN-major
+            // A of P V): 4 boxes of 64 dims; rows past the cache's end read as zeros.
             mbar_arrive_expect_tx(&bars[j % kStages], kTileBytes);
             for (int bx = 0; bx < 4; ++bx)
-                sm100::tma_load_3d(stage + (j % kStages) * kTileBytes + bx * (kTileBytes / 4), &map_k,
-                                   bx * 64, start + t * T::kPositions, b * p.kv_heads + kvh,
-                                   &bars[j % kStages]);
+                sm100::tma_load_3d(stage + (j % kStages) * kTileBytes + bx * (kTileBytes / 4),
+                                   j < ntiles ? &map_k : &map_v, bx * 64, start + t * T::kPositions,
+                                   b * p.kv_heads + kvh, &bars[j % kStages]);
             return;
         }
         const unsigned char *src = (j < ntiles ? kbase : vbase) + size_t(t) * kTileBytes;
@@ -379,6 +384,8 @@ __global__ void __launch_bounds__(kThreads, 2)
             mbar_init(&mma_done[s], 2);  // one commit per issuing warp
             mbar_init(&read_done[s], 4);  // the four reader warps
         }
+        mbar_init(&pv_final, 2);  // the two P V chains
+        issued_s = 0;
         fence_barrier_init();
     }
     if (kTc && warp == 0) {
@@ -550,7 +557,121 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
     __syncthreads();
 
-    // Pass 2: acc[h] += exp(s-m)[h] * V.
+    if constexpr (kTc) {
+        // Pass 2 on tcgen05: O^T [256 dims][heads] += V^T P^T per tile, as two
+        // M=128 (dims), N=16, K=16 MMA chains (warp 5 dims 0-127, warp 6 dims
+        // 128-255), each with P as a bf16 (hi, lo) pair into separate TMEM
+        // columns (O^T reuses the score columns, all read by now).
+        using namespace sm100;
+        const uint32_t tmem = tmem_base_s;
+        // P^T operand: K-major rows = heads (6-7 zero; the MMA also reads rows
+        // 8-15, the next kilobyte), one SW128 box per 64 keys; keys past the
+        // split's end are zero. Thread = (head row, 8 keys).
+        const int nbox = p.chunk / 64;
+        const uint32_t p_half = uint32_t(nbox) * 1024;
+        for (int idx = threadIdx.x; idx < 8 * nbox * 8; idx += kThreads) {
+            const int h = idx & 7, c8 = idx >> 3;  // c8: 8-key group
+            uint32_t hw[4] = {0u, 0u, 0u, 0u}, lw[4] = {0u, 0u, 0u, 0u};
+            if (h < kGroup && !abort_flag) {
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const int q0 = 8 * c8 + 2 * i;
+                    const float e0 = q0 < cnt ? scores[q0 * 8 + h] : 0.f;
+                    const float e1 = q0 + 1 < cnt ? scores[(q0 + 1) * 8 + h] : 0.f;
+                    hw[i] = pack_bf16x2_rn(e0, e1);
+                    const float2 hf = bf16x2_to_float2(hw[i]);
+                    lw[i] = pack_bf16x2_rn(e0 - hf.x, e1 - hf.y);
+                }
+            }
+            const uint32_t off = (c8 >> 3) * 1024 + h * 128 + (((c8 & 7) ^ h) << 4);
+            *reinterpret_cast<uint4 *>(psm + off) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+            *reinterpret_cast<uint4 *>(psm + p_half + off) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+        }
+        if (threadIdx.x < 64)
+            reinterpret_cast<uint4 *>(psm + 2 * p_half)[threadIdx.x] = make_uint4(0u, 0u, 0u, 0u);
+        fence_proxy_async_smem();
+        fence_before_sync();
+        __syncthreads();
+        fence_after_sync();
+        if ((warp == 5 || warp == 6) && lane == 0 && !abort_flag) {
+            const int mt = warp - 5;
+            const uint32_t idesc = idesc_bf16_f32(128, 16, 1, 0);  // A (V^T) MN-major
+            const uint32_t pb = smem_addr(psm);
+            for (int j = ntiles; j < total_tiles; ++j) {
+                const int t = j - ntiles;
+                if (!mbar_wait(&bars[j % kStages], uint32_t(j / kStages) & 1u)) {
+                    abort_flag = 1;
+                    set_error(p.err, kDevErrTimeout);
+                    break;
+                }
+                fence_after_sync();
+                const uint32_t vs = smem_addr(stage + (j % kStages) * kTileBytes) + 2 * mt * (kTileBytes / 4);
+#pragma unroll
+                for (int kk = 0; kk < T::kPositions / 16; ++kk) {
+                    const uint64_t ad = smem_desc_sw128(vs + kk * 2048, kTileBytes / 4, 1024);
+                    const uint32_t boff = t * 1024 + kk * 32;
+                    const uint32_t acc = (t | kk) ? 1u : 0u;
+                    mma_bf16(tmem + 32 * mt, ad, smem_desc_sw128(pb + boff, 16, 1024), idesc, acc);
+                    mma_bf16(tmem + 32 * mt + 16, ad, smem_desc_sw128(pb + p_half + boff, 16, 1024),
+                             idesc, acc);
+                }
+                mma_commit(&mma_done[j % kStages]);
+                if (abort_flag) break;
+            }
+            mma_commit(&pv_final);  // every MMA of this chain, whatever happened
+        } else if (threadIdx.x == 0) {
+            // Refill each stage once both chains have read it.
+            for (int j = ntiles; j + kStages < total_tiles && !abort_flag; ++j) {
+                if (!mbar_wait(&mma_done[j % kStages], uint32_t(j / kStages) & 1u)) {
+                    abort_flag = 1;
+                    set_error(p.err, kDevErrTimeout);
+                    break;
+                }
+                issue(j + kStages);
+            }
+        }
+        // Epilogue: warps 0-3 read O^T (lane = dim) once the last tile's MMAs
+        // (and so all earlier ones) have completed.
+        if (warp < 4) {
+            const bool ok = !abort_flag && __all_sync(0xffffffffu, mbar_wait(&pv_final, 0));
+            if (ok) {
+                fence_after_sync();
+#pragma unroll 1
+                for (int mt = 0; mt < 2; ++mt) {
+                    uint32_t hi[16], lo[16];
+                    tmem_ld16(tmem + (uint32_t(32 * warp) << 16) + 32 * mt, hi);
+                    tmem_ld16(tmem + (uint32_t(32 * warp) << 16) + 32 * mt + 16, lo);
+                    tmem_wait_ld();
+                    const int d = 128 * mt + 32 * warp + lane;
+#pragma unroll
+                    for (int h = 0; h < kGroup; ++h) {
+                        const size_t slot = (size_t(b) * p.heads + size_t(kvh) * kGroup + h) * p.max_splits + split;
+                        p.part_o[slot * kAttnHeadDim + d] = __uint_as_float(hi[h]) + __uint_as_float(lo[h]);
+                        if (d == 0) {
+                            p.part_ml[slot * 2 + 0] = ml_s[h][0];
+                            p.part_ml[slot * 2 + 1] = ml_s[h][1];
+                        }
+                    }
+                }
+            } else if (lane == 0) {
+                abort_flag = 1;
+                set_error(p.err, kDevErrTimeout);
+            }
+        }
+        fence_before_sync();
+        __syncthreads();
+        if (abort_flag && threadIdx.x == 0) {
+            // Copies still in flight are among the last kStages issued (each
+            // refill waited for the tile kStages before it): let them land.
+            for (int j = max(0, issued_s - kStages); j < issued_s; ++j)
+                (void)mbar_wait(&bars[j % kStages], uint32_t(j / kStages) & 1u);
+        }
+        if (warp == 0) {
+            __syncwarp();
+            tmem_dealloc(tmem, kDecodeTmemCols);
+        }
+    } else {
+    // Pass 2 on the CUDA cores (f32 cache): acc[h] += exp(s-m)[h] * V.
     float2 acc[kGroup][4];
 #pragma unroll
     for (int h = 0; h < kGroup; ++h)
@@ -583,7 +704,6 @@ __global__ void __launch_bounds__(kThreads, 2)
             for (int j = max(0, next - 1); j < issued; ++j)
                 (void)mbar_wait(&bars[j % kStages], uint32_t(j / kStages) & 1u);
         }
-        if (kTc && warp == 0) sm100::tmem_dealloc(tmem_base_s, kDecodeTmemCols);
         return;
     }
 
@@ -610,8 +730,7 @@ __global__ void __launch_bounds__(kThreads, 2)
             p.part_ml[slot * 2 + 1] = ml_s[h][1];
         }
     }
-    // Every TMEM read finished before pass 1's closing barrier.
-    if (kTc && warp == 0) sm100::tmem_dealloc(tmem_base_s, kDecodeTmemCols);
+    }  // f32 pass 2
 }
 
 // ----------------------------------------------------------------------------
@@ -743,16 +862,20 @@ cudaError_t launch_typed(const AttnDecodeLaunch &a, int sm_count, cudaStream_t s
                    plan.chunk, a.max_splits, a.max_position, a.pos_offset,
                    a.partial_out != nullptr};
     constexpr bool kTc = sizeof(KV) == 2;
-    CUtensorMap map_k{};
-    if (kTc && !make_map_kcache(&map_k, a.kcache, uint64_t(a.context_length),
-                                uint64_t(a.batch) * a.kv_heads))
+    CUtensorMap map_k{}, map_v{};
+    if (kTc && (!make_map_kcache(&map_k, a.kcache, uint64_t(a.context_length),
+                                 uint64_t(a.batch) * a.kv_heads) ||
+                !make_map_kcache(&map_v, a.vcache, uint64_t(a.context_length),
+                                 uint64_t(a.batch) * a.kv_heads)))
         return cudaErrorInvalidValue;
-    const size_t extra = (kTc ? kQRegionBytes : 0) + 1024;  // query operand, alignment
-    const size_t smem =
-        size_t(Tile<KV>::kStages) * kTileBytes + size_t(plan.chunk) * 8 * sizeof(float) + extra;
+    // bf16: query operand, P operand (2 x 1 KB per 64 keys + 1 KB); all: alignment.
+    auto extra_for = [&](int chunk) {
+        return (kTc ? kQRegionBytes + size_t(chunk / 64) * 2048 + 1024 : 0) + 1024;
+    };
+    const size_t smem = size_t(Tile<KV>::kStages) * kTileBytes + size_t(plan.chunk) * 8 * sizeof(float) +
+                        extra_for(plan.chunk);
     e = cudaFuncSetAttribute(attn_decode_split_kernel<KV>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             int(size_t(Tile<KV>::kStages) * kTileBytes + size_t(kMaxChunk) * 32 + extra));
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(plan.nsplit, a.kv_heads, a.batch);
@@ -761,7 +884,7 @@ cudaError_t launch_typed(const AttnDecodeLaunch &a, int sm_count, cudaStream_t s
     cfg.stream = stream;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    e = cudaLaunchKernelEx(&cfg, attn_decode_split_kernel<KV>, map_k, sp);
+    e = cudaLaunchKernelEx(&cfg, attn_decode_split_kernel<KV>, map_k, map_v, sp);
     if (e != cudaSuccess) return e;
 
     MergeParams mp{a.part_o,   a.part_ml,  a.q_and_gate, a.positions,  a.attention,
@@ -777,14 +900,16 @@ cudaError_t launch_typed(const AttnDecodeLaunch &a, int sm_count, cudaStream_t s
 
 int attn_decode_max_splits(int context_length, int kv_dtype) {
     const int tile = tile_positions(kv_dtype);
+    const int max_chunk = kv_dtype == Q38_KV_BF16 ? kMaxChunkTc : kMaxChunk;
     const int by_tile = (context_length + tile - 1) / tile;
-    const int by_chunk = (context_length + kMaxChunk - 1) / kMaxChunk;
+    const int by_chunk = (context_length + max_chunk - 1) / max_chunk;
     return std::min(by_tile, std::max(kMinSplitsCap, by_chunk));
 }
 
 DecodeSplitPlan plan_attn_decode(int batch, int kv_heads, int max_position, int kv_dtype,
                                  int sm_count) {
     const int tile = tile_positions(kv_dtype);
+    const int max_chunk = kv_dtype == Q38_KV_BF16 ? kMaxChunkTc : kMaxChunk;
     const int n = max_position + 1;
     const int units = std::max(1, batch * kv_heads);
     // Aim for at least two CTAs per SM over the whole grid.
@@ -794,9 +919,9 @@ DecodeSplitPlan plan_attn_decode(int batch, int kv_heads, int max_position, int 
     chunk = std::max(chunk, (n + kMinSplitsCap - 1) / kMinSplitsCap);
     if (int o = env_chunk_override(); o > 0) chunk = o;
     chunk = ((chunk + tile - 1) / tile) * tile;
-    chunk = std::min(std::max(chunk, tile), env_chunk_override() > 0 ? kMaxChunk : kFastChunk);
+    chunk = std::min(std::max(chunk, tile), env_chunk_override() > 0 ? max_chunk : kFastChunk);
     // Never more splits than attn_decode_max_splits allows for this n.
-    const int cap = std::max(kMinSplitsCap, (n + kMaxChunk - 1) / kMaxChunk);
+    const int cap = std::max(kMinSplitsCap, (n + max_chunk - 1) / max_chunk);
     if ((n + chunk - 1) / chunk > cap) chunk = ((n + cap - 1) / cap + tile - 1) / tile * tile;
     DecodeSplitPlan plan;
     plan.chunk = chunk;
