@@ -274,6 +274,39 @@ def test_split_count_does_not_change_the_result(cuda_ctx):
     assert relative_error(outs[0], outs[1][:1]) < 1e-6
 
 
+def test_full_decode_long_context_large_splits(cuda_ctx, oracle_lib):
+    """One sequence at position 69999 of a 70000-position bf16 cache: the split
+    plan then takes more than 512 positions per split (nine or more 64-key
+    tiles, so the tensor-core scores cycle through their TMEM columns), and
+    the last split ends inside a tile."""
+    import q38attn
+    from q38attn import synth
+    torch = _torch()
+    g = synth.rng(13)
+    w = synth.full_weights(g)
+    layer, ctx_len, pos = 3, 70000, 69999
+    cuda_ctx.bind_full_layer(layer, w["q_norm"], w["k_norm"])
+    st = cuda_ctx.state(1, ctx_len, full_slots=1, linear_slots=0, kv_dtype=q38attn.Q38_KV_BF16)
+    k, v = synth.kv_rows(g, pos, bf16=True)
+    st.upload_kv(layer, 0, 0, k, v)
+    kc = np.zeros((ctx_len, 1024), F)
+    vc = np.zeros((ctx_len, 1024), F)
+    kc[:pos], vc[:pos] = k, v
+    del k, v
+    x = synth.full_step(g, 1)
+    d = {kk: torch.from_numpy(vv.copy()).cuda() for kk, vv in x.items()}
+    att = torch.zeros(1, 6144, device="cuda")
+    cuda_ctx.full_decode(st, layer, d["q_and_gate"], d["key"], d["value"],
+                         torch.tensor([pos], dtype=torch.int32, device="cuda"), att)
+    torch.cuda.synchronize()
+    ox = {kk: vv[0].copy() for kk, vv in x.items()}
+    oatt, okey, _ = _oracle_full(oracle_lib, w, ox, kc, vc, ctx_len, pos, layer, True)
+    assert relative_error(att[0].cpu().numpy(), oatt) < TOL
+    assert relative_error(d["key"][0].cpu().numpy(), okey) < 1e-5
+    assert st.errors() == 0
+    st.close()
+
+
 def test_full_core_position_errors(cuda_ctx):
     """Err(-1) paths of full_core (ops.rs:860-864) and device-side position checks."""
     import q38attn
