@@ -361,6 +361,97 @@ int q38_full_core(q38_ctx *ctx, q38_state *st, int layer, const float *q_and_gat
                   float *key_cache, float *value_cache, size_t cache_rows,
                   size_t context_length, uint32_t current_position);
 
+/* ------------------------------------------- projections around the cores */
+
+/* ggml tensor types the projections accept (src/gguf/mod.rs:83-103). The
+ * K-quants take the integer path of the reference's `project`
+ * (matrix_type_q8_k, src/model/ops.rs:105-120): the f32 activation is
+ * quantized to Q8_K blocks and dotted in integers; the others take the f32
+ * activation directly. The IQ types the reference also reads are not
+ * accepted here (Q38_ERR_ARG). */
+#define Q38_GGML_F32 0
+#define Q38_GGML_F16 1
+#define Q38_GGML_Q8_0 8
+#define Q38_GGML_Q2_K 10
+#define Q38_GGML_Q3_K 11
+#define Q38_GGML_Q4_K 12
+#define Q38_GGML_Q5_K 13
+#define Q38_GGML_Q6_K 14
+#define Q38_GGML_BF16 30
+
+/* Bytes of one Q8_K activation block in the reference's layout
+ * (Q38Q8KBlock, src/kernel/mod.rs:20-27): f32 scale, int8 quants[256],
+ * int16 sums[16]. */
+#define Q38_Q8K_BLOCK_BYTES 292
+
+typedef struct q38_weight q38_weight;
+
+/* Copies a projection matrix to the device: `rows` rows of `width` inputs
+ * each, the GGUF tensor of shape [width, rows] (TensorEntry, whose rows are
+ * row_bytes(type, width) bytes, src/kernel/tensor.rs:46-53). data is a HOST
+ * pointer to exactly rows * row_bytes bytes (nbytes). */
+int q38_weight_create(q38_ctx *ctx, int ggml_type, int64_t width, int64_t rows, const void *data,
+                      size_t nbytes, q38_weight **out);
+int q38_weight_destroy(q38_weight *w);
+int q38_weight_info(const q38_weight *w, int *ggml_type, int64_t *width, int64_t *rows);
+
+/* The same from a GGUF checkpoint: tensor `name` must be 2-D (as
+ * tensor_gemv_* require, tensor.rs:1095-1110) of an accepted type. */
+int q38_weight_from_gguf(q38_ctx *ctx, const char *path, const char *name, q38_weight **out);
+
+/* quantize_q8_k (src/kernel/quant.rs:98-124) of `batch` rows of `width`
+ * DEVICE floats (width a multiple of 256, input 16-byte aligned) into
+ * batch * width / 256 DEVICE blocks of Q38_Q8K_BLOCK_BYTES in the reference's
+ * layout. Bit-identical to the reference. */
+int q38_quantize_q8_k(q38_ctx *ctx, int batch, int64_t width, const float *input, void *blocks,
+                      void *stream);
+
+/* project / batch_project (src/model/ops.rs:623-640, 1016-1031): output
+ * [batch][rows] = W input[batch][width], DEVICE pointers, token-major as
+ * gemm_rows writes it (tensor.rs:978-1000). K-quant weights: the input is
+ * quantized to Q8_K on the device and each output is bit-identical to the
+ * reference's scalar integer dot. F32/F16/BF16/Q8_0: f32 dot, equal to the
+ * reference's within rounding. Uses the context's projection scratch
+ * (q38_ctx_reserve_projection sizes it ahead; otherwise it grows here). */
+int q38_project(q38_ctx *ctx, const q38_weight *w, int batch, const float *input, float *output,
+                void *stream);
+/* Host-pointer form (synchronous). */
+int q38_project_host(q38_ctx *ctx, const q38_weight *w, int batch, const float *input,
+                     float *output);
+/* Sizes the projection scratch for `batch` tokens of up to `width` inputs, so
+ * that later q38_project / *_attention_decode calls allocate nothing. */
+int q38_ctx_reserve_projection(q38_ctx *ctx, int batch, int64_t width);
+
+/* The projections of one Gated DeltaNet layer (Q38Attention::Linear,
+ * src/model/mod.rs:28-48): attn_qkv [hidden -> qkv_dim], attn_gate [hidden ->
+ * v_dim], ssm_beta / ssm_alpha [hidden -> v_heads], ssm_out [v_dim -> hidden]. */
+typedef struct q38_linear_projections {
+    const q38_weight *qkv, *z, *beta, *alpha, *out;
+} q38_linear_projections;
+
+/* The projections of one full-attention layer (Q38Attention::Full):
+ * attn_q [hidden -> 2*q_dim, query and gate per head], attn_k / attn_v
+ * [hidden -> kv_dim], attn_output [q_dim -> hidden]. */
+typedef struct q38_full_projections {
+    const q38_weight *q, *k, *v, *out;
+} q38_full_projections;
+
+/* linear_attention (src/model/ops.rs:744-803) for `batch` sequences: norm
+ * [batch][hidden] DEVICE (the attn_norm output), branch [batch][hidden]
+ * DEVICE out. Quantizes norm once, runs the four input projections, the
+ * DeltaNet step on the resident state (as q38_linear_decode), quantizes the
+ * core's output and runs ssm_out. */
+int q38_linear_attention_decode(q38_ctx *ctx, q38_state *st, int layer, int batch,
+                                const q38_linear_projections *w, const float *norm, float *branch,
+                                void *stream);
+
+/* full_attention (src/model/ops.rs:941-981) for `batch` sequences at DEVICE
+ * positions[batch] (max_position as for q38_full_decode). */
+int q38_full_attention_decode(q38_ctx *ctx, q38_state *st, int layer, int batch,
+                              const q38_full_projections *w, const float *norm,
+                              const int32_t *positions, int max_position, float *branch,
+                              void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -34,7 +34,8 @@ _lib = None
 
 
 def build(force: bool = False) -> Path:
-    src = [ORACLE_DIR / "q38_oracle.cpp", ORACLE_DIR / "q38_oracle.h", ORACLE_DIR / "Makefile"]
+    src = [ORACLE_DIR / "q38_oracle.cpp", ORACLE_DIR / "q38_oracle_proj.cpp",
+           ORACLE_DIR / "q38_oracle.h", ORACLE_DIR / "Makefile"]
     if force or not LIB_PATH.exists() or any(p.stat().st_mtime > LIB_PATH.stat().st_mtime
                                                for p in src):
         subprocess.run(["make", "-C", str(ORACLE_DIR), "-B" if force else "all"], check=True)
@@ -66,6 +67,21 @@ def load() -> ctypes.CDLL:
         lib.q38o_rms_scale.restype = c_float
         lib.q38o_l2norm.argtypes = [P, c_size_t]
         lib.q38o_rope.argtypes = [P, c_size_t, c_uint32]
+        lib.q38o_f16_to_f32.argtypes = [ctypes.c_uint16]
+        lib.q38o_f16_to_f32.restype = c_float
+        lib.q38o_is_q8k_type.argtypes = [c_int]
+        lib.q38o_is_q8k_type.restype = c_int
+        lib.q38o_row_bytes.argtypes = [c_int, c_size_t, P]
+        lib.q38o_row_bytes.restype = c_int
+        lib.q38o_quantize_q8_k.argtypes = [P, c_size_t, P]
+        lib.q38o_quantize_q8_k.restype = c_int
+        lib.q38o_dot_row_f32.argtypes = [c_int, P, P, c_size_t]
+        lib.q38o_dot_row_f32.restype = c_float
+        lib.q38o_dot_row_q8_k.argtypes = [c_int, P, P, c_size_t]
+        lib.q38o_dot_row_q8_k.restype = c_float
+        for name in ("q38o_gemm_f32", "q38o_gemm_q8_k", "q38o_project"):
+            getattr(lib, name).argtypes = [c_int, P, c_size_t, c_size_t, P, c_size_t, P]
+            getattr(lib, name).restype = c_int
         for name in ("q38o_sigmoid", "q38o_silu", "q38o_softplus", "q38o_round_bf16"):
             getattr(lib, name).argtypes = [c_float]
             getattr(lib, name).restype = c_float
@@ -160,3 +176,86 @@ def softplus(x: float) -> float:
 
 def round_bf16(x: float) -> float:
     return float(load().q38o_round_bf16(x))
+
+
+# ---------------------------------------------------------------------------
+# Projections (q38_oracle_proj.cpp): Q8_K quantizer, K-quant integer dots,
+# f32-input dots, project / batch_project.
+# ---------------------------------------------------------------------------
+GGML_F32, GGML_F16, GGML_Q8_0, GGML_BF16 = 0, 1, 8, 30
+GGML_Q2_K, GGML_Q3_K, GGML_Q4_K, GGML_Q5_K, GGML_Q6_K = 10, 11, 12, 13, 14
+
+# Q38Q8KBlock (src/kernel/mod.rs:20-27), 292 bytes.
+Q8K_BLOCK = np.dtype([("scale", "<f4"), ("quants", "i1", (256,)), ("sums", "<i2", (16,))])
+assert Q8K_BLOCK.itemsize == 292
+
+
+def f16_to_f32(h: int) -> float:
+    return float(load().q38o_f16_to_f32(h))
+
+
+def is_q8k_type(ggml_type: int) -> bool:
+    return bool(load().q38o_is_q8k_type(ggml_type))
+
+
+def row_bytes(ggml_type: int, width: int) -> int:
+    out = ctypes.c_size_t(0)
+    if load().q38o_row_bytes(ggml_type, width, ctypes.byref(out)) != 0:
+        raise ValueError(f"type {ggml_type} cannot hold rows of {width}")
+    return out.value
+
+
+def quantize_q8_k(x: np.ndarray) -> np.ndarray:
+    """quantize_q8_k (src/kernel/quant.rs:98-124) of a [..., width] array: one
+    Q8K_BLOCK per 256 values, token-major."""
+    x = np.ascontiguousarray(x, np.float32)
+    out = np.zeros(x.size // 256, Q8K_BLOCK)
+    if load().q38o_quantize_q8_k(_p(x), x.size, c_void_p(out.ctypes.data)) != 0:
+        raise ValueError("length is not a multiple of 256")
+    return out
+
+
+def _w(weights: np.ndarray) -> c_void_p:
+    assert weights.dtype == np.uint8 and weights.flags.c_contiguous
+    return c_void_p(weights.ctypes.data)
+
+
+def gemm_q8_k(ggml_type: int, weights: np.ndarray, rows: int, width: int,
+              blocks: np.ndarray, batch: int) -> np.ndarray:
+    out = np.zeros((batch, rows), np.float32)
+    rc = load().q38o_gemm_q8_k(ggml_type, _w(weights), rows, width,
+                               c_void_p(blocks.ctypes.data), batch, _p(out))
+    if rc != 0:
+        raise ValueError("gemm_q8_k: unsupported type or shape")
+    return out
+
+
+def gemm_f32(ggml_type: int, weights: np.ndarray, rows: int, width: int, x: np.ndarray,
+             batch: int) -> np.ndarray:
+    x = np.ascontiguousarray(x, np.float32)
+    out = np.zeros((batch, rows), np.float32)
+    if load().q38o_gemm_f32(ggml_type, _w(weights), rows, width, _p(x), batch, _p(out)) != 0:
+        raise ValueError("gemm_f32: unsupported type or shape")
+    return out
+
+
+def project(ggml_type: int, weights: np.ndarray, rows: int, width: int,
+            x: np.ndarray) -> np.ndarray:
+    """project / batch_project (src/model/ops.rs:623-640, 1016-1031): x is
+    [batch][width] f32; returns [batch][rows]."""
+    x = np.ascontiguousarray(x, np.float32).reshape(-1, width)
+    out = np.zeros((x.shape[0], rows), np.float32)
+    rc = load().q38o_project(ggml_type, _w(weights), rows, width, _p(x), x.shape[0], _p(out))
+    if rc != 0:
+        raise ValueError("project: unsupported type or shape")
+    return out
+
+
+def dot_row_f32(ggml_type: int, row: np.ndarray, x: np.ndarray) -> float:
+    x = np.ascontiguousarray(x, np.float32)
+    return float(load().q38o_dot_row_f32(ggml_type, _w(row), _p(x), x.size))
+
+
+def dot_row_q8_k(ggml_type: int, row: np.ndarray, blocks: np.ndarray) -> float:
+    return float(load().q38o_dot_row_q8_k(ggml_type, _w(row), c_void_p(blocks.ctypes.data),
+                                          blocks.size))

@@ -135,6 +135,45 @@ int q38o_full_prefill_rows(const float *q_norm, const float *k_norm, const float
                            size_t count, const int64_t *rows, size_t row_count,
                            int kv_round_bf16);
 
+/*
+ * Projections on either side of the cores (q38_oracle_proj.cpp): the Q8_K
+ * activation quantizer (src/kernel/quant.rs:56-124), the integer dots of the
+ * K-quant types against it (src/kernel/tensor.rs:301-460), the f32-input dots
+ * (tensor.rs:79-117), the row loops with token-major output
+ * (tensor.rs:954-1027) and project / batch_project (src/model/ops.rs:617-640,
+ * 1016-1031). Weights are raw GGUF tensor bytes, rows of row_bytes(type,
+ * width) each; outputs are [batch][rows].
+ */
+#define Q38O_GGML_F32 0
+#define Q38O_GGML_F16 1
+#define Q38O_GGML_Q8_0 8
+#define Q38O_GGML_Q2_K 10
+#define Q38O_GGML_Q3_K 11
+#define Q38O_GGML_Q4_K 12
+#define Q38O_GGML_Q5_K 13
+#define Q38O_GGML_Q6_K 14
+#define Q38O_GGML_BF16 30
+
+/* Q38Q8KBlock, src/kernel/mod.rs:20-27: 292 bytes. */
+typedef struct {
+    float scale;
+    int8_t quants[256];
+    int16_t sums[16];
+} q38o_q8k_block;
+
+float q38o_f16_to_f32(uint16_t h);
+int q38o_is_q8k_type(int type);
+int q38o_row_bytes(int type, size_t width, size_t *out);
+int q38o_quantize_q8_k(const float *input, size_t length, q38o_q8k_block *out);
+float q38o_dot_row_f32(int type, const uint8_t *row, const float *x, size_t width);
+float q38o_dot_row_q8_k(int type, const uint8_t *row, const q38o_q8k_block *q, size_t blocks);
+int q38o_gemm_f32(int type, const uint8_t *w, size_t rows, size_t width, const float *input,
+                  size_t batch, float *out);
+int q38o_gemm_q8_k(int type, const uint8_t *w, size_t rows, size_t width,
+                   const q38o_q8k_block *act, size_t batch, float *out);
+int q38o_project(int type, const uint8_t *w, size_t rows, size_t width, const float *input,
+                 size_t batch, float *out);
+
 /* Primitives exposed for unit tests (ops.rs:476-610). */
 float q38o_rms_scale(const float *values, size_t length);
 void q38o_l2norm(float *values, size_t length);

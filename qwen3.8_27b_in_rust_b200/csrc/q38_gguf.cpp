@@ -308,3 +308,24 @@ int bind_gguf(q38_ctx *ctx, const char *path, int first_layer, int last_layer) {
     return Q38_OK;
 }
 }  // namespace
+
+// A projection matrix straight from the checkpoint: the 2-D tensor `name`
+// (shape [width, rows], as tensor_gemv_* require, src/kernel/tensor.rs:
+// 1095-1110) handed to q38_weight_create.
+extern "C" int q38_weight_from_gguf(q38_ctx *ctx, const char *path, const char *name,
+                                    q38_weight **out) {
+    if (!ctx || !path || !name || !out) return gguf_fail("null argument");
+    *out = nullptr;
+    try {
+        GgufFile f;
+        const std::string err = f.open(path);
+        if (!err.empty()) return gguf_fail("invalid GGUF: %s", err.c_str());
+        const Tensor *t = f.find(name);
+        if (!t) return gguf_fail("tensor %s not found", name);
+        if (t->n_dims != 2) return gguf_fail("tensor %s is not 2-dimensional", name);
+        return q38_weight_create(ctx, int(t->type), int64_t(t->shape[0]), int64_t(t->shape[1]),
+                                 t->data, size_t(t->nbytes), out);
+    } catch (const std::exception &e) {
+        return gguf_fail("GGUF read failed: %s", e.what());
+    }
+}

@@ -51,6 +51,8 @@ struct q38_ctx {
     int qk_dim = 0, v_dim = 0, qkv_dim = 0;
     std::map<int, q38::FullWeights> full;
     std::map<int, q38::LinearWeights> linear;
+    void *proj_q8k = nullptr;       // Q8_K activations of the projections (q38proj.cu)
+    size_t proj_q8k_bytes = 0;
 };
 
 struct q38_state {
@@ -80,6 +82,8 @@ struct q38_state {
     // staging for the host-pointer calls (device, sized for `batch`)
     float *stage = nullptr;
     size_t stage_floats = 0;
+    // projection outputs / core inputs of the layer-level decode calls
+    float *proj_stage = nullptr;    // stage_floats
     int32_t *stage_pos = nullptr;
 };
 

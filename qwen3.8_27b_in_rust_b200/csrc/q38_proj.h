@@ -1,0 +1,46 @@
+// q38_proj.h -- projection weights and launchers (proj.cu). Internal, not
+// part of the public ABI.
+#pragma once
+
+#include "q38_internal.h"
+
+namespace q38 {
+
+constexpr int kProjMaxTok = 8;          // tokens per integer-path launch (more: repeated launches)
+constexpr int kProjMaxTileRows = 16;    // rows per weight tile at most
+constexpr uint32_t kProjSmemBudget = 224 * 1024;
+
+// Q8_K activations on the device, structure-of-arrays (token-major blocks):
+// quants [tokens][nblk][256], scale [tokens][nblk], sums [tokens][nblk][16].
+struct Q8KActivations {
+    int8_t *quants = nullptr;
+    float *scale = nullptr;
+    int16_t *sums = nullptr;
+};
+
+// A projection matrix as the GGUF stores it: `rows` rows of row_bytes bytes,
+// each row one output over `width` inputs (shape [width, rows]).
+struct ProjWeight {
+    int type = -1;
+    int64_t rows = 0, width = 0, row_bytes = 0;
+    void *data = nullptr;  // device, proj_padded_bytes long
+};
+
+bool proj_is_q8k_type(int type);
+bool proj_type_supported(int type);
+int64_t proj_row_bytes(int type, int64_t width);  // -1: type cannot hold such rows
+size_t proj_padded_bytes(int type, int64_t rows, int64_t width);
+
+cudaError_t launch_q8k_quantize(const float *x, int batch, int width, Q8KActivations act, void *aos,
+                                cudaStream_t stream);
+cudaError_t launch_proj_q8k(const ProjWeight &w, const Q8KActivations &act, int batch, float *out,
+                            long out_ld, int *err, int sm_count, cudaStream_t stream);
+cudaError_t launch_proj_f32(const ProjWeight &w, const float *x, int batch, float *out, long out_ld,
+                            cudaStream_t stream);
+
+}  // namespace q38
+
+struct q38_weight {
+    q38_ctx *ctx = nullptr;
+    q38::ProjWeight w;
+};

@@ -162,6 +162,7 @@ void free_state(q38_state *st) {
     cudaFree(st->part_ml);
     cudaFree(st->d_err);
     cudaFree(st->stage);
+    cudaFree(st->proj_stage);
     cudaFree(st->stage_pos);
     cudaFree(st->prefill_rope);
     cudaFree(st->prefill_v16);
@@ -315,6 +316,7 @@ int q38_ctx_destroy(q38_ctx *ctx) {
         DeviceGuard guard(ctx->device);
         for (auto &kv : ctx->full) free_full(kv.second);
         for (auto &kv : ctx->linear) free_linear(kv.second);
+        cudaFree(ctx->proj_q8k);
     }
     delete ctx;
     return Q38_OK;
@@ -409,6 +411,7 @@ int q38_state_create(q38_ctx *ctx, int batch, int context_length, int full_slots
     if (e == cudaSuccess) e = alloc((void **)&st->part_ml, parts * 2 * 4);
     if (e == cudaSuccess) e = alloc((void **)&st->d_err, sizeof(int));
     if (e == cudaSuccess) e = alloc((void **)&st->stage, st->stage_floats * 4);
+    if (e == cudaSuccess) e = alloc((void **)&st->proj_stage, st->stage_floats * 4);
     if (e == cudaSuccess) e = alloc((void **)&st->stage_pos, size_t(batch) * 4);
     if (e != cudaSuccess) {
         free_state(st);

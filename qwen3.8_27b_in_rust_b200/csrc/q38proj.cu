@@ -1,0 +1,297 @@
+// q38proj.cu -- C ABI of the projections on either side of the attention
+// cores: weight upload, Q8_K quantization, project / batch_project and the
+// layer-level decode calls linear_attention / full_attention
+// (src/model/ops.rs:617-640, 744-803, 941-981, 1016-1031).
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <new>
+
+#include "q38_proj.h"
+
+namespace {
+
+int proj_fail(int code, const char *fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    std::vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    q38::record_error(buf);
+    return code;
+}
+
+int proj_cuda_fail(cudaError_t e, const char *what) {
+    cudaGetLastError();
+    return proj_fail(Q38_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+struct Guard {
+    int prev = -1, dev;
+    explicit Guard(int d) : dev(d) {
+        if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+        if (prev != dev) cudaSetDevice(dev);
+    }
+    ~Guard() {
+        if (prev >= 0 && prev != dev) cudaSetDevice(prev);
+    }
+};
+
+size_t q8k_bytes(int batch, int64_t width) {
+    const size_t nb = size_t(batch) * size_t(width / 256);
+    return nb * 256 + nb * 4 + nb * 32;
+}
+
+q38::Q8KActivations q8k_view(void *base, int batch, int64_t width) {
+    const size_t nb = size_t(batch) * size_t(width / 256);
+    unsigned char *p = static_cast<unsigned char *>(base);
+    q38::Q8KActivations a;
+    a.quants = reinterpret_cast<int8_t *>(p);
+    a.scale = reinterpret_cast<float *>(p + nb * 256);
+    a.sums = reinterpret_cast<int16_t *>(p + nb * 256 + nb * 4);
+    return a;
+}
+
+int reserve(q38_ctx *ctx, int batch, int64_t width) {
+    const size_t need = q8k_bytes(batch, width);
+    if (need <= ctx->proj_q8k_bytes) return Q38_OK;
+    if (ctx->proj_q8k) {
+        // Earlier launches on any stream may still read the old buffer.
+        cudaError_t e = cudaDeviceSynchronize();
+        if (e != cudaSuccess) return proj_cuda_fail(e, "projection scratch resize");
+        cudaFree(ctx->proj_q8k);
+        ctx->proj_q8k = nullptr;
+        ctx->proj_q8k_bytes = 0;
+    }
+    cudaError_t e = cudaMalloc(&ctx->proj_q8k, need);
+    if (e != cudaSuccess) return proj_cuda_fail(e, "projection scratch allocation");
+    ctx->proj_q8k_bytes = need;
+    return Q38_OK;
+}
+
+int check_weight(const q38_ctx *ctx, const q38_weight *w, const char *what) {
+    if (!w) return proj_fail(Q38_ERR_ARG, "null %s weight", what);
+    if (w->ctx != ctx) return proj_fail(Q38_ERR_ARG, "%s weight belongs to another context", what);
+    return Q38_OK;
+}
+
+// Quantizes `input` (when any of the weights takes the integer path) into
+// the context scratch. The input is [batch][width], 16-byte aligned.
+int quantize_for(q38_ctx *ctx, int batch, int64_t width, const float *input, cudaStream_t s) {
+    if (width % 256) return proj_fail(Q38_ERR_ARG, "input length %lld is not a multiple of 256",
+                                      static_cast<long long>(width));
+    if (reinterpret_cast<uintptr_t>(input) % 16)
+        return proj_fail(Q38_ERR_ARG, "projection input must be 16-byte aligned");
+    if (int rc = reserve(ctx, batch, width)) return rc;
+    cudaError_t e = q38::launch_q8k_quantize(input, batch, int(width), q8k_view(ctx->proj_q8k, batch, width),
+                                             nullptr, s);
+    if (e != cudaSuccess) return proj_cuda_fail(e, "Q8_K quantize launch");
+    return Q38_OK;
+}
+
+// One projection whose Q8_K input (if needed) is already in the scratch.
+int project_quantized(q38_ctx *ctx, const q38_weight *w, int batch, const float *input, float *out,
+                      int *err, cudaStream_t s) {
+    cudaError_t e;
+    if (q38::proj_is_q8k_type(w->w.type))
+        e = q38::launch_proj_q8k(w->w, q8k_view(ctx->proj_q8k, batch, w->w.width), batch, out,
+                                 long(w->w.rows), err, ctx->sm_count, s);
+    else
+        e = q38::launch_proj_f32(w->w, input, batch, out, long(w->w.rows), s);
+    if (e != cudaSuccess) return proj_cuda_fail(e, "projection launch");
+    return Q38_OK;
+}
+
+int project_device(q38_ctx *ctx, const q38_weight *w, int batch, const float *input, float *out,
+                   int *err, cudaStream_t s) {
+    if (q38::proj_is_q8k_type(w->w.type))
+        if (int rc = quantize_for(ctx, batch, w->w.width, input, s)) return rc;
+    return project_quantized(ctx, w, batch, input, out, err, s);
+}
+
+}  // namespace
+
+extern "C" {
+
+int q38_weight_create(q38_ctx *ctx, int ggml_type, int64_t width, int64_t rows, const void *data,
+                      size_t nbytes, q38_weight **out) {
+    if (!out) return proj_fail(Q38_ERR_ARG, "null output pointer");
+    *out = nullptr;
+    if (!ctx || !data) return proj_fail(Q38_ERR_ARG, "null argument");
+    if (!q38::proj_type_supported(ggml_type))
+        return proj_fail(Q38_ERR_ARG, "unsupported projection type %d", ggml_type);
+    const int64_t rb = q38::proj_row_bytes(ggml_type, width);
+    if (rb < 0 || rows <= 0 || rows > (int64_t(1) << 30))
+        return proj_fail(Q38_ERR_ARG, "type %d cannot hold %lld x %lld", ggml_type,
+                         static_cast<long long>(rows), static_cast<long long>(width));
+    if (q38::proj_is_q8k_type(ggml_type) && width % 256)
+        return proj_fail(Q38_ERR_ARG, "K-quant rows must be whole 256-blocks");
+    if (nbytes != size_t(rows * rb))
+        return proj_fail(Q38_ERR_ARG, "weight holds %zu bytes, expected %lld", nbytes,
+                         static_cast<long long>(rows * rb));
+    Guard guard(ctx->device);
+    const size_t padded = q38::proj_padded_bytes(ggml_type, rows, width);
+    void *dev = nullptr;
+    cudaError_t e = cudaMalloc(&dev, padded);
+    if (e == cudaSuccess) e = cudaMemset(dev, 0, padded);
+    if (e == cudaSuccess) e = cudaMemcpy(dev, data, nbytes, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) {
+        cudaFree(dev);
+        return proj_cuda_fail(e, "weight upload");
+    }
+    q38_weight *w = new (std::nothrow) q38_weight();
+    if (!w) {
+        cudaFree(dev);
+        return proj_fail(Q38_ERR_ARG, "out of host memory");
+    }
+    w->ctx = ctx;
+    w->w.type = ggml_type;
+    w->w.rows = rows;
+    w->w.width = width;
+    w->w.row_bytes = rb;
+    w->w.data = dev;
+    *out = w;
+    return Q38_OK;
+}
+
+int q38_weight_destroy(q38_weight *w) {
+    if (!w) return Q38_OK;
+    {
+        Guard guard(w->ctx->device);
+        cudaFree(w->w.data);
+    }
+    delete w;
+    return Q38_OK;
+}
+
+int q38_weight_info(const q38_weight *w, int *ggml_type, int64_t *width, int64_t *rows) {
+    if (!w) return proj_fail(Q38_ERR_ARG, "null weight");
+    if (ggml_type) *ggml_type = w->w.type;
+    if (width) *width = w->w.width;
+    if (rows) *rows = w->w.rows;
+    return Q38_OK;
+}
+
+int q38_ctx_reserve_projection(q38_ctx *ctx, int batch, int64_t width) {
+    if (!ctx) return proj_fail(Q38_ERR_ARG, "null context");
+    if (batch <= 0 || width <= 0 || width % 256)
+        return proj_fail(Q38_ERR_ARG, "bad projection reservation (%d x %lld)", batch,
+                         static_cast<long long>(width));
+    Guard guard(ctx->device);
+    return reserve(ctx, batch, width);
+}
+
+int q38_quantize_q8_k(q38_ctx *ctx, int batch, int64_t width, const float *input, void *blocks,
+                      void *stream) {
+    if (!ctx || !input || !blocks) return proj_fail(Q38_ERR_ARG, "null argument");
+    if (batch <= 0 || width <= 0 || width % 256)
+        return proj_fail(Q38_ERR_ARG, "input length %lld is not a multiple of 256",
+                         static_cast<long long>(width));
+    if (reinterpret_cast<uintptr_t>(input) % 16 || reinterpret_cast<uintptr_t>(blocks) % 4)
+        return proj_fail(Q38_ERR_ARG, "input must be 16-byte and blocks 4-byte aligned");
+    Guard guard(ctx->device);
+    cudaError_t e = q38::launch_q8k_quantize(input, batch, int(width), q38::Q8KActivations{}, blocks,
+                                             static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return proj_cuda_fail(e, "Q8_K quantize launch");
+    return Q38_OK;
+}
+
+int q38_project(q38_ctx *ctx, const q38_weight *w, int batch, const float *input, float *output,
+                void *stream) {
+    if (!ctx) return proj_fail(Q38_ERR_ARG, "null context");
+    if (int rc = check_weight(ctx, w, "projection")) return rc;
+    if (batch <= 0 || !input || !output) return proj_fail(Q38_ERR_ARG, "bad batch or null tensor");
+    Guard guard(ctx->device);
+    return project_device(ctx, w, batch, input, output, nullptr, static_cast<cudaStream_t>(stream));
+}
+
+int q38_project_host(q38_ctx *ctx, const q38_weight *w, int batch, const float *input,
+                     float *output) {
+    if (!ctx) return proj_fail(Q38_ERR_ARG, "null context");
+    if (int rc = check_weight(ctx, w, "projection")) return rc;
+    if (batch <= 0 || !input || !output) return proj_fail(Q38_ERR_ARG, "bad batch or null tensor");
+    Guard guard(ctx->device);
+    const size_t in_bytes = size_t(batch) * w->w.width * 4, out_bytes = size_t(batch) * w->w.rows * 4;
+    float *din = nullptr, *dout = nullptr;
+    cudaError_t e = cudaMalloc(&din, in_bytes);
+    if (e == cudaSuccess) e = cudaMalloc(&dout, out_bytes);
+    if (e == cudaSuccess) e = cudaMemcpy(din, input, in_bytes, cudaMemcpyHostToDevice);
+    int rc = Q38_OK;
+    if (e == cudaSuccess) rc = project_device(ctx, w, batch, din, dout, nullptr, nullptr);
+    if (e == cudaSuccess && rc == Q38_OK) e = cudaMemcpy(output, dout, out_bytes, cudaMemcpyDeviceToHost);
+    cudaFree(din);
+    cudaFree(dout);
+    if (e != cudaSuccess) return proj_cuda_fail(e, "q38_project_host");
+    return rc;
+}
+
+int q38_linear_attention_decode(q38_ctx *ctx, q38_state *st, int layer, int batch,
+                                const q38_linear_projections *w, const float *norm, float *branch,
+                                void *stream) {
+    if (!ctx || !st || !w || !norm || !branch) return proj_fail(Q38_ERR_ARG, "null argument");
+    if (st->ctx != ctx) return proj_fail(Q38_ERR_ARG, "state belongs to another context");
+    if (batch <= 0 || batch > st->batch) return proj_fail(Q38_ERR_ARG, "batch %d outside 1..%d", batch, st->batch);
+    for (auto [p, name] : {std::pair<const q38_weight *, const char *>{w->qkv, "qkv"}, {w->z, "z"},
+                           {w->beta, "beta"}, {w->alpha, "alpha"}, {w->out, "out"}})
+        if (int rc = check_weight(ctx, p, name)) return rc;
+    const int64_t hidden = w->qkv->w.width;
+    const int vh = ctx->geom.linear_v_heads;
+    if (w->z->w.width != hidden || w->beta->w.width != hidden || w->alpha->w.width != hidden ||
+        w->out->w.rows != hidden || w->qkv->w.rows != ctx->qkv_dim || w->z->w.rows != ctx->v_dim ||
+        w->beta->w.rows != vh || w->alpha->w.rows != vh || w->out->w.width != ctx->v_dim)
+        return proj_fail(Q38_ERR_ARG, "DeltaNet projection shapes do not match the geometry");
+    Guard guard(ctx->device);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    float *qkv = st->proj_stage, *z = qkv + size_t(batch) * ctx->qkv_dim;
+    float *beta = z + size_t(batch) * ctx->v_dim, *alpha = beta + size_t(batch) * vh;
+    float *att = alpha + size_t(batch) * vh;
+    // linear_attention, ops.rs:761-801: one quantization of the normalised
+    // input shared by the four projections.
+    const q38_weight *ins[4] = {w->qkv, w->z, w->beta, w->alpha};
+    float *outs[4] = {qkv, z, beta, alpha};
+    bool any_q8k = false;
+    for (const q38_weight *p : ins) any_q8k |= q38::proj_is_q8k_type(p->w.type);
+    if (any_q8k)
+        if (int rc = quantize_for(ctx, batch, hidden, norm, s)) return rc;
+    for (int i = 0; i < 4; ++i)
+        if (int rc = project_quantized(ctx, ins[i], batch, norm, outs[i], st->d_err, s)) return rc;
+    if (int rc = q38_linear_decode(ctx, st, layer, batch, qkv, z, beta, alpha, att, stream)) return rc;
+    return project_device(ctx, w->out, batch, att, branch, st->d_err, s);
+}
+
+int q38_full_attention_decode(q38_ctx *ctx, q38_state *st, int layer, int batch,
+                              const q38_full_projections *w, const float *norm,
+                              const int32_t *positions, int max_position, float *branch,
+                              void *stream) {
+    if (!ctx || !st || !w || !norm || !branch || !positions)
+        return proj_fail(Q38_ERR_ARG, "null argument");
+    if (st->ctx != ctx) return proj_fail(Q38_ERR_ARG, "state belongs to another context");
+    if (batch <= 0 || batch > st->batch) return proj_fail(Q38_ERR_ARG, "batch %d outside 1..%d", batch, st->batch);
+    for (auto [p, name] : {std::pair<const q38_weight *, const char *>{w->q, "q"}, {w->k, "k"},
+                           {w->v, "v"}, {w->out, "out"}})
+        if (int rc = check_weight(ctx, p, name)) return rc;
+    const int64_t hidden = w->q->w.width;
+    if (w->k->w.width != hidden || w->v->w.width != hidden || w->out->w.rows != hidden ||
+        w->q->w.rows != ctx->qg_dim || w->k->w.rows != ctx->kv_dim || w->v->w.rows != ctx->kv_dim ||
+        w->out->w.width != ctx->q_dim)
+        return proj_fail(Q38_ERR_ARG, "full-attention projection shapes do not match the geometry");
+    Guard guard(ctx->device);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    float *qg = st->proj_stage, *key = qg + size_t(batch) * ctx->qg_dim;
+    float *value = key + size_t(batch) * ctx->kv_dim, *att = value + size_t(batch) * ctx->kv_dim;
+    // full_attention, ops.rs:954-980.
+    const q38_weight *ins[3] = {w->q, w->k, w->v};
+    float *outs[3] = {qg, key, value};
+    bool any_q8k = false;
+    for (const q38_weight *p : ins) any_q8k |= q38::proj_is_q8k_type(p->w.type);
+    if (any_q8k)
+        if (int rc = quantize_for(ctx, batch, hidden, norm, s)) return rc;
+    for (int i = 0; i < 3; ++i)
+        if (int rc = project_quantized(ctx, ins[i], batch, norm, outs[i], st->d_err, s)) return rc;
+    if (int rc = q38_full_decode(ctx, st, layer, batch, qg, key, value, positions, max_position, att,
+                                 stream))
+        return rc;
+    return project_device(ctx, w->out, batch, att, branch, st->d_err, s);
+}
+
+}  // extern "C"

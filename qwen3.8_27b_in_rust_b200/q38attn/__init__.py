@@ -30,15 +30,33 @@ from typing import Optional
 import numpy as np
 
 from ._lib import (Q38_DEVERR_POSITION, Q38_DEVERR_SHAPE, Q38_DEVERR_TIMEOUT, Q38_ERR_ARG,
-                   Q38_ERR_CUDA, Q38_ERR_TIMEOUT, Q38_KV_BF16, Q38_KV_F32, Q38_OK, Q38Error,
+                   Q38_ERR_CUDA, Q38_ERR_TIMEOUT, Q38_GGML_BF16, Q38_GGML_F16, Q38_GGML_F32,
+                   Q38_GGML_Q2_K, Q38_GGML_Q3_K, Q38_GGML_Q4_K, Q38_GGML_Q5_K, Q38_GGML_Q6_K,
+                   Q38_GGML_Q8_0, Q38_KV_BF16, Q38_KV_F32, Q38_OK, Q38_Q8K_BLOCK_BYTES, Q38Error,
                    Q38Geom, check, last_error, load)
 
 __all__ = [
     "Context", "State", "Q38Error", "Q38Geom", "geometry", "load", "last_error",
     "Q38_OK", "Q38_ERR_ARG", "Q38_ERR_CUDA", "Q38_ERR_TIMEOUT", "Q38_KV_F32", "Q38_KV_BF16",
     "Q38_DEVERR_POSITION", "Q38_DEVERR_TIMEOUT", "Q38_DEVERR_SHAPE",
-    "is_full_attention", "full_index", "recurrent_index", "gguf_read_f32",
+    "is_full_attention", "full_index", "recurrent_index", "gguf_read_f32", "Weight",
+    "Q38_GGML_F32", "Q38_GGML_F16", "Q38_GGML_BF16", "Q38_GGML_Q8_0", "Q38_GGML_Q2_K",
+    "Q38_GGML_Q3_K", "Q38_GGML_Q4_K", "Q38_GGML_Q5_K", "Q38_GGML_Q6_K", "Q38_Q8K_BLOCK_BYTES",
+    "row_bytes",
 ]
+
+# ggml (elements, bytes) per block of the projection types (src/gguf/mod.rs:136-178).
+_GGML_BLOCK = {Q38_GGML_F32: (1, 4), Q38_GGML_F16: (1, 2), Q38_GGML_BF16: (1, 2),
+               Q38_GGML_Q8_0: (32, 34), Q38_GGML_Q2_K: (256, 84), Q38_GGML_Q3_K: (256, 110),
+               Q38_GGML_Q4_K: (256, 144), Q38_GGML_Q5_K: (256, 176), Q38_GGML_Q6_K: (256, 210)}
+
+
+def row_bytes(ggml_type: int, width: int) -> int:
+    """row_bytes (src/kernel/tensor.rs:46-53) of the projection types."""
+    el, by = _GGML_BLOCK[ggml_type]
+    if width % el:
+        raise ValueError(f"width {width} is not a whole number of {el}-element blocks")
+    return width // el * by
 
 # Geometry of src/model/mod.rs:13-26.
 ATTN_HEADS = 24
@@ -252,6 +270,40 @@ def gguf_read_f32(path, name: str, count: int) -> np.ndarray:
     return out
 
 
+class Weight:
+    """A projection matrix on the device: ``rows`` outputs over ``width``
+    inputs, the GGUF tensor of shape [width, rows] (q38_weight_create)."""
+
+    def __init__(self, ctx: "Context", handle: ctypes.c_void_p):
+        self._lib = ctx._lib
+        self.ctx = ctx
+        self.handle = handle
+        t, w, r = ctypes.c_int(), ctypes.c_int64(), ctypes.c_int64()
+        check(self._lib.q38_weight_info(handle, ctypes.byref(t), ctypes.byref(w), ctypes.byref(r)))
+        self.ggml_type, self.width, self.rows = t.value, w.value, r.value
+
+    def close(self) -> None:
+        if self.handle:
+            check(self._lib.q38_weight_destroy(self.handle))
+            self.handle = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class _LinearProjections(ctypes.Structure):
+    _fields_ = [("qkv", ctypes.c_void_p), ("z", ctypes.c_void_p), ("beta", ctypes.c_void_p),
+                ("alpha", ctypes.c_void_p), ("out", ctypes.c_void_p)]
+
+
+class _FullProjections(ctypes.Structure):
+    _fields_ = [("q", ctypes.c_void_p), ("k", ctypes.c_void_p), ("v", ctypes.c_void_p),
+                ("out", ctypes.c_void_p)]
+
+
 class Context:
     """A device, the model geometry and the bound per-layer weights
     (the weight half of Q38Model::bind, src/model/ops.rs:1450-1459)."""
@@ -298,6 +350,65 @@ class Context:
         """Binds layers first_layer..last_layer (64 = MTP) from a GGUF
         checkpoint by the reference's tensor names (ops.rs:53-100)."""
         check(self._lib.q38_bind_gguf(self.handle, str(path).encode(), first_layer, last_layer))
+
+    # projections ----------------------------------------------------------
+    def weight(self, ggml_type: int, width: int, rows: int, data: np.ndarray) -> Weight:
+        """Uploads a projection matrix: data holds the GGUF tensor's bytes
+        (rows * row_bytes(ggml_type, width) uint8)."""
+        data = np.ascontiguousarray(data).view(np.uint8).reshape(-1)
+        h = ctypes.c_void_p()
+        check(self._lib.q38_weight_create(self.handle, ggml_type, width, rows,
+                                          ctypes.c_void_p(data.ctypes.data), data.size,
+                                          ctypes.byref(h)))
+        return Weight(self, h)
+
+    def weight_from_gguf(self, path, name: str) -> Weight:
+        h = ctypes.c_void_p()
+        check(self._lib.q38_weight_from_gguf(self.handle, str(path).encode(), name.encode(),
+                                             ctypes.byref(h)))
+        return Weight(self, h)
+
+    def reserve_projection(self, batch: int, width: int) -> None:
+        check(self._lib.q38_ctx_reserve_projection(self.handle, batch, width))
+
+    def quantize_q8_k(self, x, blocks, stream=None) -> None:
+        """quantize_q8_k of x [batch][width] (CUDA f32) into blocks (CUDA
+        uint8, batch*width/256*292 bytes, the reference's block layout)."""
+        b, width = x.shape
+        check(self._lib.q38_quantize_q8_k(self.handle, b, width, _dev_ptr(x, "x"),
+                                          _dev_ptr(blocks, "blocks", "uint8"),
+                                          _stream_ptr(stream)))
+
+    def project(self, w: Weight, x, out, stream=None) -> None:
+        """project / batch_project: out [batch][rows] = W x [batch][width] (CUDA f32)."""
+        check(self._lib.q38_project(self.handle, w.handle, x.shape[0], _dev_ptr(x, "x"),
+                                    _dev_ptr(out, "out"), _stream_ptr(stream)))
+
+    def project_host(self, w: Weight, x: np.ndarray) -> np.ndarray:
+        x = np.ascontiguousarray(x, np.float32).reshape(-1, w.width)
+        out = np.zeros((x.shape[0], w.rows), np.float32)
+        check(self._lib.q38_project_host(self.handle, w.handle, x.shape[0], _host_ptr(x, "x"),
+                                         _host_ptr(out, "out", True)))
+        return out
+
+    def linear_attention_decode(self, state: "State", layer: int, weights: dict, norm, branch,
+                                stream=None) -> None:
+        """linear_attention (ops.rs:744-803): weights has Weight values for
+        qkv, z, beta, alpha, out; norm and branch are [batch][hidden] CUDA f32."""
+        p = _LinearProjections(*(weights[k].handle for k in ("qkv", "z", "beta", "alpha", "out")))
+        check(self._lib.q38_linear_attention_decode(
+            self.handle, state.handle, layer, norm.shape[0], ctypes.byref(p),
+            _dev_ptr(norm, "norm"), _dev_ptr(branch, "branch"), _stream_ptr(stream)))
+
+    def full_attention_decode(self, state: "State", layer: int, weights: dict, norm, positions,
+                              branch, max_position: int = -1, stream=None) -> None:
+        """full_attention (ops.rs:941-981): weights has Weight values for q,
+        k, v, out."""
+        p = _FullProjections(*(weights[k].handle for k in ("q", "k", "v", "out")))
+        check(self._lib.q38_full_attention_decode(
+            self.handle, state.handle, layer, norm.shape[0], ctypes.byref(p),
+            _dev_ptr(norm, "norm"), _dev_ptr(positions, "positions", "int32"), max_position,
+            _dev_ptr(branch, "branch"), _stream_ptr(stream)))
 
     def state(self, batch: int, context_length: int, full_slots: int = FULL_SLOTS,
               linear_slots: int = LINEAR_SLOTS, kv_dtype: int = Q38_KV_F32) -> State:

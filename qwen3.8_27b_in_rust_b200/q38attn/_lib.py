@@ -22,6 +22,9 @@ Q38_KV_BF16 = 1
 Q38_DEVERR_POSITION = 1
 Q38_DEVERR_TIMEOUT = 2
 Q38_DEVERR_SHAPE = 4
+Q38_GGML_F32, Q38_GGML_F16, Q38_GGML_Q8_0, Q38_GGML_BF16 = 0, 1, 8, 30
+Q38_GGML_Q2_K, Q38_GGML_Q3_K, Q38_GGML_Q4_K, Q38_GGML_Q5_K, Q38_GGML_Q6_K = 10, 11, 12, 13, 14
+Q38_Q8K_BLOCK_BYTES = 292
 
 
 class Q38Geom(ctypes.Structure):
@@ -96,6 +99,19 @@ SIGNATURES = {
     "q38_linear_core": (c_int, [_VP, _VP, c_int, _VP, _VP, _VP, _VP, _VP, _VP, _VP]),
     "q38_full_core": (c_int, [_VP, _VP, c_int, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP,
                               c_size_t, c_size_t, c_uint32]),
+    "q38_weight_create": (c_int, [_VP, c_int, ctypes.c_int64, ctypes.c_int64, _VP, c_size_t,
+                                  POINTER(c_void_p)]),
+    "q38_weight_destroy": (c_int, [_VP]),
+    "q38_weight_info": (c_int, [_VP, POINTER(c_int), POINTER(ctypes.c_int64),
+                                POINTER(ctypes.c_int64)]),
+    "q38_weight_from_gguf": (c_int, [_VP, c_char_p, c_char_p, POINTER(c_void_p)]),
+    "q38_quantize_q8_k": (c_int, [_VP, c_int, ctypes.c_int64, _VP, _VP, _VP]),
+    "q38_project": (c_int, [_VP, _VP, c_int, _VP, _VP, _VP]),
+    "q38_project_host": (c_int, [_VP, _VP, c_int, _VP, _VP]),
+    "q38_ctx_reserve_projection": (c_int, [_VP, c_int, ctypes.c_int64]),
+    "q38_linear_attention_decode": (c_int, [_VP, _VP, c_int, c_int, _VP, _VP, _VP, _VP]),
+    "q38_full_attention_decode": (c_int, [_VP, _VP, c_int, c_int, _VP, _VP, _VP, c_int, _VP,
+                                          _VP]),
 }
 
 _lock = threading.Lock()

@@ -90,3 +90,45 @@ def round_bf16(x: np.ndarray) -> np.ndarray:
     u = np.ascontiguousarray(x, np.float32).view(np.uint32).astype(np.uint64)
     u = (u + 0x7FFF + ((u >> 16) & 1)) & 0xFFFF0000
     return u.astype(np.uint32).view(np.float32)
+
+
+# ---------------------------------------------------------------------------
+# Projection weights in the ggml block formats (no checkpoint is available).
+# Quant bits and packed scales are uniform random bytes; the f16 super-block
+# scales d / dmin are drawn so that a dequantized weight is of order 0.02
+# (d ~ U(0.5, 1.5) * 1e-4, dmin ~ U(0, 1) * 1e-4 for the K-quants, 3e-4 for
+# Q8_0), as in a
+# trained checkpoint. F32 / F16 / BF16 weights are N(0, 0.02^2).
+# ---------------------------------------------------------------------------
+_BLOCK_LAYOUT = {
+    # type: (elements, bytes, [(offset of an f16 scale, kind)])  kind: "d" or "dmin"
+    8: (32, 34, [(0, "d")]),                    # Q8_0
+    10: (256, 84, [(80, "d"), (82, "dmin")]),   # Q2_K
+    11: (256, 110, [(108, "d")]),               # Q3_K
+    12: (256, 144, [(0, "d"), (2, "dmin")]),    # Q4_K
+    13: (256, 176, [(0, "d"), (2, "dmin")]),    # Q5_K
+    14: (256, 210, [(208, "d")]),               # Q6_K
+}
+
+
+def quant_weight(g: np.random.Generator, ggml_type: int, rows: int, width: int) -> np.ndarray:
+    """Bytes of a [width, rows] GGUF tensor of `ggml_type` (rows * row_bytes uint8)."""
+    if ggml_type == 0:
+        return normal(g, (rows, width), 0.02).view(np.uint8).reshape(-1)
+    if ggml_type in (1, 30):
+        w = normal(g, (rows, width), 0.02)
+        if ggml_type == 1:
+            bits = w.astype(np.float16).view(np.uint16)
+        else:
+            bits = round_bf16(w).view(np.uint32) >> np.uint32(16)
+        return np.ascontiguousarray(bits.astype(np.uint16)).view(np.uint8).reshape(-1)
+    el, by, scales = _BLOCK_LAYOUT[ggml_type]
+    nblk = rows * (width // el)
+    raw = g.integers(0, 256, size=(nblk, by), dtype=np.uint8)
+    for off, kind in scales:
+        lo, hi = (0.5, 1.5) if kind == "d" else (0.0, 1.0)
+        scale = 1e-4 if ggml_type != 8 else 3e-4
+        v = (g.uniform(lo, hi, nblk) * scale).astype(np.float16).view(np.uint16)
+        raw[:, off] = (v & 0xff).astype(np.uint8)
+        raw[:, off + 1] = (v >> 8).astype(np.uint8)
+    return np.ascontiguousarray(raw).reshape(-1)

@@ -23,6 +23,7 @@ GGML_F32 = (0, 1, 4)
 GGML_F16 = (1, 1, 2)
 GGML_Q8_0 = (8, 32, 34)
 GGML_Q4_K = (12, 256, 144)
+GGML_Q6_K = (14, 256, 210)
 
 
 def _string(s: str | bytes) -> bytes:
