@@ -67,6 +67,8 @@ def parse_args():
     ap.add_argument("--no-split", action="store_true")
     ap.add_argument("--split-context", type=int, default=131072)
     ap.add_argument("--split-steps", type=int, default=50)
+    ap.add_argument("--no-proj", action="store_true")
+    ap.add_argument("--proj-layers", type=int, default=12)
     return ap.parse_args()
 
 
@@ -207,6 +209,73 @@ def run_linear_prefill(args, ctx, q38attn, torch, rank: int) -> dict:
     del qkv0, z, b0, a0, qkv, beta, alpha, att
     torch.cuda.empty_cache()
     return {"ms": ms, "clocks": clocks.summary()}
+
+
+# Projection weights of one DeltaNet layer, Q4_K_M-like (ggml type, width, rows):
+# attn_qkv and attn_gate Q4_K, the 48-row ssm_beta / ssm_alpha gates Q8_0,
+# ssm_out Q6_K (src/model/mod.rs:28-48 names; no checkpoint is available).
+PROJ_SPEC = {"qkv": (12, 5120, 10240), "z": (12, 5120, 6144), "beta": (8, 5120, 48),
+             "alpha": (8, 5120, 48), "out": (14, 6144, 5120)}
+
+
+def run_projection(args, ctx, q38attn, synth, torch, rank: int) -> dict:
+    """The projections around a DeltaNet core (linear_attention, ops.rs:761-803
+    minus the core): quantize the 5120-wide input once, qkv / z / beta /
+    alpha, quantize the 6144-wide core output, ssm_out -- for `proj_layers`
+    distinct layers' weights (more bytes than L2 holds), replayed as one CUDA
+    graph; at batch 1 (the reference's decode) and at the decode batch."""
+    g = synth.rng(args.seed + 7 + rank)
+    layers, nbytes = [], 0
+    for _ in range(args.proj_layers):
+        d = {}
+        for k, (t, w, r) in PROJ_SPEC.items():
+            data = synth.quant_weight(g, t, r, w)
+            nbytes += data.size
+            d[k] = ctx.weight(t, w, r, data)
+        layers.append(d)
+    per_layer = nbytes / args.proj_layers
+    out = {}
+    for B in sorted({1, args.batch}):
+        ctx.reserve_projection(B, 6144)
+        x = torch.randn(B, 5120, device="cuda")
+        a = torch.randn(B, 6144, device="cuda")
+        outs = {k: torch.zeros(B, r, device="cuda") for k, (t, w, r) in PROJ_SPEC.items()}
+
+        def step():
+            for d in layers:
+                for k in ("qkv", "z", "beta", "alpha"):
+                    ctx.project(d[k], x, outs[k])
+                ctx.project(d["out"], a, outs["out"])
+
+        step()
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side), torch.cuda.graph(graph, stream=side):
+            step()
+        torch.cuda.current_stream().wait_stream(side)
+        for _ in range(3):
+            graph.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        iters = 10
+        e0.record()
+        for _ in range(iters):
+            graph.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / iters / args.proj_layers
+        peak, _ = load_peaks()
+        gbs = per_layer / (ms * 1e-3) / 1e9
+        out[f"batch{B}"] = {"ms_per_layer": ms, "weight_gbs": gbs, "frac": gbs / peak,
+                            "launches_per_layer": 7 * ((B + 7) // 8)}
+        del graph
+    for d in layers:
+        for w in d.values():
+            w.close()
+    out["weight_bytes_per_layer"] = per_layer
+    return out
 
 
 def run_split_sequence(args, ctx, q38attn, torch, dist, rank: int, world: int) -> dict:
@@ -576,6 +645,10 @@ def run_ours(args) -> None:
         prefill = run_prefill(args, ctx, q38attn, synth, torch, rank)
         lin_prefill = run_linear_prefill(args, ctx, q38attn, torch, rank)
 
+    proj = None
+    if not args.no_proj:
+        proj = run_projection(args, ctx, q38attn, synth, torch, rank)
+
     # End-to-end through the host-pointer C-ABI calls.
     e2e = None
     if e2e_steps:
@@ -697,6 +770,14 @@ def run_ours(args) -> None:
                     "peak_tflops": tpeak, "peak_gbs": peak,
                 },
                 "clocks": lin_prefill["clocks"],
+            }
+        if proj:
+            line["projection"] = {
+                "workload": ("linear_attention projections per DeltaNet layer (quantize_q8_k, "
+                             "attn_qkv 5120->10240 Q4_K, attn_gate 5120->6144 Q4_K, ssm_beta / "
+                             "ssm_alpha 5120->48 Q8_0, quantize, ssm_out 6144->5120 Q6_K), "
+                             f"{args.proj_layers} layers' weights, one CUDA graph"),
+                **proj,
             }
         if e2e:
             line["e2e"] = {"value": tokens * e2e_steps / e2e_s, "unit": "tok/s",

@@ -389,7 +389,9 @@ typedef struct q38_weight q38_weight;
 /* Copies a projection matrix to the device: `rows` rows of `width` inputs
  * each, the GGUF tensor of shape [width, rows] (TensorEntry, whose rows are
  * row_bytes(type, width) bytes, src/kernel/tensor.rs:46-53). data is a HOST
- * pointer to exactly rows * row_bytes bytes (nbytes). */
+ * pointer to exactly rows * row_bytes bytes (nbytes). width must be a
+ * multiple of 4 (of 256 for the K-quants) and at most 32768; the model's
+ * projections are 5120 and 6144 wide. */
 int q38_weight_create(q38_ctx *ctx, int ggml_type, int64_t width, int64_t rows, const void *data,
                       size_t nbytes, q38_weight **out);
 int q38_weight_destroy(q38_weight *w);
@@ -411,15 +413,19 @@ int q38_quantize_q8_k(q38_ctx *ctx, int batch, int64_t width, const float *input
  * gemm_rows writes it (tensor.rs:978-1000). K-quant weights: the input is
  * quantized to Q8_K on the device and each output is bit-identical to the
  * reference's scalar integer dot. F32/F16/BF16/Q8_0: f32 dot, equal to the
- * reference's within rounding. Uses the context's projection scratch
- * (q38_ctx_reserve_projection sizes it ahead; otherwise it grows here). */
+ * reference's within rounding. The Q8_K quantization runs inside the GEMV
+ * (each CTA quantizes the tokens into shared memory), so nothing is
+ * allocated; input must be 16-byte aligned. Launched as a programmatic
+ * dependent of the previous kernel on the stream: the first weight tiles are
+ * fetched while that kernel finishes. */
 int q38_project(q38_ctx *ctx, const q38_weight *w, int batch, const float *input, float *output,
                 void *stream);
 /* Host-pointer form (synchronous). */
 int q38_project_host(q38_ctx *ctx, const q38_weight *w, int batch, const float *input,
                      float *output);
-/* Sizes the projection scratch for `batch` tokens of up to `width` inputs, so
- * that later q38_project / *_attention_decode calls allocate nothing. */
+/* Checks a projection shape ahead of use. The projections need no scratch
+ * (the quantized input lives in shared memory), so this allocates nothing;
+ * kept so a host can validate its batch and width once at start-up. */
 int q38_ctx_reserve_projection(q38_ctx *ctx, int batch, int64_t width);
 
 /* The projections of one Gated DeltaNet layer (Q38Attention::Linear,

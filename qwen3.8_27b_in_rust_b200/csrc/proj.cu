@@ -41,9 +41,12 @@
 namespace q38 {
 namespace {
 
-constexpr int kProjThreads = 256;
+constexpr int kProjConsumerWarps = 8;
+constexpr int kProjQ8KThreads = 32 * (kProjConsumerWarps + 1);
+constexpr int kProjTileRows = kProjMaxTileRows;
 constexpr int kActStride = 272;  // shared bytes per activation block: 256 quants + 16 (bank spread)
 constexpr int kMaxStages = 4;
+constexpr int kMaxDevices = 64;
 constexpr uint32_t kNibbles = 0x0f0f0f0fu;
 
 __device__ __forceinline__ float half_to_float(uint32_t bits16) {
@@ -79,202 +82,248 @@ __device__ __forceinline__ void scale_min_k4(int j, const uint32_t (&s)[3], int 
 __device__ __forceinline__ int pair_sum(const int16_t *sums, int g) { return int(sums[g]) + int(sums[g + 1]); }
 
 // ---- per-block terms, one per K-quant type ----------------------------------
-// w: the weight block in shared memory; a: its 256 activation quants; sums:
-// the 16 activation group sums; as: the activation block scale. Returns the
-// block's term of the reference's running total.
+// Each type is a register image of one weight block: load() reads the block
+// from shared memory once (unpacking its scales), term() is the block's term
+// of the reference's running total for one token: `a` its 256 activation
+// quants, `sums` the 16 activation group sums, `as` the activation scale. A
+// thread reuses the image for every token of the launch.
 
-// dot_q4_k_q8_k_scalar, tensor.rs:365-391. 144 bytes: d, dmin | 12 scale bytes | 128 nibble bytes.
-__device__ __forceinline__ float block_q4_k(const uint8_t *w, const int8_t *a8, const int16_t *sums, float as) {
-    const uint8_t *a = reinterpret_cast<const uint8_t *>(a8);
-    const uint32_t dm = ld32(w);
-    const uint32_t sc[3] = {ld32(w + 4), ld32(w + 8), ld32(w + 12)};
-    int weighted = 0, minimum = 0;
+// dot_q4_k_q8_k_scalar, tensor.rs:365-391. 144 bytes: d, dmin | 12 scale
+// bytes | 128 nibble bytes (sub-block 2c in the low nibbles of bytes
+// 32c..32c+31, sub-block 2c+1 in their high nibbles).
+struct BlockQ4K {
+    uint32_t q[32];
+    int sc[8], mn[8];
+    uint32_t dm;
+    __device__ __forceinline__ void load(const uint8_t *w) {
+        dm = ld32(w);
+        const uint32_t s[3] = {ld32(w + 4), ld32(w + 8), ld32(w + 12)};
 #pragma unroll
-    for (int c = 0; c < 4; ++c) {
-        int sc0, mn0, sc1, mn1;
-        scale_min_k4(2 * c, sc, sc0, mn0);
-        scale_min_k4(2 * c + 1, sc, sc1, mn1);
-        const uint4 q[2] = {ld128(w + 16 + 32 * c), ld128(w + 32 + 32 * c)};
-        const uint4 lo[2] = {ld128(a + 64 * c), ld128(a + 64 * c + 16)};
-        const uint4 hi[2] = {ld128(a + 64 * c + 32), ld128(a + 64 * c + 48)};
-        int dot0 = 0, dot1 = 0;
+        for (int j = 0; j < 8; ++j) scale_min_k4(j, s, sc[j], mn[j]);
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-            const uint32_t qw[4] = {q[h].x, q[h].y, q[h].z, q[h].w};
-            const uint32_t lw[4] = {lo[h].x, lo[h].y, lo[h].z, lo[h].w};
-            const uint32_t hw[4] = {hi[h].x, hi[h].y, hi[h].z, hi[h].w};
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                dot0 = __dp4a(int(qw[k] & kNibbles), int(lw[k]), dot0);
-                dot1 = __dp4a(int((qw[k] >> 4) & kNibbles), int(hw[k]), dot1);
-            }
-        }
-        weighted += sc0 * dot0 + sc1 * dot1;
-        minimum += mn0 * pair_sum(sums, 4 * c) + mn1 * pair_sum(sums, 4 * c + 2);
-    }
-    const float d = half_to_float(dm) * as;
-    const float dmin = half_to_float(dm >> 16) * as;
-    return d * float(weighted) - dmin * float(minimum);
-}
-
-// dot_q5_k_q8_k_scalar, tensor.rs:393-428. 176 bytes: d, dmin | 12 scales | 32 high-bit bytes | 128 nibble bytes.
-__device__ __forceinline__ float block_q5_k(const uint8_t *w, const int8_t *a8, const int16_t *sums, float as) {
-    const uint8_t *a = reinterpret_cast<const uint8_t *>(a8);
-    const uint32_t dm = ld32(w);
-    const uint32_t sc[3] = {ld32(w + 4), ld32(w + 8), ld32(w + 12)};
-    const uint4 hb4[2] = {ld128(w + 16), ld128(w + 32)};
-    const uint32_t hb[8] = {hb4[0].x, hb4[0].y, hb4[0].z, hb4[0].w, hb4[1].x, hb4[1].y, hb4[1].z, hb4[1].w};
-    int weighted = 0, minimum = 0;
-#pragma unroll
-    for (int c = 0; c < 4; ++c) {
-        int sc0, mn0, sc1, mn1;
-        scale_min_k4(2 * c, sc, sc0, mn0);
-        scale_min_k4(2 * c + 1, sc, sc1, mn1);
-        const uint4 q[2] = {ld128(w + 48 + 32 * c), ld128(w + 64 + 32 * c)};
-        const uint4 lo[2] = {ld128(a + 64 * c), ld128(a + 64 * c + 16)};
-        const uint4 hi[2] = {ld128(a + 64 * c + 32), ld128(a + 64 * c + 48)};
-        int dot0 = 0, dot1 = 0;
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-            const uint32_t qw[4] = {q[h].x, q[h].y, q[h].z, q[h].w};
-            const uint32_t lw[4] = {lo[h].x, lo[h].y, lo[h].z, lo[h].w};
-            const uint32_t hw[4] = {hi[h].x, hi[h].y, hi[h].z, hi[h].w};
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                const uint32_t hbits = hb[4 * h + k];
-                const uint32_t q0 = (qw[k] & kNibbles) | (((hbits >> (2 * c)) & 0x01010101u) << 4);
-                const uint32_t q1 = ((qw[k] >> 4) & kNibbles) | (((hbits >> (2 * c + 1)) & 0x01010101u) << 4);
-                dot0 = __dp4a(int(q0), int(lw[k]), dot0);
-                dot1 = __dp4a(int(q1), int(hw[k]), dot1);
-            }
-        }
-        weighted += sc0 * dot0 + sc1 * dot1;
-        minimum += mn0 * pair_sum(sums, 4 * c) + mn1 * pair_sum(sums, 4 * c + 2);
-    }
-    const float d = half_to_float(dm) * as;
-    const float dmin = half_to_float(dm >> 16) * as;
-    return d * float(weighted) - dmin * float(minimum);
-}
-
-// dot_q6_k_q8_k_scalar, tensor.rs:430-460. 210 bytes: 128 low-nibble bytes |
-// 64 high-bit bytes | 16 signed scales | d. Values are 6-bit minus 32.
-__device__ __forceinline__ float block_q6_k(const uint8_t *w, const int8_t *a8, const int16_t *, float as) {
-    const uint8_t *a = reinterpret_cast<const uint8_t *>(a8);
-    int weighted = 0;
-#pragma unroll
-    for (int half = 0; half < 2; ++half) {
-        const uint32_t s4 = ld32_a2(w + 192 + 8 * half), s4b = ld32_a2(w + 196 + 8 * half);
-        const int8_t sc[8] = {int8_t(byte_of(s4, 0)), int8_t(byte_of(s4, 1)), int8_t(byte_of(s4, 2)),
-                              int8_t(byte_of(s4, 3)), int8_t(byte_of(s4b, 0)), int8_t(byte_of(s4b, 1)),
-                              int8_t(byte_of(s4b, 2)), int8_t(byte_of(s4b, 3))};
-#pragma unroll
-        for (int g = 0; g < 2; ++g) {  // 16 of the 32 positions i per group
-            int d0 = 0, d1 = 0, d2 = 0, d3 = 0;
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                const int i = 16 * g + 4 * k;
-                const uint32_t l0 = ld32_a2(w + 64 * half + i), l1 = ld32_a2(w + 64 * half + 32 + i);
-                const uint32_t hh = ld32_a2(w + 128 + 32 * half + i);
-                const uint32_t q0 = __vsub4((l0 & kNibbles) | ((hh & 0x03030303u) << 4), 0x20202020u);
-                const uint32_t q1 = __vsub4((l1 & kNibbles) | (((hh >> 2) & 0x03030303u) << 4), 0x20202020u);
-                const uint32_t q2 = __vsub4(((l0 >> 4) & kNibbles) | (((hh >> 4) & 0x03030303u) << 4), 0x20202020u);
-                const uint32_t q3 = __vsub4(((l1 >> 4) & kNibbles) | (((hh >> 6) & 0x03030303u) << 4), 0x20202020u);
-                const uint8_t *ab = a + 128 * half + i;
-                d0 = __dp4a(int(q0), int(ld32(ab)), d0);
-                d1 = __dp4a(int(q1), int(ld32(ab + 32)), d1);
-                d2 = __dp4a(int(q2), int(ld32(ab + 64)), d2);
-                d3 = __dp4a(int(q3), int(ld32(ab + 96)), d3);
-            }
-            weighted += sc[g] * d0 + sc[g + 2] * d1 + sc[g + 4] * d2 + sc[g + 6] * d3;
+        for (int k = 0; k < 8; ++k) {
+            const uint4 v = ld128(w + 16 + 16 * k);
+            q[4 * k] = v.x, q[4 * k + 1] = v.y, q[4 * k + 2] = v.z, q[4 * k + 3] = v.w;
         }
     }
-    const float d = half_to_float(ld32_a2(w + 208)) * as;
-    return d * float(weighted);
-}
-
-// dot_q3_k_q8_k_scalar, tensor.rs:335-363. 110 bytes: 32 high-bit-mask bytes |
-// 64 two-bit bytes | 12 packed scales | d. Values are 3-bit minus 4.
-__device__ __forceinline__ float block_q3_k(const uint8_t *w, const int8_t *a8, const int16_t *, float as) {
-    const uint8_t *a = reinterpret_cast<const uint8_t *>(a8);
-    // unpack_q3_scales, tensor.rs:34-44.
-    uint8_t p[12];
+    __device__ __forceinline__ float term(const uint8_t *a, const int16_t *sums, float as) const {
+        int weighted = 0, minimum = 0;
 #pragma unroll
-    for (int k = 0; k < 6; ++k) {
-        const uint32_t h = *reinterpret_cast<const uint16_t *>(w + 96 + 2 * k);
-        p[2 * k] = uint8_t(h);
-        p[2 * k + 1] = uint8_t(h >> 8);
-    }
-    int sc[16];
+        for (int c = 0; c < 4; ++c) {
+            int dot0 = 0, dot1 = 0;
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
-        const int low = i < 8 ? (p[i] & 15) : (p[i - 8] >> 4);
-        const int high = (p[8 + i % 4] >> (2 * (i / 4))) & 3;
-        sc[i] = (low | (high << 4)) - 32;
-    }
-    int weighted = 0;
-#pragma unroll
-    for (int half = 0; half < 2; ++half) {
-#pragma unroll
-        for (int field = 0; field < 4; ++field) {
-            const int group = 4 * half + field;
-#pragma unroll
-            for (int g = 0; g < 2; ++g) {
-                int dsum = 0;
+            for (int h = 0; h < 2; ++h) {
+                const uint4 lo = ld128(a + 64 * c + 16 * h), hi = ld128(a + 64 * c + 32 + 16 * h);
+                const uint32_t lw[4] = {lo.x, lo.y, lo.z, lo.w}, hw[4] = {hi.x, hi.y, hi.z, hi.w};
 #pragma unroll
                 for (int k = 0; k < 4; ++k) {
-                    const int l = 16 * g + 4 * k;
-                    const uint32_t lw = ld32_a2(w + 32 + 32 * half + l), hw = ld32_a2(w + l);
-                    const uint32_t q2 = (lw >> (2 * field)) & 0x03030303u;
-                    const uint32_t hbit = (hw >> group) & 0x01010101u;
-                    const uint32_t q = __vsub4(q2 | (hbit << 2), 0x04040404u);
-                    dsum = __dp4a(int(q), int(ld32(a + 128 * half + 32 * field + l)), dsum);
+                    const uint32_t qw = q[8 * c + 4 * h + k];
+                    dot0 = __dp4a(int(qw & kNibbles), int(lw[k]), dot0);
+                    dot1 = __dp4a(int((qw >> 4) & kNibbles), int(hw[k]), dot1);
                 }
-                weighted += sc[2 * group + g] * dsum;
             }
+            weighted += sc[2 * c] * dot0 + sc[2 * c + 1] * dot1;
+            minimum += mn[2 * c] * pair_sum(sums, 4 * c) + mn[2 * c + 1] * pair_sum(sums, 4 * c + 2);
+        }
+        const float d = half_to_float(dm) * as;
+        const float dmin = half_to_float(dm >> 16) * as;
+        return d * float(weighted) - dmin * float(minimum);
+    }
+};
+
+// dot_q5_k_q8_k_scalar, tensor.rs:393-428. 176 bytes: d, dmin | 12 scales |
+// 32 high-bit bytes | 128 nibble bytes. The fifth bit of sub-block j's value
+// i is bit j of high byte i.
+struct BlockQ5K {
+    uint32_t q[32], hb[8];
+    int sc[8], mn[8];
+    uint32_t dm;
+    __device__ __forceinline__ void load(const uint8_t *w) {
+        dm = ld32(w);
+        const uint32_t s[3] = {ld32(w + 4), ld32(w + 8), ld32(w + 12)};
+#pragma unroll
+        for (int j = 0; j < 8; ++j) scale_min_k4(j, s, sc[j], mn[j]);
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+            const uint4 v = ld128(w + 16 + 16 * k);
+            hb[4 * k] = v.x, hb[4 * k + 1] = v.y, hb[4 * k + 2] = v.z, hb[4 * k + 3] = v.w;
+        }
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            const uint4 v = ld128(w + 48 + 16 * k);
+            q[4 * k] = v.x, q[4 * k + 1] = v.y, q[4 * k + 2] = v.z, q[4 * k + 3] = v.w;
         }
     }
-    const float d = half_to_float(ld32_a2(w + 108)) * as;
-    return d * float(weighted);
-}
+    __device__ __forceinline__ float term(const uint8_t *a, const int16_t *sums, float as) const {
+        int weighted = 0, minimum = 0;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            int dot0 = 0, dot1 = 0;
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const uint4 lo = ld128(a + 64 * c + 16 * h), hi = ld128(a + 64 * c + 32 + 16 * h);
+                const uint32_t lw[4] = {lo.x, lo.y, lo.z, lo.w}, hw[4] = {hi.x, hi.y, hi.z, hi.w};
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    const uint32_t qw = q[8 * c + 4 * h + k], hbits = hb[4 * h + k];
+                    const uint32_t q0 = (qw & kNibbles) | (((hbits >> (2 * c)) & 0x01010101u) << 4);
+                    const uint32_t q1 = ((qw >> 4) & kNibbles) | (((hbits >> (2 * c + 1)) & 0x01010101u) << 4);
+                    dot0 = __dp4a(int(q0), int(lw[k]), dot0);
+                    dot1 = __dp4a(int(q1), int(hw[k]), dot1);
+                }
+            }
+            weighted += sc[2 * c] * dot0 + sc[2 * c + 1] * dot1;
+            minimum += mn[2 * c] * pair_sum(sums, 4 * c) + mn[2 * c + 1] * pair_sum(sums, 4 * c + 2);
+        }
+        const float d = half_to_float(dm) * as;
+        const float dmin = half_to_float(dm >> 16) * as;
+        return d * float(weighted) - dmin * float(minimum);
+    }
+};
+
+// dot_q6_k_q8_k_scalar, tensor.rs:430-460. 210 bytes (2-byte aligned): 128
+// low-nibble bytes | 64 high-bit bytes | 16 signed scales | d. The 6-bit
+// values minus 32 are formed per byte with __vsub4.
+struct BlockQ6K {
+    uint32_t ql[32], qh[16], sc[4];
+    uint32_t d16;
+    __device__ __forceinline__ void load(const uint8_t *w) {
+#pragma unroll
+        for (int k = 0; k < 32; ++k) ql[k] = ld32_a2(w + 4 * k);
+#pragma unroll
+        for (int k = 0; k < 16; ++k) qh[k] = ld32_a2(w + 128 + 4 * k);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) sc[k] = ld32_a2(w + 192 + 4 * k);
+        d16 = *reinterpret_cast<const uint16_t *>(w + 208);
+    }
+    __device__ __forceinline__ int scale(int i) const { return int(int8_t(byte_of(sc[i >> 2], i & 3))); }
+    __device__ __forceinline__ float term(const uint8_t *a, const int16_t *, float as) const {
+        int weighted = 0;
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+#pragma unroll
+            for (int g = 0; g < 2; ++g) {  // positions i = 16g .. 16g+15 of this half
+                int d0 = 0, d1 = 0, d2 = 0, d3 = 0;
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    const int wi = 4 * g + k;  // word index within the 32 positions
+                    const uint32_t l0 = ql[16 * half + wi], l1 = ql[16 * half + 8 + wi];
+                    const uint32_t hh = qh[8 * half + wi];
+                    const uint32_t q0 = __vsub4((l0 & kNibbles) | ((hh & 0x03030303u) << 4), 0x20202020u);
+                    const uint32_t q1 = __vsub4((l1 & kNibbles) | (((hh >> 2) & 0x03030303u) << 4), 0x20202020u);
+                    const uint32_t q2 = __vsub4(((l0 >> 4) & kNibbles) | (((hh >> 4) & 0x03030303u) << 4), 0x20202020u);
+                    const uint32_t q3 = __vsub4(((l1 >> 4) & kNibbles) | (((hh >> 6) & 0x03030303u) << 4), 0x20202020u);
+                    const uint8_t *ab = a + 128 * half + 4 * wi;
+                    d0 = __dp4a(int(q0), int(ld32(ab)), d0);
+                    d1 = __dp4a(int(q1), int(ld32(ab + 32)), d1);
+                    d2 = __dp4a(int(q2), int(ld32(ab + 64)), d2);
+                    d3 = __dp4a(int(q3), int(ld32(ab + 96)), d3);
+                }
+                const int si = 8 * half + g;
+                weighted += scale(si) * d0 + scale(si + 2) * d1 + scale(si + 4) * d2 + scale(si + 6) * d3;
+            }
+        }
+        const float d = half_to_float(d16) * as;
+        return d * float(weighted);
+    }
+};
+
+// dot_q3_k_q8_k_scalar, tensor.rs:335-363. 110 bytes (2-byte aligned): 32
+// high-bit-mask bytes | 64 two-bit bytes | 12 packed scales | d. Values are
+// the two bits minus 4 unless the mask bit is set.
+struct BlockQ3K {
+    uint32_t hm[8], qs[16];
+    int sc[16];
+    uint32_t d16;
+    __device__ __forceinline__ void load(const uint8_t *w) {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) hm[k] = ld32_a2(w + 4 * k);
+#pragma unroll
+        for (int k = 0; k < 16; ++k) qs[k] = ld32_a2(w + 32 + 4 * k);
+        // unpack_q3_scales, tensor.rs:34-44.
+        uint32_t pw[3];
+#pragma unroll
+        for (int k = 0; k < 3; ++k) pw[k] = ld32_a2(w + 96 + 4 * k);
+        auto pb = [&](int i) { return byte_of(pw[i >> 2], i & 3); };
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+            const int low = i < 8 ? (pb(i) & 15) : (pb(i - 8) >> 4);
+            const int high = (pb(8 + i % 4) >> (2 * (i / 4))) & 3;
+            sc[i] = (low | (high << 4)) - 32;
+        }
+        d16 = *reinterpret_cast<const uint16_t *>(w + 108);
+    }
+    __device__ __forceinline__ float term(const uint8_t *a, const int16_t *, float as) const {
+        int weighted = 0;
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+#pragma unroll
+            for (int field = 0; field < 4; ++field) {
+                const int group = 4 * half + field;
+#pragma unroll
+                for (int g = 0; g < 2; ++g) {
+                    int dsum = 0;
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        const int wi = 4 * g + k;  // lanes 4wi .. 4wi+3
+                        const uint32_t q2 = (qs[8 * half + wi] >> (2 * field)) & 0x03030303u;
+                        const uint32_t hbit = (hm[wi] >> group) & 0x01010101u;
+                        const uint32_t qv = __vsub4(q2 | (hbit << 2), 0x04040404u);
+                        dsum = __dp4a(int(qv), int(ld32(a + 128 * half + 32 * field + 4 * wi)), dsum);
+                    }
+                    weighted += sc[2 * group + g] * dsum;
+                }
+            }
+        }
+        const float d = half_to_float(d16) * as;
+        return d * float(weighted);
+    }
+};
 
 // dot_q2_k_q8_k_scalar, tensor.rs:301-333. 84 bytes: 16 (scale | min << 4)
 // bytes | 64 two-bit bytes | d | dmin.
-__device__ __forceinline__ float block_q2_k(const uint8_t *w, const int8_t *a8, const int16_t *sums, float as) {
-    const uint8_t *a = reinterpret_cast<const uint8_t *>(a8);
-    int weighted = 0, minimum = 0;
+struct BlockQ2K {
+    uint32_t s[4], qs[16];
+    uint32_t dm;
+    __device__ __forceinline__ void load(const uint8_t *w) {
 #pragma unroll
-    for (int half = 0; half < 2; ++half) {
-        const uint32_t s0 = ld32(w + 8 * half), s1 = ld32(w + 8 * half + 4);
+        for (int k = 0; k < 4; ++k) s[k] = ld32(w + 4 * k);
 #pragma unroll
-        for (int field = 0; field < 4; ++field) {
-            const int si = 2 * field;  // within this half's 8 scale bytes
-            const int b0 = byte_of(si < 4 ? s0 : s1, si & 3), b1 = byte_of(si < 4 ? s0 : s1, (si & 3) + 1);
-            int dot0 = 0, dot1 = 0;
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                const uint32_t q0 = (ld32(w + 16 + 32 * half + 4 * k) >> (2 * field)) & 0x03030303u;
-                const uint32_t q1 = (ld32(w + 16 + 32 * half + 16 + 4 * k) >> (2 * field)) & 0x03030303u;
-                dot0 = __dp4a(int(q0), int(ld32(a + 128 * half + 32 * field + 4 * k)), dot0);
-                dot1 = __dp4a(int(q1), int(ld32(a + 128 * half + 32 * field + 16 + 4 * k)), dot1);
-            }
-            weighted += (b0 & 15) * dot0 + (b1 & 15) * dot1;
-            minimum += (b0 >> 4) * int(sums[8 * half + si]) + (b1 >> 4) * int(sums[8 * half + si + 1]);
-        }
+        for (int k = 0; k < 16; ++k) qs[k] = ld32(w + 16 + 4 * k);
+        dm = ld32(w + 80);
     }
-    const uint32_t dm = ld32(w + 80);
-    const float d = half_to_float(dm) * as;
-    const float dmin = half_to_float(dm >> 16) * as;
-    return d * float(weighted) - dmin * float(minimum);
-}
+    __device__ __forceinline__ float term(const uint8_t *a, const int16_t *sums, float as) const {
+        int weighted = 0, minimum = 0;
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+#pragma unroll
+            for (int field = 0; field < 4; ++field) {
+                const int si = 8 * half + 2 * field;
+                const int b0 = byte_of(s[si >> 2], si & 3), b1 = byte_of(s[(si + 1) >> 2], (si + 1) & 3);
+                int dot0 = 0, dot1 = 0;
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    const uint32_t q0 = (qs[8 * half + k] >> (2 * field)) & 0x03030303u;
+                    const uint32_t q1 = (qs[8 * half + 4 + k] >> (2 * field)) & 0x03030303u;
+                    dot0 = __dp4a(int(q0), int(ld32(a + 128 * half + 32 * field + 4 * k)), dot0);
+                    dot1 = __dp4a(int(q1), int(ld32(a + 128 * half + 32 * field + 16 + 4 * k)), dot1);
+                }
+                weighted += (b0 & 15) * dot0 + (b1 & 15) * dot1;
+                minimum += (b0 >> 4) * int(sums[si]) + (b1 >> 4) * int(sums[si + 1]);
+            }
+        }
+        const float d = half_to_float(dm) * as;
+        const float dmin = half_to_float(dm >> 16) * as;
+        return d * float(weighted) - dmin * float(minimum);
+    }
+};
 
-template <int T>
-__device__ __forceinline__ float block_term(const uint8_t *w, const int8_t *a, const int16_t *sums, float as) {
-    if constexpr (T == Q38_GGML_Q4_K) return block_q4_k(w, a, sums, as);
-    else if constexpr (T == Q38_GGML_Q5_K) return block_q5_k(w, a, sums, as);
-    else if constexpr (T == Q38_GGML_Q6_K) return block_q6_k(w, a, sums, as);
-    else if constexpr (T == Q38_GGML_Q3_K) return block_q3_k(w, a, sums, as);
-    else return block_q2_k(w, a, sums, as);
-}
+template <int T> struct BlockOf;
+template <> struct BlockOf<Q38_GGML_Q2_K> { using type = BlockQ2K; };
+template <> struct BlockOf<Q38_GGML_Q3_K> { using type = BlockQ3K; };
+template <> struct BlockOf<Q38_GGML_Q4_K> { using type = BlockQ4K; };
+template <> struct BlockOf<Q38_GGML_Q5_K> { using type = BlockQ5K; };
+template <> struct BlockOf<Q38_GGML_Q6_K> { using type = BlockQ6K; };
 
 template <int T> constexpr int kBlockBytes = 0;
 template <> constexpr int kBlockBytes<Q38_GGML_Q2_K> = 84;
@@ -298,12 +347,18 @@ __device__ __forceinline__ int32_t nearest_int(float v) {
     return int32_t(__float_as_uint(shifted) & 0x007fffffu) - 0x00400000;
 }
 
-__global__ void __launch_bounds__(128) q8k_quantize_kernel(QuantizeParams p) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int blk = blockIdx.x * 4 + warp, t = blockIdx.y;
-    if (blk >= p.nblk) return;
-    const float *src = p.x + (size_t(t) * p.nblk + blk) * 256 + lane * 8;
-    const float4 v0 = reinterpret_cast<const float4 *>(src)[0], v1 = reinterpret_cast<const float4 *>(src)[1];
+// quantize_block (quant.rs:56-96) of the 256 values at src by one warp: lane
+// l owns values 8l..8l+7. Returns the lane's eight quants packed in two
+// words, the block scale, and (in even lanes) the sum of group l/2.
+struct WarpQ8K {
+    uint32_t w0, w1;
+    float scale;
+    int group_sum;
+};
+
+__device__ __forceinline__ WarpQ8K quantize_block_warp(const float *src, int lane) {
+    const float4 v0 = reinterpret_cast<const float4 *>(src)[2 * lane];
+    const float4 v1 = reinterpret_cast<const float4 *>(src)[2 * lane + 1];
     const float v[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
     // First largest magnitude: the lane's own scan, then (magnitude, index)
     // pairs where a tie keeps the smaller index. NaN never compares greater,
@@ -331,7 +386,8 @@ __global__ void __launch_bounds__(128) q8k_quantize_kernel(QuantizeParams p) {
         }
     }
     int8_t q[8];
-    float scale = 0.f;
+    WarpQ8K r;
+    r.scale = 0.f;
     if (amax == 0.f) {
 #pragma unroll
         for (int i = 0; i < 8; ++i) q[i] = 0;
@@ -339,34 +395,42 @@ __global__ void __launch_bounds__(128) q8k_quantize_kernel(QuantizeParams p) {
         const float inverse = __fdiv_rn(-127.0f, mx);
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-            int32_t r = nearest_int(__fmul_rn(inverse, v[i]));
-            if (r > 127) r = 127;
-            q[i] = int8_t(r);
+            int32_t n = nearest_int(__fmul_rn(inverse, v[i]));
+            if (n > 127) n = 127;
+            q[i] = int8_t(n);
         }
-        scale = __fdiv_rn(1.0f, inverse);
+        r.scale = __fdiv_rn(1.0f, inverse);
     }
-    int s = 0;
+    int sum = 0;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) s += q[i];
-    s += __shfl_down_sync(0xffffffffu, s, 1);  // lanes 2g and 2g+1 hold group g
-    uint32_t w0 = 0, w1 = 0;
+    for (int i = 0; i < 8; ++i) sum += q[i];
+    r.group_sum = sum + __shfl_down_sync(0xffffffffu, sum, 1);  // lanes 2g, 2g+1 hold group g
+    r.w0 = r.w1 = 0;
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-        w0 |= uint32_t(uint8_t(q[i])) << (8 * i);
-        w1 |= uint32_t(uint8_t(q[i + 4])) << (8 * i);
+        r.w0 |= uint32_t(uint8_t(q[i])) << (8 * i);
+        r.w1 |= uint32_t(uint8_t(q[i + 4])) << (8 * i);
     }
+    return r;
+}
+
+__global__ void __launch_bounds__(128) q8k_quantize_kernel(QuantizeParams p) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int blk = blockIdx.x * 4 + warp, t = blockIdx.y;
+    if (blk >= p.nblk) return;
+    const WarpQ8K r = quantize_block_warp(p.x + (size_t(t) * p.nblk + blk) * 256, lane);
     if (p.aos) {
         unsigned char *b = p.aos + (size_t(t) * p.nblk + blk) * 292;
-        if (lane == 0) *reinterpret_cast<float *>(b) = scale;
+        if (lane == 0) *reinterpret_cast<float *>(b) = r.scale;
         // 292-byte blocks: the quants are only 4-byte aligned.
-        reinterpret_cast<uint32_t *>(b + 4 + lane * 8)[0] = w0;
-        reinterpret_cast<uint32_t *>(b + 4 + lane * 8)[1] = w1;
-        if ((lane & 1) == 0) *reinterpret_cast<int16_t *>(b + 260 + lane) = int16_t(s);
+        reinterpret_cast<uint32_t *>(b + 4 + lane * 8)[0] = r.w0;
+        reinterpret_cast<uint32_t *>(b + 4 + lane * 8)[1] = r.w1;
+        if ((lane & 1) == 0) *reinterpret_cast<int16_t *>(b + 260 + lane) = int16_t(r.group_sum);
     } else {
         const size_t bi = size_t(t) * p.nblk + blk;
-        if (lane == 0) p.act.scale[bi] = scale;
-        *reinterpret_cast<uint2 *>(p.act.quants + bi * 256 + lane * 8) = make_uint2(w0, w1);
-        if ((lane & 1) == 0) p.act.sums[bi * 16 + (lane >> 1)] = int16_t(s);
+        if (lane == 0) p.act.scale[bi] = r.scale;
+        *reinterpret_cast<uint2 *>(p.act.quants + bi * 256 + lane * 8) = make_uint2(r.w0, r.w1);
+        if ((lane & 1) == 0) p.act.sums[bi * 16 + (lane >> 1)] = int16_t(r.group_sum);
     }
 }
 
@@ -375,103 +439,136 @@ __global__ void __launch_bounds__(128) q8k_quantize_kernel(QuantizeParams p) {
 // ---------------------------------------------------------------------------
 struct ProjQ8KParams {
     const uint8_t *w;      // [rows][rb], padded to whole tiles
-    Q8KActivations act;    // tokens tok0 .. tok0+batch-1
+    const float *x;        // f32 input [batch][nblk * 256], quantized in the prologue
     float *out;            // out[t * out_ld + row]
     int *err;
     long out_ld;
-    int rows, nblk, rb, batch, tile_rows, ntiles, stages;
-    uint32_t tile_bytes;
+    int rows, nblk, rb, batch, ntiles, stages;
+    uint32_t tile_bytes;   // kProjTileRows * rb (a multiple of 16)
 };
 
+// Shared-memory plan: the weight ring, the activations, and one combine
+// buffer per consumer warp ([batch][nblk + 1] block terms).
 struct ProjSmem {
-    uint32_t ring, act_q, act_d, act_s, vbuf, total;
+    uint32_t ring, act_q, act_d, act_s, vt, total;
 };
 
-__host__ __device__ ProjSmem proj_smem_plan(int stages, uint32_t tile_bytes, int batch, int nblk, int tile_rows) {
+__host__ __device__ inline ProjSmem proj_smem_plan(int stages, uint32_t tile_bytes, int batch, int nblk) {
     ProjSmem s{};
     s.ring = 0;
     s.act_q = stages * tile_bytes;
     s.act_d = s.act_q + uint32_t(batch * nblk * kActStride);
     s.act_s = s.act_d + uint32_t(batch * nblk * 4);
-    s.vbuf = s.act_s + uint32_t(batch * nblk * 32);
-    s.total = s.vbuf + uint32_t(tile_rows * batch * nblk * 4);
+    s.vt = s.act_s + uint32_t(batch * nblk * 32);
+    s.total = s.vt + uint32_t(kProjConsumerWarps * batch * (nblk + 1) * 4);
     return s;
 }
 
+// Warp roles: warps 0..kProjConsumerWarps-1 compute (warp w owns rows w and
+// w + kProjConsumerWarps of each 16-row tile; lane j owns blocks j, j+32, ...),
+// the last warp streams the tiles. Each row's block terms go through the
+// warp's combine buffer, where lane t adds token t's terms in block order.
 template <int T>
-__global__ void __launch_bounds__(kProjThreads, 1) proj_q8k_kernel(ProjQ8KParams p) {
+__global__ void __launch_bounds__(kProjQ8KThreads, 1) proj_q8k_kernel(ProjQ8KParams p) {
     extern __shared__ __align__(128) unsigned char smem[];
-    __shared__ __align__(8) uint64_t full[kMaxStages];
-    const ProjSmem lay = proj_smem_plan(p.stages, p.tile_bytes, p.batch, p.nblk, p.tile_rows);
-    int8_t *aq = reinterpret_cast<int8_t *>(smem + lay.act_q);
+    __shared__ __align__(8) uint64_t full[kMaxStages], empty[kMaxStages];
+    __shared__ volatile int abort_flag;
+    const ProjSmem lay = proj_smem_plan(p.stages, p.tile_bytes, p.batch, p.nblk);
+    const uint8_t *aq = smem + lay.act_q;
     float *ad = reinterpret_cast<float *>(smem + lay.act_d);
     int16_t *asums = reinterpret_cast<int16_t *>(smem + lay.act_s);
-    float *vbuf = reinterpret_cast<float *>(smem + lay.vbuf);
-    const int tid = threadIdx.x;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
     if (tid == 0) {
-        for (int s = 0; s < p.stages; ++s) mbar_init(&full[s], 1);
+        abort_flag = 0;
+        for (int s = 0; s < p.stages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kProjConsumerWarps);
+        }
         fence_barrier_init();
     }
     __syncthreads();
-    if (tid == 0) {
-        for (int s = 0; s < p.stages; ++s) {
-            const int tile = blockIdx.x + s * gridDim.x;
-            if (tile >= p.ntiles) break;
-            mbar_arrive_expect_tx(&full[s], p.tile_bytes);
-            bulk_load(smem + s * p.tile_bytes, p.w + size_t(tile) * p.tile_rows * p.rb, p.tile_bytes, &full[s]);
+    // The weights are constant: the first tiles are requested before waiting
+    // for the previous kernel in the stream (programmatic dependent launch).
+    const int first = min(p.stages, (p.ntiles - int(blockIdx.x) + int(gridDim.x) - 1) / int(gridDim.x));
+    if (warp == kProjConsumerWarps && lane == 0)
+        for (int k = 0; k < first; ++k) {
+            mbar_arrive_expect_tx(&full[k], p.tile_bytes);
+            bulk_load(smem + k * p.tile_bytes,
+                      p.w + size_t(blockIdx.x + k * gridDim.x) * kProjTileRows * p.rb, p.tile_bytes, &full[k]);
         }
+    pdl_wait_primary();
+    pdl_launch_dependents();
+    // quantize_q8_k of the launch's tokens into shared memory, one warp per
+    // 256-block (the same steps as q8k_quantize_kernel).
+    for (int blk = warp; blk < p.batch * p.nblk; blk += kProjConsumerWarps + 1) {
+        const WarpQ8K r = quantize_block_warp(p.x + size_t(blk) * 256, lane);
+        *reinterpret_cast<uint2 *>(smem + lay.act_q + blk * kActStride + lane * 8) = make_uint2(r.w0, r.w1);
+        if (lane == 0) ad[blk] = r.scale;
+        if ((lane & 1) == 0) asums[blk * 16 + (lane >> 1)] = int16_t(r.group_sum);
     }
-    // Activations: quants (16-byte pieces into 272-byte rows), scales, sums.
-    const int nb = p.batch * p.nblk;
-    for (int i = tid; i < nb * 16; i += kProjThreads) {
-        const int blk = i >> 4, c = i & 15;
-        *reinterpret_cast<uint4 *>(aq + blk * kActStride + 16 * c) =
-            reinterpret_cast<const uint4 *>(p.act.quants + size_t(blk) * 256)[c];
-    }
-    for (int i = tid; i < nb; i += kProjThreads) ad[i] = p.act.scale[i];
-    for (int i = tid; i < nb * 8; i += kProjThreads)
-        reinterpret_cast<uint32_t *>(asums)[i] = reinterpret_cast<const uint32_t *>(p.act.sums)[i];
     __syncthreads();
 
-    const int pairs = p.tile_rows * p.nblk;
+    if (warp == kProjConsumerWarps) {
+        // ---------------------------------------------------------- producer
+        if (lane == 0) {
+            int k = first;
+            for (int tile = blockIdx.x + first * gridDim.x; tile < p.ntiles; tile += gridDim.x, ++k) {
+                const int s = k % p.stages;
+                if (!mbar_wait(&empty[s], uint32_t(k / p.stages - 1) & 1u)) {
+                    abort_flag = 1;
+                    set_error(p.err, kDevErrTimeout);
+                    break;
+                }
+                if (abort_flag) break;
+                mbar_arrive_expect_tx(&full[s], p.tile_bytes);
+                bulk_load(smem + s * p.tile_bytes, p.w + size_t(tile) * kProjTileRows * p.rb, p.tile_bytes,
+                          &full[s]);
+            }
+            // Every issued copy lands before the CTA exits: the last use of
+            // each stage completes its barrier phase once.
+            const int issued = k;
+            for (int j = issued - p.stages; j < issued; ++j)
+                if (j >= 0) mbar_wait(&full[j % p.stages], uint32_t(j / p.stages) & 1u);
+        }
+        return;
+    }
+
+    // ------------------------------------------------------------ consumers
+    float *vt = reinterpret_cast<float *>(smem + lay.vt) + warp * p.batch * (p.nblk + 1);
     int k = 0;
     for (int tile = blockIdx.x; tile < p.ntiles; tile += gridDim.x, ++k) {
         const int s = k % p.stages;
-        const bool ok = mbar_wait(&full[s], uint32_t(k / p.stages) & 1u);
-        if (__syncthreads_or(!ok)) {
-            if (tid == 0) set_error(p.err, kDevErrTimeout);
+        if (!__all_sync(0xffffffffu, mbar_wait(&full[s], uint32_t(k / p.stages) & 1u))) {
+            if (lane == 0) {
+                abort_flag = 1;
+                set_error(p.err, kDevErrTimeout);
+            }
             break;
         }
         const uint8_t *tw = smem + s * p.tile_bytes;
-        const int row0 = tile * p.tile_rows;
-        for (int pr = tid; pr < pairs; pr += kProjThreads) {
-            const int r = pr / p.nblk, b = pr - r * p.nblk;
-            if (row0 + r >= p.rows) continue;
-            const uint8_t *wb = tw + size_t(r) * p.rb + size_t(b) * kBlockBytes<T>;
-            for (int t = 0; t < p.batch; ++t) {
-                const int ab = t * p.nblk + b;
-                vbuf[(r * p.batch + t) * p.nblk + b] = block_term<T>(wb, aq + ab * kActStride, asums + ab * 16, ad[ab]);
+#pragma unroll 1
+        for (int r = warp; r < kProjTileRows; r += kProjConsumerWarps) {
+            const int row = tile * kProjTileRows + r;
+            if (row >= p.rows) break;  // rows ascend with r
+            for (int b = lane; b < p.nblk; b += 32) {
+                typename BlockOf<T>::type blk;
+                blk.load(tw + size_t(r) * p.rb + size_t(b) * kBlockBytes<T>);
+                for (int t = 0; t < p.batch; ++t) {
+                    const int ab = t * p.nblk + b;
+                    vt[t * (p.nblk + 1) + b] = blk.term(aq + ab * kActStride, asums + ab * 16, ad[ab]);
+                }
             }
-        }
-        __syncthreads();
-        if (tid == 0) {
-            const int next = tile + p.stages * gridDim.x;
-            if (next < p.ntiles) {
-                sm100::fence_proxy_async_smem();  // generic reads of this stage before the async overwrite
-                mbar_arrive_expect_tx(&full[s], p.tile_bytes);
-                bulk_load(smem + s * p.tile_bytes, p.w + size_t(next) * p.tile_rows * p.rb, p.tile_bytes, &full[s]);
+            __syncwarp();
+            if (lane < p.batch) {
+                const float *v = vt + lane * (p.nblk + 1);
+                float total = 0.f;
+                for (int b = 0; b < p.nblk; ++b) total = __fadd_rn(total, v[b]);
+                p.out[size_t(lane) * p.out_ld + row] = total;
             }
+            __syncwarp();
         }
-        for (int q = tid; q < p.tile_rows * p.batch; q += kProjThreads) {
-            const int r = q / p.batch, t = q - r * p.batch;
-            if (row0 + r >= p.rows) continue;
-            const float *v = vbuf + q * p.nblk;
-            float total = 0.f;
-            for (int b = 0; b < p.nblk; ++b) total = __fadd_rn(total, v[b]);
-            p.out[size_t(t) * p.out_ld + row0 + r] = total;
-        }
-        __syncthreads();
+        if (lane == 0) mbar_arrive(&empty[s]);
     }
 }
 
@@ -484,47 +581,67 @@ struct ProjF32Params {
     float *out;
     long out_ld;
     int rows, width, rb, batch;
+    int split;       // warps per row: 1 (eight rows per CTA) or 8 (one row per CTA)
 };
 
+// Weight element i of a row, four at a time (i a multiple of 4).
 template <int T>
-__device__ __forceinline__ float weight_at(const uint8_t *row, int i) {
-    if constexpr (T == Q38_GGML_F32) return reinterpret_cast<const float *>(row)[i];
-    else if constexpr (T == Q38_GGML_F16) return half_to_float(reinterpret_cast<const uint16_t *>(row)[i]);
-    else return __uint_as_float(uint32_t(reinterpret_cast<const uint16_t *>(row)[i]) << 16);  // BF16
+__device__ __forceinline__ void weights4(const uint8_t *row, int i, float (&wv)[4]) {
+    if constexpr (T == Q38_GGML_F32) {
+        const float4 v = *reinterpret_cast<const float4 *>(row + 4 * size_t(i));
+        wv[0] = v.x, wv[1] = v.y, wv[2] = v.z, wv[3] = v.w;
+    } else if constexpr (T == Q38_GGML_Q8_0) {
+        // dot_q8_0_scalar, tensor.rs:103-117: the weight is d * q (one f32
+        // product), then fma'd with x.
+        const uint8_t *blk = row + size_t(i >> 5) * 34;
+        const uint16_t *qs = reinterpret_cast<const uint16_t *>(blk + 2 + (i & 31));
+        const uint32_t q01 = qs[0], q23 = qs[1];
+        const float d = half_to_float(*reinterpret_cast<const uint16_t *>(blk));
+        wv[0] = d * float(int8_t(q01 & 0xffu));
+        wv[1] = d * float(int8_t(q01 >> 8));
+        wv[2] = d * float(int8_t(q23 & 0xffu));
+        wv[3] = d * float(int8_t(q23 >> 8));
+    } else {
+        const uint2 v = *reinterpret_cast<const uint2 *>(row + 2 * size_t(i));
+        const uint32_t h[4] = {v.x & 0xffffu, v.x >> 16, v.y & 0xffffu, v.y >> 16};
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+            wv[e] = T == Q38_GGML_F16 ? half_to_float(h[e]) : __uint_as_float(h[e] << 16);
+    }
 }
 
+// The launch's tokens sit in shared memory ([batch][width] f32). Each warp
+// covers a row (split 1) or an eighth of one (split 8); lanes take four
+// consecutive elements per 128-element stride, four strides' loads issued
+// before their fmas; the partial sums of a split row are added in warp order.
 template <int T>
 __global__ void __launch_bounds__(256) proj_f32_kernel(ProjF32Params p) {
+    extern __shared__ __align__(16) float xs[];
+    __shared__ float part[8][kProjMaxTok];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int row = blockIdx.x * 8 + warp;
-    if (row >= p.rows) return;
-    const uint8_t *w = p.w + size_t(row) * p.rb;
+    pdl_wait_primary();  // x comes from an earlier kernel in the stream
+    pdl_launch_dependents();
+    for (int i = threadIdx.x; i < p.batch * p.width / 4; i += 256)
+        reinterpret_cast<float4 *>(xs)[i] = reinterpret_cast<const float4 *>(p.x)[i];
+    __syncthreads();
+    const int row = p.split == 1 ? blockIdx.x * 8 + warp : blockIdx.x;
+    const int len = p.width / p.split;
+    const int i0 = p.split == 1 ? 0 : warp * len;
     float acc[kProjMaxTok];
 #pragma unroll
     for (int t = 0; t < kProjMaxTok; ++t) acc[t] = 0.f;
-    if constexpr (T == Q38_GGML_Q8_0) {
-        // dot_q8_0_scalar, tensor.rs:103-117: (d * q) * x accumulated by fma.
-        const int nb = p.width / 32;
-        for (int b = lane; b < nb; b += 32) {
-            const uint8_t *blk = w + size_t(b) * 34;
-            const float d = half_to_float(*reinterpret_cast<const uint16_t *>(blk));
-            for (int i = 0; i < 32; i += 2) {
-                const uint32_t qq = *reinterpret_cast<const uint16_t *>(blk + 2 + i);
-                const float w0 = d * float(int8_t(qq & 0xffu)), w1 = d * float(int8_t(qq >> 8));
-#pragma unroll
-                for (int t = 0; t < kProjMaxTok; ++t)
-                    if (t < p.batch) {
-                        const float *x = p.x + size_t(t) * p.width + b * 32 + i;
-                        acc[t] = fmaf(w1, x[1], fmaf(w0, x[0], acc[t]));
-                    }
-            }
-        }
-    } else {
-        for (int i = lane; i < p.width; i += 32) {
-            const float wv = weight_at<T>(w, i);
+    if (row < p.rows) {
+        const uint8_t *w = p.w + size_t(row) * p.rb;
+#pragma unroll 4
+        for (int i = i0 + 4 * lane; i < i0 + len; i += 128) {
+            float wv[4];
+            weights4<T>(w, i, wv);
 #pragma unroll
             for (int t = 0; t < kProjMaxTok; ++t)
-                if (t < p.batch) acc[t] = fmaf(wv, p.x[size_t(t) * p.width + i], acc[t]);
+                if (t < p.batch) {
+                    const float4 x = *reinterpret_cast<const float4 *>(xs + t * p.width + i);
+                    acc[t] = fmaf(wv[3], x.w, fmaf(wv[2], x.z, fmaf(wv[1], x.y, fmaf(wv[0], x.x, acc[t]))));
+                }
         }
     }
 #pragma unroll
@@ -532,26 +649,79 @@ __global__ void __launch_bounds__(256) proj_f32_kernel(ProjF32Params p) {
         float v = acc[t];
 #pragma unroll
         for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
-        if (lane == 0 && t < p.batch) p.out[size_t(t) * p.out_ld + row] = v;
+        acc[t] = v;
+    }
+    if (p.split == 1) {
+        if (lane == 0 && row < p.rows)
+            for (int t = 0; t < p.batch; ++t) p.out[size_t(t) * p.out_ld + row] = acc[t];
+        return;
+    }
+    if (lane == 0)
+#pragma unroll
+        for (int t = 0; t < kProjMaxTok; ++t) part[warp][t] = acc[t];
+    __syncthreads();
+    if (threadIdx.x < p.batch && row < p.rows) {
+        float v = 0.f;
+        for (int k = 0; k < 8; ++k) v += part[k][threadIdx.x];
+        p.out[size_t(threadIdx.x) * p.out_ld + row] = v;
     }
 }
 
 template <int T>
-cudaError_t launch_q8k(const ProjQ8KParams &base, int sm_count, cudaStream_t stream) {
-    ProjQ8KParams p = base;
-    const ProjSmem lay = proj_smem_plan(p.stages, p.tile_bytes, p.batch, p.nblk, p.tile_rows);
-    cudaError_t e = cudaFuncSetAttribute(proj_q8k_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         int(lay.total));
+cudaError_t launch_q8k(const ProjQ8KParams &p, int sm_count, cudaStream_t stream) {
+    const ProjSmem lay = proj_smem_plan(p.stages, p.tile_bytes, p.batch, p.nblk);
+    // The attribute is set once per device to the budget, so later launches
+    // make no extra driver calls (and can be captured in a graph).
+    static bool attr_set[kMaxDevices] = {};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
-    const int grid = std::min(p.ntiles, sm_count);
-    proj_q8k_kernel<T><<<grid, kProjThreads, lay.total, stream>>>(p);
-    return cudaGetLastError();
+    if (dev >= kMaxDevices || !attr_set[dev]) {
+        e = cudaFuncSetAttribute(proj_q8k_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 int(kProjSmemBudget));
+        if (e != cudaSuccess) return e;
+        if (dev < kMaxDevices) attr_set[dev] = true;
+    }
+    // One CTA per SM (the block images take ~150 registers a thread),
+    // launched as a programmatic dependent of the previous kernel.
+    cudaLaunchConfig_t cfg{};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.gridDim = dim3(std::min(p.ntiles, sm_count));
+    cfg.blockDim = dim3(kProjQ8KThreads);
+    cfg.dynamicSmemBytes = lay.total;
+    cfg.stream = stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, proj_q8k_kernel<T>, p);
 }
 
 template <int T>
 cudaError_t launch_f32(const ProjF32Params &p, cudaStream_t stream) {
-    proj_f32_kernel<T><<<(p.rows + 7) / 8, 256, 0, stream>>>(p);
-    return cudaGetLastError();
+    static bool attr_set[kMaxDevices] = {};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev >= kMaxDevices || !attr_set[dev]) {
+        e = cudaFuncSetAttribute(proj_f32_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 int(kProjSmemBudget));
+        if (e != cudaSuccess) return e;
+        if (dev < kMaxDevices) attr_set[dev] = true;
+    }
+    const size_t smem = size_t(p.batch) * p.width * sizeof(float);
+    if (smem > kProjSmemBudget) return cudaErrorInvalidValue;
+    cudaLaunchConfig_t cfg{};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.gridDim = dim3(p.split == 1 ? (p.rows + 7) / 8 : p.rows);
+    cfg.blockDim = dim3(256);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, proj_f32_kernel<T>, p);
 }
 
 }  // namespace
@@ -597,20 +767,10 @@ cudaError_t launch_q8k_quantize(const float *x, int batch, int width, Q8KActivat
     return cudaGetLastError();
 }
 
-cudaError_t launch_proj_q8k(const ProjWeight &w, const Q8KActivations &act, int batch, float *out,
+cudaError_t launch_proj_q8k(const ProjWeight &w, const float *x, int batch, float *out,
                             long out_ld, int *err, int sm_count, cudaStream_t stream) {
     const int nblk = int(w.width / 256);
     const int rb = int(w.row_bytes);
-    // Rows per tile: even enough that every tile starts 16-byte aligned, and
-    // small enough that the tiles cover the SMs about twice.
-    int step = 1;
-    while ((int64_t(step) * rb) % 16) ++step;
-    int tile_rows = std::max(1, kProjThreads / nblk);
-    tile_rows = std::min(tile_rows, kProjMaxTileRows);
-    const int64_t want = std::max<int64_t>(1, w.rows / (2 * int64_t(sm_count)));
-    if (want < tile_rows) tile_rows = int(want);
-    tile_rows = std::max(step, tile_rows / step * step);
-    const uint32_t tile_bytes = uint32_t((int64_t(tile_rows) * rb + 15) / 16 * 16);
     ProjQ8KParams p{};
     p.w = static_cast<const uint8_t *>(w.data);
     p.out_ld = out_ld;
@@ -618,17 +778,15 @@ cudaError_t launch_proj_q8k(const ProjWeight &w, const Q8KActivations &act, int 
     p.rows = int(w.rows);
     p.nblk = nblk;
     p.rb = rb;
-    p.tile_rows = tile_rows;
-    p.ntiles = int((w.rows + tile_rows - 1) / tile_rows);
-    p.tile_bytes = tile_bytes;
+    p.ntiles = int((w.rows + kProjTileRows - 1) / kProjTileRows);
+    p.tile_bytes = uint32_t(kProjTileRows * rb);  // 16 rows: a multiple of 16 bytes
     for (int t0 = 0; t0 < batch; t0 += kProjMaxTok) {
         p.batch = std::min(kProjMaxTok, batch - t0);
-        p.act.quants = act.quants + size_t(t0) * nblk * 256;
-        p.act.scale = act.scale + size_t(t0) * nblk;
-        p.act.sums = act.sums + size_t(t0) * nblk * 16;
+        p.x = x + size_t(t0) * nblk * 256;
         p.out = out + size_t(t0) * out_ld;
-        const uint32_t fixed = proj_smem_plan(0, tile_bytes, p.batch, nblk, tile_rows).total;
-        int stages = int((kProjSmemBudget - fixed) / tile_bytes);
+        // Stages: as many as the budget allows, up to 4.
+        const uint32_t fixed = proj_smem_plan(0, p.tile_bytes, p.batch, nblk).total;
+        int stages = int((kProjSmemBudget - fixed) / p.tile_bytes);
         stages = std::min(stages, kMaxStages);
         if (stages < 2) return cudaErrorInvalidValue;
         p.stages = stages;
@@ -654,8 +812,13 @@ cudaError_t launch_proj_f32(const ProjWeight &w, const float *x, int batch, floa
     p.rows = int(w.rows);
     p.width = int(w.width);
     p.rb = int(w.row_bytes);
-    for (int t0 = 0; t0 < batch; t0 += kProjMaxTok) {
-        p.batch = std::min(kProjMaxTok, batch - t0);
+    // Few rows: eight warps per row (each an eighth of it, whole Q8_0 blocks).
+    p.split = (w.rows < 2 * 148 && w.width % 256 == 0) ? 8 : 1;
+    // Tokens per launch: as many as fit the shared-memory budget, up to 8.
+    const int per = std::min<int64_t>(kProjMaxTok, kProjSmemBudget / (w.width * sizeof(float)));
+    if (per < 1 || w.width % 4) return cudaErrorInvalidValue;
+    for (int t0 = 0; t0 < batch; t0 += per) {
+        p.batch = std::min(per, batch - t0);
         p.x = x + size_t(t0) * w.width;
         p.out = out + size_t(t0) * out_ld;
         cudaError_t e;

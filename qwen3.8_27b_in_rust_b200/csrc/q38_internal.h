@@ -51,8 +51,6 @@ struct q38_ctx {
     int qk_dim = 0, v_dim = 0, qkv_dim = 0;
     std::map<int, q38::FullWeights> full;
     std::map<int, q38::LinearWeights> linear;
-    void *proj_q8k = nullptr;       // Q8_K activations of the projections (q38proj.cu)
-    size_t proj_q8k_bytes = 0;
 };
 
 struct q38_state {

@@ -33,7 +33,8 @@ size_t proj_padded_bytes(int type, int64_t rows, int64_t width);
 
 cudaError_t launch_q8k_quantize(const float *x, int batch, int width, Q8KActivations act, void *aos,
                                 cudaStream_t stream);
-cudaError_t launch_proj_q8k(const ProjWeight &w, const Q8KActivations &act, int batch, float *out,
+// Quantizes x [batch][width] to Q8_K inside the kernel (no separate pass).
+cudaError_t launch_proj_q8k(const ProjWeight &w, const float *x, int batch, float *out,
                             long out_ld, int *err, int sm_count, cudaStream_t stream);
 cudaError_t launch_proj_f32(const ProjWeight &w, const float *x, int batch, float *out, long out_ld,
                             cudaStream_t stream);

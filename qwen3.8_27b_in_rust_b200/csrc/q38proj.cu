@@ -37,76 +37,24 @@ struct Guard {
     }
 };
 
-size_t q8k_bytes(int batch, int64_t width) {
-    const size_t nb = size_t(batch) * size_t(width / 256);
-    return nb * 256 + nb * 4 + nb * 32;
-}
-
-q38::Q8KActivations q8k_view(void *base, int batch, int64_t width) {
-    const size_t nb = size_t(batch) * size_t(width / 256);
-    unsigned char *p = static_cast<unsigned char *>(base);
-    q38::Q8KActivations a;
-    a.quants = reinterpret_cast<int8_t *>(p);
-    a.scale = reinterpret_cast<float *>(p + nb * 256);
-    a.sums = reinterpret_cast<int16_t *>(p + nb * 256 + nb * 4);
-    return a;
-}
-
-int reserve(q38_ctx *ctx, int batch, int64_t width) {
-    const size_t need = q8k_bytes(batch, width);
-    if (need <= ctx->proj_q8k_bytes) return Q38_OK;
-    if (ctx->proj_q8k) {
-        // Earlier launches on any stream may still read the old buffer.
-        cudaError_t e = cudaDeviceSynchronize();
-        if (e != cudaSuccess) return proj_cuda_fail(e, "projection scratch resize");
-        cudaFree(ctx->proj_q8k);
-        ctx->proj_q8k = nullptr;
-        ctx->proj_q8k_bytes = 0;
-    }
-    cudaError_t e = cudaMalloc(&ctx->proj_q8k, need);
-    if (e != cudaSuccess) return proj_cuda_fail(e, "projection scratch allocation");
-    ctx->proj_q8k_bytes = need;
-    return Q38_OK;
-}
-
 int check_weight(const q38_ctx *ctx, const q38_weight *w, const char *what) {
     if (!w) return proj_fail(Q38_ERR_ARG, "null %s weight", what);
     if (w->ctx != ctx) return proj_fail(Q38_ERR_ARG, "%s weight belongs to another context", what);
     return Q38_OK;
 }
 
-// Quantizes `input` (when any of the weights takes the integer path) into
-// the context scratch. The input is [batch][width], 16-byte aligned.
-int quantize_for(q38_ctx *ctx, int batch, int64_t width, const float *input, cudaStream_t s) {
-    if (width % 256) return proj_fail(Q38_ERR_ARG, "input length %lld is not a multiple of 256",
-                                      static_cast<long long>(width));
+// One projection; K-quant weights quantize the input inside the GEMV.
+int project_device(q38_ctx *ctx, const q38_weight *w, int batch, const float *input, float *out,
+                   int *err, cudaStream_t s) {
     if (reinterpret_cast<uintptr_t>(input) % 16)
         return proj_fail(Q38_ERR_ARG, "projection input must be 16-byte aligned");
-    if (int rc = reserve(ctx, batch, width)) return rc;
-    cudaError_t e = q38::launch_q8k_quantize(input, batch, int(width), q8k_view(ctx->proj_q8k, batch, width),
-                                             nullptr, s);
-    if (e != cudaSuccess) return proj_cuda_fail(e, "Q8_K quantize launch");
-    return Q38_OK;
-}
-
-// One projection whose Q8_K input (if needed) is already in the scratch.
-int project_quantized(q38_ctx *ctx, const q38_weight *w, int batch, const float *input, float *out,
-                      int *err, cudaStream_t s) {
     cudaError_t e;
     if (q38::proj_is_q8k_type(w->w.type))
-        e = q38::launch_proj_q8k(w->w, q8k_view(ctx->proj_q8k, batch, w->w.width), batch, out,
-                                 long(w->w.rows), err, ctx->sm_count, s);
+        e = q38::launch_proj_q8k(w->w, input, batch, out, long(w->w.rows), err, ctx->sm_count, s);
     else
         e = q38::launch_proj_f32(w->w, input, batch, out, long(w->w.rows), s);
     if (e != cudaSuccess) return proj_cuda_fail(e, "projection launch");
     return Q38_OK;
-}
-
-int project_device(q38_ctx *ctx, const q38_weight *w, int batch, const float *input, float *out,
-                   int *err, cudaStream_t s) {
-    if (q38::proj_is_q8k_type(w->w.type))
-        if (int rc = quantize_for(ctx, batch, w->w.width, input, s)) return rc;
-    return project_quantized(ctx, w, batch, input, out, err, s);
 }
 
 }  // namespace
@@ -126,6 +74,9 @@ int q38_weight_create(q38_ctx *ctx, int ggml_type, int64_t width, int64_t rows, 
                          static_cast<long long>(rows), static_cast<long long>(width));
     if (q38::proj_is_q8k_type(ggml_type) && width % 256)
         return proj_fail(Q38_ERR_ARG, "K-quant rows must be whole 256-blocks");
+    if (width % 4 || width > 32768)
+        return proj_fail(Q38_ERR_ARG, "projection width %lld must be a multiple of 4 up to 32768",
+                         static_cast<long long>(width));
     if (nbytes != size_t(rows * rb))
         return proj_fail(Q38_ERR_ARG, "weight holds %zu bytes, expected %lld", nbytes,
                          static_cast<long long>(rows * rb));
@@ -174,11 +125,10 @@ int q38_weight_info(const q38_weight *w, int *ggml_type, int64_t *width, int64_t
 
 int q38_ctx_reserve_projection(q38_ctx *ctx, int batch, int64_t width) {
     if (!ctx) return proj_fail(Q38_ERR_ARG, "null context");
-    if (batch <= 0 || width <= 0 || width % 256)
+    if (batch <= 0 || width <= 0 || width % 4)
         return proj_fail(Q38_ERR_ARG, "bad projection reservation (%d x %lld)", batch,
                          static_cast<long long>(width));
-    Guard guard(ctx->device);
-    return reserve(ctx, batch, width);
+    return Q38_OK;  // the projections quantize in shared memory: nothing to allocate
 }
 
 int q38_quantize_q8_k(q38_ctx *ctx, int batch, int64_t width, const float *input, void *blocks,
@@ -245,16 +195,12 @@ int q38_linear_attention_decode(q38_ctx *ctx, q38_state *st, int layer, int batc
     float *qkv = st->proj_stage, *z = qkv + size_t(batch) * ctx->qkv_dim;
     float *beta = z + size_t(batch) * ctx->v_dim, *alpha = beta + size_t(batch) * vh;
     float *att = alpha + size_t(batch) * vh;
-    // linear_attention, ops.rs:761-801: one quantization of the normalised
-    // input shared by the four projections.
+    // linear_attention, ops.rs:761-801: the four input projections (each
+    // quantizes the normalised input itself), the core, the output projection.
     const q38_weight *ins[4] = {w->qkv, w->z, w->beta, w->alpha};
     float *outs[4] = {qkv, z, beta, alpha};
-    bool any_q8k = false;
-    for (const q38_weight *p : ins) any_q8k |= q38::proj_is_q8k_type(p->w.type);
-    if (any_q8k)
-        if (int rc = quantize_for(ctx, batch, hidden, norm, s)) return rc;
     for (int i = 0; i < 4; ++i)
-        if (int rc = project_quantized(ctx, ins[i], batch, norm, outs[i], st->d_err, s)) return rc;
+        if (int rc = project_device(ctx, ins[i], batch, norm, outs[i], st->d_err, s)) return rc;
     if (int rc = q38_linear_decode(ctx, st, layer, batch, qkv, z, beta, alpha, att, stream)) return rc;
     return project_device(ctx, w->out, batch, att, branch, st->d_err, s);
 }
@@ -282,12 +228,8 @@ int q38_full_attention_decode(q38_ctx *ctx, q38_state *st, int layer, int batch,
     // full_attention, ops.rs:954-980.
     const q38_weight *ins[3] = {w->q, w->k, w->v};
     float *outs[3] = {qg, key, value};
-    bool any_q8k = false;
-    for (const q38_weight *p : ins) any_q8k |= q38::proj_is_q8k_type(p->w.type);
-    if (any_q8k)
-        if (int rc = quantize_for(ctx, batch, hidden, norm, s)) return rc;
     for (int i = 0; i < 3; ++i)
-        if (int rc = project_quantized(ctx, ins[i], batch, norm, outs[i], st->d_err, s)) return rc;
+        if (int rc = project_device(ctx, ins[i], batch, norm, outs[i], st->d_err, s)) return rc;
     if (int rc = q38_full_decode(ctx, st, layer, batch, qg, key, value, positions, max_position, att,
                                  stream))
         return rc;
