@@ -413,19 +413,22 @@ int q38_quantize_q8_k(q38_ctx *ctx, int batch, int64_t width, const float *input
  * gemm_rows writes it (tensor.rs:978-1000). K-quant weights: the input is
  * quantized to Q8_K on the device and each output is bit-identical to the
  * reference's scalar integer dot. F32/F16/BF16/Q8_0: f32 dot, equal to the
- * reference's within rounding. The Q8_K quantization runs inside the GEMV
- * (each CTA quantizes the tokens into shared memory), so nothing is
- * allocated; input must be 16-byte aligned. Launched as a programmatic
- * dependent of the previous kernel on the stream: the first weight tiles are
- * fetched while that kernel finishes. */
+ * reference's within rounding. Up to 8 tokens the Q8_K quantization runs
+ * inside the GEMV; 9 or more tokens over Q4_K / Q5_K weights run on the
+ * tensor cores, with the quantized input in a context scratch buffer that
+ * grows on first use (q38_ctx_reserve_projection sizes it ahead, so that
+ * later calls allocate nothing). Input must be 16-byte aligned. Launched as
+ * a programmatic dependent of the previous kernel on the stream: the first
+ * weight tiles are fetched while that kernel finishes. */
 int q38_project(q38_ctx *ctx, const q38_weight *w, int batch, const float *input, float *output,
                 void *stream);
 /* Host-pointer form (synchronous). */
 int q38_project_host(q38_ctx *ctx, const q38_weight *w, int batch, const float *input,
                      float *output);
-/* Checks a projection shape ahead of use. The projections need no scratch
- * (the quantized input lives in shared memory), so this allocates nothing;
- * kept so a host can validate its batch and width once at start-up. */
+/* Sizes the context's projection scratch (the quantized input of the
+ * tensor-core path) for `batch` tokens of `width` inputs (a multiple of 256),
+ * so that later q38_project / *_attention_decode calls allocate nothing.
+ * Call it before any stream capture. */
 int q38_ctx_reserve_projection(q38_ctx *ctx, int batch, int64_t width);
 
 /* The projections of one Gated DeltaNet layer (Q38Attention::Linear,

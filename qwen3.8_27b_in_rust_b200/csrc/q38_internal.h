@@ -51,6 +51,8 @@ struct q38_ctx {
     int qk_dim = 0, v_dim = 0, qkv_dim = 0;
     std::map<int, q38::FullWeights> full;
     std::map<int, q38::LinearWeights> linear;
+    void *proj_scratch = nullptr;   // quantized activations of the tensor-core projections
+    size_t proj_scratch_bytes = 0;
 };
 
 struct q38_state {

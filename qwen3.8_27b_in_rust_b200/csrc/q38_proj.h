@@ -36,6 +36,15 @@ cudaError_t launch_q8k_quantize(const float *x, int batch, int width, Q8KActivat
 // Quantizes x [batch][width] to Q8_K inside the kernel (no separate pass).
 cudaError_t launch_proj_q8k(const ProjWeight &w, const float *x, int batch, float *out,
                             long out_ld, int *err, int sm_count, cudaStream_t stream);
+// Tensor-core path for Q4_K / Q5_K weights and kProjMmaMinBatch+ tokens
+// (proj_mma.cu): quantizes x into `scratch` (proj_mma_scratch_bytes), then
+// one tcgen05 kind::i8 GEMM, bit-identical to the integer GEMV.
+constexpr int kProjMmaMinBatch = 9;
+bool proj_mma_supported(int type);
+size_t proj_mma_scratch_bytes(int batch, int64_t width);
+cudaError_t launch_proj_mma(const ProjWeight &w, const float *x, int batch, float *out, long out_ld,
+                            int *err, void *scratch, cudaStream_t stream);
+
 cudaError_t launch_proj_f32(const ProjWeight &w, const float *x, int batch, float *out, long out_ld,
                             cudaStream_t stream);
 

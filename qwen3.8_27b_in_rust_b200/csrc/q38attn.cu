@@ -316,6 +316,7 @@ int q38_ctx_destroy(q38_ctx *ctx) {
         DeviceGuard guard(ctx->device);
         for (auto &kv : ctx->full) free_full(kv.second);
         for (auto &kv : ctx->linear) free_linear(kv.second);
+        cudaFree(ctx->proj_scratch);
     }
     delete ctx;
     return Q38_OK;

@@ -43,13 +43,37 @@ int check_weight(const q38_ctx *ctx, const q38_weight *w, const char *what) {
     return Q38_OK;
 }
 
-// One projection; K-quant weights quantize the input inside the GEMV.
+// Grows the context's scratch for the tensor-core path's quantized input.
+int reserve_scratch(q38_ctx *ctx, int batch, int64_t width) {
+    const size_t need = q38::proj_mma_scratch_bytes(batch, width);
+    if (need <= ctx->proj_scratch_bytes) return Q38_OK;
+    if (ctx->proj_scratch) {
+        // Earlier launches on any stream may still read the old buffer.
+        cudaError_t e = cudaDeviceSynchronize();
+        if (e != cudaSuccess) return proj_cuda_fail(e, "projection scratch resize");
+        cudaFree(ctx->proj_scratch);
+        ctx->proj_scratch = nullptr;
+        ctx->proj_scratch_bytes = 0;
+    }
+    cudaError_t e = cudaMalloc(&ctx->proj_scratch, need);
+    if (e != cudaSuccess) return proj_cuda_fail(e, "projection scratch allocation");
+    ctx->proj_scratch_bytes = need;
+    return Q38_OK;
+}
+
+// One projection. K-quant weights: a batch of kProjMmaMinBatch or more tokens
+// over Q4_K / Q5_K runs on the tensor cores (the input quantized into the
+// context's scratch first); otherwise the integer GEMV quantizes the input
+// inside its prologue.
 int project_device(q38_ctx *ctx, const q38_weight *w, int batch, const float *input, float *out,
                    int *err, cudaStream_t s) {
     if (reinterpret_cast<uintptr_t>(input) % 16)
         return proj_fail(Q38_ERR_ARG, "projection input must be 16-byte aligned");
     cudaError_t e;
-    if (q38::proj_is_q8k_type(w->w.type))
+    if (batch >= q38::kProjMmaMinBatch && q38::proj_mma_supported(w->w.type) && w->w.row_bytes % 16 == 0) {
+        if (int rc = reserve_scratch(ctx, batch, w->w.width)) return rc;
+        e = q38::launch_proj_mma(w->w, input, batch, out, long(w->w.rows), err, ctx->proj_scratch, s);
+    } else if (q38::proj_is_q8k_type(w->w.type))
         e = q38::launch_proj_q8k(w->w, input, batch, out, long(w->w.rows), err, ctx->sm_count, s);
     else
         e = q38::launch_proj_f32(w->w, input, batch, out, long(w->w.rows), s);
@@ -125,10 +149,11 @@ int q38_weight_info(const q38_weight *w, int *ggml_type, int64_t *width, int64_t
 
 int q38_ctx_reserve_projection(q38_ctx *ctx, int batch, int64_t width) {
     if (!ctx) return proj_fail(Q38_ERR_ARG, "null context");
-    if (batch <= 0 || width <= 0 || width % 4)
+    if (batch <= 0 || width <= 0 || width % 256)
         return proj_fail(Q38_ERR_ARG, "bad projection reservation (%d x %lld)", batch,
                          static_cast<long long>(width));
-    return Q38_OK;  // the projections quantize in shared memory: nothing to allocate
+    Guard guard(ctx->device);
+    return reserve_scratch(ctx, batch, width);
 }
 
 int q38_quantize_q8_k(q38_ctx *ctx, int batch, int64_t width, const float *input, void *blocks,

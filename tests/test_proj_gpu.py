@@ -67,7 +67,9 @@ def test_project_k_quants_bitwise(cuda_ctx, oracle_lib, ggml_type, rows, width):
     g = synth.rng(100 + ggml_type + rows)
     data = synth.quant_weight(g, ggml_type, rows, width)
     w = cuda_ctx.weight(ggml_type, width, rows, data)
-    for batch in (1, 3, 11):
+    # 9 or more tokens over Q4_K / Q5_K take the tensor-core path (one or
+    # two 32-token tiles here); fewer, or other types, the integer GEMV.
+    for batch in (1, 3, 11, 40):
         x = synth.normal(g, (batch, width))
         got = _gpu_project(cuda_ctx, w, x)
         want = oracle_lib.project(ggml_type, data, rows, width, x)
