@@ -330,7 +330,7 @@ template <> constexpr int kBlockBytes<Q38_GGML_Q2_K> = 84;
 template <> constexpr int kBlockBytes<Q38_GGML_Q3_K> = 110;
 template <> constexpr int kBlockBytes<Q38_GGML_Q4_K> = 144;
 template <> constexpr int kBlockBytes<Q38_GGML_Q5_K> = 176;
-template <> constexpr int kBlockBytes<Q38_GGML_Q6_K> = 210;
+template <> constexpr int kBlockBytes<Q38_GGML_Q6_K> = kQ6KDeviceBlock;  // padded on upload
 
 // ---------------------------------------------------------------------------
 // Q8_K quantization, one warp per 256-value block (quant.rs:56-96).
@@ -444,7 +444,8 @@ struct ProjQ8KParams {
     int *err;
     long out_ld;
     int rows, nblk, rb, batch, ntiles, stages;
-    uint32_t tile_bytes;   // kProjTileRows * rb (a multiple of 16)
+    int tile_rows;         // 16, or 8 for wide rows (a tile is one contiguous byte range)
+    uint32_t tile_bytes;   // tile_rows * rb (a multiple of 16: rb is even)
 };
 
 // Shared-memory plan: the weight ring, the activations, and one combine
@@ -495,7 +496,7 @@ __global__ void __launch_bounds__(kProjQ8KThreads, 1) proj_q8k_kernel(ProjQ8KPar
         for (int k = 0; k < first; ++k) {
             mbar_arrive_expect_tx(&full[k], p.tile_bytes);
             bulk_load(smem + k * p.tile_bytes,
-                      p.w + size_t(blockIdx.x + k * gridDim.x) * kProjTileRows * p.rb, p.tile_bytes, &full[k]);
+                      p.w + size_t(blockIdx.x + k * gridDim.x) * p.tile_rows * p.rb, p.tile_bytes, &full[k]);
         }
     pdl_wait_primary();
     pdl_launch_dependents();
@@ -522,7 +523,7 @@ __global__ void __launch_bounds__(kProjQ8KThreads, 1) proj_q8k_kernel(ProjQ8KPar
                 }
                 if (abort_flag) break;
                 mbar_arrive_expect_tx(&full[s], p.tile_bytes);
-                bulk_load(smem + s * p.tile_bytes, p.w + size_t(tile) * kProjTileRows * p.rb, p.tile_bytes,
+                bulk_load(smem + s * p.tile_bytes, p.w + size_t(tile) * p.tile_rows * p.rb, p.tile_bytes,
                           &full[s]);
             }
             // Every issued copy lands before the CTA exits: the last use of
@@ -548,8 +549,8 @@ __global__ void __launch_bounds__(kProjQ8KThreads, 1) proj_q8k_kernel(ProjQ8KPar
         }
         const uint8_t *tw = smem + s * p.tile_bytes;
 #pragma unroll 1
-        for (int r = warp; r < kProjTileRows; r += kProjConsumerWarps) {
-            const int row = tile * kProjTileRows + r;
+        for (int r = warp; r < p.tile_rows; r += kProjConsumerWarps) {
+            const int row = tile * p.tile_rows + r;
             if (row >= p.rows) break;  // rows ascend with r
             for (int b = lane; b < p.nblk; b += 32) {
                 typename BlockOf<T>::type blk;
@@ -581,6 +582,7 @@ struct ProjF32Params {
     float *out;
     long out_ld;
     int rows, width, rb, batch;
+    int per;         // tokens per CTA (grid.y covers the batch)
     int split;       // warps per row: 1 (eight rows per CTA) or 8 (one row per CTA)
 };
 
@@ -619,10 +621,14 @@ __global__ void __launch_bounds__(256) proj_f32_kernel(ProjF32Params p) {
     extern __shared__ __align__(16) float xs[];
     __shared__ float part[8][kProjMaxTok];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    // blockIdx.y: this CTA's group of up to p.per tokens.
+    const int t0 = blockIdx.y * p.per, nt = min(p.per, p.batch - t0);
+    const float *xg = p.x + size_t(t0) * p.width;
+    float *outg = p.out + size_t(t0) * p.out_ld;
     pdl_wait_primary();  // x comes from an earlier kernel in the stream
     pdl_launch_dependents();
-    for (int i = threadIdx.x; i < p.batch * p.width / 4; i += 256)
-        reinterpret_cast<float4 *>(xs)[i] = reinterpret_cast<const float4 *>(p.x)[i];
+    for (int i = threadIdx.x; i < nt * p.width / 4; i += 256)
+        reinterpret_cast<float4 *>(xs)[i] = reinterpret_cast<const float4 *>(xg)[i];
     __syncthreads();
     const int row = p.split == 1 ? blockIdx.x * 8 + warp : blockIdx.x;
     const int len = p.width / p.split;
@@ -638,7 +644,7 @@ __global__ void __launch_bounds__(256) proj_f32_kernel(ProjF32Params p) {
             weights4<T>(w, i, wv);
 #pragma unroll
             for (int t = 0; t < kProjMaxTok; ++t)
-                if (t < p.batch) {
+                if (t < nt) {
                     const float4 x = *reinterpret_cast<const float4 *>(xs + t * p.width + i);
                     acc[t] = fmaf(wv[3], x.w, fmaf(wv[2], x.z, fmaf(wv[1], x.y, fmaf(wv[0], x.x, acc[t]))));
                 }
@@ -653,17 +659,17 @@ __global__ void __launch_bounds__(256) proj_f32_kernel(ProjF32Params p) {
     }
     if (p.split == 1) {
         if (lane == 0 && row < p.rows)
-            for (int t = 0; t < p.batch; ++t) p.out[size_t(t) * p.out_ld + row] = acc[t];
+            for (int t = 0; t < nt; ++t) outg[size_t(t) * p.out_ld + row] = acc[t];
         return;
     }
     if (lane == 0)
 #pragma unroll
         for (int t = 0; t < kProjMaxTok; ++t) part[warp][t] = acc[t];
     __syncthreads();
-    if (threadIdx.x < p.batch && row < p.rows) {
+    if (threadIdx.x < nt && row < p.rows) {
         float v = 0.f;
         for (int k = 0; k < 8; ++k) v += part[k][threadIdx.x];
-        p.out[size_t(threadIdx.x) * p.out_ld + row] = v;
+        outg[size_t(threadIdx.x) * p.out_ld + row] = v;
     }
 }
 
@@ -709,13 +715,13 @@ cudaError_t launch_f32(const ProjF32Params &p, cudaStream_t stream) {
         if (e != cudaSuccess) return e;
         if (dev < kMaxDevices) attr_set[dev] = true;
     }
-    const size_t smem = size_t(p.batch) * p.width * sizeof(float);
+    const size_t smem = size_t(p.per) * p.width * sizeof(float);
     if (smem > kProjSmemBudget) return cudaErrorInvalidValue;
     cudaLaunchConfig_t cfg{};
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.gridDim = dim3(p.split == 1 ? (p.rows + 7) / 8 : p.rows);
+    cfg.gridDim = dim3(p.split == 1 ? (p.rows + 7) / 8 : p.rows, (p.batch + p.per - 1) / p.per);
     cfg.blockDim = dim3(256);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
@@ -754,8 +760,13 @@ int64_t proj_row_bytes(int type, int64_t width) {
     return width / el * by;
 }
 
+int64_t proj_device_row_bytes(int type, int64_t width) {
+    if (type == Q38_GGML_Q6_K && width > 0 && width % 256 == 0) return width / 256 * kQ6KDeviceBlock;
+    return proj_row_bytes(type, width);
+}
+
 size_t proj_padded_bytes(int type, int64_t rows, int64_t width) {
-    const int64_t rb = proj_row_bytes(type, width);
+    const int64_t rb = proj_device_row_bytes(type, width);
     return size_t((rows + kProjMaxTileRows) * rb) + 16;
 }
 
@@ -778,10 +789,19 @@ cudaError_t launch_proj_q8k(const ProjWeight &w, const float *x, int batch, floa
     p.rows = int(w.rows);
     p.nblk = nblk;
     p.rb = rb;
-    p.ntiles = int((w.rows + kProjTileRows - 1) / kProjTileRows);
-    p.tile_bytes = uint32_t(kProjTileRows * rb);  // 16 rows: a multiple of 16 bytes
-    for (int t0 = 0; t0 < batch; t0 += kProjMaxTok) {
-        p.batch = std::min(kProjMaxTok, batch - t0);
+    // 16-row tiles, or 8 when three stages of 16 rows would not fit beside
+    // one token's activations (so the copies stay ahead of the compute).
+    p.tile_rows = kProjTileRows;
+    if (proj_smem_plan(0, 16u * rb, 1, nblk).total + 3u * 16u * rb > kProjSmemBudget) p.tile_rows = 8;
+    p.ntiles = int((w.rows + p.tile_rows - 1) / p.tile_rows);
+    p.tile_bytes = uint32_t(p.tile_rows * rb);
+    // Tokens per launch: up to kProjMaxTok, fewer when the activations would
+    // leave room for less than two weight stages (wide Q6_K rows).
+    int per = kProjMaxTok;
+    while (per > 1 && proj_smem_plan(0, p.tile_bytes, per, nblk).total + 2 * p.tile_bytes > kProjSmemBudget)
+        --per;
+    for (int t0 = 0; t0 < batch; t0 += per) {
+        p.batch = std::min(per, batch - t0);
         p.x = x + size_t(t0) * nblk * 256;
         p.out = out + size_t(t0) * out_ld;
         // Stages: as many as the budget allows, up to 4.
@@ -817,21 +837,17 @@ cudaError_t launch_proj_f32(const ProjWeight &w, const float *x, int batch, floa
     // Tokens per launch: as many as fit the shared-memory budget, up to 8.
     const int per = std::min<int64_t>(kProjMaxTok, kProjSmemBudget / (w.width * sizeof(float)));
     if (per < 1 || w.width % 4) return cudaErrorInvalidValue;
-    for (int t0 = 0; t0 < batch; t0 += per) {
-        p.batch = std::min(per, batch - t0);
-        p.x = x + size_t(t0) * w.width;
-        p.out = out + size_t(t0) * out_ld;
-        cudaError_t e;
-        switch (w.type) {
-            case Q38_GGML_F32: e = launch_f32<Q38_GGML_F32>(p, stream); break;
-            case Q38_GGML_F16: e = launch_f32<Q38_GGML_F16>(p, stream); break;
-            case Q38_GGML_BF16: e = launch_f32<Q38_GGML_BF16>(p, stream); break;
-            case Q38_GGML_Q8_0: e = launch_f32<Q38_GGML_Q8_0>(p, stream); break;
-            default: return cudaErrorInvalidValue;
-        }
-        if (e != cudaSuccess) return e;
+    p.batch = batch;
+    p.per = per;
+    p.x = x;
+    p.out = out;
+    switch (w.type) {
+        case Q38_GGML_F32: return launch_f32<Q38_GGML_F32>(p, stream);
+        case Q38_GGML_F16: return launch_f32<Q38_GGML_F16>(p, stream);
+        case Q38_GGML_BF16: return launch_f32<Q38_GGML_BF16>(p, stream);
+        case Q38_GGML_Q8_0: return launch_f32<Q38_GGML_Q8_0>(p, stream);
+        default: return cudaErrorInvalidValue;
     }
-    return cudaSuccess;
 }
 
 }  // namespace q38

@@ -22,13 +22,18 @@ struct Q8KActivations {
 // each row one output over `width` inputs (shape [width, rows]).
 struct ProjWeight {
     int type = -1;
-    int64_t rows = 0, width = 0, row_bytes = 0;
+    int64_t rows = 0, width = 0, row_bytes = 0;  // row_bytes: device layout
     void *data = nullptr;  // device, proj_padded_bytes long
 };
 
 bool proj_is_q8k_type(int type);
 bool proj_type_supported(int type);
-int64_t proj_row_bytes(int type, int64_t width);  // -1: type cannot hold such rows
+// Q6_K blocks are 210 bytes in the checkpoint; on the device each is padded
+// to 224 (14 x 16) so that every block starts 16-byte aligned and a tile of
+// blocks is a valid TMA box. The other types keep their checkpoint layout.
+constexpr int kQ6KDeviceBlock = 224;
+int64_t proj_row_bytes(int type, int64_t width);         // checkpoint row bytes; -1: type cannot hold such rows
+int64_t proj_device_row_bytes(int type, int64_t width);  // device row bytes
 size_t proj_padded_bytes(int type, int64_t rows, int64_t width);
 
 cudaError_t launch_q8k_quantize(const float *x, int batch, int width, Q8KActivations act, void *aos,

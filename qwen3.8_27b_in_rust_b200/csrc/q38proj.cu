@@ -6,6 +6,7 @@
 #include <cstdio>
 #include <cstring>
 #include <new>
+#include <vector>
 
 #include "q38_proj.h"
 
@@ -106,10 +107,21 @@ int q38_weight_create(q38_ctx *ctx, int ggml_type, int64_t width, int64_t rows, 
                          static_cast<long long>(rows * rb));
     Guard guard(ctx->device);
     const size_t padded = q38::proj_padded_bytes(ggml_type, rows, width);
+    const int64_t drb = q38::proj_device_row_bytes(ggml_type, width);
     void *dev = nullptr;
     cudaError_t e = cudaMalloc(&dev, padded);
     if (e == cudaSuccess) e = cudaMemset(dev, 0, padded);
-    if (e == cudaSuccess) e = cudaMemcpy(dev, data, nbytes, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess && drb == rb) {
+        e = cudaMemcpy(dev, data, nbytes, cudaMemcpyHostToDevice);
+    } else if (e == cudaSuccess) {
+        // Q6_K: each 210-byte block into a 224-byte slot (the padding stays zero).
+        const size_t nblocks = size_t(rows) * size_t(width / 256);
+        std::vector<unsigned char> staged(nblocks * q38::kQ6KDeviceBlock, 0);
+        const unsigned char *src = static_cast<const unsigned char *>(data);
+        for (size_t i = 0; i < nblocks; ++i)
+            std::memcpy(staged.data() + i * q38::kQ6KDeviceBlock, src + i * 210, 210);
+        e = cudaMemcpy(dev, staged.data(), staged.size(), cudaMemcpyHostToDevice);
+    }
     if (e != cudaSuccess) {
         cudaFree(dev);
         return proj_cuda_fail(e, "weight upload");
@@ -123,7 +135,7 @@ int q38_weight_create(q38_ctx *ctx, int ggml_type, int64_t width, int64_t rows, 
     w->w.type = ggml_type;
     w->w.rows = rows;
     w->w.width = width;
-    w->w.row_bytes = rb;
+    w->w.row_bytes = drb;
     w->w.data = dev;
     *out = w;
     return Q38_OK;
