@@ -269,7 +269,8 @@ def run_projection(args, ctx, q38attn, synth, torch, rank: int) -> dict:
         peak, _ = load_peaks()
         gbs = per_layer / (ms * 1e-3) / 1e9
         out[f"batch{B}"] = {"ms_per_layer": ms, "weight_gbs": gbs, "frac": gbs / peak,
-                            "launches_per_layer": 7 * ((B + 7) // 8)}
+                            "path": ("tcgen05 kind::i8 (K-quants), f32 GEMV (Q8_0 gates)" if B >= 9
+                                     else "dp4a integer GEMV (K-quants), f32 GEMV (Q8_0 gates)")}
         del graph
     for d in layers:
         for w in d.values():
