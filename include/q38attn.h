@@ -461,6 +461,29 @@ int q38_full_attention_decode(q38_ctx *ctx, q38_state *st, int layer, int batch,
                               const int32_t *positions, int max_position, float *branch,
                               void *stream);
 
+/* Sizes, for up to max_tokens prompt tokens per call (summed over its
+ * sequences), everything the two calls below use: the core prefill scratch
+ * (as q38_state_reserve_prefill), the projections' outputs and the context's
+ * projection scratch (~90 KB per token). Allocates; call it once at set-up. */
+int q38_state_reserve_attention_prefill(q38_state *st, int max_tokens);
+
+/* batch_linear_attention (src/model/ops.rs:1032-1114) for sequences
+ * [seq0, seq0 + nseq) of `count` tokens each: norm [nseq][count][hidden]
+ * DEVICE (the attn_norm output), branch [nseq][count][hidden] DEVICE out. The
+ * four input projections over all nseq*count tokens (tensor cores from 9
+ * tokens on), the chunked core on the resident state (as q38_linear_prefill),
+ * the output projection. */
+int q38_linear_attention_prefill(q38_ctx *ctx, q38_state *st, int layer, int seq0, int nseq, int count,
+                                 const q38_linear_projections *w, const float *norm, float *branch,
+                                 void *stream);
+
+/* batch_full_attention (src/model/ops.rs:1116-1185): positions base_position
+ * .. base_position+count-1 of each sequence, as q38_full_prefill (bf16 KV
+ * state). */
+int q38_full_attention_prefill(q38_ctx *ctx, q38_state *st, int layer, int seq0, int nseq, int count,
+                               int base_position, const q38_full_projections *w, const float *norm,
+                               float *branch, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -84,6 +84,9 @@ struct q38_state {
     size_t stage_floats = 0;
     // projection outputs / core inputs of the layer-level decode calls
     float *proj_stage = nullptr;    // stage_floats
+    // the same for the layer-level prefill calls (q38_state_reserve_attention_prefill)
+    float *layer_prefill = nullptr;
+    size_t layer_prefill_tokens = 0;
     int32_t *stage_pos = nullptr;
 };
 

@@ -163,6 +163,7 @@ void free_state(q38_state *st) {
     cudaFree(st->d_err);
     cudaFree(st->stage);
     cudaFree(st->proj_stage);
+    cudaFree(st->layer_prefill);
     cudaFree(st->stage_pos);
     cudaFree(st->prefill_rope);
     cudaFree(st->prefill_v16);

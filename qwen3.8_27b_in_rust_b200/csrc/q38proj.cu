@@ -273,4 +273,102 @@ int q38_full_attention_decode(q38_ctx *ctx, q38_state *st, int layer, int batch,
     return project_device(ctx, w->out, batch, att, branch, st->d_err, s);
 }
 
+// ---------------------------------------------------------------- prefill layer bodies
+
+namespace {
+size_t layer_prefill_floats_per_token(const q38_ctx *ctx) {
+    const size_t lin = size_t(ctx->qkv_dim) + ctx->v_dim + 2 * ctx->geom.linear_v_heads + ctx->v_dim;
+    const size_t full = size_t(ctx->qg_dim) + 2 * ctx->kv_dim + ctx->q_dim;
+    return lin > full ? lin : full;
+}
+
+int check_prefill_layer(q38_ctx *ctx, q38_state *st, int seq0, int nseq, int count, const void *w,
+                        const float *norm, float *branch) {
+    if (!ctx || !st || !w || !norm || !branch) return proj_fail(Q38_ERR_ARG, "null argument");
+    if (st->ctx != ctx) return proj_fail(Q38_ERR_ARG, "state belongs to another context");
+    if (nseq <= 0 || count <= 0 || seq0 < 0 || seq0 + nseq > st->batch)
+        return proj_fail(Q38_ERR_ARG, "sequences [%d, %d) outside the state's %d", seq0, seq0 + nseq, st->batch);
+    if (size_t(nseq) * size_t(count) > st->layer_prefill_tokens)
+        return proj_fail(Q38_ERR_ARG, "%d prompt tokens exceed q38_state_reserve_attention_prefill's %zu",
+                         nseq * count, st->layer_prefill_tokens);
+    return Q38_OK;
+}
+}  // namespace
+
+int q38_state_reserve_attention_prefill(q38_state *st, int max_tokens) {
+    if (!st) return proj_fail(Q38_ERR_ARG, "null state");
+    if (max_tokens <= 0) return proj_fail(Q38_ERR_ARG, "max_tokens must be positive");
+    if (int rc = q38_state_reserve_prefill(st, max_tokens)) return rc;
+    q38_ctx *ctx = st->ctx;
+    Guard guard(ctx->device);
+    const int64_t widest = ctx->v_dim > ctx->q_dim ? ctx->v_dim : ctx->q_dim;
+    if (int rc = reserve_scratch(ctx, max_tokens, widest > 5120 ? widest : 5120)) return rc;
+    if (size_t(max_tokens) <= st->layer_prefill_tokens) return Q38_OK;
+    cudaFree(st->layer_prefill);
+    st->layer_prefill = nullptr;
+    st->layer_prefill_tokens = 0;
+    cudaError_t e = cudaMalloc(&st->layer_prefill,
+                               size_t(max_tokens) * layer_prefill_floats_per_token(ctx) * sizeof(float));
+    if (e != cudaSuccess) return proj_cuda_fail(e, "attention prefill buffers");
+    st->layer_prefill_tokens = size_t(max_tokens);
+    return Q38_OK;
+}
+
+int q38_linear_attention_prefill(q38_ctx *ctx, q38_state *st, int layer, int seq0, int nseq, int count,
+                                 const q38_linear_projections *w, const float *norm, float *branch,
+                                 void *stream) {
+    if (int rc = check_prefill_layer(ctx, st, seq0, nseq, count, w, norm, branch)) return rc;
+    for (auto [p, name] : {std::pair<const q38_weight *, const char *>{w->qkv, "qkv"}, {w->z, "z"},
+                           {w->beta, "beta"}, {w->alpha, "alpha"}, {w->out, "out"}})
+        if (int rc = check_weight(ctx, p, name)) return rc;
+    const int64_t hidden = w->qkv->w.width;
+    const int vh = ctx->geom.linear_v_heads;
+    if (w->z->w.width != hidden || w->beta->w.width != hidden || w->alpha->w.width != hidden ||
+        w->out->w.rows != hidden || w->qkv->w.rows != ctx->qkv_dim || w->z->w.rows != ctx->v_dim ||
+        w->beta->w.rows != vh || w->alpha->w.rows != vh || w->out->w.width != ctx->v_dim)
+        return proj_fail(Q38_ERR_ARG, "DeltaNet projection shapes do not match the geometry");
+    Guard guard(ctx->device);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const int tokens = nseq * count;
+    float *qkv = st->layer_prefill, *z = qkv + size_t(tokens) * ctx->qkv_dim;
+    float *beta = z + size_t(tokens) * ctx->v_dim, *alpha = beta + size_t(tokens) * vh;
+    float *att = alpha + size_t(tokens) * vh;
+    // batch_linear_attention, ops.rs:1032-1114: the projections of every
+    // prompt token, the chunked core, the output projection.
+    const q38_weight *ins[4] = {w->qkv, w->z, w->beta, w->alpha};
+    float *outs[4] = {qkv, z, beta, alpha};
+    for (int i = 0; i < 4; ++i)
+        if (int rc = project_device(ctx, ins[i], tokens, norm, outs[i], st->d_err, s)) return rc;
+    if (int rc = q38_linear_prefill(ctx, st, layer, seq0, nseq, count, qkv, z, beta, alpha, att, stream))
+        return rc;
+    return project_device(ctx, w->out, tokens, att, branch, st->d_err, s);
+}
+
+int q38_full_attention_prefill(q38_ctx *ctx, q38_state *st, int layer, int seq0, int nseq, int count,
+                               int base_position, const q38_full_projections *w, const float *norm,
+                               float *branch, void *stream) {
+    if (int rc = check_prefill_layer(ctx, st, seq0, nseq, count, w, norm, branch)) return rc;
+    for (auto [p, name] : {std::pair<const q38_weight *, const char *>{w->q, "q"}, {w->k, "k"},
+                           {w->v, "v"}, {w->out, "out"}})
+        if (int rc = check_weight(ctx, p, name)) return rc;
+    const int64_t hidden = w->q->w.width;
+    if (w->k->w.width != hidden || w->v->w.width != hidden || w->out->w.rows != hidden ||
+        w->q->w.rows != ctx->qg_dim || w->k->w.rows != ctx->kv_dim || w->v->w.rows != ctx->kv_dim ||
+        w->out->w.width != ctx->q_dim)
+        return proj_fail(Q38_ERR_ARG, "full-attention projection shapes do not match the geometry");
+    Guard guard(ctx->device);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const int tokens = nseq * count;
+    float *qg = st->layer_prefill, *key = qg + size_t(tokens) * ctx->qg_dim;
+    float *value = key + size_t(tokens) * ctx->kv_dim, *att = value + size_t(tokens) * ctx->kv_dim;
+    // batch_full_attention, ops.rs:1116-1185.
+    const q38_weight *ins[3] = {w->q, w->k, w->v};
+    float *outs[3] = {qg, key, value};
+    for (int i = 0; i < 3; ++i)
+        if (int rc = project_device(ctx, ins[i], tokens, norm, outs[i], st->d_err, s)) return rc;
+    if (int rc = q38_full_prefill(ctx, st, layer, seq0, nseq, count, base_position, qg, key, value, att, stream))
+        return rc;
+    return project_device(ctx, w->out, tokens, att, branch, st->d_err, s);
+}
+
 }  // extern "C"

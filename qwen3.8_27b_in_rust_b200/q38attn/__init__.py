@@ -199,6 +199,9 @@ class State:
     def reserve_prefill(self, max_tokens: int) -> None:
         check(self._lib.q38_state_reserve_prefill(self.handle, max_tokens))
 
+    def reserve_attention_prefill(self, max_tokens: int) -> None:
+        check(self._lib.q38_state_reserve_attention_prefill(self.handle, max_tokens))
+
     def checkpoint(self, seq0: int = 0, nseq: Optional[int] = None, stream=None) -> None:
         """Keep the recurrent (conv + delta) state of sequences [seq0, seq0+nseq)
         for a later restore (checkpoint_state, src/model/ops.rs:1627-1640)."""
@@ -409,6 +412,25 @@ class Context:
             self.handle, state.handle, layer, norm.shape[0], ctypes.byref(p),
             _dev_ptr(norm, "norm"), _dev_ptr(positions, "positions", "int32"), max_position,
             _dev_ptr(branch, "branch"), _stream_ptr(stream)))
+
+    def linear_attention_prefill(self, state: "State", layer: int, seq0: int, weights: dict, norm,
+                                 branch, stream=None) -> None:
+        """batch_linear_attention (ops.rs:1032-1114): norm and branch are
+        [nseq][count][hidden] CUDA f32; needs State.reserve_attention_prefill."""
+        p = _LinearProjections(*(weights[k].handle for k in ("qkv", "z", "beta", "alpha", "out")))
+        nseq, count = norm.shape[0], norm.shape[1]
+        check(self._lib.q38_linear_attention_prefill(
+            self.handle, state.handle, layer, seq0, nseq, count, ctypes.byref(p),
+            _dev_ptr(norm, "norm"), _dev_ptr(branch, "branch"), _stream_ptr(stream)))
+
+    def full_attention_prefill(self, state: "State", layer: int, seq0: int, base_position: int,
+                               weights: dict, norm, branch, stream=None) -> None:
+        """batch_full_attention (ops.rs:1116-1185) at positions base_position.."""
+        p = _FullProjections(*(weights[k].handle for k in ("q", "k", "v", "out")))
+        nseq, count = norm.shape[0], norm.shape[1]
+        check(self._lib.q38_full_attention_prefill(
+            self.handle, state.handle, layer, seq0, nseq, count, base_position, ctypes.byref(p),
+            _dev_ptr(norm, "norm"), _dev_ptr(branch, "branch"), _stream_ptr(stream)))
 
     def state(self, batch: int, context_length: int, full_slots: int = FULL_SLOTS,
               linear_slots: int = LINEAR_SLOTS, kv_dtype: int = Q38_KV_F32) -> State:

@@ -112,6 +112,11 @@ SIGNATURES = {
     "q38_linear_attention_decode": (c_int, [_VP, _VP, c_int, c_int, _VP, _VP, _VP, _VP]),
     "q38_full_attention_decode": (c_int, [_VP, _VP, c_int, c_int, _VP, _VP, _VP, c_int, _VP,
                                           _VP]),
+    "q38_state_reserve_attention_prefill": (c_int, [_VP, c_int]),
+    "q38_linear_attention_prefill": (c_int, [_VP, _VP, c_int, c_int, c_int, c_int, _VP, _VP, _VP,
+                                             _VP]),
+    "q38_full_attention_prefill": (c_int, [_VP, _VP, c_int, c_int, c_int, c_int, c_int, _VP, _VP,
+                                           _VP, _VP]),
 }
 
 _lock = threading.Lock()
