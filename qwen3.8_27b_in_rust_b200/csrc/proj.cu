@@ -77,9 +77,15 @@ __device__ __forceinline__ void scale_min_k4(int j, const uint32_t (&s)[3], int 
     }
 }
 
-// Sum of two adjacent 16-value activation sums (the 32-value sub-block of
-// Q4_K / Q5_K).
-__device__ __forceinline__ int pair_sum(const int16_t *sums, int g) { return int(sums[g]) + int(sums[g + 1]); }
+// The eight 32-value sums of a block from its 16 group sums, read as two
+// 16-byte loads (the 2-byte reads of lanes 32 bytes apart hit 4-8-way bank
+// conflicts).
+__device__ __forceinline__ void pair_sums8(const int16_t *sums, int (&ps)[8]) {
+    const uint4 a = reinterpret_cast<const uint4 *>(sums)[0], b = reinterpret_cast<const uint4 *>(sums)[1];
+    const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+    for (int j = 0; j < 8; ++j) ps[j] = int(int16_t(w[j] & 0xffffu)) + int(int16_t(w[j] >> 16));
+}
 
 // ---- per-block terms, one per K-quant type ----------------------------------
 // Each type is a register image of one weight block: load() reads the block
@@ -108,6 +114,8 @@ struct BlockQ4K {
     }
     __device__ __forceinline__ float term(const uint8_t *a, const int16_t *sums, float as) const {
         int weighted = 0, minimum = 0;
+        int ps[8];
+        pair_sums8(sums, ps);
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
             int dot0 = 0, dot1 = 0;
@@ -123,7 +131,7 @@ struct BlockQ4K {
                 }
             }
             weighted += sc[2 * c] * dot0 + sc[2 * c + 1] * dot1;
-            minimum += mn[2 * c] * pair_sum(sums, 4 * c) + mn[2 * c + 1] * pair_sum(sums, 4 * c + 2);
+            minimum += mn[2 * c] * ps[2 * c] + mn[2 * c + 1] * ps[2 * c + 1];
         }
         const float d = half_to_float(dm) * as;
         const float dmin = half_to_float(dm >> 16) * as;
@@ -156,6 +164,8 @@ struct BlockQ5K {
     }
     __device__ __forceinline__ float term(const uint8_t *a, const int16_t *sums, float as) const {
         int weighted = 0, minimum = 0;
+        int ps[8];
+        pair_sums8(sums, ps);
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
             int dot0 = 0, dot1 = 0;
@@ -173,7 +183,7 @@ struct BlockQ5K {
                 }
             }
             weighted += sc[2 * c] * dot0 + sc[2 * c + 1] * dot1;
-            minimum += mn[2 * c] * pair_sum(sums, 4 * c) + mn[2 * c + 1] * pair_sum(sums, 4 * c + 2);
+            minimum += mn[2 * c] * ps[2 * c] + mn[2 * c + 1] * ps[2 * c + 1];
         }
         const float d = half_to_float(dm) * as;
         const float dmin = half_to_float(dm >> 16) * as;
@@ -181,19 +191,25 @@ struct BlockQ5K {
     }
 };
 
-// dot_q6_k_q8_k_scalar, tensor.rs:430-460. 210 bytes (2-byte aligned): 128
-// low-nibble bytes | 64 high-bit bytes | 16 signed scales | d. The 6-bit
-// values minus 32 are formed per byte with __vsub4.
+// dot_q6_k_q8_k_scalar, tensor.rs:430-460. 210 bytes, padded to 224 on the
+// device: 128 low-nibble bytes | 64 high-bit bytes | 16 signed scales | d.
+// The 6-bit values minus 32 are formed per byte with __vsub4.
 struct BlockQ6K {
     uint32_t ql[32], qh[16], sc[4];
     uint32_t d16;
-    __device__ __forceinline__ void load(const uint8_t *w) {
+    __device__ __forceinline__ void load(const uint8_t *w) {  // 224-byte device blocks: 16-byte aligned
 #pragma unroll
-        for (int k = 0; k < 32; ++k) ql[k] = ld32_a2(w + 4 * k);
+        for (int k = 0; k < 8; ++k) {
+            const uint4 v = ld128(w + 16 * k);
+            ql[4 * k] = v.x, ql[4 * k + 1] = v.y, ql[4 * k + 2] = v.z, ql[4 * k + 3] = v.w;
+        }
 #pragma unroll
-        for (int k = 0; k < 16; ++k) qh[k] = ld32_a2(w + 128 + 4 * k);
-#pragma unroll
-        for (int k = 0; k < 4; ++k) sc[k] = ld32_a2(w + 192 + 4 * k);
+        for (int k = 0; k < 4; ++k) {
+            const uint4 v = ld128(w + 128 + 16 * k);
+            qh[4 * k] = v.x, qh[4 * k + 1] = v.y, qh[4 * k + 2] = v.z, qh[4 * k + 3] = v.w;
+        }
+        const uint4 v = ld128(w + 192);
+        sc[0] = v.x, sc[1] = v.y, sc[2] = v.z, sc[3] = v.w;
         d16 = *reinterpret_cast<const uint16_t *>(w + 208);
     }
     __device__ __forceinline__ int scale(int i) const { return int(int8_t(byte_of(sc[i >> 2], i & 3))); }
@@ -356,9 +372,7 @@ struct WarpQ8K {
     int group_sum;
 };
 
-__device__ __forceinline__ WarpQ8K quantize_block_warp(const float *src, int lane) {
-    const float4 v0 = reinterpret_cast<const float4 *>(src)[2 * lane];
-    const float4 v1 = reinterpret_cast<const float4 *>(src)[2 * lane + 1];
+__device__ __forceinline__ WarpQ8K quantize_values_warp(const float4 v0, const float4 v1, int lane) {
     const float v[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
     // First largest magnitude: the lane's own scan, then (magnitude, index)
     // pairs where a tie keeps the smaller index. NaN never compares greater,
@@ -414,6 +428,11 @@ __device__ __forceinline__ WarpQ8K quantize_block_warp(const float *src, int lan
     return r;
 }
 
+__device__ __forceinline__ WarpQ8K quantize_block_warp(const float *src, int lane) {
+    return quantize_values_warp(reinterpret_cast<const float4 *>(src)[2 * lane],
+                                reinterpret_cast<const float4 *>(src)[2 * lane + 1], lane);
+}
+
 __global__ void __launch_bounds__(128) q8k_quantize_kernel(QuantizeParams p) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int blk = blockIdx.x * 4 + warp, t = blockIdx.y;
@@ -459,7 +478,7 @@ __host__ __device__ inline ProjSmem proj_smem_plan(int stages, uint32_t tile_byt
     s.ring = 0;
     s.act_q = stages * tile_bytes;
     s.act_d = s.act_q + uint32_t(batch * nblk * kActStride);
-    s.act_s = s.act_d + uint32_t(batch * nblk * 4);
+    s.act_s = (s.act_d + uint32_t(batch * nblk * 4) + 15u) & ~15u;  // 16-byte loads of the sums
     s.vt = s.act_s + uint32_t(batch * nblk * 32);
     s.total = s.vt + uint32_t(kProjConsumerWarps * batch * (nblk + 1) * 4);
     return s;
@@ -502,11 +521,29 @@ __global__ void __launch_bounds__(kProjQ8KThreads, 1) proj_q8k_kernel(ProjQ8KPar
     pdl_launch_dependents();
     // quantize_q8_k of the launch's tokens into shared memory, one warp per
     // 256-block (the same steps as q8k_quantize_kernel).
-    for (int blk = warp; blk < p.batch * p.nblk; blk += kProjConsumerWarps + 1) {
-        const WarpQ8K r = quantize_block_warp(p.x + size_t(blk) * 256, lane);
-        *reinterpret_cast<uint2 *>(smem + lay.act_q + blk * kActStride + lane * 8) = make_uint2(r.w0, r.w1);
-        if (lane == 0) ad[blk] = r.scale;
-        if ((lane & 1) == 0) asums[blk * 16 + (lane >> 1)] = int16_t(r.group_sum);
+    // Each warp's blocks are loaded before any is quantized, so the global
+    // loads overlap instead of running one round-trip per block.
+    constexpr int kQWarps = kProjConsumerWarps + 1, kQAhead = 4;
+    for (int base = warp; base < p.batch * p.nblk; base += kQWarps * kQAhead) {
+        float4 v[kQAhead][2];
+#pragma unroll
+        for (int u = 0; u < kQAhead; ++u) {
+            const int blk = base + u * kQWarps;
+            if (blk < p.batch * p.nblk) {
+                const float4 *src = reinterpret_cast<const float4 *>(p.x + size_t(blk) * 256);
+                v[u][0] = src[2 * lane];
+                v[u][1] = src[2 * lane + 1];
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < kQAhead; ++u) {
+            const int blk = base + u * kQWarps;
+            if (blk >= p.batch * p.nblk) break;
+            const WarpQ8K r = quantize_values_warp(v[u][0], v[u][1], lane);
+            *reinterpret_cast<uint2 *>(smem + lay.act_q + blk * kActStride + lane * 8) = make_uint2(r.w0, r.w1);
+            if (lane == 0) ad[blk] = r.scale;
+            if ((lane & 1) == 0) asums[blk * 16 + (lane >> 1)] = int16_t(r.group_sum);
+        }
     }
     __syncthreads();
 
@@ -552,6 +589,20 @@ __global__ void __launch_bounds__(kProjQ8KThreads, 1) proj_q8k_kernel(ProjQ8KPar
         for (int r = warp; r < p.tile_rows; r += kProjConsumerWarps) {
             const int row = tile * p.tile_rows + r;
             if (row >= p.rows) break;  // rows ascend with r
+            if (p.batch == 1 && p.nblk <= 32) {
+                // One token, one block per lane: the block terms added in
+                // block order by lane 0, straight from the other lanes.
+                float v = 0.f;
+                if (lane < p.nblk) {
+                    typename BlockOf<T>::type blk;
+                    blk.load(tw + size_t(r) * p.rb + size_t(lane) * kBlockBytes<T>);
+                    v = blk.term(aq + lane * kActStride, asums + lane * 16, ad[lane]);
+                }
+                float total = 0.f;
+                for (int b = 0; b < p.nblk; ++b) total = __fadd_rn(total, __shfl_sync(0xffffffffu, v, b));
+                if (lane == 0) p.out[row] = total;
+                continue;
+            }
             for (int b = lane; b < p.nblk; b += 32) {
                 typename BlockOf<T>::type blk;
                 blk.load(tw + size_t(r) * p.rb + size_t(b) * kBlockBytes<T>);
