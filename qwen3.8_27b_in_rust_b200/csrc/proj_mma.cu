@@ -20,21 +20,22 @@
 // below 256, so one integer multiply forms four operand bytes. The epilogue
 // combines the chains and adds the f32 term exactly as the reference does.
 //
-// CTA: 128 weight rows x 32 tokens, 21 warps; the K loop runs in half-blocks
-// (128 values, one SW128 atom per chain).
+// CTA: 128 weight rows x 32 tokens, 21 warps; the K loop runs in blocks (two
+// SW128 atoms of 128 values per chain).
 //   warp 0      TMA: raw weight blocks [128 rows][block bytes] (the first ones
 //               before the programmatic-dependent wait: weights are constant;
 //               up to 6 stages, and L2 prefetches a further 4 blocks ahead)
 //               and the activation quants [32 tokens][256] (SW128).
-//   warps 1-4   warp 1 + c issues chain c: per half-block 4 K-steps of
+//   warps 1-4   warp 1 + c issues chain c: per block 8 K-steps of
 //               kind::i8 MMAs (M=128, N=32, K=32) into the chain's
 //               accumulator (two blocks' worth of columns, alternating); a
 //               thread waits on each issue, so the chains issue in parallel.
 //               Warp 1 also allocates TMEM.
 //   warps 5-20  thread = weight row (TMEM lane); four groups of four warps:
 //               group g builds values 32g..32g+31 of each half-block and
-//               finishes tokens 8g..8g+7; three operand buffers let them
-//               run two half-blocks ahead of the MMAs.
+//               finishes tokens 8g..8g+7; a block's MMAs overlap the
+//               previous block's epilogue. (Separate build and epilogue warps
+//               measured slower: the operand build is the binding cost.)
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -253,7 +254,7 @@ struct MmaSmem {
 __host__ __device__ inline MmaSmem mma_smem_plan(int chains, int abufs, int stages, uint32_t raw_bytes, int nblk) {
     MmaSmem s{};
     s.a = 0;
-    s.raw = uint32_t(abufs * chains) * kAtomA;
+    s.raw = uint32_t(abufs * chains) * 2 * kAtomA;  // a buffer: every chain's two half-block atoms
     s.b = s.raw + stages * ((raw_bytes + 1023) / 1024 * 1024);
     s.scl = s.b + stages * kStageB;
     s.total = s.scl + uint32_t(kMmaTok * nblk * 4);
@@ -286,7 +287,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
     float *scl = reinterpret_cast<float *>(smem + lay.scl);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int row0 = blockIdx.x * kMmaRows, tok0 = blockIdx.y * kMmaTok;
-    const int steps = 2 * p.nblk;  // half-blocks
+    const int steps = p.nblk;  // one block (two half-block atoms per chain) per step
 
     if (tid == 0) {
         abort_flag = 0;
@@ -371,27 +372,28 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
         const int c = warp - 1;
         if (lane == 0 && c < NC) {
             const uint32_t idesc = idesc_i8(kMmaRows, kMmaTok, C::is_signed(c));
-            for (int st = 0; st < steps; ++st) {
-                const int b = st >> 1, h = st & 1, s = b % S, ab = st % NA;
-                if (!mbar_wait(&a_full[ab], uint32_t(st / NA) & 1u) ||
-                    (h == 0 && !mbar_wait(&b_full[s], uint32_t(b / S) & 1u)) || abort_flag) {
+            for (int b = 0; b < steps; ++b) {
+                const int s = b % S, ab = b % NA;
+                if (!mbar_wait(&a_full[ab], uint32_t(b / NA) & 1u) ||
+                    !mbar_wait(&b_full[s], uint32_t(b / S) & 1u) || abort_flag) {
                     abort_flag = 1;
                     set_error(p.err, kDevErrTimeout);
                     break;
                 }
                 fence_after_sync();
-                const uint32_t abase = smem_addr(smem + lay.a + ab * NC * kAtomA);
-                const uint32_t bbase = smem_addr(smem + lay.b + s * kStageB + h * kAtomB);
+                const uint32_t abase = smem_addr(smem + lay.a + (ab * NC + c) * 2 * kAtomA);
+                const uint32_t bbase = smem_addr(smem + lay.b + s * kStageB);
                 const uint32_t dcol = uint32_t((b & 1) * NC * 32);
 #pragma unroll
-                for (int k = 0; k < 4; ++k)  // K-steps of 32 bytes within the half-block
-                    mma_i8(tmem + dcol + c * 32, smem_desc_sw128(abase + c * kAtomA + k * 32, 16, 1024),
-                           smem_desc_sw128(bbase + k * 32, 16, 1024), idesc, (h | k) ? 1u : 0u);
+                for (int h = 0; h < 2; ++h)
+#pragma unroll
+                    for (int k = 0; k < 4; ++k)  // K-steps of 32 bytes within each half-block atom
+                        mma_i8(tmem + dcol + c * 32, smem_desc_sw128(abase + h * kAtomA + k * 32, 16, 1024),
+                               smem_desc_sw128(bbase + h * kAtomB + k * 32, 16, 1024), idesc,
+                               (h | k) ? 1u : 0u);
                 mma_commit(&a_free[ab]);
-                if (h == 1) {
-                    mma_commit(&mma_done[b & 1]);
-                    mma_commit(&b_empty[s]);
-                }
+                mma_commit(&mma_done[b & 1]);
+                mma_commit(&b_empty[s]);
             }
         }
     } else {
@@ -426,36 +428,37 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
                 total[t] = total[t] + C::term(d, dbits, as[t]);
             }
         };
-        for (int st = 0; st < steps && ok; ++st) {
-            const int b = st >> 1, h = st & 1, s = b % S, ab = st % NA;
-            if (h == 0 && !__all_sync(0xffffffffu, mbar_wait(&raw_full[s], uint32_t(b / S) & 1u))) {
+        for (int b = 0; b < steps && ok; ++b) {
+            const int s = b % S, ab = b % NA;
+            if (!__all_sync(0xffffffffu, mbar_wait(&raw_full[s], uint32_t(b / S) & 1u))) {
                 ok = false;
                 break;
             }
-            if (st >= NA && !__all_sync(0xffffffffu, mbar_wait(&a_free[ab], uint32_t(st / NA - 1) & 1u))) {
+            if (b >= NA && !__all_sync(0xffffffffu, mbar_wait(&a_free[ab], uint32_t(b / NA - 1) & 1u))) {
                 ok = false;
                 break;
             }
             const unsigned char *w = smem + lay.raw + s * raw_stride + r * C::kBytes;
-            if (h == 0) dcur = C::dscale(w);
-            unsigned char *atoms[NC];
+            dcur = C::dscale(w);
 #pragma unroll
-            for (int c = 0; c < NC; ++c) atoms[c] = smem + lay.a + (ab * NC + c) * kAtomA;
-            C::build(w, h, g, r, atoms);
+            for (int h = 0; h < 2; ++h) {
+                unsigned char *atoms[NC];
+#pragma unroll
+                for (int c = 0; c < NC; ++c) atoms[c] = smem + lay.a + ((ab * NC + c) * 2 + h) * kAtomA;
+                C::build(w, h, g, r, atoms);
+            }
             fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0) {
                 mbar_arrive(&a_full[ab]);
-                if (h == 1) mbar_arrive(&raw_empty[s]);
+                mbar_arrive(&raw_empty[s]);
             }
-            if (h == 1) {
-                if (b > 0) {
-                    epilogue(b - 1, dprev);
-                    if (!ok) break;
-                    fence_before_sync();  // TMEM reads done before the next a_full arrive
-                }
-                dprev = dcur;
+            if (b > 0) {
+                epilogue(b - 1, dprev);
+                if (!ok) break;
+                fence_before_sync();  // TMEM reads done before the next a_full arrive
             }
+            dprev = dcur;
         }
         if (ok) epilogue(p.nblk - 1, dprev);
         if (!ok) {
