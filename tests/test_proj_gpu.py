@@ -152,12 +152,14 @@ def _oracle_project(oracle_lib, spec, x):
     return oracle_lib.project(ty, data, rows, width, x)
 
 
-def test_linear_attention_decode_matches_oracle(cuda_ctx, oracle_lib):
-    """linear_attention (ops.rs:744-803) for two sequences of DeltaNet layer 0."""
+@pytest.mark.parametrize("batch", [2, 12])
+def test_linear_attention_decode_matches_oracle(cuda_ctx, oracle_lib, batch):
+    """linear_attention (ops.rs:744-803) for sequences of DeltaNet layer 0; 12
+    sequences take the tensor-core projections."""
     from q38attn import synth
     torch = _torch()
-    g = synth.rng(400)
-    layer, batch = 0, 2
+    g = synth.rng(400 + batch)
+    layer = 0
     lw = synth.linear_weights(g)
     cuda_ctx.bind_linear_layer(layer, lw["conv1d"], lw["dt_bias"], lw["ssm_a"], lw["ssm_norm"])
     host, dev = _layer_weights(cuda_ctx, g, {
@@ -193,14 +195,16 @@ def test_linear_attention_decode_matches_oracle(cuda_ctx, oracle_lib):
     st.close()
 
 
-def test_full_attention_decode_matches_oracle(cuda_ctx, oracle_lib):
-    """full_attention (ops.rs:941-981) for two sequences of full layer 3 at
-    positions 5 and 40 over an f32 cache."""
+@pytest.mark.parametrize("batch", [2, 12])
+def test_full_attention_decode_matches_oracle(cuda_ctx, oracle_lib, batch):
+    """full_attention (ops.rs:941-981) for sequences of full layer 3 at
+    positions 5, 40, ... over an f32 cache; 12 sequences take the tensor-core
+    projections."""
     from q38attn import synth
     torch = _torch()
-    g = synth.rng(401)
-    layer, batch, ctx_len = 3, 2, 64
-    positions = [5, 40]
+    g = synth.rng(401 + batch)
+    layer, ctx_len = 3, 64
+    positions = [5, 40, 0, 1, 63, 17, 30, 2, 50, 9, 33, 60][:batch]
     fw = synth.full_weights(g)
     cuda_ctx.bind_full_layer(layer, fw["q_norm"], fw["k_norm"])
     host, dev = _layer_weights(cuda_ctx, g, {
@@ -209,11 +213,12 @@ def test_full_attention_decode_matches_oracle(cuda_ctx, oracle_lib):
     st = cuda_ctx.state(batch, ctx_len, full_slots=1, linear_slots=0)
     caches = []
     for b, pos in enumerate(positions):
-        k, v = synth.kv_rows(g, pos)
-        st.upload_kv(layer, b, 0, k, v)
         kc = np.zeros((ctx_len, 1024), F)
         vc = np.zeros((ctx_len, 1024), F)
-        kc[:pos], vc[:pos] = k, v
+        if pos:
+            k, v = synth.kv_rows(g, pos)
+            st.upload_kv(layer, b, 0, k, v)
+            kc[:pos], vc[:pos] = k, v
         caches.append((kc, vc))
     norm = synth.normal(g, (batch, HIDDEN))
     branch = torch.zeros(batch, HIDDEN, device="cuda")
