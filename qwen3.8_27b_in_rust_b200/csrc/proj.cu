@@ -473,6 +473,31 @@ struct ProjSmem {
     uint32_t ring, act_q, act_d, act_s, vt, total;
 };
 
+// Floats per consumer warp's combine buffer: [batch][nblk + 1] block terms,
+// at least 32 (the one-token path stages one term per lane) and a multiple of
+// four so that every warp's buffer starts on a 16-byte boundary.
+__host__ __device__ inline int proj_vt_stride(int batch, int nblk) {
+    const int n = batch * (nblk + 1);
+    return n < 32 ? 32 : (n + 3) & ~3;
+}
+
+// The first n (<= 32) floats of a 16-byte-aligned buffer added in order:
+// all loads first, then the serial adds.
+__device__ __forceinline__ float ordered_sum32(const float *v, int n) {
+    float4 t4[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) t4[i] = reinterpret_cast<const float4 *>(v)[i];
+    float total = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const float e[4] = {t4[i].x, t4[i].y, t4[i].z, t4[i].w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+            if (4 * i + j < n) total = __fadd_rn(total, e[j]);
+    }
+    return total;
+}
+
 __host__ __device__ inline ProjSmem proj_smem_plan(int stages, uint32_t tile_bytes, int batch, int nblk) {
     ProjSmem s{};
     s.ring = 0;
@@ -480,7 +505,7 @@ __host__ __device__ inline ProjSmem proj_smem_plan(int stages, uint32_t tile_byt
     s.act_d = s.act_q + uint32_t(batch * nblk * kActStride);
     s.act_s = (s.act_d + uint32_t(batch * nblk * 4) + 15u) & ~15u;  // 16-byte loads of the sums
     s.vt = s.act_s + uint32_t(batch * nblk * 32);
-    s.total = s.vt + uint32_t(kProjConsumerWarps * batch * (nblk + 1) * 4);
+    s.total = s.vt + uint32_t(kProjConsumerWarps * proj_vt_stride(batch, nblk) * 4);
     return s;
 }
 
@@ -573,7 +598,7 @@ __global__ void __launch_bounds__(kProjQ8KThreads, 1) proj_q8k_kernel(ProjQ8KPar
     }
 
     // ------------------------------------------------------------ consumers
-    float *vt = reinterpret_cast<float *>(smem + lay.vt) + warp * p.batch * (p.nblk + 1);
+    float *vt = reinterpret_cast<float *>(smem + lay.vt) + warp * proj_vt_stride(p.batch, p.nblk);
     int k = 0;
     for (int tile = blockIdx.x; tile < p.ntiles; tile += gridDim.x, ++k) {
         const int s = k % p.stages;
@@ -590,17 +615,19 @@ __global__ void __launch_bounds__(kProjQ8KThreads, 1) proj_q8k_kernel(ProjQ8KPar
             const int row = tile * p.tile_rows + r;
             if (row >= p.rows) break;  // rows ascend with r
             if (p.batch == 1 && p.nblk <= 32) {
-                // One token, one block per lane: the block terms added in
-                // block order by lane 0, straight from the other lanes.
+                // One token, one block per lane: the block terms staged in
+                // the warp's buffer, where lane 0 reads all 32 at once and
+                // adds the first nblk in block order (only the adds are serial).
                 float v = 0.f;
                 if (lane < p.nblk) {
                     typename BlockOf<T>::type blk;
                     blk.load(tw + size_t(r) * p.rb + size_t(lane) * kBlockBytes<T>);
                     v = blk.term(aq + lane * kActStride, asums + lane * 16, ad[lane]);
                 }
-                float total = 0.f;
-                for (int b = 0; b < p.nblk; ++b) total = __fadd_rn(total, __shfl_sync(0xffffffffu, v, b));
-                if (lane == 0) p.out[row] = total;
+                vt[lane] = v;
+                __syncwarp();
+                if (lane == 0) p.out[row] = ordered_sum32(vt, p.nblk);
+                __syncwarp();
                 continue;
             }
             for (int b = lane; b < p.nblk; b += 32) {
@@ -615,6 +642,7 @@ __global__ void __launch_bounds__(kProjQ8KThreads, 1) proj_q8k_kernel(ProjQ8KPar
             if (lane < p.batch) {
                 const float *v = vt + lane * (p.nblk + 1);
                 float total = 0.f;
+#pragma unroll 8
                 for (int b = 0; b < p.nblk; ++b) total = __fadd_rn(total, v[b]);
                 p.out[size_t(lane) * p.out_ld + row] = total;
             }
