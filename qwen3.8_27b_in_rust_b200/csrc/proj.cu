@@ -13,7 +13,8 @@
 //                         quantize_block: first largest magnitude (strict >),
 //                         -127/max and 1/inverse as IEEE divisions, the
 //                         round-half-even trick of nearest_int, clamp at 127.
-//   proj_q8k_kernel<T>    persistent, one CTA per SM. Weight tiles (tile_rows
+//   proj_q8k_kernel<T,W>  persistent, one CTA per SM, W consumer warps (16
+//                         for one token, else 8). Weight tiles (tile_rows
 //                         consecutive rows = one contiguous byte range) stream
 //                         through a ring of shared-memory stages by bulk copy
 //                         (cp.async.bulk + mbarrier); the Q8_K activations of
@@ -41,8 +42,8 @@
 namespace q38 {
 namespace {
 
-constexpr int kProjConsumerWarps = 8;
-constexpr int kProjQ8KThreads = 32 * (kProjConsumerWarps + 1);
+constexpr int kProjConsumerWarps = 8;    // the general kernel
+constexpr int kProjOneTokenWarps = 16;  // one token, rows of up to 32 blocks
 constexpr int kProjTileRows = kProjMaxTileRows;
 constexpr int kActStride = 272;  // shared bytes per activation block: 256 quants + 16 (bank spread)
 constexpr int kMaxStages = 4;
@@ -498,27 +499,31 @@ __device__ __forceinline__ float ordered_sum32(const float *v, int n) {
     return total;
 }
 
-__host__ __device__ inline ProjSmem proj_smem_plan(int stages, uint32_t tile_bytes, int batch, int nblk) {
+__host__ __device__ inline ProjSmem proj_smem_plan(int stages, uint32_t tile_bytes, int batch, int nblk,
+                                                   int warps) {
     ProjSmem s{};
     s.ring = 0;
     s.act_q = stages * tile_bytes;
     s.act_d = s.act_q + uint32_t(batch * nblk * kActStride);
     s.act_s = (s.act_d + uint32_t(batch * nblk * 4) + 15u) & ~15u;  // 16-byte loads of the sums
     s.vt = s.act_s + uint32_t(batch * nblk * 32);
-    s.total = s.vt + uint32_t(kProjConsumerWarps * proj_vt_stride(batch, nblk) * 4);
+    s.total = s.vt + uint32_t(warps * proj_vt_stride(batch, nblk) * 4);
     return s;
 }
 
-// Warp roles: warps 0..kProjConsumerWarps-1 compute (warp w owns rows w and
-// w + kProjConsumerWarps of each 16-row tile; lane j owns blocks j, j+32, ...),
+// Warp roles: warps 0..W-1 compute (warp w owns rows w, w + W, ... of each
+// tile; lane j owns blocks j, j+32, ...),
 // the last warp streams the tiles. Each row's block terms go through the
 // warp's combine buffer, where lane t adds token t's terms in block order.
-template <int T>
-__global__ void __launch_bounds__(kProjQ8KThreads, 1) proj_q8k_kernel(ProjQ8KParams p) {
+// W = kProjOneTokenWarps is the one-token form (the host sends it only one
+// token and rows of up to 32 blocks): twice the warps, each with at most 120
+// registers, to hide the latency of the per-row work.
+template <int T, int W>
+__global__ void __launch_bounds__(32 * (W + 1), 1) proj_q8k_kernel(ProjQ8KParams p) {
     extern __shared__ __align__(128) unsigned char smem[];
     __shared__ __align__(8) uint64_t full[kMaxStages], empty[kMaxStages];
     __shared__ volatile int abort_flag;
-    const ProjSmem lay = proj_smem_plan(p.stages, p.tile_bytes, p.batch, p.nblk);
+    const ProjSmem lay = proj_smem_plan(p.stages, p.tile_bytes, p.batch, p.nblk, W);
     const uint8_t *aq = smem + lay.act_q;
     float *ad = reinterpret_cast<float *>(smem + lay.act_d);
     int16_t *asums = reinterpret_cast<int16_t *>(smem + lay.act_s);
@@ -528,7 +533,7 @@ __global__ void __launch_bounds__(kProjQ8KThreads, 1) proj_q8k_kernel(ProjQ8KPar
         abort_flag = 0;
         for (int s = 0; s < p.stages; ++s) {
             mbar_init(&full[s], 1);
-            mbar_init(&empty[s], kProjConsumerWarps);
+            mbar_init(&empty[s], W);
         }
         fence_barrier_init();
     }
@@ -536,7 +541,7 @@ __global__ void __launch_bounds__(kProjQ8KThreads, 1) proj_q8k_kernel(ProjQ8KPar
     // The weights are constant: the first tiles are requested before waiting
     // for the previous kernel in the stream (programmatic dependent launch).
     const int first = min(p.stages, (p.ntiles - int(blockIdx.x) + int(gridDim.x) - 1) / int(gridDim.x));
-    if (warp == kProjConsumerWarps && lane == 0)
+    if (warp == W && lane == 0)
         for (int k = 0; k < first; ++k) {
             mbar_arrive_expect_tx(&full[k], p.tile_bytes);
             bulk_load(smem + k * p.tile_bytes,
@@ -548,7 +553,7 @@ __global__ void __launch_bounds__(kProjQ8KThreads, 1) proj_q8k_kernel(ProjQ8KPar
     // 256-block (the same steps as q8k_quantize_kernel).
     // Each warp's blocks are loaded before any is quantized, so the global
     // loads overlap instead of running one round-trip per block.
-    constexpr int kQWarps = kProjConsumerWarps + 1, kQAhead = 4;
+    constexpr int kQWarps = W + 1, kQAhead = 4;
     for (int base = warp; base < p.batch * p.nblk; base += kQWarps * kQAhead) {
         float4 v[kQAhead][2];
 #pragma unroll
@@ -572,7 +577,7 @@ __global__ void __launch_bounds__(kProjQ8KThreads, 1) proj_q8k_kernel(ProjQ8KPar
     }
     __syncthreads();
 
-    if (warp == kProjConsumerWarps) {
+    if (warp == W) {
         // ---------------------------------------------------------- producer
         if (lane == 0) {
             int k = first;
@@ -611,10 +616,10 @@ __global__ void __launch_bounds__(kProjQ8KThreads, 1) proj_q8k_kernel(ProjQ8KPar
         }
         const uint8_t *tw = smem + s * p.tile_bytes;
 #pragma unroll 1
-        for (int r = warp; r < p.tile_rows; r += kProjConsumerWarps) {
+        for (int r = warp; r < p.tile_rows; r += W) {
             const int row = tile * p.tile_rows + r;
             if (row >= p.rows) break;  // rows ascend with r
-            if (p.batch == 1 && p.nblk <= 32) {
+            if constexpr (W == kProjOneTokenWarps) {
                 // One token, one block per lane: the block terms staged in
                 // the warp's buffer, where lane 0 reads all 32 at once and
                 // adds the first nblk in block order (only the adds are serial).
@@ -628,25 +633,25 @@ __global__ void __launch_bounds__(kProjQ8KThreads, 1) proj_q8k_kernel(ProjQ8KPar
                 __syncwarp();
                 if (lane == 0) p.out[row] = ordered_sum32(vt, p.nblk);
                 __syncwarp();
-                continue;
-            }
-            for (int b = lane; b < p.nblk; b += 32) {
-                typename BlockOf<T>::type blk;
-                blk.load(tw + size_t(r) * p.rb + size_t(b) * kBlockBytes<T>);
-                for (int t = 0; t < p.batch; ++t) {
-                    const int ab = t * p.nblk + b;
-                    vt[t * (p.nblk + 1) + b] = blk.term(aq + ab * kActStride, asums + ab * 16, ad[ab]);
+            } else {
+                for (int b = lane; b < p.nblk; b += 32) {
+                    typename BlockOf<T>::type blk;
+                    blk.load(tw + size_t(r) * p.rb + size_t(b) * kBlockBytes<T>);
+                    for (int t = 0; t < p.batch; ++t) {
+                        const int ab = t * p.nblk + b;
+                        vt[t * (p.nblk + 1) + b] = blk.term(aq + ab * kActStride, asums + ab * 16, ad[ab]);
+                    }
                 }
-            }
-            __syncwarp();
-            if (lane < p.batch) {
-                const float *v = vt + lane * (p.nblk + 1);
-                float total = 0.f;
+                __syncwarp();
+                if (lane < p.batch) {
+                    const float *v = vt + lane * (p.nblk + 1);
+                    float total = 0.f;
 #pragma unroll 8
-                for (int b = 0; b < p.nblk; ++b) total = __fadd_rn(total, v[b]);
-                p.out[size_t(lane) * p.out_ld + row] = total;
+                    for (int b = 0; b < p.nblk; ++b) total = __fadd_rn(total, v[b]);
+                    p.out[size_t(lane) * p.out_ld + row] = total;
+                }
+                __syncwarp();
             }
-            __syncwarp();
         }
         if (lane == 0) mbar_arrive(&empty[s]);
     }
@@ -752,9 +757,9 @@ __global__ void __launch_bounds__(256) proj_f32_kernel(ProjF32Params p) {
     }
 }
 
-template <int T>
+template <int T, int W>
 cudaError_t launch_q8k(const ProjQ8KParams &p, int sm_count, cudaStream_t stream) {
-    const ProjSmem lay = proj_smem_plan(p.stages, p.tile_bytes, p.batch, p.nblk);
+    const ProjSmem lay = proj_smem_plan(p.stages, p.tile_bytes, p.batch, p.nblk, W);
     // The attribute is set once per device to the budget, so later launches
     // make no extra driver calls (and can be captured in a graph).
     static bool attr_set[kMaxDevices] = {};
@@ -762,24 +767,25 @@ cudaError_t launch_q8k(const ProjQ8KParams &p, int sm_count, cudaStream_t stream
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
     if (dev >= kMaxDevices || !attr_set[dev]) {
-        e = cudaFuncSetAttribute(proj_q8k_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        e = cudaFuncSetAttribute(proj_q8k_kernel<T, W>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  int(kProjSmemBudget));
         if (e != cudaSuccess) return e;
         if (dev < kMaxDevices) attr_set[dev] = true;
     }
-    // One CTA per SM (the block images take ~150 registers a thread),
+    // One CTA per SM (the general form's block images take ~150 registers
+    // a thread),
     // launched as a programmatic dependent of the previous kernel.
     cudaLaunchConfig_t cfg{};
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.gridDim = dim3(std::min(p.ntiles, sm_count));
-    cfg.blockDim = dim3(kProjQ8KThreads);
+    cfg.blockDim = dim3(32 * (W + 1));
     cfg.dynamicSmemBytes = lay.total;
     cfg.stream = stream;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, proj_q8k_kernel<T>, p);
+    return cudaLaunchKernelEx(&cfg, proj_q8k_kernel<T, W>, p);
 }
 
 template <int T>
@@ -870,32 +876,56 @@ cudaError_t launch_proj_q8k(const ProjWeight &w, const float *x, int batch, floa
     p.rb = rb;
     // 16-row tiles, or 8 when three stages of 16 rows would not fit beside
     // one token's activations (so the copies stay ahead of the compute).
+    // The one-token form (16 warps, a row each) keeps 16-row tiles while two
+    // stages fit.
+    const bool one_token = batch == 1 && nblk <= 32;
     p.tile_rows = kProjTileRows;
-    if (proj_smem_plan(0, 16u * rb, 1, nblk).total + 3u * 16u * rb > kProjSmemBudget) p.tile_rows = 8;
+    if (proj_smem_plan(0, 16u * rb, 1, nblk, kProjConsumerWarps).total + (one_token ? 2u : 3u) * 16u * rb >
+        kProjSmemBudget)
+        p.tile_rows = 8;
     p.ntiles = int((w.rows + p.tile_rows - 1) / p.tile_rows);
     p.tile_bytes = uint32_t(p.tile_rows * rb);
     // Tokens per launch: up to kProjMaxTok, fewer when the activations would
     // leave room for less than two weight stages (wide Q6_K rows).
     int per = kProjMaxTok;
-    while (per > 1 && proj_smem_plan(0, p.tile_bytes, per, nblk).total + 2 * p.tile_bytes > kProjSmemBudget)
+    while (per > 1 &&
+           proj_smem_plan(0, p.tile_bytes, per, nblk, kProjConsumerWarps).total + 2 * p.tile_bytes > kProjSmemBudget)
         --per;
     for (int t0 = 0; t0 < batch; t0 += per) {
         p.batch = std::min(per, batch - t0);
         p.x = x + size_t(t0) * nblk * 256;
         p.out = out + size_t(t0) * out_ld;
         // Stages: as many as the budget allows, up to 4.
-        const uint32_t fixed = proj_smem_plan(0, p.tile_bytes, p.batch, nblk).total;
+        // One token over rows of up to 32 blocks: the 16-warp form.
+        const bool one = p.batch == 1 && nblk <= 32;
+        const uint32_t fixed =
+            proj_smem_plan(0, p.tile_bytes, p.batch, nblk, one ? kProjOneTokenWarps : kProjConsumerWarps).total;
         int stages = int((kProjSmemBudget - fixed) / p.tile_bytes);
         stages = std::min(stages, kMaxStages);
         if (stages < 2) return cudaErrorInvalidValue;
         p.stages = stages;
         cudaError_t e;
         switch (w.type) {
-            case Q38_GGML_Q2_K: e = launch_q8k<Q38_GGML_Q2_K>(p, sm_count, stream); break;
-            case Q38_GGML_Q3_K: e = launch_q8k<Q38_GGML_Q3_K>(p, sm_count, stream); break;
-            case Q38_GGML_Q4_K: e = launch_q8k<Q38_GGML_Q4_K>(p, sm_count, stream); break;
-            case Q38_GGML_Q5_K: e = launch_q8k<Q38_GGML_Q5_K>(p, sm_count, stream); break;
-            case Q38_GGML_Q6_K: e = launch_q8k<Q38_GGML_Q6_K>(p, sm_count, stream); break;
+            case Q38_GGML_Q2_K:
+                e = one ? launch_q8k<Q38_GGML_Q2_K, kProjOneTokenWarps>(p, sm_count, stream)
+                        : launch_q8k<Q38_GGML_Q2_K, kProjConsumerWarps>(p, sm_count, stream);
+                break;
+            case Q38_GGML_Q3_K:
+                e = one ? launch_q8k<Q38_GGML_Q3_K, kProjOneTokenWarps>(p, sm_count, stream)
+                        : launch_q8k<Q38_GGML_Q3_K, kProjConsumerWarps>(p, sm_count, stream);
+                break;
+            case Q38_GGML_Q4_K:
+                e = one ? launch_q8k<Q38_GGML_Q4_K, kProjOneTokenWarps>(p, sm_count, stream)
+                        : launch_q8k<Q38_GGML_Q4_K, kProjConsumerWarps>(p, sm_count, stream);
+                break;
+            case Q38_GGML_Q5_K:
+                e = one ? launch_q8k<Q38_GGML_Q5_K, kProjOneTokenWarps>(p, sm_count, stream)
+                        : launch_q8k<Q38_GGML_Q5_K, kProjConsumerWarps>(p, sm_count, stream);
+                break;
+            case Q38_GGML_Q6_K:
+                e = one ? launch_q8k<Q38_GGML_Q6_K, kProjOneTokenWarps>(p, sm_count, stream)
+                        : launch_q8k<Q38_GGML_Q6_K, kProjConsumerWarps>(p, sm_count, stream);
+                break;
             default: return cudaErrorInvalidValue;
         }
         if (e != cudaSuccess) return e;

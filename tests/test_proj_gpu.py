@@ -60,7 +60,9 @@ def test_quantize_q8_k_bitwise(cuda_ctx, oracle_lib):
 K_CASES = [(12, 10240, HIDDEN), (13, 6144, HIDDEN), (14, 1000, HIDDEN), (12, 48, HIDDEN),
            (14, HIDDEN, 6144), (11, 300, HIDDEN), (10, 300, HIDDEN), (13, 37, 6144),
            # one and two 256-blocks per row: the pipelines' first / last stages coincide
-           (12, 130, 256), (14, 200, 512), (13, 129, 768)]
+           (12, 130, 256), (14, 200, 512), (13, 129, 768),
+           # more than 32 blocks per row: one token takes the general (8-warp) form
+           (12, 64, 9216), (14, 40, 8448)]
 
 
 @pytest.mark.parametrize("ggml_type,rows,width", K_CASES)
