@@ -21,6 +21,9 @@ flush is needed between steps.
   cpu_baseline  the CPU oracle (a restatement of the reference's Rust cores,
          threaded over heads like its rayon regions) on a bounded sample of the
          same workload, rank 0 at N=1 only.
+  projection  the quantized projections around a DeltaNet core (12 layers'
+         weights, one CUDA graph) at batch 1 and the decode batch, with the
+         oracle's projection path timed beside them (projection.cpu_baseline).
 
 --impl reference runs only the CPU oracle (the reference's algorithm; the
 Rust crate itself cannot be built here), rank 0 only.
@@ -456,6 +459,41 @@ class CpuWorkload:
         self.pos += 1
 
 
+def cpu_projection_baseline(args, batches) -> dict:
+    """The projection leg's CPU side: the oracle's quantize_q8_k + integer dots
+    (the reference's project / batch_project path, threaded over rows like its
+    row-parallel gemm) for one DeltaNet layer's five projections, repeated for
+    about `cpu_seconds` / 4 per batch size."""
+    sys.path.insert(0, str(REPO / "oracle"))
+    import oracle
+    from q38attn import synth
+    oracle.build()
+    oracle.set_threads(os.cpu_count() or 1)
+    g = synth.rng(args.seed + 2000)
+    ws = {k: (t, w, r, synth.quant_weight(g, t, r, w)) for k, (t, w, r) in PROJ_SPEC.items()}
+    out = {}
+    for B in batches:
+        x, a = synth.normal(g, (B, 5120)), synth.normal(g, (B, 6144))
+
+        def layer():
+            for k, (t, w, r, d) in ws.items():
+                oracle.project(t, d, r, w, a if k == "out" else x)
+
+        layer()  # warm
+        t0, n = time.perf_counter(), 0
+        while True:
+            layer()
+            n += 1
+            if time.perf_counter() - t0 >= args.cpu_seconds / 4:
+                break
+        dt = time.perf_counter() - t0
+        out[f"batch{B}"] = {"ms_per_layer": dt / n * 1e3, "sample": f"{n} layers, {dt:.1f} s"}
+    out.update({"unit": "ms per layer", "cores": oracle.get_threads(), "kind": "port",
+                "what": "C++ restatement of quantize_q8_k and the dot_q*_k_q8_k / f32 dots "
+                        "(bit-identical outputs), OpenMP over rows"})
+    return out
+
+
 def cpu_baseline(args) -> dict:
     w = CpuWorkload(args.context, args.seed)
     w.token()  # warm
@@ -691,6 +729,8 @@ def run_ours(args) -> None:
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         cpu = cpu_baseline(args)
+        if proj:
+            proj["cpu_baseline"] = cpu_projection_baseline(args, sorted({1, args.batch}))
 
     if rank == 0:
         step_ms = ms / args.steps
