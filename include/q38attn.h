@@ -364,10 +364,12 @@ int q38_full_core(q38_ctx *ctx, q38_state *st, int layer, const float *q_and_gat
 /* ------------------------------------------- projections around the cores */
 
 /* ggml tensor types the projections accept (src/gguf/mod.rs:83-103). The
- * K-quants take the integer path of the reference's `project`
- * (matrix_type_q8_k, src/model/ops.rs:105-120): the f32 activation is
- * quantized to Q8_K blocks and dotted in integers; the others take the f32
- * activation directly. The IQ types the reference also reads are not
+ * K-quants and IQ4_NL / IQ4_XS take the integer path of the reference's
+ * `project` (matrix_type_q8_k, src/model/ops.rs:105-120): the f32 activation
+ * is quantized to Q8_K blocks and dotted in integers (src/kernel/tensor.rs:
+ * 301-460, src/kernel/iq.rs:355-405); the others take the f32 activation
+ * directly. The reference's other IQ types (IQ1_S, IQ1_M, IQ2_XXS, IQ2_XS,
+ * IQ2_S, IQ3_XXS, IQ3_S), which decode through ggml's lookup grids, are not
  * accepted here (Q38_ERR_ARG). */
 #define Q38_GGML_F32 0
 #define Q38_GGML_F16 1
@@ -377,6 +379,8 @@ int q38_full_core(q38_ctx *ctx, q38_state *st, int layer, const float *q_and_gat
 #define Q38_GGML_Q4_K 12
 #define Q38_GGML_Q5_K 13
 #define Q38_GGML_Q6_K 14
+#define Q38_GGML_IQ4_NL 20
+#define Q38_GGML_IQ4_XS 23
 #define Q38_GGML_BF16 30
 
 /* Bytes of one Q8_K activation block in the reference's layout
@@ -390,7 +394,7 @@ typedef struct q38_weight q38_weight;
  * each, the GGUF tensor of shape [width, rows] (TensorEntry, whose rows are
  * row_bytes(type, width) bytes, src/kernel/tensor.rs:46-53). data is a HOST
  * pointer to exactly rows * row_bytes bytes (nbytes). width must be a
- * multiple of 4 (of 256 for the K-quants) and at most 32768; the model's
+ * multiple of 4 (of 256 for the integer-path types) and at most 32768; the model's
  * projections are 5120 and 6144 wide. */
 int q38_weight_create(q38_ctx *ctx, int ggml_type, int64_t width, int64_t rows, const void *data,
                       size_t nbytes, q38_weight **out);

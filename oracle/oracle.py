@@ -184,6 +184,7 @@ def round_bf16(x: float) -> float:
 # ---------------------------------------------------------------------------
 GGML_F32, GGML_F16, GGML_Q8_0, GGML_BF16 = 0, 1, 8, 30
 GGML_Q2_K, GGML_Q3_K, GGML_Q4_K, GGML_Q5_K, GGML_Q6_K = 10, 11, 12, 13, 14
+GGML_IQ4_NL, GGML_IQ4_XS = 20, 23
 
 # Q38Q8KBlock (src/kernel/mod.rs:20-27), 292 bytes.
 Q8K_BLOCK = np.dtype([("scale", "<f4"), ("quants", "i1", (256,)), ("sums", "<i2", (16,))])

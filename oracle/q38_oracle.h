@@ -138,7 +138,8 @@ int q38o_full_prefill_rows(const float *q_norm, const float *k_norm, const float
 /*
  * Projections on either side of the cores (q38_oracle_proj.cpp): the Q8_K
  * activation quantizer (src/kernel/quant.rs:56-124), the integer dots of the
- * K-quant types against it (src/kernel/tensor.rs:301-460), the f32-input dots
+ * K-quant types against it (src/kernel/tensor.rs:301-460) and of IQ4_NL /
+ * IQ4_XS (src/kernel/iq.rs:355-405; their f32 path iq.rs:311-335), the f32-input dots
  * (tensor.rs:79-117), the row loops with token-major output
  * (tensor.rs:954-1027) and project / batch_project (src/model/ops.rs:617-640,
  * 1016-1031). Weights are raw GGUF tensor bytes, rows of row_bytes(type,
@@ -153,6 +154,8 @@ int q38o_full_prefill_rows(const float *q_norm, const float *k_norm, const float
 #define Q38O_GGML_Q5_K 13
 #define Q38O_GGML_Q6_K 14
 #define Q38O_GGML_BF16 30
+#define Q38O_GGML_IQ4_NL 20
+#define Q38O_GGML_IQ4_XS 23
 
 /* Q38Q8KBlock, src/kernel/mod.rs:20-27: 292 bytes. */
 typedef struct {

@@ -9,6 +9,9 @@
 //   src/kernel/tensor.rs:46-53    row_bytes
 //   src/kernel/tensor.rs:79-117   dot_{f32,f16,bf16,q8_0}_scalar (the f32-input path)
 //   src/kernel/tensor.rs:301-460  dot_q{2,3,4,5,6}_k_q8_k_scalar (the integer path)
+//   src/kernel/iq.rs:96-135, 311-335, 355-405  IQ4_NL / IQ4_XS: group layout,
+//                                 f32 decode + fma dot, integer dots
+//   src/kernel/iq_tables.rs:52-56 kvalues_iq4nl
 //   src/kernel/tensor.rs:954-1027 gemv_rows / gemm_rows (token-major output)
 //   src/model/ops.rs:105-120      matrix_type_q8_k (which weights take the integer path)
 //   src/model/ops.rs:617-640      quantize_input / project
@@ -302,6 +305,95 @@ float dot_q6_k(const uint8_t *data, const q38o_q8k_block *q, size_t blocks) {
     return total;
 }
 
+// ---- IQ4_NL / IQ4_XS, src/kernel/iq.rs -------------------------------------
+// Both map a 4-bit index to one of 16 signed values (kvalues_iq4nl,
+// iq_tables.rs:52-56: the format's own table, kept as it is). Within a
+// 32-value group, byte i holds value i in its low nibble and value i + 16 in
+// its high nibble.
+constexpr int8_t kIq4Values[16] = {-127, -104, -83, -65, -49, -35, -22, -10,
+                                   1,    13,   25,  38,  53,  69,  89,  113};
+constexpr size_t kIq4NlSuper = 144;  // eight 18-byte IQ4_NL blocks per 256 values
+constexpr size_t kIq4XsBlock = 136;
+
+// IQ4_XS group scale (iq.rs:392-393): 4 bits from scales_l, 2 from scales_h.
+inline int iq4_xs_scale(const uint8_t *blk, int g) {
+    const uint16_t high = rd16(blk + 2);
+    return ((blk[4 + g / 2] >> (4 * (g % 2))) & 15) | (((high >> (2 * g)) & 3) << 4);
+}
+
+// dot_iq4_nl_q8_k, iq.rs:355-377: per 32-value group an f16 scale and 16
+// nibble bytes; every group adds its own term d * weighted to the total.
+float dot_iq4_nl(const uint8_t *data, const q38o_q8k_block *q, size_t blocks) {
+    float total = 0.0f;
+    for (size_t b = 0; b < blocks; ++b)
+        for (int g = 0; g < 8; ++g) {
+            const uint8_t *grp = data + b * kIq4NlSuper + g * 18;
+            const float d = f16_to_f32(rd16(grp)) * q[b].scale;
+            int32_t weighted = 0;
+            for (int i = 0; i < 16; ++i) {
+                weighted += q[b].quants[g * 32 + i] * kIq4Values[grp[2 + i] & 15];
+                weighted += q[b].quants[g * 32 + i + 16] * kIq4Values[grp[2 + i] >> 4];
+            }
+            total += d * float(weighted);
+        }
+    return total;
+}
+
+// dot_iq4_xs_q8_k, iq.rs:379-405: 136 bytes (d | scales_h | scales_l[4] |
+// 128 nibble bytes); the group sums weighted by (scale - 32), one term per
+// block.
+float dot_iq4_xs(const uint8_t *data, const q38o_q8k_block *q, size_t blocks) {
+    float total = 0.0f;
+    for (size_t b = 0; b < blocks; ++b) {
+        const uint8_t *blk = data + b * kIq4XsBlock;
+        const float d = f16_to_f32(rd16(blk)) * q[b].scale;
+        int32_t weighted = 0;
+        for (int g = 0; g < 8; ++g) {
+            int32_t sub = 0;
+            for (int i = 0; i < 16; ++i) {
+                const uint8_t packed = blk[8 + 16 * g + i];
+                sub += q[b].quants[g * 32 + i] * kIq4Values[packed & 15];
+                sub += q[b].quants[g * 32 + i + 16] * kIq4Values[packed >> 4];
+            }
+            weighted += (iq4_xs_scale(blk, g) - 32) * sub;
+        }
+        total += d * float(weighted);
+    }
+    return total;
+}
+
+// dequant_block (iq.rs:109-135) of one 256-value unit, then dot_row_f32
+// (iq.rs:311-335): an fma chain over the decoded values in element order.
+float dot_iq4_f32(int type, const uint8_t *data, const float *x, size_t n) {
+    float total = 0.0f;
+    float v[256];
+    for (size_t base = 0, b = 0; base < n; base += 256, ++b) {
+        if (type == Q38O_GGML_IQ4_NL) {
+            for (int g = 0; g < 8; ++g) {
+                const uint8_t *grp = data + b * kIq4NlSuper + g * 18;
+                const float d = f16_to_f32(rd16(grp));
+                for (int i = 0; i < 16; ++i) {
+                    v[g * 32 + i] = d * float(kIq4Values[grp[2 + i] & 15]);
+                    v[g * 32 + i + 16] = d * float(kIq4Values[grp[2 + i] >> 4]);
+                }
+            }
+        } else {
+            const uint8_t *blk = data + b * kIq4XsBlock;
+            const float d = f16_to_f32(rd16(blk));
+            for (int g = 0; g < 8; ++g) {
+                const float ds = d * float(iq4_xs_scale(blk, g) - 32);
+                for (int i = 0; i < 16; ++i) {
+                    const uint8_t packed = blk[8 + 16 * g + i];
+                    v[g * 32 + i] = ds * float(kIq4Values[packed & 15]);
+                    v[g * 32 + i + 16] = ds * float(kIq4Values[packed >> 4]);
+                }
+            }
+        }
+        for (int i = 0; i < 256; ++i) total = std::fmaf(v[i], x[base + i], total);
+    }
+    return total;
+}
+
 bool parallel_rows(size_t rows, size_t per_row) {
     // q38_parallel_over, src/kernel/mod.rs:15-17 (the result does not depend
     // on it: every output is the same dot on the same bytes).
@@ -316,7 +408,8 @@ float q38o_f16_to_f32(uint16_t h) { return f16_to_f32(h); }
 
 int q38o_is_q8k_type(int type) {
     return type == Q38O_GGML_Q2_K || type == Q38O_GGML_Q3_K || type == Q38O_GGML_Q4_K ||
-           type == Q38O_GGML_Q5_K || type == Q38O_GGML_Q6_K;
+           type == Q38O_GGML_Q5_K || type == Q38O_GGML_Q6_K || type == Q38O_GGML_IQ4_NL ||
+           type == Q38O_GGML_IQ4_XS;
 }
 
 int q38o_row_bytes(int type, size_t width, size_t *out) {
@@ -331,6 +424,8 @@ int q38o_row_bytes(int type, size_t width, size_t *out) {
         case Q38O_GGML_Q4_K: elems = 256; bytes = 144; break;
         case Q38O_GGML_Q5_K: elems = 256; bytes = 176; break;
         case Q38O_GGML_Q6_K: elems = 256; bytes = 210; break;
+        case Q38O_GGML_IQ4_NL: elems = 32; bytes = 18; break;
+        case Q38O_GGML_IQ4_XS: elems = 256; bytes = 136; break;
         default: return -1;
     }
     if (width % elems) return -1;
@@ -352,6 +447,9 @@ float q38o_dot_row_f32(int type, const uint8_t *row, const float *x, size_t widt
         case Q38O_GGML_F16: return dot_f16(row, x, width);
         case Q38O_GGML_BF16: return dot_bf16(row, x, width);
         case Q38O_GGML_Q8_0: return dot_q8_0(row, x, width);
+        // The IQ kernels step over 256-value units (iq.rs:43-61).
+        case Q38O_GGML_IQ4_NL:
+        case Q38O_GGML_IQ4_XS: return width % kBlock ? NAN : dot_iq4_f32(type, row, x, width);
         default: return NAN;
     }
 }
@@ -363,6 +461,8 @@ float q38o_dot_row_q8_k(int type, const uint8_t *row, const q38o_q8k_block *q, s
         case Q38O_GGML_Q4_K: return dot_q4_k(row, q, blocks);
         case Q38O_GGML_Q5_K: return dot_q5_k(row, q, blocks);
         case Q38O_GGML_Q6_K: return dot_q6_k(row, q, blocks);
+        case Q38O_GGML_IQ4_NL: return dot_iq4_nl(row, q, blocks);
+        case Q38O_GGML_IQ4_XS: return dot_iq4_xs(row, q, blocks);
         default: return NAN;
     }
 }

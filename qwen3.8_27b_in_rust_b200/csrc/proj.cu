@@ -3,8 +3,9 @@
 // The reference feeds every attention core from `project` (src/model/ops.rs:
 // 623-640; batch_project, :1016-1031): the f32 activation is quantized once to
 // Q8_K blocks (quantize_q8_k, src/kernel/quant.rs:56-124) and each K-quant
-// weight row (Q2_K..Q6_K) is dotted with it in integers
-// (dot_q*_k_q8_k_scalar, src/kernel/tensor.rs:301-460); F32 / F16 / BF16 /
+// weight row (Q2_K..Q6_K, IQ4_NL, IQ4_XS) is dotted with it in integers
+// (dot_q*_k_q8_k_scalar, src/kernel/tensor.rs:301-460; dot_iq4_*_q8_k,
+// src/kernel/iq.rs:355-405); F32 / F16 / BF16 /
 // Q8_0 weights take the f32 activation directly (tensor.rs:79-117). Outputs
 // are token-major, output[token * rows + row] (gemm_rows, tensor.rs:978-1000).
 //
@@ -335,12 +336,118 @@ struct BlockQ2K {
     }
 };
 
+// ---- IQ4_NL / IQ4_XS (src/kernel/iq.rs:355-405) ----------------------------
+// A 4-bit index selects one of 16 signed values (kvalues_iq4nl,
+// src/kernel/iq_tables.rs:52-56: the format's own table). Within a 32-value
+// group, byte i holds value i in its low nibble and value i + 16 in its high
+// nibble.
+constexpr int8_t kIq4Values[16] = {-127, -104, -83, -65, -49, -35, -22, -10, 1, 13, 25, 38, 53, 69, 89, 113};
+__host__ __device__ constexpr uint32_t iq4_word(int k) {
+    return uint32_t(uint8_t(kIq4Values[4 * k])) | (uint32_t(uint8_t(kIq4Values[4 * k + 1])) << 8) |
+           (uint32_t(uint8_t(kIq4Values[4 * k + 2])) << 16) | (uint32_t(uint8_t(kIq4Values[4 * k + 3])) << 24);
+}
+
+// The table values of four indices (bits 0-3 of each byte of idx), packed as
+// four signed bytes: two byte permutes over the table's halves pick by the low
+// three bits, bit 3 chooses between them.
+__device__ __forceinline__ uint32_t iq4_values4(uint32_t idx) {
+    uint32_t x = idx & 0x07070707u;
+    x = (x | (x >> 4)) & 0x00ff00ffu;
+    const uint32_t sel = (x | (x >> 8)) & 0xffffu;  // one 3-bit selector per nibble
+    const uint32_t lo = __byte_perm(iq4_word(0), iq4_word(1), sel);
+    const uint32_t hi = __byte_perm(iq4_word(2), iq4_word(3), sel);
+    const uint32_t m = ((idx >> 3) & 0x01010101u) * 0xffu;
+    return (hi & m) | (lo & ~m);
+}
+
+// The integer sum of one 32-value group: 4 nibble words against its 32
+// activation quants (low nibbles with a[0..15], high with a[16..31]).
+__device__ __forceinline__ int iq4_group_sum(const uint32_t *q, const uint8_t *a) {
+    const uint4 lo = ld128(a), hi = ld128(a + 16);
+    const uint32_t lw[4] = {lo.x, lo.y, lo.z, lo.w}, hw[4] = {hi.x, hi.y, hi.z, hi.w};
+    int s = 0;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        s = __dp4a(int(iq4_values4(q[k] & kNibbles)), int(lw[k]), s);
+        s = __dp4a(int(iq4_values4((q[k] >> 4) & kNibbles)), int(hw[k]), s);
+    }
+    return s;
+}
+
+// dot_iq4_xs_q8_k, iq.rs:379-405. 136 bytes (8-byte aligned): d | scales_h |
+// scales_l[4] | 128 nibble bytes; group g's scale is 4 bits of scales_l and 2
+// of scales_h, minus 32; one term per block.
+struct BlockIQ4XS {
+    uint32_t q[32];
+    uint32_t dsh, sl;  // d | scales_h << 16, scales_l
+    __device__ __forceinline__ void load(const uint8_t *w) {
+        const uint2 h = *reinterpret_cast<const uint2 *>(w);
+        dsh = h.x, sl = h.y;
+#pragma unroll
+        for (int k = 0; k < 16; ++k) {
+            const uint2 v = *reinterpret_cast<const uint2 *>(w + 8 + 8 * k);
+            q[2 * k] = v.x, q[2 * k + 1] = v.y;
+        }
+    }
+    __device__ __forceinline__ float term(const uint8_t *a, const int16_t *, float as) const {
+        int weighted = 0;
+#pragma unroll
+        for (int g = 0; g < 8; ++g) {
+            const int scale = int((sl >> (4 * g)) & 15u) | int(((dsh >> (16 + 2 * g)) & 3u) << 4);
+            weighted += (scale - 32) * iq4_group_sum(q + 4 * g, a + 32 * g);
+        }
+        const float d = half_to_float(dsh) * as;
+        return d * float(weighted);
+    }
+};
+
+// dot_iq4_nl_q8_k, iq.rs:355-377. Eight 18-byte blocks per 256 values (a
+// 144-byte unit; groups 2-byte aligned): an f16 scale and 16 nibble bytes per
+// 32-value group, and one term per GROUP added to the running total, so a
+// 256-value unit yields eight terms in order (terms()).
+struct BlockIQ4NL {
+    uint32_t q[32];
+    uint32_t d16[8];
+    __device__ __forceinline__ void load(const uint8_t *w) {
+#pragma unroll
+        for (int g = 0; g < 8; ++g) {
+            d16[g] = *reinterpret_cast<const uint16_t *>(w + 18 * g);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) q[4 * g + k] = ld32_a2(w + 18 * g + 2 + 4 * k);
+        }
+    }
+    __device__ __forceinline__ void terms(const uint8_t *a, const int16_t *, float as, float *dst) const {
+#pragma unroll
+        for (int g = 0; g < 8; ++g) {
+            const float d = half_to_float(d16[g]) * as;
+            dst[g] = d * float(iq4_group_sum(q + 4 * g, a + 32 * g));
+        }
+    }
+};
+
 template <int T> struct BlockOf;
 template <> struct BlockOf<Q38_GGML_Q2_K> { using type = BlockQ2K; };
 template <> struct BlockOf<Q38_GGML_Q3_K> { using type = BlockQ3K; };
 template <> struct BlockOf<Q38_GGML_Q4_K> { using type = BlockQ4K; };
 template <> struct BlockOf<Q38_GGML_Q5_K> { using type = BlockQ5K; };
 template <> struct BlockOf<Q38_GGML_Q6_K> { using type = BlockQ6K; };
+template <> struct BlockOf<Q38_GGML_IQ4_NL> { using type = BlockIQ4NL; };
+template <> struct BlockOf<Q38_GGML_IQ4_XS> { using type = BlockIQ4XS; };
+
+// f32 terms a 256-value unit adds to a row's running total: one, or eight for
+// IQ4_NL (a term per 32-value group).
+template <int T> constexpr int kTermsPerBlock = T == Q38_GGML_IQ4_NL ? 8 : 1;
+__host__ __device__ inline int proj_terms_per_block(int type) { return type == Q38_GGML_IQ4_NL ? 8 : 1; }
+
+// A unit's terms into dst[0 .. kTermsPerBlock<T>).
+template <int T, class B>
+__device__ __forceinline__ void block_terms(const B &blk, const uint8_t *a, const int16_t *sums, float as,
+                                            float *dst) {
+    if constexpr (kTermsPerBlock<T> == 1)
+        dst[0] = blk.term(a, sums, as);
+    else
+        blk.terms(a, sums, as, dst);
+}
 
 template <int T> constexpr int kBlockBytes = 0;
 template <> constexpr int kBlockBytes<Q38_GGML_Q2_K> = 84;
@@ -348,6 +455,8 @@ template <> constexpr int kBlockBytes<Q38_GGML_Q3_K> = 110;
 template <> constexpr int kBlockBytes<Q38_GGML_Q4_K> = 144;
 template <> constexpr int kBlockBytes<Q38_GGML_Q5_K> = 176;
 template <> constexpr int kBlockBytes<Q38_GGML_Q6_K> = kQ6KDeviceBlock;  // padded on upload
+template <> constexpr int kBlockBytes<Q38_GGML_IQ4_NL> = 144;            // eight 18-byte blocks
+template <> constexpr int kBlockBytes<Q38_GGML_IQ4_XS> = 136;
 
 // ---------------------------------------------------------------------------
 // Q8_K quantization, one warp per 256-value block (quant.rs:56-96).
@@ -500,14 +609,14 @@ __device__ __forceinline__ float ordered_sum32(const float *v, int n) {
 }
 
 __host__ __device__ inline ProjSmem proj_smem_plan(int stages, uint32_t tile_bytes, int batch, int nblk,
-                                                   int warps) {
+                                                   int warps, int terms) {
     ProjSmem s{};
     s.ring = 0;
     s.act_q = stages * tile_bytes;
     s.act_d = s.act_q + uint32_t(batch * nblk * kActStride);
     s.act_s = (s.act_d + uint32_t(batch * nblk * 4) + 15u) & ~15u;  // 16-byte loads of the sums
     s.vt = s.act_s + uint32_t(batch * nblk * 32);
-    s.total = s.vt + uint32_t(warps * proj_vt_stride(batch, nblk) * 4);
+    s.total = s.vt + uint32_t(warps * proj_vt_stride(batch, nblk * terms) * 4);
     return s;
 }
 
@@ -523,7 +632,9 @@ __global__ void __launch_bounds__(32 * (W + 1), 1) proj_q8k_kernel(ProjQ8KParams
     extern __shared__ __align__(128) unsigned char smem[];
     __shared__ __align__(8) uint64_t full[kMaxStages], empty[kMaxStages];
     __shared__ volatile int abort_flag;
-    const ProjSmem lay = proj_smem_plan(p.stages, p.tile_bytes, p.batch, p.nblk, W);
+    constexpr int kT = kTermsPerBlock<T>;
+    const int nterms = p.nblk * kT;  // f32 terms per (row, token)
+    const ProjSmem lay = proj_smem_plan(p.stages, p.tile_bytes, p.batch, p.nblk, W, kT);
     const uint8_t *aq = smem + lay.act_q;
     float *ad = reinterpret_cast<float *>(smem + lay.act_d);
     int16_t *asums = reinterpret_cast<int16_t *>(smem + lay.act_s);
@@ -603,7 +714,7 @@ __global__ void __launch_bounds__(32 * (W + 1), 1) proj_q8k_kernel(ProjQ8KParams
     }
 
     // ------------------------------------------------------------ consumers
-    float *vt = reinterpret_cast<float *>(smem + lay.vt) + warp * proj_vt_stride(p.batch, p.nblk);
+    float *vt = reinterpret_cast<float *>(smem + lay.vt) + warp * proj_vt_stride(p.batch, nterms);
     int k = 0;
     for (int tile = blockIdx.x; tile < p.ntiles; tile += gridDim.x, ++k) {
         const int s = k % p.stages;
@@ -621,17 +732,33 @@ __global__ void __launch_bounds__(32 * (W + 1), 1) proj_q8k_kernel(ProjQ8KParams
             if (row >= p.rows) break;  // rows ascend with r
             if constexpr (W == kProjOneTokenWarps) {
                 // One token, one block per lane: the block terms staged in
-                // the warp's buffer, where lane 0 reads all 32 at once and
-                // adds the first nblk in block order (only the adds are serial).
-                float v = 0.f;
-                if (lane < p.nblk) {
-                    typename BlockOf<T>::type blk;
-                    blk.load(tw + size_t(r) * p.rb + size_t(lane) * kBlockBytes<T>);
-                    v = blk.term(aq + lane * kActStride, asums + lane * 16, ad[lane]);
+                // the warp's buffer, where lane 0 reads them with vector
+                // loads and adds them in block order (only the adds are
+                // serial).
+                if constexpr (kT == 1) {
+                    float v = 0.f;
+                    if (lane < p.nblk) {
+                        typename BlockOf<T>::type blk;
+                        blk.load(tw + size_t(r) * p.rb + size_t(lane) * kBlockBytes<T>);
+                        v = blk.term(aq + lane * kActStride, asums + lane * 16, ad[lane]);
+                    }
+                    vt[lane] = v;
+                    __syncwarp();
+                    if (lane == 0) p.out[row] = ordered_sum32(vt, p.nblk);
+                } else {
+                    if (lane < p.nblk) {
+                        typename BlockOf<T>::type blk;
+                        blk.load(tw + size_t(r) * p.rb + size_t(lane) * kBlockBytes<T>);
+                        blk.terms(aq + lane * kActStride, asums + lane * 16, ad[lane], vt + lane * kT);
+                    }
+                    __syncwarp();
+                    if (lane == 0) {
+                        float total = 0.f;
+#pragma unroll 8
+                        for (int i = 0; i < nterms; ++i) total = __fadd_rn(total, vt[i]);
+                        p.out[row] = total;
+                    }
                 }
-                vt[lane] = v;
-                __syncwarp();
-                if (lane == 0) p.out[row] = ordered_sum32(vt, p.nblk);
                 __syncwarp();
             } else {
                 for (int b = lane; b < p.nblk; b += 32) {
@@ -639,15 +766,16 @@ __global__ void __launch_bounds__(32 * (W + 1), 1) proj_q8k_kernel(ProjQ8KParams
                     blk.load(tw + size_t(r) * p.rb + size_t(b) * kBlockBytes<T>);
                     for (int t = 0; t < p.batch; ++t) {
                         const int ab = t * p.nblk + b;
-                        vt[t * (p.nblk + 1) + b] = blk.term(aq + ab * kActStride, asums + ab * 16, ad[ab]);
+                        block_terms<T>(blk, aq + ab * kActStride, asums + ab * 16, ad[ab],
+                                       vt + t * (nterms + 1) + b * kT);
                     }
                 }
                 __syncwarp();
                 if (lane < p.batch) {
-                    const float *v = vt + lane * (p.nblk + 1);
+                    const float *v = vt + lane * (nterms + 1);
                     float total = 0.f;
 #pragma unroll 8
-                    for (int b = 0; b < p.nblk; ++b) total = __fadd_rn(total, v[b]);
+                    for (int i = 0; i < nterms; ++i) total = __fadd_rn(total, v[i]);
                     p.out[size_t(lane) * p.out_ld + row] = total;
                 }
                 __syncwarp();
@@ -759,7 +887,7 @@ __global__ void __launch_bounds__(256) proj_f32_kernel(ProjF32Params p) {
 
 template <int T, int W>
 cudaError_t launch_q8k(const ProjQ8KParams &p, int sm_count, cudaStream_t stream) {
-    const ProjSmem lay = proj_smem_plan(p.stages, p.tile_bytes, p.batch, p.nblk, W);
+    const ProjSmem lay = proj_smem_plan(p.stages, p.tile_bytes, p.batch, p.nblk, W, kTermsPerBlock<T>);
     // The attribute is set once per device to the budget, so later launches
     // make no extra driver calls (and can be captured in a graph).
     static bool attr_set[kMaxDevices] = {};
@@ -819,7 +947,8 @@ cudaError_t launch_f32(const ProjF32Params &p, cudaStream_t stream) {
 
 bool proj_is_q8k_type(int type) {
     return type == Q38_GGML_Q2_K || type == Q38_GGML_Q3_K || type == Q38_GGML_Q4_K ||
-           type == Q38_GGML_Q5_K || type == Q38_GGML_Q6_K;
+           type == Q38_GGML_Q5_K || type == Q38_GGML_Q6_K || type == Q38_GGML_IQ4_NL ||
+           type == Q38_GGML_IQ4_XS;
 }
 
 bool proj_type_supported(int type) {
@@ -839,6 +968,8 @@ int64_t proj_row_bytes(int type, int64_t width) {
         case Q38_GGML_Q4_K: el = 256; by = 144; break;
         case Q38_GGML_Q5_K: el = 256; by = 176; break;
         case Q38_GGML_Q6_K: el = 256; by = 210; break;
+        case Q38_GGML_IQ4_NL: el = 32; by = 18; break;
+        case Q38_GGML_IQ4_XS: el = 256; by = 136; break;
         default: return -1;
     }
     if (width <= 0 || width % el) return -1;
@@ -880,7 +1011,8 @@ cudaError_t launch_proj_q8k(const ProjWeight &w, const float *x, int batch, floa
     // stages fit.
     const bool one_token = batch == 1 && nblk <= 32;
     p.tile_rows = kProjTileRows;
-    if (proj_smem_plan(0, 16u * rb, 1, nblk, kProjConsumerWarps).total + (one_token ? 2u : 3u) * 16u * rb >
+    const int terms = proj_terms_per_block(w.type);
+    if (proj_smem_plan(0, 16u * rb, 1, nblk, kProjConsumerWarps, terms).total + (one_token ? 2u : 3u) * 16u * rb >
         kProjSmemBudget)
         p.tile_rows = 8;
     p.ntiles = int((w.rows + p.tile_rows - 1) / p.tile_rows);
@@ -889,7 +1021,8 @@ cudaError_t launch_proj_q8k(const ProjWeight &w, const float *x, int batch, floa
     // leave room for less than two weight stages (wide Q6_K rows).
     int per = kProjMaxTok;
     while (per > 1 &&
-           proj_smem_plan(0, p.tile_bytes, per, nblk, kProjConsumerWarps).total + 2 * p.tile_bytes > kProjSmemBudget)
+           proj_smem_plan(0, p.tile_bytes, per, nblk, kProjConsumerWarps, terms).total + 2 * p.tile_bytes >
+               kProjSmemBudget)
         --per;
     for (int t0 = 0; t0 < batch; t0 += per) {
         p.batch = std::min(per, batch - t0);
@@ -899,7 +1032,8 @@ cudaError_t launch_proj_q8k(const ProjWeight &w, const float *x, int batch, floa
         // One token over rows of up to 32 blocks: the 16-warp form.
         const bool one = p.batch == 1 && nblk <= 32;
         const uint32_t fixed =
-            proj_smem_plan(0, p.tile_bytes, p.batch, nblk, one ? kProjOneTokenWarps : kProjConsumerWarps).total;
+            proj_smem_plan(0, p.tile_bytes, p.batch, nblk, one ? kProjOneTokenWarps : kProjConsumerWarps, terms)
+                .total;
         int stages = int((kProjSmemBudget - fixed) / p.tile_bytes);
         stages = std::min(stages, kMaxStages);
         if (stages < 2) return cudaErrorInvalidValue;
@@ -925,6 +1059,14 @@ cudaError_t launch_proj_q8k(const ProjWeight &w, const float *x, int batch, floa
             case Q38_GGML_Q6_K:
                 e = one ? launch_q8k<Q38_GGML_Q6_K, kProjOneTokenWarps>(p, sm_count, stream)
                         : launch_q8k<Q38_GGML_Q6_K, kProjConsumerWarps>(p, sm_count, stream);
+                break;
+            case Q38_GGML_IQ4_NL:
+                e = one ? launch_q8k<Q38_GGML_IQ4_NL, kProjOneTokenWarps>(p, sm_count, stream)
+                        : launch_q8k<Q38_GGML_IQ4_NL, kProjConsumerWarps>(p, sm_count, stream);
+                break;
+            case Q38_GGML_IQ4_XS:
+                e = one ? launch_q8k<Q38_GGML_IQ4_XS, kProjOneTokenWarps>(p, sm_count, stream)
+                        : launch_q8k<Q38_GGML_IQ4_XS, kProjConsumerWarps>(p, sm_count, stream);
                 break;
             default: return cudaErrorInvalidValue;
         }

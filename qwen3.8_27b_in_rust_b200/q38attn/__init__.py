@@ -31,8 +31,8 @@ import numpy as np
 
 from ._lib import (Q38_DEVERR_POSITION, Q38_DEVERR_SHAPE, Q38_DEVERR_TIMEOUT, Q38_ERR_ARG,
                    Q38_ERR_CUDA, Q38_ERR_TIMEOUT, Q38_GGML_BF16, Q38_GGML_F16, Q38_GGML_F32,
-                   Q38_GGML_Q2_K, Q38_GGML_Q3_K, Q38_GGML_Q4_K, Q38_GGML_Q5_K, Q38_GGML_Q6_K,
-                   Q38_GGML_Q8_0, Q38_KV_BF16, Q38_KV_F32, Q38_OK, Q38_Q8K_BLOCK_BYTES, Q38Error,
+                   Q38_GGML_IQ4_NL, Q38_GGML_IQ4_XS, Q38_GGML_Q2_K, Q38_GGML_Q3_K,
+                   Q38_GGML_Q4_K, Q38_GGML_Q5_K, Q38_GGML_Q6_K, Q38_GGML_Q8_0, Q38_KV_BF16, Q38_KV_F32, Q38_OK, Q38_Q8K_BLOCK_BYTES, Q38Error,
                    Q38Geom, check, last_error, load)
 
 __all__ = [
@@ -41,14 +41,16 @@ __all__ = [
     "Q38_DEVERR_POSITION", "Q38_DEVERR_TIMEOUT", "Q38_DEVERR_SHAPE",
     "is_full_attention", "full_index", "recurrent_index", "gguf_read_f32", "Weight",
     "Q38_GGML_F32", "Q38_GGML_F16", "Q38_GGML_BF16", "Q38_GGML_Q8_0", "Q38_GGML_Q2_K",
-    "Q38_GGML_Q3_K", "Q38_GGML_Q4_K", "Q38_GGML_Q5_K", "Q38_GGML_Q6_K", "Q38_Q8K_BLOCK_BYTES",
+    "Q38_GGML_Q3_K", "Q38_GGML_Q4_K", "Q38_GGML_Q5_K", "Q38_GGML_Q6_K", "Q38_GGML_IQ4_NL",
+    "Q38_GGML_IQ4_XS", "Q38_Q8K_BLOCK_BYTES",
     "row_bytes",
 ]
 
 # ggml (elements, bytes) per block of the projection types (src/gguf/mod.rs:136-178).
 _GGML_BLOCK = {Q38_GGML_F32: (1, 4), Q38_GGML_F16: (1, 2), Q38_GGML_BF16: (1, 2),
                Q38_GGML_Q8_0: (32, 34), Q38_GGML_Q2_K: (256, 84), Q38_GGML_Q3_K: (256, 110),
-               Q38_GGML_Q4_K: (256, 144), Q38_GGML_Q5_K: (256, 176), Q38_GGML_Q6_K: (256, 210)}
+               Q38_GGML_Q4_K: (256, 144), Q38_GGML_Q5_K: (256, 176), Q38_GGML_Q6_K: (256, 210),
+               Q38_GGML_IQ4_NL: (32, 18), Q38_GGML_IQ4_XS: (256, 136)}
 
 
 def row_bytes(ggml_type: int, width: int) -> int:

@@ -24,6 +24,7 @@ Q38_DEVERR_TIMEOUT = 2
 Q38_DEVERR_SHAPE = 4
 Q38_GGML_F32, Q38_GGML_F16, Q38_GGML_Q8_0, Q38_GGML_BF16 = 0, 1, 8, 30
 Q38_GGML_Q2_K, Q38_GGML_Q3_K, Q38_GGML_Q4_K, Q38_GGML_Q5_K, Q38_GGML_Q6_K = 10, 11, 12, 13, 14
+Q38_GGML_IQ4_NL, Q38_GGML_IQ4_XS = 20, 23
 Q38_Q8K_BLOCK_BYTES = 292
 
 

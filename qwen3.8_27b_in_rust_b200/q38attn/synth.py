@@ -97,7 +97,8 @@ def round_bf16(x: np.ndarray) -> np.ndarray:
 # Quant bits and packed scales are uniform random bytes; the f16 super-block
 # scales d / dmin are drawn so that a dequantized weight is of order 0.02
 # (d ~ U(0.5, 1.5) * 1e-4, dmin ~ U(0, 1) * 1e-4 for the K-quants, 3e-4 for
-# Q8_0), as in a
+# Q8_0 and IQ4_NL, 1e-5 for IQ4_XS, whose values are table entries up to 127
+# times a group scale up to 32; the last is an f16 subnormal), as in a
 # trained checkpoint. F32 / F16 / BF16 weights are N(0, 0.02^2).
 # ---------------------------------------------------------------------------
 _BLOCK_LAYOUT = {
@@ -108,7 +109,10 @@ _BLOCK_LAYOUT = {
     12: (256, 144, [(0, "d"), (2, "dmin")]),    # Q4_K
     13: (256, 176, [(0, "d"), (2, "dmin")]),    # Q5_K
     14: (256, 210, [(208, "d")]),               # Q6_K
+    20: (32, 18, [(0, "d")]),                   # IQ4_NL
+    23: (256, 136, [(0, "d")]),                 # IQ4_XS
 }
+_D_SCALE = {8: 3e-4, 20: 3e-4, 23: 1e-5}
 
 
 def quant_weight(g: np.random.Generator, ggml_type: int, rows: int, width: int) -> np.ndarray:
@@ -127,7 +131,7 @@ def quant_weight(g: np.random.Generator, ggml_type: int, rows: int, width: int) 
     raw = g.integers(0, 256, size=(nblk, by), dtype=np.uint8)
     for off, kind in scales:
         lo, hi = (0.5, 1.5) if kind == "d" else (0.0, 1.0)
-        scale = 1e-4 if ggml_type != 8 else 3e-4
+        scale = _D_SCALE.get(ggml_type, 1e-4)
         v = (g.uniform(lo, hi, nblk) * scale).astype(np.float16).view(np.uint16)
         raw[:, off] = (v & 0xff).astype(np.uint8)
         raw[:, off + 1] = (v >> 8).astype(np.uint8)

@@ -7,6 +7,9 @@ the oracle (oracle/q38_oracle_proj.cpp):
   type, from which the integer dot of dot_q*_k_q8_k_scalar
   (src/kernel/tensor.rs:301-460) is an exact int64 sum, and the f32 running
   total over blocks is replayed in float32;
+* the same for IQ4_XS and IQ4_NL (src/kernel/iq.rs:355-405): 4-bit indices
+  into the 16-value IQ4 table, a 6-bit group scale minus 32 (IQ4_XS, one term
+  per block) or an f16 scale per 32-value group (IQ4_NL, one term per group);
 * dequantized weights (d * scale * q - dmin * min), for the reference's own
   consistency bar between the integer path and a plain f32 dot
   (tensor.rs:604-700).
@@ -53,6 +56,23 @@ def _scale_min_k4(s: np.ndarray):
     sc[:, 4:] = (s[:, 8:12] & 15) | ((s[:, 0:4] >> 6) << 4)
     mn[:, 4:] = (s[:, 8:12] >> 4) | ((s[:, 4:8] >> 6) << 4)
     return sc, mn
+
+
+# The IQ4 format's 16 values (kvalues_iq4nl).
+IQ4_VALUES = np.array([-127, -104, -83, -65, -49, -35, -22, -10, 1, 13, 25, 38, 53, 69, 89, 113], np.int64)
+
+
+def _iq4_nibbles(qs: np.ndarray) -> np.ndarray:
+    """[n][16] group bytes -> [n][32] table values: byte i gives value i (low
+    nibble) and value i + 16 (high nibble)."""
+    return np.concatenate([IQ4_VALUES[qs & 15], IQ4_VALUES[qs >> 4]], axis=1)
+
+
+def decode_iq4_nl(raw: np.ndarray, nblk: int):
+    """Per 256 values: (q [nb][256], d [nb][8] f32 group scales)."""
+    g = raw.reshape(nblk * 8, 18).astype(np.int64)
+    d = f16(g[:, 0], g[:, 1]).reshape(nblk, 8)
+    return _iq4_nibbles(g[:, 2:]).reshape(nblk, 256), d
 
 
 def decode(ggml_type: int, raw: np.ndarray, nblk: int):
@@ -111,6 +131,14 @@ def decode(ggml_type: int, raw: np.ndarray, nblk: int):
                 se[:, seg.start:seg.start + 16] = sc[:, 2 * group:2 * group + 1]
                 se[:, seg.start + 16:seg.stop] = sc[:, 2 * group + 1:2 * group + 2]
         return q, se, mg, d, np.zeros_like(d)
+    if ggml_type == 23:  # IQ4_XS
+        d = f16(b[:, 0], b[:, 1])
+        high = b[:, 2] | (b[:, 3] << 8)
+        for grp in range(8):
+            low = (b[:, 4 + grp // 2] >> (4 * (grp % 2))) & 15
+            se[:, 32 * grp:32 * grp + 32] = (low | (((high >> (2 * grp)) & 3) << 4))[:, None] - 32
+            q[:, 32 * grp:32 * grp + 32] = _iq4_nibbles(b[:, 8 + 16 * grp:24 + 16 * grp])
+        return q, se, mg, d, np.zeros_like(d)
     if ggml_type == 10:  # Q2_K
         scales, qs = b[:, 0:16], b[:, 16:80]
         d, dmin = f16(b[:, 80], b[:, 81]), f16(b[:, 82], b[:, 83])
@@ -131,6 +159,14 @@ def decode(ggml_type: int, raw: np.ndarray, nblk: int):
 def dot_q8_k(ggml_type: int, row: np.ndarray, scale, quants, sums) -> np.float32:
     """The reference's integer dot of one weight row with Q8_K blocks."""
     nblk = quants.shape[0]
+    if ggml_type == 20:  # IQ4_NL: a term per 32-value group
+        q, d = decode_iq4_nl(row, nblk)
+        weighted = (q * quants.astype(np.int64)).reshape(nblk, 8, 32).sum(axis=2)
+        total = F32(0)
+        for blk in range(nblk):
+            for grp in range(8):
+                total = F32(total + F32(F32(d[blk, grp] * scale[blk]) * F32(weighted[blk, grp])))
+        return total
     q, se, mg, d, dmin = decode(ggml_type, row, nblk)
     weighted = (se * q * quants.astype(np.int64)).sum(axis=1)
     minimum = (mg * sums.astype(np.int64)).sum(axis=1)
@@ -156,6 +192,9 @@ def dequantize(ggml_type: int, raw: np.ndarray, rows: int, width: int) -> np.nda
         d = f16(b[:, 0], b[:, 1]).astype(np.float64)
         return (d[:, None] * b[:, 2:].view(np.int8)).reshape(rows, width)
     nblk = rows * width // 256
+    if ggml_type == 20:
+        q, d = decode_iq4_nl(raw, nblk)
+        return (np.repeat(d.astype(np.float64), 32, axis=1) * q).reshape(rows, width)
     q, se, mg, d, dmin = decode(ggml_type, raw, nblk)
     mins = np.repeat(mg, 16, axis=1)
     v = d.astype(np.float64)[:, None] * se * q - dmin.astype(np.float64)[:, None] * mins

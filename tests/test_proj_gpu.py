@@ -62,7 +62,10 @@ K_CASES = [(12, 10240, HIDDEN), (13, 6144, HIDDEN), (14, 1000, HIDDEN), (12, 48,
            # one and two 256-blocks per row: the pipelines' first / last stages coincide
            (12, 130, 256), (14, 200, 512), (13, 129, 768),
            # more than 32 blocks per row: one token takes the general (8-warp) form
-           (12, 64, 9216), (14, 40, 8448)]
+           (12, 64, 9216), (14, 40, 8448),
+           # IQ4_NL (a term per 32-value group) and IQ4_XS; odd block counts give
+           # IQ4_XS rows 8-byte aligned only
+           (20, 300, HIDDEN), (23, 300, HIDDEN), (23, 77, 2304), (23, 130, 256), (20, 64, 9216)]
 
 
 @pytest.mark.parametrize("ggml_type,rows,width", K_CASES)

@@ -6,9 +6,10 @@ checks of this code (src/kernel/tensor.rs:604-925):
   largest magnitude winning a tie, all-zero blocks and the reference's
   deterministic test activation ((i*7919) % 101) / 50 - 1;
 * f16_to_f32 (quant.rs:21-45) over all 65536 half values;
-* every K-quant integer dot bit for bit against the numpy restatement, and
-  within the reference's 0.05 of a plain dot over the dequantized row
-  (kernel_consistency, tensor.rs:604-700); the f32-input dots within 1e-3;
+* every K-quant and IQ4 integer dot bit for bit against the numpy
+  restatement, and within the reference's 0.05 of a plain dot over the
+  dequantized row (kernel_consistency, tensor.rs:604-700); the f32-input dots
+  (the IQ4 types' f32 path, iq.rs:311-335, included) within 1e-3;
 * token-major batched output equal to the per-row dots
   (gemv_and_gemm_match_serial_row_dot, tensor.rs:792-925).
 """
@@ -24,6 +25,7 @@ from q38attn import synth
 K_TYPES = [oracle.GGML_Q2_K, oracle.GGML_Q3_K, oracle.GGML_Q4_K, oracle.GGML_Q5_K,
            oracle.GGML_Q6_K]
 F_TYPES = [oracle.GGML_F32, oracle.GGML_F16, oracle.GGML_BF16, oracle.GGML_Q8_0]
+IQ_TYPES = [oracle.GGML_IQ4_NL, oracle.GGML_IQ4_XS]
 
 
 def reference_activation(width: int) -> np.ndarray:
@@ -80,7 +82,7 @@ def test_quantize_q8_k_rejects_ragged_length():
         oracle.quantize_q8_k(np.zeros(300, np.float32))
 
 
-@pytest.mark.parametrize("ggml_type", K_TYPES)
+@pytest.mark.parametrize("ggml_type", K_TYPES + IQ_TYPES)
 def test_integer_dot_matches_numpy_restatement(ggml_type):
     g = synth.rng(10 + ggml_type)
     rows, width = 6, 1024
@@ -96,7 +98,7 @@ def test_integer_dot_matches_numpy_restatement(ggml_type):
             assert np.float32(got).view(np.uint32) == np.float32(want).view(np.uint32), (r, got, want)
 
 
-@pytest.mark.parametrize("ggml_type", K_TYPES + F_TYPES)
+@pytest.mark.parametrize("ggml_type", K_TYPES + F_TYPES + IQ_TYPES)
 def test_kernel_consistency_against_dequantized_dot(ggml_type):
     """The reference's kernel_consistency bars (tensor.rs:604-700): the
     f32-input dot within 1e-3 and the integer dot within 0.05 of a plain dot
@@ -113,13 +115,13 @@ def test_kernel_consistency_against_dequantized_dot(ggml_type):
         if oracle.is_q8k_type(ggml_type):
             got = oracle.dot_row_q8_k(ggml_type, row, oracle.quantize_q8_k(x))
             assert relative(got, want) < 0.05
-        else:
+        if not oracle.is_q8k_type(ggml_type) or ggml_type in IQ_TYPES:
             got = oracle.dot_row_f32(ggml_type, row, x)
             assert relative(got, want) < 1e-3
 
 
 @pytest.mark.parametrize("ggml_type", [oracle.GGML_Q4_K, oracle.GGML_Q6_K, oracle.GGML_Q8_0,
-                                       oracle.GGML_BF16])
+                                       oracle.GGML_BF16, oracle.GGML_IQ4_NL, oracle.GGML_IQ4_XS])
 def test_batched_project_is_token_major_row_dots(ggml_type):
     """gemv_and_gemm_match_serial_row_dot (tensor.rs:792-925): every output
     [token * rows + row] is the single-row dot, bitwise; tokens are
@@ -146,6 +148,9 @@ def test_row_bytes_and_shape_errors():
     assert oracle.row_bytes(oracle.GGML_Q4_K, 5120) == 2880
     assert oracle.row_bytes(oracle.GGML_Q6_K, 5120) == 4200
     assert oracle.row_bytes(oracle.GGML_Q8_0, 5120) == 5440
+    assert oracle.row_bytes(oracle.GGML_IQ4_NL, 5120) == 2880
+    assert oracle.row_bytes(oracle.GGML_IQ4_XS, 5120) == 2720
+    assert oracle.is_q8k_type(oracle.GGML_IQ4_NL) and oracle.is_q8k_type(oracle.GGML_IQ4_XS)
     with pytest.raises(ValueError):
         oracle.row_bytes(oracle.GGML_Q4_K, 300)
     with pytest.raises(ValueError):
