@@ -144,7 +144,7 @@ __global__ void __launch_bounds__(kStateThreads) linear_decode_state_kernel(Stat
 
 }  // namespace
 
-cudaError_t launch_linear_decode(const LinearDecodeLaunch &a, cudaStream_t stream) {
+cudaError_t launch_linear_decode(const LinearDecodeLaunch &a, cudaStream_t stream, cudaEvent_t prep_done) {
     const int qkv_dim = (2 * a.qk_heads + a.v_heads) * kLinHeadDim;
     PrepParams pp{a.qkv,    a.beta,    a.alpha,     a.conv_state, a.conv_w, a.dt_bias,
                   a.ssm_a,  a.qk_heads, a.v_heads,  qkv_dim,      a.eps};
@@ -152,6 +152,9 @@ cudaError_t launch_linear_decode(const LinearDecodeLaunch &a, cudaStream_t strea
                                 stream>>>(pp);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
+    // With prep_done recorded between the two kernels, D2 is an ordinary
+    // launch (no programmatic overlap across the record).
+    if (prep_done && (e = cudaEventRecord(prep_done, stream)) != cudaSuccess) return e;
 
     StateParams sp{a.qkv,      a.z,        a.beta,    a.alpha,   a.delta_state,
                    a.ssm_norm, a.attention, a.qk_heads, a.v_heads, qkv_dim, a.eps};
@@ -164,7 +167,7 @@ cudaError_t launch_linear_decode(const LinearDecodeLaunch &a, cudaStream_t strea
     cfg.dynamicSmemBytes = 0;
     cfg.stream = stream;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = prep_done ? 0 : 1;
     return cudaLaunchKernelEx(&cfg, linear_decode_state_kernel, sp);
 }
 

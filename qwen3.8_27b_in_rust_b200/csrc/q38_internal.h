@@ -88,6 +88,10 @@ struct q38_state {
     float *layer_prefill = nullptr;
     size_t layer_prefill_tokens = 0;
     int32_t *stage_pos = nullptr;
+    // Host-pointer decode: a stream for the write-back copies that overlap the
+    // state kernel, and its events (created on first use).
+    cudaStream_t host_out = nullptr;
+    cudaEvent_t host_ev_prep = nullptr, host_ev_back = nullptr;
 };
 
 namespace q38 {
@@ -168,6 +172,8 @@ struct LinearDecodeLaunch {
     int batch, qk_heads, v_heads;
     float eps;
 };
-cudaError_t launch_linear_decode(const LinearDecodeLaunch &a, cudaStream_t stream);
+// prep_done (optional) is recorded once the prep kernel is done.
+cudaError_t launch_linear_decode(const LinearDecodeLaunch &a, cudaStream_t stream,
+                                 cudaEvent_t prep_done = nullptr);
 
 }  // namespace q38

@@ -171,6 +171,33 @@ void free_state(q38_state *st) {
     cudaFree(st->prefill_stage);
     cudaFree(st->ckpt_conv);
     cudaFree(st->ckpt_delta);
+    if (st->host_ev_prep) cudaEventDestroy(st->host_ev_prep);
+    if (st->host_ev_back) cudaEventDestroy(st->host_ev_back);
+    if (st->host_out) cudaStreamDestroy(st->host_out);
+}
+
+// The write-back stream and events of the host-pointer decode, created once
+// per state.
+cudaError_t ensure_host_out(q38_state *st) {
+    if (st->host_out) return cudaSuccess;
+    cudaError_t e = cudaEventCreateWithFlags(&st->host_ev_prep, cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&st->host_ev_back, cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&st->host_out, cudaStreamNonBlocking);
+    return e;
+}
+
+// True when p lies in pinned host memory mapped into this device's address
+// space (cudaHostAlloc, or registered with cudaHostRegisterMapped); *dev is
+// then the device's address of p. Pageable memory gives false.
+bool mapped_host(const void *p, void **dev) {
+    cudaPointerAttributes at{};
+    if (cudaPointerGetAttributes(&at, p) != cudaSuccess) {
+        cudaGetLastError();  // the error is not sticky; clear it
+        return false;
+    }
+    if (at.type != cudaMemoryTypeHost || !at.devicePointer) return false;
+    *dev = at.devicePointer;
+    return true;
 }
 
 // Validates a decode call and fills the launch arguments (device pointers).
@@ -992,10 +1019,13 @@ int q38_full_decode_host(q38_ctx *ctx, q38_state *st, int layer, int batch,
     Q38_CUDA(cudaMemcpyAsync(d_k, key, nkv * 4, cudaMemcpyHostToDevice, s));
     Q38_CUDA(cudaMemcpyAsync(d_v, value, nkv * 4, cudaMemcpyHostToDevice, s));
     Q38_CUDA(cudaMemcpyAsync(st->stage_pos, positions, size_t(batch) * 4, cudaMemcpyHostToDevice, s));
+    // A pinned, mapped `attention` buffer is written by the merge kernel directly.
+    void *att_dev = nullptr;
+    const bool att_mapped = mapped_host(attention, &att_dev);
     if (int rc = q38_full_decode(ctx, st, layer, batch, d_qg, d_k, d_v, st->stage_pos, max_pos,
-                                 d_out, stream))
+                                 att_mapped ? static_cast<float *>(att_dev) : d_out, stream))
         return rc;
-    Q38_CUDA(cudaMemcpyAsync(attention, d_out, nq * 4, cudaMemcpyDeviceToHost, s));
+    if (!att_mapped) Q38_CUDA(cudaMemcpyAsync(attention, d_out, nq * 4, cudaMemcpyDeviceToHost, s));
     Q38_CUDA(cudaMemcpyAsync(key, d_k, nkv * 4, cudaMemcpyDeviceToHost, s));
     Q38_CUDA(cudaStreamSynchronize(s));
     return Q38_OK;
@@ -1015,16 +1045,31 @@ int q38_linear_decode_host(q38_ctx *ctx, q38_state *st, int layer, int batch, fl
                  nh = size_t(batch) * ctx->geom.linear_v_heads;
     float *d_qkv = st->stage, *d_z = d_qkv + nqkv, *d_b = d_z + nv, *d_a = d_b + nh,
           *d_out = d_a + nh;
+    // A pinned, mapped `attention` buffer is written by the state kernel
+    // directly (posted writes over PCIe, overlapping its state sweep).
+    void *att_dev = nullptr;
+    const bool att_mapped = mapped_host(attention, &att_dev);
+    q38::LinearDecodeLaunch a;
+    if (int rc = prepare_linear_decode(ctx, st, layer, batch, d_qkv, d_z, d_b, d_a,
+                                       att_mapped ? static_cast<float *>(att_dev) : d_out, &a))
+        return rc;
+    Q38_CUDA(ensure_host_out(st));
     Q38_CUDA(cudaMemcpyAsync(d_qkv, qkv, nqkv * 4, cudaMemcpyHostToDevice, s));
     Q38_CUDA(cudaMemcpyAsync(d_z, z, nv * 4, cudaMemcpyHostToDevice, s));
     Q38_CUDA(cudaMemcpyAsync(d_b, beta, nh * 4, cudaMemcpyHostToDevice, s));
     Q38_CUDA(cudaMemcpyAsync(d_a, alpha, nh * 4, cudaMemcpyHostToDevice, s));
-    if (int rc = q38_linear_decode(ctx, st, layer, batch, d_qkv, d_z, d_b, d_a, d_out, stream))
-        return rc;
-    Q38_CUDA(cudaMemcpyAsync(attention, d_out, nv * 4, cudaMemcpyDeviceToHost, s));
-    Q38_CUDA(cudaMemcpyAsync(qkv, d_qkv, nqkv * 4, cudaMemcpyDeviceToHost, s));
-    Q38_CUDA(cudaMemcpyAsync(beta, d_b, nh * 4, cudaMemcpyDeviceToHost, s));
-    Q38_CUDA(cudaMemcpyAsync(alpha, d_a, nh * 4, cudaMemcpyDeviceToHost, s));
+    cudaError_t e = q38::launch_linear_decode(a, s, st->host_ev_prep);
+    if (e != cudaSuccess) return cuda_fail(e, "DeltaNet decode launch");
+    // The prep kernel's in-place results (qkv, beta, alpha) go back while the
+    // state kernel, which only reads them, runs.
+    Q38_CUDA(cudaStreamWaitEvent(st->host_out, st->host_ev_prep, 0));
+    Q38_CUDA(cudaMemcpyAsync(qkv, d_qkv, nqkv * 4, cudaMemcpyDeviceToHost, st->host_out));
+    Q38_CUDA(cudaMemcpyAsync(beta, d_b, nh * 4, cudaMemcpyDeviceToHost, st->host_out));
+    Q38_CUDA(cudaMemcpyAsync(alpha, d_a, nh * 4, cudaMemcpyDeviceToHost, st->host_out));
+    Q38_CUDA(cudaEventRecord(st->host_ev_back, st->host_out));
+    if (!att_mapped)
+        Q38_CUDA(cudaMemcpyAsync(attention, d_out, nv * 4, cudaMemcpyDeviceToHost, s));
+    Q38_CUDA(cudaStreamWaitEvent(s, st->host_ev_back, 0));  // later work on s follows them
     Q38_CUDA(cudaStreamSynchronize(s));
     return Q38_OK;
 }

@@ -115,6 +115,53 @@ def test_linear_decode_batched_multi_token(cuda_ctx, oracle_lib):
     st.close()
 
 
+@pytest.mark.parametrize("pinned_host", [True, False])
+@pytest.mark.parametrize("batch", [1, 32])
+def test_linear_decode_host_equals_device_call(cuda_ctx, batch, pinned_host):
+    """The host-pointer decode over pinned buffers lets the kernels read and
+    write them in place (mapped host memory); over pageable buffers it stages
+    copies. Either way its outputs, its in-place inputs and the state it
+    leaves equal the device-pointer call bit for bit, two tokens in a row."""
+    torch = _torch()
+    from q38attn import synth
+    g = synth.rng(12 + batch)
+    w = synth.linear_weights(g)
+    layer = 0
+    cuda_ctx.bind_linear_layer(layer, w["conv1d"], w["dt_bias"], w["ssm_a"], w["ssm_norm"])
+    sts = [cuda_ctx.state(batch, 16, full_slots=0, linear_slots=1) for _ in range(2)]
+    for b in range(batch):
+        s0 = synth.linear_state(g)
+        for st in sts:
+            st.upload_linear(layer, b, s0["conv_state"], s0["delta_state"])
+    keep = []
+
+    def pinned(a):
+        if not pinned_host:
+            return np.ascontiguousarray(a).copy()
+        t = torch.from_numpy(np.ascontiguousarray(a)).pin_memory()
+        keep.append(t)
+        return t.numpy()
+
+    for _ in range(2):
+        x = synth.linear_step(g, batch)
+        h = {k: pinned(v) for k, v in x.items()}
+        att_h = pinned(np.zeros((batch, 6144), F))
+        cuda_ctx.linear_decode_host(sts[0], layer, h["qkv"], h["z"], h["beta"], h["alpha"], att_h)
+        d = {k: torch.from_numpy(v.copy()).cuda() for k, v in x.items()}
+        att = torch.zeros(batch, 6144, device="cuda")
+        cuda_ctx.linear_decode(sts[1], layer, d["qkv"], d["z"], d["beta"], d["alpha"], att)
+        torch.cuda.synchronize()
+        np.testing.assert_array_equal(att_h.view(np.uint32), att.cpu().numpy().view(np.uint32))
+        for k in ("qkv", "beta", "alpha"):
+            np.testing.assert_array_equal(h[k].view(np.uint32), d[k].cpu().numpy().view(np.uint32))
+    for b in range(batch):
+        for a, c in zip(sts[0].download_linear(layer, b), sts[1].download_linear(layer, b)):
+            np.testing.assert_array_equal(a, c)
+    assert sts[0].errors() == 0 and sts[1].errors() == 0
+    for st in sts:
+        st.close()
+
+
 def test_linear_decode_rejects_full_layer(cuda_ctx):
     import q38attn
     st = cuda_ctx.state(1, 16, full_slots=1, linear_slots=1)
@@ -240,6 +287,56 @@ def test_full_decode_batch_mixed_positions(cuda_ctx, oracle_lib, bf16):
         assert relative_error(d["key"][b].cpu().numpy(), okey) < 1e-5
     assert st.errors() == 0
     st.close()
+
+
+@pytest.mark.parametrize("pinned_host", [True, False])
+def test_full_decode_host_equals_device_call(cuda_ctx, pinned_host):
+    """The host-pointer decode over pinned buffers (the merge kernel writes
+    `attention` into mapped host memory) and over pageable ones (staged
+    copies) equals the device-pointer call on an identical state bit for bit:
+    attention, the in-place key and the appended cache rows."""
+    import q38attn
+    from q38attn import synth
+    torch = _torch()
+    g = synth.rng(21)
+    w = synth.full_weights(g)
+    layer, ctx_len = 3, 320
+    positions = np.array([0, 5, 64, 300], np.int32)
+    B = len(positions)
+    cuda_ctx.bind_full_layer(layer, w["q_norm"], w["k_norm"])
+    sts = [cuda_ctx.state(B, ctx_len, full_slots=1, linear_slots=0, kv_dtype=q38attn.Q38_KV_BF16)
+           for _ in range(2)]
+    for b, pos in enumerate(positions):
+        if pos:
+            k, v = synth.kv_rows(g, int(pos), bf16=True)
+            for st in sts:
+                st.upload_kv(layer, b, 0, k, v)
+    keep = []
+
+    def host(a):
+        if not pinned_host:
+            return np.ascontiguousarray(a).copy()
+        t = torch.from_numpy(np.ascontiguousarray(a)).pin_memory()
+        keep.append(t)
+        return t.numpy()
+
+    x = synth.full_step(g, B)
+    h = {k: host(v) for k, v in x.items()}
+    att_h = host(np.zeros((B, 6144), F))
+    cuda_ctx.full_decode_host(sts[0], layer, h["q_and_gate"], h["key"], h["value"], positions, att_h)
+    d = {k: torch.from_numpy(v.copy()).cuda() for k, v in x.items()}
+    att = torch.zeros(B, 6144, device="cuda")
+    cuda_ctx.full_decode(sts[1], layer, d["q_and_gate"], d["key"], d["value"],
+                         torch.from_numpy(positions).cuda(), att)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(att_h.view(np.uint32), att.cpu().numpy().view(np.uint32))
+    np.testing.assert_array_equal(h["key"].view(np.uint32), d["key"].cpu().numpy().view(np.uint32))
+    for b, pos in enumerate(positions):
+        for a, c in zip(sts[0].download_kv(layer, b, int(pos), 1), sts[1].download_kv(layer, b, int(pos), 1)):
+            np.testing.assert_array_equal(a, c)
+    assert sts[0].errors() == 0 and sts[1].errors() == 0
+    for st in sts:
+        st.close()
 
 
 def test_split_count_does_not_change_the_result(cuda_ctx):
