@@ -24,6 +24,8 @@ GGML_F16 = (1, 1, 2)
 GGML_Q8_0 = (8, 32, 34)
 GGML_Q4_K = (12, 256, 144)
 GGML_Q6_K = (14, 256, 210)
+GGML_IQ4_NL = (20, 32, 18)
+GGML_IQ4_XS = (23, 256, 136)
 
 
 def _string(s: str | bytes) -> bytes:

@@ -110,16 +110,22 @@ def test_project_host_matches_device(cuda_ctx):
 
 
 def test_weight_from_gguf_equals_array_upload(cuda_ctx, tmp_path):
-    from gguf_writer import GGML_Q4_K, GGML_Q6_K, write_gguf
+    from gguf_writer import GGML_IQ4_NL, GGML_IQ4_XS, GGML_Q4_K, GGML_Q6_K, write_gguf
     from q38attn import synth
     g = synth.rng(302)
     q4 = synth.quant_weight(g, 12, 64, HIDDEN)
     q6 = synth.quant_weight(g, 14, 32, 6144)
+    nl = synth.quant_weight(g, 20, 48, HIDDEN)
+    xs = synth.quant_weight(g, 23, 40, 6144)
     path = tmp_path / "proj.gguf"
     write_gguf(path, [("blk.0.attn_qkv.weight", [HIDDEN, 64], GGML_Q4_K, q4.tobytes()),
-                      ("blk.0.ssm_out.weight", [6144, 32], GGML_Q6_K, q6.tobytes())])
+                      ("blk.0.ssm_out.weight", [6144, 32], GGML_Q6_K, q6.tobytes()),
+                      ("blk.1.attn_gate.weight", [HIDDEN, 48], GGML_IQ4_NL, nl.tobytes()),
+                      ("blk.1.ssm_out.weight", [6144, 40], GGML_IQ4_XS, xs.tobytes())])
     for name, ty, width, rows, data in (("blk.0.attn_qkv.weight", 12, HIDDEN, 64, q4),
-                                        ("blk.0.ssm_out.weight", 14, 6144, 32, q6)):
+                                        ("blk.0.ssm_out.weight", 14, 6144, 32, q6),
+                                        ("blk.1.attn_gate.weight", 20, HIDDEN, 48, nl),
+                                        ("blk.1.ssm_out.weight", 23, 6144, 40, xs)):
         a = cuda_ctx.weight_from_gguf(path, name)
         assert (a.ggml_type, a.width, a.rows) == (ty, width, rows)
         b = cuda_ctx.weight(ty, width, rows, data)
