@@ -3,10 +3,13 @@ ABI, against the CPU oracle:
 
 * q38_quantize_q8_k is bit-identical to quantize_q8_k (src/kernel/quant.rs:
   56-124), block layout included;
-* q38_project over K-quant weights is bit-identical to the reference's
-  integer path (project -> tensor_gemv_q8_k / tensor_gemm_q8_k, ops.rs:623-640,
-  1016-1031), at the model's shapes (5120 -> 10240, 6144 -> 5120, 48-row
-  gates), over a batch that spans several 8-token launches;
+* q38_project over K-quant and IQ4_NL / IQ4_XS weights is bit-identical to
+  the reference's integer path (project -> tensor_gemv_q8_k /
+  tensor_gemm_q8_k, ops.rs:623-640, 1016-1031; dot_iq4_*_q8_k,
+  src/kernel/iq.rs:355-405), at the model's shapes (5120 -> 10240,
+  6144 -> 5120, 48-row gates), over a batch that spans several 8-token
+  launches, through both GEMV forms and the tensor-core kernel;
+* weights uploaded from a GGUF file equal the same bytes uploaded as arrays;
 * F32 / F16 / BF16 / Q8_0 weights agree with the reference's f32 dot within
   its tolerance |a-b|/max(|b|,1) < 1e-4 (src/kernel/x86/tensor.rs:411-413);
 * the layer-level calls (linear_attention, ops.rs:744-803; full_attention,
