@@ -64,6 +64,9 @@ __device__ __forceinline__ uint32_t ld32_a2(const uint8_t *p) {
     return uint32_t(h[0]) | (uint32_t(h[1]) << 16);
 }
 __device__ __forceinline__ uint4 ld128(const uint8_t *p) { return *reinterpret_cast<const uint4 *>(p); }
+__device__ __forceinline__ void prefetch_l2(const void *p) {
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
+}
 __device__ __forceinline__ int byte_of(uint32_t w, int k) { return int((w >> (8 * k)) & 0xffu); }
 
 // scale_min_k4 (src/kernel/tensor.rs:23-32) over the 12 packed bytes held in
@@ -837,6 +840,16 @@ __global__ void __launch_bounds__(256) proj_f32_kernel(ProjF32Params p) {
     const int t0 = blockIdx.y * p.per, nt = min(p.per, p.batch - t0);
     const float *xg = p.x + size_t(t0) * p.width;
     float *outg = p.out + size_t(t0) * p.out_ld;
+    {
+        // The weights are constant: this CTA's rows are requested into L2
+        // before the wait for the previous kernel, so the loads below find
+        // them there.
+        const int r0 = p.split == 1 ? blockIdx.x * 8 : blockIdx.x;
+        const int nr = p.split == 1 ? min(8, p.rows - r0) : 1;
+        const uint8_t *base = p.w + size_t(r0) * p.rb;
+        const size_t bytes = size_t(nr) * p.rb;
+        for (size_t off = size_t(threadIdx.x) * 128; off < bytes; off += 256 * 128) prefetch_l2(base + off);
+    }
     pdl_wait_primary();  // x comes from an earlier kernel in the stream
     pdl_launch_dependents();
     for (int i = threadIdx.x; i < nt * p.width / 4; i += 256)
