@@ -186,16 +186,17 @@ cudaError_t ensure_host_out(q38_state *st) {
     return e;
 }
 
-// True when p lies in pinned host memory mapped into this device's address
-// space (cudaHostAlloc, or registered with cudaHostRegisterMapped); *dev is
-// then the device's address of p. Pageable memory gives false.
-bool mapped_host(const void *p, void **dev) {
+// True when p lies in pinned host memory mapped into `device`'s address
+// space (cudaHostAlloc, or registered with cudaHostRegisterMapped, against
+// that device); *dev is then the device's address of p. Pageable memory, and
+// pinned memory registered against another device, give false.
+bool mapped_host(const void *p, int device, void **dev) {
     cudaPointerAttributes at{};
     if (cudaPointerGetAttributes(&at, p) != cudaSuccess) {
         cudaGetLastError();  // the error is not sticky; clear it
         return false;
     }
-    if (at.type != cudaMemoryTypeHost || !at.devicePointer) return false;
+    if (at.type != cudaMemoryTypeHost || !at.devicePointer || at.device != device) return false;
     *dev = at.devicePointer;
     return true;
 }
@@ -1021,7 +1022,7 @@ int q38_full_decode_host(q38_ctx *ctx, q38_state *st, int layer, int batch,
     Q38_CUDA(cudaMemcpyAsync(st->stage_pos, positions, size_t(batch) * 4, cudaMemcpyHostToDevice, s));
     // A pinned, mapped `attention` buffer is written by the merge kernel directly.
     void *att_dev = nullptr;
-    const bool att_mapped = mapped_host(attention, &att_dev);
+    const bool att_mapped = mapped_host(attention, ctx->device, &att_dev);
     if (int rc = q38_full_decode(ctx, st, layer, batch, d_qg, d_k, d_v, st->stage_pos, max_pos,
                                  att_mapped ? static_cast<float *>(att_dev) : d_out, stream))
         return rc;
@@ -1048,7 +1049,7 @@ int q38_linear_decode_host(q38_ctx *ctx, q38_state *st, int layer, int batch, fl
     // A pinned, mapped `attention` buffer is written by the state kernel
     // directly (posted writes over PCIe, overlapping its state sweep).
     void *att_dev = nullptr;
-    const bool att_mapped = mapped_host(attention, &att_dev);
+    const bool att_mapped = mapped_host(attention, ctx->device, &att_dev);
     q38::LinearDecodeLaunch a;
     if (int rc = prepare_linear_decode(ctx, st, layer, batch, d_qkv, d_z, d_b, d_a,
                                        att_mapped ? static_cast<float *>(att_dev) : d_out, &a))
