@@ -158,3 +158,13 @@ def test_row_bytes_and_shape_errors():
     w = synth.quant_weight(synth.rng(0), oracle.GGML_Q8_0, 4, 96)
     with pytest.raises(ValueError):  # the integer path needs whole 256-blocks
         oracle.gemm_q8_k(oracle.GGML_Q8_0, w, 4, 96, oracle.quantize_q8_k(np.zeros(256, np.float32)), 1)
+
+
+def test_package_row_bytes_match_the_oracle():
+    """The Python package's row sizes (what a caller sizes host buffers with)
+    agree with the oracle's row_bytes (src/kernel/tensor.rs:46-53) for every
+    projection type, IQ4_NL / IQ4_XS included."""
+    import q38attn
+    for ggml_type in K_TYPES + F_TYPES + IQ_TYPES:
+        for width in (256, 5120, 6144):
+            assert q38attn.row_bytes(ggml_type, width) == oracle.row_bytes(ggml_type, width)
