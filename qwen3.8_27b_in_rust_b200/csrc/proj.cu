@@ -840,10 +840,10 @@ __global__ void __launch_bounds__(256) proj_f32_kernel(ProjF32Params p) {
     const int t0 = blockIdx.y * p.per, nt = min(p.per, p.batch - t0);
     const float *xg = p.x + size_t(t0) * p.width;
     float *outg = p.out + size_t(t0) * p.out_ld;
-    {
+    if (blockIdx.y == 0) {
         // The weights are constant: this CTA's rows are requested into L2
         // before the wait for the previous kernel, so the loads below find
-        // them there.
+        // them there (once per row: the first token group asks).
         const int r0 = p.split == 1 ? blockIdx.x * 8 : blockIdx.x;
         const int nr = p.split == 1 ? min(8, p.rows - r0) : 1;
         const uint8_t *base = p.w + size_t(r0) * p.rb;
