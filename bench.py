@@ -28,8 +28,13 @@ flush is needed between steps.
 --impl reference runs only the CPU oracle (the reference's algorithm; the
 Rust crate itself cannot be built here), rank 0 only.
 
-Multi-GPU: one process per GPU (torchrun); every rank owns its own 32
-sequences (weak scaling, no data-path collective).
+Multi-GPU: one process per GPU (torchrun). The headline decode shards by
+sequence: every rank owns its own 32 sequences (weak scaling, no data-path
+collective). The prefill legs keep the global config-4 / config-5 workload
+fixed and split its units across the ranks (strong scaling): (sequence,
+KV-head group) units for the attention prefill, value heads for the DeltaNet
+prefill. The split-sequence leg spreads one sequence's positions over the
+ranks and exchanges softmax partials with the library's NCCL all-gather.
 """
 from __future__ import annotations
 
@@ -123,15 +128,20 @@ def prefill_flops(batch: int, seq: int) -> float:
     return float(batch) * 24 * 4 * 256 * seq * (seq + 1) / 2
 
 
-def run_prefill(args, ctx, q38attn, synth, torch, rank: int) -> dict:
+def run_prefill(args, ctx, q38attn, synth, torch, rank: int, world: int, dist) -> dict:
     """Config 4: causal prefill of `prefill_batch` prompts of `prefill_len`
-    tokens through one full-attention layer, on the tensor cores."""
+    tokens through one full-attention layer, on the tensor cores. The global
+    workload is fixed; its (sequence, KV-head group) units are split across
+    the ranks (strong scaling), each rank running q38_full_prefill_heads over
+    its share on the same global inputs."""
+    from q38attn.parallel import prefill_segments
     B, S = args.prefill_batch, args.prefill_len
     layer = FULL_LAYER
+    segs = prefill_segments(B, 4, world, rank)
     st = ctx.state(B, S, full_slots=1, linear_slots=0, kv_dtype=q38attn.Q38_KV_BF16)
-    st.reserve_prefill(B * S)
+    st.reserve_prefill(max(n for _, n, _, _ in segs) * S)
     tg = torch.Generator(device="cuda")
-    tg.manual_seed(args.seed + 77 + rank)
+    tg.manual_seed(args.seed + 77)  # the same global prompts on every rank
     qg = torch.randn(B, S, 12288, device="cuda", generator=tg)
     key0 = torch.randn(B, S, 1024, device="cuda", generator=tg)
     val = torch.randn(B, S, 1024, device="cuda", generator=tg)
@@ -140,15 +150,23 @@ def run_prefill(args, ctx, q38attn, synth, torch, rank: int) -> dict:
     stream = torch.cuda.current_stream()
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
            for _ in range(args.prefill_iters)]
+
+    def one():
+        for s0, n, h0, nh in segs:
+            ctx.full_prefill_heads(st, layer, s0, qg[s0:s0 + n], key[s0:s0 + n], val[s0:s0 + n],
+                                   att[s0:s0 + n], 0, h0, nh, stream=stream)
+
     for it in range(2):
         key.copy_(key0)  # key is rewritten in place (RMSNorm + RoPE)
-        ctx.full_prefill(st, layer, 0, qg, key, val, att, 0, stream=stream)
+        one()
     torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
     with ClockSampler(torch.cuda.current_device(), period_s=0.002) as clocks:
         for it in range(args.prefill_iters):
             key.copy_(key0)
             evs[it][0].record(stream)
-            ctx.full_prefill(st, layer, 0, qg, key, val, att, 0, stream=stream)
+            one()
             evs[it][1].record(stream)
         torch.cuda.synchronize()
     if st.errors():
@@ -157,7 +175,8 @@ def run_prefill(args, ctx, q38attn, synth, torch, rank: int) -> dict:
     st.close()
     del qg, key0, val, key, att
     torch.cuda.empty_cache()
-    return {"ms": ms, "clocks": clocks.summary()}
+    return {"ms": ms, "clocks": clocks.summary(),
+            "units": sum(n * nh for _, n, _, nh in segs)}
 
 
 def linear_prefill_flops(batch: int, seq: int) -> float:
@@ -169,15 +188,19 @@ def linear_prefill_flops(batch: int, seq: int) -> float:
     return float(batch) * 48 * (seq // C) * per_chunk
 
 
-def run_linear_prefill(args, ctx, q38attn, torch, rank: int) -> dict:
+def run_linear_prefill(args, ctx, q38attn, torch, rank: int, world: int, dist) -> dict:
     """Config 5: chunked DeltaNet prefill of `prefill_batch` prompts of
-    `prefill_len` tokens through one DeltaNet layer from a zero state."""
+    `prefill_len` tokens through one DeltaNet layer from a zero state. The
+    global workload is fixed; its 48 value heads are split across the ranks
+    (strong scaling; every rank convolves the shared q/k channels itself)."""
+    from q38attn.parallel import shard_range
     B, S = args.prefill_batch, args.prefill_len
     layer = LINEAR_LAYERS[0]
+    h0, h1 = shard_range(48, world, rank)
     st = ctx.state(B, 16, full_slots=0, linear_slots=1)
     st.reserve_prefill(B * S)
     tg = torch.Generator(device="cuda")
-    tg.manual_seed(args.seed + 99 + rank)
+    tg.manual_seed(args.seed + 99)  # the same global prompts on every rank
     qkv0 = torch.randn(B, S, 10240, device="cuda", generator=tg)
     z = torch.randn(B, S, 6144, device="cuda", generator=tg)
     b0 = torch.randn(B, S, 48, device="cuda", generator=tg)
@@ -194,13 +217,16 @@ def run_linear_prefill(args, ctx, q38attn, torch, rank: int) -> dict:
         alpha.copy_(a0)
         if it >= 0:
             evs[it][0].record(stream)
-        ctx.linear_prefill(st, layer, 0, qkv, z, beta, alpha, att, stream=stream)
+        ctx.linear_prefill_heads(st, layer, 0, qkv, z, beta, alpha, att, h0, h1 - h0,
+                                 stream=stream)
         if it >= 0:
             evs[it][1].record(stream)
 
     one(-1)
     one(-1)
     torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
     with ClockSampler(torch.cuda.current_device(), period_s=0.002) as clocks:
         for it in range(args.prefill_iters):
             one(it)
@@ -211,7 +237,7 @@ def run_linear_prefill(args, ctx, q38attn, torch, rank: int) -> dict:
     st.close()
     del qkv0, z, b0, a0, qkv, beta, alpha, att
     torch.cuda.empty_cache()
-    return {"ms": ms, "clocks": clocks.summary()}
+    return {"ms": ms, "clocks": clocks.summary(), "heads": h1 - h0}
 
 
 # Projection weights of one DeltaNet layer, Q4_K_M-like (ggml type, width, rows):
@@ -308,6 +334,8 @@ def run_split_sequence(args, ctx, q38attn, torch, dist, rank: int, world: int) -
     out = torch.empty(1, 6144, device="cuda")
     pos = torch.arange(P, P + args.split_steps + 3, device="cuda", dtype=torch.int32)
     dec = SplitSequenceDecoder(ctx, st, FULL_LAYER, p0) if world > 1 else None
+    if dist is not None:
+        dist.barrier()
     stream = torch.cuda.current_stream()
 
     def one(i):
@@ -332,6 +360,8 @@ def run_split_sequence(args, ctx, q38attn, torch, dist, rank: int, world: int) -
     ms = e0.elapsed_time(e1) / args.split_steps
     if st.errors():
         raise RuntimeError("device error bits set during split-sequence decode")
+    if dec is not None:
+        dec.close()
     st.close()
     return {"ms": ms}
 
@@ -681,8 +711,8 @@ def run_ours(args) -> None:
 
     prefill = lin_prefill = None
     if not args.no_prefill:
-        prefill = run_prefill(args, ctx, q38attn, synth, torch, rank)
-        lin_prefill = run_linear_prefill(args, ctx, q38attn, torch, rank)
+        prefill = run_prefill(args, ctx, q38attn, synth, torch, rank, world, dist)
+        lin_prefill = run_linear_prefill(args, ctx, q38attn, torch, rank, world, dist)
 
     proj = None
     if not args.no_proj:
@@ -765,15 +795,17 @@ def run_ours(args) -> None:
         }
         tpeak, tpeak_kind = load_tensor_peak()
         if prefill:
-            flops = prefill_flops(args.prefill_batch, args.prefill_len) * world
+            flops = prefill_flops(args.prefill_batch, args.prefill_len)
             tflops = flops / (prefill_ms * 1e-3) / 1e12
             line["prefill"] = {
                 "workload": (f"config4: {args.prefill_batch} x {args.prefill_len}-token causal "
-                             "prefill per GPU, 24Q/4KV x 256, RoPE 64, sigmoid gate; "
-                             "QK^T bf16, PV f16, f32 accumulate (tcgen05)"),
-                "ms": prefill_ms, "flops": flops, "tflops": tflops,
-                # Per GPU: every rank runs the same prefill, so one GPU's rate is
-                # the whole-job rate over the ranks.
+                             "prefill (the whole job), 24Q/4KV x 256, RoPE 64, sigmoid gate; "
+                             "QK^T bf16, PV f16, f32 accumulate (tcgen05); its "
+                             f"{args.prefill_batch * 4} (sequence, KV-head group) units split "
+                             f"over {world} GPU(s)"),
+                "scaling": "strong", "ms": prefill_ms, "flops": flops, "tflops": tflops,
+                "units_per_gpu": prefill["units"],
+                # Per GPU: the whole job's rate over the ranks (slowest rank's time).
                 "roofline": {"bound": "tensor", "achieved": tflops / world, "peak": tpeak,
                              "unit": "TFLOP/s", "frac": tflops / world / tpeak,
                              "peak_source": f"{tpeak_kind} bf16_tflops (burst)",
@@ -785,23 +817,26 @@ def run_ours(args) -> None:
             line["split_sequence"] = {
                 "workload": (f"config3 split-sequence: 1 sequence, {args.split_context} cached "
                              f"bf16 positions sharded over {world} GPU(s); per-shard partials, "
-                             "NCCL all-gather, LSE merge (strong scaling)"),
-                "ms_per_token": split_ms, "tok_s": 1e3 / split_ms,
+                             "NCCL all-gather inside q38_full_decode_split, LSE merge"),
+                "scaling": "strong", "ms_per_token": split_ms, "tok_s": 1e3 / split_ms,
                 "kv_gbs": kv_bytes / (split_ms * 1e-3) / 1e9,
+                "hbm_frac_per_gpu": kv_bytes / world / (split_ms * 1e-3) / 1e9 / peak,
             }
         if lin_prefill:
-            flops = linear_prefill_flops(args.prefill_batch, args.prefill_len) * world
-            toks = args.prefill_batch * args.prefill_len * world
+            flops = linear_prefill_flops(args.prefill_batch, args.prefill_len)
+            toks = args.prefill_batch * args.prefill_len
             # Config 5's stated per-token traffic (~45 KB: q/k/v/z/gates in, output
             # out, f32) and the WY-form FLOPs; the path is mixed-bound, so both
             # fractions are reported.
             lp_bytes = toks * 45 * 1024
             line["deltanet_prefill"] = {
                 "workload": (f"config5: {args.prefill_batch} x {args.prefill_len}-token chunked "
-                             "Gated DeltaNet prefill per GPU (C=64, 16K/48V x 128) from a zero "
-                             "state, outputs + final f32 state; chunk-local WY products and "
+                             "Gated DeltaNet prefill (the whole job; C=64, 16K/48V x 128) from a "
+                             "zero state, outputs + final f32 state; chunk-local WY products and "
                              "state pass on tcgen05 with bf16 hi/lo operand pairs (3 products, "
-                             "~1e-5 of the per-token recurrence), TMA-tiled conv"),
+                             "~1e-5 of the per-token recurrence), TMA-tiled conv; the 48 value "
+                             f"heads split over {world} GPU(s), q/k convolved on every GPU"),
+                "scaling": "strong", "heads_per_gpu": lin_prefill["heads"],
                 "ms": lin_prefill_ms, "tok_s": toks / (lin_prefill_ms * 1e-3),
                 "flops": flops, "tflops": flops / (lin_prefill_ms * 1e-3) / 1e12,
                 "roofline": {

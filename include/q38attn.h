@@ -4,8 +4,8 @@
  * decode and prefill.
  *
  * This is the boundary the reference's Rust host binds with a thin
- * `extern "C"` FFI crate (INTEGRATION.md shows the binding). It replaces the
- * two crate-private cores and the per-token loops that call them:
+ * `extern "C"` FFI crate. It replaces the two crate-private cores and the
+ * per-token loops that call them:
  *
  *   linear_core   src/model/ops.rs:647-742   -> q38_linear_decode / q38_linear_core
  *   full_core     src/model/ops.rs:812-940   -> q38_full_decode   / q38_full_core
@@ -59,6 +59,7 @@ extern "C" {
 #define Q38_DEVERR_POSITION 1
 #define Q38_DEVERR_TIMEOUT 2
 #define Q38_DEVERR_SHAPE 4
+#define Q38_DEVERR_RANGE 8 /* a prefill V value beyond the f16 range (|v| > 65504) */
 
 typedef struct q38_ctx q38_ctx;
 typedef struct q38_state q38_state;
@@ -162,6 +163,18 @@ int q38_state_restore(q38_state *st, int seq0, int nseq, void *stream);
 /* Reads and clears the device error bits (synchronises the device). */
 int q38_state_errors(q38_state *st, int *bits);
 
+/* Error-path testing only. flags = Q38_DEBUG_SKIP_KV_LOADS makes the split-KV
+ * kernel of this state's decode calls issue none of its KV tile loads, so
+ * its bounded waits run out: the kernel records Q38_DEVERR_TIMEOUT, returns
+ * without touching memory beyond its own partials, and the host-pointer
+ * decode call returns Q38_ERR_TIMEOUT (the step's outputs are then
+ * undefined). wait_ns is the limit of those waits (0: the library's 1 s).
+ * flags = 0, wait_ns = 0 restores normal operation. Nothing is in flight when
+ * such a wait gives up, and the context stays usable. Not thread-safe with
+ * calls in flight on the state. */
+#define Q38_DEBUG_SKIP_KV_LOADS 1
+int q38_state_set_debug(q38_state *st, int flags, uint64_t wait_ns);
+
 /* Device pointers of one slot's buffers, for callers that manage their own
  * copies. Any output pointer may be NULL. */
 int q38_state_full_slot(q38_state *st, int layer, void **key_cache, void **value_cache,
@@ -211,6 +224,39 @@ int q38_full_decode_shard(q38_ctx *ctx, q38_state *st, int layer, int batch,
                           const int32_t *positions, int max_position, int pos_offset,
                           float *partials, void *stream);
 
+/* Split-sequence decode in one call, with the exchange over NCCL: this rank
+ * holds positions pos_offset .. pos_offset+context_length-1 of every
+ * sequence (as for q38_full_decode_shard); the call runs the shard kernels,
+ * an ncclAllGather of every rank's (o, m, l) partials into this state's
+ * local gather buffer (24 x 258 floats per sequence and rank; no kernel
+ * reads another GPU's memory), and the merge, all on `stream`. Every rank of
+ * nccl_comm (an ncclComm_t of the caller's NCCL, or one from
+ * q38_nccl_comm_create) makes the same call with the same q_and_gate / key /
+ * value / positions and receives the full attention [batch][heads*256].
+ * Needs q38_state_reserve_split(st, ranks of nccl_comm). The split-sequence
+ * form of full_core's position loop (src/model/ops.rs:884-913), with the
+ * positions spread over the ranks. */
+int q38_full_decode_split(q38_ctx *ctx, q38_state *st, int layer, int batch,
+                          const float *q_and_gate, float *key, const float *value,
+                          const int32_t *positions, int max_position, int pos_offset,
+                          void *nccl_comm, float *attention, void *stream);
+
+/* Sizes the split-sequence buffers of q38_full_decode_split for `nranks`
+ * ranks and the state's batch (allocates; call it once at set-up). */
+int q38_state_reserve_split(q38_state *st, int nranks);
+
+/* NCCL communicator helpers for hosts without their own NCCL plumbing. The
+ * library resolves NCCL (libnccl.so.2) at run time, on first use, and uses
+ * the copy the process has already loaded if there is one. Rank 0 makes an
+ * id (Q38_NCCL_ID_BYTES bytes) with q38_nccl_unique_id, the host sends it to
+ * every rank by its own means, and each rank creates its communicator on its
+ * device with q38_nccl_comm_create (collective over the ranks: every rank
+ * must call it). comm receives an ncclComm_t. */
+#define Q38_NCCL_ID_BYTES 128
+int q38_nccl_unique_id(void *id);
+int q38_nccl_comm_create(const void *id, int nranks, int rank, int device, void **comm);
+int q38_nccl_comm_destroy(void *comm);
+
 /* Split-sequence decode, merge side: combines nparts shard partials
  * [nparts][batch][heads][258] (gathered from every shard, e.g. by an NCCL
  * all-gather) by log-sum-exp, normalises and applies the sigmoid output gate
@@ -247,15 +293,23 @@ int q38_linear_decode(q38_ctx *ctx, q38_state *st, int layer, int batch, float *
  * error_bits is an optional device int that receives Q38_DEVERR_* bits (it is
  * OR-ed into, never cleared; NULL to skip).
  *
+ * key_cache and value_cache must be 16-byte aligned and every other pointer
+ * 4-byte aligned; a misaligned pointer is rejected with Q38_ERR_ARG before
+ * any work.
+ *
  * The kernels' scratch (prepared queries and split-KV partials) lives in a
- * fixed 16 MiB device array inside the library, held on every GPU that loads
- * the library until the process exits. A call whose batch and max_position
- * would need more than 16 MiB is rejected with Q38_ERR_ARG before any work.
- * The first call on each device looks the array's address up
- * (cudaGetSymbolAddress) and caches it; make that first call before any
- * stream capture. All calls on a device share the array, which keeps the
- * last call's contents (no call relies on it starting at zero): calls whose
- * executions overlap on the GPU race on it, so order them on one stream. */
+ * fixed 16 MiB device array inside the library, held on every GPU where the
+ * library's device code has been loaded, until the process exits. A call
+ * whose batch and max_position would need more than 16 MiB is rejected with
+ * Q38_ERR_ARG before any work. The first call on each device looks the
+ * array's address up (cudaGetSymbolAddress) and caches it; under CUDA's
+ * default lazy module loading this is also when the 16 MiB are taken from
+ * the device. So make that first call (a warm-up step) before reserving the
+ * device's free memory for a pool, and before any stream capture. The cached
+ * address does not survive a cudaDeviceReset of that device. All calls on a
+ * device share the array, which keeps the last call's contents (no call
+ * relies on it starting at zero): calls whose executions overlap on the GPU
+ * race on it, so order them on one stream. */
 int q38_full_decode_noalloc(const float *q_norm, const float *k_norm, void *key_cache,
                             void *value_cache, int batch, int context_length, int kv_dtype,
                             const float *q_and_gate, float *key, const float *value,
@@ -278,8 +332,12 @@ int q38_state_reserve_prefill(q38_state *st, int max_tokens);
  * attends to positions 0..base_position+t, exactly as the reference's
  * per-token loop over full_core (batch_full_attention, ops.rs:1156-1172).
  * Runs on the tcgen05 tensor cores: S = Q K^T from bf16 Q and K, O = P V in
- * f16, f32 accumulation;
- * needs a Q38_KV_BF16 state and q38_state_reserve_prefill(nseq*count).
+ * f16, f32 accumulation (tolerance 2e-3 against the f32 reference).
+ * Needs q38_state_reserve_prefill(nseq*count). Either cache type: a
+ * Q38_KV_F32 state keeps the reference's f32 rows in its cache (decode then
+ * reads exactly what the reference's Vec<f32> cache holds) and the
+ * tensor-core operands are bf16 / f16 copies in the prefill scratch; a
+ * Q38_KV_BF16 state stores the rows in bf16.
  * DEVICE pointers (16-byte aligned, else Q38_ERR_ARG), token-major per
  * sequence:
  *   q_and_gate [nseq][count][heads*512]
@@ -287,16 +345,31 @@ int q38_state_reserve_prefill(q38_state *st, int max_tokens);
  *   value      [nseq][count][kv_heads*256]
  *   attention  [nseq][count][heads*256]  output
  * The K/V rows of positions base_position..base_position+count-1 are
- * appended to the cache. */
+ * appended to the cache. A V value beyond the f16 range (|v| > 65504) sets
+ * Q38_DEVERR_RANGE (its rows' outputs are then not finite). */
 int q38_full_prefill(q38_ctx *ctx, q38_state *st, int layer, int seq0, int nseq, int count,
                      int base_position, const float *q_and_gate, float *key, const float *value,
                      float *attention, void *stream);
+
+/* The same for the KV heads kv_head0 .. kv_head0+kv_head_count-1 only (their
+ * 6 query heads each): the tensors keep their full row widths, and only the
+ * range's columns of q_and_gate, key, value and attention are read or
+ * written, and only the range's K/V cache rows appended. The reference runs
+ * one task per query head with kv_head = head / 6 (ops.rs:922-938, :877);
+ * a (sequence, KV-head group) is the unit that prefill shards across GPUs. */
+int q38_full_prefill_heads(q38_ctx *ctx, q38_state *st, int layer, int seq0, int nseq,
+                           int count, int base_position, int kv_head0, int kv_head_count,
+                           const float *q_and_gate, float *key, const float *value,
+                           float *attention, void *stream);
 
 /* Chunked Gated DeltaNet prefill of `count` prompt tokens for each of the
  * nseq sequences seq0..seq0+nseq-1, continuing each sequence's conv and
  * delta state: the same result as the reference's per-token loop over
  * linear_core (batch_linear_attention, ops.rs:1088-1099), computed in chunks
- * of 64 tokens (WY form; f32). Needs q38_state_reserve_prefill(nseq*count).
+ * of 64 tokens in WY form: the chunk products run on the tcgen05 tensor cores
+ * with every operand split into a bf16 (hi, lo) pair and f32 accumulation
+ * (about 16 mantissa bits per operand; within ~1e-5 of the per-token
+ * recurrence). Needs q38_state_reserve_prefill(nseq*count).
  * DEVICE pointers (qkv, z, attention 16-byte aligned, else Q38_ERR_ARG),
  * token-major per sequence:
  *   qkv   [nseq][count][qkv_dim]  in: projections; out: conv+SiLU+L2 values
@@ -307,6 +380,17 @@ int q38_full_prefill(q38_ctx *ctx, q38_state *st, int layer, int seq0, int nseq,
 int q38_linear_prefill(q38_ctx *ctx, q38_state *st, int layer, int seq0, int nseq, int count,
                        float *qkv, const float *z, float *beta, float *alpha, float *attention,
                        void *stream);
+
+/* The same for the value heads v_head0 .. v_head0+v_head_count-1 only. The q
+ * and k channels (all key heads) are convolved and normalised by every call,
+ * since value head h reads key head h % qk_heads (ops.rs:699); of the v
+ * channels, gates, z and output only the range's are read or written, and
+ * only the range's conv-state channels and delta-state heads advance. The
+ * reference runs one task per value head (ops.rs:717-733); value heads are
+ * the unit that DeltaNet prefill shards across GPUs. */
+int q38_linear_prefill_heads(q38_ctx *ctx, q38_state *st, int layer, int seq0, int nseq,
+                             int count, int v_head0, int v_head_count, float *qkv, const float *z,
+                             float *beta, float *alpha, float *attention, void *stream);
 
 /* Host-pointer forms of the two prefill calls, for the reference's host
  * slices (batch_full_attention / batch_linear_attention, ops.rs:1156-1172,

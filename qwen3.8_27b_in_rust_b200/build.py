@@ -18,7 +18,7 @@ PKG_DIR = Path(__file__).resolve().parent
 CSRC = PKG_DIR / "csrc"
 LIB_PATH = PKG_DIR / "libq38attn.so"
 SOURCES = ["q38attn.cu", "attn_decode.cu", "deltanet_decode.cu", "attn_decode_noalloc.cu",
-           "attn_prefill.cu", "deltanet_prefill.cu", "q38_gguf.cpp", "proj.cu", "proj_mma.cu", "q38proj.cu"]
+           "attn_prefill.cu", "deltanet_prefill.cu", "q38_gguf.cpp", "proj.cu", "proj_mma.cu", "q38proj.cu", "q38_nccl.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 
@@ -37,6 +37,7 @@ def nvcc_command(out: Path = LIB_PATH, extra: list[str] | None = None) -> list[s
         *(extra or []),
         "-o", str(out),
         *[str(CSRC / s) for s in SOURCES],
+        "-ldl",
     ]
 
 

@@ -26,7 +26,6 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
-#include <cstdlib>
 
 namespace q38 {
 namespace {
@@ -151,6 +150,8 @@ struct SplitParams {
     float *part_o, *part_ml;
     int *err;
     int context_length, heads, kv_heads, chunk, max_splits, max_position, pos_offset, sharded;
+    uint64_t wait_ns;  // limit of every bounded wait
+    int skip_loads;    // error-path testing: issue no KV loads (every wait runs out)
 };
 
 // Rows of the local cache a sequence at global position pos attends to.
@@ -348,6 +349,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     };
     auto issue = [&](int j) {
         const int t = j < ntiles ? j : j - ntiles;
+        if (p.skip_loads) return;  // nothing in flight: every wait on this tile runs out
         issued_s = j + 1;
         if (kTc) {
             // K or V tile as an SW128 MMA operand (K-major A of the scores, MN-major
@@ -366,7 +368,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     };
     // Waits for tile j; false (and the CTA-wide abort flag set) on timeout.
     auto wait_tile = [&](int j) {
-        if (!mbar_wait(&bars[j % kStages], uint32_t(j / kStages) & 1u)) {
+        if (!mbar_wait_ns(&bars[j % kStages], uint32_t(j / kStages) & 1u, p.wait_ns)) {
             abort_flag = 1;
             set_error(p.err, kDevErrTimeout);
         }
@@ -448,7 +450,7 @@ __global__ void __launch_bounds__(kThreads, 2)
                 const int part = warp - 5;  // 0: hi, 1: lo
                 const uint32_t qx = smem_addr(qsm) + part * kQOperandBytes;
                 for (int j = 0; j < ntiles; ++j) {
-                    if (!mbar_wait(&bars[j % kStages], uint32_t(j / kStages) & 1u)) {
+                    if (!mbar_wait_ns(&bars[j % kStages], uint32_t(j / kStages) & 1u, p.wait_ns)) {
                         abort_flag = 1;
                         set_error(p.err, kDevErrTimeout);
                         break;
@@ -472,7 +474,7 @@ __global__ void __launch_bounds__(kThreads, 2)
             // so lanes 0-15 of warp w hold keys 16 w .. 16 w + 15 of the tile.
             const uint32_t lane_addr = uint32_t(32 * warp) << 16;
             for (int j = 0; j < ntiles; ++j) {
-                if (!__all_sync(0xffffffffu, mbar_wait(&mma_done[j % kStages], uint32_t(j / kStages) & 1u))) {
+                if (!__all_sync(0xffffffffu, mbar_wait_ns(&mma_done[j % kStages], uint32_t(j / kStages) & 1u, p.wait_ns))) {
                     if (lane == 0) {
                         abort_flag = 1;
                         set_error(p.err, kDevErrTimeout);
@@ -497,7 +499,7 @@ __global__ void __launch_bounds__(kThreads, 2)
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&read_done[j % kStages]);
                 if (threadIdx.x == 0 && !abort_flag && j + kStages < total_tiles) {
-                    if (mbar_wait(&read_done[j % kStages], uint32_t(j / kStages) & 1u)) {
+                    if (mbar_wait_ns(&read_done[j % kStages], uint32_t(j / kStages) & 1u, p.wait_ns)) {
                         issue(j + kStages);
                     } else {
                         abort_flag = 1;
@@ -599,7 +601,7 @@ __global__ void __launch_bounds__(kThreads, 2)
             const uint32_t pb = smem_addr(psm);
             for (int j = ntiles; j < total_tiles; ++j) {
                 const int t = j - ntiles;
-                if (!mbar_wait(&bars[j % kStages], uint32_t(j / kStages) & 1u)) {
+                if (!mbar_wait_ns(&bars[j % kStages], uint32_t(j / kStages) & 1u, p.wait_ns)) {
                     abort_flag = 1;
                     set_error(p.err, kDevErrTimeout);
                     break;
@@ -622,7 +624,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         } else if (threadIdx.x == 0) {
             // Refill each stage once both chains have read it.
             for (int j = ntiles; j + kStages < total_tiles && !abort_flag; ++j) {
-                if (!mbar_wait(&mma_done[j % kStages], uint32_t(j / kStages) & 1u)) {
+                if (!mbar_wait_ns(&mma_done[j % kStages], uint32_t(j / kStages) & 1u, p.wait_ns)) {
                     abort_flag = 1;
                     set_error(p.err, kDevErrTimeout);
                     break;
@@ -633,7 +635,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         // Epilogue: warps 0-3 read O^T (lane = dim) once the last tile's MMAs
         // (and so all earlier ones) have completed.
         if (warp < 4) {
-            const bool ok = !abort_flag && __all_sync(0xffffffffu, mbar_wait(&pv_final, 0));
+            const bool ok = !abort_flag && __all_sync(0xffffffffu, mbar_wait_ns(&pv_final, 0, p.wait_ns));
             if (ok) {
                 fence_after_sync();
 #pragma unroll 1
@@ -664,7 +666,7 @@ __global__ void __launch_bounds__(kThreads, 2)
             // Copies still in flight are among the last kStages issued (each
             // refill waited for the tile kStages before it): let them land.
             for (int j = max(0, issued_s - kStages); j < issued_s; ++j)
-                (void)mbar_wait(&bars[j % kStages], uint32_t(j / kStages) & 1u);
+                (void)mbar_wait_ns(&bars[j % kStages], uint32_t(j / kStages) & 1u, p.wait_ns);
         }
         if (warp == 0) {
             __syncwarp();
@@ -702,7 +704,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         if (threadIdx.x == 0) {
             const int issued = min(total_tiles, next + kStages - 1);
             for (int j = max(0, next - 1); j < issued; ++j)
-                (void)mbar_wait(&bars[j % kStages], uint32_t(j / kStages) & 1u);
+                (void)mbar_wait_ns(&bars[j % kStages], uint32_t(j / kStages) & 1u, p.wait_ns);
         }
         return;
     }
@@ -828,14 +830,6 @@ bool make_map_kcache(CUtensorMap *m, const void *base, uint64_t rows, uint64_t p
                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-int env_chunk_override() {
-    static const int v = [] {
-        const char *s = std::getenv("Q38_DECODE_CHUNK");
-        return s ? std::atoi(s) : 0;
-    }();
-    return v;
-}
-
 template <typename KV>
 cudaError_t launch_typed(const AttnDecodeLaunch &a, int sm_count, cudaStream_t stream) {
     // Rows any sequence of this call attends to in the local cache.
@@ -860,7 +854,8 @@ cudaError_t launch_typed(const AttnDecodeLaunch &a, int sm_count, cudaStream_t s
     SplitParams sp{a.kcache,   a.vcache,  a.qprep,  a.positions,       a.part_o,
                    a.part_ml,  a.err,     a.context_length, a.heads, a.kv_heads,
                    plan.chunk, a.max_splits, a.max_position, a.pos_offset,
-                   a.partial_out != nullptr};
+                   a.partial_out != nullptr, a.wait_ns ? a.wait_ns : kWaitTimeoutNs,
+                   a.skip_kv_loads};
     constexpr bool kTc = sizeof(KV) == 2;
     CUtensorMap map_k{}, map_v{};
     if (kTc && (!make_map_kcache(&map_k, a.kcache, uint64_t(a.context_length),
@@ -898,31 +893,56 @@ cudaError_t launch_typed(const AttnDecodeLaunch &a, int sm_count, cudaStream_t s
 
 }  // namespace
 
+// Splits per (sequence, kv head) that the partial buffers hold for a cache of
+// context_length positions: enough for splits of a quarter of kFastChunk at
+// any length (the partials then stay near 2% of the KV bytes), at least
+// kMinSplitsCap, never more than one per tile.
 int attn_decode_max_splits(int context_length, int kv_dtype) {
     const int tile = tile_positions(kv_dtype);
     const int max_chunk = kv_dtype == Q38_KV_BF16 ? kMaxChunkTc : kMaxChunk;
     const int by_tile = (context_length + tile - 1) / tile;
     const int by_chunk = (context_length + max_chunk - 1) / max_chunk;
-    return std::min(by_tile, std::max(kMinSplitsCap, by_chunk));
+    const int by_quarter = (context_length + kFastChunk / 4 - 1) / (kFastChunk / 4);
+    return std::min(by_tile, std::max({kMinSplitsCap, by_chunk, by_quarter}));
 }
 
+// Split plan: the chunk (a whole number of tiles, at most kFastChunk so that
+// two CTAs fit on an SM) that minimises the estimated makespan
+//   ceil(CTAs / (2 * SMs)) * (chunk + per-CTA overhead),
+// i.e. whole waves of equal CTAs; a smaller chunk replaces a larger one only
+// when it is at least 3% cheaper (fewer partials to write and merge).
+// Batched long-context decode keeps 512-position splits; a single long
+// sequence gets enough splits to fill every SM in near-whole waves.
 DecodeSplitPlan plan_attn_decode(int batch, int kv_heads, int max_position, int kv_dtype,
                                  int sm_count) {
+    constexpr int kOverheadPositions = 128;  // setup, softmax and partial write of a CTA
     const int tile = tile_positions(kv_dtype);
     const int max_chunk = kv_dtype == Q38_KV_BF16 ? kMaxChunkTc : kMaxChunk;
-    const int n = max_position + 1;
-    const int units = std::max(1, batch * kv_heads);
-    // Aim for at least two CTAs per SM over the whole grid.
-    const int want = std::max(1, (2 * sm_count + units - 1) / units);
-    int chunk = (n + want - 1) / want;
-    // Bound the number of splits (partial buffers are sized for it).
-    chunk = std::max(chunk, (n + kMinSplitsCap - 1) / kMinSplitsCap);
-    if (int o = env_chunk_override(); o > 0) chunk = o;
-    chunk = ((chunk + tile - 1) / tile) * tile;
-    chunk = std::min(std::max(chunk, tile), env_chunk_override() > 0 ? max_chunk : kFastChunk);
-    // Never more splits than attn_decode_max_splits allows for this n.
-    const int cap = std::max(kMinSplitsCap, (n + max_chunk - 1) / max_chunk);
-    if ((n + chunk - 1) / chunk > cap) chunk = ((n + cap - 1) / cap + tile - 1) / tile * tile;
+    const int n = std::max(max_position + 1, 1);
+    const int tiles = (n + tile - 1) / tile;
+    const int64_t units = std::max(1, batch * kv_heads);
+    const int64_t slots = 2 * int64_t(std::max(sm_count, 1));
+    // Never more splits than attn_decode_max_splits allows for this n (the
+    // state's partial buffers hold that many for its whole context).
+    const int cap = attn_decode_max_splits(n, kv_dtype);
+    int best_ct = 0;
+    int64_t best = 0;
+    for (int ct = std::min(kFastChunk / tile, tiles); ct >= 1; --ct) {
+        const int nsplit = (tiles + ct - 1) / ct;
+        if (nsplit > cap) break;  // smaller chunks only need more splits
+        const int64_t waves = (units * nsplit + slots - 1) / slots;
+        const int64_t cost = waves * (int64_t(ct) * tile + kOverheadPositions);
+        if (best_ct == 0 || cost * 100 < best * 97) {
+            best = cost;
+            best_ct = ct;
+        }
+    }
+    int chunk = best_ct * tile;
+    if (best_ct == 0) {
+        // Longer than cap fast splits: the smallest chunk that respects the cap.
+        chunk = ((n + cap - 1) / cap + tile - 1) / tile * tile;
+        chunk = std::min(chunk, max_chunk);
+    }
     DecodeSplitPlan plan;
     plan.chunk = chunk;
     plan.nsplit = (n + chunk - 1) / chunk;

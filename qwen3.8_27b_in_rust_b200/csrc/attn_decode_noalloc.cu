@@ -13,13 +13,19 @@
 // scratch is a fixed, file-scope device array, so the entry point allocates
 // nothing.
 //
-// The array holds kNoAllocScratchBytes (16 MiB) on every GPU that loads this
-// library, from module load until the process exits. Every call on a device
-// shares it and it keeps the last call's contents; nothing in it needs to
-// start at zero, because each word a call reads was written earlier in the
-// same call. Calls whose executions overlap on the GPU (different streams, or
-// different host threads without ordering) race on the array and corrupt each
-// other's results: order them.
+// The array holds kNoAllocScratchBytes (16 MiB) on every GPU whose context
+// loads this library's device code, until the process exits. Under CUDA's
+// default lazy module loading that happens at the first call on the device
+// (the address lookup below loads the module), so a caller that reserves all
+// free HBM for its own pool must make one call before reserving it. Every
+// call on a device shares the array and it keeps the last call's contents;
+// nothing in it needs to start at zero, because each word a call reads was
+// written earlier in the same call. Calls whose executions overlap on the GPU
+// (different streams, or different host threads without ordering) race on
+// the array and corrupt each other's results: order them. The looked-up
+// address is kept per device for the life of the process; a cudaDeviceReset
+// invalidates it, so a caller that resets a device must not call this entry
+// point on that device afterwards.
 #include "q38_common.cuh"
 
 #include <cmath>
@@ -90,6 +96,15 @@ extern "C" int q38_full_decode_noalloc(const float *q_norm, const float *k_norm,
     if (max_position < 0) max_position = context_length - 1;
     if (max_position >= context_length)
         return reject(Q38_ERR_ARG, "max_position must be below context_length");
+    // The split kernel streams the caller's KV cache with the bulk-copy engine
+    // (f32) or by TMA (bf16); both need 16-byte aligned rows. Every other
+    // buffer is read and written as 4-byte words.
+    auto addr = [](const void *p) { return reinterpret_cast<uintptr_t>(p); };
+    if ((addr(key_cache) | addr(value_cache)) & 15u)
+        return reject(Q38_ERR_ARG, "key_cache and value_cache must be 16-byte aligned");
+    if ((addr(q_norm) | addr(k_norm) | addr(q_and_gate) | addr(key) | addr(value) |
+         addr(positions) | addr(attention) | addr(error_bits)) & 3u)
+        return reject(Q38_ERR_ARG, "tensor arguments must be 4-byte aligned");
 
     int device = 0, sms = 0, major = 0;
     if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= kMaxDevices ||

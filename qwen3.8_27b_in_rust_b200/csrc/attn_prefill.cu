@@ -34,7 +34,8 @@
 // Precision: S = Q K^T from bf16 Q and K (the bf16 cache); O = P V in f16
 // (P rounded to f16 has 4x less error than bf16, which matters for the first
 // rows of a prompt that see only a few keys; bf16 V values are exact in f16
-// for 2^-14 <= |v| <= 65504); f32 accumulation throughout. Tolerance 2e-3.
+// for 2^-14 <= |v| <= 65504; a V value beyond 65504 sets kDevErrRange, as
+// its f16 copy would overflow); f32 accumulation throughout. Tolerance 2e-3.
 #include "q38_sm100.cuh"
 
 #include <cudaTypedefs.h>
@@ -63,25 +64,36 @@ constexpr float kRescaleThreshold = 8.0f;  // log2 units
 struct PrefillPrepParams {
     float *key;               // [nseq][count][kv_heads*256]
     const float *value;
-    __nv_bfloat16 *kcache, *vcache;  // slot base: [batch][kv_heads][ctx][256]
-    __half *v16;                     // [nseq][kv_heads][ctx][256]: V as f16 for P V
-    float *rope;                     // RoPE table, blocks of [64][128] (see kRopeBlockFloats)
+    void *kcache, *vcache;    // slot base: [batch][kv_heads][ctx][256], bf16 or f32 (kv_f32)
+    __half *v16;              // [nseq][kv_heads][ctx][256]: V as f16 for P V
+    __nv_bfloat16 *k16;       // kv_f32 only: [nseq][kv_heads][ctx][256], K as bf16 for Q K^T
+    float *rope;              // RoPE table, blocks of [64][128] (see kRopeBlockFloats)
     const float *k_norm;
-    int seq0, count, base, context_length, kv_heads;
+    int *err;
+    int seq0, count, base, context_length, kv_heads, kv_head0, kv_head_count, kv_f32;
     float theta_scale, eps;
 };
 
-// One warp per (token, kv head), 8 / kv_heads tokens per CTA. Lane l holds
-// dims [8l, 8l+8) of a head, so the RoPE partner of dim i < 32 (dim i + 32)
-// sits in lane l ^ 4 at the same slot. The CTAs of the first sequence also
-// write the RoPE table that the attention kernel applies to the queries.
+// True when a bf16 pair (one 32-bit word) holds a value that f16 cannot
+// represent (|v| > 65504, infinities included): the P V operand would
+// overflow, so the call flags kDevErrRange.
+__device__ __forceinline__ bool f16_overflow(uint32_t w) {
+    const float2 f = bf16x2_to_float2(w);
+    return fabsf(f.x) > 65504.f || fabsf(f.y) > 65504.f;
+}
+
+// One warp per (token, kv head of the call's range), 8 / kv_head_count tokens
+// per CTA. Lane l holds dims [8l, 8l+8) of a head, so the RoPE partner of dim
+// i < 32 (dim i + 32) sits in lane l ^ 4 at the same slot. The CTAs of the
+// first sequence also write the RoPE table that the attention kernel applies
+// to the queries.
 constexpr int kPrepWarps = 8;
 
 __global__ void __launch_bounds__(kPrepWarps * 32) attn_prefill_prep_kernel(PrefillPrepParams p) {
     pdl_launch_dependents();
     __shared__ float cs[kPrepWarps][32], sn[kPrepWarps][32];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int tokens = kPrepWarps / p.kv_heads;  // per CTA
+    const int tokens = kPrepWarps / p.kv_head_count;  // per CTA
     const int s = blockIdx.y;
     // rope (ops.rs:595-610): theta_i = pos * scale^i by repeated f32 products.
     if (warp < tokens) {
@@ -100,9 +112,9 @@ __global__ void __launch_bounds__(kPrepWarps * 32) attn_prefill_prep_kernel(Pref
         }
     }
     __syncthreads();
-    const int slot = warp / p.kv_heads, kvh = warp % p.kv_heads;
+    const int slot = warp / p.kv_head_count, kvh = p.kv_head0 + warp % p.kv_head_count;
     const int t = blockIdx.x * tokens + slot;
-    if (t >= p.count) return;
+    if (slot >= tokens || t >= p.count) return;
     const int pos = p.base + t;
     const size_t tok = size_t(s) * p.count + t;
     const int d0 = 8 * lane;
@@ -136,52 +148,93 @@ __global__ void __launch_bounds__(kPrepWarps * 32) attn_prefill_prep_kernel(Pref
     reinterpret_cast<float4 *>(p.key + off)[1] = make_float4(x[4], x[5], x[6], x[7]);
     const size_t row =
         ((size_t(p.seq0 + s) * p.kv_heads + kvh) * p.context_length + pos) * kAttnHeadDim + d0;
-    uint4 kk, vv;
+    const size_t srow = ((size_t(s) * p.kv_heads + kvh) * p.context_length + pos) * kAttnHeadDim + d0;
+    uint4 kk, vv, vh;
     kk.x = pack_bf16x2_rn(x[0], x[1]);
     kk.y = pack_bf16x2_rn(x[2], x[3]);
     kk.z = pack_bf16x2_rn(x[4], x[5]);
     kk.w = pack_bf16x2_rn(x[6], x[7]);
-    vv.x = pack_bf16x2_rn(va.x, va.y);
-    vv.y = pack_bf16x2_rn(va.z, va.w);
-    vv.z = pack_bf16x2_rn(vb.x, vb.y);
-    vv.w = pack_bf16x2_rn(vb.z, vb.w);
-    *reinterpret_cast<uint4 *>(p.kcache + row) = kk;
-    *reinterpret_cast<uint4 *>(p.vcache + row) = vv;
-    // The same bf16 values as f16 (exact for 2^-14 <= |v| <= 65504).
-    uint4 vh;
-    float2 f;
-    f = bf16x2_to_float2(vv.x); vh.x = pack_f16x2(f.x, f.y);
-    f = bf16x2_to_float2(vv.y); vh.y = pack_f16x2(f.x, f.y);
-    f = bf16x2_to_float2(vv.z); vh.z = pack_f16x2(f.x, f.y);
-    f = bf16x2_to_float2(vv.w); vh.w = pack_f16x2(f.x, f.y);
-    *reinterpret_cast<uint4 *>(
-        p.v16 + ((size_t(s) * p.kv_heads + kvh) * p.context_length + pos) * kAttnHeadDim + d0) = vh;
+    if (p.kv_f32) {
+        // The reference's f32 rows go to the cache; the tensor-core operands
+        // are K as bf16 and V as f16 (rounded once from f32) in the scratch.
+        float4 *kc = reinterpret_cast<float4 *>(static_cast<float *>(p.kcache) + row);
+        float4 *vc = reinterpret_cast<float4 *>(static_cast<float *>(p.vcache) + row);
+        kc[0] = make_float4(x[0], x[1], x[2], x[3]);
+        kc[1] = make_float4(x[4], x[5], x[6], x[7]);
+        vc[0] = va;
+        vc[1] = vb;
+        *reinterpret_cast<uint4 *>(p.k16 + srow) = kk;
+        const float vmax = fmaxf(fmaxf(fmaxf(fabsf(va.x), fabsf(va.y)), fmaxf(fabsf(va.z), fabsf(va.w))),
+                                 fmaxf(fmaxf(fabsf(vb.x), fabsf(vb.y)), fmaxf(fabsf(vb.z), fabsf(vb.w))));
+        if (vmax > 65504.f) set_error(p.err, kDevErrRange);
+        vh.x = pack_f16x2(va.x, va.y);
+        vh.y = pack_f16x2(va.z, va.w);
+        vh.z = pack_f16x2(vb.x, vb.y);
+        vh.w = pack_f16x2(vb.z, vb.w);
+    } else {
+        vv.x = pack_bf16x2_rn(va.x, va.y);
+        vv.y = pack_bf16x2_rn(va.z, va.w);
+        vv.z = pack_bf16x2_rn(vb.x, vb.y);
+        vv.w = pack_bf16x2_rn(vb.z, vb.w);
+        *reinterpret_cast<uint4 *>(static_cast<__nv_bfloat16 *>(p.kcache) + row) = kk;
+        *reinterpret_cast<uint4 *>(static_cast<__nv_bfloat16 *>(p.vcache) + row) = vv;
+        // The same bf16 values as f16 (exact for 2^-14 <= |v| <= 65504).
+        if (f16_overflow(vv.x) || f16_overflow(vv.y) || f16_overflow(vv.z) || f16_overflow(vv.w))
+            set_error(p.err, kDevErrRange);
+        float2 f;
+        f = bf16x2_to_float2(vv.x); vh.x = pack_f16x2(f.x, f.y);
+        f = bf16x2_to_float2(vv.y); vh.y = pack_f16x2(f.x, f.y);
+        f = bf16x2_to_float2(vv.z); vh.z = pack_f16x2(f.x, f.y);
+        f = bf16x2_to_float2(vv.w); vh.w = pack_f16x2(f.x, f.y);
+    }
+    *reinterpret_cast<uint4 *>(p.v16 + srow) = vh;
 }
 
 // --------------------------------------------------------------------------
 // P1b: f16 copy of the cached prefix's V rows
 // --------------------------------------------------------------------------
 struct PrefixParams {
-    const __nv_bfloat16 *vcache;  // slot base [batch][kv_heads][ctx][256]
+    const void *kcache, *vcache;  // slot base [batch][kv_heads][ctx][256], bf16 or f32 (kv_f32)
     __half *v16;                  // [nseq][kv_heads][ctx][256]
-    int seq0, base, context_length, kv_heads;
+    __nv_bfloat16 *k16;           // kv_f32 only: [nseq][kv_heads][ctx][256]
+    int *err;
+    int seq0, base, context_length, kv_heads, kv_head0, kv_f32;
 };
 
-// One thread per 8 values of the rows [0, base) of each (sequence, kv head).
+// One thread per 8 values of the rows [0, base) of each (sequence, kv head of
+// the call's range): V as f16 into the V scratch; for an f32 cache also K as
+// bf16 into the K scratch.
 __global__ void __launch_bounds__(256) attn_prefill_prefix_kernel(PrefixParams p) {
     const int i = blockIdx.x * 256 + threadIdx.x;
     if (i >= p.base * (kAttnHeadDim / 8)) return;
-    const int kvh = blockIdx.y, s = blockIdx.z;
+    const int kvh = p.kv_head0 + blockIdx.y, s = blockIdx.z;
     const size_t row = size_t(i) / (kAttnHeadDim / 8), c8 = size_t(i) % (kAttnHeadDim / 8);
     const size_t src =
         ((size_t(p.seq0 + s) * p.kv_heads + kvh) * p.context_length + row) * kAttnHeadDim + c8 * 8;
     const size_t dst = ((size_t(s) * p.kv_heads + kvh) * p.context_length + row) * kAttnHeadDim + c8 * 8;
-    uint4 w = *reinterpret_cast<const uint4 *>(p.vcache + src);
-    float2 f;
-    f = bf16x2_to_float2(w.x); w.x = pack_f16x2(f.x, f.y);
-    f = bf16x2_to_float2(w.y); w.y = pack_f16x2(f.x, f.y);
-    f = bf16x2_to_float2(w.z); w.z = pack_f16x2(f.x, f.y);
-    f = bf16x2_to_float2(w.w); w.w = pack_f16x2(f.x, f.y);
+    uint4 w;
+    if (p.kv_f32) {
+        const float4 *kr = reinterpret_cast<const float4 *>(static_cast<const float *>(p.kcache) + src);
+        const float4 *vr = reinterpret_cast<const float4 *>(static_cast<const float *>(p.vcache) + src);
+        const float4 ka = kr[0], kb = kr[1], va = vr[0], vb = vr[1];
+        *reinterpret_cast<uint4 *>(p.k16 + dst) =
+            make_uint4(pack_bf16x2_rn(ka.x, ka.y), pack_bf16x2_rn(ka.z, ka.w),
+                       pack_bf16x2_rn(kb.x, kb.y), pack_bf16x2_rn(kb.z, kb.w));
+        const float vmax = fmaxf(fmaxf(fmaxf(fabsf(va.x), fabsf(va.y)), fmaxf(fabsf(va.z), fabsf(va.w))),
+                                 fmaxf(fmaxf(fabsf(vb.x), fabsf(vb.y)), fmaxf(fabsf(vb.z), fabsf(vb.w))));
+        if (vmax > 65504.f) set_error(p.err, kDevErrRange);
+        w = make_uint4(pack_f16x2(va.x, va.y), pack_f16x2(va.z, va.w), pack_f16x2(vb.x, vb.y),
+                       pack_f16x2(vb.z, vb.w));
+    } else {
+        w = *reinterpret_cast<const uint4 *>(static_cast<const __nv_bfloat16 *>(p.vcache) + src);
+        if (f16_overflow(w.x) || f16_overflow(w.y) || f16_overflow(w.z) || f16_overflow(w.w))
+            set_error(p.err, kDevErrRange);
+        float2 f;
+        f = bf16x2_to_float2(w.x); w.x = pack_f16x2(f.x, f.y);
+        f = bf16x2_to_float2(w.y); w.y = pack_f16x2(f.x, f.y);
+        f = bf16x2_to_float2(w.z); w.z = pack_f16x2(f.x, f.y);
+        f = bf16x2_to_float2(w.w); w.w = pack_f16x2(f.x, f.y);
+    }
     *reinterpret_cast<uint4 *>(p.v16 + dst) = w;
 }
 
@@ -192,7 +245,8 @@ struct PrefillParams {
     const float *q_norm;  // [256]
     const float *rope;    // RoPE table, blocks of [64][128] (see kRopeBlockFloats)
     int *err;
-    int seq0, count, base, heads, kv_heads, n_qtiles;
+    int kseq0;            // sequence index of the call's first sequence in the K map's planes
+    int count, base, head0, kv_heads, n_qtiles;
     float eps;
 };
 
@@ -289,7 +343,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsPF, 1)
     const bool leader = rank == 0;
     const int n_pairs = (p.n_qtiles + 1) / 2;
     const int pair = n_pairs - 1 - int(blockIdx.x >> 1);  // latest (heaviest) pairs first
-    const int h = blockIdx.y, s = blockIdx.z;
+    const int h = p.head0 + int(blockIdx.y), s = blockIdx.z;
     const int kvh = h / kGroup;
     const int q0 = pair * kPairRows + int(rank) * kBlockQ;
     const int q_rows = min(kBlockQ, p.count - q0);        // may be <= 0 for the peer
@@ -457,7 +511,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsPF, 1)
         // ------------------------------------------------------------ K-half producer
         if (lane == 0) {
             tma_prefetch_desc(&map_k);
-            const int kplane = (p.seq0 + s) * p.kv_heads + kvh;
+            const int kplane = (p.kseq0 + s) * p.kv_heads + kvh;
             bool ok = true;
             const int gate_x = kAttnHeadDim;  // the gate half of each head's 512 values
             for (int j = 0; ok && j < nkt; ++j) {
@@ -797,17 +851,22 @@ size_t attn_prefill_rope_floats(int max_tokens) {
 
 cudaError_t launch_attn_prefill(const AttnPrefillLaunch &a, cudaStream_t stream) {
     cudaError_t e;
+    const int nkvh = a.kv_head_count;
+    if (nkvh <= 0 || nkvh > kPrepWarps || a.kv_head0 < 0 || a.kv_head0 + nkvh > a.kv_heads ||
+        (a.kv_f32 && !a.k16))
+        return cudaErrorInvalidValue;
     if (a.base > 0) {
-        PrefixParams xp{a.vcache, a.v16, a.seq0, a.base, a.context_length, a.kv_heads};
+        PrefixParams xp{a.kcache, a.vcache, a.v16, a.k16, a.err, a.seq0, a.base, a.context_length,
+                        a.kv_heads, a.kv_head0, a.kv_f32};
         const int n8 = a.base * (kAttnHeadDim / 8);
-        attn_prefill_prefix_kernel<<<dim3((n8 + 255) / 256, a.kv_heads, a.nseq), 256, 0, stream>>>(xp);
+        attn_prefill_prefix_kernel<<<dim3((n8 + 255) / 256, nkvh, a.nseq), 256, 0, stream>>>(xp);
         if ((e = cudaGetLastError()) != cudaSuccess) return e;
     }
-    if (a.kv_heads <= 0 || kPrepWarps % a.kv_heads != 0) return cudaErrorInvalidValue;
-    PrefillPrepParams pp{a.key,    a.value, a.kcache,         a.vcache,   a.v16,
-                         a.rope,   a.k_norm, a.seq0,          a.count,    a.base,
-                         a.context_length,   a.kv_heads,      a.theta_scale, a.eps};
-    const int prep_tokens = kPrepWarps / a.kv_heads;
+    PrefillPrepParams pp{a.key,  a.value, a.kcache, a.vcache, a.v16, a.k16,
+                         a.rope, a.k_norm, a.err,   a.seq0,   a.count, a.base,
+                         a.context_length, a.kv_heads, a.kv_head0, nkvh, a.kv_f32,
+                         a.theta_scale, a.eps};
+    const int prep_tokens = kPrepWarps / nkvh;
     attn_prefill_prep_kernel<<<dim3((a.count + prep_tokens - 1) / prep_tokens, a.nseq),
                                kPrepWarps * 32, 0, stream>>>(pp);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
@@ -817,16 +876,18 @@ cudaError_t launch_attn_prefill(const AttnPrefillLaunch &a, cudaStream_t stream)
                            uint64_t(a.nseq)) ||
         !make_map_rows_f32(&mo, a.attention, kAttnHeadDim, uint64_t(a.heads), uint64_t(a.count),
                            uint64_t(a.nseq)) ||
-        !make_map_16(&mk, a.kcache, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, uint64_t(a.context_length),
-                     uint64_t(a.batch) * a.kv_heads, kBlockK / 2) ||
+        // Q K^T reads bf16 K: the cache itself, or (f32 cache) the K scratch.
+        !make_map_16(&mk, a.kv_f32 ? static_cast<void *>(a.k16) : a.kcache,
+                     CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, uint64_t(a.context_length),
+                     uint64_t(a.kv_f32 ? a.nseq : a.batch) * a.kv_heads, kBlockK / 2) ||
         !make_map_16(&mv, a.v16, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, uint64_t(a.context_length),
                      uint64_t(a.nseq) * a.kv_heads, kBlockK))
         return cudaErrorInvalidValue;
 
     const int n_qtiles = (a.count + kBlockQ - 1) / kBlockQ;
     const int n_pairs = (n_qtiles + 1) / 2;
-    PrefillParams p{a.q_norm, a.rope,     a.err,     a.seq0, a.count, a.base,
-                    a.heads,  a.kv_heads, n_qtiles, a.eps};
+    PrefillParams p{a.q_norm, a.rope, a.err, a.kv_f32 ? 0 : a.seq0, a.count, a.base,
+                    kGroup * a.kv_head0, a.kv_heads, n_qtiles, a.eps};
     e = cudaFuncSetAttribute(attn_prefill_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              int(kSmemPair));
     if (e != cudaSuccess) return e;
@@ -834,7 +895,7 @@ cudaError_t launch_attn_prefill(const AttnPrefillLaunch &a, cudaStream_t stream)
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cudaLaunchConfig_t cfg{};
-    cfg.gridDim = dim3(2 * n_pairs, a.heads, a.nseq);
+    cfg.gridDim = dim3(2 * n_pairs, kGroup * nkvh, a.nseq);
     cfg.blockDim = dim3(kThreadsPF);
     cfg.dynamicSmemBytes = kSmemPair;
     cfg.stream = stream;

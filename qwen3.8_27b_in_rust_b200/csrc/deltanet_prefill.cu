@@ -60,16 +60,25 @@ struct ConvParams {
     float *bounds;       // [nseq][nseg][3][qkv_dim]: inputs preceding each segment
     int seq0, count, qkv_dim, nseg;
     int qk_channels;     // 2 * qk_heads * 128: the q and k channels, L2-normalised per head
+    int v_head0;         // the call's first value head: grid block qk_channels/128 + i is
+                         // the channel block of value head v_head0 + i
     float eps;
     int *err;
 };
+
+// Channel block (128 channels) of grid block bx: every q and k block, then the
+// blocks of the call's value heads.
+__device__ __forceinline__ int conv_channel_block(const ConvParams &p, int bx) {
+    const int qk_blocks = p.qk_channels / 128;
+    return bx < qk_blocks ? bx : qk_blocks + p.v_head0 + (bx - qk_blocks);
+}
 
 constexpr int kSeg = 64;  // tokens per conv segment
 
 // The three inputs that precede segment g: the carried conv state for g = 0,
 // otherwise the (not yet convolved) inputs g*kSeg-3 .. g*kSeg-1.
 __global__ void __launch_bounds__(128) linear_prefill_conv_bounds_kernel(ConvParams p) {
-    const int c = blockIdx.x * 128 + threadIdx.x;
+    const int c = conv_channel_block(p, blockIdx.x) * 128 + threadIdx.x;
     const int g = blockIdx.y, s = blockIdx.z;
     if (c >= p.qkv_dim) return;
     float *dst = p.bounds + (size_t(s) * p.nseg + g) * 3 * p.qkv_dim + c;
@@ -99,7 +108,7 @@ __global__ void __launch_bounds__(128) linear_prefill_conv_kernel(const __grid_c
     using namespace sm100;
     extern __shared__ __align__(128) float tile[];  // [kSeg][128]
     __shared__ __align__(8) uint64_t bar;
-    const int cb = blockIdx.x, g = blockIdx.y, s = blockIdx.z;
+    const int cb = conv_channel_block(p, blockIdx.x), g = blockIdx.y, s = blockIdx.z;
     const int c = cb * 128 + threadIdx.x;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const bool live = c < p.qkv_dim;
@@ -176,14 +185,14 @@ struct NormParams {
     float *qkv;
     float *beta, *alpha;  // [nseq][count][v_heads]
     const float *dt_bias, *ssm_a;
-    int count, qk_heads, v_heads, qkv_dim;
+    int count, qk_heads, v_heads, qkv_dim, v_head0, v_head_count;
     float eps;
 };
 
 __global__ void __launch_bounds__(256) linear_prefill_norm_kernel(NormParams p) {
     const int t = blockIdx.x, s = blockIdx.y;
     const size_t tok = size_t(s) * p.count + t;
-    for (int h = threadIdx.x; h < p.v_heads; h += blockDim.x) {
+    for (int h = p.v_head0 + threadIdx.x; h < p.v_head0 + p.v_head_count; h += blockDim.x) {
         float *bp = p.beta + tok * p.v_heads + h;
         float *ap = p.alpha + tok * p.v_heads + h;
         *bp = sigmoidf_ref(*bp);
@@ -207,7 +216,7 @@ struct LocalParams {
     float *ut_out;               // [planes][64][128]          Ut (f32)
     float *eg_out;               // [planes][64]               e^{gamma_r}
     int *err;
-    int count, nchunk, qk_heads, v_heads, qkv_dim;
+    int count, nchunk, qk_heads, v_heads, qkv_dim, v_head0, v_head_count;
 };
 
 // (a, b) -> bf16x2 pairs hi = bf16(a, b), lo = bf16(a - hi.a, b - hi.b): hi + lo
@@ -290,6 +299,13 @@ __global__ void __launch_bounds__(256, 2) linear_prefill_local_kernel(LocalParam
     const int chunk = blockIdx.x, kh = blockIdx.y, s = blockIdx.z;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int t0 = chunk * kC;
+    // The call's value heads that read key head kh; none: nothing to do.
+    auto in_call = [&](int h) { return h >= p.v_head0 && h < p.v_head0 + p.v_head_count; };
+    {
+        bool any = false;
+        for (int h = kh; h < p.v_heads; h += p.qk_heads) any = any || in_call(h);
+        if (!any) return;
+    }
     const int qk_dim = p.qk_heads * kD;
     const float *rows = p.qkv + (size_t(s) * p.count + t0) * p.qkv_dim;  // the chunk's first row
     auto row_ok = [&](int r) { return t0 + r < p.count; };
@@ -372,8 +388,10 @@ __global__ void __launch_bounds__(256, 2) linear_prefill_local_kernel(LocalParam
 
     const uint32_t idesc_x = idesc_bf16_f32(128, kD, 0, 1);
     const uint32_t d_w = tmem, d_u = tmem + kD;  // W columns 0-127, Ut columns 128-255
-    int head_i = 0;
-    for (int h = kh; h < p.v_heads; h += p.qk_heads, ++head_i) {
+    int head_i = -1;  // value heads of this CTA processed so far, minus one
+    for (int h = kh; h < p.v_heads; h += p.qk_heads) {
+        if (!in_call(h)) continue;
+        ++head_i;
         const size_t plane = (size_t(s) * p.nchunk + chunk) * p.v_heads + h;
         fence_before_sync();
         __syncthreads();  // previous head done with R, gam/bet and TMEM
@@ -727,7 +745,7 @@ struct StateTcParams {
     float *delta_state;   // slot base [batch][v_heads][128][128]
     float *o_out;         // [nseq][count][v_heads*128]
     int *err;
-    int seq0, count, nchunk, qk_heads, v_heads;
+    int seq0, count, nchunk, qk_heads, v_heads, v_head0;
 };
 
 struct __align__(8) StateTcBarriers {
@@ -771,7 +789,7 @@ __global__ void __launch_bounds__(kThreadsLS, 1)
     __shared__ volatile int abort_flag;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int h = blockIdx.x, s = blockIdx.y;
+    const int h = p.v_head0 + int(blockIdx.x), s = blockIdx.y;
     auto plane = [&](int c) { return (s * p.nchunk + c) * p.v_heads + h; };
 
     if (threadIdx.x == 0) {
@@ -1096,7 +1114,7 @@ struct OutParams {
     const float *z;
     const float *ssm_norm;
     float *attention;  // in: O; out: normalised, gated
-    int count, v_heads;
+    int count, v_heads, v_head0, v_head_count;
     float eps;
 };
 
@@ -1104,7 +1122,7 @@ __global__ void __launch_bounds__(256) linear_prefill_out_kernel(OutParams p) {
     const int t = blockIdx.x, s = blockIdx.y;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const size_t base = (size_t(s) * p.count + t) * size_t(p.v_heads) * kD;
-    for (int h = warp; h < p.v_heads; h += 8) {
+    for (int h = p.v_head0 + warp; h < p.v_head0 + p.v_head_count; h += 8) {
         float4 *o4 = reinterpret_cast<float4 *>(p.attention + base + h * kD) + lane;
         const float4 z4 = reinterpret_cast<const float4 *>(p.z + base + h * kD)[lane];
         const float4 w4 = reinterpret_cast<const float4 *>(p.ssm_norm)[lane];
@@ -1135,9 +1153,12 @@ cudaError_t launch_linear_prefill(const LinearPrefillLaunch &a, cudaStream_t str
     // The segment boundaries live at the start of the W scratch, which L3
     // only writes after the conv has finished.
     const int nseg = (a.count + kSeg - 1) / kSeg;
+    if (a.v_head_count <= 0 || a.v_head0 < 0 || a.v_head0 + a.v_head_count > a.v_heads)
+        return cudaErrorInvalidValue;
     ConvParams cp{a.qkv, a.conv_state, a.conv_w, a.scratch, a.seq0, a.count, qkv_dim, nseg,
-                  2 * a.qk_heads * kD, a.eps, a.err};
-    const dim3 conv_grid((qkv_dim + 127) / 128, nseg, a.nseq);
+                  2 * a.qk_heads * kD, a.v_head0, a.eps, a.err};
+    // Every q and k channel block, and the blocks of the call's value heads.
+    const dim3 conv_grid(2 * a.qk_heads + a.v_head_count, nseg, a.nseq);
     linear_prefill_conv_bounds_kernel<<<conv_grid, 128, 0, stream>>>(cp);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
@@ -1152,7 +1173,7 @@ cudaError_t launch_linear_prefill(const LinearPrefillLaunch &a, cudaStream_t str
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
 
     NormParams np{a.qkv, a.beta, a.alpha, a.dt_bias, a.ssm_a, a.count, a.qk_heads, a.v_heads,
-                  qkv_dim, a.eps};
+                  qkv_dim, a.v_head0, a.v_head_count, a.eps};
     linear_prefill_norm_kernel<<<dim3(a.count, a.nseq), 256, 0, stream>>>(np);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
 
@@ -1164,7 +1185,7 @@ cudaError_t launch_linear_prefill(const LinearPrefillLaunch &a, cudaStream_t str
     float *ut = reinterpret_cast<float *>(k2 + per * 2 * kD * kC);
     float *eg = ut + per * kC * kD;
     LocalParams lp{a.qkv, a.beta, a.alpha, w2, q2, p2, k2, ut, eg, a.err, a.count, nchunk,
-                   a.qk_heads, a.v_heads, qkv_dim};
+                   a.qk_heads, a.v_heads, qkv_dim, a.v_head0, a.v_head_count};
     if ((e = cudaFuncSetAttribute(linear_prefill_local_kernel,
                                   cudaFuncAttributeMaxDynamicSharedMemorySize, int(kLocSmem))) !=
         cudaSuccess)
@@ -1179,16 +1200,17 @@ cudaError_t launch_linear_prefill(const LinearPrefillLaunch &a, cudaStream_t str
         !make_map_bf16_ls(&mk, k2, kD, kC, 2 * per, kC))
         return cudaErrorInvalidValue;
     StateTcParams sp{ut, eg, a.delta_state, a.attention, a.err, a.seq0, a.count, nchunk,
-                     a.qk_heads, a.v_heads};
+                     a.qk_heads, a.v_heads, a.v_head0};
     if ((e = cudaFuncSetAttribute(linear_prefill_state_kernel,
                                   cudaFuncAttributeMaxDynamicSharedMemorySize, int(kSmemLS))) !=
         cudaSuccess)
         return e;
-    linear_prefill_state_kernel<<<dim3(a.v_heads, a.nseq), kThreadsLS, kSmemLS, stream>>>(
+    linear_prefill_state_kernel<<<dim3(a.v_head_count, a.nseq), kThreadsLS, kSmemLS, stream>>>(
         mw, mq, mp, mk, sp);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
 
-    OutParams op{a.z, a.ssm_norm, a.attention, a.count, a.v_heads, a.eps};
+    OutParams op{a.z, a.ssm_norm, a.attention, a.count, a.v_heads, a.v_head0, a.v_head_count,
+                 a.eps};
     linear_prefill_out_kernel<<<dim3(a.count, a.nseq), 256, 0, stream>>>(op);
     return cudaGetLastError();
 }

@@ -22,6 +22,7 @@ namespace q38 {
 constexpr int kDevErrPosition = 1;   // a position outside [0, context_length)
 constexpr int kDevErrTimeout = 2;    // a bounded wait gave up
 constexpr int kDevErrShape = 4;      // a launch-shape invariant failed
+constexpr int kDevErrRange = 8;      // a V value outside the f16 range of the prefill's P V operand
 
 // Bounded waits give up after this many nanoseconds of %globaltimer.
 constexpr uint64_t kWaitTimeoutNs = 1000000000ull;
@@ -77,17 +78,22 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
 }
 
 // Waits for the barrier phase with the given parity to complete, for at most
-// kWaitTimeoutNs. Returns false on timeout; the caller records the error and
-// abandons the work.
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
+// limit_ns nanoseconds. Returns false on timeout; the caller records the
+// error and abandons the work.
+__device__ __forceinline__ bool mbar_wait_ns(uint64_t *bar, uint32_t parity, uint64_t limit_ns) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = global_timer_ns();
     for (;;) {
 #pragma unroll 1
         for (int i = 0; i < 64; ++i)
             if (mbar_try_wait(bar, parity)) return true;
-        if (global_timer_ns() - t0 > kWaitTimeoutNs) return false;
+        if (global_timer_ns() - t0 > limit_ns) return false;
     }
+}
+
+// The same with the library's limit, kWaitTimeoutNs.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
+    return mbar_wait_ns(bar, parity, kWaitTimeoutNs);
 }
 
 // Global -> shared bulk copy completing on `bar` (bytes: multiple of 16,

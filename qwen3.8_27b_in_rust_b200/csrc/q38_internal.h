@@ -92,6 +92,17 @@ struct q38_state {
     // state kernel, and its events (created on first use).
     cudaStream_t host_out = nullptr;
     cudaEvent_t host_ev_prep = nullptr, host_ev_back = nullptr;
+    // Pinned word the host-pointer calls read the device error bits into.
+    int *host_err = nullptr;
+    // Error-path testing (q38_state_set_debug).
+    int debug_flags = 0;
+    uint64_t debug_wait_ns = 0;
+    // Split-sequence decode over NCCL (q38_state_reserve_split).
+    float *split_local = nullptr;     // [batch][heads][258]
+    float *split_gathered = nullptr;  // [split_ranks][batch][heads][258]
+    int split_ranks = 0;
+    // f32-cache prefill: the K rows as bf16 for the tensor cores.
+    __nv_bfloat16 *prefill_k16 = nullptr;  // [v16_seqs][kv_heads][context][256]
 };
 
 namespace q38 {
@@ -103,6 +114,12 @@ inline int recurrent_index(int layer) { return layer - (layer + 1) / 4; }
 
 // Sets the calling thread's q38_last_error() message (q38attn.cu).
 void record_error(const char *msg);
+
+// NCCL, resolved at run time (q38_nccl.cu). Both return a Q38 status and
+// record the reason.
+int nccl_comm_ranks(void *comm, int *nranks);
+int nccl_all_gather_f32(void *comm, const float *send, float *recv, size_t count,
+                        cudaStream_t stream);
 
 // Kernel launchers (attn_decode.cu, deltanet_decode.cu).
 struct AttnDecodeLaunch {
@@ -120,6 +137,8 @@ struct AttnDecodeLaunch {
     float theta_scale, eps;
     int pos_offset = 0;            // first global position held by this cache (sharding)
     float *partial_out = nullptr;  // non-null: packed (o, m, l) partials instead of output
+    uint64_t wait_ns = 0;          // bounded-wait limit of the split kernel (0: the default)
+    int skip_kv_loads = 0;         // error-path testing (Q38_DEBUG_SKIP_KV_LOADS)
 };
 cudaError_t launch_attn_decode(const AttnDecodeLaunch &a, int sm_count, cudaStream_t stream);
 cudaError_t launch_attn_merge_shards(const float *partials, int nparts, int batch, int heads,
@@ -135,11 +154,14 @@ struct AttnPrefillLaunch {
     const float *value;
     float *attention;         // [nseq][count][heads*256]
     float *rope;              // scratch: RoPE table (attn_prefill_rope_floats)
-    __nv_bfloat16 *kcache, *vcache;  // slot base [batch][kv_heads][ctx][256]
-    __half *v16;                     // scratch [nseq][kv_heads][ctx][256]
+    void *kcache, *vcache;    // slot base [batch][kv_heads][ctx][256], bf16 or f32
+    __half *v16;              // scratch [nseq][kv_heads][ctx][256]: V as f16
+    __nv_bfloat16 *k16;       // f32 cache only: scratch [nseq][kv_heads][ctx][256], K as bf16
     const float *q_norm, *k_norm;
     int *err;
     int batch, seq0, nseq, count, base, context_length, heads, kv_heads;
+    int kv_head0, kv_head_count;  // the KV heads this call covers
+    int kv_f32;                   // the cache holds f32 rows
     float theta_scale, eps;
 };
 cudaError_t launch_attn_prefill(const AttnPrefillLaunch &a, cudaStream_t stream);
@@ -157,6 +179,7 @@ struct LinearPrefillLaunch {
     float *scratch;             // linear_prefill_scratch_floats(nseq*nchunk, v_heads)
     int *err;                   // device error bits
     int seq0, nseq, count, qk_heads, v_heads;
+    int v_head0, v_head_count;  // the value heads this call covers
     float eps;
 };
 cudaError_t launch_linear_prefill(const LinearPrefillLaunch &a, cudaStream_t stream);

@@ -171,6 +171,10 @@ void free_state(q38_state *st) {
     cudaFree(st->prefill_stage);
     cudaFree(st->ckpt_conv);
     cudaFree(st->ckpt_delta);
+    cudaFree(st->split_local);
+    cudaFree(st->split_gathered);
+    cudaFree(st->prefill_k16);
+    if (st->host_err) cudaFreeHost(st->host_err);
     if (st->host_ev_prep) cudaEventDestroy(st->host_ev_prep);
     if (st->host_ev_back) cudaEventDestroy(st->host_ev_back);
     if (st->host_out) cudaStreamDestroy(st->host_out);
@@ -184,6 +188,29 @@ cudaError_t ensure_host_out(q38_state *st) {
     if (e == cudaSuccess) e = cudaEventCreateWithFlags(&st->host_ev_back, cudaEventDisableTiming);
     if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&st->host_out, cudaStreamNonBlocking);
     return e;
+}
+
+// Host-pointer calls: enqueues on `s` a copy of the state's device error bits
+// into a pinned host word (read after the call's final synchronisation by
+// host_call_status).
+cudaError_t enqueue_error_read(q38_state *st, cudaStream_t s) {
+    if (!st->host_err) {
+        cudaError_t e = cudaHostAlloc(reinterpret_cast<void **>(&st->host_err), sizeof(int),
+                                      cudaHostAllocDefault);
+        if (e != cudaSuccess) return e;
+        *st->host_err = 0;
+    }
+    return cudaMemcpyAsync(st->host_err, st->d_err, sizeof(int), cudaMemcpyDeviceToHost, s);
+}
+
+// Status of a host-pointer call once its stream has synchronised: a bounded
+// device wait that gave up (the bits stay set until q38_state_errors reads
+// and clears them) is Q38_ERR_TIMEOUT.
+int host_call_status(const q38_state *st) {
+    if (st->host_err && (*st->host_err & Q38_DEVERR_TIMEOUT))
+        return fail(Q38_ERR_TIMEOUT, "a bounded device wait gave up (device error bits 0x%x)",
+                    *st->host_err);
+    return Q38_OK;
 }
 
 // True when p lies in pinned host memory mapped into `device`'s address
@@ -246,6 +273,8 @@ int prepare_full_decode(q38_ctx *ctx, q38_state *st, int layer, int batch,
     a->max_splits = st->max_splits;
     a->theta_scale = ctx->theta_scale;
     a->eps = g.rms_eps;
+    a->wait_ns = st->debug_wait_ns;
+    a->skip_kv_loads = (st->debug_flags & Q38_DEBUG_SKIP_KV_LOADS) ? 1 : 0;
     return Q38_OK;
 }
 
@@ -545,6 +574,14 @@ int q38_state_errors(q38_state *st, int *bits) {
     return Q38_OK;
 }
 
+int q38_state_set_debug(q38_state *st, int flags, uint64_t wait_ns) {
+    if (!st) return fail(Q38_ERR_ARG, "null state");
+    if (flags & ~Q38_DEBUG_SKIP_KV_LOADS) return fail(Q38_ERR_ARG, "unknown debug flags 0x%x", flags);
+    st->debug_flags = flags;
+    st->debug_wait_ns = wait_ns;
+    return Q38_OK;
+}
+
 int q38_state_full_slot(q38_state *st, int layer, void **key_cache, void **value_cache,
                         size_t *bytes_each) {
     if (!st) return fail(Q38_ERR_ARG, "null state");
@@ -710,6 +747,49 @@ int q38_attn_merge_shards(q38_ctx *ctx, int nparts, int batch, const float *part
     return Q38_OK;
 }
 
+int q38_state_reserve_split(q38_state *st, int nranks) {
+    if (!st) return fail(Q38_ERR_ARG, "null state");
+    if (nranks <= 0) return fail(Q38_ERR_ARG, "nranks must be positive");
+    if (st->split_ranks == nranks) return Q38_OK;
+    DeviceGuard guard(st->ctx->device);
+    cudaFree(st->split_local);
+    cudaFree(st->split_gathered);
+    st->split_local = st->split_gathered = nullptr;
+    st->split_ranks = 0;
+    const size_t per = size_t(st->batch) * st->ctx->geom.attn_heads * (q38::kAttnHeadDim + 2);
+    Q38_CUDA(cudaMalloc(&st->split_local, per * sizeof(float)));
+    Q38_CUDA(cudaMalloc(&st->split_gathered, size_t(nranks) * per * sizeof(float)));
+    st->split_ranks = nranks;
+    return Q38_OK;
+}
+
+int q38_full_decode_split(q38_ctx *ctx, q38_state *st, int layer, int batch,
+                          const float *q_and_gate, float *key, const float *value,
+                          const int32_t *positions, int max_position, int pos_offset,
+                          void *nccl_comm, float *attention, void *stream) {
+    if (int rc = check_state(ctx, st)) return rc;
+    if (!nccl_comm || !attention) return fail(Q38_ERR_ARG, "null communicator or attention");
+    if (!st->split_local) return fail(Q38_ERR_ARG, "q38_state_reserve_split was not called");
+    if (batch <= 0 || batch > st->batch)
+        return fail(Q38_ERR_ARG, "batch %d outside 1..%d", batch, st->batch);
+    int nranks = 0;
+    if (int rc = q38::nccl_comm_ranks(nccl_comm, &nranks)) return rc;
+    if (nranks != st->split_ranks)
+        return fail(Q38_ERR_ARG, "the communicator has %d ranks, the split buffers %d", nranks,
+                    st->split_ranks);
+    if (int rc = q38_full_decode_shard(ctx, st, layer, batch, q_and_gate, key, value, positions,
+                                       max_position, pos_offset, st->split_local, stream))
+        return rc;
+    DeviceGuard guard(ctx->device);
+    // Every rank's [batch][heads][258] partials, rank-major, in this GPU's memory.
+    const size_t count = size_t(batch) * ctx->geom.attn_heads * (q38::kAttnHeadDim + 2);
+    if (int rc = q38::nccl_all_gather_f32(nccl_comm, st->split_local, st->split_gathered, count,
+                                          static_cast<cudaStream_t>(stream)))
+        return rc;
+    return q38_attn_merge_shards(ctx, nranks, batch, st->split_gathered, q_and_gate, attention,
+                                 stream);
+}
+
 int q38_linear_decode(q38_ctx *ctx, q38_state *st, int layer, int batch, float *qkv,
                       const float *z, float *beta, float *alpha, float *attention,
                       void *stream) {
@@ -762,10 +842,12 @@ int q38_state_reserve_prefill(q38_state *st, int max_tokens) {
     DeviceGuard guard(st->ctx->device);
     cudaFree(st->prefill_rope);
     cudaFree(st->prefill_v16);
+    cudaFree(st->prefill_k16);
     cudaFree(st->prefill_lin);
     cudaFree(st->prefill_stage);
     st->prefill_rope = nullptr;
     st->prefill_v16 = nullptr;
+    st->prefill_k16 = nullptr;
     st->prefill_v16_seqs = 0;
     st->prefill_lin = nullptr;
     st->prefill_stage = nullptr;
@@ -784,6 +866,11 @@ int q38_state_reserve_prefill(q38_state *st, int max_tokens) {
         // Rows past a prompt's last position sit in its last key tile with
         // P = 0; they must hold finite values (0 * NaN would be NaN).
         Q38_CUDA(cudaMemset(st->prefill_v16, 0, v16_bytes));
+        if (st->kv_dtype == Q38_KV_F32) {
+            // An f32 cache keeps the reference's rows; Q K^T reads a bf16 copy.
+            Q38_CUDA(cudaMalloc(&st->prefill_k16, v16_bytes));
+            Q38_CUDA(cudaMemset(st->prefill_k16, 0, v16_bytes));
+        }
         st->prefill_v16_seqs = seqs;
     }
     if (st->linear_slots > 0) {
@@ -805,14 +892,20 @@ int q38_state_reserve_prefill(q38_state *st, int max_tokens) {
     return Q38_OK;
 }
 
-int q38_full_prefill(q38_ctx *ctx, q38_state *st, int layer, int seq0, int nseq, int count,
-                     int base_position, const float *q_and_gate, float *key, const float *value,
-                     float *attention, void *stream) {
+namespace {
+
+int full_prefill_impl(q38_ctx *ctx, q38_state *st, int layer, int seq0, int nseq, int count,
+                      int base_position, int kv_head0, int kv_head_count,
+                      const float *q_and_gate, float *key, const float *value, float *attention,
+                      void *stream) {
     if (int rc = check_state(ctx, st)) return rc;
     int slot;
     if (int rc = full_slot_of(st, layer, &slot)) return rc;
-    if (st->kv_dtype != Q38_KV_BF16)
-        return fail(Q38_ERR_ARG, "tensor-core prefill needs a bf16 KV cache");
+    if (kv_head_count <= 0 || kv_head0 < 0 || kv_head0 + kv_head_count > ctx->geom.attn_kv_heads)
+        return fail(Q38_ERR_ARG, "KV heads [%d, %d) outside 0..%d", kv_head0,
+                    kv_head0 + kv_head_count, ctx->geom.attn_kv_heads);
+    if (kv_head_count > 8)
+        return fail(Q38_ERR_ARG, "a prefill call covers at most 8 KV heads (got %d)", kv_head_count);
     if (nseq <= 0 || seq0 < 0 || seq0 + nseq > st->batch)
         return fail(Q38_ERR_ARG, "sequences [%d, %d) outside the state's %d", seq0, seq0 + nseq,
                     st->batch);
@@ -839,8 +932,12 @@ int q38_full_prefill(q38_ctx *ctx, q38_state *st, int layer, int seq0, int nseq,
     a.attention = attention;
     a.rope = st->prefill_rope;
     a.v16 = st->prefill_v16;
-    a.kcache = reinterpret_cast<__nv_bfloat16 *>(kv_seq_base(st, st->kcache, slot, 0));
-    a.vcache = reinterpret_cast<__nv_bfloat16 *>(kv_seq_base(st, st->vcache, slot, 0));
+    a.k16 = st->prefill_k16;
+    a.kv_f32 = st->kv_dtype == Q38_KV_F32 ? 1 : 0;
+    a.kv_head0 = kv_head0;
+    a.kv_head_count = kv_head_count;
+    a.kcache = kv_seq_base(st, st->kcache, slot, 0);
+    a.vcache = kv_seq_base(st, st->vcache, slot, 0);
     a.q_norm = it->second.q_norm;
     a.k_norm = it->second.k_norm;
     a.err = st->d_err;
@@ -860,12 +957,15 @@ int q38_full_prefill(q38_ctx *ctx, q38_state *st, int layer, int seq0, int nseq,
     return Q38_OK;
 }
 
-int q38_linear_prefill(q38_ctx *ctx, q38_state *st, int layer, int seq0, int nseq, int count,
-                       float *qkv, const float *z, float *beta, float *alpha, float *attention,
-                       void *stream) {
+int linear_prefill_impl(q38_ctx *ctx, q38_state *st, int layer, int seq0, int nseq, int count,
+                        int v_head0, int v_head_count, float *qkv, const float *z, float *beta,
+                        float *alpha, float *attention, void *stream) {
     if (int rc = check_state(ctx, st)) return rc;
     int slot;
     if (int rc = linear_slot_of(st, layer, &slot)) return rc;
+    if (v_head_count <= 0 || v_head0 < 0 || v_head0 + v_head_count > ctx->geom.linear_v_heads)
+        return fail(Q38_ERR_ARG, "value heads [%d, %d) outside 0..%d", v_head0,
+                    v_head0 + v_head_count, ctx->geom.linear_v_heads);
     if (nseq <= 0 || seq0 < 0 || seq0 + nseq > st->batch)
         return fail(Q38_ERR_ARG, "sequences [%d, %d) outside the state's %d", seq0, seq0 + nseq,
                     st->batch);
@@ -902,11 +1002,46 @@ int q38_linear_prefill(q38_ctx *ctx, q38_state *st, int layer, int seq0, int nse
     a.count = count;
     a.qk_heads = ctx->geom.linear_qk_heads;
     a.v_heads = ctx->geom.linear_v_heads;
+    a.v_head0 = v_head0;
+    a.v_head_count = v_head_count;
     a.eps = ctx->geom.rms_eps;
     DeviceGuard guard(ctx->device);
     cudaError_t e = q38::launch_linear_prefill(a, static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return cuda_fail(e, "DeltaNet prefill launch");
     return Q38_OK;
+}
+
+}  // namespace
+
+int q38_full_prefill(q38_ctx *ctx, q38_state *st, int layer, int seq0, int nseq, int count,
+                     int base_position, const float *q_and_gate, float *key, const float *value,
+                     float *attention, void *stream) {
+    if (int rc = check_ctx(ctx)) return rc;
+    return full_prefill_impl(ctx, st, layer, seq0, nseq, count, base_position, 0,
+                             ctx->geom.attn_kv_heads, q_and_gate, key, value, attention, stream);
+}
+
+int q38_full_prefill_heads(q38_ctx *ctx, q38_state *st, int layer, int seq0, int nseq,
+                           int count, int base_position, int kv_head0, int kv_head_count,
+                           const float *q_and_gate, float *key, const float *value,
+                           float *attention, void *stream) {
+    return full_prefill_impl(ctx, st, layer, seq0, nseq, count, base_position, kv_head0,
+                             kv_head_count, q_and_gate, key, value, attention, stream);
+}
+
+int q38_linear_prefill(q38_ctx *ctx, q38_state *st, int layer, int seq0, int nseq, int count,
+                       float *qkv, const float *z, float *beta, float *alpha, float *attention,
+                       void *stream) {
+    if (int rc = check_ctx(ctx)) return rc;
+    return linear_prefill_impl(ctx, st, layer, seq0, nseq, count, 0, ctx->geom.linear_v_heads, qkv,
+                               z, beta, alpha, attention, stream);
+}
+
+int q38_linear_prefill_heads(q38_ctx *ctx, q38_state *st, int layer, int seq0, int nseq,
+                             int count, int v_head0, int v_head_count, float *qkv, const float *z,
+                             float *beta, float *alpha, float *attention, void *stream) {
+    return linear_prefill_impl(ctx, st, layer, seq0, nseq, count, v_head0, v_head_count, qkv, z,
+                               beta, alpha, attention, stream);
 }
 
 int q38_full_prefill_host(q38_ctx *ctx, q38_state *st, int layer, int seq0, int nseq, int count,
@@ -948,8 +1083,9 @@ int q38_full_prefill_host(q38_ctx *ctx, q38_state *st, int layer, int seq0, int 
                             cudaMemcpyDeviceToHost, s));
         Q38_CUDA(copy_piece(key, d_k, nseq, count, t0, n, ctx->kv_dim, cudaMemcpyDeviceToHost, s));
     }
+    Q38_CUDA(enqueue_error_read(st, s));
     Q38_CUDA(cudaStreamSynchronize(s));
-    return Q38_OK;
+    return host_call_status(st);
 }
 
 int q38_linear_prefill_host(q38_ctx *ctx, q38_state *st, int layer, int seq0, int nseq,
@@ -992,8 +1128,9 @@ int q38_linear_prefill_host(q38_ctx *ctx, q38_state *st, int layer, int seq0, in
         Q38_CUDA(copy_piece(beta, d_b, nseq, count, t0, n, vh, cudaMemcpyDeviceToHost, s));
         Q38_CUDA(copy_piece(alpha, d_a, nseq, count, t0, n, vh, cudaMemcpyDeviceToHost, s));
     }
+    Q38_CUDA(enqueue_error_read(st, s));
     Q38_CUDA(cudaStreamSynchronize(s));
-    return Q38_OK;
+    return host_call_status(st);
 }
 
 int q38_full_decode_host(q38_ctx *ctx, q38_state *st, int layer, int batch,
@@ -1028,8 +1165,9 @@ int q38_full_decode_host(q38_ctx *ctx, q38_state *st, int layer, int batch,
         return rc;
     if (!att_mapped) Q38_CUDA(cudaMemcpyAsync(attention, d_out, nq * 4, cudaMemcpyDeviceToHost, s));
     Q38_CUDA(cudaMemcpyAsync(key, d_k, nkv * 4, cudaMemcpyDeviceToHost, s));
+    Q38_CUDA(enqueue_error_read(st, s));
     Q38_CUDA(cudaStreamSynchronize(s));
-    return Q38_OK;
+    return host_call_status(st);
 }
 
 int q38_linear_decode_host(q38_ctx *ctx, q38_state *st, int layer, int batch, float *qkv,
@@ -1071,8 +1209,9 @@ int q38_linear_decode_host(q38_ctx *ctx, q38_state *st, int layer, int batch, fl
     if (!att_mapped)
         Q38_CUDA(cudaMemcpyAsync(attention, d_out, nv * 4, cudaMemcpyDeviceToHost, s));
     Q38_CUDA(cudaStreamWaitEvent(s, st->host_ev_back, 0));  // later work on s follows them
+    Q38_CUDA(enqueue_error_read(st, s));
     Q38_CUDA(cudaStreamSynchronize(s));
-    return Q38_OK;
+    return host_call_status(st);
 }
 
 int q38_linear_core(q38_ctx *ctx, q38_state *st, int layer, float *conv_state,

@@ -29,7 +29,8 @@ from typing import Optional
 
 import numpy as np
 
-from ._lib import (Q38_DEVERR_POSITION, Q38_DEVERR_SHAPE, Q38_DEVERR_TIMEOUT, Q38_ERR_ARG,
+from ._lib import (Q38_DEBUG_SKIP_KV_LOADS, Q38_DEVERR_RANGE, Q38_NCCL_ID_BYTES,
+                   Q38_DEVERR_POSITION, Q38_DEVERR_SHAPE, Q38_DEVERR_TIMEOUT, Q38_ERR_ARG,
                    Q38_ERR_CUDA, Q38_ERR_TIMEOUT, Q38_GGML_BF16, Q38_GGML_F16, Q38_GGML_F32,
                    Q38_GGML_IQ4_NL, Q38_GGML_IQ4_XS, Q38_GGML_Q2_K, Q38_GGML_Q3_K,
                    Q38_GGML_Q4_K, Q38_GGML_Q5_K, Q38_GGML_Q6_K, Q38_GGML_Q8_0, Q38_KV_BF16, Q38_KV_F32, Q38_OK, Q38_Q8K_BLOCK_BYTES, Q38Error,
@@ -38,7 +39,8 @@ from ._lib import (Q38_DEVERR_POSITION, Q38_DEVERR_SHAPE, Q38_DEVERR_TIMEOUT, Q3
 __all__ = [
     "Context", "State", "Q38Error", "Q38Geom", "geometry", "load", "last_error",
     "Q38_OK", "Q38_ERR_ARG", "Q38_ERR_CUDA", "Q38_ERR_TIMEOUT", "Q38_KV_F32", "Q38_KV_BF16",
-    "Q38_DEVERR_POSITION", "Q38_DEVERR_TIMEOUT", "Q38_DEVERR_SHAPE",
+    "Q38_DEVERR_POSITION", "Q38_DEVERR_TIMEOUT", "Q38_DEVERR_SHAPE", "Q38_DEVERR_RANGE",
+    "Q38_DEBUG_SKIP_KV_LOADS", "Q38_NCCL_ID_BYTES", "nccl_unique_id", "NcclComm",
     "is_full_attention", "full_index", "recurrent_index", "gguf_read_f32", "Weight",
     "Q38_GGML_F32", "Q38_GGML_F16", "Q38_GGML_BF16", "Q38_GGML_Q8_0", "Q38_GGML_Q2_K",
     "Q38_GGML_Q3_K", "Q38_GGML_Q4_K", "Q38_GGML_Q5_K", "Q38_GGML_Q6_K", "Q38_GGML_IQ4_NL",
@@ -201,6 +203,16 @@ class State:
     def reserve_prefill(self, max_tokens: int) -> None:
         check(self._lib.q38_state_reserve_prefill(self.handle, max_tokens))
 
+    def reserve_split(self, nranks: int) -> None:
+        """Sizes the buffers of split-sequence decode over `nranks` ranks."""
+        check(self._lib.q38_state_reserve_split(self.handle, nranks))
+
+    def set_debug(self, flags: int = 0, wait_ns: int = 0) -> None:
+        """Error-path testing (q38_state_set_debug): Q38_DEBUG_SKIP_KV_LOADS
+        makes the decode's split kernel load nothing, so its waits run out
+        after wait_ns; set_debug() restores normal operation."""
+        check(self._lib.q38_state_set_debug(self.handle, flags, wait_ns))
+
     def reserve_attention_prefill(self, max_tokens: int) -> None:
         check(self._lib.q38_state_reserve_attention_prefill(self.handle, max_tokens))
 
@@ -273,6 +285,34 @@ def gguf_read_f32(path, name: str, count: int) -> np.ndarray:
     check(load().q38_gguf_read_f32(str(path).encode(), name.encode(),
                                    out.ctypes.data_as(ctypes.c_void_p), count))
     return out
+
+
+def nccl_unique_id() -> bytes:
+    """A fresh NCCL unique id (Q38_NCCL_ID_BYTES bytes) for q38_nccl_comm_create,
+    made on one rank and sent to the others by the host."""
+    buf = ctypes.create_string_buffer(Q38_NCCL_ID_BYTES)
+    check(load().q38_nccl_unique_id(buf))
+    return buf.raw
+
+
+class NcclComm:
+    """An NCCL communicator made by the library (q38_nccl_comm_create); every
+    rank of the group must construct it with the same id."""
+
+    def __init__(self, unique_id: bytes, nranks: int, rank: int, device: int):
+        if len(unique_id) != Q38_NCCL_ID_BYTES:
+            raise ValueError("an NCCL unique id has 128 bytes")
+        self._lib = load()
+        h = ctypes.c_void_p()
+        buf = ctypes.create_string_buffer(unique_id, Q38_NCCL_ID_BYTES)
+        check(self._lib.q38_nccl_comm_create(buf, nranks, rank, device, ctypes.byref(h)))
+        self.handle = h
+        self.nranks, self.rank = nranks, rank
+
+    def close(self) -> None:
+        if self.handle:
+            check(self._lib.q38_nccl_comm_destroy(self.handle))
+            self.handle = ctypes.c_void_p()
 
 
 class Weight:
@@ -461,6 +501,18 @@ class Context:
             _dev_ptr(positions, "positions", "int32"), max_position, pos_offset,
             _dev_ptr(partials, "partials"), _stream_ptr(stream)))
 
+    def full_decode_split(self, state: State, layer: int, q_and_gate, key, value, positions,
+                          attention, max_position: int, pos_offset: int, comm, stream=None) -> None:
+        """Split-sequence decode in one call: shard partials, NCCL all-gather
+        over `comm` (an NcclComm or a raw ncclComm_t address), merge."""
+        b = q_and_gate.shape[0]
+        handle = comm.handle if isinstance(comm, NcclComm) else ctypes.c_void_p(comm)
+        check(self._lib.q38_full_decode_split(
+            self.handle, state.handle, layer, b, _dev_ptr(q_and_gate, "q_and_gate"),
+            _dev_ptr(key, "key"), _dev_ptr(value, "value"),
+            _dev_ptr(positions, "positions", "int32"), max_position, pos_offset, handle,
+            _dev_ptr(attention, "attention"), _stream_ptr(stream)))
+
     def merge_shards(self, partials, q_and_gate, attention, stream=None) -> None:
         """Split-sequence decode, merge side: partials [nparts][batch][24][258]."""
         nparts, b = partials.shape[0], partials.shape[1]
@@ -489,6 +541,26 @@ class Context:
                                          base_position, _dev_ptr(q_and_gate, "q_and_gate"),
                                          _dev_ptr(key, "key"), _dev_ptr(value, "value"),
                                          _dev_ptr(attention, "attention"), _stream_ptr(stream)))
+
+    def full_prefill_heads(self, state: State, layer: int, seq0: int, q_and_gate, key, value,
+                           attention, base_position: int, kv_head0: int, kv_head_count: int,
+                           stream=None) -> None:
+        """full_prefill for KV heads [kv_head0, kv_head0 + kv_head_count) only
+        (full-width tensors; only the range's columns are touched)."""
+        nseq, count = q_and_gate.shape[0], q_and_gate.shape[1]
+        check(self._lib.q38_full_prefill_heads(
+            self.handle, state.handle, layer, seq0, nseq, count, base_position, kv_head0,
+            kv_head_count, _dev_ptr(q_and_gate, "q_and_gate"), _dev_ptr(key, "key"),
+            _dev_ptr(value, "value"), _dev_ptr(attention, "attention"), _stream_ptr(stream)))
+
+    def linear_prefill_heads(self, state: State, layer: int, seq0: int, qkv, z, beta, alpha,
+                             attention, v_head0: int, v_head_count: int, stream=None) -> None:
+        """linear_prefill for value heads [v_head0, v_head0 + v_head_count) only."""
+        nseq, count = qkv.shape[0], qkv.shape[1]
+        check(self._lib.q38_linear_prefill_heads(
+            self.handle, state.handle, layer, seq0, nseq, count, v_head0, v_head_count,
+            _dev_ptr(qkv, "qkv"), _dev_ptr(z, "z"), _dev_ptr(beta, "beta"),
+            _dev_ptr(alpha, "alpha"), _dev_ptr(attention, "attention"), _stream_ptr(stream)))
 
     def linear_prefill(self, state: State, layer: int, seq0: int, qkv, z, beta, alpha,
                        attention, stream=None) -> None:

@@ -1,20 +1,28 @@
 """Multi-GPU partitioning of the hot path (one process per GPU).
 
-Two schemes, following where the work shards naturally:
+Work is split only where it shards naturally:
 
-* Sequence sharding (batched decode, prefill): every rank owns whole
-  sequences; no data-path collective. `shard_range` gives a rank's share.
+* Sequence sharding (batched decode): every rank owns whole sequences; no
+  data-path collective. `shard_range` gives a rank's share.
+* Prefill attention: the unit is one (sequence, KV-head group) -- a KV head
+  and its 6 query heads, the reference's per-head tasks grouped by
+  kv_head = head / 6 (src/model/ops.rs:922-938, :877). `prefill_segments`
+  turns a rank's contiguous range of units into q38_full_prefill_heads calls.
+  No collective.
+* DeltaNet prefill: the unit is one value head (ops.rs:717-733); q/k are
+  replicated because value head h reads key head h % 16 (ops.rs:699).
+  `shard_range(48, world, rank)` is a rank's head range for
+  q38_linear_prefill_heads. No collective.
 * Split-sequence decode (one long sequence): the sequence's cached positions
   are split into contiguous ranges, one per rank (`position_ranges`). Each
-  rank computes softmax partials (o, m, l) over its range with
-  q38_full_decode_shard, the partials of all ranks are exchanged with one
-  all-gather over NCCL (24 x 258 floats per rank and sequence), and every rank
-  merges them with q38_attn_merge_shards. This replaces the single position
-  loop of full_core (src/model/ops.rs:884-913) across GPUs.
+  rank computes softmax partials (o, m, l) over its range, the partials of
+  all ranks are exchanged with one NCCL all-gather (24 x 258 floats per rank
+  and sequence) and merged by log-sum-exp -- all inside the library call
+  q38_full_decode_split on an NCCL communicator, so a host needs no
+  framework for it. This replaces the single position loop of full_core
+  (src/model/ops.rs:884-913) across GPUs.
 """
 from __future__ import annotations
-
-from typing import Optional
 
 PARTIAL_FLOATS = 256 + 2  # o[256], m, l
 
@@ -35,34 +43,64 @@ def position_ranges(capacity: int, world: int) -> list[tuple[int, int]]:
     return [shard_range(capacity, world, r) for r in range(world)]
 
 
+def prefill_segments(nseq: int, kv_heads: int, world: int,
+                     rank: int) -> list[tuple[int, int, int, int]]:
+    """A rank's share of the nseq * kv_heads prefill units (sequence-major: unit
+    u is sequence u // kv_heads, KV head u % kv_heads) as calls
+    (seq0, nseq, kv_head0, kv_head_count): whole sequences in one call, a
+    partial sequence at either end of the range in a call of its own."""
+    u0, u1 = shard_range(nseq * kv_heads, world, rank)
+    out: list[tuple[int, int, int, int]] = []
+    u = u0
+    while u < u1:
+        s, h = divmod(u, kv_heads)
+        if h == 0 and u1 - u >= kv_heads:
+            n = (u1 - u) // kv_heads  # whole sequences
+            out.append((s, n, 0, kv_heads))
+            u += n * kv_heads
+        else:
+            n = min(kv_heads - h, u1 - u)
+            out.append((s, 1, h, n))
+            u += n
+    return out
+
+
+def exchange_unique_id(dist, make_id, group=None) -> bytes:
+    """Rank 0's NCCL unique id on every rank of `group`, sent over the host's
+    own process group (any backend)."""
+    obj = [make_id() if dist.get_rank(group) == 0 else None]
+    src = dist.get_global_rank(group, 0) if group is not None else 0
+    dist.broadcast_object_list(obj, src=src, group=group)
+    return obj[0]
+
+
 class SplitSequenceDecoder:
     """Runs one full-attention decode step of sequences whose KV positions are
-    sharded across the ranks of `group` (torch.distributed, NCCL backend).
+    sharded across the ranks of `group` (torch.distributed only exchanges the
+    NCCL id at set-up; the step's all-gather is the library's).
 
     `state` on each rank holds positions [pos_offset, pos_offset + its
     context_length) of every sequence."""
 
-    def __init__(self, ctx, state, layer: int, pos_offset: int, group=None,
-                 batch: Optional[int] = None):
-        import torch
+    def __init__(self, ctx, state, layer: int, pos_offset: int, group=None):
         import torch.distributed as dist
+
+        import q38attn
         self.ctx, self.state, self.layer = ctx, state, layer
         self.pos_offset = pos_offset
-        self.group = group
-        self.dist = dist
-        self.world = dist.get_world_size(group)
-        b = batch or state.batch
-        heads = 24
-        self.local = torch.empty(b, heads, PARTIAL_FLOATS, device="cuda")
-        # Concatenated along dim 0 ([world*b][heads][258]), viewed per rank.
-        self.flat = torch.empty(self.world * b, heads, PARTIAL_FLOATS, device="cuda")
-        self.gathered = self.flat.view(self.world, b, heads, PARTIAL_FLOATS)
+        world = dist.get_world_size(group)
+        rank = dist.get_rank(group)
+        uid = exchange_unique_id(dist, q38attn.nccl_unique_id, group)
+        self.comm = q38attn.NcclComm(uid, world, rank, ctx.device)
+        state.reserve_split(world)
 
     def step(self, q_and_gate, key, value, positions, attention, max_position: int,
              stream=None) -> None:
         """Every rank passes the same q_and_gate/key/value/positions (the
         token's projections); every rank receives the merged attention."""
-        self.ctx.full_decode_shard(self.state, self.layer, q_and_gate, key, value, positions,
-                                   self.local, max_position, self.pos_offset, stream=stream)
-        self.dist.all_gather_into_tensor(self.flat, self.local, group=self.group)
-        self.ctx.merge_shards(self.gathered, q_and_gate, attention, stream=stream)
+        self.ctx.full_decode_split(self.state, self.layer, q_and_gate, key, value, positions,
+                                   attention, max_position, self.pos_offset, self.comm,
+                                   stream=stream)
+
+    def close(self) -> None:
+        self.comm.close()

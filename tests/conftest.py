@@ -50,3 +50,41 @@ def relative_error(a, b):
     a = np.asarray(a, np.float64)
     b = np.asarray(b, np.float64)
     return float(np.max(np.abs(a - b) / np.maximum(np.abs(b), 1.0))) if a.size else 0.0
+
+
+def scaled_error(a, b):
+    """max|a-b| / max|b|: the error relative to the expected tensor's own scale.
+    Unlike the reference's metric it does not turn into an absolute error when
+    the values are below 1 (attention outputs at long context are ~0.01)."""
+    import numpy as np
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    if not a.size:
+        return 0.0
+    diff = float(np.max(np.abs(a - b)))
+    scale = float(np.max(np.abs(b)))
+    return diff / scale if scale > 0 else diff
+
+
+# Every check_parity result of the session: (test, what, reference metric,
+# scaled error, tolerance). Written as JSON to $Q38_PARITY_LOG at the end.
+PARITY_LOG: list = []
+
+
+def check_parity(a, b, tol, what=""):
+    """Asserts that both the reference's metric and the scale-aware error are
+    below `tol`; records and returns them."""
+    r, s = relative_error(a, b), scaled_error(a, b)
+    test = os.environ.get("PYTEST_CURRENT_TEST", "").split(" ")[0]
+    PARITY_LOG.append({"test": test, "what": what, "ref_metric": r, "scaled": s, "tol": tol})
+    print(f"[parity] {test} {what}: ref metric {r:.3e}, scaled {s:.3e} (tol {tol:g})")
+    assert r < tol and s < tol, (what, r, s, tol)
+    return r, s
+
+
+def pytest_sessionfinish(session, exitstatus):
+    path = os.environ.get("Q38_PARITY_LOG")
+    if path and PARITY_LOG:
+        import json
+        Path(path).parent.mkdir(parents=True, exist_ok=True)
+        Path(path).write_text(json.dumps(PARITY_LOG, indent=1))

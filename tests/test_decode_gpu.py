@@ -7,7 +7,7 @@ import numpy as np
 import pytest
 
 import vectors as V
-from conftest import REPO, relative_error
+from conftest import REPO, check_parity, relative_error
 
 pytestmark = pytest.mark.gpu
 
@@ -50,8 +50,8 @@ def test_linear_core_mirror_matches_oracle_config2(cuda_ctx, oracle_lib):
     assert relative_error(gx["qkv"], ox["qkv"]) < 1e-5
     assert relative_error(gx["beta"], ox["beta"]) < 1e-6
     assert relative_error(gx["alpha"], ox["alpha"]) < 1e-6
-    assert relative_error(gd, od) < TOL
-    assert relative_error(gatt, oatt) < TOL
+    check_parity(gd, od, TOL, "")
+    check_parity(gatt, oatt, TOL, "")
     assert st.errors() == 0
     st.close()
 
@@ -69,14 +69,14 @@ def test_linear_golden_vectors_on_gpu(cuda_ctx):
         att = np.zeros((1, 6144), F)
         qkv, beta, alpha = x["qkv"][None].copy(), x["beta"][None].copy(), x["alpha"][None].copy()
         cuda_ctx.linear_decode_host(st, layer, qkv, x["z"][None].copy(), beta, alpha, att)
-        assert relative_error(att[0], GOLDEN[f"lin_attention_{t}"]) < TOL
+        check_parity(att[0], GOLDEN[f"lin_attention_{t}"], TOL, "")
         assert relative_error(beta[0], GOLDEN[f"lin_beta_{t}"]) < 1e-6
         assert relative_error(alpha[0], GOLDEN[f"lin_alpha_{t}"]) < 1e-6
         if t == 0:
             assert relative_error(qkv[0], GOLDEN["lin_qkv_0"]) < 1e-5
     conv, delta = st.download_linear(layer, 0)
-    assert relative_error(delta[0], GOLDEN["lin_delta_head0"]) < TOL
-    assert relative_error(delta[47], GOLDEN["lin_delta_head47"]) < TOL
+    check_parity(delta[0], GOLDEN["lin_delta_head0"], TOL, "")
+    check_parity(delta[47], GOLDEN["lin_delta_head47"], TOL, "")
     np.testing.assert_array_equal(conv[::16], GOLDEN["lin_conv_final"])
     st.close()
 
@@ -105,12 +105,12 @@ def test_linear_decode_batched_multi_token(cuda_ctx, oracle_lib):
             oatt = np.zeros(6144, F)
             oracle_lib.linear_core(w, states[b]["conv_state"], states[b]["delta_state"],
                                    ox["qkv"], ox["z"], ox["beta"], ox["alpha"], oatt)
-            assert relative_error(att[b].cpu().numpy(), oatt) < TOL, (t, b)
+            check_parity(att[b].cpu().numpy(), oatt, TOL, str((t, b)))
             assert relative_error(d["qkv"][b].cpu().numpy(), ox["qkv"]) < 1e-5
     for b in range(B):
         conv, delta = st.download_linear(layer, b)
         np.testing.assert_array_equal(conv, states[b]["conv_state"])
-        assert relative_error(delta, states[b]["delta_state"]) < TOL
+        check_parity(delta, states[b]["delta_state"], TOL, "")
     assert st.errors() == 0
     st.close()
 
@@ -209,7 +209,7 @@ def test_full_core_mirror_matches_oracle_config1(cuda_ctx, oracle_lib):
     kc2, vc2 = kc.copy(), vc.copy()
     cuda_ctx.full_core(st, layer, x["q_and_gate"], key, x["value"], q, gate, None, att, kc2, vc2,
                        ctx_len, pos)
-    assert relative_error(att, oatt) < TOL
+    check_parity(att, oatt, TOL, "")
     assert relative_error(key, okey) < 1e-5
     assert relative_error(q, oq) < 1e-5
     np.testing.assert_array_equal(gate.reshape(24, 256), x["q_and_gate"].reshape(24, 512)[:, 256:])
@@ -238,7 +238,7 @@ def test_full_golden_vectors_on_gpu(cuda_ctx, bf16):
         key = x["key"][None].copy()
         cuda_ctx.full_decode_host(st, layer, x["q_and_gate"][None].copy(), key,
                                   x["value"][None].copy(), np.array([pre + t], np.int32), att)
-        assert relative_error(att[0], GOLDEN[f"{tag}_attention_{t}"]) < TOL, t
+        check_parity(att[0], GOLDEN[f"{tag}_attention_{t}"], TOL, str(t))
         assert relative_error(key[0], GOLDEN[f"{tag}_key_{t}"]) < 1e-5
     k, v = st.download_kv(layer, 0, pre, 3)
     for t in range(3):
@@ -283,7 +283,7 @@ def test_full_decode_batch_mixed_positions(cuda_ctx, oracle_lib, bf16):
         ox = {k: v[b].copy() for k, v in x.items()}
         oatt, okey, _ = _oracle_full(oracle_lib, w, ox, caches[b][0], caches[b][1], ctx_len, pos,
                                      layer, bf16)
-        assert relative_error(att[b].cpu().numpy(), oatt) < TOL, (b, pos)
+        check_parity(att[b].cpu().numpy(), oatt, TOL, str((b, pos)))
         assert relative_error(d["key"][b].cpu().numpy(), okey) < 1e-5
     assert st.errors() == 0
     st.close()
@@ -341,9 +341,9 @@ def test_full_decode_host_equals_device_call(cuda_ctx, pinned_host):
 
 def test_split_count_does_not_change_the_result(cuda_ctx):
     """The LSE merge is invariant to how positions are split across CTAs. The
-    split plan depends on the batch (it aims for two CTAs per SM), so the same
-    sequence decoded alone (64-position splits) and as one of 8 identical
-    sequences (320-position splits) must agree to rounding."""
+    split plan depends on the batch (it fills the SMs in whole waves), so the
+    same sequence decoded alone (64-position splits) and as one of 8 identical
+    sequences (384-position splits) must agree to rounding."""
     import q38attn
     from q38attn import synth
     torch = _torch()
@@ -372,10 +372,9 @@ def test_split_count_does_not_change_the_result(cuda_ctx):
 
 
 def test_full_decode_long_context_large_splits(cuda_ctx, oracle_lib):
-    """One sequence at position 69999 of a 70000-position bf16 cache: the split
-    plan then takes more than 512 positions per split (nine or more 64-key
-    tiles, so the tensor-core scores cycle through their TMEM columns), and
-    the last split ends inside a tile."""
+    """One sequence at position 69999 of a 70000-position bf16 cache: 137
+    splits of 512 positions (eight 64-key tiles, every TMEM score column in
+    use), the last split ending inside a tile."""
     import q38attn
     from q38attn import synth
     torch = _torch()
@@ -398,7 +397,7 @@ def test_full_decode_long_context_large_splits(cuda_ctx, oracle_lib):
     torch.cuda.synchronize()
     ox = {kk: vv[0].copy() for kk, vv in x.items()}
     oatt, okey, _ = _oracle_full(oracle_lib, w, ox, kc, vc, ctx_len, pos, layer, True)
-    assert relative_error(att[0].cpu().numpy(), oatt) < TOL
+    check_parity(att[0].cpu().numpy(), oatt, TOL, "")
     assert relative_error(d["key"][0].cpu().numpy(), okey) < 1e-5
     assert st.errors() == 0
     st.close()
@@ -440,4 +439,131 @@ def test_full_core_position_errors(cuda_ctx):
     assert torch.all(out[1] == 7.0)
     assert torch.isfinite(out[0]).all() and not torch.all(out[0] == 7.0)
     assert st.errors() == 0  # cleared by the read
+    st.close()
+
+
+# ---------------------------------------------------------------------------
+# The bench's shapes
+# ---------------------------------------------------------------------------
+def _kv_host_rows(view, b, n):
+    """Rows 0..n-1 of sequence b of a device KV view [batch][4][ctx][256] in
+    the reference's host layout [n][1024] (f32)."""
+    return np.ascontiguousarray(view[b, :, :n].permute(1, 0, 2).reshape(n, 1024).float().cpu()
+                                .numpy())
+
+
+def test_full_decode_headline_shape(cuda_ctx, oracle_lib):
+    """The headline workload's attention layer: 32 sequences at 32778 cached
+    bf16 positions (the bench's first timed step: 32768 + 10 warm-up steps),
+    one new token each, with the split plan the planner picks for that batch
+    (512-position splits, 65 per kv head). Four sampled sequences against the
+    oracle (bf16 cache rows, new row rounded as the cache stores it)."""
+    torch = _torch()
+    import q38attn
+    from q38attn import synth
+    g = synth.rng(40)
+    w = synth.full_weights(g)
+    layer, B, pos = 3, 32, 32768 + 10
+    cap = pos + 8
+    cuda_ctx.bind_full_layer(layer, w["q_norm"], w["k_norm"])
+    st = cuda_ctx.state(B, cap, full_slots=1, linear_slots=0, kv_dtype=q38attn.Q38_KV_BF16)
+    kview, vview = st.kv_views(layer)
+    tg = torch.Generator(device="cuda")
+    tg.manual_seed(40)
+    kview[:, :, :pos].normal_(generator=tg)
+    vview[:, :, :pos].normal_(generator=tg)
+    sample = [0, 9, 22, 31]
+    caches = {b: (_kv_host_rows(kview, b, cap), _kv_host_rows(vview, b, cap)) for b in sample}
+    x = synth.full_step(g, B)
+    d = {k: torch.from_numpy(v.copy()).cuda() for k, v in x.items()}
+    att = torch.zeros(B, 6144, device="cuda")
+    positions = torch.full((B,), pos, dtype=torch.int32, device="cuda")
+    cuda_ctx.full_decode(st, layer, d["q_and_gate"], d["key"], d["value"], positions, att,
+                         max_position=pos)
+    torch.cuda.synchronize()
+    assert st.errors() == 0
+    for b in sample:
+        kc, vc = caches[b]
+        okey = x["key"][b].copy()
+        q = np.zeros(6144, F)
+        gate = np.zeros(6144, F)
+        scores = np.zeros(24 * cap, F)
+        oatt = np.zeros(6144, F)
+        assert oracle_lib.full_core(w, x["q_and_gate"][b], okey, x["value"][b], q, gate, scores,
+                                    oatt, kc, vc, cap, pos, layer, 1) == 0
+        check_parity(att[b].cpu().numpy(), oatt, TOL, f"seq {b}")
+        assert relative_error(d["key"][b].cpu().numpy(), okey) < 1e-5
+    del kview, vview
+    st.close()
+
+
+def test_full_decode_split_sequence_length_one_gpu(cuda_ctx, oracle_lib):
+    """Config 3's split-sequence length on one GPU: one sequence at 131072
+    cached bf16 positions (the planner's many-split plan for a batch of one)."""
+    torch = _torch()
+    import q38attn
+    from q38attn import synth
+    g = synth.rng(41)
+    w = synth.full_weights(g)
+    layer, pos = 3, 131072
+    cap = pos + 4
+    cuda_ctx.bind_full_layer(layer, w["q_norm"], w["k_norm"])
+    st = cuda_ctx.state(1, cap, full_slots=1, linear_slots=0, kv_dtype=q38attn.Q38_KV_BF16)
+    kview, vview = st.kv_views(layer)
+    tg = torch.Generator(device="cuda")
+    tg.manual_seed(41)
+    kview[:, :, :pos].normal_(generator=tg)
+    vview[:, :, :pos].normal_(generator=tg)
+    kc, vc = _kv_host_rows(kview, 0, cap), _kv_host_rows(vview, 0, cap)
+    x = synth.full_step(g, 1)
+    d = {k: torch.from_numpy(v.copy()).cuda() for k, v in x.items()}
+    att = torch.zeros(1, 6144, device="cuda")
+    cuda_ctx.full_decode(st, layer, d["q_and_gate"], d["key"], d["value"],
+                         torch.tensor([pos], dtype=torch.int32, device="cuda"), att,
+                         max_position=pos)
+    torch.cuda.synchronize()
+    assert st.errors() == 0
+    okey = x["key"][0].copy()
+    q = np.zeros(6144, F)
+    gate = np.zeros(6144, F)
+    scores = np.zeros(24 * cap, F)
+    oatt = np.zeros(6144, F)
+    assert oracle_lib.full_core(w, x["q_and_gate"][0], okey, x["value"][0], q, gate, scores, oatt,
+                                kc, vc, cap, pos, layer, 1) == 0
+    check_parity(att[0].cpu().numpy(), oatt, TOL, "131072 positions")
+    del kview, vview
+    st.close()
+
+
+def test_linear_decode_headline_batch(cuda_ctx, oracle_lib):
+    """The headline workload's DeltaNet layer: 32 sequences, two tokens, every
+    sequence's output and final state against the oracle."""
+    torch = _torch()
+    from q38attn import synth
+    g = synth.rng(42)
+    w = synth.linear_weights(g)
+    layer, B = 0, 32
+    cuda_ctx.bind_linear_layer(layer, w["conv1d"], w["dt_bias"], w["ssm_a"], w["ssm_norm"])
+    st = cuda_ctx.state(B, 16, full_slots=0, linear_slots=1)
+    states = [synth.linear_state(g) for _ in range(B)]
+    for b in range(B):
+        st.upload_linear(layer, b, states[b]["conv_state"], states[b]["delta_state"])
+    for t in range(2):
+        x = synth.linear_step(g, B)
+        d = {k: torch.from_numpy(v.copy()).cuda() for k, v in x.items()}
+        att = torch.zeros(B, 6144, device="cuda")
+        cuda_ctx.linear_decode(st, layer, d["qkv"], d["z"], d["beta"], d["alpha"], att)
+        torch.cuda.synchronize()
+        got = att.cpu().numpy()
+        want = np.zeros((B, 6144), F)
+        for b in range(B):
+            ox = {k: v[b].copy() for k, v in x.items()}
+            oracle_lib.linear_core(w, states[b]["conv_state"], states[b]["delta_state"],
+                                   ox["qkv"], ox["z"], ox["beta"], ox["alpha"], want[b])
+        check_parity(got, want, TOL, f"token {t}, 32 sequences")
+    for b in range(B):
+        conv, delta = st.download_linear(layer, b)
+        np.testing.assert_array_equal(conv, states[b]["conv_state"])
+        check_parity(delta, states[b]["delta_state"], TOL, f"state seq {b}")
+    assert st.errors() == 0
     st.close()

@@ -12,7 +12,7 @@ from __future__ import annotations
 import numpy as np
 import pytest
 
-from conftest import relative_error
+from conftest import check_parity, relative_error
 from gguf_writer import STRING, U32, layer_tensors, write_gguf
 
 pytestmark = pytest.mark.gpu
@@ -103,7 +103,7 @@ def test_mtp_layer_matches_oracle(cuda_ctx, oracle_lib, tmp_path):
     st = cuda_ctx.state(1, ctx_len, full_slots=17, linear_slots=0)
     gkc, gvc = kc.copy(), vc.copy()
     att, key = _full_core(cuda_ctx, st, 64, x, gkc, gvc, ctx_len, pos)
-    assert relative_error(att, oatt) < TOL
+    check_parity(att, oatt, TOL, "")
     assert relative_error(key, okey) < 1e-5
     row = 16 * ctx_len + pos
     assert relative_error(gkc[row], okc[row]) < 1e-5

@@ -24,6 +24,24 @@ def test_shard_ranges_cover_exactly():
         shard_range(10, 2, 2)
 
 
+def test_prefill_segments_cover_units_once():
+    """Each rank's calls cover its contiguous range of (sequence, KV head)
+    units exactly once; 16 units (config 4) over 1/2/4/8 GPUs give whole
+    sequences or whole-sequence halves and quarters."""
+    from q38attn.parallel import prefill_segments
+    for nseq, kvh in ((4, 4), (3, 4), (1, 4), (5, 2)):
+        for world in (1, 2, 3, 4, 5, 8):
+            seen = []
+            for rank in range(world):
+                for s0, n, h0, nh in prefill_segments(nseq, kvh, world, rank):
+                    assert n >= 1 and nh >= 1 and 0 <= h0 and h0 + nh <= kvh
+                    assert n == 1 or (h0, nh) == (0, kvh)
+                    seen += [(s, h) for s in range(s0, s0 + n) for h in range(h0, h0 + nh)]
+            assert sorted(seen) == [(s, h) for s in range(nseq) for h in range(kvh)]
+    assert prefill_segments(4, 4, 8, 3) == [(1, 1, 2, 2)]
+    assert prefill_segments(4, 4, 2, 1) == [(2, 2, 0, 4)]
+
+
 def _partial(q, K, V):
     """(o, m, l) of one head over rows K/V: the shard's softmax partial."""
     if K.shape[0] == 0:
@@ -81,6 +99,41 @@ def _free_port():
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
         return s.getsockname()[1]
+
+
+def _id_worker(rank, world, port, result):
+    import torch.distributed as dist
+
+    from q38attn.parallel import exchange_unique_id
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        made = []
+
+        def make():
+            made.append(rank)
+            return bytes(range(128))
+        result[rank] = (exchange_unique_id(dist, make), made)
+    finally:
+        dist.destroy_process_group()
+
+
+def test_nccl_id_exchange_gloo():
+    """The split-sequence decoder's set-up: rank 0 alone makes the NCCL id and
+    every rank receives the same 128 bytes over the host's process group."""
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    manager = ctx.Manager()
+    result = manager.dict()
+    port = _free_port()
+    procs = [ctx.Process(target=_id_worker, args=(r, 2, port, result)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(120)
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    assert result[0][0] == result[1][0] == bytes(range(128))
+    assert result[0][1] == [0] and result[1][1] == []
 
 
 @pytest.mark.parametrize("world", [2])

@@ -2,7 +2,10 @@
 into contiguous shards, each shard's softmax partial computed by
 q38_full_decode_shard, and the shards merged with q38_attn_merge_shards. On one
 GPU the shards are separate states; with two or more GPUs the real NCCL path
-(q38attn.parallel.SplitSequenceDecoder) runs under torch.distributed."""
+runs: q38_full_decode_split (shard kernels, ncclAllGather inside the library on
+a communicator from q38_nccl_comm_create, merge), driven by
+q38attn.parallel.SplitSequenceDecoder with torch.distributed only exchanging
+the NCCL id."""
 from __future__ import annotations
 
 import os
@@ -12,7 +15,7 @@ import sys
 import numpy as np
 import pytest
 
-from conftest import REPO, relative_error
+from conftest import REPO, check_parity, relative_error
 
 pytestmark = pytest.mark.gpu
 F = np.float32
@@ -71,7 +74,7 @@ def test_shards_on_one_gpu_match_unsharded(cuda_ctx, oracle_lib, nshards, bf16):
         okey = x["key"][0].copy()
         assert oracle_lib.full_core(w, x["q_and_gate"][0], okey, x["value"][0], q, gt, sc, oo,
                                     kc, vc, cap, pos, layer, int(bf16)) == 0
-        assert relative_error(merged[0].cpu().numpy(), oo) < 1e-4, step
+        check_parity(merged[0].cpu().numpy(), oo, 1e-4, str(step))
     for st in shards:
         assert st.errors() == 0
         st.close()
@@ -115,8 +118,8 @@ assert st.errors() == 0
 errs = [None] * world
 dist.all_gather_object(errs, err)
 if rank == 0:
-    print(json.dumps({"world": world, "max_err": max(errs)}))
-st.close(); full.close()
+    print(json.dumps({"world": world, "max_err": max(errs), "path": "q38_full_decode_split (NCCL in the library)"}))
+dec.close(); st.close(); full.close()
 dist.barrier(); dist.destroy_process_group()
 '''
 

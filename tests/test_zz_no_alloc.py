@@ -11,10 +11,11 @@ passes every input and output, its KV cache included.
 This test calls that entry point through the C ABI and checks it against the
 regular entry point (q38_full_decode with a q38_state) on the same inputs, for
 two calls in a row (each appends one position per sequence), within the 1e-4
-tolerance of the other decode tests; and checks that a size beyond the
-scratch's maximum is refused with an argument error. The test's own buffers
-come from torch; the entry point under test allocates nothing. The file name
-makes pytest collect it last.
+tolerance of the other decode tests; checks that later calls leave the
+device's free memory unchanged; and checks that a size beyond the scratch's
+maximum, or a misaligned pointer, is refused with an argument error before any
+device work. The test's own buffers come from torch; the entry point under
+test allocates nothing. The file name makes pytest collect it last.
 """
 from __future__ import annotations
 
@@ -92,6 +93,69 @@ def test_noalloc_decode_matches_regular_entry_point(bf16):
     del kview, vview
     st.close()
     ctx.close()
+
+
+def test_noalloc_decode_allocates_nothing_on_later_calls():
+    """Once the first call has loaded the library's device code (and with it
+    the fixed scratch array), further calls leave the device's free memory
+    unchanged: the entry point itself allocates nothing."""
+    import torch
+
+    import q38attn
+    from q38attn import synth
+    lib = q38attn.load()
+    torch.cuda.set_device(0)
+    g = synth.rng(23)
+    w = synth.full_weights(g)
+    B, ctx_len = 2, 256
+    kc = torch.randn(B, 4, ctx_len, 256, device="cuda").to(torch.bfloat16)
+    vc = torch.randn(B, 4, ctx_len, 256, device="cuda").to(torch.bfloat16)
+    qn = torch.from_numpy(w["q_norm"]).cuda()
+    kn = torch.from_numpy(w["k_norm"]).cuda()
+    x = {k: torch.from_numpy(v.copy()).cuda() for k, v in synth.full_step(g, B).items()}
+    pos = torch.tensor([100, 200], dtype=torch.int32, device="cuda")
+    out = torch.zeros(B, 6144, device="cuda")
+    args = (_p(qn), _p(kn), _p(kc), _p(vc), B, ctx_len, q38attn.Q38_KV_BF16, _p(x["q_and_gate"]),
+            _p(x["key"]), _p(x["value"]), _p(pos), -1, _p(out), None, None)
+    assert lib.q38_full_decode_noalloc(*args) == q38attn.Q38_OK, q38attn.last_error()
+    torch.cuda.synchronize()
+    free0, _ = torch.cuda.mem_get_info()
+    for _ in range(3):
+        assert lib.q38_full_decode_noalloc(*args) == q38attn.Q38_OK, q38attn.last_error()
+    torch.cuda.synchronize()
+    free1, _ = torch.cuda.mem_get_info()
+    assert free1 == free0
+    assert torch.isfinite(out).all()
+
+
+def test_noalloc_decode_rejects_misaligned_pointers():
+    """The KV cache is streamed by the bulk-copy engine or by TMA, which need
+    16-byte aligned rows: a cache pointer off by 4 bytes (and any tensor off by
+    2) is refused on the host before any device work."""
+    import torch
+
+    import q38attn
+    lib = q38attn.load()
+    torch.cuda.set_device(0)
+    buf = torch.zeros(1 << 20, device="cuda")
+    pos = torch.zeros(1, dtype=torch.int32, device="cuda")
+    base = buf.data_ptr()
+    ok = ctypes.c_void_p(base)
+    off4 = ctypes.c_void_p(base + 4)
+    off2 = ctypes.c_void_p(base + 2)
+    for kv_dtype in (q38attn.Q38_KV_F32, q38attn.Q38_KV_BF16):
+        rc = lib.q38_full_decode_noalloc(ok, ok, off4, ok, 1, 64, kv_dtype, ok, ok, ok, _p(pos),
+                                         -1, ok, None, None)
+        assert rc == q38attn.Q38_ERR_ARG
+        assert "16-byte" in q38attn.last_error()
+        rc = lib.q38_full_decode_noalloc(ok, ok, ok, off4, 1, 64, kv_dtype, ok, ok, ok, _p(pos),
+                                         -1, ok, None, None)
+        assert rc == q38attn.Q38_ERR_ARG
+        rc = lib.q38_full_decode_noalloc(ok, ok, ok, ok, 1, 64, kv_dtype, off2, ok, ok, _p(pos),
+                                         -1, ok, None, None)
+        assert rc == q38attn.Q38_ERR_ARG
+        assert "4-byte" in q38attn.last_error()
+    torch.cuda.synchronize()
 
 
 def test_noalloc_decode_rejects_sizes_beyond_its_scratch():
