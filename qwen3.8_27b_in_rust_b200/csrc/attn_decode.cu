@@ -745,39 +745,111 @@ struct MergeParams {
     float *attention;
     float *partial_out;  // non-null: write (o, m, l) [batch][heads][258] instead
     int context_length, heads, chunk, max_splits, max_position, pos_offset, sharded;
+    int merge_ctas;      // CTAs (one cluster) per (head, sequence)
 };
 
+__device__ __forceinline__ float ld_cluster_f32(uint32_t addr) {
+    float v;
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+    return v;
+}
+
+// A cluster of merge_ctas CTAs (256 threads each) per (head, sequence); CTA g
+// of the cluster merges splits [g * per, (g + 1) * per). Inside a CTA all 8
+// warps read at once: warp w takes splits w, w + 8, ..., lane l dims
+// [8l, 8l + 8) of each (two 16-byte loads), and the 8 per-warp sums are added
+// in shared memory in warp order. The cluster's partials (o, m, l) are then
+// combined by CTA 0 through distributed shared memory (log-sum-exp), so a
+// single long sequence's hundreds of splits are read by many SMs at once.
 __global__ void __launch_bounds__(kAttnHeadDim) attn_decode_merge_kernel(MergeParams p) {
-    const int h = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
+    __shared__ float red[kWarps][kAttnHeadDim];
+    __shared__ float lred[kWarps], mred[kWarps];
+    __shared__ float cta_o[kAttnHeadDim], cta_ml[2];
+    const int h = blockIdx.x, b = blockIdx.y, tid = threadIdx.x;
+    const int warp = tid >> 5, lane = tid & 31;
+    const int G = p.merge_ctas;
+    const uint32_t g = G > 1 ? sm100::cluster_ctarank() : 0u;
     const int pos = p.positions[b];
     pdl_wait_primary();
+    // Uniform over the cluster (one sequence), so every CTA of it returns here or none.
     if (!position_ok(pos, p.pos_offset, p.context_length, p.max_position, p.sharded)) return;
     const int n = local_rows(pos, p.pos_offset, p.context_length);
     const int nsplit = n > 0 ? (n + p.chunk - 1) / p.chunk : 0;
+    const int per = (nsplit + G - 1) / G;
+    const int s0 = min(nsplit, int(g) * per), s1 = min(nsplit, s0 + per);
     const size_t base = (size_t(b) * p.heads + h) * p.max_splits;
     const float2 *ml = reinterpret_cast<const float2 *>(p.part_ml) + base;
     float m = -INFINITY;
-    for (int s = 0; s < nsplit; ++s) m = fmaxf(m, ml[s].x);
-    float l = 0.f, o = 0.f;
-    for (int s = 0; s < nsplit; ++s) {
+    for (int s = s0 + tid; s < s1; s += kAttnHeadDim) m = fmaxf(m, ml[s].x);
+    m = warp_max(m);
+    if (lane == 0) mred[warp] = m;
+    __syncthreads();
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) m = fmaxf(m, mred[w]);
+    float l = 0.f;
+    float o[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll 4
+    for (int s = s0 + warp; s < s1; s += kWarps) {
         const float2 v = ml[s];
+        const float4 *src = reinterpret_cast<const float4 *>(p.part_o + (base + s) * kAttnHeadDim) + 2 * lane;
+        const float4 a = src[0], c = src[1];
         const float w = expf(v.x - m);
         l += w * v.y;
-        o += w * p.part_o[(base + s) * kAttnHeadDim + d];
+        o[0] += w * a.x; o[1] += w * a.y; o[2] += w * a.z; o[3] += w * a.w;
+        o[4] += w * c.x; o[5] += w * c.y; o[6] += w * c.z; o[7] += w * c.w;
     }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) red[warp][8 * lane + i] = o[i];
+    if (lane == 0) lred[warp] = l;
+    __syncthreads();
+    float ot = 0.f, lt = 0.f;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) {
+        ot += red[w][tid];
+        lt += lred[w];
+    }
+    if (G > 1) {
+        // This CTA's (o, m, l) (m = -inf, l = o = 0 for a CTA without splits)
+        // to CTA 0 of the cluster.
+        cta_o[tid] = s1 > s0 ? ot : 0.f;
+        if (tid == 0) {
+            cta_ml[0] = m;
+            cta_ml[1] = lt;
+        }
+        sm100::cluster_sync();
+        if (g == 0) {
+            float mm = -INFINITY;
+            for (int r = 0; r < G; ++r)
+                mm = fmaxf(mm, ld_cluster_f32(sm100::cluster_addr(&cta_ml[0], uint32_t(r))));
+            float lsum = 0.f, osum = 0.f;
+            for (int r = 0; r < G; ++r) {
+                const float mr = ld_cluster_f32(sm100::cluster_addr(&cta_ml[0], uint32_t(r)));
+                if (mr == -INFINITY) continue;
+                const float w = expf(mr - mm);
+                lsum += w * ld_cluster_f32(sm100::cluster_addr(&cta_ml[1], uint32_t(r)));
+                osum += w * ld_cluster_f32(sm100::cluster_addr(&cta_o[tid], uint32_t(r)));
+            }
+            m = mm;
+            lt = lsum;
+            ot = osum;
+        }
+        sm100::cluster_sync();  // every CTA's shared memory stays until CTA 0 has read it
+        if (g != 0) return;
+    }
+    const int d = tid;
     if (p.partial_out) {
         // This shard's (o, m, l) relative to its own max m (m = -inf, l = 0,
         // o = 0 when the shard holds no visible row).
         float *dst = p.partial_out + (size_t(b) * p.heads + h) * (kAttnHeadDim + 2);
-        dst[d] = nsplit > 0 ? o : 0.f;
+        dst[d] = nsplit > 0 ? ot : 0.f;
         if (d == 0) {
             dst[kAttnHeadDim] = m;
-            dst[kAttnHeadDim + 1] = l;
+            dst[kAttnHeadDim + 1] = lt;
         }
         return;
     }
     const float gate = p.q_and_gate[(size_t(b) * p.heads + h) * 2 * kAttnHeadDim + kAttnHeadDim + d];
-    p.attention[(size_t(b) * p.heads + h) * kAttnHeadDim + d] = (o / l) * sigmoidf_ref(gate);
+    p.attention[(size_t(b) * p.heads + h) * kAttnHeadDim + d] = (ot / lt) * sigmoidf_ref(gate);
 }
 
 // Cross-shard merge: nparts packed (o, m, l) partials per (sequence, head),
@@ -882,12 +954,26 @@ cudaError_t launch_typed(const AttnDecodeLaunch &a, int sm_count, cudaStream_t s
     e = cudaLaunchKernelEx(&cfg, attn_decode_split_kernel<KV>, map_k, map_v, sp);
     if (e != cudaSuccess) return e;
 
+    // Merge CTAs per (head, sequence): one while the (head, sequence) grid
+    // alone fills the SMs twice over; otherwise a cluster of up to 8 (a
+    // portable size), about 32 splits each, so that a small batch's many
+    // splits are read by many SMs.
+    const int fill = std::max(1, (2 * sm_count) / std::max(1, a.heads * a.batch));
+    const int merge_ctas = std::min({8, fill, std::max(1, (plan.nsplit + 31) / 32)});
     MergeParams mp{a.part_o,   a.part_ml,  a.q_and_gate, a.positions,  a.attention,
                    a.partial_out, a.context_length, a.heads, plan.chunk, a.max_splits,
-                   a.max_position, a.pos_offset, a.partial_out != nullptr};
-    cfg.gridDim = dim3(a.heads, a.batch);
+                   a.max_position, a.pos_offset, a.partial_out != nullptr, merge_ctas};
+    cudaLaunchAttribute mattr[2];
+    mattr[0] = attr[0];
+    mattr[1].id = cudaLaunchAttributeClusterDimension;
+    mattr[1].val.clusterDim.x = 1;
+    mattr[1].val.clusterDim.y = 1;
+    mattr[1].val.clusterDim.z = unsigned(merge_ctas);
+    cfg.gridDim = dim3(a.heads, a.batch, merge_ctas);
     cfg.blockDim = dim3(kAttnHeadDim);
     cfg.dynamicSmemBytes = 0;
+    cfg.attrs = mattr;
+    cfg.numAttrs = 2;
     return cudaLaunchKernelEx(&cfg, attn_decode_merge_kernel, mp);
 }
 

@@ -31,11 +31,13 @@
 //                                    then the epilogue O / l * sigmoid(gate).
 //                         TMEM per CTA: S0..S3 (64 columns each) | O (256).
 //
-// Precision: S = Q K^T from bf16 Q and K (the bf16 cache); O = P V in f16
-// (P rounded to f16 has 4x less error than bf16, which matters for the first
-// rows of a prompt that see only a few keys; bf16 V values are exact in f16
-// for 2^-14 <= |v| <= 65504; a V value beyond 65504 sets kDevErrRange, as
-// its f16 copy would overflow); f32 accumulation throughout. Tolerance 2e-3.
+// Precision: S = Q K^T from bf16 Q and K (the bf16 cache) or from f16 Q and K
+// (an f32 cache: the f32 rows stay in the cache and f16 copies, 8x finer than
+// bf16, feed the tensor cores); O = P V in f16 (P rounded to f16 has 4x less
+// error than bf16, which matters for the first rows of a prompt that see only
+// a few keys; bf16 V values are exact in f16 for 2^-14 <= |v| <= 65504). A
+// value beyond the f16 range (|x| > 65504) in an f16 operand sets
+// kDevErrRange. f32 accumulation throughout. Tolerance 2e-3.
 #include "q38_sm100.cuh"
 
 #include <cudaTypedefs.h>
@@ -66,7 +68,7 @@ struct PrefillPrepParams {
     const float *value;
     void *kcache, *vcache;    // slot base: [batch][kv_heads][ctx][256], bf16 or f32 (kv_f32)
     __half *v16;              // [nseq][kv_heads][ctx][256]: V as f16 for P V
-    __nv_bfloat16 *k16;       // kv_f32 only: [nseq][kv_heads][ctx][256], K as bf16 for Q K^T
+    __half *k16;              // kv_f32 only: [nseq][kv_heads][ctx][256], K as f16 for Q K^T
     float *rope;              // RoPE table, blocks of [64][128] (see kRopeBlockFloats)
     const float *k_norm;
     int *err;
@@ -156,17 +158,23 @@ __global__ void __launch_bounds__(kPrepWarps * 32) attn_prefill_prep_kernel(Pref
     kk.w = pack_bf16x2_rn(x[6], x[7]);
     if (p.kv_f32) {
         // The reference's f32 rows go to the cache; the tensor-core operands
-        // are K as bf16 and V as f16 (rounded once from f32) in the scratch.
+        // are K and V as f16 (each rounded once from f32, 8x finer than bf16)
+        // in the scratch, and the attention kernel rounds Q to f16 as well.
         float4 *kc = reinterpret_cast<float4 *>(static_cast<float *>(p.kcache) + row);
         float4 *vc = reinterpret_cast<float4 *>(static_cast<float *>(p.vcache) + row);
         kc[0] = make_float4(x[0], x[1], x[2], x[3]);
         kc[1] = make_float4(x[4], x[5], x[6], x[7]);
         vc[0] = va;
         vc[1] = vb;
-        *reinterpret_cast<uint4 *>(p.k16 + srow) = kk;
+        float kmax = 0.f;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) kmax = fmaxf(kmax, fabsf(x[j]));
+        *reinterpret_cast<uint4 *>(p.k16 + srow) =
+            make_uint4(pack_f16x2(x[0], x[1]), pack_f16x2(x[2], x[3]), pack_f16x2(x[4], x[5]),
+                       pack_f16x2(x[6], x[7]));
         const float vmax = fmaxf(fmaxf(fmaxf(fabsf(va.x), fabsf(va.y)), fmaxf(fabsf(va.z), fabsf(va.w))),
                                  fmaxf(fmaxf(fabsf(vb.x), fabsf(vb.y)), fmaxf(fabsf(vb.z), fabsf(vb.w))));
-        if (vmax > 65504.f) set_error(p.err, kDevErrRange);
+        if (fmaxf(vmax, kmax) > 65504.f) set_error(p.err, kDevErrRange);
         vh.x = pack_f16x2(va.x, va.y);
         vh.y = pack_f16x2(va.z, va.w);
         vh.z = pack_f16x2(vb.x, vb.y);
@@ -196,14 +204,14 @@ __global__ void __launch_bounds__(kPrepWarps * 32) attn_prefill_prep_kernel(Pref
 struct PrefixParams {
     const void *kcache, *vcache;  // slot base [batch][kv_heads][ctx][256], bf16 or f32 (kv_f32)
     __half *v16;                  // [nseq][kv_heads][ctx][256]
-    __nv_bfloat16 *k16;           // kv_f32 only: [nseq][kv_heads][ctx][256]
+    __half *k16;                  // kv_f32 only: [nseq][kv_heads][ctx][256]
     int *err;
     int seq0, base, context_length, kv_heads, kv_head0, kv_f32;
 };
 
 // One thread per 8 values of the rows [0, base) of each (sequence, kv head of
 // the call's range): V as f16 into the V scratch; for an f32 cache also K as
-// bf16 into the K scratch.
+// f16 into the K scratch.
 __global__ void __launch_bounds__(256) attn_prefill_prefix_kernel(PrefixParams p) {
     const int i = blockIdx.x * 256 + threadIdx.x;
     if (i >= p.base * (kAttnHeadDim / 8)) return;
@@ -218,11 +226,13 @@ __global__ void __launch_bounds__(256) attn_prefill_prefix_kernel(PrefixParams p
         const float4 *vr = reinterpret_cast<const float4 *>(static_cast<const float *>(p.vcache) + src);
         const float4 ka = kr[0], kb = kr[1], va = vr[0], vb = vr[1];
         *reinterpret_cast<uint4 *>(p.k16 + dst) =
-            make_uint4(pack_bf16x2_rn(ka.x, ka.y), pack_bf16x2_rn(ka.z, ka.w),
-                       pack_bf16x2_rn(kb.x, kb.y), pack_bf16x2_rn(kb.z, kb.w));
+            make_uint4(pack_f16x2(ka.x, ka.y), pack_f16x2(ka.z, ka.w), pack_f16x2(kb.x, kb.y),
+                       pack_f16x2(kb.z, kb.w));
         const float vmax = fmaxf(fmaxf(fmaxf(fabsf(va.x), fabsf(va.y)), fmaxf(fabsf(va.z), fabsf(va.w))),
                                  fmaxf(fmaxf(fabsf(vb.x), fabsf(vb.y)), fmaxf(fabsf(vb.z), fabsf(vb.w))));
-        if (vmax > 65504.f) set_error(p.err, kDevErrRange);
+        const float kmax = fmaxf(fmaxf(fmaxf(fabsf(ka.x), fabsf(ka.y)), fmaxf(fabsf(ka.z), fabsf(ka.w))),
+                                 fmaxf(fmaxf(fabsf(kb.x), fabsf(kb.y)), fmaxf(fabsf(kb.z), fabsf(kb.w))));
+        if (fmaxf(vmax, kmax) > 65504.f) set_error(p.err, kDevErrRange);
         w = make_uint4(pack_f16x2(va.x, va.y), pack_f16x2(va.z, va.w), pack_f16x2(vb.x, vb.y),
                        pack_f16x2(vb.z, vb.w));
     } else {
@@ -247,6 +257,7 @@ struct PrefillParams {
     int *err;
     int kseq0;            // sequence index of the call's first sequence in the K map's planes
     int count, base, head0, kv_heads, n_qtiles;
+    int op_f16;           // Q and K operands in f16 (f32 cache) instead of bf16
     float eps;
 };
 
@@ -487,14 +498,31 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsPF, 1)
                     }
                 }
                 unsigned char *dst = sQ + qb * (kQBytes / 4) + r * 128;
+                if (p.op_f16) {
+                    // f16 operands (f32 cache): the same type as the f16 K copy.
+                    float qmax = 0.f;
 #pragma unroll
-                for (int ch = 0; ch < 8; ++ch) {
-                    uint4 o;
-                    o.x = pack_bf16x2_rn(x[8 * ch + 0], x[8 * ch + 1]);
-                    o.y = pack_bf16x2_rn(x[8 * ch + 2], x[8 * ch + 3]);
-                    o.z = pack_bf16x2_rn(x[8 * ch + 4], x[8 * ch + 5]);
-                    o.w = pack_bf16x2_rn(x[8 * ch + 6], x[8 * ch + 7]);
-                    *reinterpret_cast<uint4 *>(dst + ((ch ^ (r & 7)) << 4)) = o;
+                    for (int ch = 0; ch < 8; ++ch) {
+                        uint4 o;
+                        o.x = pack_f16x2(x[8 * ch + 0], x[8 * ch + 1]);
+                        o.y = pack_f16x2(x[8 * ch + 2], x[8 * ch + 3]);
+                        o.z = pack_f16x2(x[8 * ch + 4], x[8 * ch + 5]);
+                        o.w = pack_f16x2(x[8 * ch + 6], x[8 * ch + 7]);
+                        *reinterpret_cast<uint4 *>(dst + ((ch ^ (r & 7)) << 4)) = o;
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) qmax = fmaxf(qmax, fabsf(x[8 * ch + e]));
+                    }
+                    if (qmax > 65504.f) set_error(p.err, kDevErrRange);
+                } else {
+#pragma unroll
+                    for (int ch = 0; ch < 8; ++ch) {
+                        uint4 o;
+                        o.x = pack_bf16x2_rn(x[8 * ch + 0], x[8 * ch + 1]);
+                        o.y = pack_bf16x2_rn(x[8 * ch + 2], x[8 * ch + 3]);
+                        o.z = pack_bf16x2_rn(x[8 * ch + 4], x[8 * ch + 5]);
+                        o.w = pack_bf16x2_rn(x[8 * ch + 6], x[8 * ch + 7]);
+                        *reinterpret_cast<uint4 *>(dst + ((ch ^ (r & 7)) << 4)) = o;
+                    }
                 }
             }
             fence_proxy_async_smem();  // the QK MMA reads sQ through the async proxy
@@ -574,7 +602,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsPF, 1)
         // A thread issuing tcgen05.mma waits ~100 cycles per instruction, so
         // even and odd tiles are issued from two warps.
         if (leader && lane == 0) {
-            const uint32_t id_qk = idesc_bf16_f32(kPairRows, kBlockK, 0, 0);
+            // Q and K: both bf16 (bf16 cache) or both f16 (f32 cache).
+            const uint32_t id_qk = idesc_f16_f32(kPairRows, kBlockK, 0, 0, p.op_f16 == 0);
             const uint32_t sq = smem_addr(sQ), sk = smem_addr(sK);
             bool ok = mbar_wait_cluster(&bar.q_pair, 0);  // Q of both CTAs in shared memory
             for (int j = warp == 1 ? 0 : 1; ok && j < nkt; j += 2) {
@@ -876,9 +905,10 @@ cudaError_t launch_attn_prefill(const AttnPrefillLaunch &a, cudaStream_t stream)
                            uint64_t(a.nseq)) ||
         !make_map_rows_f32(&mo, a.attention, kAttnHeadDim, uint64_t(a.heads), uint64_t(a.count),
                            uint64_t(a.nseq)) ||
-        // Q K^T reads bf16 K: the cache itself, or (f32 cache) the K scratch.
+        // Q K^T reads the bf16 cache itself, or (f32 cache) the f16 K scratch.
         !make_map_16(&mk, a.kv_f32 ? static_cast<void *>(a.k16) : a.kcache,
-                     CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, uint64_t(a.context_length),
+                     a.kv_f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                     uint64_t(a.context_length),
                      uint64_t(a.kv_f32 ? a.nseq : a.batch) * a.kv_heads, kBlockK / 2) ||
         !make_map_16(&mv, a.v16, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, uint64_t(a.context_length),
                      uint64_t(a.nseq) * a.kv_heads, kBlockK))
@@ -887,7 +917,7 @@ cudaError_t launch_attn_prefill(const AttnPrefillLaunch &a, cudaStream_t stream)
     const int n_qtiles = (a.count + kBlockQ - 1) / kBlockQ;
     const int n_pairs = (n_qtiles + 1) / 2;
     PrefillParams p{a.q_norm, a.rope, a.err, a.kv_f32 ? 0 : a.seq0, a.count, a.base,
-                    kGroup * a.kv_head0, a.kv_heads, n_qtiles, a.eps};
+                    kGroup * a.kv_head0, a.kv_heads, n_qtiles, a.kv_f32, a.eps};
     e = cudaFuncSetAttribute(attn_prefill_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              int(kSmemPair));
     if (e != cudaSuccess) return e;

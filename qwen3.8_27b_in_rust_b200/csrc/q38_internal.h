@@ -101,8 +101,8 @@ struct q38_state {
     float *split_local = nullptr;     // [batch][heads][258]
     float *split_gathered = nullptr;  // [split_ranks][batch][heads][258]
     int split_ranks = 0;
-    // f32-cache prefill: the K rows as bf16 for the tensor cores.
-    __nv_bfloat16 *prefill_k16 = nullptr;  // [v16_seqs][kv_heads][context][256]
+    // f32-cache prefill: the K rows as f16 for the tensor cores.
+    __half *prefill_k16 = nullptr;  // [v16_seqs][kv_heads][context][256]
 };
 
 namespace q38 {
@@ -156,7 +156,7 @@ struct AttnPrefillLaunch {
     float *rope;              // scratch: RoPE table (attn_prefill_rope_floats)
     void *kcache, *vcache;    // slot base [batch][kv_heads][ctx][256], bf16 or f32
     __half *v16;              // scratch [nseq][kv_heads][ctx][256]: V as f16
-    __nv_bfloat16 *k16;       // f32 cache only: scratch [nseq][kv_heads][ctx][256], K as bf16
+    __half *k16;              // f32 cache only: scratch [nseq][kv_heads][ctx][256], K as f16
     const float *q_norm, *k_norm;
     int *err;
     int batch, seq0, nseq, count, base, context_length, heads, kv_heads;

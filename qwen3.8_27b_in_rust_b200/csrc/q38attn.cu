@@ -867,7 +867,7 @@ int q38_state_reserve_prefill(q38_state *st, int max_tokens) {
         // P = 0; they must hold finite values (0 * NaN would be NaN).
         Q38_CUDA(cudaMemset(st->prefill_v16, 0, v16_bytes));
         if (st->kv_dtype == Q38_KV_F32) {
-            // An f32 cache keeps the reference's rows; Q K^T reads a bf16 copy.
+            // An f32 cache keeps the reference's rows; Q K^T reads an f16 copy.
             Q38_CUDA(cudaMalloc(&st->prefill_k16, v16_bytes));
             Q38_CUDA(cudaMemset(st->prefill_k16, 0, v16_bytes));
         }
