@@ -139,4 +139,9 @@ def test_split_sequence_nccl_two_gpus(tmp_path):
     assert out.returncode == 0, out.stderr[-3000:]
     import json
     line = [l for l in out.stdout.splitlines() if l.startswith("{")][-1]
-    assert json.loads(line)["max_err"] < 1e-5
+    res = json.loads(line)
+    print(f"[nccl] {line}")
+    from conftest import PARITY_LOG
+    PARITY_LOG.append({"test": "test_split_sequence_nccl_two_gpus", "what": "world 2 vs 1-GPU decode",
+                       "ref_metric": res["max_err"], "scaled": None, "tol": 1e-5})
+    assert res["world"] == 2 and res["max_err"] < 1e-5
