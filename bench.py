@@ -308,12 +308,14 @@ def run_projection(args, ctx, q38attn, synth, torch, rank: int) -> dict:
     return out
 
 
-def run_split_sequence(args, ctx, q38attn, torch, dist, rank: int, world: int) -> dict:
+def run_split_sequence(args, ctx, q38attn, torch, dist, rank: int, world: int,
+                       transport: str = "p2p") -> dict:
     """Config 3, split-sequence variant: one sequence with `split_context`
     cached bf16 positions, sharded into contiguous ranges across the ranks;
-    each decode step computes per-shard softmax partials, all-gathers them over
-    NCCL and merges (q38attn.parallel.SplitSequenceDecoder). At one GPU the
-    plain decode runs over the whole range."""
+    each decode step computes per-shard softmax partials, exchanges them and
+    merges (q38attn.parallel.SplitSequenceDecoder): over peer memory inside
+    the merge kernel ("p2p") or with an NCCL all-gather ("nccl"). At one GPU
+    the plain decode runs over the whole range."""
     from q38attn.parallel import SplitSequenceDecoder, position_ranges
     P = args.split_context
     cap = P + args.split_steps + 8
@@ -333,7 +335,7 @@ def run_split_sequence(args, ctx, q38attn, torch, dist, rank: int, world: int) -
     key = torch.empty_like(key0)
     out = torch.empty(1, 6144, device="cuda")
     pos = torch.arange(P, P + args.split_steps + 3, device="cuda", dtype=torch.int32)
-    dec = SplitSequenceDecoder(ctx, st, FULL_LAYER, p0) if world > 1 else None
+    dec = SplitSequenceDecoder(ctx, st, FULL_LAYER, p0, transport=transport) if world > 1 else None
     if dist is not None:
         dist.barrier()
     stream = torch.cuda.current_stream()
@@ -705,9 +707,11 @@ def run_ours(args) -> None:
     if st.errors():
         raise RuntimeError("device error bits set during the timed region")
 
-    split = None
+    split = split_nccl = None
     if not args.no_split:
-        split = run_split_sequence(args, ctx, q38attn, torch, dist, rank, world)
+        split = run_split_sequence(args, ctx, q38attn, torch, dist, rank, world, "p2p")
+        if world > 1:
+            split_nccl = run_split_sequence(args, ctx, q38attn, torch, dist, rank, world, "nccl")
 
     prefill = lin_prefill = None
     if not args.no_prefill:
@@ -750,11 +754,12 @@ def run_ours(args) -> None:
     vals = torch.tensor([ms, attn_ms, lin_ms, e2e[0] if e2e else 0.0,
                          prefill["ms"] if prefill else 0.0,
                          lin_prefill["ms"] if lin_prefill else 0.0,
-                         split["ms"] if split else 0.0],
+                         split["ms"] if split else 0.0,
+                         split_nccl["ms"] if split_nccl else 0.0],
                         device="cuda", dtype=torch.float64)
     if dist is not None:
         dist.all_reduce(vals, op=dist.ReduceOp.MAX)
-    ms, attn_ms, lin_ms, e2e_s, prefill_ms, lin_prefill_ms, split_ms = vals.tolist()
+    ms, attn_ms, lin_ms, e2e_s, prefill_ms, lin_prefill_ms, split_ms, split_nccl_ms = vals.tolist()
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -816,12 +821,18 @@ def run_ours(args) -> None:
             kv_bytes = args.split_context * 4 * 256 * 2 * 2
             line["split_sequence"] = {
                 "workload": (f"config3 split-sequence: 1 sequence, {args.split_context} cached "
-                             f"bf16 positions sharded over {world} GPU(s); per-shard partials, "
-                             "NCCL all-gather inside q38_full_decode_split, LSE merge"),
+                             f"bf16 positions sharded over {world} GPU(s); per-shard partials "
+                             "exchanged over peer memory inside the merge kernel "
+                             "(q38_full_decode_split_p2p), LSE merge"),
                 "scaling": "strong", "ms_per_token": split_ms, "tok_s": 1e3 / split_ms,
                 "kv_gbs": kv_bytes / (split_ms * 1e-3) / 1e9,
                 "hbm_frac_per_gpu": kv_bytes / world / (split_ms * 1e-3) / 1e9 / peak,
             }
+            if split_nccl:
+                line["split_sequence"]["nccl_transport"] = {
+                    "what": "the same step with an ncclAllGather between the shard kernels and "
+                            "the merge (q38_full_decode_split)",
+                    "ms_per_token": split_nccl_ms, "tok_s": 1e3 / split_nccl_ms}
         if lin_prefill:
             flops = linear_prefill_flops(args.prefill_batch, args.prefill_len)
             toks = args.prefill_batch * args.prefill_len

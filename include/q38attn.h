@@ -257,6 +257,35 @@ int q38_nccl_unique_id(void *id);
 int q38_nccl_comm_create(const void *id, int nranks, int rank, int device, void **comm);
 int q38_nccl_comm_destroy(void *comm);
 
+/* Split-sequence decode with the exchange fused into the merge kernel, over
+ * peer memory instead of NCCL. Set-up, once per state and group of ranks
+ * (one process per GPU, every GPU able to reach every other by NVLink P2P):
+ * each rank calls q38_state_split_p2p_handle(st, nranks, handle), which
+ * allocates the state's exchange buffer (every rank's (o, m, l) partials per
+ * sequence and head, twice, plus one flag each) and returns its CUDA IPC
+ * handle (Q38_IPC_HANDLE_BYTES bytes); the host gathers the nranks handles,
+ * rank-major, on every rank by its own means; each rank then calls
+ * q38_state_split_p2p_open(st, rank, handles), which maps every peer's
+ * buffer into this process (cudaIpcOpenMemHandle).
+ *
+ * Then every rank makes the same sequence of q38_full_decode_split_p2p calls
+ * (same arguments as q38_full_decode_split, no communicator). The merge
+ * kernel of each (sequence, head) stores this rank's partial straight into
+ * every peer's buffer over NVLink, raises a flag there with the call's epoch
+ * (the state counts its calls), waits for every rank's flag in its own
+ * buffer, and merges: the exchange overlaps the other heads' merging, and no
+ * library collective or second kernel runs. No kernel reads another GPU's
+ * memory. A rank whose peers do not make the matching call gives up after
+ * the bounded wait (1 s) and records Q38_DEVERR_TIMEOUT. Destroy the states
+ * only after every rank has finished its last call. */
+#define Q38_IPC_HANDLE_BYTES 64
+int q38_state_split_p2p_handle(q38_state *st, int nranks, void *handle);
+int q38_state_split_p2p_open(q38_state *st, int rank, const void *handles);
+int q38_full_decode_split_p2p(q38_ctx *ctx, q38_state *st, int layer, int batch,
+                              const float *q_and_gate, float *key, const float *value,
+                              const int32_t *positions, int max_position, int pos_offset,
+                              float *attention, void *stream);
+
 /* Split-sequence decode, merge side: combines nparts shard partials
  * [nparts][batch][heads][258] (gathered from every shard, e.g. by an NCCL
  * all-gather) by log-sum-exp, normalises and applies the sigmoid output gate

@@ -746,7 +746,105 @@ struct MergeParams {
     float *partial_out;  // non-null: write (o, m, l) [batch][heads][258] instead
     int context_length, heads, chunk, max_splits, max_position, pos_offset, sharded;
     int merge_ctas;      // CTAs (one cluster) per (head, sequence)
+    // Split-sequence exchange over peer memory (p2p_nranks > 0; see
+    // p2p_exchange_merge): every rank's exchange buffer, this rank's index,
+    // the buffers' batch (the state's), the call's epoch, the wait limit and
+    // the error word.
+    float *const *p2p_peers;
+    int p2p_rank, p2p_nranks, p2p_batch;
+    uint32_t p2p_epoch;
+    uint64_t wait_ns;
+    int *err;
 };
+
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t *p) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void st_release_sys(uint32_t *p, uint32_t v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Waits until *flag == epoch, for at most limit_ns of %globaltimer.
+__device__ __forceinline__ bool wait_flag_sys(const uint32_t *flag, uint32_t epoch, uint64_t limit_ns) {
+    if (ld_acquire_sys(flag) == epoch) return true;
+    const uint64_t t0 = global_timer_ns();
+    for (;;) {
+#pragma unroll 1
+        for (int i = 0; i < 64; ++i)
+            if (ld_acquire_sys(flag) == epoch) return true;
+        if (global_timer_ns() - t0 > limit_ns) return false;
+    }
+}
+
+// Exchange buffer of one rank (allocated by q38_state_split_p2p_handle):
+//   partials [2][nranks][batch][heads][258] f32 (o[256], m, l)
+//   flags    [2][nranks][batch][heads] u32
+// The leading 2 is the call's epoch parity: a rank writes epoch e + 2 into a
+// peer's slot only after it has seen that peer's flag for e + 1, which the
+// peer raises only after it has finished reading epoch e, so no slot is
+// overwritten before it is read.
+__host__ __device__ inline size_t p2p_partial_floats(int nranks, int batch, int heads) {
+    return size_t(2) * nranks * batch * heads * (kAttnHeadDim + 2);
+}
+
+// The split-sequence exchange of one (head, sequence), by CTA 0 of its merge
+// cluster after the local merge: this rank's (o, m, l) is stored into slot
+// p2p_rank of every rank's exchange buffer over NVLink (plain stores; the
+// buffers are CUDA IPC mappings), made visible with a system-scope fence,
+// and announced by one release store of the epoch into each rank's flag;
+// then the CTA waits (bounded) until every rank's flag for this (head,
+// sequence) in its own buffer holds the epoch, merges the nranks partials by
+// log-sum-exp and writes the gated output. No kernel reads another GPU's
+// memory and nothing is exchanged by TMA.
+__device__ void p2p_exchange_merge(const MergeParams &p, int h, int b, float ot, float m, float lt,
+                                   bool has_rows) {
+    const int d = threadIdx.x;
+    const int R = p.p2p_nranks, H = p.heads, B = p.p2p_batch;
+    const int par = int(p.p2p_epoch & 1u);
+    const size_t nparts = p2p_partial_floats(R, B, H);
+    auto slot = [&](int r) { return ((size_t(par) * R + r) * B + b) * H + h; };
+    const float o_send = has_rows ? ot : 0.f;
+    for (int r = 0; r < R; ++r) {
+        float *dst = p.p2p_peers[r] + slot(p.p2p_rank) * (kAttnHeadDim + 2);
+        dst[d] = o_send;
+        if (d == 0) {
+            dst[kAttnHeadDim] = m;
+            dst[kAttnHeadDim + 1] = lt;
+        }
+    }
+    __threadfence_system();
+    __syncthreads();
+    if (d == 0) {
+        for (int r = 0; r < R; ++r)
+            st_release_sys(reinterpret_cast<uint32_t *>(p.p2p_peers[r] + nparts) + slot(p.p2p_rank),
+                           p.p2p_epoch);
+        const uint32_t *flags = reinterpret_cast<const uint32_t *>(p.p2p_peers[p.p2p_rank] + nparts);
+        bool ok = true;
+        for (int r = 0; r < R && ok; ++r) ok = wait_flag_sys(flags + slot(r), p.p2p_epoch, p.wait_ns);
+        if (!ok) set_error(p.err, kDevErrTimeout);  // the output is then undefined
+    }
+    __syncthreads();
+    // Peers wrote these words over NVLink into this GPU's L2; read them at L2
+    // (ld.global.cg), never from L1, which may still hold the same parity
+    // slot from two calls before.
+    const float *mine = p.p2p_peers[p.p2p_rank];
+    float mm = -INFINITY;
+    for (int r = 0; r < R; ++r) mm = fmaxf(mm, __ldcg(mine + slot(r) * (kAttnHeadDim + 2) + kAttnHeadDim));
+    float lsum = 0.f, osum = 0.f;
+    for (int r = 0; r < R; ++r) {
+        const float *part = mine + slot(r) * (kAttnHeadDim + 2);
+        const float mr = __ldcg(part + kAttnHeadDim);
+        if (mr == -INFINITY) continue;  // a shard without visible rows
+        const float w = expf(mr - mm);
+        lsum += w * __ldcg(part + kAttnHeadDim + 1);
+        osum += w * __ldcg(part + d);
+    }
+    const float gate = p.q_and_gate[(size_t(b) * H + h) * 2 * kAttnHeadDim + kAttnHeadDim + d];
+    p.attention[(size_t(b) * H + h) * kAttnHeadDim + d] = (osum / lsum) * sigmoidf_ref(gate);
+}
 
 __device__ __forceinline__ float ld_cluster_f32(uint32_t addr) {
     float v;
@@ -837,6 +935,10 @@ __global__ void __launch_bounds__(kAttnHeadDim) attn_decode_merge_kernel(MergePa
         if (g != 0) return;
     }
     const int d = tid;
+    if (p.p2p_nranks > 0) {
+        p2p_exchange_merge(p, h, b, ot, m, lt, nsplit > 0);
+        return;
+    }
     if (p.partial_out) {
         // This shard's (o, m, l) relative to its own max m (m = -inf, l = 0,
         // o = 0 when the shard holds no visible row).
@@ -910,10 +1012,11 @@ cudaError_t launch_typed(const AttnDecodeLaunch &a, int sm_count, cudaStream_t s
         plan_attn_decode(a.batch, a.kv_heads, std::max(max_rows, 1) - 1, a.kv_dtype, sm_count);
     if (plan.nsplit > a.max_splits) return cudaErrorInvalidValue;
 
+    const int sharded = (a.partial_out != nullptr || a.p2p_nranks > 0) ? 1 : 0;
     PrepParams pp{a.q_and_gate, a.key,      a.value,        a.positions,  a.kcache,
                   a.vcache,     a.qprep,    a.err,          a.q_norm,     a.k_norm,
                   a.context_length, a.heads, a.kv_heads,    a.max_position, a.pos_offset,
-                  a.partial_out != nullptr, a.theta_scale, a.eps};
+                  sharded,      a.theta_scale, a.eps};
     attn_decode_prep_kernel<KV>
         <<<dim3(a.heads + a.kv_heads, a.batch), kAttnHeadDim, 0, stream>>>(pp);
     cudaError_t e = cudaGetLastError();
@@ -926,7 +1029,7 @@ cudaError_t launch_typed(const AttnDecodeLaunch &a, int sm_count, cudaStream_t s
     SplitParams sp{a.kcache,   a.vcache,  a.qprep,  a.positions,       a.part_o,
                    a.part_ml,  a.err,     a.context_length, a.heads, a.kv_heads,
                    plan.chunk, a.max_splits, a.max_position, a.pos_offset,
-                   a.partial_out != nullptr, a.wait_ns ? a.wait_ns : kWaitTimeoutNs,
+                   sharded, a.wait_ns ? a.wait_ns : kWaitTimeoutNs,
                    a.skip_kv_loads};
     constexpr bool kTc = sizeof(KV) == 2;
     CUtensorMap map_k{}, map_v{};
@@ -962,7 +1065,9 @@ cudaError_t launch_typed(const AttnDecodeLaunch &a, int sm_count, cudaStream_t s
     const int merge_ctas = std::min({8, fill, std::max(1, (plan.nsplit + 31) / 32)});
     MergeParams mp{a.part_o,   a.part_ml,  a.q_and_gate, a.positions,  a.attention,
                    a.partial_out, a.context_length, a.heads, plan.chunk, a.max_splits,
-                   a.max_position, a.pos_offset, a.partial_out != nullptr, merge_ctas};
+                   a.max_position, a.pos_offset, sharded, merge_ctas,
+                   a.p2p_peers, a.p2p_rank, a.p2p_nranks, a.p2p_batch, a.p2p_epoch,
+                   a.wait_ns ? a.wait_ns : kWaitTimeoutNs, a.err};
     cudaLaunchAttribute mattr[2];
     mattr[0] = attr[0];
     mattr[1].id = cudaLaunchAttributeClusterDimension;
@@ -1033,6 +1138,11 @@ DecodeSplitPlan plan_attn_decode(int batch, int kv_heads, int max_position, int 
     plan.chunk = chunk;
     plan.nsplit = (n + chunk - 1) / chunk;
     return plan;
+}
+
+size_t attn_p2p_exchange_bytes(int nranks, int batch, int heads) {
+    return p2p_partial_floats(nranks, batch, heads) * sizeof(float) +
+           size_t(2) * nranks * batch * heads * sizeof(uint32_t);
 }
 
 cudaError_t launch_attn_merge_shards(const float *partials, int nparts, int batch, int heads,

@@ -101,6 +101,12 @@ struct q38_state {
     float *split_local = nullptr;     // [batch][heads][258]
     float *split_gathered = nullptr;  // [split_ranks][batch][heads][258]
     int split_ranks = 0;
+    // Split-sequence exchange over peer memory (q38_state_split_p2p_*).
+    void *p2p_buf = nullptr;          // this rank's exchange buffer (IPC-exported)
+    int p2p_nranks = 0, p2p_rank = -1;
+    std::vector<void *> p2p_opened;   // peers' buffers opened with cudaIpcOpenMemHandle
+    float **p2p_peers_dev = nullptr;  // device array [nranks] of the buffers' addresses
+    uint32_t p2p_epoch = 0;           // calls made so far (the next call's epoch is +1)
     // f32-cache prefill: the K rows as f16 for the tensor cores.
     __half *prefill_k16 = nullptr;  // [v16_seqs][kv_heads][context][256]
 };
@@ -139,6 +145,11 @@ struct AttnDecodeLaunch {
     float *partial_out = nullptr;  // non-null: packed (o, m, l) partials instead of output
     uint64_t wait_ns = 0;          // bounded-wait limit of the split kernel (0: the default)
     int skip_kv_loads = 0;         // error-path testing (Q38_DEBUG_SKIP_KV_LOADS)
+    // Split-sequence exchange over peer memory (p2p_nranks > 0): the merge
+    // kernel exchanges the shards' partials itself and writes `attention`.
+    float *const *p2p_peers = nullptr;  // device array: every rank's exchange buffer
+    int p2p_rank = 0, p2p_nranks = 0, p2p_batch = 0;
+    uint32_t p2p_epoch = 0;
 };
 cudaError_t launch_attn_decode(const AttnDecodeLaunch &a, int sm_count, cudaStream_t stream);
 cudaError_t launch_attn_merge_shards(const float *partials, int nparts, int batch, int heads,
@@ -147,6 +158,8 @@ cudaError_t launch_attn_merge_shards(const float *partials, int nparts, int batc
 DecodeSplitPlan plan_attn_decode(int batch, int kv_heads, int max_position, int kv_dtype,
                                  int sm_count);
 int attn_decode_max_splits(int context_length, int kv_dtype);
+// Bytes of one rank's split-sequence exchange buffer (partials and flags).
+size_t attn_p2p_exchange_bytes(int nranks, int batch, int heads);
 
 struct AttnPrefillLaunch {
     const float *q_and_gate;  // [nseq][count][heads*512]

@@ -173,6 +173,10 @@ void free_state(q38_state *st) {
     cudaFree(st->ckpt_delta);
     cudaFree(st->split_local);
     cudaFree(st->split_gathered);
+    for (void *q : st->p2p_opened) cudaIpcCloseMemHandle(q);
+    st->p2p_opened.clear();
+    cudaFree(st->p2p_buf);
+    cudaFree(st->p2p_peers_dev);
     cudaFree(st->prefill_k16);
     if (st->host_err) cudaFreeHost(st->host_err);
     if (st->host_ev_prep) cudaEventDestroy(st->host_ev_prep);
@@ -754,6 +758,10 @@ int q38_state_reserve_split(q38_state *st, int nranks) {
     DeviceGuard guard(st->ctx->device);
     cudaFree(st->split_local);
     cudaFree(st->split_gathered);
+    for (void *q : st->p2p_opened) cudaIpcCloseMemHandle(q);
+    st->p2p_opened.clear();
+    cudaFree(st->p2p_buf);
+    cudaFree(st->p2p_peers_dev);
     st->split_local = st->split_gathered = nullptr;
     st->split_ranks = 0;
     const size_t per = size_t(st->batch) * st->ctx->geom.attn_heads * (q38::kAttnHeadDim + 2);
@@ -788,6 +796,91 @@ int q38_full_decode_split(q38_ctx *ctx, q38_state *st, int layer, int batch,
         return rc;
     return q38_attn_merge_shards(ctx, nranks, batch, st->split_gathered, q_and_gate, attention,
                                  stream);
+}
+
+int q38_state_split_p2p_handle(q38_state *st, int nranks, void *handle) {
+    static_assert(sizeof(cudaIpcMemHandle_t) == Q38_IPC_HANDLE_BYTES, "IPC handle size");
+    if (!st || !handle) return fail(Q38_ERR_ARG, "null argument");
+    if (nranks <= 0 || nranks > 64) return fail(Q38_ERR_ARG, "nranks %d outside 1..64", nranks);
+    DeviceGuard guard(st->ctx->device);
+    if (st->p2p_buf && st->p2p_nranks != nranks) {
+        for (void *q : st->p2p_opened) cudaIpcCloseMemHandle(q);
+        st->p2p_opened.clear();
+        cudaFree(st->p2p_buf);
+        st->p2p_buf = nullptr;
+        st->p2p_rank = -1;
+    }
+    if (!st->p2p_buf) {
+        const size_t bytes =
+            q38::attn_p2p_exchange_bytes(nranks, st->batch, st->ctx->geom.attn_heads);
+        Q38_CUDA(cudaMalloc(&st->p2p_buf, bytes));
+        Q38_CUDA(cudaMemset(st->p2p_buf, 0, bytes));  // flags start below every epoch
+        st->p2p_nranks = nranks;
+        st->p2p_rank = -1;
+        st->p2p_epoch = 0;
+    }
+    Q38_CUDA(cudaIpcGetMemHandle(static_cast<cudaIpcMemHandle_t *>(handle), st->p2p_buf));
+    return Q38_OK;
+}
+
+int q38_state_split_p2p_open(q38_state *st, int rank, const void *handles) {
+    if (!st || !handles) return fail(Q38_ERR_ARG, "null argument");
+    if (!st->p2p_buf) return fail(Q38_ERR_ARG, "q38_state_split_p2p_handle was not called");
+    const int nranks = st->p2p_nranks;
+    if (rank < 0 || rank >= nranks) return fail(Q38_ERR_ARG, "rank %d outside 0..%d", rank, nranks - 1);
+    DeviceGuard guard(st->ctx->device);
+    for (void *q : st->p2p_opened) cudaIpcCloseMemHandle(q);
+    st->p2p_opened.clear();
+    st->p2p_rank = -1;
+    std::vector<float *> ptrs(size_t(nranks), nullptr);
+    for (int r = 0; r < nranks; ++r) {
+        if (r == rank) {
+            ptrs[size_t(r)] = static_cast<float *>(st->p2p_buf);
+            continue;
+        }
+        cudaIpcMemHandle_t h;
+        std::memcpy(&h, static_cast<const unsigned char *>(handles) + size_t(r) * sizeof h, sizeof h);
+        void *q = nullptr;
+        const cudaError_t e = cudaIpcOpenMemHandle(&q, h, cudaIpcMemLazyEnablePeerAccess);
+        if (e != cudaSuccess) {
+            for (void *o : st->p2p_opened) cudaIpcCloseMemHandle(o);
+            st->p2p_opened.clear();
+            return cuda_fail(e, "cudaIpcOpenMemHandle of a peer's exchange buffer");
+        }
+        st->p2p_opened.push_back(q);
+        ptrs[size_t(r)] = static_cast<float *>(q);
+    }
+    if (!st->p2p_peers_dev) Q38_CUDA(cudaMalloc(&st->p2p_peers_dev, 64 * sizeof(float *)));
+    Q38_CUDA(cudaMemcpy(st->p2p_peers_dev, ptrs.data(), size_t(nranks) * sizeof(float *),
+                        cudaMemcpyHostToDevice));
+    st->p2p_rank = rank;
+    st->p2p_epoch = 0;
+    return Q38_OK;
+}
+
+int q38_full_decode_split_p2p(q38_ctx *ctx, q38_state *st, int layer, int batch,
+                              const float *q_and_gate, float *key, const float *value,
+                              const int32_t *positions, int max_position, int pos_offset,
+                              float *attention, void *stream) {
+    if (int rc = check_state(ctx, st)) return rc;
+    if (st->p2p_rank < 0) return fail(Q38_ERR_ARG, "q38_state_split_p2p_open was not called");
+    if (pos_offset < 0) return fail(Q38_ERR_ARG, "pos_offset must be >= 0");
+    if (max_position < 0) return fail(Q38_ERR_ARG, "max_position is required when sharding");
+    if (!attention) return fail(Q38_ERR_ARG, "null attention");
+    q38::AttnDecodeLaunch a;
+    if (int rc = prepare_full_decode(ctx, st, layer, batch, q_and_gate, key, value, positions,
+                                     max_position, attention, &a, true))
+        return rc;
+    a.pos_offset = pos_offset;
+    a.p2p_peers = st->p2p_peers_dev;
+    a.p2p_rank = st->p2p_rank;
+    a.p2p_nranks = st->p2p_nranks;
+    a.p2p_batch = st->batch;
+    a.p2p_epoch = ++st->p2p_epoch;
+    DeviceGuard guard(ctx->device);
+    cudaError_t e = q38::launch_attn_decode(a, ctx->sm_count, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "split-sequence decode launch (peer exchange)");
+    return Q38_OK;
 }
 
 int q38_linear_decode(q38_ctx *ctx, q38_state *st, int layer, int batch, float *qkv,

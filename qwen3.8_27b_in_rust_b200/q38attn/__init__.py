@@ -29,7 +29,8 @@ from typing import Optional
 
 import numpy as np
 
-from ._lib import (Q38_DEBUG_SKIP_KV_LOADS, Q38_DEVERR_RANGE, Q38_NCCL_ID_BYTES,
+from ._lib import (Q38_DEBUG_SKIP_KV_LOADS, Q38_DEVERR_RANGE, Q38_IPC_HANDLE_BYTES,
+                   Q38_NCCL_ID_BYTES,
                    Q38_DEVERR_POSITION, Q38_DEVERR_SHAPE, Q38_DEVERR_TIMEOUT, Q38_ERR_ARG,
                    Q38_ERR_CUDA, Q38_ERR_TIMEOUT, Q38_GGML_BF16, Q38_GGML_F16, Q38_GGML_F32,
                    Q38_GGML_IQ4_NL, Q38_GGML_IQ4_XS, Q38_GGML_Q2_K, Q38_GGML_Q3_K,
@@ -41,6 +42,7 @@ __all__ = [
     "Q38_OK", "Q38_ERR_ARG", "Q38_ERR_CUDA", "Q38_ERR_TIMEOUT", "Q38_KV_F32", "Q38_KV_BF16",
     "Q38_DEVERR_POSITION", "Q38_DEVERR_TIMEOUT", "Q38_DEVERR_SHAPE", "Q38_DEVERR_RANGE",
     "Q38_DEBUG_SKIP_KV_LOADS", "Q38_NCCL_ID_BYTES", "nccl_unique_id", "NcclComm",
+    "Q38_IPC_HANDLE_BYTES",
     "is_full_attention", "full_index", "recurrent_index", "gguf_read_f32", "Weight",
     "Q38_GGML_F32", "Q38_GGML_F16", "Q38_GGML_BF16", "Q38_GGML_Q8_0", "Q38_GGML_Q2_K",
     "Q38_GGML_Q3_K", "Q38_GGML_Q4_K", "Q38_GGML_Q5_K", "Q38_GGML_Q6_K", "Q38_GGML_IQ4_NL",
@@ -206,6 +208,19 @@ class State:
     def reserve_split(self, nranks: int) -> None:
         """Sizes the buffers of split-sequence decode over `nranks` ranks."""
         check(self._lib.q38_state_reserve_split(self.handle, nranks))
+
+    def split_p2p_handle(self, nranks: int) -> bytes:
+        """Allocates this rank's split-sequence exchange buffer for `nranks`
+        ranks and returns its CUDA IPC handle (q38_state_split_p2p_handle)."""
+        buf = ctypes.create_string_buffer(Q38_IPC_HANDLE_BYTES)
+        check(self._lib.q38_state_split_p2p_handle(self.handle, nranks, buf))
+        return buf.raw
+
+    def split_p2p_open(self, rank: int, handles: list) -> None:
+        """Maps every peer's exchange buffer (handles: every rank's, in rank order)."""
+        blob = b"".join(handles)
+        buf = ctypes.create_string_buffer(blob, len(blob))
+        check(self._lib.q38_state_split_p2p_open(self.handle, rank, buf))
 
     def set_debug(self, flags: int = 0, wait_ns: int = 0) -> None:
         """Error-path testing (q38_state_set_debug): Q38_DEBUG_SKIP_KV_LOADS
@@ -511,6 +526,17 @@ class Context:
             self.handle, state.handle, layer, b, _dev_ptr(q_and_gate, "q_and_gate"),
             _dev_ptr(key, "key"), _dev_ptr(value, "value"),
             _dev_ptr(positions, "positions", "int32"), max_position, pos_offset, handle,
+            _dev_ptr(attention, "attention"), _stream_ptr(stream)))
+
+    def full_decode_split_p2p(self, state: State, layer: int, q_and_gate, key, value, positions,
+                              attention, max_position: int, pos_offset: int, stream=None) -> None:
+        """Split-sequence decode with the exchange fused into the merge kernel
+        (peer-memory stores and flags; State.split_p2p_open first)."""
+        b = q_and_gate.shape[0]
+        check(self._lib.q38_full_decode_split_p2p(
+            self.handle, state.handle, layer, b, _dev_ptr(q_and_gate, "q_and_gate"),
+            _dev_ptr(key, "key"), _dev_ptr(value, "value"),
+            _dev_ptr(positions, "positions", "int32"), max_position, pos_offset,
             _dev_ptr(attention, "attention"), _stream_ptr(stream)))
 
     def merge_shards(self, partials, q_and_gate, attention, stream=None) -> None:

@@ -25,6 +25,7 @@ Q38_DEVERR_SHAPE = 4
 Q38_DEVERR_RANGE = 8
 Q38_DEBUG_SKIP_KV_LOADS = 1
 Q38_NCCL_ID_BYTES = 128
+Q38_IPC_HANDLE_BYTES = 64
 Q38_GGML_F32, Q38_GGML_F16, Q38_GGML_Q8_0, Q38_GGML_BF16 = 0, 1, 8, 30
 Q38_GGML_Q2_K, Q38_GGML_Q3_K, Q38_GGML_Q4_K, Q38_GGML_Q5_K, Q38_GGML_Q6_K = 10, 11, 12, 13, 14
 Q38_GGML_IQ4_NL, Q38_GGML_IQ4_XS = 20, 23
@@ -77,6 +78,10 @@ SIGNATURES = {
     "q38_state_reserve_split": (c_int, [_VP, c_int]),
     "q38_full_decode_split": (c_int, [_VP, _VP, c_int, c_int, _VP, _VP, _VP, _VP, c_int, c_int,
                                       _VP, _VP, _VP]),
+    "q38_state_split_p2p_handle": (c_int, [_VP, c_int, _VP]),
+    "q38_state_split_p2p_open": (c_int, [_VP, c_int, _VP]),
+    "q38_full_decode_split_p2p": (c_int, [_VP, _VP, c_int, c_int, _VP, _VP, _VP, _VP, c_int,
+                                          c_int, _VP, _VP]),
     "q38_nccl_unique_id": (c_int, [_VP]),
     "q38_nccl_comm_create": (c_int, [_VP, c_int, c_int, c_int, POINTER(c_void_p)]),
     "q38_nccl_comm_destroy": (c_int, [_VP]),

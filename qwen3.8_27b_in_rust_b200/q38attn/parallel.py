@@ -16,10 +16,13 @@ Work is split only where it shards naturally:
 * Split-sequence decode (one long sequence): the sequence's cached positions
   are split into contiguous ranges, one per rank (`position_ranges`). Each
   rank computes softmax partials (o, m, l) over its range, the partials of
-  all ranks are exchanged with one NCCL all-gather (24 x 258 floats per rank
-  and sequence) and merged by log-sum-exp -- all inside the library call
-  q38_full_decode_split on an NCCL communicator, so a host needs no
-  framework for it. This replaces the single position loop of full_core
+  all ranks are exchanged (24 x 258 floats per rank and sequence) and merged
+  by log-sum-exp, inside one library call, so a host needs no framework for
+  it. Two transports: "p2p" (q38_full_decode_split_p2p: the merge kernel
+  stores its partial into every peer's buffer over NVLink and waits for
+  theirs -- the exchange fused into the kernel), and "nccl"
+  (q38_full_decode_split: one ncclAllGather between the shard kernels and the
+  merge). This replaces the single position loop of full_core
   (src/model/ops.rs:884-913) across GPUs.
 """
 from __future__ import annotations
@@ -74,33 +77,59 @@ def exchange_unique_id(dist, make_id, group=None) -> bytes:
     return obj[0]
 
 
+def exchange_handles(dist, handle: bytes, group=None) -> list:
+    """Every rank's IPC handle, in rank order, on every rank of `group`."""
+    out = [None] * dist.get_world_size(group)
+    dist.all_gather_object(out, handle, group=group)
+    return out
+
+
 class SplitSequenceDecoder:
     """Runs one full-attention decode step of sequences whose KV positions are
-    sharded across the ranks of `group` (torch.distributed only exchanges the
-    NCCL id at set-up; the step's all-gather is the library's).
+    sharded across the ranks of `group`. torch.distributed only carries the
+    set-up bytes (the NCCL id or the IPC handles); the step's exchange is the
+    library's.
 
     `state` on each rank holds positions [pos_offset, pos_offset + its
-    context_length) of every sequence."""
+    context_length) of every sequence. transport: "p2p" (the exchange fused
+    into the merge kernel over peer memory) or "nccl"."""
 
-    def __init__(self, ctx, state, layer: int, pos_offset: int, group=None):
+    def __init__(self, ctx, state, layer: int, pos_offset: int, group=None,
+                 transport: str = "p2p"):
         import torch.distributed as dist
 
         import q38attn
+        if transport not in ("p2p", "nccl"):
+            raise ValueError("transport is 'p2p' or 'nccl'")
         self.ctx, self.state, self.layer = ctx, state, layer
         self.pos_offset = pos_offset
+        self.transport = transport
         world = dist.get_world_size(group)
         rank = dist.get_rank(group)
-        uid = exchange_unique_id(dist, q38attn.nccl_unique_id, group)
-        self.comm = q38attn.NcclComm(uid, world, rank, ctx.device)
-        state.reserve_split(world)
+        self.comm = None
+        if transport == "nccl":
+            uid = exchange_unique_id(dist, q38attn.nccl_unique_id, group)
+            self.comm = q38attn.NcclComm(uid, world, rank, ctx.device)
+            state.reserve_split(world)
+        else:
+            handles = exchange_handles(dist, state.split_p2p_handle(world), group)
+            state.split_p2p_open(rank, handles)
+            dist.barrier(group)  # every rank has mapped every buffer before the first step
 
     def step(self, q_and_gate, key, value, positions, attention, max_position: int,
              stream=None) -> None:
         """Every rank passes the same q_and_gate/key/value/positions (the
         token's projections); every rank receives the merged attention."""
-        self.ctx.full_decode_split(self.state, self.layer, q_and_gate, key, value, positions,
-                                   attention, max_position, self.pos_offset, self.comm,
-                                   stream=stream)
+        if self.transport == "nccl":
+            self.ctx.full_decode_split(self.state, self.layer, q_and_gate, key, value,
+                                       positions, attention, max_position, self.pos_offset,
+                                       self.comm, stream=stream)
+        else:
+            self.ctx.full_decode_split_p2p(self.state, self.layer, q_and_gate, key, value,
+                                           positions, attention, max_position, self.pos_offset,
+                                           stream=stream)
 
     def close(self) -> None:
-        self.comm.close()
+        if self.comm is not None:
+            self.comm.close()
+            self.comm = None

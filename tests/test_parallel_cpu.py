@@ -118,6 +118,36 @@ def _id_worker(rank, world, port, result):
         dist.destroy_process_group()
 
 
+def _handle_worker(rank, world, port, result):
+    import torch.distributed as dist
+
+    from q38attn.parallel import exchange_handles
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        result[rank] = exchange_handles(dist, bytes([rank]) * 64)
+    finally:
+        dist.destroy_process_group()
+
+
+def test_ipc_handle_exchange_gloo():
+    """The peer-memory transport's set-up: every rank receives every rank's
+    64-byte handle in rank order."""
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    manager = ctx.Manager()
+    result = manager.dict()
+    port = _free_port()
+    procs = [ctx.Process(target=_handle_worker, args=(r, 2, port, result)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(120)
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    want = [bytes([0]) * 64, bytes([1]) * 64]
+    assert result[0] == want and result[1] == want
+
+
 def test_nccl_id_exchange_gloo():
     """The split-sequence decoder's set-up: rank 0 alone makes the NCCL id and
     every rank receives the same 128 bytes over the host's process group."""
