@@ -262,7 +262,8 @@ int q38_nccl_comm_destroy(void *comm);
  * (one process per GPU, every GPU able to reach every other by NVLink P2P):
  * each rank calls q38_state_split_p2p_handle(st, nranks, handle), which
  * allocates the state's exchange buffer (every rank's (o, m, l) partials per
- * sequence and head, twice, plus one flag each) and returns its CUDA IPC
+ * sequence and head, twice, each value stored with its call's epoch in one
+ * 8-byte word) and returns its CUDA IPC
  * handle (Q38_IPC_HANDLE_BYTES bytes); the host gathers the nranks handles,
  * rank-major, on every rank by its own means; each rank then calls
  * q38_state_split_p2p_open(st, rank, handles), which maps every peer's
@@ -271,10 +272,10 @@ int q38_nccl_comm_destroy(void *comm);
  * Then every rank makes the same sequence of q38_full_decode_split_p2p calls
  * (same arguments as q38_full_decode_split, no communicator). The merge
  * kernel of each (sequence, head) stores this rank's partial straight into
- * every peer's buffer over NVLink, raises a flag there with the call's epoch
- * (the state counts its calls), waits for every rank's flag in its own
- * buffer, and merges: the exchange overlaps the other heads' merging, and no
- * library collective or second kernel runs. No kernel reads another GPU's
+ * every peer's buffer over NVLink, every value tagged with the call's epoch
+ * (the state counts its calls), waits until its own buffer holds every
+ * rank's values of this epoch, and merges: the exchange overlaps the other
+ * heads' merging, and no library collective or second kernel runs. No kernel reads another GPU's
  * memory. A rank whose peers do not make the matching call gives up after
  * the bounded wait (1 s) and records Q38_DEVERR_TIMEOUT. Destroy the states
  * only after every rank has finished its last call. */

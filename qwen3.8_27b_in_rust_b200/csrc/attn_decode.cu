@@ -757,91 +757,84 @@ struct MergeParams {
     int *err;
 };
 
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t *p) {
-    uint32_t v;
-    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
+// One exchanged value with the epoch of its call: (epoch << 32) | bits. An
+// aligned 8-byte store is seen whole or not at all, so a reader that finds
+// the current epoch in a word also has its value: no fence and no separate
+// flag are needed.
+__device__ __forceinline__ void st_word_sys(unsigned long long *p, float v, uint32_t epoch) {
+    const unsigned long long w = (static_cast<unsigned long long>(epoch) << 32) | __float_as_uint(v);
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
 }
 
-__device__ __forceinline__ void st_release_sys(uint32_t *p, uint32_t v) {
-    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-
-// Waits until *flag == epoch, for at most limit_ns of %globaltimer.
-__device__ __forceinline__ bool wait_flag_sys(const uint32_t *flag, uint32_t epoch, uint64_t limit_ns) {
-    if (ld_acquire_sys(flag) == epoch) return true;
+// Waits (at most limit_ns of %globaltimer) for the word to carry `epoch`;
+// returns its value, or NaN if the wait gave up (*ok cleared).
+__device__ __forceinline__ float wait_word_sys(const unsigned long long *p, uint32_t epoch,
+                                               uint64_t limit_ns, bool *ok) {
+    unsigned long long w;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+    if (uint32_t(w >> 32) == epoch) return __uint_as_float(uint32_t(w));
     const uint64_t t0 = global_timer_ns();
     for (;;) {
 #pragma unroll 1
-        for (int i = 0; i < 64; ++i)
-            if (ld_acquire_sys(flag) == epoch) return true;
-        if (global_timer_ns() - t0 > limit_ns) return false;
+        for (int i = 0; i < 64; ++i) {
+            asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+            if (uint32_t(w >> 32) == epoch) return __uint_as_float(uint32_t(w));
+        }
+        if (global_timer_ns() - t0 > limit_ns) {
+            *ok = false;
+            return __uint_as_float(0x7fc00000u);
+        }
     }
 }
 
 // Exchange buffer of one rank (allocated by q38_state_split_p2p_handle):
-//   partials [2][nranks][batch][heads][258] f32 (o[256], m, l)
-//   flags    [2][nranks][batch][heads] u32
-// The leading 2 is the call's epoch parity: a rank writes epoch e + 2 into a
-// peer's slot only after it has seen that peer's flag for e + 1, which the
-// peer raises only after it has finished reading epoch e, so no slot is
+//   [2][nranks][batch][heads][258] 8-byte words (o[256], m, l, each with its
+//   call's epoch).
+// The leading 2 is the epoch's parity: a rank writes epoch e + 2 into a
+// peer's slot only after it has read that peer's words of e + 1, which the
+// peer writes only after it has finished reading epoch e, so no slot is
 // overwritten before it is read.
-__host__ __device__ inline size_t p2p_partial_floats(int nranks, int batch, int heads) {
+__host__ __device__ inline size_t p2p_words(int nranks, int batch, int heads) {
     return size_t(2) * nranks * batch * heads * (kAttnHeadDim + 2);
 }
 
 // The split-sequence exchange of one (head, sequence), by CTA 0 of its merge
-// cluster after the local merge: this rank's (o, m, l) is stored into slot
-// p2p_rank of every rank's exchange buffer over NVLink (plain stores; the
-// buffers are CUDA IPC mappings), made visible with a system-scope fence,
-// and announced by one release store of the epoch into each rank's flag;
-// then the CTA waits (bounded) until every rank's flag for this (head,
-// sequence) in its own buffer holds the epoch, merges the nranks partials by
-// log-sum-exp and writes the gated output. No kernel reads another GPU's
-// memory and nothing is exchanged by TMA.
+// cluster after the local merge: thread d stores this rank's o[d] (threads 0
+// and 1 also m and l) as epoch-tagged words into slot p2p_rank of every
+// rank's exchange buffer over NVLink (plain stores; the buffers are CUDA IPC
+// mappings), then waits (bounded) until its own words of every rank carry
+// the epoch, and the CTA merges the nranks partials by log-sum-exp and writes
+// the gated output. No kernel reads another GPU's memory and nothing is
+// exchanged by TMA.
 __device__ void p2p_exchange_merge(const MergeParams &p, int h, int b, float ot, float m, float lt,
                                    bool has_rows) {
     const int d = threadIdx.x;
     const int R = p.p2p_nranks, H = p.heads, B = p.p2p_batch;
     const int par = int(p.p2p_epoch & 1u);
-    const size_t nparts = p2p_partial_floats(R, B, H);
-    auto slot = [&](int r) { return ((size_t(par) * R + r) * B + b) * H + h; };
+    auto slot = [&](int r) { return (((size_t(par) * R + r) * B + b) * H + h) * (kAttnHeadDim + 2); };
     const float o_send = has_rows ? ot : 0.f;
     for (int r = 0; r < R; ++r) {
-        float *dst = p.p2p_peers[r] + slot(p.p2p_rank) * (kAttnHeadDim + 2);
-        dst[d] = o_send;
-        if (d == 0) {
-            dst[kAttnHeadDim] = m;
-            dst[kAttnHeadDim + 1] = lt;
-        }
+        unsigned long long *dst =
+            reinterpret_cast<unsigned long long *>(p.p2p_peers[r]) + slot(p.p2p_rank);
+        st_word_sys(dst + d, o_send, p.p2p_epoch);
+        if (d < 2) st_word_sys(dst + kAttnHeadDim + d, d == 0 ? m : lt, p.p2p_epoch);
     }
-    __threadfence_system();
-    __syncthreads();
-    if (d == 0) {
-        for (int r = 0; r < R; ++r)
-            st_release_sys(reinterpret_cast<uint32_t *>(p.p2p_peers[r] + nparts) + slot(p.p2p_rank),
-                           p.p2p_epoch);
-        const uint32_t *flags = reinterpret_cast<const uint32_t *>(p.p2p_peers[p.p2p_rank] + nparts);
-        bool ok = true;
-        for (int r = 0; r < R && ok; ++r) ok = wait_flag_sys(flags + slot(r), p.p2p_epoch, p.wait_ns);
-        if (!ok) set_error(p.err, kDevErrTimeout);  // the output is then undefined
-    }
-    __syncthreads();
-    // Peers wrote these words over NVLink into this GPU's L2; read them at L2
-    // (ld.global.cg), never from L1, which may still hold the same parity
-    // slot from two calls before.
-    const float *mine = p.p2p_peers[p.p2p_rank];
+    const unsigned long long *mine = reinterpret_cast<const unsigned long long *>(p.p2p_peers[p.p2p_rank]);
+    bool ok = true;
     float mm = -INFINITY;
-    for (int r = 0; r < R; ++r) mm = fmaxf(mm, __ldcg(mine + slot(r) * (kAttnHeadDim + 2) + kAttnHeadDim));
+    for (int r = 0; r < R; ++r)
+        mm = fmaxf(mm, wait_word_sys(mine + slot(r) + kAttnHeadDim, p.p2p_epoch, p.wait_ns, &ok));
     float lsum = 0.f, osum = 0.f;
-    for (int r = 0; r < R; ++r) {
-        const float *part = mine + slot(r) * (kAttnHeadDim + 2);
-        const float mr = __ldcg(part + kAttnHeadDim);
+    for (int r = 0; r < R && ok; ++r) {
+        const float mr = wait_word_sys(mine + slot(r) + kAttnHeadDim, p.p2p_epoch, p.wait_ns, &ok);
+        const float lr = wait_word_sys(mine + slot(r) + kAttnHeadDim + 1, p.p2p_epoch, p.wait_ns, &ok);
+        const float orr = wait_word_sys(mine + slot(r) + d, p.p2p_epoch, p.wait_ns, &ok);
         if (mr == -INFINITY) continue;  // a shard without visible rows
         const float w = expf(mr - mm);
-        lsum += w * __ldcg(part + kAttnHeadDim + 1);
-        osum += w * __ldcg(part + d);
+        lsum += w * lr;
+        osum += w * orr;
     }
+    if (!ok) set_error(p.err, kDevErrTimeout);  // the output is then undefined
     const float gate = p.q_and_gate[(size_t(b) * H + h) * 2 * kAttnHeadDim + kAttnHeadDim + d];
     p.attention[(size_t(b) * H + h) * kAttnHeadDim + d] = (osum / lsum) * sigmoidf_ref(gate);
 }
@@ -1141,8 +1134,7 @@ DecodeSplitPlan plan_attn_decode(int batch, int kv_heads, int max_position, int 
 }
 
 size_t attn_p2p_exchange_bytes(int nranks, int batch, int heads) {
-    return p2p_partial_floats(nranks, batch, heads) * sizeof(float) +
-           size_t(2) * nranks * batch * heads * sizeof(uint32_t);
+    return p2p_words(nranks, batch, heads) * sizeof(unsigned long long);
 }
 
 cudaError_t launch_attn_merge_shards(const float *partials, int nparts, int batch, int heads,
