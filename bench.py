@@ -301,11 +301,66 @@ def run_projection(args, ctx, q38attn, synth, torch, rank: int) -> dict:
                             "path": ("tcgen05 kind::i8 (K-quants), f32 GEMV (Q8_0 gates)" if B >= 9
                                      else "dp4a integer GEMV (K-quants), f32 GEMV (Q8_0 gates)")}
         del graph
+    out["weight_bytes_per_layer"] = per_layer
+    out["layer_decode"] = run_layer_decode(args, ctx, synth, torch, layers, rank)
     for d in layers:
         for w in d.values():
             w.close()
-    out["weight_bytes_per_layer"] = per_layer
     return out
+
+
+def run_layer_decode(args, ctx, synth, torch, layers, rank: int) -> dict:
+    """linear_attention (src/model/ops.rs:744-803) through the layer-level call
+    q38_linear_attention_decode -- the four input projections, the DeltaNet
+    core on the resident state, the output projection -- for the projection
+    leg's distinct layers (DeltaNet layers 0, 1, 2, 4, 5, ...), one CUDA graph,
+    at batch 1 and at the decode batch: ms per layer."""
+    import q38attn
+    g = synth.rng(args.seed + 11 + rank)
+    idx = [l for l in range(64) if not q38attn.is_full_attention(l)][:len(layers)]
+    for l in idx:
+        wl = synth.linear_weights(g)
+        ctx.bind_linear_layer(l, wl["conv1d"], wl["dt_bias"], wl["ssm_a"], wl["ssm_norm"])
+    res = {}
+    for B in sorted({1, args.batch}):
+        st = ctx.state(B, 16, full_slots=0, linear_slots=q38attn.recurrent_index(idx[-1]) + 1)
+        for l in idx:
+            cview, dview = st.linear_views(l)
+            cview.normal_()
+            dview.normal_(0.0, 0.02)
+        del cview, dview
+        ctx.reserve_projection(B, 6144)
+        norm = torch.randn(B, 5120, device="cuda")
+        branch = torch.empty(B, 5120, device="cuda")
+
+        def step():
+            for l, d in zip(idx, layers):
+                ctx.linear_attention_decode(st, l, d, norm, branch)
+
+        step()
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side), torch.cuda.graph(graph, stream=side):
+            step()
+        torch.cuda.current_stream().wait_stream(side)
+        for _ in range(3):
+            graph.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        iters = 10
+        e0.record()
+        for _ in range(iters):
+            graph.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        if st.errors():
+            raise RuntimeError("device error bits set during the layer-decode leg")
+        res[f"batch{B}"] = {"ms_per_layer": e0.elapsed_time(e1) / iters / len(idx)}
+        del graph
+        st.close()
+    return res
 
 
 def run_split_sequence(args, ctx, q38attn, torch, dist, rank: int, world: int,

@@ -15,6 +15,10 @@
 //                           (ops.rs:735-740). Its state loads are issued before
 //                           it waits on D1, so they overlap D1's tail.
 //
+// In the layer-level decode call the projections' epilogues apply the conv,
+// SiLU and gates (proj_epilogue), so D1 is not launched and D2 L2-normalises
+// q and k in its prologue.
+//
 // HBM layout (reference layouts): conv state [batch][qkv_dim][3], delta state
 // [batch][v_heads][128 columns][128], f32.
 #include "q38_common.cuh"
@@ -77,6 +81,7 @@ struct StateParams {
     const float *ssm_norm;
     float *attention;
     int qk_heads, v_heads, qkv_dim;
+    int l2_prologue;  // q and k arrive convolved but not yet L2-normalised
     float eps;
 };
 
@@ -99,8 +104,22 @@ __global__ void __launch_bounds__(kStateThreads) linear_decode_state_kernel(Stat
     const int kh = hv % p.qk_heads;  // ops.rs:699
     const int qk_dim = p.qk_heads * kLinHeadDim;
     const float *row = p.qkv + size_t(b) * p.qkv_dim;
-    const float4 q = reinterpret_cast<const float4 *>(row + kh * kLinHeadDim)[lane];
-    const float4 k = reinterpret_cast<const float4 *>(row + qk_dim + kh * kLinHeadDim)[lane];
+    float4 q = reinterpret_cast<const float4 *>(row + kh * kLinHeadDim)[lane];
+    float4 k = reinterpret_cast<const float4 *>(row + qk_dim + kh * kLinHeadDim)[lane];
+    if (p.l2_prologue) {
+        // l2norm (ops.rs:562-571) of the key head's q and k, here rather than
+        // in D1 (the layer-level call's projections already applied the conv,
+        // SiLU and gates): every warp holds both heads whole, four values per
+        // lane, and sums their squares in f64.
+        const double sq = warp_sum_f64(double(q.x) * q.x + double(q.y) * q.y + double(q.z) * q.z +
+                                       double(q.w) * q.w);
+        const double sk = warp_sum_f64(double(k.x) * k.x + double(k.y) * k.y + double(k.z) * k.z +
+                                       double(k.w) * k.w);
+        const float cq = 1.0f / fmaxf(sqrtf(float(sq)), p.eps);
+        const float ck = 1.0f / fmaxf(sqrtf(float(sk)), p.eps);
+        q.x *= cq, q.y *= cq, q.z *= cq, q.w *= cq;
+        k.x *= ck, k.y *= ck, k.z *= ck, k.w *= ck;
+    }
     const float vmine = lane < kColsPerWarp ? row[2 * qk_dim + hv * kLinHeadDim + col0 + lane] : 0.f;
     const float beta = p.beta[size_t(b) * p.v_heads + hv];
     const float decay = expf(p.alpha[size_t(b) * p.v_heads + hv]);
@@ -146,18 +165,24 @@ __global__ void __launch_bounds__(kStateThreads) linear_decode_state_kernel(Stat
 
 cudaError_t launch_linear_decode(const LinearDecodeLaunch &a, cudaStream_t stream, cudaEvent_t prep_done) {
     const int qkv_dim = (2 * a.qk_heads + a.v_heads) * kLinHeadDim;
-    PrepParams pp{a.qkv,    a.beta,    a.alpha,     a.conv_state, a.conv_w, a.dt_bias,
-                  a.ssm_a,  a.qk_heads, a.v_heads,  qkv_dim,      a.eps};
-    linear_decode_prep_kernel<<<dim3(2 * a.qk_heads + a.v_heads, a.batch), kPrepThreads, 0,
-                                stream>>>(pp);
-    cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess) return e;
+    cudaError_t e = cudaSuccess;
+    if (!a.prepped) {
+        PrepParams pp{a.qkv,    a.beta,    a.alpha,     a.conv_state, a.conv_w, a.dt_bias,
+                      a.ssm_a,  a.qk_heads, a.v_heads,  qkv_dim,      a.eps};
+        linear_decode_prep_kernel<<<dim3(2 * a.qk_heads + a.v_heads, a.batch), kPrepThreads, 0,
+                                    stream>>>(pp);
+        if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    }
     // With prep_done recorded between the two kernels, D2 is an ordinary
     // launch (no programmatic overlap across the record).
     if (prep_done && (e = cudaEventRecord(prep_done, stream)) != cudaSuccess) return e;
 
+    // Prepped inputs (conv, SiLU and gates applied by the projections): the
+    // state kernel normalises q and k itself and follows the last projection
+    // as its programmatic dependent.
     StateParams sp{a.qkv,      a.z,        a.beta,    a.alpha,   a.delta_state,
-                   a.ssm_norm, a.attention, a.qk_heads, a.v_heads, qkv_dim, a.eps};
+                   a.ssm_norm, a.attention, a.qk_heads, a.v_heads, qkv_dim,
+                   a.prepped ? 1 : 0,       a.eps};
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;

@@ -575,6 +575,7 @@ struct ProjQ8KParams {
     float *out;            // out[t * out_ld + row]
     int *err;
     long out_ld;
+    ProjEpilogue epi;      // applied to every output before it is stored
     int rows, nblk, rb, batch, ntiles, stages;
     int tile_rows;         // 16, or 8 for wide rows (a tile is one contiguous byte range)
     uint32_t tile_bytes;   // tile_rows * rb (a multiple of 16: rb is even)
@@ -747,7 +748,7 @@ __global__ void __launch_bounds__(32 * (W + 1), 1) proj_q8k_kernel(ProjQ8KParams
                     }
                     vt[lane] = v;
                     __syncwarp();
-                    if (lane == 0) p.out[row] = ordered_sum32(vt, p.nblk);
+                    if (lane == 0) p.out[row] = proj_epilogue(p.epi, p.rows, 0, row, ordered_sum32(vt, p.nblk));
                 } else {
                     if (lane < p.nblk) {
                         typename BlockOf<T>::type blk;
@@ -759,7 +760,7 @@ __global__ void __launch_bounds__(32 * (W + 1), 1) proj_q8k_kernel(ProjQ8KParams
                         float total = 0.f;
 #pragma unroll 8
                         for (int i = 0; i < nterms; ++i) total = __fadd_rn(total, vt[i]);
-                        p.out[row] = total;
+                        p.out[row] = proj_epilogue(p.epi, p.rows, 0, row, total);
                     }
                 }
                 __syncwarp();
@@ -779,7 +780,7 @@ __global__ void __launch_bounds__(32 * (W + 1), 1) proj_q8k_kernel(ProjQ8KParams
                     float total = 0.f;
 #pragma unroll 8
                     for (int i = 0; i < nterms; ++i) total = __fadd_rn(total, v[i]);
-                    p.out[size_t(lane) * p.out_ld + row] = total;
+                    p.out[size_t(lane) * p.out_ld + row] = proj_epilogue(p.epi, p.rows, lane, row, total);
                 }
                 __syncwarp();
             }
@@ -796,6 +797,7 @@ struct ProjF32Params {
     const float *x;  // [batch][width]
     float *out;
     long out_ld;
+    ProjEpilogue epi;  // applied to every output before it is stored
     int rows, width, rb, batch;
     int per;         // tokens per CTA (grid.y covers the batch)
     int split;       // warps per row: 1 (eight rows per CTA) or 8 (one row per CTA)
@@ -884,7 +886,8 @@ __global__ void __launch_bounds__(256) proj_f32_kernel(ProjF32Params p) {
     }
     if (p.split == 1) {
         if (lane == 0 && row < p.rows)
-            for (int t = 0; t < nt; ++t) outg[size_t(t) * p.out_ld + row] = acc[t];
+            for (int t = 0; t < nt; ++t)
+                outg[size_t(t) * p.out_ld + row] = proj_epilogue(p.epi, p.rows, t0 + t, row, acc[t]);
         return;
     }
     if (lane == 0)
@@ -894,7 +897,7 @@ __global__ void __launch_bounds__(256) proj_f32_kernel(ProjF32Params p) {
     if (threadIdx.x < nt && row < p.rows) {
         float v = 0.f;
         for (int k = 0; k < 8; ++k) v += part[k][threadIdx.x];
-        outg[size_t(threadIdx.x) * p.out_ld + row] = v;
+        outg[size_t(threadIdx.x) * p.out_ld + row] = proj_epilogue(p.epi, p.rows, t0 + int(threadIdx.x), row, v);
     }
 }
 
@@ -1008,7 +1011,8 @@ cudaError_t launch_q8k_quantize(const float *x, int batch, int width, Q8KActivat
 }
 
 cudaError_t launch_proj_q8k(const ProjWeight &w, const float *x, int batch, float *out,
-                            long out_ld, int *err, int sm_count, cudaStream_t stream) {
+                            long out_ld, int *err, int sm_count, cudaStream_t stream,
+                            const ProjEpilogue &epi) {
     const int nblk = int(w.width / 256);
     const int rb = int(w.row_bytes);
     ProjQ8KParams p{};
@@ -1041,6 +1045,8 @@ cudaError_t launch_proj_q8k(const ProjWeight &w, const float *x, int batch, floa
         p.batch = std::min(per, batch - t0);
         p.x = x + size_t(t0) * nblk * 256;
         p.out = out + size_t(t0) * out_ld;
+        p.epi = epi;
+        p.epi.tok0 = epi.tok0 + t0;
         // Stages: as many as the budget allows, up to 4.
         // One token over rows of up to 32 blocks: the 16-warp form.
         const bool one = p.batch == 1 && nblk <= 32;
@@ -1089,8 +1095,9 @@ cudaError_t launch_proj_q8k(const ProjWeight &w, const float *x, int batch, floa
 }
 
 cudaError_t launch_proj_f32(const ProjWeight &w, const float *x, int batch, float *out,
-                            long out_ld, cudaStream_t stream) {
+                            long out_ld, cudaStream_t stream, const ProjEpilogue &epi) {
     ProjF32Params p{};
+    p.epi = epi;
     p.w = static_cast<const uint8_t *>(w.data);
     p.out_ld = out_ld;
     p.rows = int(w.rows);

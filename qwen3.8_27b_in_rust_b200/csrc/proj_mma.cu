@@ -243,6 +243,7 @@ struct MmaParams {
     float *out;            // out[t * out_ld + row]
     int *err;
     long out_ld;
+    ProjEpilogue epi;      // applied to every output before it is stored
     int rows, nblk, batch, stages, abufs;
     uint32_t raw_bytes;    // kMmaRows * block bytes
 };
@@ -470,7 +471,9 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
 #pragma unroll
             for (int t = 0; t < kGroupTok; ++t) {
                 const int tok = tok0 + kGroupTok * g + t;
-                if (tok < p.batch) p.out[size_t(tok) * p.out_ld + row0 + r] = total[t];
+                if (tok < p.batch)
+                    p.out[size_t(tok) * p.out_ld + row0 + r] =
+                        proj_epilogue(p.epi, p.rows, tok, int(row0 + r), total[t]);
             }
         }
     }
@@ -563,7 +566,7 @@ size_t proj_mma_scratch_bytes(int batch, int64_t width) {
 }
 
 cudaError_t launch_proj_mma(const ProjWeight &w, const float *x, int batch, float *out, long out_ld,
-                            int *err, void *scratch, cudaStream_t stream) {
+                            int *err, void *scratch, cudaStream_t stream, const ProjEpilogue &epi) {
     if (!proj_mma_supported(w.type) || w.width % 256 || w.row_bytes % 16) return cudaErrorInvalidValue;
     const int nblk = int(w.width / 256);
     const size_t nb = size_t(batch) * nblk;
@@ -584,6 +587,7 @@ cudaError_t launch_proj_mma(const ProjWeight &w, const float *x, int batch, floa
     p.out = out;
     p.err = err;
     p.out_ld = out_ld;
+    p.epi = epi;
     p.rows = int(w.rows);
     p.nblk = nblk;
     p.batch = batch;

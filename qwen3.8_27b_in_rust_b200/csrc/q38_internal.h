@@ -121,6 +121,15 @@ inline int recurrent_index(int layer) { return layer - (layer + 1) / 4; }
 // Sets the calling thread's q38_last_error() message (q38attn.cu).
 void record_error(const char *msg);
 
+// The layer-level DeltaNet decode (q38proj.cu): the core on projection
+// outputs whose conv + SiLU and gates were applied by the projections'
+// epilogues; and the layer's conv state / weights those epilogues need.
+int linear_decode_prepped(q38_ctx *ctx, q38_state *st, int layer, int batch, float *qkv,
+                          const float *z, float *beta, float *alpha, float *attention,
+                          cudaStream_t stream);
+int linear_layer_prologue_args(q38_ctx *ctx, q38_state *st, int layer, float **conv_state,
+                               const float **conv_w, const float **dt_bias, const float **ssm_a);
+
 // NCCL, resolved at run time (q38_nccl.cu). Both return a Q38 status and
 // record the reason.
 int nccl_comm_ranks(void *comm, int *nranks);
@@ -207,6 +216,7 @@ struct LinearDecodeLaunch {
     const float *conv_w, *dt_bias, *ssm_a, *ssm_norm;
     int batch, qk_heads, v_heads;
     float eps;
+    int prepped = 0;  // conv + SiLU and gates already applied (layer-level call)
 };
 // prep_done (optional) is recorded once the prep kernel is done.
 cudaError_t launch_linear_decode(const LinearDecodeLaunch &a, cudaStream_t stream,

@@ -2,9 +2,51 @@
 // part of the public ABI.
 #pragma once
 
-#include "q38_internal.h"
+#include "q38_common.cuh"
 
 namespace q38 {
+
+// What a projection does to each output before storing it: nothing, or the
+// prologue of the DeltaNet core fused onto the projection's epilogue (the
+// layer-level decode call, where the projection outputs are internal):
+//   kEpiConvSilu   the qkv projection: kernel-4 causal conv of channel `row`
+//                  with the sequence's carried state, multiply then add
+//                  (ops.rs:665-676), state shifted in place, then SiLU
+//                  (ops.rs:677);
+//   kEpiSigmoid    the beta projection: sigmoid (ops.rs:685-686);
+//   kEpiGateAlpha  the alpha projection: ssm_a * softplus(x + dt_bias)
+//                  (ops.rs:687-688).
+// Token t of a decode batch is sequence t.
+constexpr int kEpiNone = 0, kEpiConvSilu = 1, kEpiSigmoid = 2, kEpiGateAlpha = 3;
+struct ProjEpilogue {
+    int kind = kEpiNone;
+    float *conv_state = nullptr;    // kEpiConvSilu: [batch][rows][3]
+    const float *conv_w = nullptr;  // kEpiConvSilu: [rows][4]
+    const float *dt_bias = nullptr, *ssm_a = nullptr;  // kEpiGateAlpha: [rows]
+    int tok0 = 0;                   // the launch's first token in the batch
+};
+
+__device__ __forceinline__ float proj_epilogue(const ProjEpilogue &e, int rows, int t, int row,
+                                               float x) {
+    switch (e.kind) {
+        case kEpiConvSilu: {
+            float *s = e.conv_state + (size_t(e.tok0 + t) * rows + row) * 3;
+            const float4 w = reinterpret_cast<const float4 *>(e.conv_w)[row];
+            const float s0 = s[0], s1 = s[1], s2 = s[2];
+            float v = s0 * w.x;
+            v += s1 * w.y;
+            v += s2 * w.z;
+            v += x * w.w;
+            s[0] = s1;
+            s[1] = s2;
+            s[2] = x;
+            return siluf_ref(v);
+        }
+        case kEpiSigmoid: return sigmoidf_ref(x);
+        case kEpiGateAlpha: return e.ssm_a[row] * softplusf_ref(x + e.dt_bias[row]);
+        default: return x;
+    }
+}
 
 constexpr int kProjMaxTok = 8;          // tokens per integer-path launch (more: repeated launches)
 constexpr int kProjMaxTileRows = 16;    // rows per weight tile at most
@@ -40,7 +82,8 @@ cudaError_t launch_q8k_quantize(const float *x, int batch, int width, Q8KActivat
                                 cudaStream_t stream);
 // Quantizes x [batch][width] to Q8_K inside the kernel (no separate pass).
 cudaError_t launch_proj_q8k(const ProjWeight &w, const float *x, int batch, float *out,
-                            long out_ld, int *err, int sm_count, cudaStream_t stream);
+                            long out_ld, int *err, int sm_count, cudaStream_t stream,
+                            const ProjEpilogue &epi = {});
 // Tensor-core path for Q4_K / Q5_K weights and kProjMmaMinBatch+ tokens
 // (proj_mma.cu): quantizes x into `scratch` (proj_mma_scratch_bytes), then
 // one tcgen05 kind::i8 GEMM, bit-identical to the integer GEMV.
@@ -48,10 +91,11 @@ constexpr int kProjMmaMinBatch = 9;
 bool proj_mma_supported(int type);
 size_t proj_mma_scratch_bytes(int batch, int64_t width);
 cudaError_t launch_proj_mma(const ProjWeight &w, const float *x, int batch, float *out, long out_ld,
-                            int *err, void *scratch, cudaStream_t stream);
+                            int *err, void *scratch, cudaStream_t stream,
+                            const ProjEpilogue &epi = {});
 
 cudaError_t launch_proj_f32(const ProjWeight &w, const float *x, int batch, float *out, long out_ld,
-                            cudaStream_t stream);
+                            cudaStream_t stream, const ProjEpilogue &epi = {});
 
 }  // namespace q38
 

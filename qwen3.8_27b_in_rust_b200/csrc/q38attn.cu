@@ -319,6 +319,35 @@ int prepare_linear_decode(q38_ctx *ctx, q38_state *st, int layer, int batch, flo
 
 void q38::record_error(const char *msg) { g_last_error = msg ? msg : ""; }
 
+int q38::linear_decode_prepped(q38_ctx *ctx, q38_state *st, int layer, int batch, float *qkv,
+                               const float *z, float *beta, float *alpha, float *attention,
+                               cudaStream_t stream) {
+    q38::LinearDecodeLaunch a;
+    if (int rc = prepare_linear_decode(ctx, st, layer, batch, qkv, z, beta, alpha, attention, &a))
+        return rc;
+    a.prepped = 1;
+    DeviceGuard guard(ctx->device);
+    cudaError_t e = q38::launch_linear_decode(a, stream);
+    if (e != cudaSuccess) return cuda_fail(e, "DeltaNet decode launch");
+    return Q38_OK;
+}
+
+int q38::linear_layer_prologue_args(q38_ctx *ctx, q38_state *st, int layer, float **conv_state,
+                                    const float **conv_w, const float **dt_bias,
+                                    const float **ssm_a) {
+    if (int rc = check_state(ctx, st)) return rc;
+    int slot;
+    if (int rc = linear_slot_of(st, layer, &slot)) return rc;
+    auto it = ctx->linear.find(layer);
+    if (it == ctx->linear.end())
+        return fail(Q38_ERR_ARG, "DeltaNet layer %d has no bound weights", layer);
+    *conv_state = st->conv_state + size_t(slot) * st->batch * conv_seq_floats(ctx);
+    *conv_w = it->second.conv_w;
+    *dt_bias = it->second.dt_bias;
+    *ssm_a = it->second.ssm_a;
+    return Q38_OK;
+}
+
 extern "C" {
 
 void q38_geom_default(q38_geom *g) {

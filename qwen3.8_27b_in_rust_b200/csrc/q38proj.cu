@@ -67,17 +67,18 @@ int reserve_scratch(q38_ctx *ctx, int batch, int64_t width) {
 // context's scratch first); otherwise the integer GEMV quantizes the input
 // inside its prologue.
 int project_device(q38_ctx *ctx, const q38_weight *w, int batch, const float *input, float *out,
-                   int *err, cudaStream_t s) {
+                   int *err, cudaStream_t s, const q38::ProjEpilogue &epi = {}) {
     if (reinterpret_cast<uintptr_t>(input) % 16)
         return proj_fail(Q38_ERR_ARG, "projection input must be 16-byte aligned");
     cudaError_t e;
     if (batch >= q38::kProjMmaMinBatch && q38::proj_mma_supported(w->w.type) && w->w.row_bytes % 16 == 0) {
         if (int rc = reserve_scratch(ctx, batch, w->w.width)) return rc;
-        e = q38::launch_proj_mma(w->w, input, batch, out, long(w->w.rows), err, ctx->proj_scratch, s);
+        e = q38::launch_proj_mma(w->w, input, batch, out, long(w->w.rows), err, ctx->proj_scratch, s,
+                                 epi);
     } else if (q38::proj_is_q8k_type(w->w.type))
-        e = q38::launch_proj_q8k(w->w, input, batch, out, long(w->w.rows), err, ctx->sm_count, s);
+        e = q38::launch_proj_q8k(w->w, input, batch, out, long(w->w.rows), err, ctx->sm_count, s, epi);
     else
-        e = q38::launch_proj_f32(w->w, input, batch, out, long(w->w.rows), s);
+        e = q38::launch_proj_f32(w->w, input, batch, out, long(w->w.rows), s, epi);
     if (e != cudaSuccess) return proj_cuda_fail(e, "projection launch");
     return Q38_OK;
 }
@@ -234,11 +235,33 @@ int q38_linear_attention_decode(q38_ctx *ctx, q38_state *st, int layer, int batc
     float *att = alpha + size_t(batch) * vh;
     // linear_attention, ops.rs:761-801: the four input projections (each
     // quantizes the normalised input itself), the core, the output projection.
+    // The core's prologue is fused onto the projections' epilogues: the qkv
+    // projection applies the conv (with the layer's carried state) and SiLU
+    // to each channel it produces, the beta / alpha projections the gates,
+    // and the state kernel L2-normalises q and k itself -- no separate prep
+    // kernel. The results equal q38_linear_decode's (the same operations on
+    // the same values; only the f64 sum of the L2 norm is added in another
+    // order).
+    q38::ProjEpilogue conv, gbeta, galpha;
+    const float *conv_w = nullptr, *dt_bias = nullptr, *ssm_a = nullptr;
+    if (int rc = q38::linear_layer_prologue_args(ctx, st, layer, &conv.conv_state, &conv_w, &dt_bias,
+                                                 &ssm_a))
+        return rc;
+    conv.kind = q38::kEpiConvSilu;
+    conv.conv_w = conv_w;
+    gbeta.kind = q38::kEpiSigmoid;
+    galpha.kind = q38::kEpiGateAlpha;
+    galpha.dt_bias = dt_bias;
+    galpha.ssm_a = ssm_a;
     const q38_weight *ins[4] = {w->qkv, w->z, w->beta, w->alpha};
     float *outs[4] = {qkv, z, beta, alpha};
+    const q38::ProjEpilogue *epis[4] = {&conv, nullptr, &gbeta, &galpha};
     for (int i = 0; i < 4; ++i)
-        if (int rc = project_device(ctx, ins[i], batch, norm, outs[i], st->d_err, s)) return rc;
-    if (int rc = q38_linear_decode(ctx, st, layer, batch, qkv, z, beta, alpha, att, stream)) return rc;
+        if (int rc = project_device(ctx, ins[i], batch, norm, outs[i], st->d_err, s,
+                                    epis[i] ? *epis[i] : q38::ProjEpilogue{}))
+            return rc;
+    if (int rc = q38::linear_decode_prepped(ctx, st, layer, batch, qkv, z, beta, alpha, att, s))
+        return rc;
     return project_device(ctx, w->out, batch, att, branch, st->d_err, s);
 }
 
