@@ -43,6 +43,8 @@
 
 #include <cudaTypedefs.h>
 
+#include <algorithm>
+
 namespace q38 {
 namespace {
 
@@ -746,6 +748,7 @@ struct StateTcParams {
     float *o_out;         // [nseq][count][v_heads*128]
     int *err;
     int seq0, count, nchunk, qk_heads, v_heads, v_head0;
+    int s_off;  // the launch's first sequence within the call
 };
 
 struct __align__(8) StateTcBarriers {
@@ -789,7 +792,7 @@ __global__ void __launch_bounds__(kThreadsLS, 1)
     __shared__ volatile int abort_flag;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int h = p.v_head0 + int(blockIdx.x), s = blockIdx.y;
+    const int h = p.v_head0 + int(blockIdx.x), s = p.s_off + int(blockIdx.y);
     auto plane = [&](int c) { return (s * p.nchunk + c) * p.v_heads + h; };
 
     if (threadIdx.x == 0) {
@@ -1116,10 +1119,11 @@ struct OutParams {
     float *attention;  // in: O; out: normalised, gated
     int count, v_heads, v_head0, v_head_count;
     float eps;
+    int s_off;         // the launch's first sequence within the call
 };
 
 __global__ void __launch_bounds__(256) linear_prefill_out_kernel(OutParams p) {
-    const int t = blockIdx.x, s = blockIdx.y;
+    const int t = blockIdx.x, s = p.s_off + int(blockIdx.y);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const size_t base = (size_t(s) * p.count + t) * size_t(p.v_heads) * kD;
     for (int h = p.v_head0 + warp; h < p.v_head0 + p.v_head_count; h += 8) {
@@ -1200,19 +1204,44 @@ cudaError_t launch_linear_prefill(const LinearPrefillLaunch &a, cudaStream_t str
         !make_map_bf16_ls(&mk, k2, kD, kC, 2 * per, kC))
         return cudaErrorInvalidValue;
     StateTcParams sp{ut, eg, a.delta_state, a.attention, a.err, a.seq0, a.count, nchunk,
-                     a.qk_heads, a.v_heads, a.v_head0};
+                     a.qk_heads, a.v_heads, a.v_head0, 0};
     if ((e = cudaFuncSetAttribute(linear_prefill_state_kernel,
                                   cudaFuncAttributeMaxDynamicSharedMemorySize, int(kSmemLS))) !=
         cudaSuccess)
         return e;
-    linear_prefill_state_kernel<<<dim3(a.v_head_count, a.nseq), kThreadsLS, kSmemLS, stream>>>(
-        mw, mq, mp, mk, sp);
-    if ((e = cudaGetLastError()) != cudaSuccess) return e;
-
     OutParams op{a.z, a.ssm_norm, a.attention, a.count, a.v_heads, a.v_head0, a.v_head_count,
-                 a.eps};
-    linear_prefill_out_kernel<<<dim3(a.count, a.nseq), 256, 0, stream>>>(op);
-    return cudaGetLastError();
+                 a.eps, 0};
+    // The state pass has one CTA per (value head, sequence) and needs a whole
+    // SM each, so a large call runs in more than one wave; the output pass of
+    // a sequence only needs that sequence's state pass. With side streams,
+    // groups of sequences get their own state + output passes (launched in
+    // sequence order, so the first groups fill the first wave), and a
+    // group's output pass runs on the SMs the last wave leaves idle.
+    const int groups = (a.nside > 1 && a.side && a.join && a.fork) ? std::min(a.nside, a.nseq) : 1;
+    if (groups <= 1) {
+        linear_prefill_state_kernel<<<dim3(a.v_head_count, a.nseq), kThreadsLS, kSmemLS, stream>>>(
+            mw, mq, mp, mk, sp);
+        if ((e = cudaGetLastError()) != cudaSuccess) return e;
+        linear_prefill_out_kernel<<<dim3(a.count, a.nseq), 256, 0, stream>>>(op);
+        return cudaGetLastError();
+    }
+    if ((e = cudaEventRecord(a.fork, stream)) != cudaSuccess) return e;
+    for (int g = 0; g < groups; ++g) {
+        const int s0 = a.nseq * g / groups, s1 = a.nseq * (g + 1) / groups;
+        cudaStream_t side = a.side[g];
+        if ((e = cudaStreamWaitEvent(side, a.fork, 0)) != cudaSuccess) return e;
+        sp.s_off = s0;
+        op.s_off = s0;
+        linear_prefill_state_kernel<<<dim3(a.v_head_count, s1 - s0), kThreadsLS, kSmemLS, side>>>(
+            mw, mq, mp, mk, sp);
+        if ((e = cudaGetLastError()) != cudaSuccess) return e;
+        linear_prefill_out_kernel<<<dim3(a.count, s1 - s0), 256, 0, side>>>(op);
+        if ((e = cudaGetLastError()) != cudaSuccess) return e;
+        if ((e = cudaEventRecord(a.join[g], side)) != cudaSuccess) return e;
+    }
+    for (int g = 0; g < groups; ++g)
+        if ((e = cudaStreamWaitEvent(stream, a.join[g], 0)) != cudaSuccess) return e;
+    return cudaSuccess;
 }
 
 }  // namespace q38

@@ -107,6 +107,11 @@ struct q38_state {
     std::vector<void *> p2p_opened;   // peers' buffers opened with cudaIpcOpenMemHandle
     float **p2p_peers_dev = nullptr;  // device array [nranks] of the buffers' addresses
     uint32_t p2p_epoch = 0;           // calls made so far (the next call's epoch is +1)
+    // DeltaNet prefill side streams and their fork / join events (created by
+    // q38_state_reserve_prefill when the state has DeltaNet slots).
+    static constexpr int kPrefillSides = 4;
+    cudaStream_t lin_side[kPrefillSides] = {};
+    cudaEvent_t lin_fork = nullptr, lin_join[kPrefillSides] = {};
     // f32-cache prefill: the K rows as f16 for the tensor cores.
     __half *prefill_k16 = nullptr;  // [v16_seqs][kv_heads][context][256]
 };
@@ -203,6 +208,14 @@ struct LinearPrefillLaunch {
     int seq0, nseq, count, qk_heads, v_heads;
     int v_head0, v_head_count;  // the value heads this call covers
     float eps;
+    // Optional side streams (the state's): the state and output passes run
+    // per group of sequences, forked from and joined back into the caller's
+    // stream, so a group's output pass runs while the state pass of later
+    // groups still occupies some SMs.
+    const cudaStream_t *side = nullptr;
+    cudaEvent_t fork = nullptr;
+    const cudaEvent_t *join = nullptr;
+    int nside = 0;
 };
 cudaError_t launch_linear_prefill(const LinearPrefillLaunch &a, cudaStream_t stream);
 size_t linear_prefill_scratch_floats(int nchunk_total, int v_heads);

@@ -201,6 +201,9 @@ def test_linear_attention_decode_matches_oracle(cuda_ctx, oracle_lib, batch):
         assert oracle_lib.linear_core(lw, cs, ds, row[0], row[1], row[2], row[3], out) == 0
         att[b] = out
         gcs, gds = st.download_linear(layer, b)
+        # The conv state is advanced by the qkv projection's epilogue: exactly
+        # the reference's shift.
+        np.testing.assert_array_equal(gcs, cs)
         assert relative_error(gds, ds) < 1e-4
     want = _oracle_project(oracle_lib, host["out"], att)
     assert relative_error(branch.cpu().numpy(), want) < 2e-3
