@@ -734,6 +734,11 @@ __global__ void __launch_bounds__(32 * (W + 1), 1) proj_q8k_kernel(ProjQ8KParams
         for (int r = warp; r < p.tile_rows; r += W) {
             const int row = tile * p.tile_rows + r;
             if (row >= p.rows) break;  // rows ascend with r
+            // The epilogue's inputs for this row, requested now: lane t
+            // finishes token t (lane 0 the single token of the one-token form).
+            const EpilogueIn ein = (p.epi.kind != kEpiNone && lane < p.batch)
+                                       ? proj_epilogue_load(p.epi, p.rows, lane, row)
+                                       : EpilogueIn{};
             if constexpr (W == kProjOneTokenWarps) {
                 // One token, one block per lane: the block terms staged in
                 // the warp's buffer, where lane 0 reads them with vector
@@ -748,7 +753,8 @@ __global__ void __launch_bounds__(32 * (W + 1), 1) proj_q8k_kernel(ProjQ8KParams
                     }
                     vt[lane] = v;
                     __syncwarp();
-                    if (lane == 0) p.out[row] = proj_epilogue(p.epi, p.rows, 0, row, ordered_sum32(vt, p.nblk));
+                    if (lane == 0)
+                        p.out[row] = proj_epilogue_apply(p.epi, ein, p.rows, 0, row, ordered_sum32(vt, p.nblk));
                 } else {
                     if (lane < p.nblk) {
                         typename BlockOf<T>::type blk;
@@ -760,7 +766,7 @@ __global__ void __launch_bounds__(32 * (W + 1), 1) proj_q8k_kernel(ProjQ8KParams
                         float total = 0.f;
 #pragma unroll 8
                         for (int i = 0; i < nterms; ++i) total = __fadd_rn(total, vt[i]);
-                        p.out[row] = proj_epilogue(p.epi, p.rows, 0, row, total);
+                        p.out[row] = proj_epilogue_apply(p.epi, ein, p.rows, 0, row, total);
                     }
                 }
                 __syncwarp();
@@ -780,7 +786,7 @@ __global__ void __launch_bounds__(32 * (W + 1), 1) proj_q8k_kernel(ProjQ8KParams
                     float total = 0.f;
 #pragma unroll 8
                     for (int i = 0; i < nterms; ++i) total = __fadd_rn(total, v[i]);
-                    p.out[size_t(lane) * p.out_ld + row] = proj_epilogue(p.epi, p.rows, lane, row, total);
+                    p.out[size_t(lane) * p.out_ld + row] = proj_epilogue_apply(p.epi, ein, p.rows, lane, row, total);
                 }
                 __syncwarp();
             }

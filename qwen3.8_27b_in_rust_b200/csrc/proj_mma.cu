@@ -468,12 +468,19 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
                 set_error(p.err, kDevErrTimeout);
             }
         } else if (row0 + int(r) < p.rows) {
+            // All tokens' epilogue inputs first, then the outputs.
+            EpilogueIn ein[kGroupTok];
+#pragma unroll
+            for (int t = 0; t < kGroupTok; ++t) {
+                const int tok = tok0 + kGroupTok * g + t;
+                if (tok < p.batch) ein[t] = proj_epilogue_load(p.epi, p.rows, tok, int(row0 + r));
+            }
 #pragma unroll
             for (int t = 0; t < kGroupTok; ++t) {
                 const int tok = tok0 + kGroupTok * g + t;
                 if (tok < p.batch)
                     p.out[size_t(tok) * p.out_ld + row0 + r] =
-                        proj_epilogue(p.epi, p.rows, tok, int(row0 + r), total[t]);
+                        proj_epilogue_apply(p.epi, ein[t], p.rows, tok, int(row0 + r), total[t]);
             }
         }
     }

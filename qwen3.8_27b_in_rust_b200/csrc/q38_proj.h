@@ -26,26 +26,53 @@ struct ProjEpilogue {
     int tok0 = 0;                   // the launch's first token in the batch
 };
 
-__device__ __forceinline__ float proj_epilogue(const ProjEpilogue &e, int rows, int t, int row,
-                                               float x) {
+// The values an epilogue reads for output (t, row), loaded ahead of the
+// output itself so that their latency overlaps the row's dot products.
+struct EpilogueIn {
+    float s0 = 0.f, s1 = 0.f, s2 = 0.f;  // kEpiConvSilu: the carried conv state
+    float4 w = {0.f, 0.f, 0.f, 0.f};     // kEpiConvSilu: the channel's conv weights
+    float a = 0.f, bias = 0.f;           // kEpiGateAlpha: ssm_a, dt_bias
+};
+
+__device__ __forceinline__ EpilogueIn proj_epilogue_load(const ProjEpilogue &e, int rows, int t,
+                                                         int row) {
+    EpilogueIn in;
+    if (e.kind == kEpiConvSilu) {
+        const float *s = e.conv_state + (size_t(e.tok0 + t) * rows + row) * 3;
+        in.s0 = s[0];
+        in.s1 = s[1];
+        in.s2 = s[2];
+        in.w = reinterpret_cast<const float4 *>(e.conv_w)[row];
+    } else if (e.kind == kEpiGateAlpha) {
+        in.a = e.ssm_a[row];
+        in.bias = e.dt_bias[row];
+    }
+    return in;
+}
+
+__device__ __forceinline__ float proj_epilogue_apply(const ProjEpilogue &e, const EpilogueIn &in,
+                                                     int rows, int t, int row, float x) {
     switch (e.kind) {
         case kEpiConvSilu: {
+            float v = in.s0 * in.w.x;
+            v += in.s1 * in.w.y;
+            v += in.s2 * in.w.z;
+            v += x * in.w.w;
             float *s = e.conv_state + (size_t(e.tok0 + t) * rows + row) * 3;
-            const float4 w = reinterpret_cast<const float4 *>(e.conv_w)[row];
-            const float s0 = s[0], s1 = s[1], s2 = s[2];
-            float v = s0 * w.x;
-            v += s1 * w.y;
-            v += s2 * w.z;
-            v += x * w.w;
-            s[0] = s1;
-            s[1] = s2;
+            s[0] = in.s1;
+            s[1] = in.s2;
             s[2] = x;
             return siluf_ref(v);
         }
         case kEpiSigmoid: return sigmoidf_ref(x);
-        case kEpiGateAlpha: return e.ssm_a[row] * softplusf_ref(x + e.dt_bias[row]);
+        case kEpiGateAlpha: return in.a * softplusf_ref(x + in.bias);
         default: return x;
     }
+}
+
+__device__ __forceinline__ float proj_epilogue(const ProjEpilogue &e, int rows, int t, int row,
+                                               float x) {
+    return proj_epilogue_apply(e, proj_epilogue_load(e, rows, t, row), rows, t, row, x);
 }
 
 constexpr int kProjMaxTok = 8;          // tokens per integer-path launch (more: repeated launches)
