@@ -572,18 +572,35 @@ size_t proj_mma_scratch_bytes(int batch, int64_t width) {
     return nb * 256 + nb * 4 + nb * 32;
 }
 
-cudaError_t launch_proj_mma(const ProjWeight &w, const float *x, int batch, float *out, long out_ld,
-                            int *err, void *scratch, cudaStream_t stream, const ProjEpilogue &epi) {
-    if (!proj_mma_supported(w.type) || w.width % 256 || w.row_bytes % 16) return cudaErrorInvalidValue;
-    const int nblk = int(w.width / 256);
-    const size_t nb = size_t(batch) * nblk;
+namespace {
+// The scratch's layout: quants [batch][nblk][256], scales, group sums.
+Q8KActivations mma_activations(void *scratch, int batch, int64_t width) {
+    const size_t nb = size_t(batch) * size_t(width / 256);
     unsigned char *sp = static_cast<unsigned char *>(scratch);
     Q8KActivations act;
     act.quants = reinterpret_cast<int8_t *>(sp);
     act.scale = reinterpret_cast<float *>(sp + nb * 256);
     act.sums = reinterpret_cast<int16_t *>(sp + nb * 256 + nb * 4);
-    cudaError_t e = launch_q8k_quantize(x, batch, int(w.width), act, nullptr, stream);
-    if (e != cudaSuccess) return e;
+    return act;
+}
+}  // namespace
+
+cudaError_t launch_proj_mma_quantize(const float *x, int batch, int64_t width, void *scratch,
+                                     cudaStream_t stream) {
+    if (width % 256) return cudaErrorInvalidValue;
+    return launch_q8k_quantize(x, batch, int(width), mma_activations(scratch, batch, width), nullptr,
+                               stream);
+}
+
+cudaError_t launch_proj_mma(const ProjWeight &w, const float *x, int batch, float *out, long out_ld,
+                            int *err, void *scratch, cudaStream_t stream, const ProjEpilogue &epi,
+                            bool prequantized) {
+    if (!proj_mma_supported(w.type) || w.width % 256 || w.row_bytes % 16) return cudaErrorInvalidValue;
+    const int nblk = int(w.width / 256);
+    const Q8KActivations act = mma_activations(scratch, batch, w.width);
+    cudaError_t e = cudaSuccess;
+    if (!prequantized && (e = launch_q8k_quantize(x, batch, int(w.width), act, nullptr, stream)) != cudaSuccess)
+        return e;
     const uint32_t bb = w.type == Q38_GGML_Q6_K ? kQ6KDeviceBlock : w.type == Q38_GGML_Q4_K ? 144 : 176;
     CUtensorMap mw, ma;
     if (!make_map_u8(&mw, w.data, uint64_t(w.row_bytes), uint64_t(w.rows), bb, kMmaRows, false) ||

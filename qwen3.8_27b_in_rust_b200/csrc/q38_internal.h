@@ -107,11 +107,13 @@ struct q38_state {
     std::vector<void *> p2p_opened;   // peers' buffers opened with cudaIpcOpenMemHandle
     float **p2p_peers_dev = nullptr;  // device array [nranks] of the buffers' addresses
     uint32_t p2p_epoch = 0;           // calls made so far (the next call's epoch is +1)
-    // DeltaNet prefill side streams and their fork / join events (created by
-    // q38_state_reserve_prefill when the state has DeltaNet slots).
-    static constexpr int kPrefillSides = 4;
-    cudaStream_t lin_side[kPrefillSides] = {};
-    cudaEvent_t lin_fork = nullptr, lin_join[kPrefillSides] = {};
+    // Side streams and their fork / join events (created with the state):
+    // the DeltaNet prefill's per-group state passes and the layer-level
+    // decode call's concurrent projections fork onto them and join back into
+    // the caller's stream.
+    static constexpr int kSides = 4;
+    cudaStream_t side[kSides] = {};
+    cudaEvent_t side_fork = nullptr, side_join[kSides] = {};
     // f32-cache prefill: the K rows as f16 for the tensor cores.
     __half *prefill_k16 = nullptr;  // [v16_seqs][kv_heads][context][256]
 };

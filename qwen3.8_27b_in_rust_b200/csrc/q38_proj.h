@@ -117,9 +117,13 @@ cudaError_t launch_proj_q8k(const ProjWeight &w, const float *x, int batch, floa
 constexpr int kProjMmaMinBatch = 9;
 bool proj_mma_supported(int type);
 size_t proj_mma_scratch_bytes(int batch, int64_t width);
+// prequantized: `scratch` already holds x's quantization (an earlier
+// launch_proj_mma or launch_proj_mma_quantize of the same x and width).
 cudaError_t launch_proj_mma(const ProjWeight &w, const float *x, int batch, float *out, long out_ld,
                             int *err, void *scratch, cudaStream_t stream,
-                            const ProjEpilogue &epi = {});
+                            const ProjEpilogue &epi = {}, bool prequantized = false);
+cudaError_t launch_proj_mma_quantize(const float *x, int batch, int64_t width, void *scratch,
+                                     cudaStream_t stream);
 
 cudaError_t launch_proj_f32(const ProjWeight &w, const float *x, int batch, float *out, long out_ld,
                             cudaStream_t stream, const ProjEpilogue &epi = {});

@@ -179,11 +179,11 @@ void free_state(q38_state *st) {
     cudaFree(st->p2p_peers_dev);
     cudaFree(st->prefill_k16);
     if (st->host_err) cudaFreeHost(st->host_err);
-    for (int i = 0; i < q38_state::kPrefillSides; ++i) {
-        if (st->lin_side[i]) cudaStreamDestroy(st->lin_side[i]);
-        if (st->lin_join[i]) cudaEventDestroy(st->lin_join[i]);
+    for (int i = 0; i < q38_state::kSides; ++i) {
+        if (st->side[i]) cudaStreamDestroy(st->side[i]);
+        if (st->side_join[i]) cudaEventDestroy(st->side_join[i]);
     }
-    if (st->lin_fork) cudaEventDestroy(st->lin_fork);
+    if (st->side_fork) cudaEventDestroy(st->side_fork);
     if (st->host_ev_prep) cudaEventDestroy(st->host_ev_prep);
     if (st->host_ev_back) cudaEventDestroy(st->host_ev_back);
     if (st->host_out) cudaStreamDestroy(st->host_out);
@@ -509,6 +509,11 @@ int q38_state_create(q38_ctx *ctx, int batch, int context_length, int full_slots
     if (e == cudaSuccess) e = alloc((void **)&st->stage, st->stage_floats * 4);
     if (e == cudaSuccess) e = alloc((void **)&st->proj_stage, st->stage_floats * 4);
     if (e == cudaSuccess) e = alloc((void **)&st->stage_pos, size_t(batch) * 4);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&st->side_fork, cudaEventDisableTiming);
+    for (int i = 0; i < q38_state::kSides && e == cudaSuccess; ++i) {
+        e = cudaStreamCreateWithFlags(&st->side[i], cudaStreamNonBlocking);
+        if (e == cudaSuccess) e = cudaEventCreateWithFlags(&st->side_join[i], cudaEventDisableTiming);
+    }
     if (e != cudaSuccess) {
         free_state(st);
         delete st;
@@ -1007,13 +1012,6 @@ int q38_state_reserve_prefill(q38_state *st, int max_tokens) {
             q38::linear_prefill_scratch_floats(int(chunks), st->ctx->geom.linear_v_heads);
         Q38_CUDA(cudaMalloc(&st->prefill_lin, floats * sizeof(float)));
         st->prefill_chunks = chunks;
-        if (!st->lin_fork) {
-            Q38_CUDA(cudaEventCreateWithFlags(&st->lin_fork, cudaEventDisableTiming));
-            for (int i = 0; i < q38_state::kPrefillSides; ++i) {
-                Q38_CUDA(cudaStreamCreateWithFlags(&st->lin_side[i], cudaStreamNonBlocking));
-                Q38_CUDA(cudaEventCreateWithFlags(&st->lin_join[i], cudaEventDisableTiming));
-            }
-        }
     }
     // Host-pointer prefill streams the prompt through a staging buffer of at
     // most kHostPieceTokens tokens (but never fewer than one per sequence).
@@ -1139,12 +1137,10 @@ int linear_prefill_impl(q38_ctx *ctx, q38_state *st, int layer, int seq0, int ns
     a.v_head0 = v_head0;
     a.v_head_count = v_head_count;
     a.eps = ctx->geom.rms_eps;
-    if (st->lin_fork) {
-        a.side = st->lin_side;
-        a.fork = st->lin_fork;
-        a.join = st->lin_join;
-        a.nside = q38_state::kPrefillSides;
-    }
+    a.side = st->side;
+    a.fork = st->side_fork;
+    a.join = st->side_join;
+    a.nside = q38_state::kSides;
     DeviceGuard guard(ctx->device);
     cudaError_t e = q38::launch_linear_prefill(a, static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return cuda_fail(e, "DeltaNet prefill launch");

@@ -66,15 +66,23 @@ int reserve_scratch(q38_ctx *ctx, int batch, int64_t width) {
 // over Q4_K / Q5_K runs on the tensor cores (the input quantized into the
 // context's scratch first); otherwise the integer GEMV quantizes the input
 // inside its prologue.
+bool takes_mma(const q38_weight *w, int batch) {
+    return batch >= q38::kProjMmaMinBatch && q38::proj_mma_supported(w->w.type) &&
+           w->w.row_bytes % 16 == 0;
+}
+
+// prequantized: the context's scratch already holds `input` quantized (MMA
+// path only; see the layer call below).
 int project_device(q38_ctx *ctx, const q38_weight *w, int batch, const float *input, float *out,
-                   int *err, cudaStream_t s, const q38::ProjEpilogue &epi = {}) {
+                   int *err, cudaStream_t s, const q38::ProjEpilogue &epi = {},
+                   bool prequantized = false) {
     if (reinterpret_cast<uintptr_t>(input) % 16)
         return proj_fail(Q38_ERR_ARG, "projection input must be 16-byte aligned");
     cudaError_t e;
-    if (batch >= q38::kProjMmaMinBatch && q38::proj_mma_supported(w->w.type) && w->w.row_bytes % 16 == 0) {
+    if (takes_mma(w, batch)) {
         if (int rc = reserve_scratch(ctx, batch, w->w.width)) return rc;
         e = q38::launch_proj_mma(w->w, input, batch, out, long(w->w.rows), err, ctx->proj_scratch, s,
-                                 epi);
+                                 epi, prequantized);
     } else if (q38::proj_is_q8k_type(w->w.type))
         e = q38::launch_proj_q8k(w->w, input, batch, out, long(w->w.rows), err, ctx->sm_count, s, epi);
     else
@@ -256,10 +264,33 @@ int q38_linear_attention_decode(q38_ctx *ctx, q38_state *st, int layer, int batc
     const q38_weight *ins[4] = {w->qkv, w->z, w->beta, w->alpha};
     float *outs[4] = {qkv, z, beta, alpha};
     const q38::ProjEpilogue *epis[4] = {&conv, nullptr, &gbeta, &galpha};
-    for (int i = 0; i < 4; ++i)
-        if (int rc = project_device(ctx, ins[i], batch, norm, outs[i], st->d_err, s,
-                                    epis[i] ? *epis[i] : q38::ProjEpilogue{}))
+    if (takes_mma(w->qkv, batch) && takes_mma(w->z, batch) && !takes_mma(w->beta, batch) &&
+        !takes_mma(w->alpha, batch) && st->side_fork) {
+        // Tensor-core qkv and z over the same quantized input, and the two
+        // small gate projections, run concurrently: each alone leaves most
+        // SMs idle (qkv 80, z 48 and each gate 48 CTAs, every CTA walking all
+        // the row's blocks). The input is quantized once, then qkv runs on
+        // the caller's stream, z on a side stream and the gates on another.
+        if (int rc = reserve_scratch(ctx, batch, hidden)) return rc;
+        cudaError_t e = q38::launch_proj_mma_quantize(norm, batch, hidden, ctx->proj_scratch, s);
+        if (e == cudaSuccess) e = cudaEventRecord(st->side_fork, s);
+        for (int i = 0; i < 2 && e == cudaSuccess; ++i) e = cudaStreamWaitEvent(st->side[i], st->side_fork, 0);
+        if (e != cudaSuccess) return proj_cuda_fail(e, "layer projections fork");
+        if (int rc = project_device(ctx, w->qkv, batch, norm, qkv, st->d_err, s, conv, true)) return rc;
+        if (int rc = project_device(ctx, w->z, batch, norm, z, st->d_err, st->side[0], {}, true)) return rc;
+        if (int rc = project_device(ctx, w->beta, batch, norm, beta, st->d_err, st->side[1], gbeta))
             return rc;
+        if (int rc = project_device(ctx, w->alpha, batch, norm, alpha, st->d_err, st->side[1], galpha))
+            return rc;
+        for (int i = 0; i < 2 && e == cudaSuccess; ++i) e = cudaEventRecord(st->side_join[i], st->side[i]);
+        for (int i = 0; i < 2 && e == cudaSuccess; ++i) e = cudaStreamWaitEvent(s, st->side_join[i], 0);
+        if (e != cudaSuccess) return proj_cuda_fail(e, "layer projections join");
+    } else {
+        for (int i = 0; i < 4; ++i)
+            if (int rc = project_device(ctx, ins[i], batch, norm, outs[i], st->d_err, s,
+                                        epis[i] ? *epis[i] : q38::ProjEpilogue{}))
+                return rc;
+    }
     if (int rc = q38::linear_decode_prepped(ctx, st, layer, batch, qkv, z, beta, alpha, att, s))
         return rc;
     return project_device(ctx, w->out, batch, att, branch, st->d_err, s);
