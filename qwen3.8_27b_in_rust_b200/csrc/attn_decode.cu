@@ -997,6 +997,50 @@ bool make_map_kcache(CUtensorMap *m, const void *base, uint64_t rows, uint64_t p
                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// Encoded tensor maps of recent calls, per host thread: a decode call's maps
+// depend only on the cache's base address and shape, which stay the same
+// from one step to the next, so each is encoded once (keeps the host side of
+// a launch-bound decode step short).
+bool cached_map_kcache(CUtensorMap *m, const void *base, uint64_t rows, uint64_t planes) {
+    struct Entry {
+        const void *base = nullptr;
+        uint64_t rows = 0, planes = 0;
+        CUtensorMap map;
+    };
+    constexpr int kEntries = 8;
+    thread_local Entry cache[kEntries];
+    thread_local int next = 0;
+    for (const Entry &e : cache)
+        if (e.base == base && e.rows == rows && e.planes == planes) {
+            *m = e.map;
+            return true;
+        }
+    if (!make_map_kcache(m, base, rows, planes)) return false;
+    cache[next] = Entry{base, rows, planes, *m};
+    next = (next + 1) % kEntries;
+    return true;
+}
+
+// Largest dynamic shared memory a split launch can ask for (the largest
+// chunk the planner can choose), set as the kernel's limit once per device.
+template <typename KV>
+cudaError_t ensure_split_smem_limit() {
+    constexpr bool kTc = sizeof(KV) == 2;
+    constexpr int kMaxC = kTc ? kMaxChunkTc : kMaxChunk;
+    constexpr size_t kSmemMax = size_t(Tile<KV>::kStages) * kTileBytes + size_t(kMaxC) * 8 * sizeof(float) +
+                                (kTc ? kQRegionBytes + size_t(kMaxC / 64) * 2048 + 1024 : 0) + 1024;
+    static_assert(kSmemMax <= 227 * 1024, "split kernel shared memory");
+    static bool set[128] = {};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 128 && set[dev]) return cudaSuccess;
+    e = cudaFuncSetAttribute(attn_decode_split_kernel<KV>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             int(kSmemMax));
+    if (e == cudaSuccess && dev < 128) set[dev] = true;
+    return e;
+}
+
 template <typename KV>
 cudaError_t launch_typed(const AttnDecodeLaunch &a, int sm_count, cudaStream_t stream) {
     // Rows any sequence of this call attends to in the local cache.
@@ -1026,10 +1070,10 @@ cudaError_t launch_typed(const AttnDecodeLaunch &a, int sm_count, cudaStream_t s
                    a.skip_kv_loads};
     constexpr bool kTc = sizeof(KV) == 2;
     CUtensorMap map_k{}, map_v{};
-    if (kTc && (!make_map_kcache(&map_k, a.kcache, uint64_t(a.context_length),
-                                 uint64_t(a.batch) * a.kv_heads) ||
-                !make_map_kcache(&map_v, a.vcache, uint64_t(a.context_length),
-                                 uint64_t(a.batch) * a.kv_heads)))
+    if (kTc && (!cached_map_kcache(&map_k, a.kcache, uint64_t(a.context_length),
+                                   uint64_t(a.batch) * a.kv_heads) ||
+                !cached_map_kcache(&map_v, a.vcache, uint64_t(a.context_length),
+                                   uint64_t(a.batch) * a.kv_heads)))
         return cudaErrorInvalidValue;
     // bf16: query operand, P operand (2 x 1 KB per 64 keys + 1 KB); all: alignment.
     auto extra_for = [&](int chunk) {
@@ -1037,9 +1081,7 @@ cudaError_t launch_typed(const AttnDecodeLaunch &a, int sm_count, cudaStream_t s
     };
     const size_t smem = size_t(Tile<KV>::kStages) * kTileBytes + size_t(plan.chunk) * 8 * sizeof(float) +
                         extra_for(plan.chunk);
-    e = cudaFuncSetAttribute(attn_decode_split_kernel<KV>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
-    if (e != cudaSuccess) return e;
+    if ((e = ensure_split_smem_limit<KV>()) != cudaSuccess) return e;
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(plan.nsplit, a.kv_heads, a.batch);
     cfg.blockDim = dim3(kThreads);
