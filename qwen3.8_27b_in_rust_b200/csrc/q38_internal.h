@@ -63,6 +63,7 @@ struct q38_state {
     void *kcache = nullptr, *vcache = nullptr;
     float *conv_state = nullptr;    // [linear_slots][batch][qkv_dim][3]
     float *delta_state = nullptr;   // [linear_slots][batch][v_heads][128][128]
+    int *lin_group_count = nullptr; // [linear_slots][batch][qk_heads] (decode sweep)
     float *qprep = nullptr;         // [batch][heads][256]
     float *part_o = nullptr;        // [batch][heads][max_splits][256]
     float *part_ml = nullptr;       // [batch][heads][max_splits][2]
@@ -232,8 +233,13 @@ struct LinearDecodeLaunch {
     int batch, qk_heads, v_heads;
     float eps;
     int prepped = 0;  // conv + SiLU and gates already applied (layer-level call)
+    int *group_count = nullptr;  // this slot: [batch][qk_heads], zero between calls
+    int *err = nullptr;
+    uint64_t wait_ns = 0;        // bounded-wait limit (0: the library's)
+    int sm_count = 0;
 };
-// prep_done (optional) is recorded once the prep kernel is done.
+// prep_done (optional) is recorded once the prep kernel is done; the call then
+// runs as two kernels (prep, state pass) instead of the fused sweep.
 cudaError_t launch_linear_decode(const LinearDecodeLaunch &a, cudaStream_t stream,
                                  cudaEvent_t prep_done = nullptr);
 

@@ -157,6 +157,7 @@ void free_state(q38_state *st) {
     cudaFree(st->vcache);
     cudaFree(st->conv_state);
     cudaFree(st->delta_state);
+    cudaFree(st->lin_group_count);
     cudaFree(st->qprep);
     cudaFree(st->part_o);
     cudaFree(st->part_ml);
@@ -317,6 +318,10 @@ int prepare_linear_decode(q38_ctx *ctx, q38_state *st, int layer, int batch, flo
     a->qk_heads = g.linear_qk_heads;
     a->v_heads = g.linear_v_heads;
     a->eps = g.rms_eps;
+    a->group_count = st->lin_group_count + size_t(slot) * st->batch * g.linear_qk_heads;
+    a->err = st->d_err;
+    a->wait_ns = st->debug_wait_ns;
+    a->sm_count = ctx->sm_count;
     return Q38_OK;
 }
 
@@ -502,6 +507,9 @@ int q38_state_create(q38_ctx *ctx, int batch, int context_length, int full_slots
     if (e == cudaSuccess) e = alloc(&st->vcache, kv_bytes);
     if (e == cudaSuccess) e = alloc((void **)&st->conv_state, conv_floats * 4);
     if (e == cudaSuccess) e = alloc((void **)&st->delta_state, delta_floats * 4);
+    if (e == cudaSuccess)
+        e = alloc((void **)&st->lin_group_count,
+                  size_t(linear_slots) * batch * g.linear_qk_heads * sizeof(int));
     if (e == cudaSuccess) e = alloc((void **)&st->qprep, size_t(batch) * ctx->q_dim * 4);
     if (e == cudaSuccess) e = alloc((void **)&st->part_o, parts * q38::kAttnHeadDim * 4);
     if (e == cudaSuccess) e = alloc((void **)&st->part_ml, parts * 2 * 4);
@@ -546,6 +554,8 @@ int q38_state_reset(q38_state *st, void *stream) {
     if (n) {
         Q38_CUDA(cudaMemsetAsync(st->conv_state, 0, n * conv_seq_floats(st->ctx) * 4, s));
         Q38_CUDA(cudaMemsetAsync(st->delta_state, 0, n * delta_seq_floats(st->ctx) * 4, s));
+        Q38_CUDA(cudaMemsetAsync(st->lin_group_count, 0,
+                                 n * st->ctx->geom.linear_qk_heads * sizeof(int), s));
     }
     return Q38_OK;
 }
@@ -614,6 +624,11 @@ int q38_state_errors(q38_state *st, int *bits) {
     Q38_CUDA(cudaDeviceSynchronize());
     Q38_CUDA(cudaMemcpy(bits, st->d_err, sizeof(int), cudaMemcpyDeviceToHost));
     Q38_CUDA(cudaMemset(st->d_err, 0, sizeof(int)));
+    // A decode sweep that gave up may leave key-head reader counts behind.
+    if (*bits && st->lin_group_count)
+        Q38_CUDA(cudaMemset(st->lin_group_count, 0,
+                            size_t(st->linear_slots) * st->batch * st->ctx->geom.linear_qk_heads *
+                                sizeof(int)));
     return Q38_OK;
 }
 
