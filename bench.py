@@ -263,8 +263,23 @@ def run_projection(args, ctx, q38attn, synth, torch, rank: int) -> dict:
             d[k] = ctx.weight(t, w, r, data)
         layers.append(d)
     per_layer = nbytes / args.proj_layers
+    plane_bytes = None
     out = {}
-    for B in sorted({1, args.batch}):
+    legs = [(1, False)] + ([(args.batch, False), (args.batch, True)] if args.batch >= 9 else
+                           [(args.batch, False)] if args.batch != 1 else [])
+    for B, planes in legs:
+        if planes and plane_bytes is None:
+            # Integer planes for the K-quant weights (q38_weight_build_planes).
+            plane_bytes = 0
+            for d in layers:
+                for k in ("qkv", "z", "out"):
+                    d[k].build_planes()
+                    t, w, r = PROJ_SPEC[k]
+                    rp = (r + 127) // 128 * 128  # rows padded to the 128-row tile
+                    # quant planes (Q4_K / Q5_K) 1 byte per weight, product planes
+                    # (Q6_K) 2, plus a 16-byte record per (row, 256-block)
+                    plane_bytes += (2 if t == 14 else 1) * rp * w + (w // 256) * rp * 16
+            plane_bytes /= args.proj_layers
         ctx.reserve_projection(B, 6144)
         x = torch.randn(B, 5120, device="cuda")
         a = torch.randn(B, 6144, device="cuda")
@@ -297,9 +312,19 @@ def run_projection(args, ctx, q38attn, synth, torch, rank: int) -> dict:
         ms = e0.elapsed_time(e1) / iters / args.proj_layers
         peak, _ = load_peaks()
         gbs = per_layer / (ms * 1e-3) / 1e9
-        out[f"batch{B}"] = {"ms_per_layer": ms, "weight_gbs": gbs, "frac": gbs / peak,
-                            "path": ("tcgen05 kind::i8 (K-quants), f32 GEMV (Q8_0 gates)" if B >= 9
-                                     else "dp4a integer GEMV (K-quants), f32 GEMV (Q8_0 gates)")}
+        leg = {"ms_per_layer": ms, "weight_gbs": gbs, "frac": gbs / peak,
+               "path": ("tcgen05 kind::i8 from integer planes (K-quants), f32 GEMV (Q8_0 gates)" if planes
+                        else "tcgen05 kind::i8, operands built per call (K-quants), f32 GEMV (Q8_0 gates)"
+                        if B >= 9 else "dp4a integer GEMV (K-quants), f32 GEMV (Q8_0 gates)")}
+        if planes:
+            # Bytes the kernels stream: the planes of the K-quant matrices plus
+            # the gates' Q8_0 bytes.
+            streamed = plane_bytes + sum(r * w * 34 / 32 for k, (t, w, r) in PROJ_SPEC.items()
+                                         if k in ("beta", "alpha"))
+            leg["streamed_bytes_per_layer"] = streamed
+            leg["streamed_gbs"] = streamed / (ms * 1e-3) / 1e9
+            leg["streamed_frac"] = leg["streamed_gbs"] / peak
+        out[f"batch{B}" + ("" if planes or B < 9 or args.batch < 9 else "_operands_per_call")] = leg
         del graph
     out["weight_bytes_per_layer"] = per_layer
     out["layer_decode"] = run_layer_decode(args, ctx, synth, torch, layers, rank)

@@ -519,6 +519,19 @@ int q38_weight_info(const q38_weight *w, int *ggml_type, int64_t *width, int64_t
  * tensor_gemv_* require, tensor.rs:1095-1110) of an accepted type. */
 int q38_weight_from_gguf(q38_ctx *ctx, const char *path, const char *name, q38_weight **out);
 
+/* Builds, once, the weight's integer planes for projections of 9 or more
+ * tokens (Q4_K, Q5_K and Q6_K only; Q38_ERR_ARG for other types). Per weight
+ * value the reference's integer product scale * quant is kept as two bytes,
+ * and per (row, 256-block) a 16-byte record of d, dmin and the sub-block
+ * mins: 2 bytes per weight + 1/16 byte, i.e. 3.7x a Q4_K matrix's bytes and
+ * 2.5x a Q6_K one's, in device memory next to the GGUF copy. Every later
+ * projection of 9+ tokens through this weight (q38_project, the layer calls)
+ * then streams the planes into tcgen05 kind::i8 products instead of building
+ * its tensor-core operands from the packed blocks; results stay
+ * bit-identical to the reference's scalar integer dot. Synchronous;
+ * q38_weight_destroy frees the planes. */
+int q38_weight_build_planes(q38_weight *w);
+
 /* quantize_q8_k (src/kernel/quant.rs:98-124) of `batch` rows of `width`
  * DEVICE floats (width a multiple of 256, input 16-byte aligned) into
  * batch * width / 256 DEVICE blocks of Q38_Q8K_BLOCK_BYTES in the reference's
@@ -532,8 +545,10 @@ int q38_quantize_q8_k(q38_ctx *ctx, int batch, int64_t width, const float *input
  * quantized to Q8_K on the device and each output is bit-identical to the
  * reference's scalar integer dot. F32/F16/BF16/Q8_0: f32 dot, equal to the
  * reference's within rounding. Up to 8 tokens the Q8_K quantization runs
- * inside the GEMV; 9 or more tokens over Q4_K / Q5_K weights run on the
- * tensor cores, with the quantized input in a context scratch buffer that
+ * inside the GEMV; 9 or more tokens over Q4_K / Q5_K / Q6_K weights run on
+ * the tensor cores (from the weight's integer planes when
+ * q38_weight_build_planes made them), with the quantized input in a context
+ * scratch buffer that
  * grows on first use (q38_ctx_reserve_projection sizes it ahead, so that
  * later calls allocate nothing). Input must be 16-byte aligned. Launched as
  * a programmatic dependent of the previous kernel on the stream: the first

@@ -18,7 +18,7 @@ PKG_DIR = Path(__file__).resolve().parent
 CSRC = PKG_DIR / "csrc"
 LIB_PATH = PKG_DIR / "libq38attn.so"
 SOURCES = ["q38attn.cu", "attn_decode.cu", "deltanet_decode.cu", "attn_decode_noalloc.cu",
-           "attn_prefill.cu", "deltanet_prefill.cu", "q38_gguf.cpp", "proj.cu", "proj_mma.cu", "q38proj.cu", "q38_nccl.cu"]
+           "attn_prefill.cu", "deltanet_prefill.cu", "q38_gguf.cpp", "proj.cu", "proj_mma.cu", "proj_planes.cu", "q38proj.cu", "q38_nccl.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

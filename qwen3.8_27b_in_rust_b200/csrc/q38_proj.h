@@ -93,6 +93,11 @@ struct ProjWeight {
     int type = -1;
     int64_t rows = 0, width = 0, row_bytes = 0;  // row_bytes: device layout
     void *data = nullptr;  // device, proj_padded_bytes long
+    // Integer planes for batched projections (proj_planes.cu), or null: the
+    // tile-major atoms (planes) and the tile-major 16-byte side records
+    // (plane_side), one allocation.
+    void *planes = nullptr, *plane_side = nullptr;
+    int64_t plane_rows = 0;
 };
 
 bool proj_is_q8k_type(int type);
@@ -124,6 +129,17 @@ cudaError_t launch_proj_mma(const ProjWeight &w, const float *x, int batch, floa
                             const ProjEpilogue &epi = {}, bool prequantized = false);
 cudaError_t launch_proj_mma_quantize(const float *x, int batch, int64_t width, void *scratch,
                                      cudaStream_t stream);
+
+// Integer planes of a Q4_K / Q5_K / Q6_K weight (proj_planes.cu): built once
+// (synchronously on `stream`), then every 9+ token projection of the weight
+// streams them on the tensor cores, bit-identical to the integer GEMV.
+bool proj_planes_type(int type);
+size_t proj_plane_bytes(int type, int64_t rows, int64_t width);
+cudaError_t build_proj_planes(ProjWeight &w, cudaStream_t stream);
+void free_proj_planes(ProjWeight &w);
+cudaError_t launch_proj_planes(const ProjWeight &w, const float *x, int batch, float *out, long out_ld,
+                               int *err, void *scratch, cudaStream_t stream, const ProjEpilogue &epi = {},
+                               bool prequantized = false);
 
 cudaError_t launch_proj_f32(const ProjWeight &w, const float *x, int batch, float *out, long out_ld,
                             cudaStream_t stream, const ProjEpilogue &epi = {});

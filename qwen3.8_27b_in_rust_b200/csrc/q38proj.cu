@@ -81,8 +81,11 @@ int project_device(q38_ctx *ctx, const q38_weight *w, int batch, const float *in
     cudaError_t e;
     if (takes_mma(w, batch)) {
         if (int rc = reserve_scratch(ctx, batch, w->w.width)) return rc;
-        e = q38::launch_proj_mma(w->w, input, batch, out, long(w->w.rows), err, ctx->proj_scratch, s,
-                                 epi, prequantized);
+        e = w->w.planes
+                ? q38::launch_proj_planes(w->w, input, batch, out, long(w->w.rows), err, ctx->proj_scratch,
+                                          s, epi, prequantized)
+                : q38::launch_proj_mma(w->w, input, batch, out, long(w->w.rows), err, ctx->proj_scratch, s,
+                                       epi, prequantized);
     } else if (q38::proj_is_q8k_type(w->w.type))
         e = q38::launch_proj_q8k(w->w, input, batch, out, long(w->w.rows), err, ctx->sm_count, s, epi);
     else
@@ -154,9 +157,21 @@ int q38_weight_destroy(q38_weight *w) {
     if (!w) return Q38_OK;
     {
         Guard guard(w->ctx->device);
+        q38::free_proj_planes(w->w);
         cudaFree(w->w.data);
     }
     delete w;
+    return Q38_OK;
+}
+
+int q38_weight_build_planes(q38_weight *w) {
+    if (!w) return proj_fail(Q38_ERR_ARG, "null weight");
+    if (!q38::proj_planes_type(w->w.type))
+        return proj_fail(Q38_ERR_ARG, "integer planes are built for Q4_K, Q5_K and Q6_K weights, not type %d",
+                         w->w.type);
+    Guard guard(w->ctx->device);
+    cudaError_t e = q38::build_proj_planes(w->w, nullptr);
+    if (e != cudaSuccess) return proj_cuda_fail(e, "integer plane build");
     return Q38_OK;
 }
 

@@ -342,6 +342,12 @@ class Weight:
         check(self._lib.q38_weight_info(handle, ctypes.byref(t), ctypes.byref(w), ctypes.byref(r)))
         self.ggml_type, self.width, self.rows = t.value, w.value, r.value
 
+    def build_planes(self) -> "Weight":
+        """Builds the weight's integer planes (q38_weight_build_planes): later
+        projections of 9+ tokens stream them on the tensor cores."""
+        check(self._lib.q38_weight_build_planes(self.handle))
+        return self
+
     def close(self) -> None:
         if self.handle:
             check(self._lib.q38_weight_destroy(self.handle))

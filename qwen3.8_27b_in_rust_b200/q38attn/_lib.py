@@ -122,6 +122,7 @@ SIGNATURES = {
     "q38_weight_create": (c_int, [_VP, c_int, ctypes.c_int64, ctypes.c_int64, _VP, c_size_t,
                                   POINTER(c_void_p)]),
     "q38_weight_destroy": (c_int, [_VP]),
+    "q38_weight_build_planes": (c_int, [_VP]),
     "q38_weight_info": (c_int, [_VP, POINTER(c_int), POINTER(ctypes.c_int64),
                                 POINTER(ctypes.c_int64)]),
     "q38_weight_from_gguf": (c_int, [_VP, c_char_p, c_char_p, POINTER(c_void_p)]),

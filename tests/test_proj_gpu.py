@@ -87,6 +87,39 @@ def test_project_k_quants_bitwise(cuda_ctx, oracle_lib, ggml_type, rows, width):
     w.close()
 
 
+PLANE_CASES = [(12, 10240, HIDDEN), (13, 6144, HIDDEN), (14, HIDDEN, 6144), (12, 300, HIDDEN),
+               (14, 130, 256), (13, 129, 768), (12, 64, 9216), (14, 40, 8448)]
+
+
+@pytest.mark.parametrize("ggml_type,rows,width", PLANE_CASES)
+def test_project_planes_bitwise(cuda_ctx, oracle_lib, ggml_type, rows, width):
+    """Projections of 9+ tokens from the weight's integer planes
+    (q38_weight_build_planes) equal the reference's integer dot bit for bit:
+    full and ragged 32-token tiles, ragged 128-row tiles, one to 36 blocks."""
+    from q38attn import synth
+    g = synth.rng(300 + ggml_type + rows)
+    data = synth.quant_weight(g, ggml_type, rows, width)
+    w = cuda_ctx.weight(ggml_type, width, rows, data).build_planes()
+    w.build_planes()  # a second call keeps the planes it has
+    for batch in (9, 32, 40, 71):
+        x = synth.normal(g, (batch, width))
+        x[0, :256] = 0.0  # an all-zero activation block (scale 0)
+        got = _gpu_project(cuda_ctx, w, x)
+        want = oracle_lib.project(ggml_type, data, rows, width, x)
+        np.testing.assert_array_equal(got.view(np.uint32), want.view(np.uint32), err_msg=f"batch {batch}")
+    w.close()
+
+
+def test_planes_refuse_other_types(cuda_ctx):
+    import q38attn
+    from q38attn import synth
+    g = synth.rng(5)
+    w = cuda_ctx.weight(8, HIDDEN, 16, synth.quant_weight(g, 8, 16, HIDDEN))
+    with pytest.raises(q38attn.Q38Error):
+        w.build_planes()
+    w.close()
+
+
 @pytest.mark.parametrize("ggml_type", [0, 1, 30, 8])
 def test_project_f32_input_types(cuda_ctx, oracle_lib, ggml_type):
     from q38attn import synth
@@ -166,10 +199,11 @@ def _oracle_project(oracle_lib, spec, x):
     return oracle_lib.project(ty, data, rows, width, x)
 
 
-@pytest.mark.parametrize("batch", [2, 12])
-def test_linear_attention_decode_matches_oracle(cuda_ctx, oracle_lib, batch):
+@pytest.mark.parametrize("batch,planes", [(2, False), (12, False), (12, True)])
+def test_linear_attention_decode_matches_oracle(cuda_ctx, oracle_lib, batch, planes):
     """linear_attention (ops.rs:744-803) for sequences of DeltaNet layer 0; 12
-    sequences take the tensor-core projections."""
+    sequences take the tensor-core projections (from the integer planes with
+    `planes`)."""
     from q38attn import synth
     torch = _torch()
     g = synth.rng(400 + batch)
@@ -179,6 +213,9 @@ def test_linear_attention_decode_matches_oracle(cuda_ctx, oracle_lib, batch):
     host, dev = _layer_weights(cuda_ctx, g, {
         "qkv": (12, HIDDEN, 10240), "z": (13, HIDDEN, 6144), "beta": (8, HIDDEN, 48),
         "alpha": (0, HIDDEN, 48), "out": (14, 6144, HIDDEN)})
+    if planes:
+        for name in ("qkv", "z", "out"):
+            dev[name].build_planes()
     st = cuda_ctx.state(batch, 16, full_slots=0, linear_slots=1)
     states = [synth.linear_state(g) for _ in range(batch)]
     for b, s0 in enumerate(states):
@@ -212,8 +249,8 @@ def test_linear_attention_decode_matches_oracle(cuda_ctx, oracle_lib, batch):
     st.close()
 
 
-@pytest.mark.parametrize("batch", [2, 12])
-def test_full_attention_decode_matches_oracle(cuda_ctx, oracle_lib, batch):
+@pytest.mark.parametrize("batch,planes", [(2, False), (12, False), (12, True)])
+def test_full_attention_decode_matches_oracle(cuda_ctx, oracle_lib, batch, planes):
     """full_attention (ops.rs:941-981) for sequences of full layer 3 at
     positions 5, 40, ... over an f32 cache; 12 sequences take the tensor-core
     projections."""
@@ -227,6 +264,9 @@ def test_full_attention_decode_matches_oracle(cuda_ctx, oracle_lib, batch):
     host, dev = _layer_weights(cuda_ctx, g, {
         "q": (12, HIDDEN, 12288), "k": (14, HIDDEN, 1024), "v": (8, HIDDEN, 1024),
         "out": (12, 6144, HIDDEN)})
+    if planes:
+        for name in ("q", "k", "out"):
+            dev[name].build_planes()
     st = cuda_ctx.state(batch, ctx_len, full_slots=1, linear_slots=0)
     caches = []
     for b, pos in enumerate(positions):
