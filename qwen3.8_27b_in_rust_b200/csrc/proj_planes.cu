@@ -42,7 +42,7 @@
 // reached ~120 GB/s.) The side records are tile-major, [row tile][block][128
 // rows], so a CTA copies all of its own into shared memory once.
 //
-// CTA: 128 weight rows x 32 tokens, 19 warps.
+// CTA: 128 weight rows x 32 (or 16) tokens, 19 warps.
 //   warp 0      copies: a step's 32 KB of planes (one bulk copy; the first
 //               stages before the programmatic-dependent wait, weights are
 //               constant) and its activation quants [32 tokens][128 B] per
@@ -52,9 +52,9 @@
 //               columns (256 columns a block, two buffers); product planes,
 //               warp 1 chain lo and warp 2 chain hi, each accumulating over
 //               the block (64 columns a block, four buffers).
-//   warps 3-18  epilogue: thread = weight row (TMEM lane quarter = warp % 4),
-//               8 tokens per warp; per block the f32 term per (row, token),
-//               added in block order.
+//   warps 3-18  epilogue (warps 3-10 for 16 tokens): thread = weight row
+//               (TMEM lane quarter = warp % 4), 8 tokens per warp; per block
+//               the f32 term per (row, token), added in block order.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -67,26 +67,27 @@ namespace q38 {
 namespace {
 
 constexpr int kPlRows = 128;
-constexpr int kPlTok = 32;
 constexpr int kPlEpiWarp0 = 3;
-constexpr int kPlEpiWarps = 16;
-constexpr int kPlThreads = 32 * (kPlEpiWarp0 + kPlEpiWarps);
+constexpr int kPlThreads = 32 * (kPlEpiWarp0 + 16);
 constexpr uint32_t kPlAtomA = kPlRows * 128;               // a plane atom: 128 rows x 128 B
-constexpr uint32_t kPlAtomB = kPlTok * 128;                // an activation atom: 32 tokens x 128 B
 constexpr uint32_t kPlStepPlanes = 2 * kPlAtomA;           // 32 KB of planes per step
 constexpr int kPlMaxStages = 8;
 
-// The two plane forms (see the file comment).
-template <int T>
+// The two plane forms (see the file comment), for token tiles of kTok = 32
+// or 16 (a matrix of few row tiles splits its tokens over two CTAs so that
+// more SMs stream it; the second CTA's plane reads mostly hit L2).
+template <int T, int kTok>
 struct PlForm {
     static constexpr bool kQuant = T != Q38_GGML_Q6_K;         // quant planes
     static constexpr int kStepValues = kQuant ? 256 : 128;      // K values per step
     static constexpr int kStepAct = kQuant ? 2 : 1;             // activation atoms per step
-    static constexpr uint32_t kStage = kPlStepPlanes + kStepAct * kPlAtomB;
+    static constexpr uint32_t kAtomB = kTok * 128;              // an activation atom: kTok tokens x 128 B
+    static constexpr uint32_t kStage = kPlStepPlanes + kStepAct * kAtomB;
     static constexpr int kAcc = kQuant ? 2 : 4;                 // accumulator buffers
-    static constexpr uint32_t kAccCols = kQuant ? 8 * kPlTok : 2 * kPlTok;
-    static constexpr uint32_t kTmemCols = kAcc * kAccCols;      // 512 / 256
+    static constexpr uint32_t kAccCols = kQuant ? 8 * kTok : 2 * kTok;
+    static constexpr uint32_t kTmemCols = kAcc * kAccCols;      // 512 / 256 (kTok 32), half for 16
     static constexpr uint32_t kSide = kQuant ? 16 : 4;          // side record bytes
+    static constexpr int kEpiWarps = kTok / 2;                  // 4 lane quarters x kTok / 8 token groups
 };
 constexpr bool plane_quant(int type) { return type != Q38_GGML_Q6_K; }
 constexpr uint32_t plane_side_bytes(int type) { return plane_quant(type) ? 16 : 4; }
@@ -125,7 +126,7 @@ template <int T>
 __global__ void __launch_bounds__(256) planes_build_kernel(const unsigned char *raw, int64_t row_bytes,
                                                            unsigned char *planes, unsigned char *side,
                                                            int64_t width) {
-    using F = PlForm<T>;
+    using F = PlForm<T, 32>;
     const int b = blockIdx.y, v = threadIdx.x;
     const int64_t row = blockIdx.x;
     const int nblk = int(width / 256);
@@ -191,13 +192,13 @@ struct PlSmem {
 // side_bytes: the form's record size; psum: whether the group-sum table is
 // needed (quant planes).
 __host__ __device__ inline PlSmem pl_smem_plan(int stages, int nblk, uint32_t stage_bytes,
-                                               uint32_t side_bytes, bool psum) {
+                                               uint32_t side_bytes, bool psum, int tok) {
     PlSmem s{};
     s.stage = 0;
     s.side = uint32_t(stages) * stage_bytes;                           // [nblk][128 rows] records
     s.psum = s.side + (uint32_t(nblk) * kPlRows * side_bytes + 15) / 16 * 16;
-    s.scl = s.psum + (psum ? uint32_t(nblk) * kPlTok * 16 : 0);       // psum: [nblk][32] x 4 words
-    s.total = s.scl + uint32_t(nblk) * kPlTok * 4;                    // scl: [nblk][32] f32
+    s.scl = s.psum + (psum ? uint32_t(nblk) * tok * 16 : 0);          // psum: [nblk][tok] x 4 words
+    s.total = s.scl + uint32_t(nblk) * tok * 4;                       // scl: [nblk][tok] f32
     return s;
 }
 
@@ -207,11 +208,11 @@ __device__ __forceinline__ int pl_sbyte(const uint4 &rec, int k) {
     return int((w >> (8 * (k & 3))) & 0xffu);
 }
 
-template <int T>
+template <int T, int kTok>
 __global__ void __launch_bounds__(kPlThreads, 1)
     proj_planes_kernel(const __grid_constant__ CUtensorMap map_a, PlParams p) {
     using namespace sm100;
-    using F = PlForm<T>;
+    using F = PlForm<T, kTok>;
     constexpr bool kQ = F::kQuant;
     constexpr uint32_t kStage = F::kStage;
     extern __shared__ __align__(1024) unsigned char smem_raw[];
@@ -222,12 +223,12 @@ __global__ void __launch_bounds__(kPlThreads, 1)
     __shared__ uint32_t tmem_base_s;
     __shared__ volatile int abort_flag;
     const int S = p.stages;
-    const PlSmem lay = pl_smem_plan(S, p.nblk, kStage, F::kSide, kQ);
+    const PlSmem lay = pl_smem_plan(S, p.nblk, kStage, F::kSide, kQ, kTok);
     uint4 *psum = reinterpret_cast<uint4 *>(smem + lay.psum);
     const unsigned char *side_s = smem + lay.side;
     float *scl = reinterpret_cast<float *>(smem + lay.scl);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int row0 = blockIdx.x * kPlRows, tok0 = blockIdx.y * kPlTok;
+    const int row0 = blockIdx.x * kPlRows, tok0 = blockIdx.y * kTok;
     const int steps = p.nblk * 256 / F::kStepValues;
     // This CTA's planes: step s at stripe + s * step_stride.
     const unsigned char *stripe = p.planes + size_t(blockIdx.x) * kPlStepPlanes;
@@ -241,7 +242,7 @@ __global__ void __launch_bounds__(kPlThreads, 1)
         }
         for (int a = 0; a < F::kAcc; ++a) {
             mbar_init(&acc_full[a], 2);
-            mbar_init(&acc_empty[a], kPlEpiWarps);
+            mbar_init(&acc_empty[a], F::kEpiWarps);
         }
         mbar_init(&side_full, 1);
         fence_barrier_init();
@@ -259,7 +260,7 @@ __global__ void __launch_bounds__(kPlThreads, 1)
     auto load_act = [&](int s, int st) {
 #pragma unroll
         for (int c = 0; c < F::kStepAct; ++c)
-            tma_load_3d(smem + st * kStage + kPlStepPlanes + c * kPlAtomB, &map_a, s * F::kStepValues + 128 * c,
+            tma_load_3d(smem + st * kStage + kPlStepPlanes + c * F::kAtomB, &map_a, s * F::kStepValues + 128 * c,
                         tok0, 0, &full[st]);
     };
     if (warp == 0 && lane == 0) {
@@ -281,8 +282,8 @@ __global__ void __launch_bounds__(kPlThreads, 1)
     pdl_launch_dependents();
     // Per (block, token): the activation scale and, for quant planes, the
     // four packed pairs of sub-block sums (sub-block j = Q8_K groups 2j, 2j+1).
-    for (int i = tid; i < kPlTok * p.nblk; i += kPlThreads) {
-        const int b = i / kPlTok, t = i - b * kPlTok;
+    for (int i = tid; i < kTok * p.nblk; i += kPlThreads) {
+        const int b = i / kTok, t = i - b * kTok;
         const bool in = tok0 + t < p.batch;
         scl[i] = in ? p.scale[size_t(tok0 + t) * p.nblk + b] : 0.f;
         if constexpr (kQ) {
@@ -335,7 +336,7 @@ __global__ void __launch_bounds__(kPlThreads, 1)
         // half-blocks of each block.
         const int c = warp - 1;
         if (lane == 0) {
-            const uint32_t idesc = pl_idesc_i8(kPlRows, kPlTok, !kQ && c == 1);
+            const uint32_t idesc = pl_idesc_i8(kPlRows, kTok, !kQ && c == 1);
             constexpr int kStepsPerBlock = 256 / F::kStepValues;
             for (int b = 0; b < p.nblk; ++b) {
                 const int a = b % F::kAcc;
@@ -356,16 +357,16 @@ __global__ void __launch_bounds__(kPlThreads, 1)
                     }
                     fence_after_sync();
                     const uint32_t abase = smem_addr(smem + st * kStage + c * kPlAtomA);
-                    const uint32_t bbase = smem_addr(smem + st * kStage + kPlStepPlanes + (kQ ? c * kPlAtomB : 0));
+                    const uint32_t bbase = smem_addr(smem + st * kStage + kPlStepPlanes + (kQ ? c * F::kAtomB : 0));
 #pragma unroll
                     for (int k = 0; k < 4; ++k) {  // K-steps of 32 values within the atom
                         const uint64_t ad = smem_desc_sw128(abase + k * 32, 16, 1024);
                         const uint64_t bd = smem_desc_sw128(bbase + k * 32, 16, 1024);
                         if constexpr (kQ)
                             // sub-block 4c + k into its own 32 columns
-                            pl_mma_i8(dacc + uint32_t(4 * c + k) * kPlTok, ad, bd, idesc, 0u);
+                            pl_mma_i8(dacc + uint32_t(4 * c + k) * kTok, ad, bd, idesc, 0u);
                         else
-                            pl_mma_i8(dacc + uint32_t(c) * kPlTok, ad, bd, idesc, (h | k) ? 1u : 0u);
+                            pl_mma_i8(dacc + uint32_t(c) * kTok, ad, bd, idesc, (h | k) ? 1u : 0u);
                     }
                     mma_commit(&empty[st]);
                 }
@@ -377,7 +378,7 @@ __global__ void __launch_bounds__(kPlThreads, 1)
                 mma_commit(&acc_full[a]);
             }
         }
-    } else {
+    } else if (warp < kPlEpiWarp0 + F::kEpiWarps) {
         // ------------------------------------------------------------ epilogue
         const int e = warp - kPlEpiWarp0;
         const int quarter = warp & 3;  // the TMEM lanes this warp may read
@@ -428,7 +429,7 @@ __global__ void __launch_bounds__(kPlThreads, 1)
                 for (int jh = 0; jh < 2; ++jh) {
                     uint32_t D[4][8];
 #pragma unroll
-                    for (int jj = 0; jj < 4; ++jj) pl_tmem_ld8(dacc + uint32_t(4 * jh + jj) * kPlTok, D[jj]);
+                    for (int jj = 0; jj < 4; ++jj) pl_tmem_ld8(dacc + uint32_t(4 * jh + jj) * kTok, D[jj]);
                     tmem_wait_ld();
 #pragma unroll
                     for (int jj = 0; jj < 4; ++jj)
@@ -438,7 +439,7 @@ __global__ void __launch_bounds__(kPlThreads, 1)
             } else {
                 uint32_t dlo[8], dhi[8];
                 pl_tmem_ld8(dacc, dlo);
-                pl_tmem_ld8(dacc + kPlTok, dhi);
+                pl_tmem_ld8(dacc + kTok, dhi);
                 tmem_wait_ld();
 #pragma unroll
                 for (int t = 0; t < 8; ++t) weighted[t] = int(dlo[t]) + 256 * int(dhi[t]);
@@ -446,15 +447,15 @@ __global__ void __launch_bounds__(kPlThreads, 1)
             fence_before_sync();
             __syncwarp();
             if (lane == 0) mbar_arrive(&acc_empty[a]);
-            const float4 s0 = *reinterpret_cast<const float4 *>(scl + b * kPlTok + 8 * g);
-            const float4 s1 = *reinterpret_cast<const float4 *>(scl + b * kPlTok + 8 * g + 4);
+            const float4 s0 = *reinterpret_cast<const float4 *>(scl + b * kTok + 8 * g);
+            const float4 s1 = *reinterpret_cast<const float4 *>(scl + b * kTok + 8 * g + 4);
             const float as[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
 #pragma unroll
             for (int t = 0; t < 8; ++t) {
                 const float d = pl_half(cur.x) * as[t];
                 float term;
                 if constexpr (kQ) {
-                    const uint4 ps = psum[b * kPlTok + 8 * g + t];
+                    const uint4 ps = psum[b * kTok + 8 * g + t];
                     int minimum = __dp2a_lo(int(ps.x), int(mins0), 0);
                     minimum = __dp2a_hi(int(ps.y), int(mins0), minimum);
                     minimum = __dp2a_lo(int(ps.z), int(mins1), minimum);
@@ -520,25 +521,25 @@ bool pl_map_u8(CUtensorMap *m, const void *base, uint64_t cols, uint64_t rows, u
 }
 
 // As many stages as the shared-memory budget holds (at least 2); 0: none fit.
-int pl_stages_for(int type, int nblk) {
+int pl_stages_for(int type, int nblk, int tok) {
     const bool quant = plane_quant(type);
-    const uint32_t stage = kPlStepPlanes + (quant ? 2 : 1) * kPlAtomB;
+    const uint32_t stage = kPlStepPlanes + (quant ? 2 : 1) * uint32_t(tok) * 128;
     for (int s = kPlMaxStages; s >= 2; --s)
-        if (pl_smem_plan(s, nblk, stage, plane_side_bytes(type), quant).total + 1024 <= kProjSmemBudget)
+        if (pl_smem_plan(s, nblk, stage, plane_side_bytes(type), quant, tok).total + 1024 <= kProjSmemBudget)
             return s;
     return 0;
 }
 
-template <int T>
+template <int T, int kTok>
 cudaError_t launch_planes_typed(const CUtensorMap &ma, const PlParams &p, cudaStream_t stream) {
-    using F = PlForm<T>;
-    const size_t smem = pl_smem_plan(p.stages, p.nblk, F::kStage, F::kSide, F::kQuant).total + 1024;
+    using F = PlForm<T, kTok>;
+    const size_t smem = pl_smem_plan(p.stages, p.nblk, F::kStage, F::kSide, F::kQuant, kTok).total + 1024;
     static bool attr_set[64] = {};
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
     if (dev >= 64 || !attr_set[dev]) {
-        e = cudaFuncSetAttribute(proj_planes_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        e = cudaFuncSetAttribute(proj_planes_kernel<T, kTok>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  int(kProjSmemBudget));
         if (e != cudaSuccess) return e;
         if (dev < 64) attr_set[dev] = true;
@@ -547,13 +548,13 @@ cudaError_t launch_planes_typed(const CUtensorMap &ma, const PlParams &p, cudaSt
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.gridDim = dim3((p.rows + kPlRows - 1) / kPlRows, (p.batch + kPlTok - 1) / kPlTok);
+    cfg.gridDim = dim3((p.rows + kPlRows - 1) / kPlRows, (p.batch + kTok - 1) / kTok);
     cfg.blockDim = dim3(kPlThreads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, proj_planes_kernel<T>, ma, p);
+    return cudaLaunchKernelEx(&cfg, proj_planes_kernel<T, kTok>, ma, p);
 }
 
 }  // namespace
@@ -571,7 +572,7 @@ size_t proj_plane_bytes(int type, int64_t rows, int64_t width) {
 }
 
 cudaError_t build_proj_planes(ProjWeight &w, cudaStream_t stream) {
-    if (!proj_planes_type(w.type) || w.width % 256 || pl_stages_for(w.type, int(w.width / 256)) == 0)
+    if (!proj_planes_type(w.type) || w.width % 256 || pl_stages_for(w.type, int(w.width / 256), 32) == 0)
         return cudaErrorInvalidValue;
     if (w.planes) return cudaSuccess;
     const int64_t rp = proj_plane_rows(w.rows);
@@ -618,10 +619,14 @@ void free_proj_planes(ProjWeight &w) {
 
 cudaError_t launch_proj_planes(const ProjWeight &w, const float *x, int batch, float *out, long out_ld,
                                int *err, void *scratch, cudaStream_t stream, const ProjEpilogue &epi,
-                               bool prequantized) {
+                               bool prequantized, int sm_budget) {
     if (!w.planes || w.width % 256) return cudaErrorInvalidValue;
     const int nblk = int(w.width / 256);
-    const int stages = pl_stages_for(w.type, nblk);
+    // 16-token tiles when the batch fits one, or when twice the 32-token grid
+    // still fits the SMs this launch may take.
+    const int tiles = int((w.rows + kPlRows - 1) / kPlRows);
+    const int tok = batch <= 16 || 2 * tiles * ((batch + 31) / 32) <= sm_budget ? 16 : 32;
+    const int stages = pl_stages_for(w.type, nblk, tok);
     if (stages == 0) return cudaErrorInvalidValue;
     cudaError_t e = cudaSuccess;
     if (!prequantized && (e = launch_proj_mma_quantize(x, batch, w.width, scratch, stream)) != cudaSuccess)
@@ -631,7 +636,7 @@ cudaError_t launch_proj_planes(const ProjWeight &w, const float *x, int batch, f
     const size_t nb = size_t(batch) * size_t(nblk);
     unsigned char *sp = static_cast<unsigned char *>(scratch);
     CUtensorMap ma;
-    if (!pl_map_u8(&ma, sp, uint64_t(w.width), uint64_t(batch), kPlTok)) return cudaErrorInvalidValue;
+    if (!pl_map_u8(&ma, sp, uint64_t(w.width), uint64_t(batch), uint32_t(tok))) return cudaErrorInvalidValue;
     PlParams p{};
     p.planes = static_cast<const unsigned char *>(w.planes);
     p.scale = reinterpret_cast<const float *>(sp + nb * 256);
@@ -645,10 +650,17 @@ cudaError_t launch_proj_planes(const ProjWeight &w, const float *x, int batch, f
     p.nblk = nblk;
     p.batch = batch;
     p.stages = stages;
+    if (tok == 16) {
+        switch (w.type) {
+            case Q38_GGML_Q4_K: return launch_planes_typed<Q38_GGML_Q4_K, 16>(ma, p, stream);
+            case Q38_GGML_Q5_K: return launch_planes_typed<Q38_GGML_Q5_K, 16>(ma, p, stream);
+            default: return launch_planes_typed<Q38_GGML_Q6_K, 16>(ma, p, stream);
+        }
+    }
     switch (w.type) {
-        case Q38_GGML_Q4_K: return launch_planes_typed<Q38_GGML_Q4_K>(ma, p, stream);
-        case Q38_GGML_Q5_K: return launch_planes_typed<Q38_GGML_Q5_K>(ma, p, stream);
-        default: return launch_planes_typed<Q38_GGML_Q6_K>(ma, p, stream);
+        case Q38_GGML_Q4_K: return launch_planes_typed<Q38_GGML_Q4_K, 32>(ma, p, stream);
+        case Q38_GGML_Q5_K: return launch_planes_typed<Q38_GGML_Q5_K, 32>(ma, p, stream);
+        default: return launch_planes_typed<Q38_GGML_Q6_K, 32>(ma, p, stream);
     }
 }
 

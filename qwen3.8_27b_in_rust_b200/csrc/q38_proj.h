@@ -137,9 +137,11 @@ bool proj_planes_type(int type);
 size_t proj_plane_bytes(int type, int64_t rows, int64_t width);
 cudaError_t build_proj_planes(ProjWeight &w, cudaStream_t stream);
 void free_proj_planes(ProjWeight &w);
+// sm_budget: the SMs this launch may assume free (fewer when projections run
+// concurrently); it picks 16- or 32-token tiles.
 cudaError_t launch_proj_planes(const ProjWeight &w, const float *x, int batch, float *out, long out_ld,
                                int *err, void *scratch, cudaStream_t stream, const ProjEpilogue &epi = {},
-                               bool prequantized = false);
+                               bool prequantized = false, int sm_budget = 148);
 
 cudaError_t launch_proj_f32(const ProjWeight &w, const float *x, int batch, float *out, long out_ld,
                             cudaStream_t stream, const ProjEpilogue &epi = {});

@@ -2,6 +2,7 @@
 // cores: weight upload, Q8_K quantization, project / batch_project and the
 // layer-level decode calls linear_attention / full_attention
 // (src/model/ops.rs:617-640, 744-803, 941-981, 1016-1031).
+#include <algorithm>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -72,10 +73,11 @@ bool takes_mma(const q38_weight *w, int batch) {
 }
 
 // prequantized: the context's scratch already holds `input` quantized (MMA
-// path only; see the layer call below).
+// path only; see the layer call below). sm_budget: the SMs the launch may
+// take (0: all; fewer while other projections run beside it).
 int project_device(q38_ctx *ctx, const q38_weight *w, int batch, const float *input, float *out,
                    int *err, cudaStream_t s, const q38::ProjEpilogue &epi = {},
-                   bool prequantized = false) {
+                   bool prequantized = false, int sm_budget = 0) {
     if (reinterpret_cast<uintptr_t>(input) % 16)
         return proj_fail(Q38_ERR_ARG, "projection input must be 16-byte aligned");
     cudaError_t e;
@@ -83,7 +85,7 @@ int project_device(q38_ctx *ctx, const q38_weight *w, int batch, const float *in
         if (int rc = reserve_scratch(ctx, batch, w->w.width)) return rc;
         e = w->w.planes
                 ? q38::launch_proj_planes(w->w, input, batch, out, long(w->w.rows), err, ctx->proj_scratch,
-                                          s, epi, prequantized)
+                                          s, epi, prequantized, sm_budget > 0 ? sm_budget : ctx->sm_count)
                 : q38::launch_proj_mma(w->w, input, batch, out, long(w->w.rows), err, ctx->proj_scratch, s,
                                        epi, prequantized);
     } else if (q38::proj_is_q8k_type(w->w.type))
@@ -291,8 +293,13 @@ int q38_linear_attention_decode(q38_ctx *ctx, q38_state *st, int layer, int batc
         if (e == cudaSuccess) e = cudaEventRecord(st->side_fork, s);
         for (int i = 0; i < 2 && e == cudaSuccess; ++i) e = cudaStreamWaitEvent(st->side[i], st->side_fork, 0);
         if (e != cudaSuccess) return proj_cuda_fail(e, "layer projections fork");
-        if (int rc = project_device(ctx, w->qkv, batch, norm, qkv, st->d_err, s, conv, true)) return rc;
-        if (int rc = project_device(ctx, w->z, batch, norm, z, st->d_err, st->side[0], {}, true)) return rc;
+        // Each of qkv and z may take the SMs the other leaves.
+        const int tiles_qkv = int((w->qkv->w.rows + 127) / 128), tiles_z = int((w->z->w.rows + 127) / 128);
+        const int budget_qkv = std::max(1, ctx->sm_count - tiles_z), budget_z = std::max(1, ctx->sm_count - tiles_qkv);
+        if (int rc = project_device(ctx, w->qkv, batch, norm, qkv, st->d_err, s, conv, true, budget_qkv))
+            return rc;
+        if (int rc = project_device(ctx, w->z, batch, norm, z, st->d_err, st->side[0], {}, true, budget_z))
+            return rc;
         if (int rc = project_device(ctx, w->beta, batch, norm, beta, st->d_err, st->side[1], gbeta))
             return rc;
         if (int rc = project_device(ctx, w->alpha, batch, norm, alpha, st->d_err, st->side[1], galpha))
