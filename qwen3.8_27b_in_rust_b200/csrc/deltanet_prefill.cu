@@ -234,7 +234,7 @@ constexpr int kPadA = kC + 1;  // padded f32 rows of A and T (conflict-free colu
 // Shared-memory plan of L3 (bytes). Region R is reused phase by phase:
 //   G phase:       [K; Q] hi | [K; Q] lo, each two SW128 boxes of 128 rows x 64 dims
 //   A/P phase:     A f32 [64][65] | decay factors [64][65] | ... | P staging (hi | lo) at 40 KB
-//   inverse phase: A f32 [64][65] | T f32 [64][65] | block products [3][16][16]
+//   inverse phase: A f32 [64][65] | T f32 [64][65] | ... | block products [32][65] at 40 KB
 //   MMA phase:     B_W hi | B_W lo | B_U hi | B_U lo, each two SW128 boxes of 64 rows x 64 cols
 //   epilogue:      W hi | W lo | Ut staging for coalesced stores
 // Staging tiles hold 16-byte chunk c of row r at chunk c ^ (r % chunks per
@@ -246,11 +246,12 @@ constexpr uint32_t kLocR = 64 * 1024;
 constexpr uint32_t kLocKQBox = 128 * 128;          // 128 rows x 128 B
 constexpr uint32_t kLocBBox = 64 * 128;            // 64 rows x 128 B
 constexpr uint32_t kLocTs = kC * kPadA * 4;        // offset of T within R
-constexpr uint32_t kLocXs = 2 * kC * kPadA * 4;    // offset of the block products
+constexpr uint32_t kLocXs = 40 * 1024;             // the inverse's block products (P staging, stored by then)
 constexpr uint32_t kLocPst = 40 * 1024;            // P (hi | lo) staging during the A/P phase
 constexpr uint32_t kLocTu = kLocR;                 // Tu hi at +0, lo at +8 KB, padding +16 KB
 constexpr uint32_t kLocSmem = kLocR + 3 * 8192 + 1024;
-static_assert(kLocXs + 3 * 256 * 4 <= kLocPst && kLocPst + 2 * kC * kC * 2 <= kLocR,
+static_assert(2 * kC * kPadA * 4 <= kLocXs && kLocXs + 32 * kPadA * 4 <= kLocR &&
+                  kLocPst + 2 * kC * kC * 2 <= kLocR,
               "inverse workspace and P staging fit R");
 constexpr uint32_t kLocTmemCols = 256;  // G (64) while it is read out, then W (128) | Ut (128)
 
@@ -475,10 +476,13 @@ __global__ void __launch_bounds__(256, 2) linear_prefill_local_kernel(LocalParam
             }
         }
 
-        // T = (I + A)^-1 in 16x16 blocks (A strictly lower). The diagonal
-        // blocks T_ii = (I + A_ii)^-1 by forward substitution, one warp each;
-        // then the block sub-diagonals d = 1, 2, 3 in turn:
-        //   T_ij = -T_ii sum_{k=j}^{i-1} A_ik T_kj   (j = i - d).
+        // T = (I + A)^-1 (A strictly lower) by block doubling: for a lower
+        // block matrix L = [L11 0; L21 L22], L^-1 = [T11 0; -T22 L21 T11 T22],
+        // and the off-diagonal block of L = I + A is A's. The four 16x16
+        // diagonal blocks by forward substitution, one warp each; then the two
+        // 16x16 pairs (T10 = -T11 A10 T00, T32 = -T33 A32 T22); then the
+        // 32x32 halves (T[32:64][0:32] = -T_BB A_BA T_AA). The products run
+        // on 2x2 register tiles (four shared-memory loads per four FMAs).
         for (int idx = tid; idx < kC * kPadA; idx += 256) Ts[idx] = 0.f;
         __syncthreads();
         if (warp < 4 && lane < 16) {
@@ -498,28 +502,54 @@ __global__ void __launch_bounds__(256, 2) linear_prefill_local_kernel(LocalParam
             for (int r = 0; r < 16; ++r) Ts[(b0 + r) * kPadA + b0 + c] = t[r];
         }
         __syncthreads();
-        for (int d = 1; d < 4; ++d) {
-            const int nblk = 4 - d;
-            for (int idx = tid; idx < nblk * 256; idx += 256) {
-                const int blk = idx >> 8, e = idx & 255, r = e >> 4, c = e & 15;
-                const int i = blk + d, j = blk;
-                float acc = 0.f;
-                for (int k = j; k < i; ++k)
-#pragma unroll
-                    for (int m = 0; m < 16; ++m)
-                        acc = fmaf(As[(16 * i + r) * kPadA + 16 * k + m],
-                                   Ts[(16 * k + m) * kPadA + 16 * j + c], acc);
-                Xs[idx] = acc;
+        // X [n x n] (row stride kPadA, in Xs) = L (rows lr0, cols lc0) x R
+        // (rows rr0, cols rc0), k over [k0, k1); thread tiles (2 rows, 2 cols).
+        // sign: +1 or -1 applied to the result.
+        auto prod2x2 = [&](const float *L, int lr0, int lc0, const float *R, int rr0, int rc0, float *X,
+                           int xr0, int xc0, int ti, int tj, int kbeg, int kend, float sign) {
+            const int r = 2 * ti, c = 2 * tj;
+            float a00 = 0.f, a01 = 0.f, a10 = 0.f, a11 = 0.f;
+            for (int k = kbeg; k < kend; ++k) {
+                const float l0 = L[(lr0 + r) * kPadA + lc0 + k], l1 = L[(lr0 + r + 1) * kPadA + lc0 + k];
+                const float r0 = R[(rr0 + k) * kPadA + rc0 + c], r1 = R[(rr0 + k) * kPadA + rc0 + c + 1];
+                a00 = fmaf(l0, r0, a00);
+                a01 = fmaf(l0, r1, a01);
+                a10 = fmaf(l1, r0, a10);
+                a11 = fmaf(l1, r1, a11);
+            }
+            X[(xr0 + r) * kPadA + xc0 + c] = sign * a00;
+            X[(xr0 + r) * kPadA + xc0 + c + 1] = sign * a01;
+            X[(xr0 + r + 1) * kPadA + xc0 + c] = sign * a10;
+            X[(xr0 + r + 1) * kPadA + xc0 + c + 1] = sign * a11;
+        };
+        {
+            // Level 1: X0 = A10 T00 and X1 = A32 T22 (64 tiles of 2x2 each,
+            // threads 0-127), into Xs rows 0-15 / 16-31, columns 0-15.
+            // T00 is lower triangular: row k of T00 is zero left of k, so
+            // column c needs k >= c only -- the full range is kept (zeros).
+            if (tid < 128) {
+                const int pr = tid >> 6, e = tid & 63, ti = e >> 3, tj = e & 7;
+                const int bi = 16 + 32 * pr, bj = 32 * pr;  // A block (i, j), T block (j, j)
+                prod2x2(As, bi, bj, Ts, bj, bj, Xs, 16 * pr, 0, ti, tj, 0, 16, 1.f);
             }
             __syncthreads();
-            for (int idx = tid; idx < nblk * 256; idx += 256) {
-                const int blk = idx >> 8, e = idx & 255, r = e >> 4, c = e & 15;
-                const int i = blk + d, j = blk;
-                float acc = 0.f;
-#pragma unroll
-                for (int m = 0; m < 16; ++m)
-                    acc = fmaf(Ts[(16 * i + r) * kPadA + 16 * i + m], Xs[(blk << 8) + m * 16 + c], acc);
-                Ts[(16 * i + r) * kPadA + 16 * j + c] = -acc;
+            // T10 = -T11 X0, T32 = -T33 X1 (T11 lower triangular: k <= row).
+            if (tid < 128) {
+                const int pr = tid >> 6, e = tid & 63, ti = e >> 3, tj = e & 7;
+                const int bi = 16 + 32 * pr;
+                prod2x2(Ts, bi, bi, Xs, 16 * pr, 0, Ts, bi, 32 * pr, ti, tj, 0, 2 * ti + 2, -1.f);
+            }
+            __syncthreads();
+            // Level 2: X = A[32:64][0:32] T[0:32][0:32] (256 tiles of 2x2).
+            {
+                const int ti = tid >> 4, tj = tid & 15;
+                prod2x2(As, 32, 0, Ts, 0, 0, Xs, 0, 0, ti, tj, 0, 32, 1.f);
+            }
+            __syncthreads();
+            // T[32:64][0:32] = -T[32:64][32:64] X (lower triangular: k <= row).
+            {
+                const int ti = tid >> 4, tj = tid & 15;
+                prod2x2(Ts, 32, 32, Xs, 0, 0, Ts, 32, 0, ti, tj, 0, 2 * ti + 2, -1.f);
             }
             __syncthreads();
         }
