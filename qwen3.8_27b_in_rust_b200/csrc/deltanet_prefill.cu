@@ -391,20 +391,36 @@ __global__ void __launch_bounds__(256, 2) linear_prefill_local_kernel(LocalParam
 
     const uint32_t idesc_x = idesc_bf16_f32(128, kD, 0, 1);
     const uint32_t d_w = tmem, d_u = tmem + kD;  // W columns 0-127, Ut columns 128-255
+    // The call's value heads of key head kh, in order; each head's gates
+    // (beta, g of the chunk's tokens) are loaded one head ahead.
+    auto next_head = [&](int h) {
+        for (h += p.qk_heads; h < p.v_heads; h += p.qk_heads)
+            if (in_call(h)) return h;
+        return -1;
+    };
+    auto load_gates = [&](int h, float &bv, float &gv_) {
+        bv = gv_ = 0.f;
+        if (h >= 0 && tid < kC && row_ok(tid)) {
+            const size_t gi = (size_t(s) * p.count + t0 + tid) * p.v_heads + h;
+            bv = p.beta[gi];
+            gv_ = p.alpha[gi];
+        }
+    };
+    int h = in_call(kh) ? kh : next_head(kh);
+    float nb, ng;  // the gates of head h
+    load_gates(h, nb, ng);
     int head_i = -1;  // value heads of this CTA processed so far, minus one
-    for (int h = kh; h < p.v_heads; h += p.qk_heads) {
-        if (!in_call(h)) continue;
+    for (; h >= 0; h = next_head(h)) {
         ++head_i;
         const size_t plane = (size_t(s) * p.nchunk + chunk) * p.v_heads + h;
         fence_before_sync();
         __syncthreads();  // previous head done with R, gam/bet and TMEM
         fence_after_sync();
         if (tid < kC) {
-            const bool in = row_ok(tid);
-            const size_t gi = (size_t(s) * p.count + t0 + tid) * p.v_heads + h;
-            bet[tid] = in ? p.beta[gi] : 0.f;
-            gam[tid] = in ? p.alpha[gi] : 0.f;
+            bet[tid] = nb;
+            gam[tid] = ng;
         }
+        load_gates(next_head(h), nb, ng);
         __syncthreads();
         if (tid < 32) {
             // Inclusive prefix sum of g over the 64 tokens (two per lane).
