@@ -442,24 +442,20 @@ __global__ void __launch_bounds__(256, 2) linear_prefill_local_kernel(LocalParam
             dec[tid] = expf(gam[kC - 1] - gam[tid]);
         }
         // A = beta_r e^{gamma_r - gamma_s} K K^T (strictly lower) into smem;
-        // P = e^{gamma_r - gamma_s} Q K^T (lower) as bf16 pairs to global. The
-        // K K^T warp of a (rows, columns) block computes the decay factors and
-        // hands them to the Q K^T warp of the same block through smem (Ts,
-        // not yet in use).
+        // P = e^{gamma_r - gamma_s} Q K^T (lower) as bf16 pairs to global.
+        // Every warp forms the decay factors of its own (rows, columns) block.
         {
             const int r = gr;
-            float *Dm = Ts;
+            const float gr_ = gam[r];
             if (is_kk) {
+                const float br = bet[r];
 #pragma unroll
                 for (int i = 0; i < 32; ++i) {
                     const int c = gc0 + i;
-                    const float d = (c <= r) ? decay_exp(gam[r] - gam[c]) : 0.f;
-                    Dm[r * kPadA + c] = d;
-                    As[r * kPadA + c] = c < r ? bet[r] * d * gv[i] : 0.f;
+                    const float d = (c <= r) ? decay_exp(gr_ - gam[c]) : 0.f;
+                    As[r * kPadA + c] = c < r ? br * d * gv[i] : 0.f;
                 }
-            }
-            __syncthreads();
-            if (!is_kk) {
+            } else {
                 unsigned char *pst = R + kLocPst;
 #pragma unroll
                 for (int q = 0; q < 4; ++q) {
@@ -467,7 +463,7 @@ __global__ void __launch_bounds__(256, 2) linear_prefill_local_kernel(LocalParam
 #pragma unroll
                     for (int b = 0; b < 8; ++b) {
                         const int c = gc0 + 8 * q + b;
-                        pv[b] = c <= r ? Dm[r * kPadA + c] * gv[8 * q + b] : 0.f;
+                        pv[b] = c <= r ? decay_exp(gr_ - gam[c]) * gv[8 * q + b] : 0.f;
                     }
                     uint4 hq, lq;
                     split_bf16x2(pv[0], pv[1], hq.x, lq.x);
@@ -671,6 +667,40 @@ __global__ void __launch_bounds__(256, 2) linear_prefill_local_kernel(LocalParam
             }
             mma_commit(&mma_done);
         }
+        if (!is_kk) {
+            // Warps 2, 3, 6, 7 (128 threads), while the MMAs run: Q~ =
+            // diag(e^gamma) Q from the normalised rows. Thread: 8 columns
+            // (chunk t % 16) of rows t / 16 + 8 k, one 16-byte chunk per lane
+            // in each store.
+            const int t = 32 * ((warp & 1) + 2 * (warp >> 2)) + lane;  // 0..127
+            const int c = t & 15;
+            __nv_bfloat16 *qh = p.q2 + plane * 2 * kC * kD + 8 * c, *ql = qh + kC * kD;
+#pragma unroll
+            for (int half = 0; half < 2; ++half) {
+                float4 x[8];
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    const int r = (t >> 4) + 8 * (4 * half + k);
+                    const float4 *q4 = reinterpret_cast<const float4 *>(rows + size_t(r) * p.qkv_dim + kh * kD + 8 * c);
+                    x[2 * k] = row_ok(r) ? __ldg(q4) : make_float4(0.f, 0.f, 0.f, 0.f);
+                    x[2 * k + 1] = row_ok(r) ? __ldg(q4 + 1) : make_float4(0.f, 0.f, 0.f, 0.f);
+                }
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    const int r = (t >> 4) + 8 * (4 * half + k);
+                    const float e = egs[r];
+                    const float4 a = x[2 * k], b = x[2 * k + 1];
+                    uint4 hq, lq;
+                    split_bf16x2(a.x * e, a.y * e, hq.x, lq.x);
+                    split_bf16x2(a.z * e, a.w * e, hq.y, lq.y);
+                    split_bf16x2(b.x * e, b.y * e, hq.z, lq.z);
+                    split_bf16x2(b.z * e, b.w * e, hq.w, lq.w);
+                    *reinterpret_cast<uint4 *>(qh + r * kD) = hq;
+                    *reinterpret_cast<uint4 *>(ql + r * kD) = lq;
+                }
+            }
+            if (t < kC) p.eg_out[plane * kC + t] = egs[t];
+        }
         if (!__all_sync(0xffffffffu, mbar_wait(&mma_done, uint32_t(head_i & 1)))) {
             if (lane == 0) set_error(p.err, kDevErrTimeout);
         }
@@ -720,38 +750,6 @@ __global__ void __launch_bounds__(256, 2) linear_prefill_local_kernel(LocalParam
                 const int idx = t + 128 * k, rr = idx >> 5, cc = idx & 31;
                 udst[idx] = *reinterpret_cast<const uint4 *>(ust + stage_at(rr, cc, 32));
             }
-        } else {
-            // Warps 2, 3, 6, 7 (128 threads): Q~ = diag(e^gamma) Q from the
-            // normalised rows. Thread: 8 columns (chunk t % 16) of rows
-            // t / 16 + 8 k, one 16-byte chunk per lane in each store.
-            const int t = 32 * ((warp & 1) + 2 * (warp >> 2)) + lane;  // 0..127
-            const int c = t & 15;
-            __nv_bfloat16 *qh = p.q2 + plane * 2 * kC * kD + 8 * c, *ql = qh + kC * kD;
-#pragma unroll
-            for (int half = 0; half < 2; ++half) {
-                float4 x[8];
-#pragma unroll
-                for (int k = 0; k < 4; ++k) {
-                    const int r = (t >> 4) + 8 * (4 * half + k);
-                    const float4 *q4 = reinterpret_cast<const float4 *>(rows + size_t(r) * p.qkv_dim + kh * kD + 8 * c);
-                    x[2 * k] = row_ok(r) ? __ldg(q4) : make_float4(0.f, 0.f, 0.f, 0.f);
-                    x[2 * k + 1] = row_ok(r) ? __ldg(q4 + 1) : make_float4(0.f, 0.f, 0.f, 0.f);
-                }
-#pragma unroll
-                for (int k = 0; k < 4; ++k) {
-                    const int r = (t >> 4) + 8 * (4 * half + k);
-                    const float e = egs[r];
-                    const float4 a = x[2 * k], b = x[2 * k + 1];
-                    uint4 hq, lq;
-                    split_bf16x2(a.x * e, a.y * e, hq.x, lq.x);
-                    split_bf16x2(a.z * e, a.w * e, hq.y, lq.y);
-                    split_bf16x2(b.x * e, b.y * e, hq.z, lq.z);
-                    split_bf16x2(b.z * e, b.w * e, hq.w, lq.w);
-                    *reinterpret_cast<uint4 *>(qh + r * kD) = hq;
-                    *reinterpret_cast<uint4 *>(ql + r * kD) = lq;
-                }
-            }
-            if (t < kC) p.eg_out[plane * kC + t] = egs[t];
         }
         tmem_wait_ld();
     }
