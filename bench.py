@@ -410,9 +410,9 @@ def run_split_sequence(args, ctx, q38attn, torch, dist, rank: int, world: int,
         vview[0, :, :n].normal_(generator=tg)
     del kview, vview
     qg = torch.randn(1, 12288, device="cuda", generator=tg)
-    key0 = torch.randn(1, 1024, device="cuda", generator=tg)
+    # One key row per step: the call normalises and rotates its key in place.
+    keys = torch.randn(args.split_steps + 3, 1024, device="cuda", generator=tg)
     val = torch.randn(1, 1024, device="cuda", generator=tg)
-    key = torch.empty_like(key0)
     out = torch.empty(1, 6144, device="cuda")
     pos = torch.arange(P, P + args.split_steps + 3, device="cuda", dtype=torch.int32)
     dec = SplitSequenceDecoder(ctx, st, FULL_LAYER, p0, transport=transport) if world > 1 else None
@@ -421,7 +421,7 @@ def run_split_sequence(args, ctx, q38attn, torch, dist, rank: int, world: int,
     stream = torch.cuda.current_stream()
 
     def one(i):
-        key.copy_(key0)
+        key = keys[i:i + 1]
         if dec is not None:
             dec.step(qg, key, val, pos[i:i + 1], out, cap - 1, stream=stream)
         else:
@@ -715,7 +715,10 @@ def run_ours(args) -> None:
         dview.normal_(0.0, 0.02, generator=tg)
     del kview, vview
 
-    # Two pristine per-step input sets in one flat buffer each.
+    # Per-step inputs, generated ahead: the calls rewrite qkv, beta, alpha and
+    # key in place, so each step reads a slice of its own (a pool of up to 512
+    # slices, reused cyclically by longer runs) and no copy kernel runs inside
+    # the timed region.
     n_lin = len(LINEAR_LAYERS)
     sizes = [("qg", (B, 12288)), ("key", (B, 1024)), ("value", (B, 1024))]
     for i in range(n_lin):
@@ -731,9 +734,10 @@ def run_ours(args) -> None:
             off += n
         return out
 
-    pristine = [torch.randn(total, device="cuda", generator=tg) for _ in range(2)]
-    work = torch.empty(total, device="cuda")
-    wv = views(work)
+    pool = min(total_steps, 512)
+    inputs = torch.randn(pool, total, device="cuda", generator=tg)
+    pristine = [inputs[0].clone(), inputs[min(1, pool - 1)].clone()]  # the e2e leg's host inputs
+    step_views = [views(inputs[i]) for i in range(pool)]
     out_full = torch.empty(B, 6144, device="cuda")
     out_lin = [torch.empty(B, 6144, device="cuda") for _ in range(n_lin)]
     positions = (torch.arange(total_steps, device="cuda", dtype=torch.int32)[:, None] + ctx_pos
@@ -746,7 +750,7 @@ def run_ours(args) -> None:
               for _ in range(args.steps)]
 
     def step(s: int, timed_index: int = -1):
-        work.copy_(pristine[s % 2])
+        wv = step_views[s % pool]
         if timed_index >= 0:
             ev_lin[timed_index][0].record(stream)
         for i, l in enumerate(LINEAR_LAYERS):
