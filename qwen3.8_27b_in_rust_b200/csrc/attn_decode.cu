@@ -397,9 +397,17 @@ __global__ void __launch_bounds__(kThreads, 2)
     sm100::fence_before_sync();
     __syncthreads();
     sm100::fence_after_sync();
-    // K1 wrote this sequence's new KV row and its prepared queries.
+    // K1 (a full-dependency launch: everything before it has completed)
+    // writes only the sequence's new KV row, local row pos - pos_offset, and
+    // the prepared queries. A split whose rows end before that row fetches
+    // its first tiles now, while K1 runs; the split holding it waits first.
+    const int new_row = pos - p.pos_offset;
+    const bool early = new_row >= p.context_length || start + cnt <= new_row;
+    if (early && threadIdx.x == 0) {
+        for (int j = 0; j < kStages && j < total_tiles; ++j) issue(j);
+    }
     pdl_wait_primary();
-    if (threadIdx.x == 0) {
+    if (!early && threadIdx.x == 0) {
         for (int j = 0; j < kStages && j < total_tiles; ++j) issue(j);
     }
     const float score_scale = 1.0f / sqrtf(float(kAttnHeadDim));  // ops.rs:873
