@@ -72,10 +72,14 @@ constexpr int kPlThreads = 32 * (kPlEpiWarp0 + 16);
 constexpr uint32_t kPlAtomA = kPlRows * 128;               // a plane atom: 128 rows x 128 B
 constexpr uint32_t kPlStepPlanes = 2 * kPlAtomA;           // 32 KB of planes per step
 constexpr int kPlMaxStages = 8;
+constexpr int kPlLargeBatch = 128;  // tokens from which 64-token tiles are used
 
-// The two plane forms (see the file comment), for token tiles of kTok = 32
-// or 16 (a matrix of few row tiles splits its tokens over two CTAs so that
-// more SMs stream it; the second CTA's plane reads mostly hit L2).
+// The two plane forms (see the file comment), for token tiles of kTok = 16,
+// 32 or 64: 32 for decode batches; 16 when a matrix of few row tiles splits
+// its tokens over two CTAs so that more SMs stream it (the second CTA's
+// plane reads mostly hit L2); 64 for prompt-sized batches, where each CTA's
+// planes serve twice the tokens (quant planes then fill TMEM with one
+// block's 8 x 64 accumulators, so MMA and epilogue alternate).
 template <int T, int kTok>
 struct PlForm {
     static constexpr bool kQuant = T != Q38_GGML_Q6_K;         // quant planes
@@ -83,11 +87,13 @@ struct PlForm {
     static constexpr int kStepAct = kQuant ? 2 : 1;             // activation atoms per step
     static constexpr uint32_t kAtomB = kTok * 128;              // an activation atom: kTok tokens x 128 B
     static constexpr uint32_t kStage = kPlStepPlanes + kStepAct * kAtomB;
-    static constexpr int kAcc = kQuant ? 2 : 4;                 // accumulator buffers
     static constexpr uint32_t kAccCols = kQuant ? 8 * kTok : 2 * kTok;
-    static constexpr uint32_t kTmemCols = kAcc * kAccCols;      // 512 / 256 (kTok 32), half for 16
+    static constexpr int kAcc = int(512 / kAccCols) > 4 ? 4 : int(512 / kAccCols);  // accumulator buffers
+    static constexpr uint32_t kTmemCols = kAcc * kAccCols;      // <= 512
     static constexpr uint32_t kSide = kQuant ? 16 : 4;          // side record bytes
-    static constexpr int kEpiWarps = kTok / 2;                  // 4 lane quarters x kTok / 8 token groups
+    static constexpr int kEpiWarps = kTok >= 32 ? 16 : 8;       // 4 lane quarters x token groups
+    static constexpr int kTokPerWarp = kTok * 4 / kEpiWarps;    // 8 or 16
+    static_assert(kTmemCols == 128 || kTmemCols == 256 || kTmemCols == 512, "TMEM allocation");
 };
 constexpr bool plane_quant(int type) { return type != Q38_GGML_Q6_K; }
 constexpr uint32_t plane_side_bytes(int type) { return plane_quant(type) ? 16 : 4; }
@@ -380,14 +386,15 @@ __global__ void __launch_bounds__(kPlThreads, 1)
         }
     } else if (warp < kPlEpiWarp0 + F::kEpiWarps) {
         // ------------------------------------------------------------ epilogue
+        constexpr int kTPW = F::kTokPerWarp;
         const int e = warp - kPlEpiWarp0;
         const int quarter = warp & 3;  // the TMEM lanes this warp may read
-        const int g = e >> 2;          // tokens 8g .. 8g+7
+        const int tg0 = (e >> 2) * kTPW;  // this warp's first token in the tile
         const uint32_t r = uint32_t(32 * quarter + lane);
         const uint32_t lane_addr = uint32_t(32 * quarter) << 16;
-        float total[8];
+        float total[kTPW];
 #pragma unroll
-        for (int t = 0; t < 8; ++t) total[t] = 0.f;
+        for (int t = 0; t < kTPW; ++t) total[t] = 0.f;
         bool ok = __all_sync(0xffffffffu, mbar_wait(&side_full, 0));
         for (int b = 0; b < p.nblk && ok; ++b) {
             const int a = b % F::kAcc;
@@ -401,13 +408,11 @@ __global__ void __launch_bounds__(kPlThreads, 1)
                 break;
             }
             fence_after_sync();
-            const uint32_t dacc = tmem + lane_addr + uint32_t(a) * F::kAccCols + uint32_t(8 * g);
-            int weighted[8];
+            const uint32_t dacc = tmem + lane_addr + uint32_t(a) * F::kAccCols;
+            int sc[8];
             uint32_t mins0 = 0, mins1 = 0;
             if constexpr (kQ) {
-                // weighted = sum_j sc_j D_j; scale_min_k4 (tensor.rs:23-32)
-                // for the sub-blocks' scales and mins.
-                int sc[8];
+                // scale_min_k4 (tensor.rs:23-32): the sub-blocks' scales and mins.
 #pragma unroll
                 for (int j = 0; j < 8; ++j) {
                     int mn;
@@ -423,49 +428,62 @@ __global__ void __launch_bounds__(kPlThreads, 1)
                     else
                         mins1 |= uint32_t(mn) << (8 * (j - 4));
                 }
+            }
+            // This warp's tokens in chunks of 8: the block's integer sums
+            // weighted (and minimum) per token, then the f32 term.
+            int weighted[kTPW];
 #pragma unroll
-                for (int t = 0; t < 8; ++t) weighted[t] = 0;
+            for (int tc = 0; tc < kTPW; tc += 8) {
+                const uint32_t col = uint32_t(tg0 + tc);
+                if constexpr (kQ) {
+                    // weighted = sum_j sc_j D_j
 #pragma unroll
-                for (int jh = 0; jh < 2; ++jh) {
-                    uint32_t D[4][8];
+                    for (int t = 0; t < 8; ++t) weighted[tc + t] = 0;
 #pragma unroll
-                    for (int jj = 0; jj < 4; ++jj) pl_tmem_ld8(dacc + uint32_t(4 * jh + jj) * kTok, D[jj]);
+                    for (int jh = 0; jh < 2; ++jh) {
+                        uint32_t D[4][8];
+#pragma unroll
+                        for (int jj = 0; jj < 4; ++jj) pl_tmem_ld8(dacc + uint32_t(4 * jh + jj) * kTok + col, D[jj]);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int jj = 0; jj < 4; ++jj)
+#pragma unroll
+                            for (int t = 0; t < 8; ++t) weighted[tc + t] += sc[4 * jh + jj] * int(D[jj][t]);
+                    }
+                } else {
+                    uint32_t dlo[8], dhi[8];
+                    pl_tmem_ld8(dacc + col, dlo);
+                    pl_tmem_ld8(dacc + kTok + col, dhi);
                     tmem_wait_ld();
 #pragma unroll
-                    for (int jj = 0; jj < 4; ++jj)
-#pragma unroll
-                        for (int t = 0; t < 8; ++t) weighted[t] += sc[4 * jh + jj] * int(D[jj][t]);
+                    for (int t = 0; t < 8; ++t) weighted[tc + t] = int(dlo[t]) + 256 * int(dhi[t]);
                 }
-            } else {
-                uint32_t dlo[8], dhi[8];
-                pl_tmem_ld8(dacc, dlo);
-                pl_tmem_ld8(dacc + kTok, dhi);
-                tmem_wait_ld();
-#pragma unroll
-                for (int t = 0; t < 8; ++t) weighted[t] = int(dlo[t]) + 256 * int(dhi[t]);
             }
             fence_before_sync();
             __syncwarp();
             if (lane == 0) mbar_arrive(&acc_empty[a]);
-            const float4 s0 = *reinterpret_cast<const float4 *>(scl + b * kTok + 8 * g);
-            const float4 s1 = *reinterpret_cast<const float4 *>(scl + b * kTok + 8 * g + 4);
-            const float as[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
 #pragma unroll
-            for (int t = 0; t < 8; ++t) {
-                const float d = pl_half(cur.x) * as[t];
-                float term;
-                if constexpr (kQ) {
-                    const uint4 ps = psum[b * kTok + 8 * g + t];
-                    int minimum = __dp2a_lo(int(ps.x), int(mins0), 0);
-                    minimum = __dp2a_hi(int(ps.y), int(mins0), minimum);
-                    minimum = __dp2a_lo(int(ps.z), int(mins1), minimum);
-                    minimum = __dp2a_hi(int(ps.w), int(mins1), minimum);
-                    const float dmin = pl_half(cur.x >> 16) * as[t];
-                    term = d * float(weighted[t]) - dmin * float(minimum);
-                } else {
-                    term = d * float(weighted[t]);
+            for (int tc = 0; tc < kTPW; tc += 8) {
+                const float4 s0 = *reinterpret_cast<const float4 *>(scl + b * kTok + tg0 + tc);
+                const float4 s1 = *reinterpret_cast<const float4 *>(scl + b * kTok + tg0 + tc + 4);
+                const float as[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+#pragma unroll
+                for (int t = 0; t < 8; ++t) {
+                    const float d = pl_half(cur.x) * as[t];
+                    float term;
+                    if constexpr (kQ) {
+                        const uint4 ps = psum[b * kTok + tg0 + tc + t];
+                        int minimum = __dp2a_lo(int(ps.x), int(mins0), 0);
+                        minimum = __dp2a_hi(int(ps.y), int(mins0), minimum);
+                        minimum = __dp2a_lo(int(ps.z), int(mins1), minimum);
+                        minimum = __dp2a_hi(int(ps.w), int(mins1), minimum);
+                        const float dmin = pl_half(cur.x >> 16) * as[t];
+                        term = d * float(weighted[tc + t]) - dmin * float(minimum);
+                    } else {
+                        term = d * float(weighted[tc + t]);
+                    }
+                    total[tc + t] = total[tc + t] + term;
                 }
-                total[t] = total[t] + term;
             }
         }
         if (!ok) {
@@ -474,18 +492,23 @@ __global__ void __launch_bounds__(kPlThreads, 1)
                 set_error(p.err, kDevErrTimeout);
             }
         } else if (row0 + int(r) < p.rows) {
-            EpilogueIn ein[8];
+            // In chunks of 8 tokens: all the chunk's epilogue inputs first, then
+            // its outputs.
 #pragma unroll
-            for (int t = 0; t < 8; ++t) {
-                const int tok = tok0 + 8 * g + t;
-                if (tok < p.batch) ein[t] = proj_epilogue_load(p.epi, p.rows, tok, int(row0 + r));
-            }
+            for (int tc = 0; tc < kTPW; tc += 8) {
+                EpilogueIn ein[8];
 #pragma unroll
-            for (int t = 0; t < 8; ++t) {
-                const int tok = tok0 + 8 * g + t;
-                if (tok < p.batch)
-                    p.out[size_t(tok) * p.out_ld + row0 + r] =
-                        proj_epilogue_apply(p.epi, ein[t], p.rows, tok, int(row0 + r), total[t]);
+                for (int t = 0; t < 8; ++t) {
+                    const int tok = tok0 + tg0 + tc + t;
+                    if (tok < p.batch) ein[t] = proj_epilogue_load(p.epi, p.rows, tok, int(row0 + r));
+                }
+#pragma unroll
+                for (int t = 0; t < 8; ++t) {
+                    const int tok = tok0 + tg0 + tc + t;
+                    if (tok < p.batch)
+                        p.out[size_t(tok) * p.out_ld + row0 + r] =
+                            proj_epilogue_apply(p.epi, ein[t], p.rows, tok, int(row0 + r), total[tc + t]);
+                }
             }
         }
     }
@@ -623,9 +646,11 @@ cudaError_t launch_proj_planes(const ProjWeight &w, const float *x, int batch, f
     if (!w.planes || w.width % 256) return cudaErrorInvalidValue;
     const int nblk = int(w.width / 256);
     // 16-token tiles when the batch fits one, or when twice the 32-token grid
-    // still fits the SMs this launch may take.
+    // still fits the SMs this launch may take; 64-token tiles for prompt-sized
+    // batches (when their stages fit); else 32.
     const int tiles = int((w.rows + kPlRows - 1) / kPlRows);
-    const int tok = batch <= 16 || 2 * tiles * ((batch + 31) / 32) <= sm_budget ? 16 : 32;
+    int tok = batch <= 16 || 2 * tiles * ((batch + 31) / 32) <= sm_budget ? 16 : 32;
+    if (batch >= kPlLargeBatch && pl_stages_for(w.type, nblk, 64) > 0) tok = 64;
     const int stages = pl_stages_for(w.type, nblk, tok);
     if (stages == 0) return cudaErrorInvalidValue;
     cudaError_t e = cudaSuccess;
@@ -655,6 +680,13 @@ cudaError_t launch_proj_planes(const ProjWeight &w, const float *x, int batch, f
             case Q38_GGML_Q4_K: return launch_planes_typed<Q38_GGML_Q4_K, 16>(ma, p, stream);
             case Q38_GGML_Q5_K: return launch_planes_typed<Q38_GGML_Q5_K, 16>(ma, p, stream);
             default: return launch_planes_typed<Q38_GGML_Q6_K, 16>(ma, p, stream);
+        }
+    }
+    if (tok == 64) {
+        switch (w.type) {
+            case Q38_GGML_Q4_K: return launch_planes_typed<Q38_GGML_Q4_K, 64>(ma, p, stream);
+            case Q38_GGML_Q5_K: return launch_planes_typed<Q38_GGML_Q5_K, 64>(ma, p, stream);
+            default: return launch_planes_typed<Q38_GGML_Q6_K, 64>(ma, p, stream);
         }
     }
     switch (w.type) {

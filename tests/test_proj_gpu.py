@@ -95,13 +95,14 @@ PLANE_CASES = [(12, 10240, HIDDEN), (13, 6144, HIDDEN), (14, HIDDEN, 6144), (12,
 def test_project_planes_bitwise(cuda_ctx, oracle_lib, ggml_type, rows, width):
     """Projections of 9+ tokens from the weight's integer planes
     (q38_weight_build_planes) equal the reference's integer dot bit for bit:
-    full and ragged 32-token tiles, ragged 128-row tiles, one to 36 blocks."""
+    full and ragged 16-, 32- and 64-token tiles, ragged 128-row tiles, one to
+    36 blocks."""
     from q38attn import synth
     g = synth.rng(300 + ggml_type + rows)
     data = synth.quant_weight(g, ggml_type, rows, width)
     w = cuda_ctx.weight(ggml_type, width, rows, data).build_planes()
     w.build_planes()  # a second call keeps the planes it has
-    for batch in (9, 32, 40, 71):
+    for batch in (9, 32, 40, 71, 300):  # 16-, 32- and (from 128 tokens) 64-token tiles
         x = synth.normal(g, (batch, width))
         x[0, :256] = 0.0  # an all-zero activation block (scale 0)
         got = _gpu_project(cuda_ctx, w, x)

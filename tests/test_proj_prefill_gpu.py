@@ -9,7 +9,8 @@ path, tests/test_proj_gpu.py) and q38_linear_prefill / q38_full_prefill
 (checked against the per-token oracle loop in tests/test_deltanet_prefill_gpu.py
 and tests/test_prefill_gpu.py) -- including the state they leave (conv and
 delta state, appended KV rows). Prompts of 100 tokens per sequence take the
-tensor-core projections (9+ tokens) and a ragged last DeltaNet chunk.
+tensor-core projections (9+ tokens) and a ragged last DeltaNet chunk; each
+test runs with and without the weights' integer planes.
 """
 from __future__ import annotations
 
@@ -21,9 +22,16 @@ pytestmark = pytest.mark.gpu
 HIDDEN = 5120
 
 
-def _weights(ctx, g, spec):
+def _weights(ctx, g, spec, planes=False):
+    """The layer's weights; with `planes`, the K-quant ones (Q4_K, Q5_K,
+    Q6_K) also get integer planes (q38_weight_build_planes)."""
     from q38attn import synth
-    return {k: ctx.weight(t, w, r, synth.quant_weight(g, t, r, w)) for k, (t, w, r) in spec.items()}
+    out = {k: ctx.weight(t, w, r, synth.quant_weight(g, t, r, w)) for k, (t, w, r) in spec.items()}
+    if planes:
+        for k, (t, _, _) in spec.items():
+            if t in (12, 13, 14):
+                out[k].build_planes()
+    return out
 
 
 def _project(ctx, w, x):
@@ -33,7 +41,8 @@ def _project(ctx, w, x):
     return out
 
 
-def test_linear_attention_prefill_equals_its_steps(cuda_ctx):
+@pytest.mark.parametrize("planes", [False, True])
+def test_linear_attention_prefill_equals_its_steps(cuda_ctx, planes):
     import torch
     from q38attn import synth
     g = synth.rng(500)
@@ -42,7 +51,7 @@ def test_linear_attention_prefill_equals_its_steps(cuda_ctx):
     cuda_ctx.bind_linear_layer(layer, lw["conv1d"], lw["dt_bias"], lw["ssm_a"], lw["ssm_norm"])
     w = _weights(cuda_ctx, g, {"qkv": (12, HIDDEN, 10240), "z": (13, HIDDEN, 6144),
                                "beta": (8, HIDDEN, 48), "alpha": (0, HIDDEN, 48),
-                               "out": (14, 6144, HIDDEN)})
+                               "out": (14, 6144, HIDDEN)}, planes)
     init = [synth.linear_state(g) for _ in range(nseq)]
     norm = torch.from_numpy(synth.normal(g, (nseq, count, HIDDEN))).cuda()
     states = []
@@ -78,7 +87,8 @@ def test_linear_attention_prefill_equals_its_steps(cuda_ctx):
         x.close()
 
 
-def test_full_attention_prefill_equals_its_steps(cuda_ctx):
+@pytest.mark.parametrize("planes", [False, True])
+def test_full_attention_prefill_equals_its_steps(cuda_ctx, planes):
     """Two calls in a row: a 100-token prompt at position 0, then 100 more
     tokens at position 100 over the cached rows."""
     import q38attn
@@ -89,7 +99,7 @@ def test_full_attention_prefill_equals_its_steps(cuda_ctx):
     fw = synth.full_weights(g)
     cuda_ctx.bind_full_layer(layer, fw["q_norm"], fw["k_norm"])
     w = _weights(cuda_ctx, g, {"q": (12, HIDDEN, 12288), "k": (14, HIDDEN, 1024),
-                               "v": (8, HIDDEN, 1024), "out": (12, 6144, HIDDEN)})
+                               "v": (8, HIDDEN, 1024), "out": (12, 6144, HIDDEN)}, planes)
     states = []
     for _ in range(2):
         st = cuda_ctx.state(nseq, ctx_len, full_slots=1, linear_slots=0, kv_dtype=q38attn.Q38_KV_BF16)
