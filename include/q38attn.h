@@ -559,9 +559,11 @@ int q38_project(q38_ctx *ctx, const q38_weight *w, int batch, const float *input
 int q38_project_host(q38_ctx *ctx, const q38_weight *w, int batch, const float *input,
                      float *output);
 /* Sizes the context's projection scratch (the quantized input of the
- * tensor-core path) for `batch` tokens of `width` inputs (a multiple of 256),
- * so that later q38_project / *_attention_decode calls allocate nothing.
- * Call it before any stream capture. */
+ * tensor-core path, and the partial sums of the chunked f32-input form that
+ * 9+ tokens over F32/F16/BF16/Q8_0 weights of up to 128 rows take) for
+ * `batch` tokens of `width` inputs (a multiple of 256), so that later
+ * q38_project / *_attention_decode calls allocate nothing. Call it before
+ * any stream capture. */
 int q38_ctx_reserve_projection(q38_ctx *ctx, int batch, int64_t width);
 
 /* The projections of one Gated DeltaNet layer (Q38Attention::Linear,

@@ -965,7 +965,142 @@ cudaError_t launch_f32(const ProjF32Params &p, cudaStream_t stream) {
     return cudaLaunchKernelEx(&cfg, proj_f32_kernel<T>, p);
 }
 
+// ---- f32-input projection of many tokens over few rows ---------------------
+// Batches of 9+ tokens over up to 128 rows (the 48-row DeltaNet gates): the
+// warp form above would stage each CTA's eight tokens whole (160 KB for a
+// 5120-wide row) for one row, re-reading the batch from L2 once per row. Here
+// a CTA takes one 128-value chunk of the width for 64 rows x 32 tokens: the
+// tokens' values transposed ([k][t]) and the rows' weights decoded to f32
+// ([k][row]) in shared memory, each thread a 4-row x 4-token register tile of
+// fma chains over the chunk. The chunks' partial sums go to a workspace and a
+// second kernel adds them in chunk order, then applies the epilogue.
+// (Agrees with the reference's sequential fma chain to rounding, as the warp
+// form does.)
+constexpr int kTileK = 128, kTileRows = 64, kTileTok = 32, kTileThreads = 128;
+constexpr int kTileXStride = kTileTok + 4;   // floats per k of the token tile (16-byte rows)
+constexpr int kTileWStride = kTileRows + 4;  // floats per k of the weight tile
+constexpr uint32_t kTileSmem = uint32_t(kTileK) * (kTileXStride + kTileWStride) * sizeof(float);
+constexpr int kTileOut = kTileRows * kTileTok;  // partial sums per CTA
+
+struct ProjTileParams {
+    const uint8_t *w;
+    const float *x;  // [batch][width]
+    float *part;     // [chunk][row block][token block][kTileTok][kTileRows]
+    float *out;
+    long out_ld;
+    ProjEpilogue epi;
+    int rows, width, rb, batch, chunks;
+};
+
+template <int T>
+__global__ void __launch_bounds__(kTileThreads) proj_f32_tile_kernel(ProjTileParams p) {
+    extern __shared__ __align__(16) float tile_smem[];
+    float *xs = tile_smem;                          // [kTileK][kTileXStride]
+    float *ws = tile_smem + kTileK * kTileXStride;  // [kTileK][kTileWStride]
+    const int chunk = blockIdx.x, r0 = blockIdx.y * kTileRows, t0 = blockIdx.z * kTileTok;
+    const int k0 = chunk * kTileK, tid = threadIdx.x;
+    // The weights are constant: decoded before the wait for the kernel that
+    // wrote x. Lanes run over rows, so the transposed stores hit distinct banks.
+    for (int i = tid; i < kTileRows * (kTileK / 4); i += kTileThreads) {
+        const int r = i % kTileRows, kq = (i / kTileRows) * 4;
+        float wv[4] = {0.f, 0.f, 0.f, 0.f};
+        if (r0 + r < p.rows) weights4<T>(p.w + size_t(r0 + r) * p.rb, k0 + kq, wv);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) ws[(kq + e) * kTileWStride + r] = wv[e];
+    }
+    pdl_wait_primary();
+    pdl_launch_dependents();
+    for (int i = tid; i < kTileTok * (kTileK / 4); i += kTileThreads) {
+        const int t = i % kTileTok, kq = (i / kTileTok) * 4;
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (t0 + t < p.batch) v = *reinterpret_cast<const float4 *>(p.x + size_t(t0 + t) * p.width + k0 + kq);
+        xs[(kq + 0) * kTileXStride + t] = v.x;
+        xs[(kq + 1) * kTileXStride + t] = v.y;
+        xs[(kq + 2) * kTileXStride + t] = v.z;
+        xs[(kq + 3) * kTileXStride + t] = v.w;
+    }
+    __syncthreads();
+    // Thread: rows 4 rq .. +3, tokens 4 tq .. +3.
+    const int rq = tid & 15, tq = tid >> 4;
+    float acc[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
+#pragma unroll 4
+    for (int k = 0; k < kTileK; ++k) {
+        const float4 w4 = *reinterpret_cast<const float4 *>(ws + k * kTileWStride + 4 * rq);
+        const float4 x4 = *reinterpret_cast<const float4 *>(xs + k * kTileXStride + 4 * tq);
+        const float wr[4] = {w4.x, w4.y, w4.z, w4.w}, xt[4] = {x4.x, x4.y, x4.z, x4.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(wr[i], xt[j], acc[i][j]);
+    }
+    float *part = p.part + ((size_t(chunk) * gridDim.y + blockIdx.y) * gridDim.z + blockIdx.z) * kTileOut;
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+        *reinterpret_cast<float4 *>(part + (4 * tq + j) * kTileRows + 4 * rq) =
+            make_float4(acc[0][j], acc[1][j], acc[2][j], acc[3][j]);
+}
+
+// Output (t, row) = the chunks' partial sums added in chunk order, then the
+// epilogue. Grid: (kTileOut / 256, row blocks, token blocks).
+__global__ void __launch_bounds__(256) proj_f32_tile_reduce_kernel(ProjTileParams p) {
+    const int i = blockIdx.x * 256 + threadIdx.x;
+    const int tl = i / kTileRows, rl = i % kTileRows;
+    const int row = blockIdx.y * kTileRows + rl, t = blockIdx.z * kTileTok + tl;
+    pdl_wait_primary();
+    pdl_launch_dependents();
+    if (row >= p.rows || t >= p.batch) return;
+    const size_t stride = size_t(gridDim.y) * gridDim.z * kTileOut;
+    const float *part = p.part + (size_t(blockIdx.y) * gridDim.z + blockIdx.z) * kTileOut + i;
+    float v = part[0];
+    for (int c = 1; c < p.chunks; ++c) v += part[size_t(c) * stride];
+    p.out[size_t(t) * p.out_ld + row] = proj_epilogue(p.epi, p.rows, t, row, v);
+}
+
+template <int T>
+cudaError_t launch_f32_tile(const ProjTileParams &p, cudaStream_t stream) {
+    static bool attr_set[kMaxDevices] = {};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev >= kMaxDevices || !attr_set[dev]) {
+        e = cudaFuncSetAttribute(proj_f32_tile_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 int(kTileSmem));
+        if (e != cudaSuccess) return e;
+        if (dev < kMaxDevices) attr_set[dev] = true;
+    }
+    const dim3 blocks((p.rows + kTileRows - 1) / kTileRows, (p.batch + kTileTok - 1) / kTileTok);
+    cudaLaunchConfig_t cfg{};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.gridDim = dim3(p.chunks, blocks.x, blocks.y);
+    cfg.blockDim = dim3(kTileThreads);
+    cfg.dynamicSmemBytes = kTileSmem;
+    cfg.stream = stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if ((e = cudaLaunchKernelEx(&cfg, proj_f32_tile_kernel<T>, p)) != cudaSuccess) return e;
+    cfg.gridDim = dim3(kTileOut / 256, blocks.x, blocks.y);
+    cfg.blockDim = dim3(256);
+    cfg.dynamicSmemBytes = 0;
+    return cudaLaunchKernelEx(&cfg, proj_f32_tile_reduce_kernel, p);
+}
+
 }  // namespace
+
+size_t proj_f32_tile_part_bytes(int64_t rows, int64_t width, int batch) {
+    return size_t((rows + kTileRows - 1) / kTileRows) * size_t((batch + kTileTok - 1) / kTileTok) *
+           size_t(width / kTileK) * kTileOut * sizeof(float);
+}
+
+bool proj_f32_takes_tile(int type, int64_t rows, int64_t width, int batch) {
+    return !proj_is_q8k_type(type) && batch >= 9 && rows <= kProjTileMaxRows && width % kTileK == 0 &&
+           width >= kTileK;
+}
 
 bool proj_is_q8k_type(int type) {
     return type == Q38_GGML_Q2_K || type == Q38_GGML_Q3_K || type == Q38_GGML_Q4_K ||
@@ -1101,7 +1236,29 @@ cudaError_t launch_proj_q8k(const ProjWeight &w, const float *x, int batch, floa
 }
 
 cudaError_t launch_proj_f32(const ProjWeight &w, const float *x, int batch, float *out,
-                            long out_ld, cudaStream_t stream, const ProjEpilogue &epi) {
+                            long out_ld, cudaStream_t stream, const ProjEpilogue &epi, float *part) {
+    if (part && proj_f32_takes_tile(w.type, w.rows, w.width, batch)) {
+        if (reinterpret_cast<uintptr_t>(x) % 16) return cudaErrorInvalidValue;
+        ProjTileParams t{};
+        t.w = static_cast<const uint8_t *>(w.data);
+        t.x = x;
+        t.part = part;
+        t.out = out;
+        t.out_ld = out_ld;
+        t.epi = epi;
+        t.rows = int(w.rows);
+        t.width = int(w.width);
+        t.rb = int(w.row_bytes);
+        t.batch = batch;
+        t.chunks = int(w.width / kTileK);
+        switch (w.type) {
+            case Q38_GGML_F32: return launch_f32_tile<Q38_GGML_F32>(t, stream);
+            case Q38_GGML_F16: return launch_f32_tile<Q38_GGML_F16>(t, stream);
+            case Q38_GGML_BF16: return launch_f32_tile<Q38_GGML_BF16>(t, stream);
+            case Q38_GGML_Q8_0: return launch_f32_tile<Q38_GGML_Q8_0>(t, stream);
+            default: return cudaErrorInvalidValue;
+        }
+    }
     ProjF32Params p{};
     p.epi = epi;
     p.w = static_cast<const uint8_t *>(w.data);

@@ -53,6 +53,8 @@ struct q38_ctx {
     std::map<int, q38::LinearWeights> linear;
     void *proj_scratch = nullptr;   // quantized activations of the tensor-core projections
     size_t proj_scratch_bytes = 0;
+    float *proj_part = nullptr;     // partial sums of the chunked f32-input projections
+    size_t proj_part_bytes = 0;
 };
 
 struct q38_state {

@@ -143,8 +143,15 @@ cudaError_t launch_proj_planes(const ProjWeight &w, const float *x, int batch, f
                                int *err, void *scratch, cudaStream_t stream, const ProjEpilogue &epi = {},
                                bool prequantized = false, int sm_budget = 148);
 
+// f32-input projections (F32 / F16 / BF16 / Q8_0). part: a workspace of
+// proj_f32_tile_part_bytes for the chunked form that batches of 9+ tokens
+// over up to kProjTileMaxRows rows take (proj_f32_takes_tile), or null for
+// the warp form.
+constexpr int kProjTileMaxRows = 128;
+bool proj_f32_takes_tile(int type, int64_t rows, int64_t width, int batch);
+size_t proj_f32_tile_part_bytes(int64_t rows, int64_t width, int batch);
 cudaError_t launch_proj_f32(const ProjWeight &w, const float *x, int batch, float *out, long out_ld,
-                            cudaStream_t stream, const ProjEpilogue &epi = {});
+                            cudaStream_t stream, const ProjEpilogue &epi = {}, float *part = nullptr);
 
 }  // namespace q38
 

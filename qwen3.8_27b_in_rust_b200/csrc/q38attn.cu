@@ -418,6 +418,7 @@ int q38_ctx_destroy(q38_ctx *ctx) {
         for (auto &kv : ctx->full) free_full(kv.second);
         for (auto &kv : ctx->linear) free_linear(kv.second);
         cudaFree(ctx->proj_scratch);
+        cudaFree(ctx->proj_part);
     }
     delete ctx;
     return Q38_OK;

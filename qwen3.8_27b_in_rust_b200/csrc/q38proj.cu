@@ -63,6 +63,25 @@ int reserve_scratch(q38_ctx *ctx, int batch, int64_t width) {
     return Q38_OK;
 }
 
+// Grows the context's workspace for the chunked f32-input projections' partial
+// sums (the same rules as the scratch above).
+int reserve_part(q38_ctx *ctx, size_t need) {
+    if (need <= ctx->proj_part_bytes) return Q38_OK;
+    if (ctx->proj_part) {
+        cudaError_t e = cudaDeviceSynchronize();
+        if (e != cudaSuccess) return proj_cuda_fail(e, "projection workspace resize");
+        cudaFree(ctx->proj_part);
+        ctx->proj_part = nullptr;
+        ctx->proj_part_bytes = 0;
+    }
+    void *p = nullptr;
+    cudaError_t e = cudaMalloc(&p, need);
+    if (e != cudaSuccess) return proj_cuda_fail(e, "projection workspace allocation");
+    ctx->proj_part = static_cast<float *>(p);
+    ctx->proj_part_bytes = need;
+    return Q38_OK;
+}
+
 // One projection. K-quant weights: a batch of kProjMmaMinBatch or more tokens
 // over Q4_K / Q5_K runs on the tensor cores (the input quantized into the
 // context's scratch first); otherwise the integer GEMV quantizes the input
@@ -90,8 +109,14 @@ int project_device(q38_ctx *ctx, const q38_weight *w, int batch, const float *in
                                        epi, prequantized);
     } else if (q38::proj_is_q8k_type(w->w.type))
         e = q38::launch_proj_q8k(w->w, input, batch, out, long(w->w.rows), err, ctx->sm_count, s, epi);
-    else
-        e = q38::launch_proj_f32(w->w, input, batch, out, long(w->w.rows), s, epi);
+    else {
+        float *part = nullptr;
+        if (q38::proj_f32_takes_tile(w->w.type, w->w.rows, w->w.width, batch)) {
+            if (int rc = reserve_part(ctx, q38::proj_f32_tile_part_bytes(w->w.rows, w->w.width, batch))) return rc;
+            part = ctx->proj_part;
+        }
+        e = q38::launch_proj_f32(w->w, input, batch, out, long(w->w.rows), s, epi, part);
+    }
     if (e != cudaSuccess) return proj_cuda_fail(e, "projection launch");
     return Q38_OK;
 }
@@ -191,7 +216,10 @@ int q38_ctx_reserve_projection(q38_ctx *ctx, int batch, int64_t width) {
         return proj_fail(Q38_ERR_ARG, "bad projection reservation (%d x %lld)", batch,
                          static_cast<long long>(width));
     Guard guard(ctx->device);
-    return reserve_scratch(ctx, batch, width);
+    if (int rc = reserve_scratch(ctx, batch, width)) return rc;
+    // The chunked f32-input form's workspace, for weights of up to
+    // kProjTileMaxRows rows at this width.
+    return reserve_part(ctx, q38::proj_f32_tile_part_bytes(q38::kProjTileMaxRows, width, batch));
 }
 
 int q38_quantize_q8_k(q38_ctx *ctx, int batch, int64_t width, const float *input, void *blocks,

@@ -136,6 +136,24 @@ def test_project_f32_input_types(cuda_ctx, oracle_lib, ggml_type):
     w.close()
 
 
+@pytest.mark.parametrize("ggml_type", [0, 1, 30, 8])
+def test_project_f32_input_many_tokens(cuda_ctx, oracle_lib, ggml_type):
+    """9+ tokens over up to 128 rows (the DeltaNet gates' shape) take the
+    chunked form: 128-value chunks of 64 rows x 32 tokens, partial sums added
+    in chunk order. Ragged row and token blocks, two of each."""
+    from q38attn import synth
+    g = synth.rng(210 + ggml_type)
+    for rows, width in ((48, HIDDEN), (100, 1024)):
+        data = synth.quant_weight(g, ggml_type, rows, width)
+        w = cuda_ctx.weight(ggml_type, width, rows, data)
+        for batch in (9, 32, 40):
+            x = synth.normal(g, (batch, width))
+            got = _gpu_project(cuda_ctx, w, x)
+            want = oracle_lib.project(ggml_type, data, rows, width, x)
+            assert relative_error(got, want) < 1e-4
+        w.close()
+
+
 def test_project_host_matches_device(cuda_ctx):
     from q38attn import synth
     g = synth.rng(301)
