@@ -420,26 +420,45 @@ def run_split_sequence(args, ctx, q38attn, torch, dist, rank: int, world: int,
         dist.barrier()
     stream = torch.cuda.current_stream()
 
-    def one(i):
+    def one(i, s):
         key = keys[i:i + 1]
         if dec is not None:
-            dec.step(qg, key, val, pos[i:i + 1], out, cap - 1, stream=stream)
+            dec.step(qg, key, val, pos[i:i + 1], out, cap - 1, stream=s)
         else:
             ctx.full_decode(st, FULL_LAYER, qg, key, val, pos[i:i + 1], out,
-                            max_position=P + i, stream=stream)
+                            max_position=P + i, stream=s)
 
     for i in range(3):
-        one(i)
+        one(i, stream)
     torch.cuda.synchronize()
+    # The timed tokens as one CUDA graph (one GPU, or the peer-memory exchange,
+    # whose epoch counter lives on the device): a token's three launches take
+    # the host ~24 us to issue, more than a small shard's kernels run. The NCCL
+    # transport stays eager.
+    graph = None
+    if dec is None or transport == "p2p":
+        graph = torch.cuda.CUDAGraph()
+        side = torch.cuda.Stream()
+        side.wait_stream(stream)
+        with torch.cuda.stream(side), torch.cuda.graph(graph, stream=side):
+            for i in range(args.split_steps):
+                one(3 + i, side)
+        stream.wait_stream(side)
+        graph.replay()  # warm
+        torch.cuda.synchronize()
     if dist is not None:
         dist.barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
-    for i in range(args.split_steps):
-        one(3 + i)
+    if graph is not None:
+        graph.replay()
+    else:
+        for i in range(args.split_steps):
+            one(3 + i, stream)
     e1.record(stream)
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / args.split_steps
+    del graph
     if st.errors():
         raise RuntimeError("device error bits set during split-sequence decode")
     if dec is not None:
@@ -907,7 +926,8 @@ def run_ours(args) -> None:
                 "workload": (f"config3 split-sequence: 1 sequence, {args.split_context} cached "
                              f"bf16 positions sharded over {world} GPU(s); per-shard partials "
                              "exchanged over peer memory inside the merge kernel "
-                             "(q38_full_decode_split_p2p), LSE merge"),
+                             "(q38_full_decode_split_p2p), LSE merge; the timed tokens "
+                             "replayed as one CUDA graph"),
                 "scaling": "strong", "ms_per_token": split_ms, "tok_s": 1e3 / split_ms,
                 "kv_gbs": kv_bytes / (split_ms * 1e-3) / 1e9,
                 "hbm_frac_per_gpu": kv_bytes / world / (split_ms * 1e-3) / 1e9 / peak,
@@ -915,7 +935,7 @@ def run_ours(args) -> None:
             if split_nccl:
                 line["split_sequence"]["nccl_transport"] = {
                     "what": "the same step with an ncclAllGather between the shard kernels and "
-                            "the merge (q38_full_decode_split)",
+                            "the merge (q38_full_decode_split), issued token by token",
                     "ms_per_token": split_nccl_ms, "tok_s": 1e3 / split_nccl_ms}
         if lin_prefill:
             flops = linear_prefill_flops(args.prefill_batch, args.prefill_len)

@@ -75,6 +75,7 @@ struct PrepParams {
     const float *q_norm, *k_norm;
     int context_length, heads, kv_heads, max_position, pos_offset, sharded;
     float theta_scale, eps;
+    uint32_t *p2p_epoch;  // peer-memory exchange: the call counter this kernel advances, or null
 };
 
 // A sequence at global position pos appends its K/V row at local cache row
@@ -92,6 +93,11 @@ __device__ __forceinline__ bool position_ok(int pos, int pos_offset, int context
 template <typename KV>
 __global__ void __launch_bounds__(kAttnHeadDim) attn_decode_prep_kernel(PrepParams p) {
     pdl_launch_dependents();
+    // This call's exchange epoch. The kernel is launched in stream order, so
+    // the previous call's merge, the last reader of the counter, has finished;
+    // this call's merge reads it after waiting for the split kernel, which
+    // waited for this kernel.
+    if (p.p2p_epoch && blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) *p.p2p_epoch += 1u;
     __shared__ double red[32];
     __shared__ float cs[32], sn[32];
     __shared__ float xs[kAttnHeadDim];
@@ -756,11 +762,11 @@ struct MergeParams {
     int merge_ctas;      // CTAs (one cluster) per (head, sequence)
     // Split-sequence exchange over peer memory (p2p_nranks > 0; see
     // p2p_exchange_merge): every rank's exchange buffer, this rank's index,
-    // the buffers' batch (the state's), the call's epoch, the wait limit and
+    // the buffers' batch (the state's), the epoch counter, the wait limit and
     // the error word.
     float *const *p2p_peers;
     int p2p_rank, p2p_nranks, p2p_batch;
-    uint32_t p2p_epoch;
+    const uint32_t *p2p_epoch;  // device counter, advanced by this call's prep kernel
     uint64_t wait_ns;
     int *err;
 };
@@ -818,25 +824,26 @@ __device__ void p2p_exchange_merge(const MergeParams &p, int h, int b, float ot,
                                    bool has_rows) {
     const int d = threadIdx.x;
     const int R = p.p2p_nranks, H = p.heads, B = p.p2p_batch;
-    const int par = int(p.p2p_epoch & 1u);
+    const uint32_t epoch = *reinterpret_cast<const volatile uint32_t *>(p.p2p_epoch);
+    const int par = int(epoch & 1u);
     auto slot = [&](int r) { return (((size_t(par) * R + r) * B + b) * H + h) * (kAttnHeadDim + 2); };
     const float o_send = has_rows ? ot : 0.f;
     for (int r = 0; r < R; ++r) {
         unsigned long long *dst =
             reinterpret_cast<unsigned long long *>(p.p2p_peers[r]) + slot(p.p2p_rank);
-        st_word_sys(dst + d, o_send, p.p2p_epoch);
-        if (d < 2) st_word_sys(dst + kAttnHeadDim + d, d == 0 ? m : lt, p.p2p_epoch);
+        st_word_sys(dst + d, o_send, epoch);
+        if (d < 2) st_word_sys(dst + kAttnHeadDim + d, d == 0 ? m : lt, epoch);
     }
     const unsigned long long *mine = reinterpret_cast<const unsigned long long *>(p.p2p_peers[p.p2p_rank]);
     bool ok = true;
     float mm = -INFINITY;
     for (int r = 0; r < R; ++r)
-        mm = fmaxf(mm, wait_word_sys(mine + slot(r) + kAttnHeadDim, p.p2p_epoch, p.wait_ns, &ok));
+        mm = fmaxf(mm, wait_word_sys(mine + slot(r) + kAttnHeadDim, epoch, p.wait_ns, &ok));
     float lsum = 0.f, osum = 0.f;
     for (int r = 0; r < R && ok; ++r) {
-        const float mr = wait_word_sys(mine + slot(r) + kAttnHeadDim, p.p2p_epoch, p.wait_ns, &ok);
-        const float lr = wait_word_sys(mine + slot(r) + kAttnHeadDim + 1, p.p2p_epoch, p.wait_ns, &ok);
-        const float orr = wait_word_sys(mine + slot(r) + d, p.p2p_epoch, p.wait_ns, &ok);
+        const float mr = wait_word_sys(mine + slot(r) + kAttnHeadDim, epoch, p.wait_ns, &ok);
+        const float lr = wait_word_sys(mine + slot(r) + kAttnHeadDim + 1, epoch, p.wait_ns, &ok);
+        const float orr = wait_word_sys(mine + slot(r) + d, epoch, p.wait_ns, &ok);
         if (mr == -INFINITY) continue;  // a shard without visible rows
         const float w = expf(mr - mm);
         lsum += w * lr;
@@ -1061,7 +1068,7 @@ cudaError_t launch_typed(const AttnDecodeLaunch &a, int sm_count, cudaStream_t s
     PrepParams pp{a.q_and_gate, a.key,      a.value,        a.positions,  a.kcache,
                   a.vcache,     a.qprep,    a.err,          a.q_norm,     a.k_norm,
                   a.context_length, a.heads, a.kv_heads,    a.max_position, a.pos_offset,
-                  sharded,      a.theta_scale, a.eps};
+                  sharded,      a.theta_scale, a.eps, a.p2p_nranks > 0 ? a.p2p_epoch : nullptr};
     attn_decode_prep_kernel<KV>
         <<<dim3(a.heads + a.kv_heads, a.batch), kAttnHeadDim, 0, stream>>>(pp);
     cudaError_t e = cudaGetLastError();

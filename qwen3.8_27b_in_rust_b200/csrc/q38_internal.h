@@ -108,8 +108,11 @@ struct q38_state {
     void *p2p_buf = nullptr;          // this rank's exchange buffer (IPC-exported)
     int p2p_nranks = 0, p2p_rank = -1;
     std::vector<void *> p2p_opened;   // peers' buffers opened with cudaIpcOpenMemHandle
-    float **p2p_peers_dev = nullptr;  // device array [nranks] of the buffers' addresses
-    uint32_t p2p_epoch = 0;           // calls made so far (the next call's epoch is +1)
+    // Device array [64] of the buffers' addresses, then the exchange's epoch
+    // counter (a uint32: calls made so far, incremented on the device by each
+    // call's prep kernel, so the launches carry no per-call value and can be
+    // captured in a CUDA graph).
+    float **p2p_peers_dev = nullptr;
     // Side streams and their fork / join events (created with the state):
     // the DeltaNet prefill's per-group state passes and the layer-level
     // decode call's concurrent projections fork onto them and join back into
@@ -168,7 +171,7 @@ struct AttnDecodeLaunch {
     // kernel exchanges the shards' partials itself and writes `attention`.
     float *const *p2p_peers = nullptr;  // device array: every rank's exchange buffer
     int p2p_rank = 0, p2p_nranks = 0, p2p_batch = 0;
-    uint32_t p2p_epoch = 0;
+    uint32_t *p2p_epoch = nullptr;  // device counter of the exchange calls
 };
 cudaError_t launch_attn_decode(const AttnDecodeLaunch &a, int sm_count, cudaStream_t stream);
 cudaError_t launch_attn_merge_shards(const float *partials, int nparts, int batch, int heads,

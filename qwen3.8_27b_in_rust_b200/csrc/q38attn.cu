@@ -872,7 +872,6 @@ int q38_state_split_p2p_handle(q38_state *st, int nranks, void *handle) {
         Q38_CUDA(cudaMemset(st->p2p_buf, 0, bytes));  // flags start below every epoch
         st->p2p_nranks = nranks;
         st->p2p_rank = -1;
-        st->p2p_epoch = 0;
     }
     Q38_CUDA(cudaIpcGetMemHandle(static_cast<cudaIpcMemHandle_t *>(handle), st->p2p_buf));
     return Q38_OK;
@@ -905,11 +904,13 @@ int q38_state_split_p2p_open(q38_state *st, int rank, const void *handles) {
         st->p2p_opened.push_back(q);
         ptrs[size_t(r)] = static_cast<float *>(q);
     }
-    if (!st->p2p_peers_dev) Q38_CUDA(cudaMalloc(&st->p2p_peers_dev, 64 * sizeof(float *)));
+    // 64 addresses, then the epoch counter (zero: the first call's epoch is 1,
+    // above the zeroed exchange words).
+    if (!st->p2p_peers_dev) Q38_CUDA(cudaMalloc(&st->p2p_peers_dev, 64 * sizeof(float *) + 16));
+    Q38_CUDA(cudaMemset(st->p2p_peers_dev + 64, 0, sizeof(uint32_t)));
     Q38_CUDA(cudaMemcpy(st->p2p_peers_dev, ptrs.data(), size_t(nranks) * sizeof(float *),
                         cudaMemcpyHostToDevice));
     st->p2p_rank = rank;
-    st->p2p_epoch = 0;
     return Q38_OK;
 }
 
@@ -931,7 +932,7 @@ int q38_full_decode_split_p2p(q38_ctx *ctx, q38_state *st, int layer, int batch,
     a.p2p_rank = st->p2p_rank;
     a.p2p_nranks = st->p2p_nranks;
     a.p2p_batch = st->batch;
-    a.p2p_epoch = ++st->p2p_epoch;
+    a.p2p_epoch = reinterpret_cast<uint32_t *>(st->p2p_peers_dev + 64);
     DeviceGuard guard(ctx->device);
     cudaError_t e = q38::launch_attn_decode(a, ctx->sm_count, static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return cuda_fail(e, "split-sequence decode launch (peer exchange)");
