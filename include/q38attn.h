@@ -272,11 +272,15 @@ int q38_nccl_comm_destroy(void *comm);
  * Then every rank makes the same sequence of q38_full_decode_split_p2p calls
  * (same arguments as q38_full_decode_split, no communicator). The merge
  * kernel of each (sequence, head) stores this rank's partial straight into
- * every peer's buffer over NVLink, every value tagged with the call's epoch
- * (the state counts its calls), waits until its own buffer holds every
- * rank's values of this epoch, and merges: the exchange overlaps the other
- * heads' merging, and no library collective or second kernel runs. No kernel reads another GPU's
- * memory. A rank whose peers do not make the matching call gives up after
+ * every peer's buffer over NVLink, every value tagged with the call's epoch,
+ * waits until its own buffer holds every rank's values of this epoch, and
+ * merges: the exchange overlaps the other heads' merging, and no library
+ * collective or second kernel runs. No kernel reads another GPU's memory.
+ * The epoch is a counter in the state's device memory that each call
+ * advances on the device, so the call's launches depend on no host-side
+ * per-call value: a run of calls may be captured in a CUDA graph and
+ * replayed, every replay being further calls (every rank replaying the same
+ * number). A rank whose peers do not make the matching call gives up after
  * the bounded wait (1 s) and records Q38_DEVERR_TIMEOUT. Destroy the states
  * only after every rank has finished its last call. */
 #define Q38_IPC_HANDLE_BYTES 64
