@@ -1000,24 +1000,44 @@ __global__ void __launch_bounds__(kTileThreads) proj_f32_tile_kernel(ProjTilePar
     const int chunk = blockIdx.x, r0 = blockIdx.y * kTileRows, t0 = blockIdx.z * kTileTok;
     const int k0 = chunk * kTileK, tid = threadIdx.x;
     // The weights are constant: decoded before the wait for the kernel that
-    // wrote x. Lanes run over rows, so the transposed stores hit distinct banks.
-    for (int i = tid; i < kTileRows * (kTileK / 4); i += kTileThreads) {
-        const int r = i % kTileRows, kq = (i / kTileRows) * 4;
-        float wv[4] = {0.f, 0.f, 0.f, 0.f};
-        if (r0 + r < p.rows) weights4<T>(p.w + size_t(r0 + r) * p.rb, k0 + kq, wv);
+    // wrote x. Lanes run over rows, so the transposed stores hit distinct banks;
+    // the loops are unrolled so that every load is in flight before the first
+    // is used.
+    constexpr int kWIters = kTileRows * (kTileK / 4) / kTileThreads, kXIters = kTileTok * (kTileK / 4) / kTileThreads;
+    {
+        float wv[kWIters][4];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) ws[(kq + e) * kTileWStride + r] = wv[e];
+        for (int it = 0; it < kWIters; ++it) {
+            const int i = tid + it * kTileThreads, r = i % kTileRows, kq = (i / kTileRows) * 4;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) wv[it][e] = 0.f;
+            if (r0 + r < p.rows) weights4<T>(p.w + size_t(r0 + r) * p.rb, k0 + kq, wv[it]);
+        }
+#pragma unroll
+        for (int it = 0; it < kWIters; ++it) {
+            const int i = tid + it * kTileThreads, r = i % kTileRows, kq = (i / kTileRows) * 4;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) ws[(kq + e) * kTileWStride + r] = wv[it][e];
+        }
     }
     pdl_wait_primary();
     pdl_launch_dependents();
-    for (int i = tid; i < kTileTok * (kTileK / 4); i += kTileThreads) {
-        const int t = i % kTileTok, kq = (i / kTileTok) * 4;
-        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (t0 + t < p.batch) v = *reinterpret_cast<const float4 *>(p.x + size_t(t0 + t) * p.width + k0 + kq);
-        xs[(kq + 0) * kTileXStride + t] = v.x;
-        xs[(kq + 1) * kTileXStride + t] = v.y;
-        xs[(kq + 2) * kTileXStride + t] = v.z;
-        xs[(kq + 3) * kTileXStride + t] = v.w;
+    {
+        float4 xv[kXIters];
+#pragma unroll
+        for (int it = 0; it < kXIters; ++it) {
+            const int i = tid + it * kTileThreads, t = i % kTileTok, kq = (i / kTileTok) * 4;
+            xv[it] = t0 + t < p.batch ? *reinterpret_cast<const float4 *>(p.x + size_t(t0 + t) * p.width + k0 + kq)
+                                      : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int it = 0; it < kXIters; ++it) {
+            const int i = tid + it * kTileThreads, t = i % kTileTok, kq = (i / kTileTok) * 4;
+            xs[(kq + 0) * kTileXStride + t] = xv[it].x;
+            xs[(kq + 1) * kTileXStride + t] = xv[it].y;
+            xs[(kq + 2) * kTileXStride + t] = xv[it].z;
+            xs[(kq + 3) * kTileXStride + t] = xv[it].w;
+        }
     }
     __syncthreads();
     // Thread: rows 4 rq .. +3, tokens 4 tq .. +3.
@@ -1055,8 +1075,17 @@ __global__ void __launch_bounds__(256) proj_f32_tile_reduce_kernel(ProjTileParam
     if (row >= p.rows || t >= p.batch) return;
     const size_t stride = size_t(gridDim.y) * gridDim.z * kTileOut;
     const float *part = p.part + (size_t(blockIdx.y) * gridDim.z + blockIdx.z) * kTileOut + i;
+    // Eight chunks' partials loaded at a time, added in chunk order.
     float v = part[0];
-    for (int c = 1; c < p.chunks; ++c) v += part[size_t(c) * stride];
+    int c = 1;
+    for (; c + 8 <= p.chunks; c += 8) {
+        float t[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) t[u] = part[size_t(c + u) * stride];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) v += t[u];
+    }
+    for (; c < p.chunks; ++c) v += part[size_t(c) * stride];
     p.out[size_t(t) * p.out_ld + row] = proj_epilogue(p.epi, p.rows, t, row, v);
 }
 
