@@ -1003,7 +1003,8 @@ __global__ void __launch_bounds__(kTileThreads) proj_f32_tile_kernel(ProjTilePar
     // wrote x. Lanes run over rows, so the transposed stores hit distinct banks;
     // the loops are unrolled so that every load is in flight before the first
     // is used.
-    constexpr int kWIters = kTileRows * (kTileK / 4) / kTileThreads, kXIters = kTileTok * (kTileK / 4) / kTileThreads;
+    constexpr int kWIters = kTileRows * (kTileK / 4) / kTileThreads;
+    constexpr int kXIters = kTileTok * (kTileK / 4) / kTileThreads;
     {
         float wv[kWIters][4];
 #pragma unroll
@@ -1079,11 +1080,11 @@ __global__ void __launch_bounds__(256) proj_f32_tile_reduce_kernel(ProjTileParam
     float v = part[0];
     int c = 1;
     for (; c + 8 <= p.chunks; c += 8) {
-        float t[8];
+        float pv[8];
 #pragma unroll
-        for (int u = 0; u < 8; ++u) t[u] = part[size_t(c + u) * stride];
+        for (int u = 0; u < 8; ++u) pv[u] = part[size_t(c + u) * stride];
 #pragma unroll
-        for (int u = 0; u < 8; ++u) v += t[u];
+        for (int u = 0; u < 8; ++u) v += pv[u];
     }
     for (; c < p.chunks; ++c) v += part[size_t(c) * stride];
     p.out[size_t(t) * p.out_ld + row] = proj_epilogue(p.epi, p.rows, t, row, v);
