@@ -854,23 +854,23 @@ __device__ void p2p_exchange_merge(const MergeParams &p, int h, int b, float ot,
     p.attention[(size_t(b) * H + h) * kAttnHeadDim + d] = (osum / lsum) * sigmoidf_ref(gate);
 }
 
-__device__ __forceinline__ float ld_cluster_f32(uint32_t addr) {
-    float v;
-    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
-    return v;
+__device__ __forceinline__ void st_cluster_f32(uint32_t addr, float v) {
+    asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
 }
 
 // A cluster of merge_ctas CTAs (256 threads each) per (head, sequence); CTA g
 // of the cluster merges splits [g * per, (g + 1) * per). Inside a CTA all 8
 // warps read at once: warp w takes splits w, w + 8, ..., lane l dims
 // [8l, 8l + 8) of each (two 16-byte loads), and the 8 per-warp sums are added
-// in shared memory in warp order. The cluster's partials (o, m, l) are then
-// combined by CTA 0 through distributed shared memory (log-sum-exp), so a
-// single long sequence's hundreds of splits are read by many SMs at once.
+// in shared memory in warp order. Each CTA then stores its (o, m, l) into CTA
+// 0's shared memory (distributed shared memory, remote stores), and after one
+// cluster barrier CTA 0 combines them by log-sum-exp, so a single long
+// sequence's hundreds of splits are read by many SMs at once.
 __global__ void __launch_bounds__(kAttnHeadDim) attn_decode_merge_kernel(MergeParams p) {
     __shared__ float red[kWarps][kAttnHeadDim];
     __shared__ float lred[kWarps], mred[kWarps];
-    __shared__ float cta_o[kAttnHeadDim], cta_ml[2];
+    // CTA 0 of a cluster: every CTA's (o, m, l), pushed here by remote stores.
+    __shared__ float gath_o[8][kAttnHeadDim], gath_ml[8][2];
     const int h = blockIdx.x, b = blockIdx.y, tid = threadIdx.x;
     const int warp = tid >> 5, lane = tid & 31;
     const int G = p.merge_ctas;
@@ -916,31 +916,29 @@ __global__ void __launch_bounds__(kAttnHeadDim) attn_decode_merge_kernel(MergePa
     }
     if (G > 1) {
         // This CTA's (o, m, l) (m = -inf, l = o = 0 for a CTA without splits)
-        // to CTA 0 of the cluster.
-        cta_o[tid] = s1 > s0 ? ot : 0.f;
+        // stored straight into CTA 0's shared memory; one cluster barrier
+        // (release / acquire) orders the stores before CTA 0 reads them, and
+        // the other CTAs are done.
+        st_cluster_f32(sm100::cluster_addr(&gath_o[g][tid], 0u), s1 > s0 ? ot : 0.f);
         if (tid == 0) {
-            cta_ml[0] = m;
-            cta_ml[1] = lt;
+            st_cluster_f32(sm100::cluster_addr(&gath_ml[g][0], 0u), m);
+            st_cluster_f32(sm100::cluster_addr(&gath_ml[g][1], 0u), lt);
         }
         sm100::cluster_sync();
-        if (g == 0) {
-            float mm = -INFINITY;
-            for (int r = 0; r < G; ++r)
-                mm = fmaxf(mm, ld_cluster_f32(sm100::cluster_addr(&cta_ml[0], uint32_t(r))));
-            float lsum = 0.f, osum = 0.f;
-            for (int r = 0; r < G; ++r) {
-                const float mr = ld_cluster_f32(sm100::cluster_addr(&cta_ml[0], uint32_t(r)));
-                if (mr == -INFINITY) continue;
-                const float w = expf(mr - mm);
-                lsum += w * ld_cluster_f32(sm100::cluster_addr(&cta_ml[1], uint32_t(r)));
-                osum += w * ld_cluster_f32(sm100::cluster_addr(&cta_o[tid], uint32_t(r)));
-            }
-            m = mm;
-            lt = lsum;
-            ot = osum;
-        }
-        sm100::cluster_sync();  // every CTA's shared memory stays until CTA 0 has read it
         if (g != 0) return;
+        float mm = -INFINITY;
+        for (int r = 0; r < G; ++r) mm = fmaxf(mm, gath_ml[r][0]);
+        float lsum = 0.f, osum = 0.f;
+        for (int r = 0; r < G; ++r) {
+            const float mr = gath_ml[r][0];
+            if (mr == -INFINITY) continue;
+            const float w = expf(mr - mm);
+            lsum += w * gath_ml[r][1];
+            osum += w * gath_o[r][tid];
+        }
+        m = mm;
+        lt = lsum;
+        ot = osum;
     }
     const int d = tid;
     if (p.p2p_nranks > 0) {
