@@ -92,11 +92,14 @@ __device__ __forceinline__ bool position_ok(int pos, int pos_offset, int context
 
 template <typename KV>
 __global__ void __launch_bounds__(kAttnHeadDim) attn_decode_prep_kernel(PrepParams p) {
+    // Launched as a programmatic dependent so that it is resident when the
+    // previous kernel ends; nothing is read or written before that kernel has
+    // completed.
+    pdl_wait_primary();
     pdl_launch_dependents();
-    // This call's exchange epoch. The kernel is launched in stream order, so
-    // the previous call's merge, the last reader of the counter, has finished;
-    // this call's merge reads it after waiting for the split kernel, which
-    // waited for this kernel.
+    // This call's exchange epoch: the previous call's merge, the last reader
+    // of the counter, has finished; this call's merge reads it after waiting
+    // for the split kernel, which waited for this kernel.
     if (p.p2p_epoch && blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) *p.p2p_epoch += 1u;
     __shared__ double red[32];
     __shared__ float cs[32], sn[32];
@@ -403,10 +406,11 @@ __global__ void __launch_bounds__(kThreads, 2)
     sm100::fence_before_sync();
     __syncthreads();
     sm100::fence_after_sync();
-    // K1 (a full-dependency launch: everything before it has completed)
-    // writes only the sequence's new KV row, local row pos - pos_offset, and
-    // the prepared queries. A split whose rows end before that row fetches
-    // its first tiles now, while K1 runs; the split holding it waits first.
+    // K1 triggers this launch only after its own wait on the kernel before it,
+    // so everything before K1 has completed, and K1 writes only the
+    // sequence's new KV row, local row pos - pos_offset, and the prepared
+    // queries. A split whose rows end before that row fetches its first tiles
+    // now, while K1 runs; the split holding it waits first.
     const int new_row = pos - p.pos_offset;
     const bool early = new_row >= p.context_length || start + cnt <= new_row;
     if (early && threadIdx.x == 0) {
@@ -877,6 +881,7 @@ __global__ void __launch_bounds__(kAttnHeadDim) attn_decode_merge_kernel(MergePa
     const uint32_t g = G > 1 ? sm100::cluster_ctarank() : 0u;
     const int pos = p.positions[b];
     pdl_wait_primary();
+    pdl_launch_dependents();  // the next call's prep may become resident
     // Uniform over the cluster (one sequence), so every CTA of it returns here or none.
     if (!position_ok(pos, p.pos_offset, p.context_length, p.max_position, p.sharded)) return;
     const int n = local_rows(pos, p.pos_offset, p.context_length);
@@ -885,6 +890,21 @@ __global__ void __launch_bounds__(kAttnHeadDim) attn_decode_merge_kernel(MergePa
     const int s0 = min(nsplit, int(g) * per), s1 = min(nsplit, s0 + per);
     const size_t base = (size_t(b) * p.heads + h) * p.max_splits;
     const float2 *ml = reinterpret_cast<const float2 *>(p.part_ml) + base;
+    // This warp's first two splits are loaded before the CTA-wide max, so
+    // that their loads overlap it; they are added first, in the same order.
+    float2 vpre[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+    float4 apre[2] = {make_float4(0.f, 0.f, 0.f, 0.f), make_float4(0.f, 0.f, 0.f, 0.f)};
+    float4 cpre[2] = {make_float4(0.f, 0.f, 0.f, 0.f), make_float4(0.f, 0.f, 0.f, 0.f)};
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+        const int s = s0 + warp + u * kWarps;
+        if (s < s1) {
+            vpre[u] = ml[s];
+            const float4 *src = reinterpret_cast<const float4 *>(p.part_o + (base + s) * kAttnHeadDim) + 2 * lane;
+            apre[u] = src[0];
+            cpre[u] = src[1];
+        }
+    }
     float m = -INFINITY;
     for (int s = s0 + tid; s < s1; s += kAttnHeadDim) m = fmaxf(m, ml[s].x);
     m = warp_max(m);
@@ -894,15 +914,19 @@ __global__ void __launch_bounds__(kAttnHeadDim) attn_decode_merge_kernel(MergePa
     for (int w = 0; w < kWarps; ++w) m = fmaxf(m, mred[w]);
     float l = 0.f;
     float o[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-#pragma unroll 4
-    for (int s = s0 + warp; s < s1; s += kWarps) {
-        const float2 v = ml[s];
-        const float4 *src = reinterpret_cast<const float4 *>(p.part_o + (base + s) * kAttnHeadDim) + 2 * lane;
-        const float4 a = src[0], c = src[1];
+    auto add_split = [&](const float2 v, const float4 a, const float4 c) {
         const float w = expf(v.x - m);
         l += w * v.y;
         o[0] += w * a.x; o[1] += w * a.y; o[2] += w * a.z; o[3] += w * a.w;
         o[4] += w * c.x; o[5] += w * c.y; o[6] += w * c.z; o[7] += w * c.w;
+    };
+#pragma unroll
+    for (int u = 0; u < 2; ++u)
+        if (s0 + warp + u * kWarps < s1) add_split(vpre[u], apre[u], cpre[u]);
+#pragma unroll 4
+    for (int s = s0 + warp + 2 * kWarps; s < s1; s += kWarps) {
+        const float4 *src = reinterpret_cast<const float4 *>(p.part_o + (base + s) * kAttnHeadDim) + 2 * lane;
+        add_split(ml[s], src[0], src[1]);
     }
 #pragma unroll
     for (int i = 0; i < 8; ++i) red[warp][8 * lane + i] = o[i];
@@ -1067,14 +1091,17 @@ cudaError_t launch_typed(const AttnDecodeLaunch &a, int sm_count, cudaStream_t s
                   a.vcache,     a.qprep,    a.err,          a.q_norm,     a.k_norm,
                   a.context_length, a.heads, a.kv_heads,    a.max_position, a.pos_offset,
                   sharded,      a.theta_scale, a.eps, a.p2p_nranks > 0 ? a.p2p_epoch : nullptr};
-    attn_decode_prep_kernel<KV>
-        <<<dim3(a.heads + a.kv_heads, a.batch), kAttnHeadDim, 0, stream>>>(pp);
-    cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess) return e;
-
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t pcfg{};
+    pcfg.gridDim = dim3(a.heads + a.kv_heads, a.batch);
+    pcfg.blockDim = dim3(kAttnHeadDim);
+    pcfg.stream = stream;
+    pcfg.attrs = attr;
+    pcfg.numAttrs = 1;
+    cudaError_t e = cudaLaunchKernelEx(&pcfg, attn_decode_prep_kernel<KV>, pp);
+    if (e != cudaSuccess) return e;
 
     SplitParams sp{a.kcache,   a.vcache,  a.qprep,  a.positions,       a.part_o,
                    a.part_ml,  a.err,     a.context_length, a.heads, a.kv_heads,
