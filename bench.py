@@ -71,6 +71,10 @@ def parse_args():
     ap.add_argument("--prefill-batch", type=int, default=4)
     ap.add_argument("--prefill-len", type=int, default=8192)
     ap.add_argument("--prefill-iters", type=int, default=5)
+    ap.add_argument("--prefill-base", type=int, default=0,
+                    help="config-4 leg: cached positions before each prompt (a continuation)")
+    ap.add_argument("--prefill-kv", choices=["bf16", "f32"], default="bf16",
+                    help="config-4 leg: KV cache type (f32: the reference's cache)")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-split", action="store_true")
     ap.add_argument("--split-context", type=int, default=131072)
@@ -122,10 +126,11 @@ def load_tensor_peak() -> tuple[float, str]:
     return 1590.0, "fallback"
 
 
-def prefill_flops(batch: int, seq: int) -> float:
+def prefill_flops(batch: int, seq: int, base: int = 0) -> float:
     """Causal attention FLOPs (config 4): batch * 24 heads * (2*256 for QK^T +
-    2*256 for PV) per visible (query, key) pair, seq*(seq+1)/2 pairs."""
-    return float(batch) * 24 * 4 * 256 * seq * (seq + 1) / 2
+    2*256 for PV) per visible (query, key) pair: seq*(seq+1)/2 pairs, plus
+    seq*base with `base` cached positions before the prompt."""
+    return float(batch) * 24 * 4 * 256 * (seq * (seq + 1) / 2 + float(seq) * base)
 
 
 def run_prefill(args, ctx, q38attn, synth, torch, rank: int, world: int, dist) -> dict:
@@ -135,13 +140,20 @@ def run_prefill(args, ctx, q38attn, synth, torch, rank: int, world: int, dist) -
     the ranks (strong scaling), each rank running q38_full_prefill_heads over
     its share on the same global inputs."""
     from q38attn.parallel import prefill_segments
-    B, S = args.prefill_batch, args.prefill_len
+    B, S, base = args.prefill_batch, args.prefill_len, args.prefill_base
     layer = FULL_LAYER
     segs = prefill_segments(B, 4, world, rank)
-    st = ctx.state(B, S, full_slots=1, linear_slots=0, kv_dtype=q38attn.Q38_KV_BF16)
+    kv = q38attn.Q38_KV_F32 if args.prefill_kv == "f32" else q38attn.Q38_KV_BF16
+    st = ctx.state(B, base + S, full_slots=1, linear_slots=0, kv_dtype=kv)
     st.reserve_prefill(max(n for _, n, _, _ in segs) * S)
     tg = torch.Generator(device="cuda")
     tg.manual_seed(args.seed + 77)  # the same global prompts on every rank
+    if base:
+        # The cached prefix (a continuation prompt), filled on the device.
+        kview, vview = st.kv_views(layer)
+        kview[:, :, :base].normal_(generator=tg)
+        vview[:, :, :base].normal_(generator=tg)
+        del kview, vview
     qg = torch.randn(B, S, 12288, device="cuda", generator=tg)
     key0 = torch.randn(B, S, 1024, device="cuda", generator=tg)
     val = torch.randn(B, S, 1024, device="cuda", generator=tg)
@@ -154,7 +166,7 @@ def run_prefill(args, ctx, q38attn, synth, torch, rank: int, world: int, dist) -
     def one():
         for s0, n, h0, nh in segs:
             ctx.full_prefill_heads(st, layer, s0, qg[s0:s0 + n], key[s0:s0 + n], val[s0:s0 + n],
-                                   att[s0:s0 + n], 0, h0, nh, stream=stream)
+                                   att[s0:s0 + n], base, h0, nh, stream=stream)
 
     for it in range(2):
         key.copy_(key0)  # key is rewritten in place (RMSNorm + RoPE)
@@ -903,11 +915,14 @@ def run_ours(args) -> None:
         }
         tpeak, tpeak_kind = load_tensor_peak()
         if prefill:
-            flops = prefill_flops(args.prefill_batch, args.prefill_len)
+            flops = prefill_flops(args.prefill_batch, args.prefill_len, args.prefill_base)
             tflops = flops / (prefill_ms * 1e-3) / 1e12
             line["prefill"] = {
                 "workload": (f"config4: {args.prefill_batch} x {args.prefill_len}-token causal "
-                             "prefill (the whole job), 24Q/4KV x 256, RoPE 64, sigmoid gate; "
+                             "prefill (the whole job)"
+                             + (f" after {args.prefill_base} cached positions each"
+                                if args.prefill_base else "")
+                             + f", {args.prefill_kv} KV cache, 24Q/4KV x 256, RoPE 64, sigmoid gate; "
                              "QK^T bf16, PV f16, f32 accumulate (tcgen05); its "
                              f"{args.prefill_batch * 4} (sequence, KV-head group) units split "
                              f"over {world} GPU(s)"),
