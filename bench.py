@@ -33,8 +33,12 @@ sequence: every rank owns its own 32 sequences (weak scaling, no data-path
 collective). The prefill legs keep the global config-4 / config-5 workload
 fixed and split its units across the ranks (strong scaling): (sequence,
 KV-head group) units for the attention prefill, value heads for the DeltaNet
-prefill. The split-sequence leg spreads one sequence's positions over the
-ranks and exchanges softmax partials with the library's NCCL all-gather.
+prefill (--prefill-base N runs the attention prefill as a continuation after N
+cached positions, --prefill-kv f32 over the reference's f32 cache). The
+split-sequence leg spreads one sequence's positions over the ranks; the merge
+kernel exchanges the softmax partials over peer memory (the timed tokens
+replayed as one CUDA graph), and the same step with the library's NCCL
+all-gather is reported beside it.
 """
 from __future__ import annotations
 
