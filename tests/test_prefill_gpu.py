@@ -185,6 +185,24 @@ def test_prefill_f32_cache(cuda_ctx, oracle_lib):
               kv_f32=True)
 
 
+LONG_PREFIX_ROWS = list(range(0, 512, 37)) + [63, 64, 511]
+
+
+def test_prefill_long_prefix(cuda_ctx, oracle_lib):
+    """A continuation after a 4096-position bf16 prefix (the prefix copied to
+    f16 V operands in whole 64-row tiles, every query tile's prefix part
+    unmasked): 2 sequences x 512 tokens, sampled rows against the oracle."""
+    _run_case(cuda_ctx, oracle_lib, nseq=2, count=512, base=4096, ctx_len=4608, layer=3, seed=11,
+              rows=LONG_PREFIX_ROWS)
+
+
+def test_prefill_f32_cache_long_prefix(cuda_ctx, oracle_lib):
+    """The same over the reference's f32 cache (K and V of the prefix copied
+    to f16 operands): 1 sequence x 512 tokens after 4096 f32 positions."""
+    _run_case(cuda_ctx, oracle_lib, nseq=1, count=512, base=4096, ctx_len=4608, layer=3, seed=12,
+              kv_f32=True, rows=LONG_PREFIX_ROWS)
+
+
 def test_prefill_f32_cache_head_range(cuda_ctx, oracle_lib):
     _run_case(cuda_ctx, oracle_lib, nseq=1, count=260, base=0, ctx_len=512, layer=3, seed=10,
               kv_f32=True, kv_range=(2, 2))
